@@ -1,0 +1,189 @@
+/*
+ * wxx_cuda.h -- C ABI of libwxx_cuda.so, the sm_100a (B200) kernel library
+ * behind the wxx.functional operator layer.
+ *
+ * Conventions
+ *   - Every function returns 0 on success or a negative status:
+ *       -1 WXX_E_ARG  -2 WXX_E_CUDA  -3 WXX_E_TIMEOUT  -4 WXX_E_UNSUPPORTED  -5 WXX_E_STATE
+ *     and wxx_last_error() returns the message of the last failure (per host thread).
+ *   - All pointers are device pointers unless stated; sizes and strides are in
+ *     elements (4-byte f32/u32 or 8-byte interleaved c64) unless stated.
+ *   - Work is enqueued on the library's per-process stream in call order; the
+ *     only host synchronisation points are wxx_sync, wxx_memcpy_d2h and
+ *     wxx_device_status.  One process drives one GPU (wxx_init(device)).
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths relative to the reference project Mo-Ehab/wxx, src/wxx/...).
+ */
+#ifndef WXX_CUDA_H
+#define WXX_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- runtime
+ * Replaces backend/device.py:9-28 (WebGPUContext), :31-141 (GPUBufferPool),
+ * :144-255 (GPUCommandBuffer: batching, keep_alive, flush).                 */
+
+const char* wxx_last_error(void);
+const char* wxx_version(void);
+int wxx_device_count(int* count);
+/* backend/device.py:258 (module-level WebGPUContext()) */
+int wxx_init(int device);
+int wxx_current_device(int* device);
+int wxx_num_sms(int* sms);
+/* backend/device.py:40-47 create_buffer / :91-105 release */
+int wxx_malloc(void** out, uint64_t nbytes);
+int wxx_free(void* ptr);
+/* backend/device.py:115-133 get_memory_snapshot: out[0] active bytes, out[1] live
+ * blocks, out[2] pool reserved bytes, out[3] peak active, out[4] allocs, out[5] frees */
+int wxx_mem_stats(int64_t* out6);
+/* backend/device.py:135-141 clear_cache */
+int wxx_mem_trim(void);
+int wxx_host_alloc(void** out, uint64_t nbytes);          /* pinned host memory */
+int wxx_host_free(void* ptr);
+/* Tensor.py:66-90 (buffer upload), Tensor.py:552-569 read_buffer */
+int wxx_memcpy_h2d(void* dst, const void* src, uint64_t nbytes);
+int wxx_memcpy_d2h(void* dst, const void* src, uint64_t nbytes);
+int wxx_memcpy_d2h_async(void* dst, const void* src, uint64_t nbytes);
+int wxx_memcpy_d2d(void* dst, const void* src, uint64_t nbytes);
+int wxx_memset(void* dst, int value, uint64_t nbytes);
+/* backend/device.py:208-247 flush(wait=True) */
+int wxx_sync(void);
+void* wxx_get_stream(void);
+int wxx_set_stream(void* stream);
+/* No reference counterpart (kernels have no error channel there): reads and
+ * clears the device error word (1 = bounded wait expired, 2 = index out of range). */
+int wxx_device_status(int* code);
+int wxx_event_create(void** ev);
+int wxx_event_destroy(void* ev);
+int wxx_event_record(void* ev);
+int wxx_event_elapsed_ms(void* start, void* stop, float* ms);
+
+/* ---------------------------------------------------------------- elementwise */
+
+/* functional/pointwise.py:29-98 pointwise (pointwise.wgsl) and :232-291
+ * _pointwise (in place when out == a).  op: 0 add, 1 sub, 2 mul, 3 div. */
+int wxx_binary(float* out, const float* a, int64_t a_off, const int64_t* stride_a,
+               const float* b, int64_t b_off, const int64_t* stride_b, int rank,
+               const int64_t* shape, int op);
+/* functional/pointwise.py:101-146 scalarpointwise.  op: 0 add, 1 sub, 2 mul, 3 pow, 4 div;
+ * op 5 is functional/utils.py:585-616 masked_fill (maskedfill.wgsl): x != 0 ? x : c. */
+int wxx_scalar(float* out, const float* x, int64_t n, int op, float c, int reverse);
+/* functional/pointwise.py:149-178 clamp (clamp.wgsl) */
+int wxx_clamp(float* out, const float* x, int64_t n, float lo, float hi);
+/* functional/activations.py:22-120 and functional/pointwise.py:294-355 via
+ * backend/dispatch.py:59-89 _unary_op.  op: 0 relu, 1 gelu (tanh form, +-10 clamps),
+ * 2 sigmoid (input clamped to +-88), 3 sin, 4 cos, 5 exp, 6 log, 7 sqrt, 8 rsqrt,
+ * 9 abs, 10 sign, 11 negate, 12 square, 13 silu, 14 selu. */
+int wxx_unary(float* out, const float* x, int64_t n, int op);
+/* functional/utils.py:316-369 contiguous (contiguous.wgsl), :29-101 assign
+ * (assign.wgsl), functional/fft.py:295-342 complex_contiguous.  elem_bytes 4 or 8. */
+int wxx_strided_copy(void* dst, int64_t dst_off, const int64_t* dst_stride, const void* src,
+                     int64_t src_off, const int64_t* src_stride, int rank, const int64_t* shape,
+                     int elem_bytes);
+/* functional/utils.py:36-55 assign with a scalar value */
+int wxx_strided_fill(void* dst, int64_t dst_off, const int64_t* dst_stride, int rank,
+                     const int64_t* shape, uint32_t value_bits);
+/* functional/layers.py:161-206 embed (embed.wgsl) */
+int wxx_embed(float* out, const uint32_t* ids, const float* weight, int64_t n_tokens, int dim,
+              uint32_t vocab);
+/* functional/convolution.py:1188-1257 causal_conv1d (causal_conv1d.wgsl) */
+int wxx_causal_conv1d(float* out, const float* x, int64_t x_off, int64_t sb, int64_t sc,
+                      int64_t sl, const float* w, const float* bias, int B, int D, int L, int K);
+/* functional/pointwise.py:357-404 decay_window (decay_window.wgsl) */
+int wxx_decay_window(float* out, const float* decay, int rows, int channels, int length,
+                     int stage);
+/* functional/fft.py:168-213 complex_mul (complex_mul.wgsl) */
+int wxx_complex_mul(void* out, const void* a, int64_t a_off, const int64_t* stride_a,
+                    const void* b, int64_t b_off, const int64_t* stride_b, int rank,
+                    const int64_t* shape, int conj_a, int conj_b);
+/* functional/fft.py:344-383 complex_conj / complex_add_inplace */
+int wxx_complex_conj(void* out, const void* x, int64_t n);
+int wxx_complex_add_inplace(void* acc, const void* x, int64_t n);
+/* functional/utils.py:509-582 equal / equal_number (equal.wgsl) */
+int wxx_equal(float* out, const void* a, const void* b, int64_t n, int mode, uint32_t number);
+
+/* ---------------------------------------------------------------- reductions / norms */
+
+/* functional/reductions.py:27-197 sum / mean / sumsq (reduce.wgsl) with the
+ * (outer, reduce, inner) mapping of backend/dispatch.py:173-214.  mode 0 sum, 1 mean, 2 sumsq. */
+int wxx_reduce(float* out, const float* x, int64_t outer, int64_t reduce, int64_t inner, int mode);
+/* functional/reductions.py:241-342 max / min (reduce_minmax.wgsl), op 0 max, 1 min;
+ * indices follow the reference's tie rule bit for bit. */
+int wxx_argminmax(float* vals, uint32_t* idx, const float* x, int64_t outer, int64_t reduce,
+                  int64_t inner, int op);
+/* functional/activations.py:126-173 softmax (softmax.wgsl) */
+int wxx_softmax(float* y, const float* x, int64_t outer, int64_t n, int64_t inner);
+/* nn/module.py:484-488 (score + mask, then softmax) fused: row r uses mask row r % mask_rows. */
+int wxx_softmax_masked(float* y, const float* x, int64_t rows, int64_t n, const float* mask,
+                       int64_t mask_ld, int64_t mask_rows);
+/* functional/normalization.py:82-145 meanvarnorm (meanvarnorm.wgsl), eps 1e-5 */
+int wxx_layernorm(float* y, float* mean, float* inv_std, const float* x, const float* gamma,
+                  const float* beta, int64_t outer, int64_t n, int64_t inner, float eps);
+/* functional/normalization.py:24-79 rmsnorm (rmsnorm.wgsl), eps 1e-6 */
+int wxx_rmsnorm(float* y, float* inv_rms, const float* x, const float* gamma, int64_t outer,
+                int64_t n, int64_t inner, float eps);
+/* functional/normalization.py:148-206 batchnorm (batchnorm.wgsl) */
+int wxx_batchnorm(float* y, float* saved_mean, float* saved_inv, const float* x,
+                  const float* gamma, const float* beta, float* running_mean, float* running_var,
+                  int B, int C, int64_t hw, float eps, float momentum, int training);
+
+/* ---------------------------------------------------------------- contractions */
+
+/* functional/utils.py:378-499 matmul_add (matmul.wgsl).  C dense [batch, M, N].
+ * trans_a: element (m, k) at A[b*a_bs + k*lda + m]; else A[b*a_bs + m*lda + k].
+ * trans_b: element (k, n) at B[b*b_bs + n*ldb + k]; else B[b*b_bs + k*ldb + n].
+ * a_bs/b_bs = 0 broadcasts over the batch.  bias_mode 0 none, 1 (N,), 2 (M,N), 3 (batch,M,N).
+ * mode 0 TF32 tcgen05, 1 3xTF32 tcgen05, 2 fp32 SIMT.  C = alpha * op(A) op(B) + bias. */
+int wxx_matmul(float* C, const float* A, const float* B, const float* bias, int64_t batch,
+               int64_t M, int64_t N, int64_t K, int64_t a_bs, int64_t b_bs, int64_t lda,
+               int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha, int mode);
+/* functional/convolution.py:658-729 conv2d (conv2d.wgsl), NCHW implicit GEMM on tcgen05.
+ * mode 0 TF32, 1 or 2 3xTF32. */
+int wxx_conv2d(float* Y, const float* X, const float* W, const float* bias, int B, int Cin,
+               int H, int Wd, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int dh,
+               int dw, int mode);
+
+/* ---------------------------------------------------------------- pooling */
+
+/* functional/convolution.py:60-125 maxpool2d (maxpool2d.wgsl); idx may be NULL */
+int wxx_maxpool2d(float* Y, uint32_t* idx, const float* X, int B, int C, int H, int W, int KH,
+                  int KW, int sh, int sw, int ph, int pw);
+/* functional/convolution.py:490-543 adaptive_avgpool2d (adaptive_avgpool2d.wgsl) */
+int wxx_adaptive_avgpool2d(float* Y, const float* X, int B, int C, int H, int W, int Ho, int Wo);
+
+/* ---------------------------------------------------------------- FFT */
+
+/* functional/fft.py:484-563 rfft (fft_bitrev_real / fft_stage / fft_copy_out / fft_wg_real) */
+int wxx_rfft(void* X, int64_t out_ld, const float* x, int64_t in_ld, int64_t rows, int64_t in_len,
+             int64_t n);
+/* functional/fft.py:566-645 irfft (fft_bitrev_complex / fft_stage / ifft_write_real / fft_wg_inverse) */
+int wxx_irfft(float* y, int64_t out_ld, const void* X, int64_t in_ld, int64_t rows,
+              int64_t in_len, int64_t n);
+/* nn/hyena.py:208-216 HyenaOperator.fft_conv1d = irfft(rfft(x, n) * H, n)[..., :out_len]
+ * with a precomputed filter spectrum H (D, n/2+1). */
+int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                         int64_t sl, const void* H, int64_t h_ld, int B, int D, int L, int64_t n,
+                         int out_len);
+/* nn/hyena.py:208-216 fft_conv1d with a time-domain filter h (D, Lh) */
+int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd, int64_t sl,
+                const float* h, int64_t h_ld, int Lh, int B, int D, int L, int64_t n, int out_len);
+
+/* ---------------------------------------------------------------- NCCL
+ * No reference counterpart (the reference drives one WebGPU device): the
+ * all-gather of batch-sharded outputs across the GPUs of one node. */
+int wxx_nccl_unique_id(uint8_t* out128);
+int wxx_nccl_init(const uint8_t* id128, int nranks, int rank);
+int wxx_nccl_allgather(void* recv, const void* send, uint64_t nbytes);
+int wxx_nccl_async_error(int* code);
+int wxx_nccl_destroy(int abort);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WXX_CUDA_H */

@@ -1,0 +1,411 @@
+"""Kernel parity: every wxx_b200.functional op on the GPU against the CPU oracle.
+
+Tolerances (norm-wise: max |got - ref| / max |ref|):
+  integer / index / copy / gather work  bit-exact
+  fp32 elementwise, reductions, norms   1e-5 (activations with transcendental
+                                         functions 2e-6 absolute on unit-scale data)
+  matmul / conv2d                       2e-3 in TF32 mode, 1e-5 in 3xTF32 mode
+  FFT (rfft / irfft / fftconv)          2e-5 of the largest output
+"""
+
+import numpy as np
+import pytest
+
+from oracle import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+
+def _w():
+    import wxx_b200 as wxx
+
+    return wxx
+
+
+def up(a, dtype=np.float32):
+    return _w().functional.from_numpy(np.asarray(a), dtype=dtype)
+
+
+def rel(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = max(np.abs(ref).max(), 1e-30) if ref.size else 1.0
+    return float(np.abs(got - ref).max() / scale) if ref.size else 0.0
+
+
+# ------------------------------------------------------------ elementwise / copies
+
+@pytest.mark.parametrize("shape_a,shape_b", [((5, 7), (5, 7)), ((4, 3, 8), (8,)),
+                                             ((2, 1, 6), (3, 1)), ((1031,), (1031,)),
+                                             ((3, 256, 256), (256, 256))])
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+def test_pointwise_broadcast(shape_a, shape_b, op, rng):
+    F = _w().functional
+    a = rng.standard_normal(shape_a).astype(np.float32)
+    b = rng.standard_normal(shape_b).astype(np.float32) + (3.0 if op == 3 else 0.0)
+    got = F.pointwise(up(a), up(b), op).numpy()
+    assert np.array_equal(got, K.pointwise(a, b, op))
+
+
+def test_pointwise_strided_views(rng):
+    F = _w().functional
+    a = rng.standard_normal((4, 6, 8)).astype(np.float32)
+    b = rng.standard_normal((8, 6)).astype(np.float32)
+    ta = up(a).permute(0, 2, 1)          # (4, 8, 6) strided
+    tb = up(b)[1:7:2]                    # (3, 6) strided rows... broadcast below
+    got = F.pointwise(ta, up(b), 2).numpy()
+    assert np.array_equal(got, np.transpose(a, (0, 2, 1)) * b)
+    got2 = F.pointwise(up(a)[:, 1:4, ::2], tb[:, :4], 0).numpy()
+    assert np.array_equal(got2, a[:, 1:4, ::2] + b[1:7:2][:, :4])
+
+
+@pytest.mark.parametrize("op,c,rev", [(0, 1.5, 0), (1, 2.0, 1), (2, -0.5, 0), (4, 3.0, 0),
+                                      (4, 2.0, 1), (3, 2.0, 0), (3, 3.0, 0), (3, 0.5, 0),
+                                      (3, 2.0, 1)])
+def test_scalar_ops(op, c, rev, rng):
+    F = _w().functional
+    x = rng.standard_normal((37, 11)).astype(np.float32)
+    if op == 4 and rev:
+        x = x + np.sign(x) * 0.5
+    got = F.scalarpointwise(up(x), c, op, reverse=rev).numpy()
+    ref = K.scalarpointwise(x, c, op, rev)
+    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-6, equal_nan=True)
+
+
+@pytest.mark.parametrize("name", ["relu", "gelu", "sigmoid", "silu", "sin", "cos", "exp",
+                                  "abs", "sign", "negate", "square"])
+def test_unary(name, rng):
+    F = _w().functional
+    x = (rng.standard_normal(4099) * 3).astype(np.float32)
+    x[:4] = [25.0, -25.0, 0.0, -0.0]
+    got = getattr(F, name)(up(x)).numpy()
+    ref = K.unary(x, name)
+    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=2e-6)
+
+
+def test_contiguous_and_assign_bit_exact(rng):
+    F = _w().functional
+    a = rng.standard_normal((3, 5, 7, 9)).astype(np.float32)
+    t = up(a)
+    for view, ref in [(t.permute(3, 1, 0, 2), np.transpose(a, (3, 1, 0, 2))),
+                      (t[1:, ::2, 3], a[1:, ::2, 3]),
+                      (t.transpose(2, 3), np.swapaxes(a, 2, 3))]:
+        assert np.array_equal(F.contiguous(view).numpy(), ref)
+    dst = up(np.zeros((4, 6), np.float32))
+    F.assign(dst[1:3, 2:5], up(np.arange(6, dtype=np.float32).reshape(2, 3)))
+    ref = np.zeros((4, 6), np.float32)
+    ref[1:3, 2:5] = np.arange(6).reshape(2, 3)
+    assert np.array_equal(dst.numpy(), ref)
+    F.assign(dst[:, 0], 7.0)
+    ref[:, 0] = 7.0
+    assert np.array_equal(dst.numpy(), ref)
+
+
+@pytest.mark.parametrize("B,S,V,D", [(4, 256, 1024, 256), (8, 300, 64, 32), (2, 5, 7, 3)])
+def test_embed_bit_exact(B, S, V, D, rng):
+    F = _w().functional
+    ids = rng.integers(0, V, size=(B, S)).astype(np.uint32)
+    w = rng.standard_normal((V, D)).astype(np.float32)
+    got = F.embed(up(ids, np.uint32), up(w), B * S, D).numpy()
+    assert got.shape == (B, S, D)
+    assert np.array_equal(got, K.embed(ids, w))
+
+
+def test_causal_conv1d_dense_and_transposed(rng):
+    F = _w().functional
+    x = rng.standard_normal((3, 5, 40)).astype(np.float32)
+    w = rng.standard_normal((5, 3)).astype(np.float32)
+    b = rng.standard_normal(5).astype(np.float32)
+    got = F.causal_conv1d(up(x), up(w), up(b)).numpy()
+    np.testing.assert_allclose(got, K.causal_conv1d(x, w, b), rtol=1e-5, atol=1e-5)
+    xt = rng.standard_normal((2, 70, 37)).astype(np.float32)     # (B, L, D)
+    w2 = rng.standard_normal((37, 4)).astype(np.float32)
+    b2 = rng.standard_normal(37).astype(np.float32)
+    got2 = F.causal_conv1d(up(xt).permute(0, 2, 1), up(w2), up(b2)).numpy()
+    np.testing.assert_allclose(got2, K.causal_conv1d(np.transpose(xt, (0, 2, 1)), w2, b2),
+                               rtol=1e-5, atol=1e-5)
+
+
+def test_decay_window(rng):
+    F = _w().functional
+    d = rng.random((4, 33)).astype(np.float32)
+    got = F.decay_window(up(d), 2, 100).numpy()
+    np.testing.assert_allclose(got, K.decay_window(d, 2, 100), rtol=2e-6, atol=1e-7)
+
+
+# ------------------------------------------------------------ reductions / norms
+
+@pytest.mark.parametrize("shape,axis", [((4, 5), None), ((4, 5), 0), ((4, 5), 1),
+                                        ((37, 4099), 1), ((4099, 37), 0), ((3, 300, 70), 1),
+                                        ((2, 3, 4, 5), (1, 2)), ((1024, 1024), 0)])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_reduce(shape, axis, mode, rng):
+    F = _w().functional
+    x = rng.standard_normal(shape).astype(np.float32)
+    fn = [F.sum, F.mean, F.sumsq][mode]
+    got = fn(up(x), axis).numpy()
+    ref = K.reduce(x, axis, mode)
+    # error relative to the l2 norm of the reduced slice (sums can cancel to ~0)
+    o, r, i, _ = K.reduce_dims(x.shape, axis)
+    scale = np.sqrt((x.reshape(o, r, i).astype(np.float64) ** 2).sum(1)).reshape(ref.shape)
+    if mode == 1:
+        scale = scale / r
+    if mode == 2:
+        scale = ref.astype(np.float64)
+    assert np.all(np.abs(got.astype(np.float64) - ref) <= 1e-5 * np.maximum(scale, 1e-12))
+
+
+def test_reduce_keepdims(rng):
+    F = _w().functional
+    x = rng.standard_normal((4, 5)).astype(np.float32)
+    assert F.sum(up(x), 1, keepdims=True).numpy().shape == (4, 1)
+    assert F.mean(up(x), None, keepdims=True).numpy().shape == (1, 1)
+
+
+@pytest.mark.parametrize("shape,axis", [((3, 4), 1), ((3, 4), 0), ((4, 256, 1024), -1),
+                                        ((7, 1000, 3), 1), ((5, 70000), 1)])
+@pytest.mark.parametrize("op", [0, 1])
+def test_argminmax_bit_exact(shape, axis, op, rng):
+    F = _w().functional
+    x = rng.standard_normal(shape).astype(np.float32)
+    vals, idx = (F.max if op == 0 else F.min)(up(x), axis)
+    rv, ri = K.argminmax(x, axis, op)
+    assert np.array_equal(vals.numpy(), rv)
+    assert np.array_equal(idx.numpy(), ri)
+
+
+def test_argmax_ties_follow_reference_tree(rng):
+    """Ties resolved exactly like reduce_minmax.wgsl (not always the lowest index)."""
+    F = _w().functional
+    x = rng.integers(0, 3, size=(64, 1000)).astype(np.float32)   # heavy ties
+    x[5, 128] = 9.0
+    x[5, 64] = 9.0                                                 # slot 64 vs 128 -> 128 wins
+    vals, idx = F.max(up(x), 1)
+    rv, ri = K.argminmax(x, 1, 0)
+    assert np.array_equal(idx.numpy(), ri)
+    assert ri[5] == 128
+    x2 = np.full((2, 10), -np.inf, np.float32)                     # below the -1e38 start
+    v2, i2 = F.max(up(x2), 1)
+    assert np.array_equal(v2.numpy(), K.argminmax(x2, 1, 0)[0])
+    assert np.array_equal(i2.numpy(), np.zeros(2, np.uint32))
+
+
+@pytest.mark.parametrize("shape,dim", [((3, 5), -1), ((32, 256, 256), -1), ((8, 1024), -1),
+                                       ((4, 3000), -1), ((6, 9, 5), 1)])
+def test_softmax(shape, dim, rng):
+    F = _w().functional
+    x = (rng.standard_normal(shape) * 3).astype(np.float32)
+    got = F.softmax(up(x), dim).numpy()
+    np.testing.assert_allclose(got, K.softmax(x, dim), rtol=1e-5, atol=1e-7)
+
+
+def test_masked_softmax_matches_add_then_softmax(rng):
+    F = _w().functional
+    x = rng.standard_normal((6, 40, 40)).astype(np.float32)
+    m = np.where(np.arange(64)[None, :] <= np.arange(64)[:, None], 0.0, -1e9).astype(np.float32)
+    tm = up(m).narrow(0, 0, 40).narrow(1, 0, 40)
+    got = F.masked_softmax(up(x), tm).numpy()
+    ref = K.softmax((x + m[:40, :40]).astype(np.float32), -1)
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("shape,axis", [((2, 3, 4), -1), ((1024, 256), -1), ((8, 1024), -1),
+                                        ((3, 2000), -1), ((4, 6, 5), (1, 2)), ((5, 7, 3), 1)])
+def test_layernorm_rmsnorm(shape, axis, rng):
+    F = _w().functional
+    x = rng.standard_normal(shape).astype(np.float32)
+    n = K.reduce_dims(shape, axis)[1]
+    g = rng.standard_normal(n).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    y, mean, inv = F.meanvarnorm(up(x), up(g), up(b), axis)
+    ry, rm, ri = K.layernorm(x, g, b, axis)
+    assert rel(y.numpy(), ry) < 1e-5
+    assert rel(mean.numpy(), rm) < 1e-5 and rel(inv.numpy(), ri) < 1e-5
+    y2, inv2 = F.rmsnorm(up(x), up(g), axis)
+    ry2, ri2 = K.rmsnorm(x, g, axis)
+    assert rel(y2.numpy(), ry2) < 1e-5 and rel(inv2.numpy(), ri2) < 1e-5
+
+
+def test_norm_zero_rows_and_many_rows(rng):
+    F = _w().functional
+    x = rng.standard_normal((70000, 8)).astype(np.float32)   # > 65535 rows
+    x[3] = 0.0
+    g = np.ones(8, np.float32)
+    y, inv = F.rmsnorm(up(x), up(g), -1)
+    ry, ri = K.rmsnorm(x, g, -1)
+    assert rel(y.numpy(), ry) < 1e-5
+    assert inv.numpy()[3] == 0.0
+
+
+def test_batchnorm_eval(rng):
+    F = _w().functional
+    x = rng.standard_normal((4, 6, 5, 5)).astype(np.float32)
+    g = rng.standard_normal(6).astype(np.float32)
+    b = rng.standard_normal(6).astype(np.float32)
+    rm = rng.standard_normal(6).astype(np.float32)
+    rv = rng.random(6).astype(np.float32) + 0.5
+    y = F.batchnorm(up(x), up(g), up(b), up(rm), up(rv), False)[0].numpy()
+    assert rel(y, K.batchnorm_eval(x, g, b, rm, rv)) < 1e-5
+
+
+# ------------------------------------------------------------ contractions
+
+GEMM_SHAPES = [
+    # (batch_a, batch_b, M, N, K)
+    ((), (), 1, 1, 1),
+    ((), (), 3, 5, 7),
+    ((), (), 128, 128, 128),
+    ((), (), 127, 129, 33),
+    ((), (), 300, 257, 96),
+    ((), (), 512, 512, 512),
+    ((), (), 256, 1024, 256),
+    ((4,), (), 256, 256, 256),
+    ((), (3,), 64, 200, 64),
+    ((32,), (32,), 256, 256, 32),
+    ((2, 3), (2, 3), 70, 40, 24),
+    ((), (), 96, 682, 256),
+    ((), (), 100, 256, 682),
+    ((), (), 256, 10, 512),
+    ((), (), 8192 // 16, 64, 17),
+]
+
+
+@pytest.mark.parametrize("shape", GEMM_SHAPES)
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False)])
+@pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
+def test_matmul(shape, ta, tb, mode, rng):
+    wxx = _w()
+    F = wxx.functional
+    ba, bb, M, N, K_ = shape
+    a = rng.standard_normal(ba + ((K_, M) if ta else (M, K_))).astype(np.float32)
+    b = rng.standard_normal(bb + ((N, K_) if tb else (K_, N))).astype(np.float32)
+    F.set_matmul_mode(mode)
+    try:
+        got = F.matmul_add(up(a), up(b), None, transpose_A=ta, transpose_B=tb).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    ref = K.matmul_add(a, b, None, ta, tb)
+    tol = 2e-3 if mode == "tf32" else 1e-5
+    assert got.shape == ref.shape
+    assert rel(got, ref) < tol, rel(got, ref)
+    assert _w().backend.device_status() == 0
+
+
+@pytest.mark.parametrize("bias_kind", ["N", "MN", "BMN"])
+def test_matmul_bias_modes(bias_kind, rng):
+    F = _w().functional
+    a = rng.standard_normal((3, 70, 48)).astype(np.float32)
+    b = rng.standard_normal((48, 90)).astype(np.float32)
+    bias = {"N": rng.standard_normal(90), "MN": rng.standard_normal((70, 90)),
+            "BMN": rng.standard_normal((3, 70, 90))}[bias_kind].astype(np.float32)
+    got = F.matmul_add(up(a), up(b), up(bias)).numpy()
+    assert rel(got, K.matmul_add(a, b, bias)) < 2e-3
+
+
+def test_matmul_fp32_mode_exact_products(rng):
+    F = _w().functional
+    a = rng.standard_normal((65, 33)).astype(np.float32)
+    b = rng.standard_normal((33, 70)).astype(np.float32)
+    F.set_matmul_mode("fp32")
+    try:
+        got = F.matmul_add(up(a), up(b), None).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    assert rel(got, K.matmul_add(a, b)) < 1e-6
+
+
+def test_matmul_shape_errors():
+    F = _w().functional
+    with pytest.raises(ValueError):
+        F.matmul_add(up(np.zeros((3, 4))), up(np.zeros((5, 6))), None)
+    with pytest.raises(ValueError):
+        F.matmul_add(up(np.zeros((2, 3, 4))), up(np.zeros((3, 4, 6))), None)
+
+
+CONV_SHAPES = [
+    # B, Cin, H, W, Cout, k, stride, pad, dil
+    (2, 2, 8, 8, 3, 3, 1, 1, 1),
+    (4, 3, 32, 32, 64, 7, 2, 3, 1),
+    (8, 64, 8, 8, 64, 3, 1, 1, 1),
+    (8, 64, 8, 8, 128, 3, 2, 1, 1),
+    (8, 64, 8, 8, 128, 1, 2, 0, 1),
+    (4, 256, 2, 2, 512, 3, 2, 1, 1),
+    (3, 5, 11, 13, 7, 3, 2, 2, 2),
+]
+
+
+@pytest.mark.parametrize("shape", CONV_SHAPES)
+@pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
+def test_conv2d(shape, mode, rng):
+    F = _w().functional
+    B, C, H, W, O, k, s, p, d = shape
+    x = rng.standard_normal((B, C, H, W)).astype(np.float32)
+    w = (rng.standard_normal((O, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    bias = rng.standard_normal(O).astype(np.float32)
+    F.set_matmul_mode(mode)
+    try:
+        got = F.conv2d(up(x), up(w), (s, s), (p, p), (d, d), up(bias)).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    ref = K.conv2d(x, w, (s, s), (p, p), (d, d), bias)
+    assert got.shape == ref.shape
+    assert rel(got, ref) < (2e-3 if mode == "tf32" else 1e-5)
+
+
+def test_pooling(rng):
+    F = _w().functional
+    x = rng.standard_normal((4, 6, 16, 16)).astype(np.float32)
+    out, idx = F.maxpool2d(up(x), (3, 3), (2, 2), (1, 1), return_indices=True)
+    rv, ri = K.maxpool2d(x, (3, 3), (2, 2), (1, 1))
+    assert np.array_equal(out.numpy(), rv) and np.array_equal(idx.numpy(), ri)
+    for hw in [(1, 1), (3, 5), (16, 16)]:
+        got = F.adaptive_avgpool2d(up(x), hw).numpy()
+        assert rel(got, K.adaptive_avgpool2d(x, hw)) < 1e-6
+
+
+# ------------------------------------------------------------ FFT
+
+@pytest.mark.parametrize("rows,L,n", [(3, 5, 8), (4, 16, 16), (2, 100, 256), (5, 1000, 1024),
+                                      (3, 3000, 4096), (2, 8192, 16384), (2, 16384, 32768),
+                                      (2, 20, 2), (3, 1, 1), (2, 40000, 65536)])
+def test_rfft_irfft(rows, L, n, rng):
+    F = _w().functional
+    x = rng.standard_normal((rows, L)).astype(np.float32)
+    spec, nn = F.rfft(up(x), n)
+    assert nn == n
+    ref = K.rfft(x, n)
+    assert rel(spec.numpy(), ref) < 2e-5
+    if n >= 2:
+        back = F.irfft(spec, n).numpy()
+        assert rel(back, K.irfft(ref, n)) < 2e-5
+
+
+def test_irfft_truncated_and_padded_spectrum(rng):
+    F = _w().functional
+    X = (rng.standard_normal((3, 40)) + 1j * rng.standard_normal((3, 40))).astype(np.complex64)
+    for n in (32, 128, 2048):
+        got = F.irfft(F.from_numpy_complex(X), n).numpy()
+        assert rel(got, K.irfft(X, n)) < 2e-5
+
+
+def test_complex_mul_broadcast(rng):
+    F = _w().functional
+    a = (rng.standard_normal((3, 4, 9)) + 1j * rng.standard_normal((3, 4, 9))).astype(np.complex64)
+    b = (rng.standard_normal((4, 9)) + 1j * rng.standard_normal((4, 9))).astype(np.complex64)
+    got = F.complex_mul(F.from_numpy_complex(a), F.from_numpy_complex(b), conj_b=True).numpy()
+    assert rel(got, K.complex_mul(a, b, conj_b=True)) < 1e-6
+
+
+@pytest.mark.parametrize("B,D,L", [(2, 3, 64), (3, 4, 1000), (2, 8, 8192), (1, 4, 16384),
+                                   (1, 2, 40000)])
+def test_fftconv_matches_reference_chain(B, D, L, rng):
+    F = _w().functional
+    x = rng.standard_normal((B, D, L)).astype(np.float32)
+    h = rng.standard_normal((D, L)).astype(np.float32)
+    n = 1 << (2 * L - 1).bit_length()
+    got = F.fftconv(up(x), up(h), n, out_len=L).numpy()
+    ref = K.fftconv(x, h, n, L)
+    assert rel(got, ref) < 2e-5
+    # the unfused reference chain through the public ops gives the same result
+    chain = F.irfft(F.complex_mul(F.rfft(up(x), n)[0], F.rfft(up(h), n)[0]), n)
+    assert rel(chain.numpy()[..., :L], ref) < 2e-5

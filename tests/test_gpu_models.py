@@ -1,0 +1,103 @@
+"""Model parity on the GPU: GPT2 / ResNet18 / Hyena forwards through the
+unchanged wxx API against the CPU oracle on the same seeded state dict.
+
+Bar: final logits within 1e-3 max-abs in TF32 mode;
+3xTF32 mode is checked at 1e-4.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import init, models
+
+pytestmark = pytest.mark.gpu
+
+
+def _wxx():
+    import wxx_b200 as wxx
+
+    return wxx
+
+
+def _run(model, ids_or_x, is_ids=True):
+    wxx = _wxx()
+    F = wxx.functional
+    t = F.from_numpy(ids_or_x, dtype=np.uint32) if is_ids else F.from_numpy(ids_or_x)
+    with wxx.backend.inferenceMode():
+        return model(t).numpy()
+
+
+@pytest.mark.parametrize("mode,tol", [("tf32", 1e-3), ("3xtf32", 1e-4)])
+def test_gpt2_config1_logits(mode, tol):
+    """GPT2(1024, 256, 8, 6), batch 4, seq 256."""
+    wxx = _wxx()
+    V, D, H, L, S = 1024, 256, 8, 6, 256
+    sd = init.gpt2_state_dict(0, V, D, H, L, S)
+    ids = init.token_ids(1, 4, S, V)
+    model = wxx.nn.GPT2(V, D, H, L, max_len=S)
+    model.load_state_dict(sd)
+    wxx.functional.set_matmul_mode(mode)
+    try:
+        got = _run(model, ids)
+    finally:
+        wxx.functional.set_matmul_mode("tf32")
+    ref = models.gpt2_forward(sd, ids, H, L)
+    assert got.shape == (4, S, V)
+    assert np.abs(got - ref).max() < tol, np.abs(got - ref).max()
+
+
+def test_gpt2_causal_and_state_dict_roundtrip(tmp_path):
+    wxx = _wxx()
+    model = wxx.nn.GPT2(50, 32, 4, 2, max_len=16)
+    ids = np.random.default_rng(0).integers(0, 50, size=(2, 16)).astype(np.uint32)
+    base = _run(model, ids)
+    ids2 = ids.copy()
+    ids2[:, 10:] = (ids2[:, 10:] + 7) % 50
+    changed = _run(model, ids2)
+    assert np.allclose(base[:, :10], changed[:, :10], atol=1e-5)     # causality
+    assert not np.allclose(base[:, 10:], changed[:, 10:])
+    path = wxx.save(model, str(tmp_path / "gpt2.npz"))
+    other = wxx.nn.GPT2(50, 32, 4, 2, max_len=16)
+    wxx.load(path, other)
+    assert np.array_equal(_run(other, ids), base)
+    keys = set(model.state_dict())
+    assert "blocks.0.ln1.weightg" in keys and "blocks.0.ln1.weight" in keys
+
+
+def test_resnet18_logits():
+    """BASELINE config 2 at a reduced batch: ResNet18(10), eval BatchNorm."""
+    wxx = _wxx()
+    sd = init.resnet18_state_dict(0, 10)
+    x = np.random.default_rng(2).standard_normal((8, 3, 32, 32)).astype(np.float32)
+    model = wxx.nn.ResNet18(num_classes=10)
+    model.load_state_dict(sd)
+    got = _run(model, x, is_ids=False)
+    ref = models.resnet18_forward(sd, x)
+    assert got.shape == (8, 10)
+    assert np.abs(got - ref).max() < 1e-3 * max(1.0, np.abs(ref).max())
+
+
+def test_hyena_logits_small():
+    wxx = _wxx()
+    V, D, NL, order, B, L = 64, 32, 2, 3, 2, 200
+    sd = init.hyena_state_dict(0, V, D, NL, order)
+    ids = init.token_ids(3, B, L, V)
+    model = wxx.nn.Hyena(V, d_model=D, n_layers=NL, order=order)
+    model.load_state_dict(sd)
+    got = _run(model, ids)
+    ref = models.hyena_forward(sd, ids, NL, order)
+    assert got.shape == (B, L, V)
+    assert np.abs(got - ref).max() < 1e-3
+
+
+def test_hyena_causal_and_batch_independent():
+    wxx = _wxx()
+    model = wxx.nn.Hyena(40, d_model=16, n_layers=1, order=2)
+    rng = np.random.default_rng(5)
+    ids = rng.integers(0, 40, size=(3, 64)).astype(np.uint32)
+    base = _run(model, ids)
+    ids2 = ids.copy()
+    ids2[0, 40:] = (ids2[0, 40:] + 1) % 40
+    out2 = _run(model, ids2)
+    assert np.allclose(base[0, :40], out2[0, :40], atol=1e-4)
+    assert np.allclose(base[1:], out2[1:], atol=1e-5)

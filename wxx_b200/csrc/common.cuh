@@ -1,0 +1,94 @@
+// Shared definitions for the wxx B200 kernel library (libwxx_cuda.so).
+//
+// Every exported entry point is `extern "C"`, takes plain pointers and sizes,
+// enqueues its work on the library's per-process stream and returns an int
+// status (0 = ok, negative = error).  The message of the last error is kept
+// per host thread and returned by wxx_last_error().
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+
+#define WXX_OK 0
+#define WXX_E_ARG (-1)
+#define WXX_E_CUDA (-2)
+#define WXX_E_TIMEOUT (-3)
+#define WXX_E_UNSUPPORTED (-4)
+#define WXX_E_STATE (-5)
+
+// Codes written into the device-side error word (first writer wins).
+#define WXX_DEV_ERR_MBAR_TIMEOUT 1
+#define WXX_DEV_ERR_BAD_INDEX 2
+
+#define WXX_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace wxx {
+
+void set_error(const char* fmt, ...);
+int require_init();                 // WXX_OK once wxx_init() succeeded
+cudaStream_t stream();              // library stream of the current device
+int num_sms();                      // SM count of the current device
+int* device_error_word();           // device pointer to the error word
+
+// Grid size for a grid-stride elementwise kernel: enough CTAs to fill the
+// GPU (a multiple of the SM count) but never more than the work needs.
+inline unsigned grid_for(int64_t work_items, int threads_per_cta, int ctas_per_sm = 8) {
+  int64_t need = (work_items + threads_per_cta - 1) / threads_per_cta;
+  int64_t cap = (int64_t)num_sms() * ctas_per_sm;
+  if (need < 1) need = 1;
+  return (unsigned)(need < cap ? need : cap);
+}
+
+}  // namespace wxx
+
+#define WXX_CUDA_CHECK(expr)                                                      \
+  do {                                                                            \
+    cudaError_t _wxx_e = (expr);                                                  \
+    if (_wxx_e != cudaSuccess) {                                                  \
+      wxx::set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_wxx_e), \
+                     __FILE__, __LINE__);                                         \
+      return WXX_E_CUDA;                                                          \
+    }                                                                             \
+  } while (0)
+
+#define WXX_LAUNCH_CHECK()                                                        \
+  do {                                                                            \
+    cudaError_t _wxx_e = cudaGetLastError();                                      \
+    if (_wxx_e != cudaSuccess) {                                                  \
+      wxx::set_error("kernel launch failed: %s (%s:%d)",                          \
+                     cudaGetErrorString(_wxx_e), __FILE__, __LINE__);             \
+      return WXX_E_CUDA;                                                          \
+    }                                                                             \
+  } while (0)
+
+#define WXX_REQUIRE(cond, ...)        \
+  do {                                \
+    if (!(cond)) {                    \
+      wxx::set_error(__VA_ARGS__);    \
+      return WXX_E_ARG;               \
+    }                                 \
+  } while (0)
+
+#define WXX_REQUIRE_INIT()                   \
+  do {                                       \
+    int _wxx_s = wxx::require_init();        \
+    if (_wxx_s != WXX_OK) return _wxx_s;     \
+  } while (0)
+
+// Records the first device-side error code; later errors are dropped so the
+// host sees the root cause.
+__device__ __forceinline__ void wxx_device_fail(int* err_word, int code) {
+  if (err_word) atomicCAS(err_word, 0, code);
+}
+
+// Strided view descriptor (element units) shared by the elementwise kernels.
+#define WXX_MAX_RANK 8
+struct WxxStrided {
+  int rank;
+  int64_t shape[WXX_MAX_RANK];
+  int64_t stride_a[WXX_MAX_RANK];
+  int64_t stride_b[WXX_MAX_RANK];
+  int64_t offset_a;
+  int64_t offset_b;
+};

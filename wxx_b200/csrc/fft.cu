@@ -1,0 +1,695 @@
+// Real FFTs and the fused FFT causal convolution.
+//
+// Reference semantics (functional/fft.py:484-645, fft_*.wgsl, nn/hyena.py:208-216):
+//   rfft(x, n)  = numpy.fft.rfft(x, n): zero-pad / truncate the last axis to
+//                 the power of two n, unnormalised forward transform, n/2+1 bins
+//   irfft(X, n) = numpy.fft.irfft(X, n): bins beyond the input are zero, the
+//                 imaginary parts of bins 0 and n/2 are ignored, 1/n scaling
+//   fft_conv1d  = irfft(rfft(x, n) * rfft(h, n), n)[..., :L]
+// The reference runs log2(n) radix-2 passes through global memory per
+// transform.  Here one CTA owns one row: the real signal of length n is packed
+// as a complex signal of length N = n/2 (z[m] = x[2m] + i x[2m+1]) held in
+// shared memory, transformed with in-place Stockham passes (radix-16
+// butterflies in registers, twiddles from a two-level table of N-th roots in
+// shared memory), and unpacked into the n/2+1 real-FFT bins.  The fused
+// convolution multiplies by the filter spectrum, re-packs for the inverse and
+// runs the inverse passes without the spectrum ever leaving the SM: HBM sees
+// one read of x, one read of H (L2-resident, shared by the batch) and one
+// write of y.
+//
+// Rows longer than n = 32768 (N > 16384 complex values, beyond one CTA's
+// shared memory) use the same algorithm with radix-2 Stockham passes through
+// global scratch.
+#include "common.cuh"
+
+#include <cstring>
+
+extern "C" int wxx_malloc(void** out, uint64_t nbytes);
+extern "C" int wxx_free(void* p);
+
+namespace {
+
+// ------------------------------------------------------------ complex helpers
+
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+__device__ __forceinline__ float2 cconj(float2 a) { return make_float2(a.x, -a.y); }
+__device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
+
+// Shared-memory index with one pad slot per 32 elements (breaks the
+// power-of-two strides of the first Stockham pass into distinct banks).
+__device__ __forceinline__ int pad(int i) { return i + (i >> 5); }
+
+__host__ __device__ constexpr int bitrev_c(int i, int bits) {
+  int r = 0;
+  for (int b = 0; b < bits; ++b) r |= ((i >> b) & 1) << (bits - 1 - b);
+  return r;
+}
+
+__host__ __device__ constexpr int log2_c(int r) { return r <= 1 ? 0 : 1 + log2_c(r >> 1); }
+
+// e^{-2 pi i q / 16} for q = 0..7 (the roots a radix-16 butterfly needs).
+__host__ __device__ constexpr float cos16(int q) {
+  return q == 0 ? 1.0f
+       : q == 1 ? 0.92387953251128674f
+       : q == 2 ? 0.70710678118654752f
+       : q == 3 ? 0.38268343236508978f
+       : q == 4 ? 0.0f
+       : q == 5 ? -0.38268343236508978f
+       : q == 6 ? -0.70710678118654752f
+                : -0.92387953251128674f;
+}
+__host__ __device__ constexpr float sin16(int q) {
+  return q == 0 ? 0.0f
+       : q == 1 ? 0.38268343236508978f
+       : q == 2 ? 0.70710678118654752f
+       : q == 3 ? 0.92387953251128674f
+       : q == 4 ? 1.0f
+       : q == 5 ? 0.92387953251128674f
+       : q == 6 ? 0.70710678118654752f
+                : 0.38268343236508978f;
+}
+
+// Multiplies b by e^{-+2 pi i q/16} (forward: minus), special-casing 1 and -+i.
+template <bool INV>
+__device__ __forceinline__ float2 rot16(float2 b, int q) {
+  if (q == 0) return b;
+  if (q == 4) return INV ? make_float2(-b.y, b.x) : make_float2(b.y, -b.x);
+  float c = cos16(q), s = INV ? sin16(q) : -sin16(q);
+  return make_float2(b.x * c - b.y * s, b.x * s + b.y * c);
+}
+
+// In-register radix-R DFT (R <= 16), natural order in and out.
+template <int R, bool INV>
+__device__ __forceinline__ void reg_fft(float2 (&v)[R]) {
+  constexpr int BITS = log2_c(R);
+  float2 t[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) t[bitrev_c(i, BITS)] = v[i];
+#pragma unroll
+  for (int m = 2; m <= R; m <<= 1) {
+#pragma unroll
+    for (int k = 0; k < R; k += m) {
+#pragma unroll
+      for (int j = 0; j < m / 2; ++j) {
+        float2 a = t[k + j];
+        float2 b = rot16<INV>(t[k + j + m / 2], j * (16 / m));
+        t[k + j] = cadd(a, b);
+        t[k + j + m / 2] = csub(a, b);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) v[i] = t[i];
+}
+
+struct Twiddles {
+  const float2* fine;    // e^{-2 pi i f / N}, f < F
+  const float2* coarse;  // e^{-2 pi i c F / N}, c < N / F
+  int fbits;
+};
+
+__device__ __forceinline__ float2 twiddle(const Twiddles& tw, int t) {
+  return cmul(tw.coarse[t >> tw.fbits], tw.fine[t & ((1 << tw.fbits) - 1)]);
+}
+
+// One in-place Stockham pass of radix R over N values (sub-transform size Ns
+// so far).  Each butterfly j loads buf[j + r*N/R], applies the twiddles
+// w^(r * (j mod Ns) * N/(Ns R)), runs the radix-R DFT and stores to
+// ((j - j mod Ns) * R + j mod Ns) + r*Ns.  All loads finish (barrier) before
+// any store, so a single buffer suffices.
+template <int R, int PER, int T, bool INV>
+__device__ __forceinline__ void stockham_pass(float2* buf, int N, int Ns, const Twiddles& tw) {
+  const int nb = N / R;
+  float2 v[PER][R];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    int j = threadIdx.x + p * T;
+    if (j < nb) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) v[p][r] = buf[pad(j + r * nb)];
+      int k = j & (Ns - 1);
+      if (Ns > 1) {
+        int step = N / (Ns * R);
+#pragma unroll
+        for (int r = 1; r < R; ++r) {
+          float2 w = twiddle(tw, r * k * step);
+          if (INV) w.y = -w.y;
+          v[p][r] = cmul(v[p][r], w);
+        }
+      }
+      reg_fft<R, INV>(v[p]);
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    int j = threadIdx.x + p * T;
+    if (j < nb) {
+      int k = j & (Ns - 1);
+      int d = (j - k) * R + k;
+#pragma unroll
+      for (int r = 0; r < R; ++r) buf[pad(d + r * Ns)] = v[p][r];
+    }
+  }
+  __syncthreads();
+}
+
+template <int LOGN, int T, bool INV>
+__device__ __forceinline__ void fft_smem(float2* buf, const Twiddles& tw) {
+  constexpr int N = 1 << LOGN;
+  constexpr int FULL = LOGN / 4;
+  constexpr int REM = LOGN % 4;
+  constexpr int P16 = (N / 16 + T - 1) / T > 0 ? (N / 16 + T - 1) / T : 1;
+  int Ns = 1;
+#pragma unroll 1
+  for (int i = 0; i < FULL; ++i) {
+    stockham_pass<16, P16, T, INV>(buf, N, Ns, tw);
+    Ns *= 16;
+  }
+  if constexpr (REM == 1) stockham_pass<2, (N / 2 + T - 1) / T, T, INV>(buf, N, Ns, tw);
+  if constexpr (REM == 2) stockham_pass<4, (N / 4 + T - 1) / T, T, INV>(buf, N, Ns, tw);
+  if constexpr (REM == 3) stockham_pass<8, (N / 8 + T - 1) / T, T, INV>(buf, N, Ns, tw);
+}
+
+// ------------------------------------------------------------ row kernels
+
+struct RowArgs {
+  // real input rows (modes 0, 2): element t of row (b, d) at
+  //   in[in_off + b*in_sb + d*in_sd + t*in_st], t < in_len (zero beyond)
+  const float* in;
+  int64_t in_off, in_sb, in_sd, in_st;
+  int in_len;
+  // spectrum input (mode 1): row r at spec_in[r*spec_ld], spec_len bins
+  const float2* spec_in;
+  int64_t spec_ld;
+  int spec_len;
+  // filter spectrum (mode 2): channel d at H[d*h_ld], N+1 bins
+  const float2* H;
+  int64_t h_ld;
+  // outputs: mode 0 -> spec_out[row*out_ld + k], k <= N
+  //          modes 1, 2 -> out[row*out_ld + t], t < out_len
+  float2* spec_out;
+  float* out;
+  int64_t out_ld;
+  int out_len;
+  int rows_b, rows_d;  // row (b, d) -> output row b*rows_d + d
+};
+
+constexpr int kModeRfft = 0;
+constexpr int kModeIrfft = 1;
+constexpr int kModeConv = 2;
+
+template <int LOGN>
+struct RowCfg {
+  static constexpr int N = 1 << LOGN;
+  static constexpr int T = N / 16 < 64 ? 64 : (N / 16 > 512 ? 512 : N / 16);
+  static constexpr int F = N < 128 ? N : 128;          // fine table size
+  static constexpr int FBITS = log2_c(F);
+  static constexpr int NC = N / F;                      // coarse table size
+  static constexpr int SMEM = (N + N / 32 + 1 + F + NC) * 8;
+  static constexpr int MINB = LOGN >= 14 ? 1 : 2;
+};
+
+// Unpacks Z (FFT of the packed real signal) into the real-FFT bins X[k] and
+// X[N-k] for k in [0, N/2] (thread-owned pairs).
+__device__ __forceinline__ void rfft_unpack_pair(float2 zk, float2 znk, int k, int N, float2& xk,
+                                                 float2& xnk) {
+  float2 bc = cconj(znk);
+  float2 fe = cscale(cadd(zk, bc), 0.5f);
+  float2 d = csub(zk, bc);
+  float2 fo = make_float2(0.5f * d.y, -0.5f * d.x);  // (zk - bc) / (2i)
+  float s, c;
+  sincospif(-(float)k / (float)N, &s, &c);
+  float2 wf = cmul(make_float2(c, s), fo);
+  xk = cadd(fe, wf);
+  xnk = cconj(csub(fe, wf));
+}
+
+// Packs the Hermitian spectrum pair (Y[k], Y[N-k]) into Z'[k], Z'[N-k] of the
+// length-N complex signal whose inverse FFT interleaves the real output.
+__device__ __forceinline__ void irfft_pack_pair(float2 yk, float2 ynk, int k, int N, float2& zk,
+                                                float2& znk) {
+  float2 bc = cconj(ynk);
+  float2 fe = cscale(cadd(yk, bc), 0.5f);
+  float2 d = cscale(csub(yk, bc), 0.5f);
+  float s, c;
+  sincospif((float)k / (float)N, &s, &c);  // conj(w^k), w = e^{-i pi / N}
+  float2 fo = cmul(make_float2(c, s), d);
+  zk = make_float2(fe.x - fo.y, fe.y + fo.x);     // fe + i fo
+  znk = make_float2(fe.x + fo.y, -fe.y + fo.x);   // conj(fe) + i conj(fo)
+}
+
+template <int LOGN, int MODE>
+__global__ void __launch_bounds__(RowCfg<LOGN>::T, RowCfg<LOGN>::MINB)
+    fft_row_kernel(RowArgs a) {
+  using C = RowCfg<LOGN>;
+  constexpr int N = C::N;
+  constexpr int T = C::T;
+  extern __shared__ float2 sm[];
+  float2* buf = sm;
+  float2* fine = sm + (N + N / 32 + 1);
+  float2* coarse = fine + C::F;
+  const int tid = threadIdx.x;
+
+  int d = blockIdx.x / a.rows_b;
+  int b = blockIdx.x - d * a.rows_b;
+  int64_t row = (int64_t)b * a.rows_d + d;
+
+  for (int i = tid; i < C::F; i += T) {
+    float s, c;
+    sincospif(-2.0f * (float)i / (float)N, &s, &c);
+    fine[i] = make_float2(c, s);
+  }
+  for (int i = tid; i < C::NC; i += T) {
+    float s, c;
+    sincospif(-2.0f * (float)(i * C::F) / (float)N, &s, &c);
+    coarse[i] = make_float2(c, s);
+  }
+  Twiddles tw{fine, coarse, C::FBITS};
+
+  if (MODE != kModeIrfft) {
+    const float* x = a.in + a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd;
+    const int len = a.in_len;
+    const bool vec = a.in_st == 1 && ((reinterpret_cast<uintptr_t>(x) & 7) == 0);
+    for (int m = tid; m < N; m += T) {
+      int t0 = 2 * m;
+      float2 z = make_float2(0.f, 0.f);
+      if (t0 + 1 < len) {
+        if (vec) z = *reinterpret_cast<const float2*>(x + t0);
+        else z = make_float2(x[(int64_t)t0 * a.in_st], x[(int64_t)(t0 + 1) * a.in_st]);
+      } else if (t0 < len) {
+        z.x = x[(int64_t)t0 * a.in_st];
+      }
+      buf[pad(m)] = z;
+    }
+    __syncthreads();
+    fft_smem<LOGN, T, false>(buf, tw);
+
+    if (MODE == kModeRfft) {
+      float2* X = a.spec_out + row * a.out_ld;
+      for (int k = tid; k <= N / 2; k += T) {
+        float2 zk = buf[pad(k)];
+        if (k == 0) {
+          X[0] = make_float2(zk.x + zk.y, 0.f);
+          X[N] = make_float2(zk.x - zk.y, 0.f);
+        } else {
+          float2 xk, xnk;
+          rfft_unpack_pair(zk, buf[pad(N - k)], k, N, xk, xnk);
+          X[k] = xk;
+          if (k != N - k) X[N - k] = xnk;
+        }
+      }
+      return;
+    }
+    // Fused convolution: Y = X * H, packed for the inverse transform.
+    const float2* H = a.H + (int64_t)d * a.h_ld;
+    for (int k = tid; k <= N / 2; k += T) {
+      float2 zk = buf[pad(k)];
+      if (k == 0) {
+        float y0 = (zk.x + zk.y) * H[0].x;   // bins 0 and N are real
+        float yn = (zk.x - zk.y) * H[N].x;
+        buf[pad(0)] = make_float2(0.5f * (y0 + yn), 0.5f * (y0 - yn));
+      } else {
+        float2 xk, xnk;
+        rfft_unpack_pair(zk, buf[pad(N - k)], k, N, xk, xnk);
+        float2 yk = cmul(xk, H[k]);
+        float2 ynk = cmul(xnk, H[N - k]);
+        float2 pk, pnk;
+        irfft_pack_pair(yk, ynk, k, N, pk, pnk);
+        buf[pad(k)] = pk;
+        if (k != N - k) buf[pad(N - k)] = pnk;
+      }
+    }
+  } else {
+    const float2* Y = a.spec_in + row * a.spec_ld;
+    const int len = a.spec_len;
+    for (int k = tid; k <= N / 2; k += T) {
+      float2 yk = k < len ? Y[k] : make_float2(0.f, 0.f);
+      float2 ynk = (N - k) < len ? Y[N - k] : make_float2(0.f, 0.f);
+      if (k == 0) {
+        float y0 = yk.x, yn = ynk.x;  // imaginary parts of bins 0 and N are ignored
+        buf[pad(0)] = make_float2(0.5f * (y0 + yn), 0.5f * (y0 - yn));
+      } else {
+        float2 pk, pnk;
+        irfft_pack_pair(yk, ynk, k, N, pk, pnk);
+        buf[pad(k)] = pk;
+        if (k != N - k) buf[pad(N - k)] = pnk;
+      }
+    }
+  }
+  __syncthreads();
+  fft_smem<LOGN, T, true>(buf, tw);
+
+  float* y = a.out + row * a.out_ld;
+  const float scale = 1.0f / (float)N;
+  const int olen = a.out_len;
+  const bool vec = ((reinterpret_cast<uintptr_t>(y) & 7) == 0);
+  for (int m = tid; m < N; m += T) {
+    int t0 = 2 * m;
+    if (t0 >= olen) break;
+    float2 z = cscale(buf[pad(m)], scale);
+    if (t0 + 1 < olen) {
+      if (vec) *reinterpret_cast<float2*>(y + t0) = z;
+      else { y[t0] = z.x; y[t0 + 1] = z.y; }
+    } else {
+      y[t0] = z.x;
+    }
+  }
+}
+
+// n == 1: rfft(x)[0] = x[0]; irfft(X)[0] = Re X[0]; conv = x[0] * Re H[0].
+__global__ void fft_n1_kernel(RowArgs a, int mode, int64_t rows) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int d = (int)(i / a.rows_b), b = (int)(i - (int64_t)d * a.rows_b);
+    int64_t row = (int64_t)b * a.rows_d + d;
+    if (mode == kModeIrfft) {
+      float v = a.spec_len > 0 ? a.spec_in[row * a.spec_ld].x : 0.f;
+      if (a.out_len > 0) a.out[row * a.out_ld] = v;
+      continue;
+    }
+    float x0 = a.in_len > 0 ? a.in[a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd] : 0.f;
+    if (mode == kModeRfft) a.spec_out[row * a.out_ld] = make_float2(x0, 0.f);
+    else if (a.out_len > 0) a.out[row * a.out_ld] = x0 * a.H[(int64_t)d * a.h_ld].x;
+  }
+}
+
+// ------------------------------------------------------------ global fallback (N > 16384)
+
+// z[row][m] = (x[2m], x[2m+1]) with zero padding.
+__global__ void pack_real_kernel(float2* __restrict__ z, RowArgs a, int N, int64_t rows) {
+  int64_t total = rows * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / N;
+    int m = (int)(i - r * N);
+    int d = (int)(r / a.rows_b), b = (int)(r - (int64_t)d * a.rows_b);
+    const float* x = a.in + a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd;
+    int t0 = 2 * m;
+    float2 v = make_float2(0.f, 0.f);
+    if (t0 < a.in_len) v.x = x[(int64_t)t0 * a.in_st];
+    if (t0 + 1 < a.in_len) v.y = x[(int64_t)(t0 + 1) * a.in_st];
+    z[(int64_t)(b * a.rows_d + d) * N + m] = v;
+  }
+}
+
+// One radix-2 Stockham pass over every row: dst[(j-k)*2 + k + r*Ns] from src[j + r*N/2].
+__global__ void stockham2_global_kernel(float2* __restrict__ dst, const float2* __restrict__ src,
+                                        int N, int Ns, int64_t rows, int inv) {
+  int half = N / 2;
+  int64_t total = rows * half;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / half;
+    int j = (int)(i - r * half);
+    const float2* s = src + r * N;
+    float2* o = dst + r * N;
+    float2 v0 = s[j], v1 = s[j + half];
+    int k = j & (Ns - 1);
+    if (Ns > 1) {
+      float sn, cs;
+      sincospif((inv ? 1.0f : -1.0f) * (float)k / (float)Ns, &sn, &cs);
+      v1 = cmul(v1, make_float2(cs, sn));
+    }
+    int dd = (j - k) * 2 + k;
+    o[dd] = cadd(v0, v1);
+    o[dd + Ns] = csub(v0, v1);
+  }
+}
+
+// Real-FFT unpack (mode 0) or unpack * H * repack (mode 2), one thread per pair.
+__global__ void unpack_global_kernel(float2* __restrict__ z, RowArgs a, int N, int64_t rows,
+                                     int mode) {
+  int pairs = N / 2 + 1;
+  int64_t total = rows * pairs;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / pairs;
+    int k = (int)(i - r * pairs);
+    int d = (int)(r / a.rows_b), b = (int)(r - (int64_t)d * a.rows_b);
+    int64_t row = (int64_t)b * a.rows_d + d;
+    float2* zr = z + row * N;
+    float2 zk = zr[k];
+    if (mode == kModeRfft) {
+      float2* X = a.spec_out + row * a.out_ld;
+      if (k == 0) {
+        X[0] = make_float2(zk.x + zk.y, 0.f);
+        X[N] = make_float2(zk.x - zk.y, 0.f);
+      } else {
+        float2 xk, xnk;
+        rfft_unpack_pair(zk, zr[N - k], k, N, xk, xnk);
+        X[k] = xk;
+        if (k != N - k) X[N - k] = xnk;
+      }
+    } else {
+      const float2* H = a.H + (int64_t)d * a.h_ld;
+      if (k == 0) {
+        float y0 = (zk.x + zk.y) * H[0].x, yn = (zk.x - zk.y) * H[N].x;
+        zr[0] = make_float2(0.5f * (y0 + yn), 0.5f * (y0 - yn));
+      } else {
+        float2 xk, xnk, pk, pnk;
+        rfft_unpack_pair(zk, zr[N - k], k, N, xk, xnk);
+        irfft_pack_pair(cmul(xk, H[k]), cmul(xnk, H[N - k]), k, N, pk, pnk);
+        zr[k] = pk;
+        if (k != N - k) zr[N - k] = pnk;
+      }
+    }
+  }
+}
+
+__global__ void pack_spectrum_global_kernel(float2* __restrict__ z, RowArgs a, int N,
+                                            int64_t rows) {
+  int pairs = N / 2 + 1;
+  int64_t total = rows * pairs;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = i / pairs;
+    int k = (int)(i - row * pairs);
+    const float2* Y = a.spec_in + row * a.spec_ld;
+    float2 yk = k < a.spec_len ? Y[k] : make_float2(0.f, 0.f);
+    float2 ynk = (N - k) < a.spec_len ? Y[N - k] : make_float2(0.f, 0.f);
+    float2* zr = z + row * N;
+    if (k == 0) {
+      zr[0] = make_float2(0.5f * (yk.x + ynk.x), 0.5f * (yk.x - ynk.x));
+    } else {
+      float2 pk, pnk;
+      irfft_pack_pair(yk, ynk, k, N, pk, pnk);
+      zr[k] = pk;
+      if (k != N - k) zr[N - k] = pnk;
+    }
+  }
+}
+
+__global__ void unpack_real_global_kernel(const float2* __restrict__ z, RowArgs a, int N,
+                                          int64_t rows) {
+  int64_t total = rows * N;
+  float scale = 1.0f / (float)N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = i / N;
+    int m = (int)(i - row * N);
+    int t0 = 2 * m;
+    if (t0 >= a.out_len) continue;
+    float2 v = cscale(z[row * N + m], scale);
+    float* y = a.out + row * a.out_ld;
+    y[t0] = v.x;
+    if (t0 + 1 < a.out_len) y[t0 + 1] = v.y;
+  }
+}
+
+// ------------------------------------------------------------ dispatch
+
+template <int LOGN, int MODE>
+int launch_row(const RowArgs& a, int64_t rows) {
+  using C = RowCfg<LOGN>;
+  static bool attr = false;
+  if (!attr) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(fft_row_kernel<LOGN, MODE>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr = true;
+  }
+  fft_row_kernel<LOGN, MODE><<<(unsigned)rows, C::T, C::SMEM, wxx::stream()>>>(a);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+template <int MODE>
+int launch_row_any(int logn, const RowArgs& a, int64_t rows) {
+  switch (logn) {
+    case 0: return launch_row<0, MODE>(a, rows);
+    case 1: return launch_row<1, MODE>(a, rows);
+    case 2: return launch_row<2, MODE>(a, rows);
+    case 3: return launch_row<3, MODE>(a, rows);
+    case 4: return launch_row<4, MODE>(a, rows);
+    case 5: return launch_row<5, MODE>(a, rows);
+    case 6: return launch_row<6, MODE>(a, rows);
+    case 7: return launch_row<7, MODE>(a, rows);
+    case 8: return launch_row<8, MODE>(a, rows);
+    case 9: return launch_row<9, MODE>(a, rows);
+    case 10: return launch_row<10, MODE>(a, rows);
+    case 11: return launch_row<11, MODE>(a, rows);
+    case 12: return launch_row<12, MODE>(a, rows);
+    case 13: return launch_row<13, MODE>(a, rows);
+    case 14: return launch_row<14, MODE>(a, rows);
+    default: wxx::set_error("fft: unsupported size"); return WXX_E_ARG;
+  }
+}
+
+int ilog2_exact(int64_t n) {
+  if (n < 1 || (n & (n - 1))) return -1;
+  int l = 0;
+  while ((int64_t(1) << l) < n) ++l;
+  return l;
+}
+
+constexpr int kMaxSmemLogN = 14;  // N = 16384 complex values per CTA
+
+// Runs `mode` over all rows, choosing the shared-memory or global path.
+int run_rows(int mode, int64_t n, RowArgs a, int64_t rows, const float2* Hspec) {
+  if (rows == 0) return WXX_OK;
+  cudaStream_t s = wxx::stream();
+  if (n == 1) {
+    fft_n1_kernel<<<wxx::grid_for(rows, 256), 256, 0, s>>>(a, mode, rows);
+    WXX_LAUNCH_CHECK();
+    return WXX_OK;
+  }
+  int logN = ilog2_exact(n) - 1;
+  int N = (int)(n / 2);
+  WXX_REQUIRE(rows < (int64_t(1) << 31), "fft: too many rows");
+  if (logN <= kMaxSmemLogN) {
+    if (mode == kModeRfft) return launch_row_any<kModeRfft>(logN, a, rows);
+    if (mode == kModeIrfft) return launch_row_any<kModeIrfft>(logN, a, rows);
+    return launch_row_any<kModeConv>(logN, a, rows);
+  }
+  // Global path: ping-pong scratch of rows * N complex values each.
+  (void)Hspec;
+  void* s0 = nullptr;
+  void* s1 = nullptr;
+  uint64_t bytes = (uint64_t)rows * N * sizeof(float2);
+  int st = wxx_malloc(&s0, bytes);
+  if (st) return st;
+  st = wxx_malloc(&s1, bytes);
+  if (st) { wxx_free(s0); return st; }
+  float2* cur = (float2*)s0;
+  float2* oth = (float2*)s1;
+  unsigned g = wxx::grid_for(rows * N, 256);
+  int rc = WXX_OK;
+  auto passes = [&](int inv) {
+    for (int Ns = 1; Ns < N; Ns *= 2) {
+      stockham2_global_kernel<<<g, 256, 0, s>>>(oth, cur, N, Ns, rows, inv);
+      float2* t = cur; cur = oth; oth = t;
+    }
+  };
+  if (mode != kModeIrfft) {
+    pack_real_kernel<<<g, 256, 0, s>>>(cur, a, N, rows);
+    passes(0);
+    unpack_global_kernel<<<g, 256, 0, s>>>(cur, a, N, rows, mode == kModeRfft ? kModeRfft : kModeConv);
+  } else {
+    pack_spectrum_global_kernel<<<g, 256, 0, s>>>(cur, a, N, rows);
+  }
+  if (mode != kModeRfft) {
+    passes(1);
+    unpack_real_global_kernel<<<g, 256, 0, s>>>(cur, a, N, rows);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    wxx::set_error("fft global path launch failed: %s", cudaGetErrorString(e));
+    rc = WXX_E_CUDA;
+  }
+  wxx_free(s0);
+  wxx_free(s1);
+  return rc;
+}
+
+}  // namespace
+
+// X[r, k] (c64, row stride out_ld complex) = rfft(x[r, :in_len], n), k <= n/2.
+// x rows are dense with row stride in_ld floats.
+WXX_EXPORT int wxx_rfft(void* X, int64_t out_ld, const float* x, int64_t in_ld, int64_t rows,
+                        int64_t in_len, int64_t n) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(ilog2_exact(n) >= 0, "wxx_rfft: n=%lld is not a positive power of two", (long long)n);
+  WXX_REQUIRE(n <= (int64_t(1) << 30), "wxx_rfft: n too large");
+  RowArgs a;
+  memset(&a, 0, sizeof(a));
+  a.in = x;
+  a.in_sb = in_ld;
+  a.in_st = 1;
+  a.in_len = (int)in_len;
+  a.spec_out = (float2*)X;
+  a.out_ld = out_ld;
+  a.rows_b = (int)rows;
+  a.rows_d = 1;
+  // row (b, d=0) -> output row b
+  return run_rows(kModeRfft, n, a, rows, nullptr);
+}
+
+// y[r, t] (row stride out_ld floats, t < n) = irfft(X[r, :in_len], n).
+WXX_EXPORT int wxx_irfft(float* y, int64_t out_ld, const void* X, int64_t in_ld, int64_t rows,
+                         int64_t in_len, int64_t n) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(ilog2_exact(n) >= 0, "wxx_irfft: n=%lld is not a positive power of two", (long long)n);
+  WXX_REQUIRE(n <= (int64_t(1) << 30), "wxx_irfft: n too large");
+  RowArgs a;
+  memset(&a, 0, sizeof(a));
+  a.spec_in = (const float2*)X;
+  a.spec_ld = in_ld;
+  a.spec_len = (int)in_len;
+  a.out = y;
+  a.out_ld = out_ld;
+  a.out_len = (int)n;
+  a.rows_b = (int)rows;
+  a.rows_d = 1;
+  return run_rows(kModeIrfft, n, a, rows, nullptr);
+}
+
+// Causal FFT convolution with a precomputed filter spectrum:
+//   y[b, d, t] = irfft(rfft(x[b, d, :], n) * H[d, :], n)[t],  t < out_len
+// x is a strided (B, D, L) view (element strides sb, sd, sl from x_off);
+// H is (D, n/2+1) c64 with row stride h_ld; y is dense (B, D, out_len).
+WXX_EXPORT int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int64_t sb,
+                                    int64_t sd, int64_t sl, const void* H, int64_t h_ld, int B,
+                                    int D, int L, int64_t n, int out_len) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(ilog2_exact(n) >= 0, "wxx_fftconv: n=%lld is not a positive power of two", (long long)n);
+  WXX_REQUIRE(out_len >= 0 && out_len <= n, "wxx_fftconv: out_len must be in [0, n]");
+  RowArgs a;
+  memset(&a, 0, sizeof(a));
+  a.in = x;
+  a.in_off = x_off;
+  a.in_sb = sb;
+  a.in_sd = sd;
+  a.in_st = sl;
+  a.in_len = L;
+  a.H = (const float2*)H;
+  a.h_ld = h_ld;
+  a.out = y;
+  a.out_ld = out_len;
+  a.out_len = out_len;
+  a.rows_b = B;
+  a.rows_d = D;
+  return run_rows(kModeConv, n, a, (int64_t)B * D, (const float2*)H);
+}
+
+// Causal FFT convolution with a time-domain filter h (D, Lh) (dense, row
+// stride h_ld floats): computes H = rfft(h, n) into a temporary and runs
+// wxx_fftconv_spectrum.  This is Hyena's fft_conv1d (nn/hyena.py:208-216):
+//   y = irfft(rfft(x, n) * rfft(h, n), n)[..., :out_len]
+WXX_EXPORT int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                           int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D, int L,
+                           int64_t n, int out_len) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(ilog2_exact(n) >= 0, "wxx_fftconv: n=%lld is not a positive power of two", (long long)n);
+  int64_t bins = n / 2 + 1;
+  void* Hs = nullptr;
+  int st = wxx_malloc(&Hs, (uint64_t)D * bins * sizeof(float2));
+  if (st) return st;
+  st = wxx_rfft(Hs, bins, h, h_ld, D, Lh, n);
+  if (st == WXX_OK) st = wxx_fftconv_spectrum(y, x, x_off, sb, sd, sl, Hs, bins, B, D, L, n, out_len);
+  int st2 = wxx_free(Hs);
+  return st ? st : st2;
+}

@@ -1,0 +1,312 @@
+// Matmul and conv2d entry points on the tcgen05 GEMM engine (tc_gemm.cuh),
+// plus an exact-fp32 SIMT kernel (mode 2) used as a cross-check and for
+// callers that ask for full fp32 products.
+//
+// Reference: functional.matmul_add (functional/utils.py:378-499, matmul.wgsl)
+//   C[b] = op(A[b]) @ op(B[b]) (+ bias), bias modes 0 none, 1 (N,), 2 (M,N),
+//   3 (batch,M,N); an unbatched operand broadcasts (batch stride 0).
+// Reference: functional.conv2d (functional/convolution.py:658-729, conv2d.wgsl)
+//   NCHW cross-correlation as an implicit GEMM: rows = B*Ho*Wo output pixels,
+//   columns = Cout, K = Cin*KH*KW.
+#include "tc_gemm.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+using namespace wxx_tc;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// Encodes a 3-D fp32 tensor map {inner, outer, batch} with a {32, box_outer, 1}
+// box.  K-major operands use the 128-byte swizzle with 16-byte chunks;
+// MN-major operands (mn_major) the 128-byte swizzle with 32-byte chunks, the
+// only shared-memory layout tcgen05 accepts for MN-major tf32.  Returns false
+// when TMA cannot address the operand (alignment), so the caller gathers it.
+bool encode_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer,
+                uint64_t batch, uint64_t ld_elems, uint64_t bs_elems, uint32_t box_outer,
+                bool mn_major) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld_elems * 4) % 16) return false;
+  if (batch > 1 && (bs_elems * 4) % 16) return false;
+  if (inner == 0 || outer == 0 || batch == 0) return false;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  cuuint64_t strides[2] = {ld_elems * 4, (batch > 1 ? bs_elems : ld_elems * outer) * 4};
+  cuuint32_t box[3] = {32, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Describes a GEMM operand: `mn` rows (M for A, N for B) by K, batch-strided.
+// k_contig: element (row, k) at row*ld + k; otherwise at k*ld + row.
+struct OperandDesc {
+  const float* base;
+  int64_t rows, K, batch, ld, bs;
+  bool k_contig;
+  bool bcast;
+};
+
+// Fills `src` (and the tensor map when TMA can be used).
+void setup_operand(const OperandDesc& d, int box_rows, bool allow_tma, OperandSrc& src,
+                   CUtensorMap* map) {
+  memset(&src, 0, sizeof(src));
+  src.bcast_batch = d.bcast ? 1 : 0;
+  int64_t nb = d.bcast ? 1 : d.batch;
+  bool tma = false;
+  if (allow_tma) {
+    if (d.k_contig) {
+      tma = encode_map(map, d.base, (uint64_t)d.K, (uint64_t)d.rows, (uint64_t)nb, (uint64_t)d.ld,
+                       (uint64_t)d.bs, (uint32_t)box_rows, false);
+      src.kind = 0;
+    } else {
+      tma = encode_map(map, d.base, (uint64_t)d.rows, (uint64_t)d.K, (uint64_t)nb, (uint64_t)d.ld,
+                       (uint64_t)d.bs, 32u, true);
+      src.kind = 1;
+    }
+  }
+  if (!tma) {
+    src.kind = 2;
+    src.base = d.base;
+    src.bs = d.bcast ? 0 : d.bs;
+    src.s_row = d.k_contig ? d.ld : 1;
+    src.s_k = d.k_contig ? 1 : d.ld;
+    src.rows_total = (int)d.rows;
+    src.k_total = (int)d.K;
+  }
+}
+
+template <int BN>
+int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+              const CUtensorMap& b1, GemmParams& p) {
+  using C = Cfg<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<BN>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM_BYTES));
+    attr_set = true;
+  }
+  p.tiles_m = (p.M + BM - 1) / BM;
+  p.tiles_n = (p.N + BN - 1) / BN;
+  int64_t tiles = (int64_t)p.batch * p.tiles_m * p.tiles_n;
+  WXX_REQUIRE(tiles < (int64_t(1) << 31), "gemm: too many tiles");
+  int grid = (int)(tiles < wxx::num_sms() ? tiles : wxx::num_sms());
+  tc_gemm_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, p);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+int pick_bn(int64_t M, int64_t N, int64_t batch) {
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  // Prefer 256-wide tiles (lower shared-memory traffic per MMA) unless that
+  // leaves most SMs idle.
+  int64_t t256 = batch * ((M + 127) / 128) * ((N + 255) / 256);
+  if (t256 >= wxx::num_sms() / 2) return 256;
+  return 128;
+}
+
+int run_tc(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+           const CUtensorMap& b1, GemmParams& p) {
+  switch (bn) {
+    case 64: return launch_tc<64>(a0, a1, b0, b1, p);
+    case 128: return launch_tc<128>(a0, a1, b0, b1, p);
+    default: return launch_tc<256>(a0, a1, b0, b1, p);
+  }
+}
+
+// ------------------------------------------------------------ exact fp32 SIMT
+
+// 64x64 output tile, K-step 16, 4x4 outputs per thread, fp32 FMA.
+__global__ void __launch_bounds__(256) simt_gemm_kernel(
+    float* __restrict__ C, const float* __restrict__ A, const float* __restrict__ B,
+    const float* __restrict__ bias, int M, int N, int K, int64_t a_bs, int64_t b_bs, int64_t lda,
+    int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha) {
+  __shared__ float As[16][68];
+  __shared__ float Bs[16][68];
+  int bt = blockIdx.z;
+  const float* Ab = A + (int64_t)bt * a_bs;
+  const float* Bb = B + (int64_t)bt * b_bs;
+  int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+      int kk = e / 64, mm = e % 64;
+      int m = m0 + mm, k = k0 + kk;
+      float v = 0.f;
+      if (m < M && k < K) v = trans_a ? Ab[(int64_t)k * lda + m] : Ab[(int64_t)m * lda + k];
+      As[kk][mm] = v;
+      int n = n0 + mm;
+      float w = 0.f;
+      if (n < N && k < K) w = trans_b ? Bb[(int64_t)n * ldb + k] : Bb[(int64_t)k * ldb + n];
+      Bs[kk][mm] = w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  for (int i = 0; i < 4; ++i) {
+    int m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+    for (int j = 0; j < 4; ++j) {
+      int n = n0 + tx * 4 + j;
+      if (n >= N) continue;
+      float o = acc[i][j] * alpha;
+      if (bias_mode == 1) o += bias[n];
+      else if (bias_mode == 2) o += bias[(int64_t)m * N + n];
+      else if (bias_mode == 3) o += bias[(int64_t)bt * M * N + (int64_t)m * N + n];
+      C[(int64_t)bt * M * N + (int64_t)m * N + n] = o;
+    }
+  }
+}
+
+}  // namespace
+
+// C (dense [batch, M, N]) = alpha * op(A) @ op(B) (+ bias).
+//   A: trans_a = 0 -> element (m, k) at A[b*a_bs + m*lda + k]; 1 -> A[b*a_bs + k*lda + m]
+//   B: trans_b = 0 -> element (k, n) at B[b*b_bs + k*ldb + n]; 1 -> B[b*b_bs + n*ldb + k]
+//   a_bs / b_bs = 0 broadcasts that operand over the batch.
+//   bias_mode: 0 none, 1 bias[n], 2 bias[m*N + n], 3 bias[b*M*N + m*N + n]
+//   mode: 0 TF32 tensor cores, 1 3xTF32 tensor cores (fp32-faithful), 2 fp32 SIMT.
+WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float* bias,
+                          int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_bs,
+                          int64_t b_bs, int64_t lda, int64_t ldb, int trans_a, int trans_b,
+                          int bias_mode, float alpha, int mode) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "wxx_matmul: negative size");
+  WXX_REQUIRE(mode >= 0 && mode <= 2, "wxx_matmul: mode %d not in 0..2", mode);
+  WXX_REQUIRE(bias_mode >= 0 && bias_mode <= 3, "wxx_matmul: bias_mode %d not in 0..3", bias_mode);
+  WXX_REQUIRE(bias_mode == 0 || bias != nullptr, "wxx_matmul: bias_mode %d needs a bias", bias_mode);
+  WXX_REQUIRE(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31),
+              "wxx_matmul: dimension exceeds 2^31");
+  if (batch * M * N == 0) return WXX_OK;
+  cudaStream_t s = wxx::stream();
+  if (K == 0) {
+    // Empty reduction: C = bias (or 0).
+    WXX_CUDA_CHECK(cudaMemsetAsync(C, 0, batch * M * N * sizeof(float), s));
+    if (bias_mode == 0) return WXX_OK;
+    mode = 2;  // the SIMT kernel adds the bias to the zero product
+  }
+  if (mode == 2) {
+    WXX_REQUIRE(batch <= 65535, "wxx_matmul: SIMT path supports batch <= 65535");
+    dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), (unsigned)batch);
+    simt_gemm_kernel<<<grid, 256, 0, s>>>(C, A, B, bias, (int)M, (int)N, (int)K, a_bs, b_bs, lda,
+                                         ldb, trans_a, trans_b, bias_mode, alpha);
+    WXX_LAUNCH_CHECK();
+    return WXX_OK;
+  }
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = (int)batch;
+  p.num_kb = (int)((K + BK - 1) / BK);
+  p.passes = mode == 1 ? 3 : 1;
+  p.err = wxx::device_error_word();
+  int bn = pick_bn(M, N, batch);
+  CUtensorMap ma0, ma1, mb0, mb1;
+  memset(&ma0, 0, sizeof(ma0));
+  memset(&mb0, 0, sizeof(mb0));
+  // 3xTF32 splits operands while gathering them, so it always uses the
+  // gather producers; TF32 uses TMA wherever the operand is 16-byte addressable.
+  bool allow_tma = (mode == 0);
+  OperandDesc da{A, M, K, batch, lda, a_bs, trans_a == 0, a_bs == 0 && batch > 1};
+  OperandDesc db{B, N, K, batch, ldb, b_bs, trans_b != 0, b_bs == 0 && batch > 1};
+  setup_operand(da, BM, allow_tma, p.a, &ma0);
+  setup_operand(db, bn, allow_tma, p.b, &mb0);
+  ma1 = ma0;
+  mb1 = mb0;
+  p.epi.kind = 0;
+  p.epi.C = C;
+  p.epi.c_bs = M * N;
+  p.epi.ldc = (int)N;
+  p.epi.bias = bias;
+  p.epi.bias_mode = bias_mode;
+  p.epi.bias_bs = M * N;
+  p.epi.alpha = alpha;
+  return run_tc(bn, ma0, ma1, mb0, mb1, p);
+}
+
+// Y (NCHW [B, Cout, Ho, Wo]) = conv2d(X [B, Cin, H, W], Wt [Cout, Cin, KH, KW]) (+ bias[Cout])
+// with stride (sh, sw), padding (ph, pw), dilation (dh, dw);
+// Ho = (H + 2ph - dh(KH-1) - 1)/sh + 1.  mode: 0 TF32, 1 3xTF32, 2 fp32 (3xTF32 path).
+WXX_EXPORT int wxx_conv2d(float* Y, const float* X, const float* Wt, const float* bias, int B,
+                          int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw, int ph,
+                          int pw, int dh, int dw, int mode) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(B >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0 && KH > 0 && KW > 0,
+              "wxx_conv2d: bad sizes");
+  WXX_REQUIRE(sh > 0 && sw > 0 && dh > 0 && dw > 0 && ph >= 0 && pw >= 0,
+              "wxx_conv2d: bad stride/padding/dilation");
+  int Ho = (H + 2 * ph - dh * (KH - 1) - 1) / sh + 1;
+  int Wo = (W + 2 * pw - dw * (KW - 1) - 1) / sw + 1;
+  WXX_REQUIRE(Ho > 0 && Wo > 0, "wxx_conv2d: empty output");
+  int64_t Mrows = (int64_t)B * Ho * Wo;
+  int64_t K = (int64_t)Cin * KH * KW;
+  WXX_REQUIRE(Mrows < (int64_t(1) << 31) && K < (int64_t(1) << 31), "wxx_conv2d: too large");
+  if (Mrows == 0) return WXX_OK;
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = (int)Mrows;
+  p.N = Cout;
+  p.K = (int)K;
+  p.batch = 1;
+  p.num_kb = (int)((K + BK - 1) / BK);
+  p.passes = mode == 0 ? 1 : 3;
+  p.err = wxx::device_error_word();
+  int bn = pick_bn(Mrows, Cout, 1);
+  CUtensorMap ma, mb;
+  memset(&ma, 0, sizeof(ma));
+  memset(&mb, 0, sizeof(mb));
+  // A: im2col gather.
+  p.a.kind = 3;
+  p.a.base = X;
+  p.a.rows_total = (int)Mrows;
+  p.a.k_total = (int)K;
+  p.a.cin = Cin; p.a.h = H; p.a.w = W; p.a.kh = KH; p.a.kw = KW;
+  p.a.sh = sh; p.a.sw = sw; p.a.ph = ph; p.a.pw = pw; p.a.dh = dh; p.a.dw = dw;
+  p.a.ho = Ho; p.a.wo = Wo;
+  // B: weights as [Cout, K] K-major.
+  OperandDesc db{Wt, Cout, K, 1, K, 0, true, false};
+  setup_operand(db, bn, mode == 0, p.b, &mb);
+  p.epi.kind = 1;
+  p.epi.C = Y;
+  p.epi.bias = bias;
+  p.epi.bias_mode = bias ? 1 : 0;
+  p.epi.alpha = 1.0f;
+  p.epi.hw_out = Ho * Wo;
+  return run_tc(bn, ma, ma, mb, mb, p);
+}

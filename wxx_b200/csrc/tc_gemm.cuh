@@ -1,0 +1,626 @@
+// tcgen05 / TMEM GEMM engine for sm_100a (TF32 tensor cores, fp32 accumulate).
+//
+// One persistent, warp-specialised kernel template computes
+//   D[tile] = sum_k A[m, k] * B[n, k]
+// for 128 x BN output tiles (BN = 64, 128 or 256) with a BK = 32 (128-byte)
+// K-block pipeline:
+//   warp 0        TMA producer: cp.async.bulk.tensor loads into 128B-swizzled
+//                 shared memory (no multicast), expect-tx on the stage barrier
+//   warp 1        TMEM allocator + single-thread tcgen05.mma issuer
+//                 (kind::tf32, M = 128, N = BN, K = 8 per instruction),
+//                 tcgen05.commit frees smem stages and publishes accumulators
+//   warps 2..5    epilogue: tcgen05.ld 32x32b from TMEM -> registers ->
+//                 bias / scale -> global memory
+//   warps 6..9    gather producers for operands that TMA cannot address
+//                 (rows not 16-byte aligned, im2col of a convolution):
+//                 ld.global -> st.shared in the same swizzled layout, then
+//                 fence.proxy.async and an mbarrier arrive
+// Two TMEM accumulator buffers (2 x BN columns) let the epilogue of tile i
+// overlap the main loop of tile i+1.
+//
+// Every mbarrier wait is bounded (wall-clock limit read from %globaltimer):
+// on expiry the waiting role records WXX_DEV_ERR_MBAR_TIMEOUT in the device
+// error word, raises a CTA-wide abort flag and leaves its loop; before the
+// CTA exits the producer drains its outstanding TMA transactions and the MMA
+// warp drains its outstanding tensor-core work, then TMEM is released.
+#pragma once
+
+#include "common.cuh"
+
+#include <cuda.h>
+
+namespace wxx_tc {
+
+constexpr int BM = 128;          // tile rows (UMMA M, one TMEM lane per row)
+constexpr int BK = 32;           // fp32 elements per K-block = one 128 B swizzle row
+constexpr int UMMA_K = 8;        // K per tcgen05.mma kind::tf32
+constexpr int NUM_THREADS = 320; // 10 warps
+constexpr int EPI_WARP0 = 2;
+constexpr int GATHER_WARP0 = 6;
+constexpr int GATHER_THREADS = 128;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 4;                 // 16 KB
+  static constexpr int B_BYTES = BN * BK * 4;                 // 8/16/32 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 4 / 6 / 8
+  static constexpr int TMEM_COLS = 2 * BN;                    // 128 / 256 / 512
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+};
+
+// ------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity.  Returns false when the
+// wall-clock limit expired or another role raised the abort flag.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag, int* err) {
+  uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((it & 255) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        wxx_device_fail(err, WXX_DEV_ERR_MBAR_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread t of the warp gets row
+// (lane base + t), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld_32x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (sm100 layout): start>>4 [0,14),
+// LBO>>4 [16,30), SBO>>4 [32,46), version 1 at [46,48), layout type at [61,64):
+// 2 = SWIZZLE_128B (16-byte chunks), 1 = SWIZZLE_128B_BASE32B (32-byte chunks).
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                          uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+
+// K-major tile: rows of 128 B (32 fp32 k-values), 8-row 1024 B swizzle atoms
+// (SBO); one MMA K-step (8 values = 32 B) advances the start address.
+__device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t tile, int kk) {
+  return sdesc(tile + kk * 32, 16, 1024, kLayoutSW128);
+}
+
+// MN-major tile (tf32 must use the 32-byte-atom 128B swizzle): each 32-wide
+// MN chunk is a TMA box of 32 k-rows x 128 B (4096 B apart: LBO); swizzle
+// atoms are 4 k-rows (512 B: SBO); one MMA K-step covers 8 rows (1024 B).
+__device__ __forceinline__ uint64_t sdesc_mnmajor(uint32_t tile, int kk) {
+  return sdesc(tile + kk * 1024, 4096, 512, kLayoutSW128Base32B);
+}
+
+// Instruction descriptor for kind::tf32: D f32, A/B tf32, M=128, N=BN.
+__host__ __device__ constexpr uint32_t idesc_tf32(int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// Byte offset of element (row, k) of a K-major 128B-swizzled tile
+// (rows of 128 B = 32 fp32 k-values, 8-row atoms of 1024 B).
+__device__ __forceinline__ uint32_t kmajor_offset(int row, int k) {
+  return (uint32_t)(row * 128 + ((((k >> 2) ^ (row & 7)) & 7) << 4) + ((k & 3) << 2));
+}
+
+// ------------------------------------------------------------ operand sources
+
+// How one operand tile (rows x 32 k) reaches shared memory.
+//   kind 0: TMA, K-major global (k contiguous): one box {32, rows}
+//   kind 1: TMA, MN-major global (rows contiguous): rows/32 boxes {32, 32}
+//   kind 2: gather, generic strided matrix
+//   kind 3: gather, im2col of an NCHW convolution input (A operand only)
+struct OperandSrc {
+  int kind;
+  int bcast_batch;        // TMA: batch coordinate always 0
+  // gather (kind 2): element (row, k) of batch b at base + b*bs + row*s_row + k*s_k
+  const float* base;
+  int64_t bs, s_row, s_k;
+  int rows_total;         // valid rows (M or N)
+  int k_total;            // valid K
+  // im2col (kind 3)
+  int cin, h, w, kh, kw, sh, sw, ph, pw, dh, dw, ho, wo;
+};
+
+struct EpiParams {
+  int kind;               // 0 = row-major matrix C, 1 = NCHW convolution output
+  float* C;
+  int64_t c_bs;           // batch stride of C (elements)
+  int ldc;                // row stride of C (elements), kind 0
+  const float* bias;
+  int bias_mode;          // 0 none, 1 (N,), 2 (M,N), 3 (batch,M,N); conv: 1 = per channel
+  int64_t bias_bs;
+  float alpha;
+  int hw_out;             // conv: Ho*Wo
+};
+
+struct GemmParams {
+  int M, N, K;
+  int batch;
+  int tiles_m, tiles_n;
+  int num_kb;             // K-blocks per pass
+  int passes;             // 1 = TF32; 3 = 3xTF32 (hi*lo, lo*hi, hi*hi)
+  OperandSrc a, b;
+  EpiParams epi;
+  int* err;
+};
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& bt, int& tm, int& tn) {
+  tm = t % p.tiles_m;
+  int r = t / p.tiles_m;
+  tn = r % p.tiles_n;
+  bt = r / p.tiles_n;
+}
+
+// 3xTF32 operand parts: the tensor core reads the top 19 bits of each fp32
+// word, so x = hi + lo with hi = x with the low 13 mantissa bits cleared and
+// lo = x - hi (exact in fp32); lo itself is then read to tf32 precision.
+__device__ __forceinline__ float split_part(float x, int part) {
+  if (part == 0) return x;
+  float hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  return part == 1 ? hi : x - hi;
+}
+
+// Gather `rows` x 32 fp32 values into a K-major swizzled tile (rows % 8 == 0).
+// Executed by the GATHER_THREADS producer threads.  part: 0 raw, 1 hi, 2 lo.
+__device__ __forceinline__ void gather_tile(const OperandSrc& s, uint8_t* dst, int rows, int row0,
+                                            int k0, int batch, int gtid, int part) {
+  if (s.kind == 2) {
+    const float* base = s.base + (int64_t)batch * s.bs;
+    if (s.s_k == 1) {
+      // lanes along k (coalesced), threads over rows, 8 loads in flight
+      int k = gtid & 31;
+      int kg = k0 + k;
+      bool kvalid = kg < s.k_total;
+      for (int r0 = gtid >> 5; r0 < rows; r0 += 8 * (GATHER_THREADS / 32)) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          int r = r0 + u * (GATHER_THREADS / 32);
+          int row = row0 + r;
+          v[u] = (r < rows && row < s.rows_total && kvalid)
+                     ? __ldg(base + (int64_t)row * s.s_row + kg)
+                     : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          int r = r0 + u * (GATHER_THREADS / 32);
+          if (r < rows) *reinterpret_cast<float*>(dst + kmajor_offset(r, k)) = split_part(v[u], part);
+        }
+      }
+    } else {
+      // lanes along rows (coalesced when s_row == 1), 8 loads in flight
+      const int total = rows * BK;
+      for (int e0 = gtid; e0 < total; e0 += 8 * GATHER_THREADS) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          int e = e0 + u * GATHER_THREADS;
+          int r = e % rows, k = e / rows;
+          int row = row0 + r, kg = k0 + k;
+          v[u] = (e < total && row < s.rows_total && kg < s.k_total)
+                     ? __ldg(base + (int64_t)row * s.s_row + (int64_t)kg * s.s_k)
+                     : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          int e = e0 + u * GATHER_THREADS;
+          if (e < total) {
+            int r = e % rows, k = e / rows;
+            *reinterpret_cast<float*>(dst + kmajor_offset(r, k)) = split_part(v[u], part);
+          }
+        }
+      }
+    }
+  } else {
+    // im2col: row = output pixel (b, oh, ow); k = (c, r, q) over the filter.
+    const int khw = s.kh * s.kw;
+    for (int r = gtid; r < rows; r += GATHER_THREADS) {
+      int m = row0 + r;
+      bool mvalid = m < s.rows_total;
+      int ow = 0, oh = 0, b = 0;
+      if (mvalid) {
+        ow = m % s.wo;
+        int t = m / s.wo;
+        oh = t % s.ho;
+        b = t / s.ho;
+      }
+      const int ih0 = oh * s.sh - s.ph, iw0 = ow * s.sw - s.pw;
+      const float* xb = s.base + (int64_t)b * s.cin * s.h * s.w;
+#pragma unroll 4
+      for (int k = 0; k < BK; ++k) {
+        int kg = k0 + k;
+        float v = 0.f;
+        if (mvalid && kg < s.k_total) {
+          int c = kg / khw;
+          int rem = kg - c * khw;
+          int fr = rem / s.kw, fq = rem - fr * s.kw;
+          int ih = ih0 + fr * s.dh, iw = iw0 + fq * s.dw;
+          if (ih >= 0 && ih < s.h && iw >= 0 && iw < s.w)
+            v = __ldg(xb + ((int64_t)c * s.h + ih) * s.w + iw);
+        }
+        *reinterpret_cast<float*>(dst + kmajor_offset(r, k)) = split_part(v, part);
+      }
+    }
+  }
+}
+
+// Epilogue store of one thread's row segment: row m, columns n0..n0+31.
+__device__ __forceinline__ void epi_store(const GemmParams& p, int bt, int m, int n0,
+                                          float (&v)[32]) {
+  const EpiParams& e = p.epi;
+  if (m >= p.M) return;
+  if (e.kind == 0) {
+    float* crow = e.C + (int64_t)bt * e.c_bs + (int64_t)m * e.ldc;
+    const float* brow = nullptr;
+    if (e.bias_mode == 1) brow = e.bias;
+    else if (e.bias_mode == 2) brow = e.bias + (int64_t)m * p.N;
+    else if (e.bias_mode == 3) brow = e.bias + (int64_t)bt * e.bias_bs + (int64_t)m * p.N;
+    bool full = (n0 + 32 <= p.N) && ((e.ldc & 3) == 0) &&
+                ((reinterpret_cast<uintptr_t>(crow + n0) & 15) == 0);
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 o;
+        o.x = v[j] * e.alpha;
+        o.y = v[j + 1] * e.alpha;
+        o.z = v[j + 2] * e.alpha;
+        o.w = v[j + 3] * e.alpha;
+        if (brow) {
+          o.x += brow[n0 + j];
+          o.y += brow[n0 + j + 1];
+          o.z += brow[n0 + j + 2];
+          o.w += brow[n0 + j + 3];
+        }
+        *reinterpret_cast<float4*>(crow + n0 + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        int n = n0 + j;
+        if (n < p.N) {
+          float o = v[j] * e.alpha;
+          if (brow) o += brow[n];
+          crow[n] = o;
+        }
+      }
+    }
+  } else {
+    // NCHW: row m = (b, pixel), column n = output channel.
+    int b = m / e.hw_out, pix = m - b * e.hw_out;
+    float* out = e.C + (int64_t)b * p.N * e.hw_out + pix;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      int n = n0 + j;
+      if (n < p.N) {
+        float o = v[j] * e.alpha;
+        if (e.bias_mode == 1) o += e.bias[n];
+        out[(int64_t)n * e.hw_out] = o;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0,
+                   const __grid_constant__ CUtensorMap tm_a1,
+                   const __grid_constant__ CUtensorMap tm_b0,
+                   const __grid_constant__ CUtensorMap tm_b1, const GemmParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const bool a_gather = p.a.kind >= 2;
+  const bool b_gather = p.b.kind >= 2;
+  const bool any_gather = a_gather || b_gather;
+  const int total_tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int total_kb = p.num_kb * p.passes;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1 + (any_gather ? GATHER_THREADS : 0));
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull_bar[s], 1);
+      mbar_init(&tempty_bar[s], 4 * 32);
+    }
+    mbar_init(&drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    if (p.a.kind < 2) { prefetch_tmap(&tm_a0); if (p.passes > 1) prefetch_tmap(&tm_a1); }
+    if (p.b.kind < 2) { prefetch_tmap(&tm_b0); if (p.passes > 1) prefetch_tmap(&tm_b1); }
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t tx_bytes = (a_gather ? 0 : C::A_BYTES) + (b_gather ? 0 : C::B_BYTES);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int bt, tm, tn;
+        tile_coords(p, t, bt, tm, tn);
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          int pass = kb / p.num_kb;
+          int kc = (kb - pass * p.num_kb) * BK;
+          // pass order for 3xTF32: (hi, lo), (lo, hi), (hi, hi)
+          const CUtensorMap* ma = (p.passes > 1 && pass == 1) ? &tm_a1 : &tm_a0;
+          const CUtensorMap* mb = (p.passes > 1 && pass == 0) ? &tm_b1 : &tm_b0;
+          mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
+          if (!a_gather) {
+            int zb = p.a.bcast_batch ? 0 : bt;
+            if (p.a.kind == 0) {
+              tma_load_3d(smem_u32(sa), ma, &full_bar[stage], kc, tm * BM, zb);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BM / 32; ++j)
+                tma_load_3d(smem_u32(sa + j * 4096), ma, &full_bar[stage], tm * BM + j * 32, kc, zb);
+            }
+          }
+          if (!b_gather) {
+            int zb = p.b.bcast_batch ? 0 : bt;
+            if (p.b.kind == 0) {
+              tma_load_3d(smem_u32(sb), mb, &full_bar[stage], kc, tn * BN, zb);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_3d(smem_u32(sb + j * 4096), mb, &full_bar[stage], tn * BN + j * 32, kc, zb);
+            }
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: every stage we issued must have completed before the CTA exits.
+      volatile int dummy_abort = 0;
+      for (int s = 0; s < C::STAGES; ++s)
+        if (issued_mask & (1u << s))
+          mbar_wait(&full_bar[s], (issued_parity >> s) & 1, &dummy_abort, p.err);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const bool a_mn = (p.a.kind == 1);
+      const bool b_mn = (p.b.kind == 1);
+      const uint32_t idesc = idesc_tf32(BN, a_mn, b_mn);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        int acc = local & 1;
+        uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, &abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            uint64_t ad = a_mn ? sdesc_mnmajor(sa, kk) : sdesc_kmajor(sa, kk);
+            uint64_t bd = b_mn ? sdesc_mnmajor(sb, kk) : sdesc_kmajor(sb, kk);
+            umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+      }
+      // Drain all tensor-core work issued by this thread before TMEM is freed.
+      umma_commit(&drain_bar);
+      volatile int dummy_abort = 0;
+      mbar_wait(&drain_bar, 0, &dummy_abort, p.err);
+    }
+  } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
+    // ---------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    int local = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      int bt, tm, tn;
+      tile_coords(p, t, bt, tm, tn);
+      int acc = local & 1;
+      uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, p.err)) break;
+      tc_fence_after();
+      int m = tm * BM + quarter * 32 + lane;
+      uint32_t row_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld_32x32(row_addr + (uint32_t)c, v);
+        int n0 = tn * BN + c;
+        if (n0 < p.N) epi_store(p, bt, m, n0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+    }
+  } else if (warp >= GATHER_WARP0 && any_gather) {
+    // ---------------------------------------------------- gather producers
+    const int gtid = threadIdx.x - GATHER_WARP0 * 32;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      int bt, tm, tn;
+      tile_coords(p, t, bt, tm, tn);
+      for (int kb = 0; kb < total_kb; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
+        uint8_t* sa = smem + stage * C::STAGE_BYTES;
+        uint8_t* sb = sa + C::A_BYTES;
+        int pass = kb / p.num_kb;
+        int kc = (kb - pass * p.num_kb) * BK;
+        // 3xTF32 pass order: (A hi, B lo), (A lo, B hi), (A hi, B hi)
+        int pa = p.passes > 1 ? (pass == 1 ? 2 : 1) : 0;
+        int pb = p.passes > 1 ? (pass == 0 ? 2 : 1) : 0;
+        if (a_gather) gather_tile(p.a, sa, BM, tm * BM, kc, p.a.bcast_batch ? 0 : bt, gtid, pa);
+        if (b_gather) gather_tile(p.b, sb, BN, tn * BN, kc, p.b.bcast_batch ? 0 : bt, gtid, pb);
+        fence_proxy_async_smem();
+        mbar_arrive(&full_bar[stage]);
+        if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace wxx_tc

@@ -1,0 +1,118 @@
+"""Convolutions and pooling (reference: src/wxx/functional/convolution.py)."""
+
+from .. import validation
+from ._common import F, check, dense, empty, matmul_mode_code
+from .pointwise import _training_only
+
+
+def _check_pool_input(tensor1, rank, name):
+    if len(tensor1.shape) != rank:
+        expected = "(B, C, L)" if rank == 3 else "(B, C, H, W)"
+        raise ValueError(f"{name} expects {expected}, got {tensor1.shape}")
+    if tensor1.type != "f32":
+        raise TypeError(f"{name} expects f32 input, got {tensor1.type!r}")
+
+
+def maxpool2d(tensor1, kernel, stride, padding, return_indices=False):
+    """Window max over (B, C, H, W), padding excluded, first strict maximum wins;
+    with ``return_indices`` also the flat input index (u32) of each maximum."""
+    _check_pool_input(tensor1, 4, "maxpool2d")
+    x = dense(tensor1)
+    B, C, H, W = x.shape
+    KH, KW = kernel
+    sh, sw = stride
+    ph, pw = padding
+    Ho = (H + 2 * ph - KH) // sh + 1
+    Wo = (W + 2 * pw - KW) // sw + 1
+    if Ho < 1 or Wo < 1:
+        raise ValueError(f"pooling produces an empty output {(Ho, Wo)}")
+    out = empty((B, C, Ho, Wo), "f32")
+    idx = empty((B, C, Ho, Wo), "u32") if return_indices else None
+    check(F.wxx_maxpool2d(out.buffer.ptr, None if idx is None else idx.buffer.ptr, x.ptr, B, C, H,
+                          W, KH, KW, sh, sw, ph, pw), "maxpool2d")
+    return (out, idx) if return_indices else out
+
+
+def _normalize_output_size(output_size):
+    if isinstance(output_size, int):
+        output_size = (output_size, output_size)
+    if len(output_size) != 2:
+        raise ValueError(f"output_size must be an int or 2-tuple, got {output_size!r}")
+    h, w = int(output_size[0]), int(output_size[1])
+    if h < 1 or w < 1:
+        raise ValueError(f"output_size entries must be positive, got {output_size!r}")
+    return h, w
+
+
+def adaptive_avgpool2d(tensor1, output_size):
+    """Adaptive average pooling with windows [floor(o*in/out), ceil((o+1)*in/out))."""
+    if tensor1.type != "f32":
+        raise TypeError(f"adaptive_avgpool2d expects f32 input, got {tensor1.type!r}")
+    if validation.check_rank(tensor1.shape, name="adaptive_avgpool2d input") != 4:
+        raise ValueError(f"adaptive_avgpool2d expects (B, C, H, W), got {tensor1.shape}")
+    Ho, Wo = _normalize_output_size(output_size)
+    x = dense(tensor1)
+    B, C, H, W = x.shape
+    out = empty((B, C, Ho, Wo), "f32", tensor1.requires_grad)
+    check(F.wxx_adaptive_avgpool2d(out.buffer.ptr, x.ptr, B, C, H, W, Ho, Wo),
+          "adaptive_avgpool2d")
+    return out
+
+
+def conv2d(tensor1, W, stride, padding, dilation, bias=None):
+    """NCHW cross-correlation as an implicit GEMM on the tcgen05 tensor cores
+    (functional/convolution.py:658-729): rows = B*Ho*Wo output pixels,
+    columns = Cout, K = Cin*KH*KW, the im2col gather done by producer warps."""
+    x = dense(tensor1)
+    w = dense(W)
+    B, Cin, H, Wd = x.shape
+    Cout, Cin_w, KH, KW = w.shape
+    if Cin_w != Cin:
+        raise ValueError(f"conv2d: input has {Cin} channels, weight expects {Cin_w}")
+    sh, sw = stride
+    ph, pw = padding
+    dh, dw = dilation
+    Ho = (H + 2 * ph - dh * (KH - 1) - 1) // sh + 1
+    Wo = (Wd + 2 * pw - dw * (KW - 1) - 1) // sw + 1
+    if Ho < 1 or Wo < 1:
+        raise ValueError(f"conv2d produces an empty output {(Ho, Wo)}")
+    b = dense(bias) if bias is not None else None
+    out = empty((B, Cout, Ho, Wo), "f32", tensor1.requires_grad)
+    mode = matmul_mode_code()
+    check(F.wxx_conv2d(out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr, B, Cin, H, Wd,
+                       Cout, KH, KW, sh, sw, ph, pw, dh, dw, 0 if mode == 0 else 1), "conv2d")
+    return out
+
+
+def causal_conv1d(tensor1, weight, bias):
+    """Depthwise causal conv ``out[b,d,n] = bias[d] + sum_k w[d,k] x[b,d,n-k]``
+    consuming a strided (B, D, L) view directly."""
+    if len(tensor1.shape) != 3:
+        raise ValueError(f"causal_conv1d expects a 3-D input, got {tensor1.shape}")
+    if len(weight.shape) != 2:
+        raise ValueError(f"causal_conv1d weight must be (D, K), got {weight.shape}")
+    x = tensor1 if all(s >= 0 for s in tensor1.stride) else tensor1.contiguous()
+    w = dense(weight)
+    b = dense(bias)
+    B, D, L = x.shape
+    K = w.shape[1]
+    out = empty((B, D, L), "f32", tensor1.requires_grad or weight.requires_grad)
+    check(F.wxx_causal_conv1d(out.buffer.ptr, x.buffer.ptr, x.offset, x.stride[0], x.stride[1],
+                              x.stride[2], w.ptr, b.ptr, B, D, L, K), "causal_conv1d")
+    return out
+
+
+conv2ddx = _training_only("conv2ddx")
+conv2ddw = _training_only("conv2ddw")
+conv2dtranspose = _training_only("conv2dtranspose")
+conv2dtranspose_dx = _training_only("conv2dtranspose_dx")
+conv2dtranspose_dw = _training_only("conv2dtranspose_dw")
+maxpool2ddx = _training_only("maxpool2ddx")
+adaptive_avgpool2ddx = _training_only("adaptive_avgpool2ddx")
+avgpool1d = _training_only("avgpool1d")
+avgpool1ddx = _training_only("avgpool1ddx")
+avgpool2d = _training_only("avgpool2d")
+avgpool2ddx = _training_only("avgpool2ddx")
+maxpool1d = _training_only("maxpool1d")
+maxpool1ddx = _training_only("maxpool1ddx")
+causal_conv1d_backward = _training_only("causal_conv1d_backward")

@@ -1,0 +1,144 @@
+"""GPT-2 style decoder (reference: src/wxx/nn/gpt.py)."""
+
+import numpy as np
+
+from .. import functional
+from ..Tensor import Tensor
+from ..backend import context
+from ..functional.utils import from_numpy
+from .module import (
+    GELU,
+    Dropout,
+    Embedding,
+    LayerNorm,
+    Linear,
+    Module,
+    ModuleList,
+    MultiHeadAttention,
+    Sequential,
+    TiedLinear,
+)
+
+
+class GPT2Block(Module):
+    """Pre-LN block: causal self-attention + GELU MLP."""
+
+    def __init__(self, d_model, n_heads, dropout=0.1):
+        super().__init__()
+        self.ln1 = LayerNorm(d_model)
+        self.attn = MultiHeadAttention(d_model, n_heads)
+        self.ln2 = LayerNorm(d_model)
+        self.mlp = Sequential(Linear(d_model, 4 * d_model), GELU(), Linear(4 * d_model, d_model))
+        self.drop = Dropout(dropout)
+
+    def forward(self, x, mask=None):
+        x = x + self.drop(self.attn(self.ln1(x), mask))
+        x = x + self.drop(self.mlp(self.ln2(x)))
+        return x
+
+
+class GPT2(Module):
+    def __init__(self, vocab_size, d_model=256, n_heads=8, n_layers=6, max_len=256, dropout=0.1,
+                 tie_weights=True):
+        super().__init__()
+        self.vocab_size = vocab_size
+        self.max_len = max_len
+        self.tok_emb = Embedding(vocab_size, d_model, init_std=0.02)
+        self.pos_emb = Embedding(max_len, d_model, init_std=0.02)
+        self.blocks = ModuleList([GPT2Block(d_model, n_heads, dropout) for _ in range(n_layers)])
+        self.ln_f = LayerNorm(d_model)
+        self.head = TiedLinear(self.tok_emb) if tie_weights else Linear(d_model, vocab_size,
+                                                                          bias=False)
+        self._gpt2_init()
+        object.__setattr__(self, "_causal_mask_cache", None)
+        object.__setattr__(self, "_pos_cache", {})
+
+    def _gpt2_init(self):
+        """Every >=2-D non-embedding weight ~ N(0, 0.02), biases 0 (gpt.py:66-73)."""
+        for name, p in self.named_parameters():
+            if name.endswith(("tok_emb.weight", "pos_emb.weight")):
+                continue
+            if len(p.shape) >= 2:
+                functional.assign(p, functional.normal(0, 0.02, p.shape))
+            elif name.endswith("bias"):
+                functional.assign(p, 0.0)
+
+    def causal_mask(self, seq):
+        """Additive (seq, seq) mask, 0 on and below the diagonal, -1e9 above."""
+        mask = self._causal_mask_cache
+        if mask is None:
+            r = np.arange(self.max_len)[:, None]
+            c = np.arange(self.max_len)[None, :]
+            mask = from_numpy(np.where(c <= r, 0.0, -1e9).astype(np.float32))
+            object.__setattr__(self, "_causal_mask_cache", mask)
+        if seq == self.max_len:
+            return mask
+        return mask.narrow(0, 0, seq).narrow(1, 0, seq)
+
+    def _positions(self, seq):
+        pos = self._pos_cache.get(seq)
+        if pos is None:
+            pos = from_numpy(np.arange(seq, dtype=np.uint32).reshape(1, seq), dtype=np.uint32)
+            self._pos_cache[seq] = pos
+        return pos
+
+    def forward(self, x, mask=None):
+        b, seq = x.shape
+        if seq > self.max_len:
+            raise ValueError(f"sequence length {seq} > max_len {self.max_len}")
+        if mask is None:
+            mask = self.causal_mask(seq)
+        h = self.tok_emb(x) + self.pos_emb(self._positions(seq))
+        for block in self.blocks:
+            h = block(h, mask)
+        return self.head(self.ln_f(h))
+
+    def generate(self, prompt, max_new_tokens=64, temperature=1.0, top_k=None, stop_token=None,
+                 rng=None):
+        """Autoregressive sampling, same contract as the reference (gpt.py:108-170)."""
+        ids = prompt.numpy() if isinstance(prompt, Tensor) else np.asarray(prompt)
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        if ids.ndim == 1:
+            ids = ids[None, :]
+        if ids.ndim != 2:
+            raise ValueError(f"prompt must be 1D or 2D, got shape {ids.shape}")
+        batch, seq = ids.shape
+        if seq == 0:
+            raise ValueError("prompt must contain at least one token")
+        if seq > self.max_len:
+            raise ValueError(f"prompt length {seq} > max_len {self.max_len}")
+        if temperature < 0:
+            raise ValueError("temperature must be non-negative")
+        if rng is None:
+            rng = np.random.default_rng()
+        steps = min(int(max_new_tokens), self.max_len - seq)
+        prev = context.MODE
+        context.MODE = 1
+        try:
+            for _ in range(steps):
+                logits = self.forward(from_numpy(ids, dtype=np.uint32))
+                last = logits[:, -1, :].numpy().astype(np.float64)
+                if temperature == 0.0:
+                    nxt = last.argmax(axis=-1)
+                else:
+                    last = last / temperature
+                    if top_k is not None:
+                        k = min(int(top_k), last.shape[-1])
+                        if k < last.shape[-1]:
+                            cut = np.partition(last, -k, axis=-1)[:, -k]
+                            last[last < cut[:, None]] = -np.inf
+                    last -= last.max(axis=-1, keepdims=True)
+                    probs = np.exp(last)
+                    probs /= probs.sum(axis=-1, keepdims=True)
+                    draws = rng.random((batch, 1))
+                    nxt = (np.cumsum(probs, axis=-1) > draws).argmax(axis=-1)
+                nxt = nxt.astype(np.uint32)
+                ids = np.concatenate([ids, nxt[:, None]], axis=1)
+                if stop_token is not None and np.all(nxt == stop_token):
+                    break
+        finally:
+            context.MODE = prev
+        return ids
+
+
+__all__ = ["GPT2", "GPT2Block"]

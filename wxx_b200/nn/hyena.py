@@ -1,0 +1,173 @@
+"""Hyena language model (reference: src/wxx/nn/hyena.py).
+
+Same modules, parameter names and default initialisation as the reference.
+The long convolution ``irfft(rfft(z, n) * rfft(h, n), n)[..., :L]`` runs as
+one fused kernel (``functional.fftconv``): each (batch, channel) row is
+transformed, multiplied by the filter spectrum and transformed back on chip.
+"""
+
+import numpy as np
+
+from .. import autograd, functional
+from ..Tensor import Parameter, Tensor
+from .module import (
+    Embedding,
+    Linear,
+    Module,
+    ModuleList,
+    PositionalEncoding,
+    RMSNorm,
+    Sequential,
+    Sine,
+    SwiGLU,
+    TiedLinear,
+)
+
+
+def _next_pow2(n):
+    n = int(n)
+    return 1 if n <= 1 else 1 << (n - 1).bit_length()
+
+
+class CausalShortConv1d(Module):
+    """Depthwise causal conv ``out[n] = sum_k w[k] x[n-k]`` over (B, D, L)."""
+
+    def __init__(self, d_model, kernel_size=3):
+        super().__init__()
+        self.d_model = d_model
+        self.kernel_size = kernel_size
+        self.weight = Parameter(Tensor((d_model, kernel_size), value=0.0))
+        self.bias = Parameter(Tensor((d_model,), value=0.0))
+        functional.assign(self.weight, functional.normal(0, 0.02, (d_model, kernel_size)))
+
+    def forward(self, x):
+        return autograd.causal_conv1d(x, self.weight, self.bias).forward(x, self.weight, self.bias)
+
+
+class ImplicitFilter(Module):
+    """``h(t) = FFN(PositionalEncoding(t))`` returned as (d_model, L)."""
+
+    def __init__(self, d_model, hidden_dim=64, pe_features=8, omega=10.0):
+        super().__init__()
+        self.d_model = d_model
+        self.hidden_dim = hidden_dim
+        self.pe_features = pe_features
+        self.positional_encoding = PositionalEncoding(pe_features)
+        self.mlp = Sequential(
+            Linear(self.positional_encoding.out_features, hidden_dim),
+            Sine(omega),
+            Linear(hidden_dim, d_model),
+        )
+
+    def forward(self, L):
+        pos = self.positional_encoding(L)
+        return self.mlp(pos).transpose(0, 1)
+
+
+class HyenaOperator(Module):
+    def __init__(self, d_model, order=2, fft_size=None, short_conv_kernel=3, filter_hidden=64,
+                 pe_features=8, filter_omega=10.0):
+        super().__init__()
+        if order < 1:
+            raise ValueError(f"order must be >= 1, got {order}")
+        if short_conv_kernel < 1:
+            raise ValueError(f"short_conv_kernel must be >= 1, got {short_conv_kernel}")
+        self.d_model = d_model
+        self.order = int(order)
+        self.fft_size = fft_size
+        self.proj_v = Linear(d_model, d_model, bias=False)
+        self.proj_x = Linear(d_model, self.order * d_model, bias=False)
+        self.out_proj = Linear(d_model, d_model, bias=False)
+        self.short_conv = CausalShortConv1d(d_model, kernel_size=short_conv_kernel)
+        self.filter_mlp = ModuleList(
+            [ImplicitFilter(d_model, hidden_dim=filter_hidden, pe_features=pe_features,
+                            omega=filter_omega) for _ in range(self.order)]
+        )
+        self.decay = Parameter(Tensor((self.order, d_model), value=0.0))
+        functional.assign(
+            self.decay, functional.from_numpy(np.random.rand(self.order, d_model).astype(np.float32))
+        )
+
+    def _fft_size(self, length):
+        size = int(self.fft_size) if self.fft_size is not None else _next_pow2(2 * length)
+        if size < length:
+            size = _next_pow2(length)
+        return size
+
+    def fft_conv1d(self, x, h):
+        """Linear convolution of (B, D, L) with (D, L), fused on the GPU."""
+        length = x.shape[-1]
+        return functional.fftconv(x, h, self._fft_size(length), out_len=length)
+
+    def _decay_window(self, stage, length):
+        return autograd.decay_window(self.decay).forward(self.decay, stage, length)
+
+    def forward(self, x):
+        _, length, _ = x.shape
+        v = self.proj_v(x)
+        gates = list(self.proj_x(x).chunk(self.order, dim=-1))
+        v = v.transpose(1, 2)
+        gates = [g.transpose(1, 2) for g in gates]
+        v = self.short_conv(v)
+        gates = [self.short_conv(g) for g in gates]
+        z = v
+        for i in range(self.order):
+            h = self.filter_mlp[i](length)
+            h = h * self._decay_window(i, length)
+            z = gates[i] * self.fft_conv1d(z, h)
+        return self.out_proj(z.transpose(1, 2))
+
+
+class HyenaBlock(Module):
+    def __init__(self, d_model, mlp_ratio=4, hidden_dim=None, order=2, short_conv_kernel=3,
+                 filter_hidden=64, pe_features=8, filter_omega=10.0):
+        super().__init__()
+        self.norm1 = RMSNorm(d_model)
+        self.mixer = HyenaOperator(d_model, order=order, short_conv_kernel=short_conv_kernel,
+                                   filter_hidden=filter_hidden, pe_features=pe_features,
+                                   filter_omega=filter_omega)
+        self.norm2 = RMSNorm(d_model)
+        self.feed_forward = SwiGLU(d_model, hidden_dim=hidden_dim, mlp_ratio=mlp_ratio)
+
+    def forward(self, x):
+        x = x + self.mixer(self.norm1(x))
+        x = x + self.feed_forward(self.norm2(x))
+        return x
+
+
+class Hyena(Module):
+    def __init__(self, vocab_size, d_model=256, n_layers=8, mlp_ratio=4, hidden_dim=None,
+                 tie_weights=True, embed_init_std=0.02, order=2, short_conv_kernel=3,
+                 filter_hidden=64, pe_features=8, filter_omega=10.0):
+        super().__init__()
+        self.vocab_size = vocab_size
+        self.d_model = d_model
+        self.order = order
+        self.embed = Embedding(vocab_size, d_model, init_std=embed_init_std)
+        self.layers = ModuleList(
+            [HyenaBlock(d_model, mlp_ratio=mlp_ratio, hidden_dim=hidden_dim, order=order,
+                        short_conv_kernel=short_conv_kernel, filter_hidden=filter_hidden,
+                        pe_features=pe_features, filter_omega=filter_omega)
+             for _ in range(n_layers)]
+        )
+        self.norm = RMSNorm(d_model)
+        self.head = TiedLinear(self.embed) if tie_weights else Linear(d_model, vocab_size)
+
+    def forward(self, x):
+        h = self.embed(x)
+        for block in self.layers:
+            h = block(h)
+        return self.head(self.norm(h))
+
+
+__all__ = [
+    "Sine",
+    "PositionalEncoding",
+    "CausalShortConv1d",
+    "ImplicitFilter",
+    "HyenaOperator",
+    "SwiGLU",
+    "HyenaBlock",
+    "TiedLinear",
+    "Hyena",
+]

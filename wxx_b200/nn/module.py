@@ -1,0 +1,466 @@
+"""Module system and layers (reference: src/wxx/nn/module.py).
+
+Same class names, constructor arguments, parameter names (so ``state_dict``
+keys and the ``.npz`` format match the reference) and default
+initialisations.  ``forward`` runs through ``wxx_b200.autograd`` /
+``wxx_b200.functional`` on the GPU.
+"""
+
+import math
+
+import numpy as np
+
+from .. import autograd, functional
+from ..Tensor import Parameter, Tensor
+from ..backend import context
+from ..backend.device import get_cmd_buffer
+from ..functional.utils import from_numpy, normal
+
+
+class Module:
+    def __init__(self):
+        object.__setattr__(self, "_parameters", {})
+        object.__setattr__(self, "_modules", {})
+
+    def __setattr__(self, name, value):
+        if isinstance(value, Parameter):
+            self._parameters[name] = value
+        elif isinstance(value, Module):
+            self._modules[name] = value
+        elif value is None and name in self._parameters:
+            self._parameters[name] = None
+        object.__setattr__(self, name, value)
+
+    def __call__(self, *x):
+        return self.forward(*x)
+
+    def parameters(self, recurse=True):
+        """Yields ``("", parameter)`` pairs, as the reference does (module.py:39-47)."""
+        for p in self._parameters.values():
+            if p is not None:
+                yield ("", p)
+        if recurse:
+            for m in self._modules.values():
+                if m is not None:
+                    yield from m.parameters(recurse=True)
+
+    def named_parameters(self, prefix="", recurse=True):
+        for name, p in self._parameters.items():
+            if p is not None:
+                yield (prefix + name, p)
+        if recurse:
+            for name, m in self._modules.items():
+                if m is not None:
+                    yield from m.named_parameters(prefix + name + ".", recurse=True)
+
+    def state_dict(self, prefix="", destination=None):
+        """Parameter name -> host numpy array."""
+        if destination is None:
+            destination = {}
+        for name, p in self._parameters.items():
+            if p is not None:
+                destination[prefix + name] = np.asarray(p.numpy()).copy()
+        for name, m in self._modules.items():
+            if m is not None:
+                m.state_dict(prefix + name + ".", destination)
+        return destination
+
+    def _state_keys(self, prefix=""):
+        keys = [prefix + n for n, p in self._parameters.items() if p is not None]
+        for name, m in self._modules.items():
+            if m is not None:
+                keys.extend(m._state_keys(prefix + name + "."))
+        return keys
+
+    def load_state_dict(self, state_dict, strict=True):
+        """Uploads arrays (or tensors) into the parameters in place."""
+        own = set(self._state_keys())
+        for name, p in self.named_parameters():
+            if name in state_dict:
+                val = state_dict[name]
+                if isinstance(val, Tensor):
+                    src = val
+                else:
+                    arr = np.asarray(val)
+                    if p.type == "c64":
+                        src = functional.from_numpy_complex(arr)
+                    elif p.type == "u32":
+                        src = from_numpy(arr, dtype=np.uint32)
+                    else:
+                        src = from_numpy(arr)
+                if tuple(src.shape) != tuple(p.shape):
+                    raise ValueError(
+                        f"state_dict[{name!r}] has shape {tuple(src.shape)}, "
+                        f"parameter has {tuple(p.shape)}"
+                    )
+                functional.assign(p, src)
+            elif strict:
+                raise KeyError(f"Missing key in state_dict: {name}")
+        if strict:
+            missing = own - set(state_dict.keys())
+            unexpected = set(state_dict.keys()) - own
+            if missing:
+                raise RuntimeError(f"Missing keys: {sorted(missing)}")
+            if unexpected:
+                raise RuntimeError(f"Unexpected keys: {sorted(unexpected)}")
+
+    def zero_grad(self, wait=False):
+        for _, p in self.named_parameters():
+            p.grad = None
+        get_cmd_buffer().flush(wait=wait)
+
+    def forward(self, *args, **kwargs):
+        raise NotImplementedError
+
+    def __repr__(self):
+        lines = [self.__class__.__name__ + "("]
+        for name, m in self._modules.items():
+            lines.append(f"  ({name}): {repr(m)}")
+        lines.append(")")
+        return "\n".join(lines)
+
+
+class ModuleList(Module):
+    def __init__(self, modules=None):
+        super().__init__()
+        if modules is not None:
+            for i, m in enumerate(modules):
+                setattr(self, str(i), m)
+
+    def __getitem__(self, idx):
+        if isinstance(idx, slice):
+            return [self._modules[str(i)] for i in range(*idx.indices(len(self)))]
+        return self._modules[str(idx)]
+
+    def __iter__(self):
+        return iter(self._modules.values())
+
+    def __len__(self):
+        return len(self._modules)
+
+    def append(self, module):
+        setattr(self, str(len(self._modules)), module)
+
+    def forward(self, x, *args, **kwargs):
+        for m in self._modules.values():
+            x = m(x, *args, **kwargs)
+        return x
+
+
+class Sequential(Module):
+    def __init__(self, *modules):
+        super().__init__()
+        for i, m in enumerate(modules):
+            setattr(self, str(i), m)
+
+    def forward(self, x, *args, **kwargs):
+        for m in self._modules.values():
+            x = m(x, *args, **kwargs)
+        return x
+
+
+class Linear(Module):
+    """``y = x @ W + b`` with ``W`` of shape (in, out), Kaiming-normal init."""
+
+    def __init__(self, in_features, out_features, bias=True):
+        super().__init__()
+        self.weight = Parameter(Tensor((in_features, out_features), value=0.0))
+        functional._kaiming_normal_init(self.weight, in_features)
+        self.bias = Parameter(Tensor((out_features,), value=0.0)) if bias else None
+
+    def forward(self, x):
+        if self.bias is None:
+            return autograd.matmul(x, self.weight).forward(x, self.weight)
+        return autograd.matmuladd(x, self.weight, self.bias).forward(x, self.weight, self.bias)
+
+
+class Embedding(Module):
+    def __init__(self, num_embeddings, embedding_dim, init_std=0.02):
+        super().__init__()
+        self.num_embeddings = num_embeddings
+        self.embedding_dim = embedding_dim
+        self.weight = Parameter(Tensor((num_embeddings, embedding_dim), value=0.0))
+        functional.assign(self.weight, normal(0, init_std, (num_embeddings, embedding_dim)))
+
+    def forward(self, x):
+        n = x.shape[0] * x.shape[1] if len(x.shape) > 1 else x.shape[0]
+        return autograd.Embedding(x, self.weight).forward(
+            x, self.weight, n, self.embedding_dim, self.num_embeddings
+        )
+
+
+class Dropout(Module):
+    """Inverted dropout in training mode; identity under ``inferenceMode``."""
+
+    def __init__(self, p=0.5):
+        super().__init__()
+        self.p = p
+
+    def forward(self, x):
+        if context.MODE != 0 or self.p == 0:
+            return x
+        return autograd.Dropout(x).forward(x, self.p)
+
+
+class LayerNorm(Module):
+    """LayerNorm over the trailing ``normalized_shape`` dims.  As in the
+    reference the kernel's eps is 1e-5 whatever ``eps`` says."""
+
+    def __init__(self, normalized_shape, eps=1e-5):
+        super().__init__()
+        if isinstance(normalized_shape, int):
+            normalized_shape = (normalized_shape,)
+        self.normalized_shape = tuple(normalized_shape)
+        self.eps = eps
+        self.weightg = Parameter(Tensor(self.normalized_shape, value=1.0))
+        self.weightb = Parameter(Tensor(self.normalized_shape, value=0.0))
+        # Registered aliases, as in the reference (module.py:207-208): the
+        # state_dict carries weightg, weightb, weight and bias.
+        self.weight = self.weightg
+        self.bias = self.weightb
+
+    def forward(self, x):
+        axis = tuple(range(len(x.shape) - len(self.normalized_shape), len(x.shape)))
+        axis_arg = axis if len(axis) > 1 else axis[0]
+        return autograd.meanvarnorm(x, self.weightg, self.weightb).forward(
+            x, self.weightg, self.weightb, axis=axis_arg
+        )
+
+
+class RMSNorm(Module):
+    """RMSNorm over the last dim (kernel eps 1e-6, as in the reference)."""
+
+    def __init__(self, d_model, eps=1e-6):
+        super().__init__()
+        self.d_model = d_model
+        self.eps = eps
+        self.weight = Parameter(Tensor((d_model,), value=1.0))
+
+    def forward(self, x):
+        return autograd.rmsnorm(x, self.weight).forward(x, self.weight, -1)
+
+
+class BatchNorm(Module):
+    """BatchNorm over NCHW.  ``running_std`` holds a variance (reference
+    module.py:237-238); running statistics are not in ``state_dict``."""
+
+    def __init__(self, num_features, eps=1e-5, momentum=0.1):
+        super().__init__()
+        self.num_features = num_features
+        self.eps = eps
+        self.momentum = momentum
+        self.weight = Parameter(Tensor((num_features,), value=1.0))
+        self.bias = Parameter(Tensor((num_features,), value=0.0))
+        self.running_mean = Tensor((num_features,), value=0.0)
+        self.running_std = Tensor((num_features,), value=1.0)
+
+    def forward(self, x):
+        training = context.MODE == 0
+        return autograd.batchnorm(x, self.weight, self.bias).forward(
+            x, self.weight, self.bias, self.running_mean, self.running_std, training
+        )
+
+
+def _pair(v):
+    return (v, v) if isinstance(v, int) else tuple(v)
+
+
+class Conv2D(Module):
+    def __init__(self, in_channels, out_channels, kernel=3, stride=1, padding=0, dilation=1,
+                 bias=True):
+        super().__init__()
+        kernel = _pair(kernel)
+        self.kernel = kernel
+        self.stride = _pair(stride)
+        self.padding = _pair(padding)
+        self.dilation = _pair(dilation)
+        self.W = Parameter(Tensor((out_channels, in_channels, kernel[0], kernel[1]), value=0.0))
+        functional._kaiming_normal_init(self.W, math.prod(kernel) * in_channels)
+        self.bias = Parameter(Tensor((out_channels,), value=0.0)) if bias else None
+
+    def forward(self, x):
+        if self.bias is None:
+            return autograd.Conv2D(x, self.W).forward(
+                x, self.W, None, self.stride, self.padding, self.dilation
+            )
+        return autograd.Conv2D(x, self.W, self.bias).forward(
+            x, self.W, self.bias, self.stride, self.padding, self.dilation
+        )
+
+
+class Conv2DTranspose(Module):
+    def __init__(self, *args, **kwargs):
+        raise NotImplementedError("Conv2DTranspose is not part of the B200 inference backend")
+
+
+class MaxPool2d(Module):
+    def __init__(self, kernel, stride=None, padding=0, return_indices=False):
+        super().__init__()
+        kernel = _pair(kernel)
+        self.kernel = kernel
+        self.stride = kernel if stride is None else _pair(stride)
+        self.padding = _pair(padding)
+        self.return_indices = return_indices
+
+    def forward(self, x):
+        return autograd.maxpooling2d(x).forward(
+            x, self.kernel, self.stride, self.padding, self.return_indices
+        )
+
+
+class _UnsupportedPool(Module):
+    def __init__(self, *args, **kwargs):
+        raise NotImplementedError(
+            f"{type(self).__name__} is not on any forward path of the B200 backend"
+        )
+
+
+class MaxPool1d(_UnsupportedPool):
+    pass
+
+
+class AvgPool1d(_UnsupportedPool):
+    pass
+
+
+class AvgPool2d(_UnsupportedPool):
+    pass
+
+
+class AdaptiveAvgPool2d(Module):
+    def __init__(self, output_size):
+        super().__init__()
+        self.output_size = tuple(int(v) for v in _pair(output_size))
+
+    def forward(self, x):
+        return autograd.adaptive_avgpooling2d(x).forward(x, self.output_size)
+
+
+class MultiHeadAttention(Module):
+    """Multi-head self-attention (module.py:447-495).
+
+    Same parameters and head layout (``reshape(b, s, H, hd).permute(0, 2, 1, 3)``).
+    The score path is fused: the 1/sqrt(hd) scale is applied in the QK^T
+    GEMM epilogue and the additive mask inside the softmax kernel, so the
+    (B*H, S, S) score tensor is written once and read once.
+    """
+
+    def __init__(self, d_model, n_heads, dropout=0.0):
+        super().__init__()
+        assert d_model % n_heads == 0
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.head_dim = d_model // n_heads
+        self.q = Linear(d_model, d_model, bias=False)
+        self.k = Linear(d_model, d_model, bias=False)
+        self.v = Linear(d_model, d_model, bias=False)
+        self.out = Linear(d_model, d_model, bias=False)
+        self.drop = Dropout(dropout)
+
+    def _heads(self, t, b, seq):
+        return (
+            t.reshape((b, seq, self.n_heads, self.head_dim))
+            .permute(0, 2, 1, 3)
+            .reshape((b * self.n_heads, seq, self.head_dim))
+        )
+
+    def forward(self, x, mask=None):
+        b, seq, _ = x.shape
+        q = self._heads(self.q(x), b, seq)
+        k = self._heads(self.k(x), b, seq)
+        v = self._heads(self.v(x), b, seq)
+        score = functional.matmul_add(q, k, None, transpose_B=True,
+                                      alpha=1.0 / math.sqrt(self.head_dim))
+        attn = functional.masked_softmax(score, mask) if mask is not None else score.softmax(-1)
+        attn = self.drop(attn)
+        out = autograd.matmul(attn, v).forward(attn, v)
+        out = (
+            out.reshape((b, self.n_heads, seq, self.head_dim))
+            .permute(0, 2, 1, 3)
+            .reshape((b, seq, self.d_model))
+        )
+        return self.out(out)
+
+
+class Attention(Module):
+    def __init__(self, d_model, n_heads=1):
+        super().__init__()
+        self.mha = MultiHeadAttention(d_model, n_heads)
+
+    def forward(self, x, mask=None):
+        return self.mha(x, mask)
+
+
+class GELU(Module):
+    def forward(self, x):
+        return x.gelu()
+
+
+class Sine(Module):
+    """``sin(omega * x)``."""
+
+    def __init__(self, omega=10.0):
+        super().__init__()
+        self.omega = float(omega)
+
+    def forward(self, x):
+        return (x * self.omega).sin()
+
+    def extra_repr(self):
+        return f"omega={self.omega}"
+
+
+class SwiGLU(Module):
+    def __init__(self, d_model, hidden_dim=None, mlp_ratio=4):
+        super().__init__()
+        if hidden_dim is None:
+            hidden_dim = int(2 * (mlp_ratio * d_model) / 3)
+        self.hidden_dim = hidden_dim
+        self.w1 = Linear(d_model, hidden_dim, bias=False)
+        self.w2 = Linear(d_model, hidden_dim, bias=False)
+        self.w3 = Linear(hidden_dim, d_model, bias=False)
+
+    def forward(self, x):
+        return self.w3(functional.silu(self.w1(x)) * self.w2(x))
+
+
+class TiedLinear(Module):
+    """Output head sharing an embedding's weight: ``x @ E^T``."""
+
+    def __init__(self, embedding):
+        super().__init__()
+        object.__setattr__(self, "_embedding", embedding)
+
+    def forward(self, x):
+        w = self._embedding.weight
+        return autograd.matmul(x, w).forward(x, w, False, True)
+
+
+class PositionalEncoding(Module):
+    """``[t, cos(2 pi k t), sin(2 pi k t)]`` over ``t = linspace(0, 1, L)``."""
+
+    def __init__(self, features=8):
+        super().__init__()
+        features = int(features)
+        if features < 1:
+            raise ValueError(f"positional features must be >= 1, got {features}")
+        self.features = features
+        self.out_features = 2 * features + 1
+        self._cache = {}
+
+    def _build(self, length):
+        t = np.linspace(0.0, 1.0, int(length), dtype=np.float32)
+        k = np.arange(self.features, dtype=np.float32)
+        ang = (2.0 * np.pi) * np.outer(t, k)
+        return np.concatenate([t[:, None], np.cos(ang), np.sin(ang)], axis=1).astype(np.float32)
+
+    def forward(self, length):
+        key = (int(length), self.features)
+        pe = self._cache.get(key)
+        if pe is None:
+            pe = from_numpy(self._build(length))
+            self._cache[key] = pe
+        return pe
+
+    def extra_repr(self):
+        return f"features={self.features}, out_features={self.out_features}"
