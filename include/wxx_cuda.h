@@ -30,6 +30,8 @@ extern "C" {
 
 const char* wxx_last_error(void);
 const char* wxx_version(void);
+/* No reference counterpart: kernels launched by this library so far (per process). */
+int wxx_launch_count(int64_t* out);
 int wxx_device_count(int* count);
 /* backend/device.py:258 (module-level WebGPUContext()) */
 int wxx_init(int device);

@@ -257,3 +257,13 @@ class PinnedHostBuffer:
                 F.wxx_host_free(self.ptr)
         except Exception:
             pass
+
+
+def launch_count():
+    """Kernels launched by libwxx_cuda.so so far in this process."""
+    from .lib import load
+
+    load()
+    out = ctypes.c_int64(0)
+    check(F.wxx_launch_count(ctypes.byref(out)))
+    return out.value

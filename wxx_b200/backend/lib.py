@@ -29,6 +29,7 @@ P_u8 = ctypes.POINTER(ctypes.c_uint8)
 SIGNATURES = {
     "wxx_last_error": [],
     "wxx_version": [],
+    "wxx_launch_count": [P_i64],
     "wxx_device_count": [P_int],
     "wxx_init": [c_int],
     "wxx_current_device": [P_int],

@@ -26,6 +26,7 @@
 namespace wxx {
 
 void set_error(const char* fmt, ...);
+void count_launch();                // one kernel launch enqueued by this library
 int require_init();                 // WXX_OK once wxx_init() succeeded
 cudaStream_t stream();              // library stream of the current device
 int num_sms();                      // SM count of the current device
@@ -54,6 +55,7 @@ inline unsigned grid_for(int64_t work_items, int threads_per_cta, int ctas_per_s
 
 #define WXX_LAUNCH_CHECK()                                                        \
   do {                                                                            \
+    wxx::count_launch();                                                          \
     cudaError_t _wxx_e = cudaGetLastError();                                      \
     if (_wxx_e != cudaSuccess) {                                                  \
       wxx::set_error("kernel launch failed: %s (%s:%d)",                          \

@@ -12,7 +12,11 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
+
+extern "C" int wxx_malloc(void** out, uint64_t nbytes);
+extern "C" int wxx_free(void* p);
 
 using namespace wxx_tc;
 
@@ -135,6 +139,63 @@ int run_tc(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorM
   }
 }
 
+// ------------------------------------------------------------ 3xTF32 residuals
+
+// lo[i] = x[i] - tf32(x[i]) where tf32() clears the 13 low mantissa bits --
+// exactly what the tensor core reads from an fp32 word (it truncates), so the
+// raw operand serves as the "hi" part and only the residual needs storage.
+__global__ void tf32_residual_kernel(float* __restrict__ lo, const float* __restrict__ x,
+                                     int64_t n) {
+  const bool vec = !((reinterpret_cast<uintptr_t>(lo) | reinterpret_cast<uintptr_t>(x)) & 15);
+  int64_t n4 = vec ? n / 4 : 0;
+  int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < n4; i += step) {
+    float4 v = reinterpret_cast<const float4*>(x)[i];
+    float4 r;
+    r.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    r.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    r.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    r.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    reinterpret_cast<float4*>(lo)[i] = r;
+  }
+  for (int64_t i = n4 * 4 + tid; i < n; i += step) {
+    float v = x[i];
+    lo[i] = v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+  }
+}
+
+// Elements spanned by an operand (from its base pointer).
+int64_t operand_extent(const OperandDesc& d) {
+  int64_t nb = d.bcast ? 1 : d.batch;
+  int64_t inner_last = d.k_contig ? (d.rows - 1) * d.ld + d.K : (d.K - 1) * d.ld + d.rows;
+  return (nb - 1) * d.bs + inner_last;
+}
+
+// For a TMA-fed operand in 3xTF32 mode: writes its residual into `*scratch`
+// (allocated here, released by the caller after the GEMM is enqueued) and
+// encodes the residual's tensor map.
+int make_residual(const OperandDesc& d, const OperandSrc& src, int box_rows, CUtensorMap* map_lo,
+                  void** scratch) {
+  *scratch = nullptr;
+  if (src.kind >= 2) return WXX_OK;  // gathered operands are split on the fly
+  int64_t n = operand_extent(d);
+  int st = wxx_malloc(scratch, (uint64_t)n * sizeof(float));
+  if (st) return st;
+  tf32_residual_kernel<<<wxx::grid_for(n / 4 + 1, 256), 256, 0, wxx::stream()>>>(
+      (float*)*scratch, d.base, n);
+  WXX_LAUNCH_CHECK();
+  OperandDesc dl = d;
+  dl.base = (const float*)*scratch;
+  OperandSrc tmp;
+  setup_operand(dl, box_rows, true, tmp, map_lo);
+  if (tmp.kind != src.kind) {
+    wxx::set_error("gemm: residual operand lost TMA addressability");
+    return WXX_E_STATE;
+  }
+  return WXX_OK;
+}
+
 // ------------------------------------------------------------ exact fp32 SIMT
 
 // 64x64 output tile, K-step 16, 4x4 outputs per thread, fp32 FMA.
@@ -240,15 +301,26 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
   CUtensorMap ma0, ma1, mb0, mb1;
   memset(&ma0, 0, sizeof(ma0));
   memset(&mb0, 0, sizeof(mb0));
-  // 3xTF32 splits operands while gathering them, so it always uses the
-  // gather producers; TF32 uses TMA wherever the operand is 16-byte addressable.
-  bool allow_tma = (mode == 0);
+  // TMA wherever the operand is 16-byte addressable, gather producers
+  // otherwise.  3xTF32 adds the residual operands (scratch, TMA-fed) or
+  // splits gathered operands on the fly.
   OperandDesc da{A, M, K, batch, lda, a_bs, trans_a == 0, a_bs == 0 && batch > 1};
   OperandDesc db{B, N, K, batch, ldb, b_bs, trans_b != 0, b_bs == 0 && batch > 1};
-  setup_operand(da, BM, allow_tma, p.a, &ma0);
-  setup_operand(db, bn, allow_tma, p.b, &mb0);
+  setup_operand(da, BM, true, p.a, &ma0);
+  setup_operand(db, bn, true, p.b, &mb0);
   ma1 = ma0;
   mb1 = mb0;
+  void* lo_a = nullptr;
+  void* lo_b = nullptr;
+  if (mode == 1) {
+    int st = make_residual(da, p.a, BM, &ma1, &lo_a);
+    if (st == WXX_OK) st = make_residual(db, p.b, bn, &mb1, &lo_b);
+    if (st != WXX_OK) {
+      wxx_free(lo_a);
+      wxx_free(lo_b);
+      return st;
+    }
+  }
   p.epi.kind = 0;
   p.epi.C = C;
   p.epi.c_bs = M * N;
@@ -257,7 +329,11 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
   p.epi.bias_mode = bias_mode;
   p.epi.bias_bs = M * N;
   p.epi.alpha = alpha;
-  return run_tc(bn, ma0, ma1, mb0, mb1, p);
+  int st = run_tc(bn, ma0, ma1, mb0, mb1, p);
+  // Stream-ordered frees: the residuals stay valid for the GEMM just enqueued.
+  int st_a = wxx_free(lo_a);
+  int st_b = wxx_free(lo_b);
+  return st ? st : (st_a ? st_a : st_b);
 }
 
 // Y (NCHW [B, Cout, Ho, Wo]) = conv2d(X [B, Cin, H, W], Wt [Cout, Cin, KH, KW]) (+ bias[Cout])

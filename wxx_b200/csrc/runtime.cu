@@ -15,6 +15,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -40,10 +41,13 @@ struct State {
 
 State g;
 thread_local char g_err[1024] = {0};
+std::atomic<int64_t> g_launches{0};
 
 }  // namespace
 
 namespace wxx {
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -69,6 +73,12 @@ int* device_error_word() { return g.err_word; }
 WXX_EXPORT const char* wxx_last_error(void) { return g_err; }
 
 WXX_EXPORT const char* wxx_version(void) { return "wxx_b200 0.1 (sm_100a)"; }
+
+// Number of kernels this library has launched since the process started.
+WXX_EXPORT int wxx_launch_count(int64_t* out) {
+  *out = g_launches.load(std::memory_order_relaxed);
+  return WXX_OK;
+}
 
 WXX_EXPORT int wxx_device_count(int* count) {
   int n = 0;

@@ -47,7 +47,9 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 4 / 6 / 8
   static constexpr int TMEM_COLS = 2 * BN;                    // 128 / 256 / 512
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr int EPI_STAGE_FLOATS = 32 * 33;            // per epilogue warp
+  static constexpr int EPI_BYTES = 4 * EPI_STAGE_FLOATS * 4;  // 16.5 KB
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -368,6 +370,54 @@ __device__ __forceinline__ void gather_tile(const OperandSrc& s, uint8_t* dst, i
   }
 }
 
+// Row-major epilogue for one warp's 32 x 32 chunk (rows m0..m0+31, columns
+// n0..n0+31).  Thread t holds row m0+t in v[]; the chunk is transposed through
+// a padded shared-memory tile so that each store instruction writes four
+// full 128-byte row segments (lane l: row r0 + l/8, columns 4*(l%8)..+3).
+__device__ __forceinline__ void epi_store_rows(const GemmParams& p, int bt, int m0, int n0,
+                                               float (&v)[32], float* stage) {
+  const EpiParams& e = p.epi;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = v[j];
+  __syncwarp();
+  const int cq = (lane & 7) * 4;
+  const int n = n0 + cq;
+  float* cbase = e.C + (int64_t)bt * e.c_bs;
+  const bool vec_ok = ((e.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0);
+  float bcol[4] = {0.f, 0.f, 0.f, 0.f};
+  if (e.bias_mode == 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) bcol[i] = (n + i < p.N) ? e.bias[n + i] : 0.f;
+  }
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    const int m = m0 + r;
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = stage[r * 33 + cq + i] * e.alpha + bcol[i];
+    if (m < p.M) {
+      if (e.bias_mode >= 2) {
+        const float* brow = e.bias + (e.bias_mode == 3 ? (int64_t)bt * e.bias_bs : 0) +
+                            (int64_t)m * p.N;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (n + i < p.N) o[i] += brow[n + i];
+      }
+      float* crow = cbase + (int64_t)m * e.ldc;
+      if (vec_ok && n + 3 < p.N) {
+        *reinterpret_cast<float4*>(crow + n) = make_float4(o[0], o[1], o[2], o[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (n + i < p.N) crow[n + i] = o[i];
+      }
+    }
+  }
+  __syncwarp();
+}
+
 // Epilogue store of one thread's row segment: row m, columns n0..n0+31.
 __device__ __forceinline__ void epi_store(const GemmParams& p, int bt, int m, int n0,
                                           float (&v)[32]) {
@@ -568,6 +618,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
     // ---------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    float* stage = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES) +
+                   (warp - EPI_WARP0) * C::EPI_STAGE_FLOATS;
     int local = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       int bt, tm, tn;
@@ -583,7 +635,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         float v[32];
         tmem_ld_32x32(row_addr + (uint32_t)c, v);
         int n0 = tn * BN + c;
-        if (n0 < p.N) epi_store(p, bt, m, n0, v);
+        if (n0 < p.N) {
+          if (p.epi.kind == 0) epi_store_rows(p, bt, tm * BM + quarter * 32, n0, v, stage);
+          else epi_store(p, bt, m, n0, v);
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);

@@ -95,3 +95,56 @@ __all__ = [
     "Tensor",
     "validation",
 ]
+
+
+# ---------------------------------------------------------------- kernel timing
+
+class KernelTimer:
+    """Brackets every tensor-core GEMM launch with CUDA events on the library
+    stream while active (``with KernelTimer() as t: ...``); ``summary()``
+    returns total FLOPs, total device milliseconds and the launch count."""
+
+    def __init__(self):
+        self.records = []
+
+    def __enter__(self):
+        global _timer
+        self._prev = _timer
+        _timer = self
+        return self
+
+    def __exit__(self, *exc):
+        global _timer
+        _timer = self._prev
+
+    def start(self):
+        from ..backend.device import Event
+
+        return Event().record()
+
+    def stop(self, ev0, flops, label):
+        from ..backend.device import Event
+
+        self.records.append((label, flops, ev0, Event().record()))
+
+    def summary(self):
+        total_ms = 0.0
+        total_flops = 0.0
+        per = {}
+        for label, flops, e0, e1 in self.records:
+            ms = e0.elapsed_ms(e1)
+            total_ms += ms
+            total_flops += flops
+            d = per.setdefault(label, [0, 0.0, 0.0])
+            d[0] += 1
+            d[1] += ms
+            d[2] += flops
+        return {"launches": len(self.records), "ms": total_ms, "flops": total_flops,
+                "per_shape": per}
+
+
+_timer = None
+
+
+def active_timer():
+    return _timer

@@ -9,7 +9,7 @@ import numpy as np
 
 from .. import validation
 from ..Tensor import Tensor, _from_host
-from ._common import F, arr64, check, dense, empty, matmul_mode_code, rng
+from ._common import F, active_timer, arr64, check, dense, empty, matmul_mode_code, rng
 
 
 def assign(tensor1, val):
@@ -189,9 +189,13 @@ def matmul_add(tensor1, tensor2, tensor3, transpose_A=False, transpose_B=False, 
     out = empty(out_batch + [M, N], "f32", requires_grad)
     lda = M if transpose_A else K
     ldb = K if transpose_B else N
+    timer = active_timer()
+    ev0 = timer.start() if timer is not None else None
     check(F.wxx_matmul(out.buffer.ptr, a.ptr, b.ptr, bias_ptr, batch, M, N, K, a_bs, b_bs, lda,
                        ldb, int(bool(transpose_A)), int(bool(transpose_B)), bias_mode,
                        float(alpha), matmul_mode_code()), "matmul_add")
+    if timer is not None:
+        timer.stop(ev0, 2.0 * batch * M * N * K, f"{batch}x{M}x{N}x{K}")
     return out
 
 
