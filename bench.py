@@ -343,6 +343,10 @@ def run_ours(args, rank, world, local):
     e1.record()
     barrier()
     launches = (dev.launch_count() - n0) / args.steps
+    log_path = os.environ.get("WXX_LAUNCH_LOG")
+    if log_path and rank == 0:
+        with open(log_path, "w") as f:
+            json.dump({"before_timed": n0, "per_step": launches}, f)
     ms = e0.elapsed_ms(e1) / args.steps
     clocks = sampler.stop()
     if dist is not None:

@@ -99,6 +99,24 @@ void setup_operand(const OperandDesc& d, int box_rows, bool allow_tma, OperandSr
   }
 }
 
+// Tensor map of the row-major output C [batch, M, N] for the TMA-store
+// epilogue (32 x 32 boxes, 128-byte swizzle).  False when C is not
+// 16-byte addressable; the epilogue then stores from registers.
+bool encode_c_map(CUtensorMap* map, const GemmParams& p) {
+  auto enc = get_encode();
+  if (!enc || p.epi.kind != 0 || p.epi.bias_mode > 1) return false;
+  if ((reinterpret_cast<uintptr_t>(p.epi.C) & 15) || ((int64_t)p.epi.ldc * 4) % 16) return false;
+  if (p.batch > 1 && (p.epi.c_bs * 4) % 16) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)p.N, (cuuint64_t)p.M, (cuuint64_t)p.batch};
+  cuuint64_t strides[2] = {(cuuint64_t)p.epi.ldc * 4,
+                           (cuuint64_t)(p.batch > 1 ? p.epi.c_bs : (int64_t)p.epi.ldc * p.M) * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.epi.C, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN>
 int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
               const CUtensorMap& b1, GemmParams& p) {
@@ -114,8 +132,11 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   p.tiles_n = (p.N + BN - 1) / BN;
   int64_t tiles = (int64_t)p.batch * p.tiles_m * p.tiles_n;
   WXX_REQUIRE(tiles < (int64_t(1) << 31), "gemm: too many tiles");
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  p.epi.tma_store = encode_c_map(&mc, p) ? 1 : 0;
   int grid = (int)(tiles < wxx::num_sms() ? tiles : wxx::num_sms());
-  tc_gemm_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, p);
+  tc_gemm_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }

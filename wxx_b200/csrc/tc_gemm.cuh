@@ -47,8 +47,10 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 4 / 6 / 8
   static constexpr int TMEM_COLS = 2 * BN;                    // 128 / 256 / 512
-  static constexpr int EPI_STAGE_FLOATS = 32 * 33;            // per epilogue warp
-  static constexpr int EPI_BYTES = 4 * EPI_STAGE_FLOATS * 4;  // 16.5 KB
+  // Per epilogue warp: two 4 KB staging tiles (32 x 32 fp32, 128B-swizzled
+  // for the TMA store); the padded-transpose fallback reuses the first 4.2 KB.
+  static constexpr int EPI_WARP_BYTES = 8192;
+  static constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;        // 32 KB
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
 };
 
@@ -121,6 +123,28 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+
+// Shared -> global tensor store of one box (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N committed bulk groups still read their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -257,6 +281,7 @@ struct EpiParams {
   int64_t bias_bs;
   float alpha;
   int hw_out;             // conv: Ho*Wo
+  int tma_store;          // kind 0 with bias_mode <= 1: C written by TMA stores
 };
 
 struct GemmParams {
@@ -481,7 +506,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0,
                    const __grid_constant__ CUtensorMap tm_a1,
                    const __grid_constant__ CUtensorMap tm_b0,
-                   const __grid_constant__ CUtensorMap tm_b1, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tm_b1,
+                   const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
@@ -618,9 +644,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
     // ---------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
-    float* stage = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES) +
-                   (warp - EPI_WARP0) * C::EPI_STAGE_FLOATS;
+    uint8_t* wstage = smem + C::STAGES * C::STAGE_BYTES + (warp - EPI_WARP0) * C::EPI_WARP_BYTES;
+    const bool use_tma = p.epi.kind == 0 && p.epi.tma_store;
     int local = 0;
+    int chunk_seq = 0;  // TMA-store staging buffer parity
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       int bt, tm, tn;
       tile_coords(p, t, bt, tm, tn);
@@ -628,21 +655,51 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, &abort_flag, p.err)) break;
       tc_fence_after();
-      int m = tm * BM + quarter * 32 + lane;
+      const int m0 = tm * BM + quarter * 32;
       uint32_t row_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
         tmem_ld_32x32(row_addr + (uint32_t)c, v);
         int n0 = tn * BN + c;
-        if (n0 < p.N) {
-          if (p.epi.kind == 0) epi_store_rows(p, bt, tm * BM + quarter * 32, n0, v, stage);
-          else epi_store(p, bt, m, n0, v);
+        if (n0 >= p.N) continue;
+        if (use_tma) {
+          // alpha and a per-column bias in registers, row -> swizzled staging
+          // tile, one TMA store per 32 x 32 chunk (clipped at the edges).
+          const float alpha = p.epi.alpha;
+          if (p.epi.bias_mode == 1) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[j] = v[j] * alpha + ((n0 + j < p.N) ? __ldg(p.epi.bias + n0 + j) : 0.f);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= alpha;
+          }
+          uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
+          if (lane == 0) bulk_wait_read<1>();  // the store that used `buf` has read it
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) = w;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tm_c, smem_u32(buf), n0, m0, bt);
+            bulk_commit();
+          }
+          ++chunk_seq;
+        } else if (p.epi.kind == 0) {
+          epi_store_rows(p, bt, m0, n0, v, reinterpret_cast<float*>(wstage));
+        } else {
+          epi_store(p, bt, m0 + lane, n0, v);
         }
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
     }
+    if (use_tma && lane == 0) bulk_wait<0>();  // all stores complete before exit
   } else if (warp >= GATHER_WARP0 && any_gather) {
     // ---------------------------------------------------- gather producers
     const int gtid = threadIdx.x - GATHER_WARP0 * 32;
