@@ -163,6 +163,51 @@ class HyenaW(Workload):
 WORKLOADS = {w.name: w for w in (GPT2Scaled(), GPT2Small(), ResNet18W(), HyenaW())}
 
 
+# ------------------------------------------------------------------ kernel sweep (config 1)
+
+class Sweep:
+    """One functional op of BASELINE config 1 on seeded N(0,1) inputs.
+
+    ``units`` is the algorithmic work of one call: FLOPs for the tensor-bound
+    matmuls, bytes that must cross HBM for the rest (inputs read once, outputs
+    written once)."""
+
+    def __init__(self, name, shapes, op, units, unit, bound, kernel, flush_l2):
+        self.name, self.shapes, self.op = name, shapes, op
+        self.units, self.unit, self.bound, self.kernel = units, unit, bound, kernel
+        self.flush_l2 = flush_l2
+        self.metric = f"{name} {unit}"
+
+
+def _mm(F, a, b):
+    return F.matmul_add(a, b, None)
+
+
+SWEEPS = {}
+for _n in (512, 2048, 8192):
+    SWEEPS[f"matmul_{_n}"] = Sweep(
+        f"matmul_{_n}", [(_n, _n), (_n, _n)], _mm, 2.0 * _n ** 3, "TFLOP/s", "tensor",
+        "tc_gemm_kernel (tcgen05 kind::tf32)", flush_l2=_n < 4096)
+SWEEPS["bmm"] = Sweep("bmm", [(64, 8, 1024, 32), (64, 8, 32, 1024)], _mm,
+                      (64 + 64 + 2048) * 2 ** 20, "GB/s", "hbm",
+                      "tc_gemm_kernel (batched, TMA-store epilogue)", flush_l2=False)
+SWEEPS["softmax"] = Sweep("softmax", [(64, 8, 1024, 1024)], lambda F, x: F.softmax(x, -1),
+                          4 * 2 ** 30, "GB/s", "hbm", "softmax_warp_kernel<32>", flush_l2=False)
+SWEEPS["fftconv"] = Sweep("fftconv", [(16, 256, 16384), (256, 16384)],
+                          lambda F, x, h: F.fftconv(x, h, 32768, out_len=16384),
+                          528 * 2 ** 20, "GB/s", "hbm",
+                          "fft_row_kernel<14, conv> (+ rfft of h)", flush_l2=False)
+for _ax in (0, 1):
+    SWEEPS[f"sum_axis{_ax}"] = Sweep(
+        f"sum_axis{_ax}", [(4096, 4096)], (lambda ax: lambda F, x: F.sum(x, ax))(_ax),
+        64 * 2 ** 20 + 16 * 2 ** 10, "GB/s", "hbm",
+        "col_reduce_cluster_kernel" if _ax == 0 else "row_reduce_kernel", flush_l2=True)
+    SWEEPS[f"mean_axis{_ax}"] = Sweep(
+        f"mean_axis{_ax}", [(4096, 4096)], (lambda ax: lambda F, x: F.mean(x, ax))(_ax),
+        64 * 2 ** 20 + 16 * 2 ** 10, "GB/s", "hbm",
+        "col_reduce_cluster_kernel" if _ax == 0 else "row_reduce_kernel", flush_l2=True)
+
+
 # ------------------------------------------------------------------ helpers
 
 def load_peaks():
@@ -258,10 +303,200 @@ def time_cpu_sample(wl, seconds=10.0, max_reps=50):
     return units * reps / dt, units, reps, dt
 
 
+# ------------------------------------------------------------------ sweep runs
+
+def _sweep_cpu(sw, arrays):
+    """fp32 numpy version of a sweep op (CPU baseline / reference arm)."""
+    import oracle.kernels as K
+
+    if sw.name.startswith("matmul") or sw.name == "bmm":
+        return lambda: np.matmul(arrays[0], arrays[1])
+    if sw.name == "softmax":
+        def f():
+            e = np.exp(arrays[0] - arrays[0].max(-1, keepdims=True))
+            return e / e.sum(-1, keepdims=True)
+        return f
+    if sw.name == "fftconv":
+        return lambda: np.fft.irfft(np.fft.rfft(arrays[0], 32768) * np.fft.rfft(arrays[1], 32768),
+                                    32768)[..., :16384]
+    ax = int(sw.name[-1])
+    if sw.name.startswith("sum"):
+        return lambda: arrays[0].sum(axis=ax)
+    _ = K
+    return lambda: arrays[0].mean(axis=ax)
+
+
+def _sweep_cpu_sample(sw, rng):
+    """A bounded slice of the sweep input for CPU timing, and its fraction."""
+    if sw.name == "softmax":
+        return [rng.standard_normal((4, 8, 1024, 1024), dtype=np.float32)], 4 / 64
+    if sw.name == "bmm":
+        return [rng.standard_normal((4, 8, 1024, 32), dtype=np.float32),
+                rng.standard_normal((4, 8, 32, 1024), dtype=np.float32)], 4 / 64
+    if sw.name == "fftconv":
+        return [rng.standard_normal((1, 256, 16384), dtype=np.float32),
+                rng.standard_normal((256, 16384), dtype=np.float32)], 1 / 16
+    if sw.name == "matmul_8192":
+        return [rng.standard_normal((1024, 8192), dtype=np.float32),
+                rng.standard_normal((8192, 8192), dtype=np.float32)], 1 / 8
+    return [rng.standard_normal(s, dtype=np.float32) for s in sw.shapes], 1.0
+
+
+def run_sweep(args, rank, world, local):
+    """Times one config-1 kernel; N > 1 runs independent replicas (weak scaling)."""
+    os.environ.setdefault("WXX_DEVICE", str(local))
+    import wxx_b200 as wxx
+    from wxx_b200.backend import device as dev
+    from wxx_b200 import distributed as wd
+
+    sw = SWEEPS[args.workload]
+    dist = wd.init_host_group() if world > 1 else None
+    F = wxx.functional
+    wxx.set_matmul_mode("tf32")
+    rng = np.random.default_rng(rank)
+    host = [rng.standard_normal(s, dtype=np.float32) for s in sw.shapes]
+    devs = [F.from_numpy(a) for a in host]
+    flush = Tensor_for_flush = None
+    if sw.flush_l2:
+        from wxx_b200.Tensor import Tensor
+
+        Tensor_for_flush = Tensor._empty([64 * 2 ** 20], "f32")   # 256 MB > 126 MB L2
+        flush = lambda: F.assign(Tensor_for_flush, 0.0)            # one fill kernel
+
+    def timed(n, fn):
+        total = 0.0
+        if flush is None:
+            e0 = dev.Event().record()
+            for _ in range(n):
+                fn()
+            e1 = dev.Event().record()
+            return e0.elapsed_ms(e1) / n
+        for _ in range(n):
+            flush()
+            e0 = dev.Event().record()
+            fn()
+            e1 = dev.Event().record()
+            total += e0.elapsed_ms(e1)
+        return total / n
+
+    for _ in range(args.warmup):
+        sw.op(F, *devs)
+    dev.synchronize()
+    if dist is not None:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    n0 = dev.launch_count()
+    ms = timed(args.steps, lambda: sw.op(F, *devs))
+    launches = dev.launch_count() - n0 - (args.steps if flush is not None else 0)
+    clocks = sampler.stop()
+    if dist is not None:
+        import torch
+
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    scale = 1e12 if sw.unit == "TFLOP/s" else 1e9
+    value = world * sw.units / (ms / 1000.0) / scale
+
+    # e2e through the public API from pinned host memory, result read back.
+    pins = []
+    for a in host:
+        pb = dev.PinnedHostBuffer(a.nbytes)
+        pb.as_numpy(np.float32, a.shape)[...] = a
+        pins.append(pb)
+    from wxx_b200.Tensor import Tensor
+
+    res_box = {}
+
+    def e2e():
+        ts = []
+        for a, pb in zip(host, pins):
+            t = Tensor._empty(list(a.shape), "f32")
+            wxx.backend.lib.F.wxx_memcpy_h2d(t.buffer.ptr, pb.ptr, a.nbytes)
+            ts.append(t)
+        out = sw.op(F, *ts)
+        if "pin" not in res_box:
+            res_box["pin"] = dev.PinnedHostBuffer(out.nbytes)
+        wxx.backend.lib.F.wxx_memcpy_d2h_async(res_box["pin"].ptr, out.ptr, out.nbytes)
+        res_box["bytes"] = out.nbytes
+
+    for _ in range(2):
+        e2e()
+    dev.synchronize()
+    e2e_ms = timed(max(3, args.steps // 2), e2e)
+    e2e_value = world * sw.units / (e2e_ms / 1000.0) / scale
+    peaks, kind = load_peaks()
+    if sw.bound == "tensor":
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2.0
+        basis = f"{kind} bf16 dense TFLOP/s / 2 (TF32 rate)"
+        achieved = sw.units / (ms / 1000.0) / 1e12
+    else:
+        peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        basis = f"{kind} HBM copy GB/s"
+        achieved = sw.units / (ms / 1000.0) / 1e9
+    line = {
+        "metric": sw.metric, "value": value, "unit": sw.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{sw.name} {sw.shapes}", "l2": "flushed between steps"
+                   if sw.flush_l2 else "inputs larger than L2", "parallelism": "replicas"},
+        "roofline": {"kernel": sw.kernel, "bound": sw.bound, "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s" if sw.bound == "tensor" else "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_basis": basis},
+        "clocks": clocks, "gpu_launches": int(launches),
+        "e2e": {"value": e2e_value, "unit": sw.unit,
+                "h2d_bytes_per_step": int(sum(a.nbytes for a in host)),
+                "d2h_bytes_per_step": int(res_box.get("bytes", 0))},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        arrays, frac = _sweep_cpu_sample(sw, np.random.default_rng(0))
+        fn = _sweep_cpu(sw, arrays)
+        fn()
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < args.cpu_seconds and reps < 200:
+            fn()
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        line["cpu_baseline"] = {"value": sw.units * frac / dt / scale, "unit": sw.unit,
+                                "cores": cpu_cores(), "kind": "port",
+                                "sample": f"{frac:.3g} of the workload per call, {reps} calls "
+                                          "(numpy fp32, host BLAS threads)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args, rank, world):
     if rank != 0:
+        return 0
+    if args.workload in SWEEPS:
+        sw = SWEEPS[args.workload]
+        arrays, frac = _sweep_cpu_sample(sw, np.random.default_rng(0))
+        fn = _sweep_cpu(sw, arrays)
+        for _ in range(args.warmup):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        dt = (time.perf_counter() - t0) / args.steps
+        scale = 1e12 if sw.unit == "TFLOP/s" else 1e9
+        value = sw.units * frac / dt / scale
+        print(json.dumps({
+            "metric": sw.metric, "value": value, "unit": sw.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": f"{sw.name} {sw.shapes}"},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": sw.unit, "cores": cpu_cores(), "kind": "port",
+                             "sample": f"{frac:.3g} of the workload per step (numpy fp32)"},
+            "e2e": {"value": value, "unit": sw.unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
         return 0
     wl = WORKLOADS[args.workload]
     from oracle import init as oracle_init, models as oracle_models
@@ -445,7 +680,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2_scaled")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(SWEEPS),
+                    default="gpt2_scaled")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
@@ -456,6 +692,8 @@ def main(argv=None):
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload in SWEEPS:
+        return run_sweep(args, rank, world, local)
     return run_ours(args, rank, world, local)
 
 

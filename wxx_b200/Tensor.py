@@ -67,16 +67,12 @@ class Tensor:
                 raw = np.ascontiguousarray(raw[: self.nbytes])
                 check(F.wxx_memcpy_h2d(buffer.ptr, raw.ctypes.data, self.nbytes), "upload")
             elif n:
-                if self.type == "c64":
-                    check(F.wxx_memset(buffer.ptr, 0, self.nbytes), "fill")
-                else:
-                    bits = _fill_bits(value, self.type)
-                    if bits == 0:
-                        check(F.wxx_memset(buffer.ptr, 0, self.nbytes), "fill")
-                    else:
-                        shp = (ctypes.c_int64 * 1)(n)
-                        one = (ctypes.c_int64 * 1)(1)
-                        check(F.wxx_strided_fill(buffer.ptr, 0, one, 1, shp, bits), "fill")
+                # every fill is a library kernel (c64 zeros: 2n zero words)
+                words = 2 * n if self.type == "c64" else n
+                bits = 0 if self.type == "c64" else _fill_bits(value, self.type)
+                shp = (ctypes.c_int64 * 1)(words)
+                one = (ctypes.c_int64 * 1)(1)
+                check(F.wxx_strided_fill(buffer.ptr, 0, one, 1, shp, bits), "fill")
         self.buffer = buffer
         self.requires_grad = requires_grad
         self.creator = None
