@@ -150,6 +150,13 @@ int wxx_conv2d(float* Y, const float* X, const float* W, const float* bias, int 
                int H, int Wd, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int dh,
                int dw, int mode);
 
+/* nn/module.py:460-495 MultiHeadAttention core fused (QK^T * scale (+ mask), softmax, PV)
+ * on tcgen05 TF32.  Q (B, Sq, H, hd) row stride q_ld, K/V (B, Sk, H, hd) row stride kv_ld,
+ * O (B, Sq, H, hd) row stride o_ld; hd 32 or 64; causal masks keys after the query. */
+int wxx_attention(float* O, const float* Q, const float* K, const float* V, int B, int H, int Sq,
+                  int Sk, int hd, int64_t q_ld, int64_t kv_ld, int64_t o_ld, float scale,
+                  const float* mask, int64_t mask_ld, int causal);
+
 /* ---------------------------------------------------------------- pooling */
 
 /* functional/convolution.py:60-125 maxpool2d (maxpool2d.wgsl); idx may be NULL */

@@ -5,6 +5,8 @@ Tolerances (norm-wise: max |got - ref| / max |ref|):
   fp32 elementwise, reductions, norms   1e-5 (activations with transcendental
                                          functions 2e-6 absolute on unit-scale data)
   matmul / conv2d                       2e-3 in TF32 mode, 1e-5 in 3xTF32 mode
+  fused attention (TF32)                4e-3: two chained TF32 products (Q K^T,
+                                         then P V), each with truncated operands
   FFT (rfft / irfft / fftconv)          2e-5 of the largest output
 """
 
@@ -409,3 +411,47 @@ def test_fftconv_matches_reference_chain(B, D, L, rng):
     # the unfused reference chain through the public ops gives the same result
     chain = F.irfft(F.complex_mul(F.rfft(up(x), n)[0], F.rfft(up(h), n)[0]), n)
     assert rel(chain.numpy()[..., :L], ref) < 2e-5
+
+
+# ------------------------------------------------------------ fused attention
+
+def _attention_ref(q, k, v, H, mask=None, causal=False):
+    """Reference chain of nn/module.py:460-495 in float64 (oracle ops)."""
+    B, S, D = q.shape
+    Sk = k.shape[1]
+    hd = D // H
+
+    def heads(t, n):
+        return t.reshape(B, n, H, hd).transpose(0, 2, 1, 3).reshape(B * H, n, hd)
+
+    s = K.matmul_add(heads(q, S), heads(k, Sk), None, transpose_b=True) * np.float32(1 / np.sqrt(hd))
+    if causal:
+        m = np.where(np.arange(Sk)[None, :] <= np.arange(S)[:, None], 0.0, -1e9).astype(np.float32)
+        s = s + m
+    elif mask is not None:
+        s = s + mask
+    p = K.softmax(s.astype(np.float32), -1)
+    o = K.matmul_add(p, heads(v, Sk))
+    return o.reshape(B, H, S, hd).transpose(0, 2, 1, 3).reshape(B, S, D)
+
+
+@pytest.mark.parametrize("B,S,H,hd,kind", [(2, 256, 4, 64, "causal"), (1, 100, 2, 32, "causal"),
+                                           (2, 300, 3, 64, "mask"), (1, 128, 2, 32, "none"),
+                                           (3, 200, 2, 64, "none"), (8, 1024, 16, 64, "causal"),
+                                           (4, 256, 8, 32, "causal")])
+def test_fused_attention(B, S, H, hd, kind, rng):
+    F = _w().functional
+    D = H * hd
+    q = rng.standard_normal((B, S, D)).astype(np.float32)
+    k = rng.standard_normal((B, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, S, D)).astype(np.float32)
+    mask = None
+    if kind == "mask":
+        mask = np.where(rng.random((S, S)) < 0.3, -1e9, rng.standard_normal((S, S))).astype(np.float32)
+        np.fill_diagonal(mask, 0.0)
+    got = F.attention(up(q), up(k), up(v), H, mask=None if mask is None else up(mask),
+                      causal=(kind == "causal")).numpy()
+    ref = _attention_ref(q, k, v, H, mask, kind == "causal")
+    assert got.shape == ref.shape
+    assert rel(got, ref) < 4e-3, rel(got, ref)
+    assert _w().backend.device_status() == 0

@@ -80,6 +80,8 @@ SIGNATURES = {
     "wxx_matmul": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_i64,
                    c_i64, c_i64, c_i64, c_int, c_int, c_int, c_float, c_int],
     "wxx_conv2d": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14,
+    "wxx_attention": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                      c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int],
     "wxx_maxpool2d": [c_void_p, c_void_p, c_void_p] + [c_int] * 10,
     "wxx_adaptive_avgpool2d": [c_void_p, c_void_p] + [c_int] * 6,
     "wxx_rfft": [c_void_p, c_i64, c_void_p, c_i64, c_i64, c_i64, c_i64],

@@ -1,0 +1,400 @@
+// Fused multi-head attention on tcgen05 (TF32), forward only.
+//
+// Computes, per (batch b, head h), the reference's MultiHeadAttention core
+// (nn/module.py:460-495):
+//     scores = (Q K^T) * scale  (+ mask)      softmax over keys      O = P V
+// without materialising the (B*H, S, S) score tensor.  Q, K, V are read in
+// place from the projection outputs laid out (B, S, H, hd) (the reshape /
+// permute / reshape head split of the reference becomes 4-D TMA boxes), and
+// O is written in the merged (B, S, H*hd) layout the output projection reads,
+// so the four head split/merge copies disappear too.
+//
+// One CTA owns 128 query rows of one (b, h); key/value blocks of 64:
+//   warp 0      TMA producer (Q once; K_j and V_j double-buffered)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
+//               S_j = Q K_j^T  (M=128, N=64, K=hd; both operands K-major)
+//               O_j = P_j V_j  (M=128, N=hd, K=64; V MN-major, 32B-atom swizzle)
+//   warps 2..5  one query row per thread: tcgen05.ld S_j, scale, mask, online
+//               softmax (running max m, running sum l), write P_j to shared
+//               memory in the K-major swizzled layout, then fold O_{j-1} from
+//               TMEM into a register accumulator rescaled by exp(m_old - m_new)
+// Masked scores (causal: key > query; or an additive mask) contribute exactly
+// zero probability, as exp(score - 1e9 - max) underflows to 0 in the
+// reference.  With `causal`, key blocks above the diagonal are skipped.
+// All waits are bounded (see tc_gemm.cuh).
+#include "tc_gemm.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+using namespace wxx_tc;
+
+namespace {
+
+constexpr int BQ = 128;   // query rows per CTA (UMMA M)
+constexpr int BKV = 64;   // keys per block (UMMA N of S, K of PV)
+constexpr int ATT_THREADS = 192;
+
+template <int HD>
+struct ACfg {
+  static constexpr int Q_BYTES = BQ * HD * 4;          // 32 KB (hd 64)
+  static constexpr int K_BYTES = BKV * HD * 4;         // 16 KB
+  static constexpr int V_BYTES = BKV * HD * 4;         // 16 KB
+  static constexpr int P_BYTES = BQ * BKV * 4;         // 32 KB
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
+  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+  static constexpr int SMEM = OFF_P + 2 * P_BYTES + 1024;
+  static constexpr int TMEM_S = 0;                     // 2 x 64 columns
+  static constexpr int TMEM_O = 2 * BKV;               // 2 x HD columns
+  static constexpr int TMEM_COLS = (2 * BKV + 2 * HD) <= 256 ? 256 : 512;
+};
+
+struct AttnParams {
+  int B, H, Sq, Sk;
+  int n_qblocks;
+  float scale;
+  int causal;
+  const float* mask;      // additive (Sq, Sk) mask, row stride mask_ld, or NULL
+  int64_t mask_ld;
+  int* err;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_o, const AttnParams p) {
+  using C = ACfg<HD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2];
+  __shared__ __align__(8) uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // Heaviest query blocks first (causal work grows with the block index).
+  const int bh = blockIdx.x % (p.B * p.H);
+  const int qb = p.n_qblocks - 1 - blockIdx.x / (p.B * p.H);
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qb * BQ;
+  int n_kv = (p.Sk + BKV - 1) / BKV;
+  if (p.causal) {
+    int last = (q0 + BQ - 1) / BKV + 1;
+    if (last < n_kv) n_kv = last;
+  }
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_full[s], 1);
+      mbar_init(&o_free[s], 128);
+    }
+    mbar_init(&drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(&q_full, C::Q_BYTES);
+#pragma unroll
+      for (int a = 0; a < HD / 32; ++a)
+        tma_load_4d(smem_u32(smem + a * (BQ * 128)), &tm_q, &q_full, a * 32, h, q0, b);
+      uint32_t issued_mask = 0, issued_par = 0;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, &abort_flag, p.err)) { ok = false; break; }
+        mbar_arrive_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
+        uint8_t* kd = smem + C::OFF_K + s * C::K_BYTES;
+        uint8_t* vd = smem + C::OFF_V + s * C::V_BYTES;
+#pragma unroll
+        for (int a = 0; a < HD / 32; ++a) {
+          tma_load_4d(smem_u32(kd + a * (BKV * 128)), &tm_k, &kv_full[s], a * 32, h, j * BKV, b);
+          tma_load_4d(smem_u32(vd + a * (BKV * 128)), &tm_v, &kv_full[s], a * 32, h, j * BKV, b);
+        }
+        issued_mask |= 1u << s;
+        issued_par = (issued_par & ~(1u << s)) | (((uint32_t)(j >> 1) & 1u) << s);
+      }
+      volatile int no_abort = 0;
+      mbar_wait(&q_full, 0, &no_abort, p.err);
+      for (int s = 0; s < 2; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&kv_full[s], (issued_par >> s) & 1, &no_abort, p.err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_s = idesc_tf32_mn(BQ, BKV, false, false);
+      const uint32_t idesc_o = idesc_tf32_mn(BQ, HD, false, true);
+      const uint32_t sq = smem_u32(smem);
+      bool ok = mbar_wait(&q_full, 0, &abort_flag, p.err);
+      tc_fence_after();
+      auto issue_pv = [&](int jj) -> bool {
+        int s = jj & 1;
+        if (!mbar_wait(&p_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
+        if (jj >= 2 && !mbar_wait(&o_free[s], ((jj - 2) >> 1) & 1, &abort_flag, p.err)) return false;
+        tc_fence_after();
+        uint32_t sp = sq + C::OFF_P + s * C::P_BYTES;
+        uint32_t sv = sq + C::OFF_V + s * C::V_BYTES;
+        uint32_t d = tmem_base + C::TMEM_O + s * HD;
+#pragma unroll
+        for (int kk = 0; kk < BKV / 8; ++kk) {
+          uint64_t ad = sdesc(sp + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          uint64_t bd = sdesc(sv + kk * 1024, BKV * 128, 512, kLayoutSW128Base32B);
+          umma_tf32(d, ad, bd, idesc_o, kk ? 1u : 0u);
+        }
+        umma_commit(&o_full[s]);
+        umma_commit(&kv_empty[s]);
+        return true;
+      };
+      for (int j = 0; j < n_kv && ok; ++j) {
+        int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sk = sq + C::OFF_K + s * C::K_BYTES;
+        uint32_t d = tmem_base + C::TMEM_S + s * BKV;
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          uint64_t ad = sdesc(sq + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          uint64_t bd = sdesc(sk + (kk >> 2) * (BKV * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+          umma_tf32(d, ad, bd, idesc_s, kk ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && n_kv >= 1) issue_pv(n_kv - 1);
+      umma_commit(&drain_bar);
+      volatile int no_abort = 0;
+      mbar_wait(&drain_bar, 0, &no_abort, p.err);
+    }
+  } else {
+    // ------------------------------------------------ softmax / correction
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;          // TMEM lane = query row in the tile
+    const int qrow = q0 + row;
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    float o_acc[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    float m_blk[2] = {-INFINITY, -INFINITY};      // running max used by P_j, j mod 2
+    float m_applied = -INFINITY;
+    bool ok = true;
+
+    auto fold = [&](int jj) -> bool {
+      int s = jj & 1;
+      if (!mbar_wait(&o_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
+      tc_fence_after();
+      float v[32];
+      float corr = (m_applied == -INFINITY) ? 0.f : __expf(m_applied - m_blk[s]);
+#pragma unroll
+      for (int c = 0; c < HD; c += 32) {
+        tmem_ld_32x32(lane_addr + C::TMEM_O + s * HD + c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o_acc[c + i] = o_acc[c + i] * corr + v[i];
+      }
+      tc_fence_before();
+      mbar_arrive(&o_free[s]);
+      m_applied = m_blk[s];
+      return true;
+    };
+
+    for (int j = 0; j < n_kv && ok; ++j) {
+      int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
+      tc_fence_after();
+      float x[BKV];
+      {
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < BKV; c += 32) {
+          tmem_ld_32x32(lane_addr + C::TMEM_S + s * BKV + c, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[c + i] = v[i];
+        }
+      }
+      const int k0 = j * BKV;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BKV; ++i) {
+        int key = k0 + i;
+        float sc = x[i] * p.scale;
+        bool masked = key >= p.Sk || (p.causal && key > qrow);
+        if (!masked && p.mask != nullptr && qrow < p.Sq) sc = sc + p.mask[(int64_t)qrow * p.mask_ld + key];
+        x[i] = masked ? -INFINITY : sc;
+        mx = fmaxf(mx, x[i]);
+      }
+      float m_new = fmaxf(m_run, mx);
+      float rs = 0.f;
+      // A row with every key masked so far keeps p = 0 (m_new = -inf).
+#pragma unroll
+      for (int i = 0; i < BKV; ++i) {
+        float pv = (x[i] == -INFINITY) ? 0.f : __expf(x[i] - m_new);
+        x[i] = pv;
+        rs += pv;
+      }
+      l_run = (m_run == -INFINITY ? 0.f : l_run * __expf(m_run - m_new)) + rs;
+      m_run = m_new;
+      m_blk[s] = m_new;
+      // P_j -> shared memory, K-major 128B-swizzled (2 atoms of 32 keys).
+      uint8_t* pb = smem + C::OFF_P + s * C::P_BYTES;
+#pragma unroll
+      for (int a = 0; a < BKV / 32; ++a) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 w = make_float4(x[a * 32 + 4 * q], x[a * 32 + 4 * q + 1], x[a * 32 + 4 * q + 2],
+                                 x[a * 32 + 4 * q + 3]);
+          *reinterpret_cast<float4*>(pb + a * (BQ * 128) + row * 128 + ((q ^ (row & 7)) << 4)) = w;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[s]);
+      if (j >= 1 && !fold(j - 1)) { ok = false; break; }
+    }
+    if (ok && n_kv >= 1) ok = fold(n_kv - 1);
+    if (ok) {
+      float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      // Stage 32 x 32 chunks in the (now idle) P region and TMA-store them
+      // into O[b, q0 + 32*quarter + r, h, c..c+31].
+      uint8_t* st = smem + C::OFF_P + (warp - 2) * 4096;
+#pragma unroll
+      for (int c = 0; c < HD; c += 32) {
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 w = make_float4(o_acc[c + 4 * q] * inv, o_acc[c + 4 * q + 1] * inv,
+                                 o_acc[c + 4 * q + 2] * inv, o_acc[c + 4 * q + 3] * inv);
+          *reinterpret_cast<float4*>(st + lane * 128 + ((q ^ (lane & 7)) << 4)) = w;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_4d(&tm_o, smem_u32(st), c, h, q0 + quarter * 32, b);
+          bulk_commit();
+        }
+      }
+      if (lane == 0) bulk_wait<0>();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_attn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// 4-D map over a (B, S, H, hd) tensor with row stride ld (elements between
+// consecutive s) and batch stride bs: dims {hd, H, S, B}, box {32, 1, rows, 1}.
+bool encode_bshd(CUtensorMap* map, const float* base, int B, int S, int H, int HD, int64_t ld,
+                 int64_t bs, int rows, bool mn_major) {
+  auto enc = get_encode_attn();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 4) % 16 || (bs * 4) % 16) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)HD * 4, (cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
+  cuuint32_t box[4] = {32, 1, (cuuint32_t)rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int HD>
+int launch_attention(float* O, const float* Q, const float* K, const float* V, int B, int H,
+                     int Sq, int Sk, int64_t q_ld, int64_t kv_ld, int64_t o_ld, float scale,
+                     const float* mask, int64_t mask_ld, int causal) {
+  using C = ACfg<HD>;
+  CUtensorMap mq, mk, mv, mo;
+  if (!encode_bshd(&mq, Q, B, Sq, H, HD, q_ld, q_ld * Sq, BQ, false) ||
+      !encode_bshd(&mk, K, B, Sk, H, HD, kv_ld, kv_ld * Sk, BKV, false) ||
+      !encode_bshd(&mv, V, B, Sk, H, HD, kv_ld, kv_ld * Sk, BKV, true) ||
+      !encode_bshd(&mo, O, B, Sq, H, HD, o_ld, o_ld * Sq, 32, false)) {
+    wxx::set_error("wxx_attention: operands are not 16-byte addressable for TMA");
+    return WXX_E_ARG;
+  }
+  static bool attr = false;
+  if (!attr) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr = true;
+  }
+  AttnParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = B;
+  p.H = H;
+  p.Sq = Sq;
+  p.Sk = Sk;
+  p.n_qblocks = (Sq + BQ - 1) / BQ;
+  p.scale = scale;
+  p.causal = causal;
+  p.mask = mask;
+  p.mask_ld = mask_ld;
+  p.err = wxx::device_error_word();
+  int64_t grid = (int64_t)B * H * p.n_qblocks;
+  WXX_REQUIRE(grid < (int64_t(1) << 31), "wxx_attention: grid too large");
+  attention_kernel<HD><<<(unsigned)grid, ATT_THREADS, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+}  // namespace
+
+// O = softmax(scale * Q K^T (+ mask)) V per (batch, head), TF32 tensor cores.
+// Q: (B, Sq, H, hd) with row stride q_ld elements between consecutive
+// positions (H*hd for the merged projection output); K, V: (B, Sk, H, hd)
+// with row stride kv_ld; O: (B, Sq, H, hd) with row stride o_ld.
+// hd must be 32 or 64; pointers and strides 16-byte aligned.  causal = 1 masks
+// keys after the query position; mask (Sq x Sk, row stride mask_ld) is added
+// to the scaled scores when given.
+WXX_EXPORT int wxx_attention(float* O, const float* Q, const float* K, const float* V, int B,
+                             int H, int Sq, int Sk, int hd, int64_t q_ld, int64_t kv_ld,
+                             int64_t o_ld, float scale, const float* mask, int64_t mask_ld,
+                             int causal) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(B > 0 && H > 0 && Sq > 0 && Sk > 0, "wxx_attention: empty problem");
+  WXX_REQUIRE(hd == 32 || hd == 64, "wxx_attention: head dim %d not in {32, 64}", hd);
+  if (hd == 32)
+    return launch_attention<32>(O, Q, K, V, B, H, Sq, Sk, q_ld, kv_ld, o_ld, scale, mask, mask_ld,
+                                causal);
+  return launch_attention<64>(O, Q, K, V, B, H, Sq, Sk, q_ld, kv_ld, o_ld, scale, mask, mask_ld,
+                              causal);
+}

@@ -29,6 +29,7 @@ SOURCES = [
     "reduce.cu",
     "gemm.cu",
     "fft.cu",
+    "attention.cu",
     "pool.cu",
     "nccl.cu",
 ]

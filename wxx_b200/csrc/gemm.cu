@@ -130,6 +130,11 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   }
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + BN - 1) / BN;
+  // When A (per batch) fits comfortably in L2, stream B once with all row
+  // blocks live; otherwise raster in bands of 16 row blocks so that a band of
+  // A stays L2-resident while B is swept.
+  int64_t a_bytes = (int64_t)p.M * p.K * 4;
+  p.group_m = (a_bytes <= (48ll << 20) || p.tiles_m <= 16) ? p.tiles_m : 16;
   int64_t tiles = (int64_t)p.batch * p.tiles_m * p.tiles_n;
   WXX_REQUIRE(tiles < (int64_t(1) << 31), "gemm: too many tiles");
   CUtensorMap mc;

@@ -125,6 +125,24 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // Shared -> global tensor store of one box (bulk-group completion).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
                                              int c2) {
@@ -240,10 +258,14 @@ __device__ __forceinline__ uint64_t sdesc_mnmajor(uint32_t tile, int kk) {
   return sdesc(tile + kk * 1024, 4096, 512, kLayoutSW128Base32B);
 }
 
-// Instruction descriptor for kind::tf32: D f32, A/B tf32, M=128, N=BN.
-__host__ __device__ constexpr uint32_t idesc_tf32(int n, bool a_mn, bool b_mn) {
+// Instruction descriptor for kind::tf32: D f32 [4,6), A/B tf32 [7,10)/[10,13),
+// A/B major [15]/[16] (1 = MN-major), N>>3 [17,23), M>>4 [24,29).
+__host__ __device__ constexpr uint32_t idesc_tf32_mn(int m, int n, bool a_mn, bool b_mn) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) |
-         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_tf32(int n, bool a_mn, bool b_mn) {
+  return idesc_tf32_mn(BM, n, a_mn, b_mn);
 }
 
 // Byte offset of element (row, k) of a K-major 128B-swizzled tile
@@ -288,6 +310,7 @@ struct GemmParams {
   int M, N, K;
   int batch;
   int tiles_m, tiles_n;
+  int group_m;            // row blocks per raster band (tiles_m: plain row-fastest order)
   int num_kb;             // K-blocks per pass
   int passes;             // 1 = TF32; 3 = 3xTF32 (hi*lo, lo*hi, hi*hi)
   OperandSrc a, b;
@@ -295,11 +318,20 @@ struct GemmParams {
   int* err;
 };
 
+// Tile order: batch-major; inside a batch, bands of `group_m` row blocks,
+// row block fastest inside a band, then column block.  Concurrent tiles then
+// share a band of A (kept in L2) and a few column blocks of B.
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& bt, int& tm, int& tn) {
-  tm = t % p.tiles_m;
-  int r = t / p.tiles_m;
-  tn = r % p.tiles_n;
-  bt = r / p.tiles_n;
+  const int per_batch = p.tiles_m * p.tiles_n;
+  bt = t / per_batch;
+  int r = t - bt * per_batch;
+  const int band_tiles = p.group_m * p.tiles_n;
+  int band = r / band_tiles;
+  int in_band = r - band * band_tiles;
+  int rows_left = p.tiles_m - band * p.group_m;
+  int gm = rows_left < p.group_m ? rows_left : p.group_m;
+  tm = band * p.group_m + in_band % gm;
+  tn = in_band / gm;
 }
 
 // 3xTF32 operand parts: the tensor core reads the top 19 bits of each fp32

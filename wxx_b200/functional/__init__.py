@@ -8,6 +8,8 @@ forward path uses exist and raise ``NotImplementedError``.
 
 from ._common import get_matmul_mode, manual_seed, set_matmul_mode
 from .activations import (
+    attention,
+    attention_supported,
     cos,
     cosback,
     gelu,

@@ -78,3 +78,52 @@ def masked_softmax(score, mask):
                                    mask.shape[0]), "masked_softmax")
         return out
     return softmax(pointwise(score, mask, 0), -1)
+
+
+def attention_supported(q, n_heads, mask=None):
+    """True when ``attention`` can run the fused tcgen05 kernel for these
+    operands (TF32 mode, head dim 32 or 64, 16-byte aligned rows)."""
+    from ._common import get_matmul_mode
+
+    if get_matmul_mode() != "tf32" or len(q.shape) != 3:
+        return False
+    D = q.shape[-1]
+    if D % n_heads or D // n_heads not in (32, 64) or D % 4:
+        return False
+    if mask is not None and not getattr(mask, "_wxx_causal", False):
+        if len(mask.shape) != 2 or mask.type != "f32" or mask.stride[1] != 1:
+            return False
+    return True
+
+
+def attention(q, k, v, n_heads, mask=None, causal=False, scale=None):
+    """Fused multi-head attention ``softmax(scale * Q K^T + mask) V``.
+
+    ``q`` (B, Sq, D), ``k``/``v`` (B, Sk, D) are the projection outputs with
+    heads interleaved along D (head h owns columns h*hd..h*hd+hd-1, as
+    ``reshape(b, s, H, hd)`` in nn/module.py:460-495); the result is
+    (B, Sq, D) in the same merged layout.  ``causal`` masks keys after the
+    query position (what GPT2's -1e9 upper-triangular mask does); ``mask`` is
+    an additive (Sq, Sk) view.  Same values as the unfused
+    matmul -> scale -> add mask -> softmax -> matmul chain up to rounding."""
+    import math
+
+    q = dense(q)
+    k = dense(k)
+    v = dense(v)
+    B, Sq, D = q.shape
+    Sk = k.shape[1]
+    if tuple(k.shape) != (B, Sk, D) or tuple(v.shape) != (B, Sk, D):
+        raise ValueError(f"attention: q {q.shape}, k {k.shape}, v {v.shape} do not match")
+    hd = D // n_heads
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    mptr, mld = None, 0
+    if mask is not None and not causal:
+        if tuple(mask.shape) != (Sq, Sk):
+            raise ValueError(f"attention: mask shape {mask.shape} != {(Sq, Sk)}")
+        mptr, mld = mask.ptr, mask.stride[0]
+    out = empty((B, Sq, D), "f32", q.requires_grad or k.requires_grad or v.requires_grad)
+    check(F.wxx_attention(out.buffer.ptr, q.ptr, k.ptr, v.ptr, B, n_heads, Sq, Sk, hd, D, D, D,
+                          float(scale), mptr, mld, int(bool(causal))), "attention")
+    return out

@@ -71,9 +71,11 @@ class GPT2(Module):
             c = np.arange(self.max_len)[None, :]
             mask = from_numpy(np.where(c <= r, 0.0, -1e9).astype(np.float32))
             object.__setattr__(self, "_causal_mask_cache", mask)
-        if seq == self.max_len:
-            return mask
-        return mask.narrow(0, 0, seq).narrow(1, 0, seq)
+        # The tag lets MultiHeadAttention skip masked key blocks instead of
+        # reading the mask (the values are the same -1e9 upper triangle).
+        view = mask if seq == self.max_len else mask.narrow(0, 0, seq).narrow(1, 0, seq)
+        view._wxx_causal = True
+        return view
 
     def _positions(self, seq):
         pos = self._pos_cache.get(seq)

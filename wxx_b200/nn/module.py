@@ -366,6 +366,13 @@ class MultiHeadAttention(Module):
 
     def forward(self, x, mask=None):
         b, seq, _ = x.shape
+        fused_ok = context.MODE != 0 or self.drop.p == 0
+        if fused_ok and functional.attention_supported(x, self.n_heads, mask):
+            causal = bool(getattr(mask, "_wxx_causal", False))
+            o = functional.attention(self.q(x), self.k(x), self.v(x), self.n_heads,
+                                     mask=None if causal else mask, causal=causal,
+                                     scale=1.0 / math.sqrt(self.head_dim))
+            return self.out(o)
         q = self._heads(self.q(x), b, seq)
         k = self._heads(self.k(x), b, seq)
         v = self._heads(self.v(x), b, seq)
