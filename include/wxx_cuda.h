@@ -181,6 +181,17 @@ int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int64_t sb, in
 /* nn/hyena.py:208-216 fft_conv1d with a time-domain filter h (D, Lh) */
 int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd, int64_t sl,
                 const float* h, int64_t h_ld, int Lh, int B, int D, int L, int64_t n, int out_len);
+/* No counterpart in the reference.  wxx_fftconv without any allocation: the
+ * filter spectrum lives in a fixed 16 MiB device array inside the library.
+ * Limits: n <= 32768 and D*(n/2+1) <= 2^21 complex values, else WXX_E_ARG and
+ * nothing is launched.  The scratch needs no zeroing (each call writes it
+ * before reading it).  One array per device: calls that overlap on the device
+ * (other streams or threads) race on it.  The first call on a device looks up
+ * the array's address (cudaGetSymbolAddress, may load device code); make it
+ * before any stream capture. */
+int wxx_fftconv_static(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                       int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D, int L,
+                       int64_t n, int out_len);
 
 /* ---------------------------------------------------------------- NCCL
  * No reference counterpart (the reference drives one WebGPU device): the

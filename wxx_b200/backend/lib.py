@@ -90,6 +90,8 @@ SIGNATURES = {
                              c_int, c_int, c_int, c_i64, c_int],
     "wxx_fftconv": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64, c_int,
                     c_int, c_int, c_int, c_i64, c_int],
+    "wxx_fftconv_static": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64,
+                           c_int, c_int, c_int, c_int, c_i64, c_int],
     "wxx_nccl_unique_id": [P_u8],
     "wxx_nccl_init": [P_u8, c_int, c_int],
     "wxx_nccl_allgather": [c_void_p, c_void_p, c_u64],

@@ -29,6 +29,7 @@ SOURCES = [
     "reduce.cu",
     "gemm.cu",
     "fft.cu",
+    "fft_static.cu",
     "attention.cu",
     "pool.cu",
     "nccl.cu",
