@@ -197,6 +197,12 @@ SWEEPS["fftconv"] = Sweep("fftconv", [(16, 256, 16384), (256, 16384)],
                           lambda F, x, h: F.fftconv(x, h, 32768, out_len=16384),
                           528 * 2 ** 20, "GB/s", "hbm",
                           "fft_row_kernel<14, conv> (+ rfft of h)", flush_l2=False)
+# GPT2-scaled attention core (B 8, S 1024, 16 heads x 64, causal): useful
+# FLOPs are the two products over the S(S+1)/2 unmasked (query, key) pairs.
+SWEEPS["attention"] = Sweep("attention", [(8, 1024, 1024)] * 3,
+                            lambda F, q, k, v: F.attention(q, k, v, 16, causal=True),
+                            4.0 * 64 * 8 * 16 * (1024 * 1025 // 2), "TFLOP/s", "tensor",
+                            "attention_kernel<64> (tcgen05 kind::tf32, TMEM S/O)", flush_l2=True)
 for _ax in (0, 1):
     SWEEPS[f"sum_axis{_ax}"] = Sweep(
         f"sum_axis{_ax}", [(4096, 4096)], (lambda ax: lambda F, x: F.sum(x, ax))(_ax),
@@ -319,6 +325,15 @@ def _sweep_cpu(sw, arrays):
     if sw.name == "fftconv":
         return lambda: np.fft.irfft(np.fft.rfft(arrays[0], 32768) * np.fft.rfft(arrays[1], 32768),
                                     32768)[..., :16384]
+    if sw.name == "attention":
+        def attn():
+            B, S, D = arrays[0].shape
+            q, k, v = (a.reshape(B, S, 16, D // 16).transpose(0, 2, 1, 3) for a in arrays)
+            sc = np.matmul(q, k.transpose(0, 1, 3, 2)) * np.float32(1 / np.sqrt(D // 16))
+            sc = sc + np.triu(np.full((S, S), -1e9, np.float32), 1)
+            e = np.exp(sc - sc.max(-1, keepdims=True))
+            return np.matmul(e / e.sum(-1, keepdims=True), v)
+        return attn
     ax = int(sw.name[-1])
     if sw.name.startswith("sum"):
         return lambda: arrays[0].sum(axis=ax)
@@ -336,6 +351,8 @@ def _sweep_cpu_sample(sw, rng):
     if sw.name == "fftconv":
         return [rng.standard_normal((1, 256, 16384), dtype=np.float32),
                 rng.standard_normal((256, 16384), dtype=np.float32)], 1 / 16
+    if sw.name == "attention":
+        return [rng.standard_normal((1, 1024, 1024), dtype=np.float32) for _ in range(3)], 1 / 8
     if sw.name == "matmul_8192":
         return [rng.standard_normal((1024, 8192), dtype=np.float32),
                 rng.standard_normal((8192, 8192), dtype=np.float32)], 1 / 8

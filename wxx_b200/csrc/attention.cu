@@ -36,6 +36,14 @@ namespace {
 constexpr int BQ = 128;   // query rows per CTA (UMMA M)
 constexpr int BKV = 64;   // keys per block (UMMA N of S, K of PV)
 constexpr int ATT_THREADS = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the SFU (ex2.approx: relative error ~2^-22, 2^-inf = +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int HD>
 struct ACfg {
@@ -62,7 +70,7 @@ struct AttnParams {
   int* err;
 };
 
-template <int HD>
+template <int HD, bool HAS_MASK>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -188,33 +196,43 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   } else {
     // ------------------------------------------------ softmax / correction
+    // Scores are carried in the log2 domain, t = (score * scale + mask) * log2(e),
+    // so each probability is one ex2: p = 2^(t - m) = exp(score' - max).
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;          // TMEM lane = query row in the tile
     const int qrow = q0 + row;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const float sl2 = p.scale * kLog2e;
+    // Keys [0, lim) are visible to this row (causal stops at the query, Sk at
+    // the end); warp_lim is the smallest lim of the warp's 32 rows.
+    const int lim = p.causal ? min(p.Sk, qrow + 1) : p.Sk;
+    const int warp_lim = p.causal ? min(p.Sk, q0 + quarter * 32 + 1) : p.Sk;
+    const float* mrow = nullptr;
+    if (HAS_MASK && qrow < p.Sq) mrow = p.mask + (int64_t)qrow * p.mask_ld;
     float o_acc[HD];
 #pragma unroll
     for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
-    float m_blk[2] = {-INFINITY, -INFINITY};      // running max used by P_j, j mod 2
-    float m_applied = -INFINITY;
+    float m_blk0 = -INFINITY, m_blk1 = -INFINITY;  // running max used by P_j, j even / odd
+    float m_applied = -INFINITY;                   // running max o_acc is scaled to
     bool ok = true;
 
     auto fold = [&](int jj) -> bool {
       int s = jj & 1;
       if (!mbar_wait(&o_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
       tc_fence_after();
-      float v[32];
-      float corr = (m_applied == -INFINITY) ? 0.f : __expf(m_applied - m_blk[s]);
+      const float mb = s ? m_blk1 : m_blk0;
+      const float corr = (m_applied == mb) ? 1.f : fast_exp2(m_applied - mb);
 #pragma unroll
       for (int c = 0; c < HD; c += 32) {
+        float v[32];
         tmem_ld_32x32(lane_addr + C::TMEM_O + s * HD + c, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o_acc[c + i] = o_acc[c + i] * corr + v[i];
+        for (int i = 0; i < 32; ++i) o_acc[c + i] = fmaf(o_acc[c + i], corr, v[i]);
       }
       tc_fence_before();
       mbar_arrive(&o_free[s]);
-      m_applied = m_blk[s];
+      m_applied = mb;
       return true;
     };
 
@@ -222,50 +240,66 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       int s = j & 1;
       if (!mbar_wait(&s_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
       tc_fence_after();
-      float x[BKV];
-      {
-        float v[32];
+      float xa[32], xb[32];
+      tmem_ld_32x32_nowait(lane_addr + C::TMEM_S + s * BKV, xa);
+      tmem_ld_32x32_nowait(lane_addr + C::TMEM_S + s * BKV + 32, xb);
+      tmem_ld_wait(xa);
+      reg_pin(xb);
+#define ATT_X(i) ((i) < 32 ? xa[(i) & 31] : xb[(i) & 31])
+      const int k0 = j * BKV;
+      // Every key of the block visible to every row of the warp, no mask:
+      // the common case skips the per-key tests (warp-uniform branch).
+      const bool full = !HAS_MASK && (k0 + BKV <= warp_lim);
+      float mm[8];
 #pragma unroll
-        for (int c = 0; c < BKV; c += 32) {
-          tmem_ld_32x32(lane_addr + C::TMEM_S + s * BKV + c, v);
+      for (int c = 0; c < 8; ++c) mm[c] = -INFINITY;
+      if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[c + i] = v[i];
+        for (int i = 0; i < BKV; ++i) mm[i & 7] = fmaxf(mm[i & 7], ATT_X(i));
+      } else {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i) {
+          const int key = k0 + i;
+          float t = ATT_X(i) * sl2;
+          if (HAS_MASK) {
+            float mv = (mrow != nullptr && key < lim) ? __ldg(mrow + key) : 0.f;
+            t = fmaf(mv, kLog2e, t);
+          }
+          t = key < lim ? t : -INFINITY;
+          if (i < 32) xa[i & 31] = t; else xb[i & 31] = t;
+          mm[i & 7] = fmaxf(mm[i & 7], t);
         }
       }
-      const int k0 = j * BKV;
-      float mx = -INFINITY;
+      float mx = fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
+                       fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
+      if (full) mx *= sl2;                        // scale > 0: max commutes with it
+      const float m_new = fmaxf(m_run, mx);
+      // A row that sees no key yet keeps p = 0 (m_new = -inf, every t = -inf).
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      float acc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[c] = 0.f;
 #pragma unroll
       for (int i = 0; i < BKV; ++i) {
-        int key = k0 + i;
-        float sc = x[i] * p.scale;
-        bool masked = key >= p.Sk || (p.causal && key > qrow);
-        if (!masked && p.mask != nullptr && qrow < p.Sq) sc = sc + p.mask[(int64_t)qrow * p.mask_ld + key];
-        x[i] = masked ? -INFINITY : sc;
-        mx = fmaxf(mx, x[i]);
+        const float pv = full ? fast_exp2(fmaf(ATT_X(i), sl2, -m_use))
+                              : fast_exp2(ATT_X(i) - m_use);
+        if (i < 32) xa[i & 31] = pv; else xb[i & 31] = pv;
+        acc[i & 7] += pv;
       }
-      float m_new = fmaxf(m_run, mx);
-      float rs = 0.f;
-      // A row with every key masked so far keeps p = 0 (m_new = -inf).
-#pragma unroll
-      for (int i = 0; i < BKV; ++i) {
-        float pv = (x[i] == -INFINITY) ? 0.f : __expf(x[i] - m_new);
-        x[i] = pv;
-        rs += pv;
-      }
-      l_run = (m_run == -INFINITY ? 0.f : l_run * __expf(m_run - m_new)) + rs;
+      const float rs = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+      l_run = (m_run == m_new ? l_run : l_run * fast_exp2(m_run - m_new)) + rs;
       m_run = m_new;
-      m_blk[s] = m_new;
+      if (s) m_blk1 = m_new; else m_blk0 = m_new;
       // P_j -> shared memory, K-major 128B-swizzled (2 atoms of 32 keys).
       uint8_t* pb = smem + C::OFF_P + s * C::P_BYTES;
 #pragma unroll
-      for (int a = 0; a < BKV / 32; ++a) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 w = make_float4(x[a * 32 + 4 * q], x[a * 32 + 4 * q + 1], x[a * 32 + 4 * q + 2],
-                                 x[a * 32 + 4 * q + 3]);
-          *reinterpret_cast<float4*>(pb + a * (BQ * 128) + row * 128 + ((q ^ (row & 7)) << 4)) = w;
-        }
+      for (int q = 0; q < 8; ++q) {
+        *reinterpret_cast<float4*>(pb + row * 128 + ((q ^ (row & 7)) << 4)) =
+            make_float4(xa[4 * q], xa[4 * q + 1], xa[4 * q + 2], xa[4 * q + 3]);
+        *reinterpret_cast<float4*>(pb + BQ * 128 + row * 128 + ((q ^ (row & 7)) << 4)) =
+            make_float4(xb[4 * q], xb[4 * q + 1], xb[4 * q + 2], xb[4 * q + 3]);
       }
+#undef ATT_X
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[s]);
@@ -353,7 +387,9 @@ int launch_attention(float* O, const float* Q, const float* K, const float* V, i
   }
   static bool attr = false;
   if (!attr) {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD>,
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD, false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD, true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr = true;
   }
@@ -371,7 +407,10 @@ int launch_attention(float* O, const float* Q, const float* K, const float* V, i
   p.err = wxx::device_error_word();
   int64_t grid = (int64_t)B * H * p.n_qblocks;
   WXX_REQUIRE(grid < (int64_t(1) << 31), "wxx_attention: grid too large");
-  attention_kernel<HD><<<(unsigned)grid, ATT_THREADS, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
+  if (mask != nullptr)
+    attention_kernel<HD, true><<<(unsigned)grid, ATT_THREADS, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
+  else
+    attention_kernel<HD, false><<<(unsigned)grid, ATT_THREADS, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }
@@ -382,7 +421,7 @@ int launch_attention(float* O, const float* Q, const float* K, const float* V, i
 // Q: (B, Sq, H, hd) with row stride q_ld elements between consecutive
 // positions (H*hd for the merged projection output); K, V: (B, Sk, H, hd)
 // with row stride kv_ld; O: (B, Sq, H, hd) with row stride o_ld.
-// hd must be 32 or 64; pointers and strides 16-byte aligned.  causal = 1 masks
+// hd must be 32 or 64 and scale > 0; pointers and strides 16-byte aligned.  causal = 1 masks
 // keys after the query position; mask (Sq x Sk, row stride mask_ld) is added
 // to the scaled scores when given.
 WXX_EXPORT int wxx_attention(float* O, const float* Q, const float* K, const float* V, int B,
@@ -392,6 +431,7 @@ WXX_EXPORT int wxx_attention(float* O, const float* Q, const float* K, const flo
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(B > 0 && H > 0 && Sq > 0 && Sk > 0, "wxx_attention: empty problem");
   WXX_REQUIRE(hd == 32 || hd == 64, "wxx_attention: head dim %d not in {32, 64}", hd);
+  WXX_REQUIRE(scale > 0.f, "wxx_attention: scale must be positive");
   if (hd == 32)
     return launch_attention<32>(O, Q, K, V, B, H, Sq, Sk, q_ld, kv_ld, o_ld, scale, mask, mask_ld,
                                 causal);
