@@ -9,19 +9,26 @@
 // O is written in the merged (B, S, H*hd) layout the output projection reads,
 // so the four head split/merge copies disappear too.
 //
-// One CTA owns 128 query rows of one (b, h); key/value blocks of 64:
-//   warp 0      TMA producer (Q once; K_j and V_j double-buffered)
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
-//               S_j = Q K_j^T  (M=128, N=64, K=hd; both operands K-major)
-//               O_j = P_j V_j  (M=128, N=hd, K=64; V MN-major, 32B-atom swizzle)
-//   warps 2..5  one query row per thread: tcgen05.ld S_j, scale, mask, online
-//               softmax (running max m, running sum l), write P_j to shared
-//               memory in the K-major swizzled layout, then fold O_{j-1} from
-//               TMEM into a register accumulator rescaled by exp(m_old - m_new)
-// Masked scores (causal: key > query; or an additive mask) contribute exactly
-// zero probability, as exp(score - 1e9 - max) underflows to 0 in the
-// reference.  With `causal`, key blocks above the diagonal are skipped.
-// All waits are bounded (see tc_gemm.cuh).
+// One CTA owns two 128-row query tiles (A, B) of one (b, h); keys/values come
+// in blocks of 64 shared by both tiles:
+//   warp 0      TMA producer (Q once; K_j and V_j double-buffered, separate
+//               barriers so K_{j+2} loads as soon as S_j has read K_j)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, per block j:
+//               S_t(j) = Q_t K_j^T for both tiles (M=128, N=64, K=hd), then
+//               O_t += P_t(j-1) V_{j-1} (M=128, N=hd, K=64; V MN-major,
+//               32B-atom swizzle), O_t accumulated in TMEM across all blocks
+//   warps 2..5  tile A, warps 6..9 tile B: one query row per thread,
+//               tcgen05.ld S, online softmax in the log2 domain, P to shared
+//               memory (K-major swizzled), final O / l through a TMA store
+// Two softmax warpgroups interleave on every SM sub-partition, so one tile's
+// exponentials overlap the other's, and both overlap the tensor core.
+// The running max used for P is only raised (and O in TMEM rescaled) when a
+// row's max grows by more than 2^8 in probability units; P and the row sum l
+// always use the same max, so O / l is unchanged by the laziness.
+// Masked scores (causal: key > query; keys >= Sk) contribute exactly zero
+// probability, as exp(score - 1e9 - max) underflows to 0 in the reference; an
+// additive mask is added to the scaled scores.  With `causal`, key blocks above
+// a tile's diagonal are skipped.  All waits are bounded (see tc_gemm.cuh).
 #include "tc_gemm.cuh"
 
 #include <cudaTypedefs.h>
@@ -33,10 +40,12 @@ using namespace wxx_tc;
 
 namespace {
 
-constexpr int BQ = 128;   // query rows per CTA (UMMA M)
+constexpr int BQ = 128;   // query rows per tile (UMMA M)
+constexpr int NT = 2;     // query tiles per CTA
 constexpr int BKV = 64;   // keys per block (UMMA N of S, K of PV)
-constexpr int ATT_THREADS = 192;
+constexpr int ATT_THREADS = 64 + NT * 128;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;   // raise the max used for P only past 2^8
 
 // 2^x on the SFU (ex2.approx: relative error ~2^-22, 2^-inf = +0).
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -47,22 +56,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 template <int HD>
 struct ACfg {
-  static constexpr int Q_BYTES = BQ * HD * 4;          // 32 KB (hd 64)
+  static constexpr int Q_BYTES = BQ * HD * 4;          // per tile: 32 KB (hd 64)
   static constexpr int K_BYTES = BKV * HD * 4;         // 16 KB
   static constexpr int V_BYTES = BKV * HD * 4;         // 16 KB
-  static constexpr int P_BYTES = BQ * BKV * 4;         // 32 KB
-  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int P_BYTES = BQ * BKV * 4;         // per tile: 32 KB
+  static constexpr int OFF_K = NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
   static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-  static constexpr int SMEM = OFF_P + 2 * P_BYTES + 1024;
-  static constexpr int TMEM_S = 0;                     // 2 x 64 columns
-  static constexpr int TMEM_O = 2 * BKV;               // 2 x HD columns
-  static constexpr int TMEM_COLS = (2 * BKV + 2 * HD) <= 256 ? 256 : 512;
+  static constexpr int SMEM = OFF_P + NT * P_BYTES + 1024;
+  // TMEM per tile: S double buffer (2 x 64 columns) then O (hd columns).
+  static constexpr int TMEM_TILE = 2 * BKV + HD;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(NT * TMEM_TILE <= TMEM_COLS, "TMEM layout");
+  static_assert(SMEM <= 227 * 1024, "shared memory layout");
 };
 
 struct AttnParams {
   int B, H, Sq, Sk;
-  int n_qblocks;
+  int n_qpairs;
   float scale;
   int causal;
   const float* mask;      // additive (Sq, Sk) mask, row stride mask_ld, or NULL
@@ -79,8 +90,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   using C = ACfg<HD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full;
-  __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2];
-  __shared__ __align__(8) uint64_t s_full[2], p_full[2], o_full[2], o_free[2];
+  __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  __shared__ __align__(8) uint64_t s_full[NT][2], p_full[NT], p_empty[NT];
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -89,27 +100,37 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Heaviest query blocks first (causal work grows with the block index).
+  // Heaviest query pairs first (causal work grows with the pair index).
   const int bh = blockIdx.x % (p.B * p.H);
-  const int qb = p.n_qblocks - 1 - blockIdx.x / (p.B * p.H);
+  const int qp = p.n_qpairs - 1 - blockIdx.x / (p.B * p.H);
   const int b = bh / p.H, h = bh % p.H;
-  const int q0 = qb * BQ;
-  int n_kv = (p.Sk + BKV - 1) / BKV;
-  if (p.causal) {
-    int last = (q0 + BQ - 1) / BKV + 1;
-    if (last < n_kv) n_kv = last;
-  }
+  const int q0 = qp * (NT * BQ);
+  const int n_kv_all = (p.Sk + BKV - 1) / BKV;
+  // Key blocks each tile visits (0 for a tile entirely past Sq).
+  auto blocks_of = [&](int t) {
+    const int qt = q0 + t * BQ;
+    int n = qt < p.Sq ? n_kv_all : 0;
+    if (p.causal && n) n = min(n, (qt + BQ - 1) / BKV + 1);
+    return n;
+  };
+  static_assert(NT == 2, "tile bookkeeping below assumes two tiles");
+  const int n_t0 = blocks_of(0), n_t1 = blocks_of(1);
+  const int n_kv = max(n_t0, n_t1);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 128);
-      mbar_init(&o_full[s], 1);
-      mbar_init(&o_free[s], 128);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(&s_full[t][0], 1);
+      mbar_init(&s_full[t][1], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&p_empty[t], 1);
     }
     mbar_init(&drain_bar, 1);
     fence_barrier_init();
@@ -124,69 +145,90 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(&q_full, C::Q_BYTES);
+      mbar_arrive_expect_tx(&q_full, NT * C::Q_BYTES);
 #pragma unroll
-      for (int a = 0; a < HD / 32; ++a)
-        tma_load_4d(smem_u32(smem + a * (BQ * 128)), &tm_q, &q_full, a * 32, h, q0, b);
-      uint32_t issued_mask = 0, issued_par = 0;
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int a = 0; a < HD / 32; ++a)
+          tma_load_4d(smem_u32(smem + t * C::Q_BYTES + a * (BQ * 128)), &tm_q, &q_full, a * 32, h,
+                      q0 + t * BQ, b);
+      int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
       for (int j = 0; j < n_kv && ok; ++j) {
-        int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, &abort_flag, p.err)) { ok = false; break; }
-        mbar_arrive_expect_tx(&kv_full[s], C::K_BYTES + C::V_BYTES);
-        uint8_t* kd = smem + C::OFF_K + s * C::K_BYTES;
-        uint8_t* vd = smem + C::OFF_V + s * C::V_BYTES;
+        const int s = j & 1;
+        const uint32_t par = ((j >> 1) & 1) ^ 1;
+        if (!mbar_wait(&k_empty[s], par, &abort_flag, p.err)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
 #pragma unroll
-        for (int a = 0; a < HD / 32; ++a) {
-          tma_load_4d(smem_u32(kd + a * (BKV * 128)), &tm_k, &kv_full[s], a * 32, h, j * BKV, b);
-          tma_load_4d(smem_u32(vd + a * (BKV * 128)), &tm_v, &kv_full[s], a * 32, h, j * BKV, b);
-        }
-        issued_mask |= 1u << s;
-        issued_par = (issued_par & ~(1u << s)) | (((uint32_t)(j >> 1) & 1u) << s);
+        for (int a = 0; a < HD / 32; ++a)
+          tma_load_4d(smem_u32(smem + C::OFF_K + s * C::K_BYTES + a * (BKV * 128)), &tm_k,
+                      &k_full[s], a * 32, h, j * BKV, b);
+        last_k[s] = j;
+        if (!mbar_wait(&v_empty[s], par, &abort_flag, p.err)) { ok = false; break; }
+        mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
+#pragma unroll
+        for (int a = 0; a < HD / 32; ++a)
+          tma_load_4d(smem_u32(smem + C::OFF_V + s * C::V_BYTES + a * (BKV * 128)), &tm_v,
+                      &v_full[s], a * 32, h, j * BKV, b);
+        last_v[s] = j;
       }
+      // No load may still be landing when the CTA exits (abort path included).
       volatile int no_abort = 0;
       mbar_wait(&q_full, 0, &no_abort, p.err);
-      for (int s = 0; s < 2; ++s)
-        if (issued_mask & (1u << s)) mbar_wait(&kv_full[s], (issued_par >> s) & 1, &no_abort, p.err);
+      for (int s = 0; s < 2; ++s) {
+        if (last_k[s] >= 0) mbar_wait(&k_full[s], (last_k[s] >> 1) & 1, &no_abort, p.err);
+        if (last_v[s] >= 0) mbar_wait(&v_full[s], (last_v[s] >> 1) & 1, &no_abort, p.err);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc_s = idesc_tf32_mn(BQ, BKV, false, false);
       const uint32_t idesc_o = idesc_tf32_mn(BQ, HD, false, true);
-      const uint32_t sq = smem_u32(smem);
+      const uint32_t sbase = smem_u32(smem);
       bool ok = mbar_wait(&q_full, 0, &abort_flag, p.err);
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
-        int s = jj & 1;
-        if (!mbar_wait(&p_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
-        if (jj >= 2 && !mbar_wait(&o_free[s], ((jj - 2) >> 1) & 1, &abort_flag, p.err)) return false;
+        const int s = jj & 1;
+        if (!mbar_wait(&v_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
         tc_fence_after();
-        uint32_t sp = sq + C::OFF_P + s * C::P_BYTES;
-        uint32_t sv = sq + C::OFF_V + s * C::V_BYTES;
-        uint32_t d = tmem_base + C::TMEM_O + s * HD;
+        const uint32_t sv = sbase + C::OFF_V + s * C::V_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BKV / 8; ++kk) {
-          uint64_t ad = sdesc(sp + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-          uint64_t bd = sdesc(sv + kk * 1024, BKV * 128, 512, kLayoutSW128Base32B);
-          umma_tf32(d, ad, bd, idesc_o, kk ? 1u : 0u);
+        for (int t = 0; t < NT; ++t) {
+          if (jj >= (t ? n_t1 : n_t0)) continue;
+          if (!mbar_wait(&p_full[t], jj & 1, &abort_flag, p.err)) return false;
+          tc_fence_after();
+          const uint32_t sp = sbase + C::OFF_P + t * C::P_BYTES;
+          const uint32_t d = tmem_base + t * C::TMEM_TILE + 2 * BKV;
+#pragma unroll
+          for (int kk = 0; kk < BKV / 8; ++kk) {
+            uint64_t ad = sdesc(sp + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+            uint64_t bd = sdesc(sv + kk * 1024, BKV * 128, 512, kLayoutSW128Base32B);
+            umma_tf32(d, ad, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&p_empty[t]);
         }
-        umma_commit(&o_full[s]);
-        umma_commit(&kv_empty[s]);
+        umma_commit(&v_empty[s]);
         return true;
       };
       for (int j = 0; j < n_kv && ok; ++j) {
-        int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
+        const int s = j & 1;
+        if (!mbar_wait(&k_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
-        uint32_t sk = sq + C::OFF_K + s * C::K_BYTES;
-        uint32_t d = tmem_base + C::TMEM_S + s * BKV;
+        const uint32_t sk = sbase + C::OFF_K + s * C::K_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk) {
-          uint64_t ad = sdesc(sq + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-          uint64_t bd = sdesc(sk + (kk >> 2) * (BKV * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-          umma_tf32(d, ad, bd, idesc_s, kk ? 1u : 0u);
+        for (int t = 0; t < NT; ++t) {
+          if (j >= (t ? n_t1 : n_t0)) continue;
+          const uint32_t sq = sbase + t * C::Q_BYTES;
+          const uint32_t d = tmem_base + t * C::TMEM_TILE + s * BKV;
+#pragma unroll
+          for (int kk = 0; kk < HD / 8; ++kk) {
+            uint64_t ad = sdesc(sq + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+            uint64_t bd = sdesc(sk + (kk >> 2) * (BKV * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+            umma_tf32(d, ad, bd, idesc_s, kk ? 1u : 0u);
+          }
+          umma_commit(&s_full[t][s]);
         }
-        umma_commit(&s_full[s]);
+        umma_commit(&k_empty[s]);
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && n_kv >= 1) issue_pv(n_kv - 1);
@@ -195,54 +237,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_wait(&drain_bar, 0, &no_abort, p.err);
     }
   } else {
-    // ------------------------------------------------ softmax / correction
+    // ------------------------------------------------ softmax (one row per thread)
     // Scores are carried in the log2 domain, t = (score * scale + mask) * log2(e),
-    // so each probability is one ex2: p = 2^(t - m) = exp(score' - max).
-    const int quarter = warp & 3;
+    // so each probability is one ex2: p = 2^(t - m) = exp(score' - max').
+    const int tile = (warp - 2) >> 2;
+    const int quarter = warp & 3;                 // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;          // TMEM lane = query row in the tile
-    const int qrow = q0 + row;
-    const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const int qt = q0 + tile * BQ;
+    const int qrow = qt + row;
+    const int nt = tile ? n_t1 : n_t0;
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + tile * C::TMEM_TILE;
+    const uint32_t o_addr = lane_addr + 2 * BKV;
     const float sl2 = p.scale * kLog2e;
     // Keys [0, lim) are visible to this row (causal stops at the query, Sk at
     // the end); warp_lim is the smallest lim of the warp's 32 rows.
     const int lim = p.causal ? min(p.Sk, qrow + 1) : p.Sk;
-    const int warp_lim = p.causal ? min(p.Sk, q0 + quarter * 32 + 1) : p.Sk;
+    const int warp_lim = p.causal ? min(p.Sk, qt + quarter * 32 + 1) : p.Sk;
     const float* mrow = nullptr;
     if (HAS_MASK && qrow < p.Sq) mrow = p.mask + (int64_t)qrow * p.mask_ld;
-    float o_acc[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-    float m_blk0 = -INFINITY, m_blk1 = -INFINITY;  // running max used by P_j, j even / odd
-    float m_applied = -INFINITY;                   // running max o_acc is scaled to
+    uint8_t* pb = smem + C::OFF_P + tile * C::P_BYTES;
+    float m_used = -INFINITY;   // max that P and l are relative to
+    float l_run = 0.f;
     bool ok = true;
 
-    auto fold = [&](int jj) -> bool {
-      int s = jj & 1;
-      if (!mbar_wait(&o_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
-      tc_fence_after();
-      const float mb = s ? m_blk1 : m_blk0;
-      const float corr = (m_applied == mb) ? 1.f : fast_exp2(m_applied - mb);
-#pragma unroll
-      for (int c = 0; c < HD; c += 32) {
-        float v[32];
-        tmem_ld_32x32(lane_addr + C::TMEM_O + s * HD + c, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o_acc[c + i] = fmaf(o_acc[c + i], corr, v[i]);
+    for (int j = 0; j < nt && ok; ++j) {
+      const int s = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[tile][s], (j >> 1) & 1, &abort_flag, p.err))) {
+        ok = false;
+        break;
       }
-      tc_fence_before();
-      mbar_arrive(&o_free[s]);
-      m_applied = mb;
-      return true;
-    };
-
-    for (int j = 0; j < n_kv && ok; ++j) {
-      int s = j & 1;
-      if (!mbar_wait(&s_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
       tc_fence_after();
       float xa[32], xb[32];
-      tmem_ld_32x32_nowait(lane_addr + C::TMEM_S + s * BKV, xa);
-      tmem_ld_32x32_nowait(lane_addr + C::TMEM_S + s * BKV + 32, xb);
+      tmem_ld_32x32_nowait(lane_addr + s * BKV, xa);
+      tmem_ld_32x32_nowait(lane_addr + s * BKV + 32, xb);
       tmem_ld_wait(xa);
       reg_pin(xb);
 #define ATT_X(i) ((i) < 32 ? xa[(i) & 31] : xb[(i) & 31])
@@ -260,22 +287,33 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < BKV; ++i) {
           const int key = k0 + i;
-          float t = ATT_X(i) * sl2;
+          float tv = ATT_X(i) * sl2;
           if (HAS_MASK) {
             float mv = (mrow != nullptr && key < lim) ? __ldg(mrow + key) : 0.f;
-            t = fmaf(mv, kLog2e, t);
+            tv = fmaf(mv, kLog2e, tv);
           }
-          t = key < lim ? t : -INFINITY;
-          if (i < 32) xa[i & 31] = t; else xb[i & 31] = t;
-          mm[i & 7] = fmaxf(mm[i & 7], t);
+          tv = key < lim ? tv : -INFINITY;
+          if (i < 32) xa[i & 31] = tv; else xb[i & 31] = tv;
+          mm[i & 7] = fmaxf(mm[i & 7], tv);
         }
       }
       float mx = fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
                        fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
       if (full) mx *= sl2;                        // scale > 0: max commutes with it
-      const float m_new = fmaxf(m_run, mx);
-      // A row that sees no key yet keeps p = 0 (m_new = -inf, every t = -inf).
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      // Raise the max P is taken against only when it grew past 2^8 (always
+      // on the first block, which starts O); otherwise P <= 2^8 stays exact
+      // in fp32 and no rescale of O is needed.
+      const bool raise = (j == 0) ? true : (mx > m_used + kRescaleLog2);
+      const bool warp_rescale = __any_sync(0xffffffffu, j > 0 && raise);
+      float factor = 1.f;
+      if (raise) {
+        const float m_new = fmaxf(m_used, mx);
+        factor = (m_used == m_new) ? 1.f : fast_exp2(m_used - m_new);
+        l_run *= factor;
+        m_used = m_new;
+      }
+      // A row that sees no key yet keeps p = 0 (m_used = -inf, every t = -inf).
+      const float m_use = (m_used == -INFINITY) ? 0.f : m_used;
       float acc[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc[c] = 0.f;
@@ -286,12 +324,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (i < 32) xa[i & 31] = pv; else xb[i & 31] = pv;
         acc[i & 7] += pv;
       }
-      const float rs = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-      l_run = (m_run == m_new ? l_run : l_run * fast_exp2(m_run - m_new)) + rs;
-      m_run = m_new;
-      if (s) m_blk1 = m_new; else m_blk0 = m_new;
+      l_run += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+      // The single P buffer is free, and O holds every block < j, once the
+      // previous P V product finished.
+      if (j >= 1) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[tile], (j - 1) & 1, &abort_flag, p.err))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
       // P_j -> shared memory, K-major 128B-swizzled (2 atoms of 32 keys).
-      uint8_t* pb = smem + C::OFF_P + s * C::P_BYTES;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         *reinterpret_cast<float4*>(pb + row * 128 + ((q ^ (row & 7)) << 4)) =
@@ -300,31 +343,47 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             make_float4(xb[4 * q], xb[4 * q + 1], xb[4 * q + 2], xb[4 * q + 3]);
       }
 #undef ATT_X
+      if (warp_rescale) {
+        // O in TMEM holds blocks < j relative to the old max: scale the rows
+        // that raised theirs before P_j V_j accumulates on top.
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          float v[32];
+          tmem_ld_32x32(o_addr + c, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= factor;
+          tmem_st_32x32(o_addr + c, v);
+        }
+      }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full[s]);
-      if (j >= 1 && !fold(j - 1)) { ok = false; break; }
+      mbar_arrive(&p_full[tile]);
     }
-    if (ok && n_kv >= 1) ok = fold(n_kv - 1);
-    if (ok) {
-      float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      // Stage 32 x 32 chunks in the (now idle) P region and TMA-store them
-      // into O[b, q0 + 32*quarter + r, h, c..c+31].
-      uint8_t* st = smem + C::OFF_P + (warp - 2) * 4096;
+    if (ok && nt >= 1) {
+      // Last P V product done -> O complete in TMEM and the P buffer free for
+      // staging the output.
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[tile], (nt - 1) & 1, &abort_flag, p.err));
+      tc_fence_after();
+    }
+    if (ok && nt >= 1) {
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      // Stage 32 x 32 chunks in this warp's slice of the P buffer and
+      // TMA-store them into O[b, qt + 32*quarter + r, h, c..c+31].
+      uint8_t* st = pb + quarter * 4096;
 #pragma unroll
       for (int c = 0; c < HD; c += 32) {
+        float v[32];
+        tmem_ld_32x32(o_addr + c, v);
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 w = make_float4(o_acc[c + 4 * q] * inv, o_acc[c + 4 * q + 1] * inv,
-                                 o_acc[c + 4 * q + 2] * inv, o_acc[c + 4 * q + 3] * inv);
-          *reinterpret_cast<float4*>(st + lane * 128 + ((q ^ (lane & 7)) << 4)) = w;
-        }
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4*>(st + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+              make_float4(v[4 * q] * inv, v[4 * q + 1] * inv, v[4 * q + 2] * inv, v[4 * q + 3] * inv);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_4d(&tm_o, smem_u32(st), c, h, q0 + quarter * 32, b);
+          tma_store_4d(&tm_o, smem_u32(st), c, h, qt + quarter * 32, b);
           bulk_commit();
         }
       }
@@ -399,13 +458,13 @@ int launch_attention(float* O, const float* Q, const float* K, const float* V, i
   p.H = H;
   p.Sq = Sq;
   p.Sk = Sk;
-  p.n_qblocks = (Sq + BQ - 1) / BQ;
+  p.n_qpairs = (Sq + NT * BQ - 1) / (NT * BQ);
   p.scale = scale;
   p.causal = causal;
   p.mask = mask;
   p.mask_ld = mask_ld;
   p.err = wxx::device_error_word();
-  int64_t grid = (int64_t)B * H * p.n_qblocks;
+  int64_t grid = (int64_t)B * H * p.n_qpairs;
   WXX_REQUIRE(grid < (int64_t(1) << 31), "wxx_attention: grid too large");
   if (mask != nullptr)
     attention_kernel<HD, true><<<(unsigned)grid, ATT_THREADS, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
