@@ -590,8 +590,10 @@ def run_ours(args, rank, world, local):
     n0 = dev.launch_count()
     e0, e1 = dev.Event(), dev.Event()
     e0.record()
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         out = step(x_dev)
+    host_ms = (time.perf_counter() - h0) * 1000.0 / args.steps   # host enqueue time per step
     e1.record()
     barrier()
     launches = (dev.launch_count() - n0) / args.steps
@@ -671,6 +673,7 @@ def run_ours(args, rank, world, local):
         "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic",
         "config": wl.config(world), "roofline": roofline, "clocks": clocks,
         "gpu_launches": int(round(launches * args.steps)),
+        "host_enqueue_ms_per_step": host_ms,
         "e2e": {"value": e2e_value, "unit": wl.unit,
                 "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(d2h),
                 "includes": "pinned H2D of inputs, forward, all-gather, argmax, D2H of ids"},

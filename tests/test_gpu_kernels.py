@@ -265,6 +265,11 @@ GEMM_SHAPES = [
     ((), (3,), 64, 200, 64),
     ((32,), (32,), 256, 256, 32),
     ((2, 3), (2, 3), 70, 40, 24),
+    # >= 74 tiles of 256 x 256: SM-pair (cta_group::2) kernel
+    ((), (), 2304, 2304, 64),
+    ((), (), 2300, 2200, 100),
+    ((), (), 2176, 2304, 40),
+    ((2,), (2,), 1280, 2048, 96),
     ((), (), 96, 682, 256),
     ((), (), 100, 256, 682),
     ((), (), 256, 10, 512),
@@ -302,6 +307,16 @@ def test_matmul_bias_modes(bias_kind, rng):
             "BMN": rng.standard_normal((3, 70, 90))}[bias_kind].astype(np.float32)
     got = F.matmul_add(up(a), up(b), up(bias)).numpy()
     assert rel(got, K.matmul_add(a, b, bias)) < 2e-3
+
+
+def test_matmul_bias_alpha_pair_tiles(rng):
+    """Per-column bias and alpha through the SM-pair kernel's epilogue."""
+    F = _w().functional
+    a = rng.standard_normal((2304, 64)).astype(np.float32)
+    b = rng.standard_normal((64, 2200)).astype(np.float32)
+    bias = rng.standard_normal(2200).astype(np.float32)
+    got = F.matmul_add(up(a), up(b), up(bias), alpha=0.5).numpy()
+    assert rel(got, 0.5 * K.matmul_add(a, b, None) + bias) < 2e-3
 
 
 def test_matmul_fp32_mode_exact_products(rng):

@@ -12,6 +12,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -144,6 +145,62 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   tc_gemm_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
+}
+
+// 256 x BN tiles on SM pairs (both operands TMA-fed, C stored by TMA).
+template <int BN>
+int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+                const CUtensorMap& b1, const CUtensorMap& mc, GemmParams& p) {
+  using C = PairCfg<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM_BYTES));
+    attr_set = true;
+  }
+  p.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+  p.tiles_n = (p.N + BN - 1) / BN;
+  int64_t a_bytes = (int64_t)p.M * p.K * 4;
+  p.group_m = (a_bytes <= (48ll << 20) || p.tiles_m <= 8) ? p.tiles_m : 8;
+  int64_t tiles = (int64_t)p.batch * p.tiles_m * p.tiles_n;
+  WXX_REQUIRE(tiles < (int64_t(1) << 31), "gemm: too many tiles");
+  // Persistent grid: as many SM pairs as can be co-resident (a GPC with an
+  // odd number of free SMs leaves one out).
+  static int max_pairs = -1;
+  if (max_pairs < 0) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)(2 * (wxx::num_sms() / 2)));
+    cfg.blockDim = dim3(PAIR_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = wxx::stream();
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)tc_gemm_pair_kernel<BN>, &cfg) !=
+            cudaSuccess ||
+        n <= 0) {
+      cudaGetLastError();
+      n = wxx::num_sms() / 2;
+    }
+    max_pairs = n < wxx::num_sms() / 2 ? n : wxx::num_sms() / 2;
+  }
+  int pairs = max_pairs;
+  if (tiles < pairs) pairs = (int)tiles;
+  tc_gemm_pair_kernel<BN><<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1,
+                                                                                     mc, p);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+// SM-pair tiles are used for large TMA-fed products (enough 256 x 256 tiles
+// to give every SM pair one); WXX_GEMM_PAIR=0 keeps single-SM tiles.
+bool pair_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("WXX_GEMM_PAIR");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
 }
 
 int pick_bn(int64_t M, int64_t N, int64_t batch) {
@@ -332,21 +389,6 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
   // splits gathered operands on the fly.
   OperandDesc da{A, M, K, batch, lda, a_bs, trans_a == 0, a_bs == 0 && batch > 1};
   OperandDesc db{B, N, K, batch, ldb, b_bs, trans_b != 0, b_bs == 0 && batch > 1};
-  setup_operand(da, BM, true, p.a, &ma0);
-  setup_operand(db, bn, true, p.b, &mb0);
-  ma1 = ma0;
-  mb1 = mb0;
-  void* lo_a = nullptr;
-  void* lo_b = nullptr;
-  if (mode == 1) {
-    int st = make_residual(da, p.a, BM, &ma1, &lo_a);
-    if (st == WXX_OK) st = make_residual(db, p.b, bn, &mb1, &lo_b);
-    if (st != WXX_OK) {
-      wxx_free(lo_a);
-      wxx_free(lo_b);
-      return st;
-    }
-  }
   p.epi.kind = 0;
   p.epi.C = C;
   p.epi.c_bs = M * N;
@@ -355,7 +397,34 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
   p.epi.bias_mode = bias_mode;
   p.epi.bias_bs = M * N;
   p.epi.alpha = alpha;
-  int st = run_tc(bn, ma0, ma1, mb0, mb1, p);
+  // SM-pair tiles when the product is large and every operand is TMA-fed;
+  // each CTA then loads 128-row boxes of both A and B.
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  int64_t pair_tiles = batch * ((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+  bool pair = bn == 256 && pair_enabled() && pair_tiles >= wxx::num_sms() / 2 &&
+              encode_c_map(&mc, p);
+  setup_operand(da, BM, true, p.a, &ma0);
+  setup_operand(db, pair ? BM : bn, true, p.b, &mb0);
+  if (pair && (p.a.kind >= 2 || p.b.kind >= 2)) {
+    pair = false;
+    setup_operand(db, bn, true, p.b, &mb0);
+  }
+  const int b_box = pair ? BM : bn;
+  ma1 = ma0;
+  mb1 = mb0;
+  void* lo_a = nullptr;
+  void* lo_b = nullptr;
+  if (mode == 1) {
+    int st = make_residual(da, p.a, BM, &ma1, &lo_a);
+    if (st == WXX_OK) st = make_residual(db, p.b, b_box, &mb1, &lo_b);
+    if (st != WXX_OK) {
+      wxx_free(lo_a);
+      wxx_free(lo_b);
+      return st;
+    }
+  }
+  int st = pair ? launch_pair<256>(ma0, ma1, mb0, mb1, mc, p) : run_tc(bn, ma0, ma1, mb0, mb1, p);
   // Stream-ordered frees: the residuals stay valid for the GEMM just enqueued.
   int st_a = wxx_free(lo_a);
   int st_b = wxx_free(lo_b);

@@ -571,6 +571,112 @@ __device__ __forceinline__ void epi_store(const GemmParams& p, int bt, int m, in
   }
 }
 
+// ------------------------------------------------------------ SM-pair (cta_group::2) helpers
+//
+// Two CTAs of a cluster (one per SM of a TPC) compute one 256 x BN tile: each
+// holds 128 rows of A and BN/2 rows of B in its own shared memory, the pair's
+// leader (cluster rank 0) issues tcgen05.mma.cta_group::2 reading both, and
+// each CTA's TMEM receives its own 128 accumulator rows.  Every tcgen05
+// instruction of such a kernel uses cta_group::2.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs; the non-.aligned form tolerates a warp whose
+// lanes arrive from different branches.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\t"
+               "barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier that may live in the peer CTA (cluster address `bar_cl`).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t bar_cl, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cl), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma2_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive (once) on the mbarrier at cluster address `bar_cl` when every
+// tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void umma2_commit(uint32_t bar_cl) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cl)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc2(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cl) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cl)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait with cluster-scope acquire (barriers that peers arrive on).
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag, int* err) {
+  uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait_cluster(addr, parity)) return true;
+  unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(addr, parity)) return true;
+    if ((it & 255) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        wxx_device_fail(err, WXX_DEV_ERR_MBAR_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ the kernel
 
 template <int BN>
@@ -804,6 +910,245 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------ SM-pair kernel
+//
+// 256 x BN output tiles on an SM pair (cluster of 2).  Per K-block each CTA
+// loads 128 rows of A and BN/2 rows of B (32 KB at BN = 256), half the B
+// traffic per SM of a 128 x 256 single-SM tile for the same tensor work.
+// Operands must be TMA-fed (kind 0 or 1) and C written by TMA stores.
+// Roles per CTA: warp 0 TMA producer, warp 1 TMEM allocator (+ MMA issuer in
+// the leader), warps 2..5 epilogue of this CTA's 128 rows.
+constexpr int PAIR_THREADS = 192;
+
+template <int BN>
+struct PairCfg {
+  static constexpr int A_BYTES = BM * BK * 4;                 // 16 KB
+  static constexpr int B_BYTES = (BN / 2) * BK * 4;           // 16 KB at BN = 256
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;   // 6
+  static constexpr int TMEM_COLS = 2 * BN;                    // double-buffered accumulator
+  static constexpr int EPI_WARP_BYTES = 8192;
+  static constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+  static_assert(TMEM_COLS <= 512, "TMEM");
+};
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a0,
+                        const __grid_constant__ CUtensorMap tm_a1,
+                        const __grid_constant__ CUtensorMap tm_b0,
+                        const __grid_constant__ CUtensorMap tm_b1,
+                        const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+  using C = PairCfg<BN>;
+  constexpr int PM = 2 * BM;  // rows per pair tile
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];   // leader: both CTAs' loads landed
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];  // each CTA: its stage consumed
+  __shared__ __align__(8) uint64_t tfull_bar[2];          // each CTA: accumulator ready
+  __shared__ __align__(8) uint64_t tempty_bar[2];         // leader: both epilogues drained it
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int total_tiles = p.batch * p.tiles_m * p.tiles_n;
+  const int total_kb = p.num_kb * p.passes;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull_bar[s], 1);
+      mbar_init(&tempty_bar[s], 2 * 4);   // one arrive per epilogue warp of both CTAs
+    }
+    mbar_init(&drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_a0);
+    prefetch_tmap(&tm_b0);
+    if (p.passes > 1) { prefetch_tmap(&tm_a1); prefetch_tmap(&tm_b1); }
+  }
+  if (warp == 1) tmem_alloc2(&tmem_base_sh, C::TMEM_COLS);
+  tc_fence_before();
+  // Both CTAs' barriers are initialised (and TMEM allocated) before any
+  // load, commit or arrive targets the peer.
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t tx_bytes = 2 * C::STAGE_BYTES;   // both CTAs' loads, counted by the leader
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += num_pairs) {
+        int bt, tm, tn;
+        tile_coords(p, t, bt, tm, tn);
+        const int row_a = tm * PM + (int)rank * BM;
+        const int row_b = tn * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait_cl(&empty_bar[stage], phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          const int pass = kb / p.num_kb;
+          const int kc = (kb - pass * p.num_kb) * BK;
+          const CUtensorMap* ma = (p.passes > 1 && pass == 1) ? &tm_a1 : &tm_a0;
+          const CUtensorMap* mb = (p.passes > 1 && pass == 0) ? &tm_b1 : &tm_b0;
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
+          const int za = p.a.bcast_batch ? 0 : bt;
+          if (p.a.kind == 0) {
+            tma_load_3d_pair(smem_u32(sa), ma, fb, kc, row_a, za);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j)
+              tma_load_3d_pair(smem_u32(sa + j * 4096), ma, fb, row_a + j * 32, kc, za);
+          }
+          const int zb = p.b.bcast_batch ? 0 : bt;
+          if (p.b.kind == 0) {
+            tma_load_3d_pair(smem_u32(sb), mb, fb, kc, row_b, zb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d_pair(smem_u32(sb + j * 4096), mb, fb, row_b + j * 32, kc, zb);
+          }
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: the stages this CTA filled last are consumed (their empty
+      // barrier completes only after the leader's MMAs read them), so no load
+      // is still landing when the CTA leaves.
+      volatile int no_abort = 0;
+      for (int i = 0; i < C::STAGES && total_kb > 0; ++i) {
+        if (--stage < 0) { stage = C::STAGES - 1; phase ^= 1; }
+        // A stage never filled in the last lap was drained by an earlier lap.
+        mbar_wait_cl(&empty_bar[stage], phase, &no_abort, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------- MMA issuer (leader only)
+    if (leader && lane == 0) {
+      const bool a_mn = (p.a.kind == 1);
+      const bool b_mn = (p.b.kind == 1);
+      const uint32_t idesc = idesc_tf32_mn(PM, BN, a_mn, b_mn);
+      const uint32_t peer = 1;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_cl(&tempty_bar[acc], acc_phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait_cl(&full_bar[stage], phase, &abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            uint64_t ad = a_mn ? sdesc_mnmajor(sa, kk) : sdesc_kmajor(sa, kk);
+            uint64_t bd = b_mn ? sdesc_mnmajor(sb, kk) : sdesc_kmajor(sb, kk);
+            umma2_tf32(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(&empty_bar[stage]);
+          umma2_commit(eb);
+          umma2_commit(mapa_shared(eb, peer));
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        const uint32_t fb = smem_u32(&tfull_bar[acc]);
+        umma2_commit(fb);
+        umma2_commit(mapa_shared(fb, peer));
+      }
+      // All tensor-core work (which also writes the peer's TMEM) completes
+      // before either CTA frees TMEM.
+      umma2_commit(smem_u32(&drain_bar));
+      volatile int no_abort = 0;
+      mbar_wait_cl(&drain_bar, 0, &no_abort, p.err);
+    }
+  } else {
+    // ---------------------------------------------------- epilogue (both CTAs)
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    uint8_t* wstage = smem + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
+    const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
+    int local = 0;
+    int chunk_seq = 0;
+    for (int t = pair; t < total_tiles; t += num_pairs, ++local) {
+      int bt, tm, tn;
+      tile_coords(p, t, bt, tm, tn);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait_cl(&tfull_bar[acc], acc_phase, &abort_flag, p.err)))
+        break;
+      tc_fence_after();
+      const int m0 = tm * PM + (int)rank * BM + quarter * 32;
+      const uint32_t row_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      const float alpha = p.epi.alpha;
+#pragma unroll 1
+      for (int c = 0; c < BN && m0 < p.M; c += 32) {
+        const int n0 = tn * BN + c;
+        if (n0 >= p.N) break;
+        float v[32];
+        tmem_ld_32x32(row_addr + (uint32_t)c, v);
+        if (p.epi.bias_mode == 1) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = v[j] * alpha + ((n0 + j < p.N) ? __ldg(p.epi.bias + n0 + j) : 0.f);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= alpha;
+        }
+        uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tm_c, smem_u32(buf), n0, m0, bt);
+          bulk_commit();
+        }
+        ++chunk_seq;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+    }
+    if (lane == 0) bulk_wait<0>();
+  }
+
+  tc_fence_before();
+  // Neither CTA frees TMEM or exits while the leader's MMAs or the peer's
+  // arrivals may still touch it.
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, C::TMEM_COLS);
   }
 }
 
