@@ -41,6 +41,7 @@ class Workload:
     name = ""
     metric = ""
     unit = ""
+    flush_l2 = False    # True when a step's weights + activations would stay in L2
 
     def units_per_rank(self, world):
         raise NotImplementedError
@@ -85,6 +86,7 @@ class GPT2Scaled(Workload):
 class GPT2Small(GPT2Scaled):
     name = "gpt2_small"
     V, D, H, L, S, B_PER_GPU = 1024, 256, 8, 6, 256, 4
+    flush_l2 = True
 
     def config(self, world):
         return {"workload": "GPT2(vocab=1024,d=256,heads=8,layers=6) fwd, batch 4, seq 256",
@@ -98,6 +100,7 @@ class ResNet18W(Workload):
     metric = "ResNet18 inference img/s"
     unit = "img/s"
     B_PER_GPU = 256
+    flush_l2 = True
 
     def config(self, world):
         return {"workload": "ResNet18(10) eval, 3x32x32", "global_batch": self.B_PER_GPU * world,
@@ -568,9 +571,23 @@ def run_ours(args, rank, world, local):
     x_dev = upload(x_host)
     comm = wd.NcclCommunicator(rank, world, dist) if world > 1 else None
 
-    def step(inp):
+    def forward(inp):
         with wxx.backend.inferenceMode():
-            out = model(inp)
+            return model(inp)
+
+    graph = None
+    if not args.eager:
+        # One CUDA graph per step: the forward is recorded once (after an
+        # eager warm-up inside capture()) and replayed with one launch; the
+        # step reads its input from x_dev.
+        graph = wxx.graph.capture(forward, x_dev)
+
+    def step(inp):
+        if graph is not None:
+            assert inp is x_dev
+            out = graph.replay()
+        else:
+            out = forward(inp)
         if comm is not None and (hi - lo) * world == rows_global:
             out = comm.allgather(out)
         return out
@@ -585,23 +602,49 @@ def run_ours(args, rank, world, local):
     barrier()
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[0]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].isdigit() else local
+    from wxx_b200.Tensor import Tensor
+
+    flush_buf = Tensor._empty([64 * 2 ** 20], "f32") if wl.flush_l2 else None   # 256 MB > L2
     sampler = ClockSampler(gpu_index)
     sampler.start()
     n0 = dev.launch_count()
-    e0, e1 = dev.Event(), dev.Event()
-    e0.record()
-    h0 = time.perf_counter()
-    for _ in range(args.steps):
-        out = step(x_dev)
-    host_ms = (time.perf_counter() - h0) * 1000.0 / args.steps   # host enqueue time per step
-    e1.record()
-    barrier()
-    launches = (dev.launch_count() - n0) / args.steps
+
+    def timed_steps(fn, n):
+        """(device ms per step, host enqueue ms per step, launches per step).
+        With flush_l2 a 256 MB fill runs before every step, outside its events."""
+        nl0 = dev.launch_count()
+        host = 0.0
+        if flush_buf is None:
+            a, b = dev.Event(), dev.Event()
+            a.record()
+            h = time.perf_counter()
+            for _ in range(n):
+                fn()
+            host = time.perf_counter() - h
+            b.record()
+            barrier()
+            total = a.elapsed_ms(b)
+        else:
+            evs = []
+            for _ in range(n):
+                F.assign(flush_buf, 0.0)
+                a, b = dev.Event(), dev.Event()
+                a.record()
+                h = time.perf_counter()
+                fn()
+                host += time.perf_counter() - h
+                b.record()
+                evs.append((a, b))
+            barrier()
+            total = sum(a.elapsed_ms(b) for a, b in evs)
+        nl = dev.launch_count() - nl0 - (n if flush_buf is not None else 0)
+        return total / n, host * 1000.0 / n, nl / n
+
+    ms, host_ms, launches = timed_steps(lambda: step(x_dev), args.steps)
     log_path = os.environ.get("WXX_LAUNCH_LOG")
     if log_path and rank == 0:
         with open(log_path, "w") as f:
             json.dump({"before_timed": n0, "per_step": launches}, f)
-    ms = e0.elapsed_ms(e1) / args.steps
     clocks = sampler.stop()
     if dist is not None:
         import torch
@@ -621,7 +664,9 @@ def run_ours(args, rank, world, local):
     from wxx_b200.Tensor import Tensor
 
     def e2e_step():
-        t = Tensor._empty(list(x_host.shape), "u32" if is_ids else "f32")
+        # the graph reads its input from x_dev; the eager path gets a new buffer
+        t = x_dev if graph is not None else Tensor._empty(list(x_host.shape),
+                                                          "u32" if is_ids else "f32")
         wxx.backend.lib.F.wxx_memcpy_h2d(t.buffer.ptr, pin_in.ptr, x_host.nbytes)
         logits = step(t)
         local_logits = logits if comm is None else logits.narrow(0, lo, hi - lo)
@@ -632,13 +677,9 @@ def run_ours(args, rank, world, local):
     for _ in range(args.warmup):
         e2e_step()
     barrier()
-    e2 = dev.Event().record()
-    d2h = 0
-    for _ in range(args.steps):
-        d2h = e2e_step()
-    e3 = dev.Event().record()
+    d2h = e2e_step()
     barrier()
-    e2e_ms = e2.elapsed_ms(e3) / args.steps
+    e2e_ms = timed_steps(e2e_step, args.steps)[0]
     if dist is not None:
         import torch
 
@@ -671,7 +712,9 @@ def run_ours(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak" if wl.name.startswith("gpt2") else "strong", "vs_baseline": None,
         "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic",
-        "config": wl.config(world), "roofline": roofline, "clocks": clocks,
+        "config": dict(wl.config(world), launch="eager" if graph is None else
+                       "CUDA graph of the forward, one replay per step"),
+        "roofline": roofline, "clocks": clocks,
         "gpu_launches": int(round(launches * args.steps)),
         "host_enqueue_ms_per_step": host_ms,
         "e2e": {"value": e2e_value, "unit": wl.unit,
@@ -704,6 +747,9 @@ def main(argv=None):
                     default="gpt2_scaled")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="model workloads: launch every kernel from Python each step "
+                         "instead of replaying the step's CUDA graph")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

@@ -45,6 +45,8 @@ int wxx_free(void* ptr);
 int wxx_mem_stats(int64_t* out6);
 /* backend/device.py:135-141 clear_cache */
 int wxx_mem_trim(void);
+/* No reference counterpart: restarts the peak of wxx_mem_stats at the active bytes. */
+int wxx_mem_reset_peak(void);
 int wxx_host_alloc(void** out, uint64_t nbytes);          /* pinned host memory */
 int wxx_host_free(void* ptr);
 /* Tensor.py:66-90 (buffer upload), Tensor.py:552-569 read_buffer */
@@ -64,6 +66,19 @@ int wxx_event_create(void** ev);
 int wxx_event_destroy(void* ev);
 int wxx_event_record(void* ev);
 int wxx_event_elapsed_ms(void* start, void* stop, float* ms);
+/* CUDA graphs.  The closest reference counterpart is backend/device.py:144-255
+ * (GPUCommandBuffer records dispatches and submits them as one batch); here a
+ * whole step is recorded once and replayed.  wxx_graph_begin opens a capture of
+ * the library stream with an arena of arena_bytes that serves every wxx_malloc
+ * until wxx_graph_end (fixed addresses for every replay; arena blocks freed
+ * after the capture stay reserved until wxx_graph_destroy).  Host
+ * synchronisation inside a capture fails it.  wxx_graph_stats: out[0] arena
+ * bytes, out[1] peak bytes used in the capture, out[2] kernels per replay. */
+int wxx_graph_begin(uint64_t arena_bytes, void** handle);
+int wxx_graph_end(void* handle);
+int wxx_graph_launch(void* handle);
+int wxx_graph_stats(void* handle, int64_t* out3);
+int wxx_graph_destroy(void* handle);
 
 /* ---------------------------------------------------------------- elementwise */
 

@@ -9,7 +9,7 @@ convolution, fused FFT convolution, single-pass reductions / softmax / norms).
 """
 
 from .Tensor import Parameter, Tensor
-from . import autograd, backend, functional, nn, serialization
+from . import autograd, backend, functional, graph, nn, serialization
 from .backend.device import get_device
 from .functional import get_matmul_mode, manual_seed, set_matmul_mode
 from .serialization import load, save
@@ -19,6 +19,7 @@ __all__ = [
     "Parameter",
     "autograd",
     "functional",
+    "graph",
     "nn",
     "backend",
     "serialization",

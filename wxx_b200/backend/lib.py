@@ -38,6 +38,7 @@ SIGNATURES = {
     "wxx_free": [c_void_p],
     "wxx_mem_stats": [P_i64],
     "wxx_mem_trim": [],
+    "wxx_mem_reset_peak": [],
     "wxx_host_alloc": [P_void, c_u64],
     "wxx_host_free": [c_void_p],
     "wxx_memcpy_h2d": [c_void_p, c_void_p, c_u64],
@@ -53,6 +54,11 @@ SIGNATURES = {
     "wxx_event_destroy": [c_void_p],
     "wxx_event_record": [c_void_p],
     "wxx_event_elapsed_ms": [c_void_p, c_void_p, P_float],
+    "wxx_graph_begin": [c_u64, P_void],
+    "wxx_graph_end": [c_void_p],
+    "wxx_graph_launch": [c_void_p],
+    "wxx_graph_stats": [c_void_p, P_i64],
+    "wxx_graph_destroy": [c_void_p],
     "wxx_binary": [c_void_p, c_void_p, c_i64, P_i64, c_void_p, c_i64, P_i64, c_int, P_i64, c_int],
     "wxx_scalar": [c_void_p, c_void_p, c_i64, c_int, c_float, c_int],
     "wxx_clamp": [c_void_p, c_void_p, c_i64, c_float, c_float],

@@ -17,8 +17,10 @@
 #include <cstdio>
 #include <atomic>
 #include <mutex>
+#include <map>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 namespace {
 
@@ -40,6 +42,66 @@ struct State {
 };
 
 State g;
+
+// Device memory a captured graph works in.  While a capture is open every
+// wxx_malloc is served from the arena by a host-side best-fit allocator
+// (stream order makes reuse of freed blocks safe), so the recorded kernels
+// see addresses that stay valid for every replay.  Blocks freed after the
+// capture stay reserved until the graph is destroyed.
+struct Arena {
+  char* base = nullptr;
+  size_t size = 0;
+  std::map<size_t, size_t> free_blocks;          // offset -> bytes
+  std::unordered_map<void*, size_t> live;        // pointer -> bytes
+  size_t used = 0, peak = 0;
+  bool capturing = false;
+  cudaGraphExec_t exec = nullptr;
+  int64_t kernels = 0;                           // kernel launches recorded
+  int64_t launches_at_begin = 0;
+};
+std::vector<Arena*> g_arenas;                    // graphs alive (guarded by g.mu)
+Arena* g_capture = nullptr;                      // arena of the open capture
+
+bool arena_alloc(Arena* a, size_t sz, void** out) {
+  auto best = a->free_blocks.end();
+  for (auto it = a->free_blocks.begin(); it != a->free_blocks.end(); ++it)
+    if (it->second >= sz && (best == a->free_blocks.end() || it->second < best->second)) best = it;
+  if (best == a->free_blocks.end()) return false;
+  size_t off = best->first, len = best->second;
+  a->free_blocks.erase(best);
+  if (len > sz) a->free_blocks[off + sz] = len - sz;
+  void* p = a->base + off;
+  a->live[p] = sz;
+  a->used += sz;
+  if (a->used > a->peak) a->peak = a->used;
+  *out = p;
+  return true;
+}
+
+void arena_release(Arena* a, void* p, size_t sz) {
+  size_t off = (size_t)((char*)p - a->base);
+  a->used -= sz;
+  auto next = a->free_blocks.lower_bound(off);
+  if (next != a->free_blocks.end() && next->first == off + sz) {
+    sz += next->second;
+    next = a->free_blocks.erase(next);
+  }
+  if (next != a->free_blocks.begin()) {
+    auto prev = std::prev(next);
+    if (prev->first + prev->second == off) {
+      prev->second += sz;
+      return;
+    }
+  }
+  a->free_blocks[off] = sz;
+}
+
+Arena* arena_of(void* p) {
+  for (Arena* a : g_arenas)
+    if ((char*)p >= a->base && (char*)p < a->base + a->size) return a;
+  return nullptr;
+}
+
 thread_local char g_err[1024] = {0};
 std::atomic<int64_t> g_launches{0};
 
@@ -139,6 +201,19 @@ WXX_EXPORT int wxx_malloc(void** out, uint64_t nbytes) {
   // the pool sees few distinct sizes.
   size_t sz = nbytes < 256 ? 256 : ((nbytes + 255) & ~size_t(255));
   void* p = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    if (g_capture != nullptr) {
+      if (!arena_alloc(g_capture, sz, &p)) {
+        wxx::set_error("wxx_malloc(%llu bytes): graph arena of %llu bytes exhausted "
+                       "(%llu in use)", (unsigned long long)nbytes,
+                       (unsigned long long)g_capture->size, (unsigned long long)g_capture->used);
+        return WXX_E_STATE;
+      }
+      *out = p;
+      return WXX_OK;
+    }
+  }
   cudaError_t e = cudaMallocFromPoolAsync(&p, sz, g.pool, wxx::stream());
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -170,6 +245,20 @@ WXX_EXPORT int wxx_free(void* p) {
   size_t sz = 0;
   {
     std::lock_guard<std::mutex> lk(g.mu);
+    if (Arena* a = arena_of(p)) {
+      auto ia = a->live.find(p);
+      if (ia == a->live.end()) {
+        wxx::set_error("wxx_free: %p freed twice inside a graph arena", p);
+        return WXX_E_ARG;
+      }
+      // Inside the capture the block is reused by later allocations; after
+      // it, replays still write there, so it stays reserved.
+      if (a == g_capture) {
+        arena_release(a, p, ia->second);
+        a->live.erase(ia);
+      }
+      return WXX_OK;
+    }
     auto it = g.live.find(p);
     if (it == g.live.end()) {
       wxx::set_error("wxx_free: %p was not allocated by wxx_malloc (or freed twice)", p);
@@ -197,6 +286,14 @@ WXX_EXPORT int wxx_mem_stats(int64_t* out) {
   out[3] = g.peak_bytes;
   out[4] = g.n_alloc;
   out[5] = g.n_free;
+  return WXX_OK;
+}
+
+// Restarts peak tracking at the current active bytes.
+WXX_EXPORT int wxx_mem_reset_peak(void) {
+  WXX_REQUIRE_INIT();
+  std::lock_guard<std::mutex> lk(g.mu);
+  g.peak_bytes = g.active_bytes;
   return WXX_OK;
 }
 
@@ -317,5 +414,141 @@ WXX_EXPORT int wxx_event_elapsed_ms(void* start, void* stop, float* ms) {
   WXX_REQUIRE_INIT();
   WXX_CUDA_CHECK(cudaEventSynchronize((cudaEvent_t)stop));
   WXX_CUDA_CHECK(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)stop));
+  return WXX_OK;
+}
+
+// ---------------------------------------------------------------- CUDA graphs
+//
+// wxx_graph_begin opens a capture of the library stream with a fresh arena of
+// arena_bytes; every library call until wxx_graph_end is recorded instead of
+// run.  wxx_graph_launch replays the recorded kernels on the library stream
+// with the same pointers (inputs are read from where they were at capture;
+// outputs land in the arena).  Host synchronisation (wxx_sync, blocking
+// copies, device_status) is invalid inside a capture and ends it with an error.
+
+WXX_EXPORT int wxx_graph_begin(uint64_t arena_bytes, void** handle) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(handle != nullptr, "wxx_graph_begin: handle is NULL");
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    WXX_REQUIRE(g_capture == nullptr, "wxx_graph_begin: a capture is already open");
+  }
+  size_t sz = arena_bytes < 256 ? 256 : ((arena_bytes + 255) & ~size_t(255));
+  Arena* a = new Arena();
+  cudaError_t e = cudaMalloc((void**)&a->base, sz);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    delete a;
+    wxx::set_error("wxx_graph_begin: arena of %llu bytes: %s", (unsigned long long)sz,
+                   cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
+  a->size = sz;
+  a->free_blocks[0] = sz;
+  e = cudaStreamBeginCapture(wxx::stream(), cudaStreamCaptureModeRelaxed);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(a->base);
+    delete a;
+    wxx::set_error("wxx_graph_begin: cudaStreamBeginCapture: %s", cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
+  a->capturing = true;
+  a->launches_at_begin = g_launches.load();
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    g_arenas.push_back(a);
+    g_capture = a;
+  }
+  *handle = a;
+  return WXX_OK;
+}
+
+// Closes the capture opened by wxx_graph_begin and instantiates it.  On
+// failure the handle is still valid and must be passed to wxx_graph_destroy.
+WXX_EXPORT int wxx_graph_end(void* handle) {
+  WXX_REQUIRE_INIT();
+  Arena* a = (Arena*)handle;
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    WXX_REQUIRE(a != nullptr && a == g_capture, "wxx_graph_end: not the open capture");
+    g_capture = nullptr;
+  }
+  a->capturing = false;
+  const int64_t recorded = g_launches.load() - a->launches_at_begin;
+  g_launches.fetch_sub(recorded);   // recorded, not run
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(wxx::stream(), &graph);
+  if (e != cudaSuccess || graph == nullptr) {
+    cudaGetLastError();
+    wxx::set_error("wxx_graph_end: capture failed: %s (a call inside the capture "
+                   "synchronised with the host or failed)", cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
+  e = cudaGraphInstantiate(&a->exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    a->exec = nullptr;
+    wxx::set_error("wxx_graph_end: cudaGraphInstantiate: %s", cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
+  a->kernels = recorded;
+  return WXX_OK;
+}
+
+WXX_EXPORT int wxx_graph_launch(void* handle) {
+  WXX_REQUIRE_INIT();
+  Arena* a = (Arena*)handle;
+  WXX_REQUIRE(a != nullptr && a->exec != nullptr, "wxx_graph_launch: no instantiated graph");
+  WXX_CUDA_CHECK(cudaGraphLaunch(a->exec, wxx::stream()));
+  g_launches.fetch_add(a->kernels);
+  return WXX_OK;
+}
+
+// out[0] arena bytes, out[1] peak bytes used during capture, out[2] kernels recorded.
+WXX_EXPORT int wxx_graph_stats(void* handle, int64_t* out) {
+  Arena* a = (Arena*)handle;
+  WXX_REQUIRE(a != nullptr && out != nullptr, "wxx_graph_stats: NULL argument");
+  out[0] = (int64_t)a->size;
+  out[1] = (int64_t)a->peak;
+  out[2] = a->kernels;
+  return WXX_OK;
+}
+
+// Ends an open capture if needed, waits for replays in flight, frees the arena.
+WXX_EXPORT int wxx_graph_destroy(void* handle) {
+  WXX_REQUIRE_INIT();
+  Arena* a = (Arena*)handle;
+  if (a == nullptr) return WXX_OK;
+  bool open;
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    open = (a == g_capture);
+    if (open) g_capture = nullptr;
+  }
+  if (open) {
+    cudaGraph_t graph = nullptr;
+    cudaStreamEndCapture(wxx::stream(), &graph);
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    g_launches.fetch_sub(g_launches.load() - a->launches_at_begin);
+  }
+  cudaError_t e = cudaStreamSynchronize(wxx::stream());
+  if (a->exec) cudaGraphExecDestroy(a->exec);
+  cudaFree(a->base);
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    for (size_t i = 0; i < g_arenas.size(); ++i)
+      if (g_arenas[i] == a) {
+        g_arenas.erase(g_arenas.begin() + i);
+        break;
+      }
+  }
+  delete a;
+  if (e != cudaSuccess) {
+    wxx::set_error("wxx_graph_destroy: %s", cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
   return WXX_OK;
 }
