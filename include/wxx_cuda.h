@@ -159,6 +159,15 @@ int wxx_batchnorm(float* y, float* saved_mean, float* saved_inv, const float* x,
 int wxx_matmul(float* C, const float* A, const float* B, const float* bias, int64_t batch,
                int64_t M, int64_t N, int64_t K, int64_t a_bs, int64_t b_bs, int64_t lda,
                int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha, int mode);
+/* nn/module.py Linear.forward followed by GELU (shaders/activations/gelu.wgsl)
+ * or by the block's residual add (functional/pointwise.py:29 add), fused into
+ * the GEMM epilogue: C = act(alpha * A @ op(B) + bias) + residual.
+ * A (M, K) row stride lda; B (K, N) row stride ldb, or (N, K) with trans_b = 1;
+ * bias (N) or NULL; residual (M, N dense) or NULL; act 0 none, 1 GELU (tanh).
+ * mode 0 TF32, 1 3xTF32.  C 16-byte aligned, N a multiple of 4. */
+int wxx_linear(float* C, const float* A, const float* B, const float* bias,
+               const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
+               int64_t ldb, int trans_b, int act, float alpha, int mode);
 /* functional/convolution.py:658-729 conv2d (conv2d.wgsl), NCHW implicit GEMM on tcgen05.
  * mode 0 TF32, 1 or 2 3xTF32. */
 int wxx_conv2d(float* Y, const float* X, const float* W, const float* bias, int B, int Cin,

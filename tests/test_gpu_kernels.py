@@ -470,3 +470,48 @@ def test_fused_attention(B, S, H, hd, kind, rng):
     assert got.shape == ref.shape
     assert rel(got, ref) < 4e-3, rel(got, ref)
     assert _w().backend.device_status() == 0
+
+
+# ------------------------------------------------------------ fused linear epilogue
+
+@pytest.mark.parametrize("M,K,N", [(100, 64, 96), (8192, 256, 1024), (2304, 64, 2300),
+                                   (3, 8, 4)])
+@pytest.mark.parametrize("act,res", [("gelu", False), (None, True), (None, False)])
+@pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
+def test_linear_fused_matches_unfused_bits(M, K, N, act, res, mode, rng):
+    """GELU / residual fused into the GEMM epilogue: same bits as matmul_add
+    followed by gelu / residual add (nn/module.py Linear + GELU, block adds)."""
+    F = _w().functional
+    x = up(rng.standard_normal((M, K)).astype(np.float32))
+    w = up((rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32))
+    b = up(rng.standard_normal(N).astype(np.float32))
+    r = up(rng.standard_normal((M, N)).astype(np.float32)) if res else None
+    F.set_matmul_mode(mode)
+    try:
+        got = F.linear(x, w, b, activation=act, residual=r).numpy()
+        y = F.matmul_add(x, w, b)
+        if act == "gelu":
+            y = F.gelu(y)
+        if r is not None:
+            y = F.pointwise(r, y, 0)
+        ref = y.numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    assert np.array_equal(got, ref)
+    assert _w().backend.device_status() == 0
+
+
+def test_linear_fp32_mode_and_ragged_n_fall_back(rng):
+    F = _w().functional
+    x = rng.standard_normal((2, 5, 16)).astype(np.float32)
+    w = rng.standard_normal((16, 7)).astype(np.float32)
+    b = rng.standard_normal(7).astype(np.float32)
+    got = F.linear(up(x), up(w), up(b), activation="gelu").numpy()        # N % 4 != 0
+    ref = K.unary(K.matmul_add(x, w, b), "gelu")
+    assert got.shape == (2, 5, 7) and rel(got, ref) < 2e-3
+    F.set_matmul_mode("fp32")
+    try:
+        got32 = F.linear(up(x), up(w), up(b)).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    assert rel(got32, K.matmul_add(x, w, b)) < 1e-5

@@ -85,6 +85,8 @@ SIGNATURES = {
                       c_void_p, c_int, c_int, c_i64, c_float, c_float, c_int],
     "wxx_matmul": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_i64,
                    c_i64, c_i64, c_i64, c_int, c_int, c_int, c_float, c_int],
+    "wxx_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64,
+                   c_i64, c_int, c_int, c_float, c_int],
     "wxx_conv2d": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14,
     "wxx_attention": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                       c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int],

@@ -47,12 +47,6 @@ constexpr int ATT_THREADS = 64 + NT * 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;   // raise the max used for P only past 2^8
 
-// 2^x on the SFU (ex2.approx: relative error ~2^-22, 2^-inf = +0).
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 template <int HD>
 struct ACfg {

@@ -78,6 +78,28 @@ inline unsigned grid_for(int64_t work_items, int threads_per_cta, int ctas_per_s
     if (_wxx_s != WXX_OK) return _wxx_s;     \
   } while (0)
 
+// 2^x on the SFU (ex2.approx: relative error ~2^-22; 2^-inf = +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU, tanh form of shaders/activations/gelu.wgsl:20-27 (x > 10 -> x,
+// x < -10 -> 0), u = 0.7978845608 (x + 0.044715 x^3).  Evaluated through the
+// identity 0.5 x (1 + tanh u) = x / (1 + e^(-2u)): one SFU exp2 and one fast
+// divide (denominator in [1, 2^126]), relative error a few ulp.  Shared by the
+// unary kernel and the GEMM epilogue so fused and unfused paths give the same
+// bits.
+// Branch-free (selects), so the 32 values of an epilogue chunk interleave.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+  const float e = fast_exp2(u * -2.8853900817779268f);   // e^(-2u) = 2^(-2u log2 e)
+  float r = __fdividef(x, 1.0f + e);                      // e = inf -> -0, selected away
+  r = (x > 10.0f) ? x : r;
+  return (x < -10.0f) ? 0.0f : r;
+}
+
 // Records the first device-side error code; later errors are dropped so the
 // host sees the root cause.
 __device__ __forceinline__ void wxx_device_fail(int* err_word, int code) {

@@ -196,12 +196,7 @@ __global__ void clamp_kernel(float* __restrict__ out, const float* __restrict__ 
 __device__ __forceinline__ float apply_unary(int op, float x) {
   switch (op) {
     case 0: return fmaxf(0.0f, x);                                    // relu
-    case 1: {                                                         // gelu (tanh form)
-      if (x > 10.0f) return x;
-      if (x < -10.0f) return 0.0f;
-      float u = 0.7978845608f * (x + 0.044715f * x * x * x);
-      return 0.5f * x * (1.0f + tanhf(u));
-    }
+    case 1: return gelu_tanh(x);                                      // gelu (tanh form)
     case 2: {                                                         // sigmoid
       float xc = fminf(fmaxf(x, -88.0f), 88.0f);
       return 1.0f / (1.0f + expf(-xc));

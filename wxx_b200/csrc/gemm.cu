@@ -141,6 +141,8 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   CUtensorMap mc;
   memset(&mc, 0, sizeof(mc));
   p.epi.tma_store = encode_c_map(&mc, p) ? 1 : 0;
+  WXX_REQUIRE(p.epi.tma_store || (p.epi.act == 0 && p.epi.res == nullptr),
+              "gemm: a fused activation/residual needs a TMA-storable C");
   int grid = (int)(tiles < wxx::num_sms() ? tiles : wxx::num_sms());
   tc_gemm_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
   WXX_LAUNCH_CHECK();
@@ -344,11 +346,15 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(
 //   a_bs / b_bs = 0 broadcasts that operand over the batch.
 //   bias_mode: 0 none, 1 bias[n], 2 bias[m*N + n], 3 bias[b*M*N + m*N + n]
 //   mode: 0 TF32 tensor cores, 1 3xTF32 tensor cores (fp32-faithful), 2 fp32 SIMT.
-WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float* bias,
-                          int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_bs,
-                          int64_t b_bs, int64_t lda, int64_t ldb, int trans_a, int trans_b,
-                          int bias_mode, float alpha, int mode) {
-  WXX_REQUIRE_INIT();
+namespace {
+
+// wxx_matmul with the TMA-store epilogue's optional GELU (act = 1) and
+// residual matrix (res, dense [batch, M, N]); act/res need mode 0/1 and a
+// 16-byte addressable C (checked by wxx_linear).
+int matmul_impl(float* C, const float* A, const float* B, const float* bias, int64_t batch,
+                int64_t M, int64_t N, int64_t K, int64_t a_bs, int64_t b_bs, int64_t lda,
+                int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha, int mode,
+                int act, const float* res) {
   WXX_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "wxx_matmul: negative size");
   WXX_REQUIRE(mode >= 0 && mode <= 2, "wxx_matmul: mode %d not in 0..2", mode);
   WXX_REQUIRE(bias_mode >= 0 && bias_mode <= 3, "wxx_matmul: bias_mode %d not in 0..3", bias_mode);
@@ -397,6 +403,10 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
   p.epi.bias_mode = bias_mode;
   p.epi.bias_bs = M * N;
   p.epi.alpha = alpha;
+  p.epi.act = act;
+  p.epi.res = res;
+  p.epi.res_ld = N;
+  p.epi.res_bs = M * N;
   // SM-pair tiles when the product is large and every operand is TMA-fed;
   // each CTA then loads 128-row boxes of both A and B.
   CUtensorMap mc;
@@ -429,6 +439,36 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
   int st_a = wxx_free(lo_a);
   int st_b = wxx_free(lo_b);
   return st ? st : (st_a ? st_a : st_b);
+}
+
+}  // namespace
+
+WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float* bias,
+                          int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_bs,
+                          int64_t b_bs, int64_t lda, int64_t ldb, int trans_a, int trans_b,
+                          int bias_mode, float alpha, int mode) {
+  WXX_REQUIRE_INIT();
+  return matmul_impl(C, A, B, bias, batch, M, N, K, a_bs, b_bs, lda, ldb, trans_a, trans_b,
+                     bias_mode, alpha, mode, 0, nullptr);
+}
+
+// Linear layer with its follow-up fused into the GEMM epilogue:
+//   C (M, N dense) = act(alpha * A @ op(B) + bias) + residual
+// A (M, K) row stride lda; B (K, N) row stride ldb, or (N, K) with trans_b = 1;
+// bias (N) or NULL; residual (M, N dense) or NULL; act 0 none, 1 GELU (tanh).
+// mode 0 TF32, 1 3xTF32.  C must be 16-byte aligned and N a multiple of 4.
+WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float* bias,
+                          const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
+                          int64_t ldb, int trans_b, int act, float alpha, int mode) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(M >= 0 && N >= 0 && K > 0, "wxx_linear: bad sizes (K must be positive)");
+  WXX_REQUIRE(mode == 0 || mode == 1, "wxx_linear: mode %d not in {0, 1}", mode);
+  WXX_REQUIRE(act == 0 || act == 1, "wxx_linear: act %d not in {0, 1}", act);
+  WXX_REQUIRE(!(reinterpret_cast<uintptr_t>(C) & 15) && N % 4 == 0,
+              "wxx_linear: C must be 16-byte aligned with N a multiple of 4");
+  if (M * N == 0) return WXX_OK;
+  return matmul_impl(C, A, B, bias, 1, M, N, K, 0, 0, lda, ldb, 0, trans_b, bias ? 1 : 0, alpha,
+                     mode, act, residual);
 }
 
 // Y (NCHW [B, Cout, Ho, Wo]) = conv2d(X [B, Cin, H, W], Wt [Cout, Cin, KH, KW]) (+ bias[Cout])

@@ -404,9 +404,18 @@ WXX_EXPORT int wxx_event_destroy(void* ev) {
   return WXX_OK;
 }
 
+// Inside a graph capture the record becomes an external event node, so every
+// replay stamps the event (timing of kernels inside a replayed graph).
 WXX_EXPORT int wxx_event_record(void* ev) {
   WXX_REQUIRE_INIT();
-  WXX_CUDA_CHECK(cudaEventRecord((cudaEvent_t)ev, wxx::stream()));
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  WXX_CUDA_CHECK(cudaStreamIsCapturing(wxx::stream(), &cs));
+  if (cs == cudaStreamCaptureStatusActive) {
+    WXX_CUDA_CHECK(cudaEventRecordWithFlags((cudaEvent_t)ev, wxx::stream(),
+                                            cudaEventRecordExternal));
+  } else {
+    WXX_CUDA_CHECK(cudaEventRecord((cudaEvent_t)ev, wxx::stream()));
+  }
   return WXX_OK;
 }
 

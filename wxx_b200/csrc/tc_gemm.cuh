@@ -344,6 +344,10 @@ struct EpiParams {
   float alpha;
   int hw_out;             // conv: Ho*Wo
   int tma_store;          // kind 0 with bias_mode <= 1: C written by TMA stores
+  // TMA-store path only: C = act(alpha * AB + bias) + res
+  int act;                // 0 none, 1 GELU (tanh form)
+  const float* res;       // residual (M, N) per batch, or NULL
+  int64_t res_ld, res_bs;
 };
 
 struct GemmParams {
@@ -677,6 +681,43 @@ __device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Epilogue math of the TMA-store path for row m, columns n0..n0+31:
+// v = act(alpha * v + bias[n]) + res[m, n].
+__device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, int n0,
+                                          float (&v)[32]) {
+  const EpiParams& e = p.epi;
+  const float alpha = e.alpha;
+  if (e.bias_mode == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      v[j] = v[j] * alpha + ((n0 + j < p.N) ? __ldg(e.bias + n0 + j) : 0.f);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= alpha;
+  }
+  if (e.act == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  }
+  if (e.res != nullptr && m < p.M) {
+    const float* r = e.res + (int64_t)bt * e.res_bs + (int64_t)m * e.res_ld + n0;
+    if (n0 + 32 <= p.N && !(reinterpret_cast<uintptr_t>(r) & 15)) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 w = __ldg(reinterpret_cast<const float4*>(r) + q);
+        v[4 * q] += w.x;
+        v[4 * q + 1] += w.y;
+        v[4 * q + 2] += w.z;
+        v[4 * q + 3] += w.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) v[j] += __ldg(r + j);
+    }
+  }
+}
+
 // ------------------------------------------------------------ the kernel
 
 template <int BN>
@@ -842,17 +883,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int n0 = tn * BN + c;
         if (n0 >= p.N) continue;
         if (use_tma) {
-          // alpha and a per-column bias in registers, row -> swizzled staging
-          // tile, one TMA store per 32 x 32 chunk (clipped at the edges).
-          const float alpha = p.epi.alpha;
-          if (p.epi.bias_mode == 1) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              v[j] = v[j] * alpha + ((n0 + j < p.N) ? __ldg(p.epi.bias + n0 + j) : 0.f);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] *= alpha;
-          }
+          // alpha, bias, activation and residual in registers, row ->
+          // swizzled staging tile, one TMA store per 32 x 32 chunk (clipped
+          // at the edges).
+          epi_apply(p, bt, m0 + lane, n0, v);
           uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
           if (lane == 0) bulk_wait_read<1>();  // the store that used `buf` has read it
           __syncwarp();
@@ -1105,21 +1139,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
       tc_fence_after();
       const int m0 = tm * PM + (int)rank * BM + quarter * 32;
       const uint32_t row_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      const float alpha = p.epi.alpha;
 #pragma unroll 1
       for (int c = 0; c < BN && m0 < p.M; c += 32) {
         const int n0 = tn * BN + c;
         if (n0 >= p.N) break;
         float v[32];
         tmem_ld_32x32(row_addr + (uint32_t)c, v);
-        if (p.epi.bias_mode == 1) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = v[j] * alpha + ((n0 + j < p.N) ? __ldg(p.epi.bias + n0 + j) : 0.f);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= alpha;
-        }
+        epi_apply(p, bt, m0 + lane, n0, v);
         uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
         if (lane == 0) bulk_wait_read<1>();
         __syncwarp();

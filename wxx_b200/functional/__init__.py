@@ -104,6 +104,7 @@ from .utils import (
     equal_number,
     from_numpy,
     from_tensor,
+    linear,
     linspace,
     masked_fill,
     matmul_add,

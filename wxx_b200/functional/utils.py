@@ -199,6 +199,54 @@ def matmul_add(tensor1, tensor2, tensor3, transpose_A=False, transpose_B=False, 
     return out
 
 
+def linear(x, weight, bias=None, *, activation=None, residual=None):
+    """``act(x @ weight + bias) + residual`` with the activation and the
+    residual add fused into the GEMM epilogue.
+
+    ``x`` (..., K), ``weight`` (K, N) (nn.Linear layout), ``bias`` (N,) or
+    None, ``activation`` None or ``"gelu"`` (tanh form), ``residual`` shaped
+    like the output or None.  The result has the same bits as
+    ``matmul_add`` followed by ``gelu`` / ``residual + y``, which is the path
+    taken when the fused form does not apply (fp32 SIMT mode, N not a
+    multiple of 4)."""
+    if activation not in (None, "gelu"):
+        raise ValueError(f"activation must be None or 'gelu', got {activation!r}")
+    a = dense(x)
+    w = dense(weight)
+    K = a.shape[-1]
+    N = w.shape[-1]
+    if len(w.shape) != 2 or w.shape[0] != K:
+        raise ValueError(f"linear: weight {tuple(w.shape)} does not match input {tuple(a.shape)}")
+    out_shape = list(a.shape[:-1]) + [N]
+    if bias is not None and tuple(bias.shape) != (N,):
+        raise ValueError(f"linear: bias {tuple(bias.shape)} is not ({N},)")
+    if residual is not None and list(residual.shape) != out_shape:
+        raise ValueError(f"linear: residual {tuple(residual.shape)} is not {tuple(out_shape)}")
+    mode = matmul_mode_code()
+    M = int(math.prod(a.shape[:-1])) if len(a.shape) > 1 else 1
+    if mode not in (0, 1) or N % 4 or K == 0:
+        y = matmul_add(x, weight, bias)
+        if activation == "gelu":
+            y = y.gelu()
+        return y if residual is None else residual + y
+    requires_grad = (x.requires_grad or weight.requires_grad
+                     or (bias is not None and bias.requires_grad)
+                     or (residual is not None and residual.requires_grad))
+    out = empty(out_shape, "f32", requires_grad)
+    if M == 0:
+        return out
+    b = dense(bias) if bias is not None else None
+    r = dense(residual) if residual is not None else None
+    timer = active_timer()
+    ev0 = timer.start() if timer is not None else None
+    check(F.wxx_linear(out.buffer.ptr, a.ptr, w.ptr, None if b is None else b.ptr,
+                       None if r is None else r.ptr, M, N, K, K, N, 0,
+                       1 if activation == "gelu" else 0, 1.0, mode), "linear")
+    if timer is not None:
+        timer.stop(ev0, 2.0 * M * N * K, f"{M}x{N}x{K}")
+    return out
+
+
 def _equal_impl(tensor1, tensor2, mode, number=0):
     a = dense(tensor1)
     b = dense(tensor2) if tensor2 is not None else None

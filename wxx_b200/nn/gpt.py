@@ -32,6 +32,15 @@ class GPT2Block(Module):
         self.drop = Dropout(dropout)
 
     def forward(self, x, mask=None):
+        if context.MODE != 0 or self.drop.p == 0:
+            # Dropout is the identity: the residual adds and the GELU ride in
+            # the GEMM epilogues (same values as the unfused lines below).
+            h = self.attn.forward(self.ln1(x), mask, residual=x)
+            fc1, act, fc2 = self.mlp._modules.values()
+            if isinstance(fc1, Linear) and isinstance(act, GELU) and isinstance(fc2, Linear):
+                u = functional.linear(self.ln2(h), fc1.weight, fc1.bias, activation="gelu")
+                return functional.linear(u, fc2.weight, fc2.bias, residual=h)
+            return h + self.mlp(self.ln2(h))
         x = x + self.drop(self.attn(self.ln1(x), mask))
         x = x + self.drop(self.mlp(self.ln2(x)))
         return x

@@ -364,7 +364,9 @@ class MultiHeadAttention(Module):
             .reshape((b * self.n_heads, seq, self.head_dim))
         )
 
-    def forward(self, x, mask=None):
+    def forward(self, x, mask=None, residual=None):
+        """``residual`` (shaped like the output) is added by the output
+        projection's epilogue: ``residual + attention(x)`` in one pass."""
         b, seq, _ = x.shape
         fused_ok = context.MODE != 0 or self.drop.p == 0
         if fused_ok and functional.attention_supported(x, self.n_heads, mask):
@@ -372,6 +374,8 @@ class MultiHeadAttention(Module):
             o = functional.attention(self.q(x), self.k(x), self.v(x), self.n_heads,
                                      mask=None if causal else mask, causal=causal,
                                      scale=1.0 / math.sqrt(self.head_dim))
+            if residual is not None:
+                return functional.linear(o, self.out.weight, self.out.bias, residual=residual)
             return self.out(o)
         q = self._heads(self.q(x), b, seq)
         k = self._heads(self.k(x), b, seq)
@@ -386,7 +390,8 @@ class MultiHeadAttention(Module):
             .permute(0, 2, 1, 3)
             .reshape((b, seq, self.d_model))
         )
-        return self.out(out)
+        out = self.out(out)
+        return out if residual is None else residual + out
 
 
 class Attention(Module):
