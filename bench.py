@@ -4,13 +4,15 @@
 
 Default workload ("gpt2_scaled"): GPT2(vocab 50304, d 1024,
 16 heads, 24 layers), seq 1024, 8 sequences per GPU (global batch 8 N, weak
-scaling), fp32 storage with TF32 tensor-core contractions, the logits
-all-gathered over NVLink when N > 1.  Other workloads: gpt2_small (config 0),
-resnet18 (config 2), hyena (config 3).  Inputs and weights are synthetic
-(seeded), resident in HBM for ``value``; ``e2e`` runs the same step through
-the public API from pinned host token ids and reads back the per-position
-argmax ids.  Under torchrun (N > 1) every rank runs its shard; times are the
-max over ranks.
+scaling), fp32 storage with TF32 tensor-core contractions.  A step is the
+forward plus its output (the argmax token id of every position; ResNet18's
+logits), all-gathered over NVLink when N > 1.  The step is recorded once as
+a CUDA graph and replayed (``--eager`` launches kernel by kernel).  Other
+workloads: gpt2_small (config 0), resnet18 (config 2), hyena (config 3).
+Inputs and weights are synthetic (seeded), resident in HBM for ``value``;
+``e2e`` runs the same step through the public API from pinned host inputs and
+reads the gathered outputs back.  Under torchrun (N > 1) every rank runs its
+shard; times are the max over ranks.
 
 ``--impl reference`` times the reference algorithm on the host CPU instead:
 the reference's own code cannot run here (its wgpu backend needs a graphics
@@ -42,6 +44,7 @@ class Workload:
     metric = ""
     unit = ""
     flush_l2 = False    # True when a step's weights + activations would stay in L2
+    output_ids = True   # the step's output is the argmax token id of every position
 
     def units_per_rank(self, world):
         raise NotImplementedError
@@ -55,7 +58,7 @@ class GPT2Scaled(Workload):
 
     def config(self, world):
         return {"workload": "GPT2(vocab=50304,d=1024,heads=16,layers=24) fwd, seq 1024, "
-                            "8 seq/GPU, logits all-gathered",
+                            "8 seq/GPU, argmax token ids all-gathered",
                 "global_batch": self.B_PER_GPU * world, "seq_len": self.S,
                 "parallelism": f"dp{world} (batch-sharded inference)",
                 "matmul_mode": "tf32", "l2": "inputs larger than L2 (1.4 GB weights)"}
@@ -101,6 +104,7 @@ class ResNet18W(Workload):
     unit = "img/s"
     B_PER_GPU = 256
     flush_l2 = True
+    output_ids = False  # the output is the (batch, 10) logits
 
     def config(self, world):
         return {"workload": "ResNet18(10) eval, 3x32x32", "global_batch": self.B_PER_GPU * world,
@@ -572,8 +576,11 @@ def run_ours(args, rank, world, local):
     comm = wd.NcclCommunicator(rank, world, dist) if world > 1 else None
 
     def forward(inp):
+        # model forward + its output: argmax ids for the language models (the
+        # tokens a generation step emits), logits for ResNet
         with wxx.backend.inferenceMode():
-            return model(inp)
+            out = model(inp)
+        return F.max(out, -1)[1] if wl.output_ids else out
 
     graph = None
     if not args.eager:
@@ -655,11 +662,12 @@ def run_ours(args, rank, world, local):
     units_total = rows_global * wl.units_per_row()
     value = units_total / (ms / 1000.0)
 
-    # e2e: pinned host ids -> device -> step -> argmax over the last axis -> host ids
+    # e2e: pinned host inputs -> device -> step (forward, output ids/logits,
+    # all-gather) -> host
     pin_in = dev.PinnedHostBuffer(x_host.nbytes)
     pin_in.as_numpy(x_host.dtype, x_host.shape)[...] = x_host
-    res_rows = (hi - lo) * (wl.units_per_row() if wl.name != "resnet18" else 1)
-    pin_out = dev.PinnedHostBuffer(max(4, res_rows * 4))
+    out_elems = rows_global * (wl.units_per_row() if wl.output_ids else 10)
+    pin_out = dev.PinnedHostBuffer(max(4, out_elems * 4))
 
     from wxx_b200.Tensor import Tensor
 
@@ -668,11 +676,9 @@ def run_ours(args, rank, world, local):
         t = x_dev if graph is not None else Tensor._empty(list(x_host.shape),
                                                           "u32" if is_ids else "f32")
         wxx.backend.lib.F.wxx_memcpy_h2d(t.buffer.ptr, pin_in.ptr, x_host.nbytes)
-        logits = step(t)
-        local_logits = logits if comm is None else logits.narrow(0, lo, hi - lo)
-        ids = F.max(local_logits, -1)[1]
-        wxx.backend.lib.F.wxx_memcpy_d2h_async(pin_out.ptr, ids.ptr, ids.nbytes)
-        return ids.nbytes
+        out = step(t)
+        wxx.backend.lib.F.wxx_memcpy_d2h_async(pin_out.ptr, out.ptr, out.nbytes)
+        return out.nbytes
 
     for _ in range(args.warmup):
         e2e_step()
@@ -734,7 +740,8 @@ def run_ours(args, rank, world, local):
         "host_enqueue_ms_per_step": host_ms,
         "e2e": {"value": e2e_value, "unit": wl.unit,
                 "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(d2h),
-                "includes": "pinned H2D of inputs, forward, all-gather, argmax, D2H of ids"},
+                "includes": "pinned H2D of inputs, forward, output (argmax ids or logits), "
+                            "all-gather, D2H of the gathered outputs"},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, units, reps, dt = time_cpu_sample(wl, seconds=args.cpu_seconds)

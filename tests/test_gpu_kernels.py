@@ -515,3 +515,21 @@ def test_linear_fp32_mode_and_ragged_n_fall_back(rng):
     finally:
         F.set_matmul_mode("tf32")
     assert rel(got32, K.matmul_add(x, w, b)) < 1e-5
+
+
+@pytest.mark.parametrize("d,hidden", [(64, 170), (256, 682)])
+def test_swiglu_padded_hidden_matches_plain(d, hidden, rng):
+    """SwiGLU with a hidden width that is not a multiple of 4 runs on
+    zero-padded weights (TMA-fed GEMMs); same values as the plain expression."""
+    wxx = _w()
+    F = wxx.functional
+    wxx.manual_seed(3)
+    m = wxx.nn.SwiGLU(d, hidden_dim=hidden)
+    x = up(rng.standard_normal((2, 300, d)).astype(np.float32))
+    got = m(x).numpy()
+    ref = m.w3(F.silu(m.w1(x)) * m.w2(x)).numpy()
+    assert got.shape == ref.shape
+    assert rel(got, ref) < 1e-6, rel(got, ref)
+    # the padded copies follow parameter updates
+    F.assign(m.w1.weight, F.from_numpy(np.zeros((d, hidden), np.float32)))
+    assert np.abs(m(x).numpy()).max() == 0.0

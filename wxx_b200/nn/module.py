@@ -433,7 +433,32 @@ class SwiGLU(Module):
         self.w3 = Linear(hidden_dim, d_model, bias=False)
 
     def forward(self, x):
+        h = self.hidden_dim
+        if h % 4 and functional.get_matmul_mode() != "fp32" and len(x.shape) >= 2:
+            return self._forward_padded(x)
         return self.w3(functional.silu(self.w1(x)) * self.w2(x))
+
+    def _forward_padded(self, x):
+        """Same product with the hidden width rounded up to a multiple of 4, so
+        every operand row is 16-byte aligned and the GEMMs are TMA-fed.  The
+        weights are copied each call into zero-padded buffers owned by the
+        module: the extra columns give silu(0) * 0 = 0 and meet zero rows of
+        W3, which is what the GEMM's K tail reads anyway."""
+        h = self.hidden_dim
+        hp = (h + 3) // 4 * 4
+        d_in = self.w1.weight.shape[0]
+        d_out = self.w3.weight.shape[1]
+        cache = self.__dict__.get("_pad_cache")
+        if cache is None or cache[0] != hp:
+            cache = (hp, Tensor((d_in, hp), value=0.0), Tensor((d_in, hp), value=0.0),
+                     Tensor((hp, d_out), value=0.0))
+            object.__setattr__(self, "_pad_cache", cache)
+        _, w1p, w2p, w3p = cache
+        functional.assign(w1p.narrow(1, 0, h), self.w1.weight)
+        functional.assign(w2p.narrow(1, 0, h), self.w2.weight)
+        functional.assign(w3p.narrow(0, 0, h), self.w3.weight)
+        g = functional.silu(functional.linear(x, w1p)) * functional.linear(x, w2p)
+        return functional.linear(g, w3p)
 
 
 class TiedLinear(Module):
