@@ -720,7 +720,7 @@ def run_ours(args, rank, world, local):
     tf32_peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2.0
     achieved = ks["flops"] / (ks["ms"] / 1000.0) / 1e12 if ks["ms"] > 0 else 0.0
     roofline = {
-        "kernel": "tc_gemm_kernel (tcgen05 kind::tf32, TMA-fed, TMEM accumulators)",
+        "kernel": "tcgen05 kind::tf32 GEMM / implicit-GEMM conv (TMA-fed, TMEM accumulators)",
         "bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
         "frac": achieved / tf32_peak, "traffic": None,
         "peak_basis": f"{peak_kind} bf16 dense TFLOP/s / 2 (B200 TF32 rate is half of BF16)",

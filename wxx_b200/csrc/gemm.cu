@@ -107,10 +107,12 @@ bool encode_c_map(CUtensorMap* map, const GemmParams& p) {
   auto enc = get_encode();
   if (!enc || p.epi.kind != 0 || p.epi.bias_mode > 1) return false;
   if ((reinterpret_cast<uintptr_t>(p.epi.C) & 15) || ((int64_t)p.epi.ldc * 4) % 16) return false;
-  if (p.batch > 1 && (p.epi.c_bs * 4) % 16) return false;
-  cuuint64_t dims[3] = {(cuuint64_t)p.N, (cuuint64_t)p.M, (cuuint64_t)p.batch};
+  // split-K partials: z runs over the K-slices of the workspace
+  const int zdim = p.epi.raw ? p.splits : p.batch;
+  if (zdim > 1 && (p.epi.c_bs * 4) % 16) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)p.N, (cuuint64_t)p.M, (cuuint64_t)zdim};
   cuuint64_t strides[2] = {(cuuint64_t)p.epi.ldc * 4,
-                           (cuuint64_t)(p.batch > 1 ? p.epi.c_bs : (int64_t)p.epi.ldc * p.M) * 4};
+                           (cuuint64_t)(zdim > 1 ? p.epi.c_bs : (int64_t)p.epi.ldc * p.M) * 4};
   cuuint32_t box[3] = {32, 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.epi.C, dims, strides, box, estr,
@@ -136,11 +138,12 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   // A stays L2-resident while B is swept.
   int64_t a_bytes = (int64_t)p.M * p.K * 4;
   p.group_m = (a_bytes <= (48ll << 20) || p.tiles_m <= 16) ? p.tiles_m : 16;
-  int64_t tiles = (int64_t)p.batch * p.tiles_m * p.tiles_n;
+  int64_t tiles = (int64_t)p.batch * p.tiles_m * p.tiles_n * p.splits;   // work units
   WXX_REQUIRE(tiles < (int64_t(1) << 31), "gemm: too many tiles");
   CUtensorMap mc;
   memset(&mc, 0, sizeof(mc));
   p.epi.tma_store = encode_c_map(&mc, p) ? 1 : 0;
+  WXX_REQUIRE(p.epi.tma_store || !p.epi.raw, "gemm: split-K workspace is not TMA-storable");
   WXX_REQUIRE(p.epi.tma_store || (p.epi.act == 0 && p.epi.res == nullptr),
               "gemm: a fused activation/residual needs a TMA-storable C");
   int grid = (int)(tiles < wxx::num_sms() ? tiles : wxx::num_sms());
@@ -213,6 +216,101 @@ int pick_bn(int64_t M, int64_t N, int64_t batch) {
   int64_t t256 = batch * ((M + 127) / 128) * ((N + 255) / 256);
   if (t256 >= wxx::num_sms() / 2) return 256;
   return 128;
+}
+
+// ------------------------------------------------------------ split-K
+
+// K-slices for a product with few output tiles: enough units to cover the
+// SMs once, at least 4 K-blocks per slice, at most 32 slices.
+int choose_splits(int64_t tiles, int total_kb) {
+  const int sms = wxx::num_sms();
+  if (tiles >= sms / 2 || total_kb < 8) return 1;
+  int64_t sp = sms / tiles;
+  if (sp > total_kb / 4) sp = total_kb / 4;
+  if (sp > 32) sp = 32;
+  return sp < 2 ? 1 : (int)sp;
+}
+
+// out = alpha * (ws[0] + ws[1] + ... ) + bias, the K-slices added in index
+// order (deterministic).  kind 0: row-major C[m*ldc + n]; kind 1: NCHW
+// C[(b*N + n)*hw + pix] with m = b*hw + pix (m fastest: coalesced writes).
+__global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restrict__ ws,
+                                     int splits, int M, int N, float alpha,
+                                     const float* __restrict__ bias, int kind, int64_t ldc,
+                                     int hw) {
+  const int64_t MN = (int64_t)M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < MN;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t m, n;
+    if (kind == 0) {
+      m = i / N;
+      n = i - m * N;
+    } else {
+      n = i / M;
+      m = i - n * M;
+    }
+    const int64_t src = m * N + n;
+    float acc = ws[src];
+    for (int k = 1; k < splits; ++k) acc += ws[(int64_t)k * MN + src];
+    float v = acc * alpha;
+    if (bias != nullptr) v += bias[n];
+    if (kind == 0) {
+      C[m * ldc + n] = v;
+    } else {
+      const int64_t b = m / hw, pix = m - b * hw;
+      C[(b * N + n) * hw + pix] = v;
+    }
+  }
+}
+
+int run_tc(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+           const CUtensorMap& b1, GemmParams& p);
+
+// Sets p.splits / p.kb_per_split for BN-wide tiles; true when split-K applies.
+bool plan_splits(GemmParams& p, int bn) {
+  const int total_kb = p.num_kb * p.passes;
+  const int64_t tiles = (int64_t)p.batch * ((p.M + BM - 1) / BM) * ((p.N + bn - 1) / bn);
+  int sp = (p.batch == 1 && p.N % 4 == 0) ? choose_splits(tiles, total_kb) : 1;
+  if (sp <= 1) return false;
+  p.kb_per_split = (total_kb + sp - 1) / sp;
+  p.splits = (total_kb + p.kb_per_split - 1) / p.kb_per_split;   // no empty slice
+  return p.splits > 1;
+}
+
+// Runs the GEMM of `p` (batch 1, epilogue kind 0 or 1 with at most a column
+// bias) as p.splits K-slices into a workspace, then reduces into the real
+// output.  p.epi holds the real output description on entry.
+int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+               const CUtensorMap& b1, GemmParams& p) {
+  const EpiParams real = p.epi;
+  const int64_t MN = (int64_t)p.M * p.N;
+  void* ws = nullptr;
+  int st = wxx_malloc(&ws, (uint64_t)p.splits * MN * sizeof(float));
+  if (st) return st;
+  p.epi.kind = 0;
+  p.epi.C = (float*)ws;
+  p.epi.ldc = p.N;
+  p.epi.c_bs = MN;
+  p.epi.bias = nullptr;
+  p.epi.bias_mode = 0;
+  p.epi.alpha = 1.0f;
+  p.epi.raw = 1;
+  st = run_tc(bn, a0, a1, b0, b1, p);
+  if (st == WXX_OK) {
+    splitk_reduce_kernel<<<wxx::grid_for(MN, 256), 256, 0, wxx::stream()>>>(
+        real.C, (const float*)ws, p.splits, p.M, p.N, real.alpha,
+        real.bias_mode == 1 ? real.bias : nullptr, real.kind,
+        real.kind == 0 ? (int64_t)real.ldc : 0, real.hw_out);
+    cudaError_t e = cudaGetLastError();
+    wxx::count_launch();
+    if (e != cudaSuccess) {
+      wxx::set_error("split-K reduce launch failed: %s", cudaGetErrorString(e));
+      st = WXX_E_CUDA;
+    }
+  }
+  int st2 = wxx_free(ws);   // stream-ordered: valid for the kernels just enqueued
+  p.epi = real;
+  return st ? st : st2;
 }
 
 int run_tc(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
@@ -385,6 +483,8 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   p.batch = (int)batch;
   p.num_kb = (int)((K + BK - 1) / BK);
   p.passes = mode == 1 ? 3 : 1;
+  p.splits = 1;
+  p.kb_per_split = p.num_kb * p.passes;
   p.err = wxx::device_error_word();
   int bn = pick_bn(M, N, batch);
   CUtensorMap ma0, ma1, mb0, mb1;
@@ -434,7 +534,14 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
       return st;
     }
   }
-  int st = pair ? launch_pair<256>(ma0, ma1, mb0, mb1, mc, p) : run_tc(bn, ma0, ma1, mb0, mb1, p);
+  int st;
+  if (pair) {
+    st = launch_pair<256>(ma0, ma1, mb0, mb1, mc, p);
+  } else if (act == 0 && res == nullptr && bias_mode <= 1 && plan_splits(p, bn)) {
+    st = run_splitk(bn, ma0, ma1, mb0, mb1, p);
+  } else {
+    st = run_tc(bn, ma0, ma1, mb0, mb1, p);
+  }
   // Stream-ordered frees: the residuals stay valid for the GEMM just enqueued.
   int st_a = wxx_free(lo_a);
   int st_b = wxx_free(lo_b);
@@ -497,6 +604,8 @@ WXX_EXPORT int wxx_conv2d(float* Y, const float* X, const float* Wt, const float
   p.batch = 1;
   p.num_kb = (int)((K + BK - 1) / BK);
   p.passes = mode == 0 ? 1 : 3;
+  p.splits = 1;
+  p.kb_per_split = p.num_kb * p.passes;
   p.err = wxx::device_error_word();
   int bn = pick_bn(Mrows, Cout, 1);
   CUtensorMap ma, mb;
@@ -519,5 +628,6 @@ WXX_EXPORT int wxx_conv2d(float* Y, const float* X, const float* Wt, const float
   p.epi.bias_mode = bias ? 1 : 0;
   p.epi.alpha = 1.0f;
   p.epi.hw_out = Ho * Wo;
+  if (plan_splits(p, bn)) return run_splitk(bn, ma, ma, mb, mb, p);
   return run_tc(bn, ma, ma, mb, mb, p);
 }

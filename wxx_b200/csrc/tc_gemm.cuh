@@ -348,6 +348,7 @@ struct EpiParams {
   int act;                // 0 none, 1 GELU (tanh form)
   const float* res;       // residual (M, N) per batch, or NULL
   int64_t res_ld, res_bs;
+  int raw;                // split-K: raw partial sums to the workspace map, slice index as z
 };
 
 struct GemmParams {
@@ -357,6 +358,8 @@ struct GemmParams {
   int group_m;            // row blocks per raster band (tiles_m: plain row-fastest order)
   int num_kb;             // K-blocks per pass
   int passes;             // 1 = TF32; 3 = 3xTF32 (hi*lo, lo*hi, hi*hi)
+  int splits;             // K-slices per tile (split-K; 1 = whole K)
+  int kb_per_split;       // K-blocks (over all passes) per slice
   OperandSrc a, b;
   EpiParams epi;
   int* err;
@@ -376,6 +379,17 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& bt,
   int gm = rows_left < p.group_m ? rows_left : p.group_m;
   tm = band * p.group_m + in_band % gm;
   tn = in_band / gm;
+}
+
+// Work unit u -> output tile t and its K-block range [kb0, kb1) (split-K
+// slices of one tile are consecutive units).
+__device__ __forceinline__ void unit_range(const GemmParams& p, int u, int& t, int& sp, int& kb0,
+                                           int& kb1) {
+  t = u / p.splits;
+  sp = u - t * p.splits;
+  const int total = p.num_kb * p.passes;
+  kb0 = sp * p.kb_per_split;
+  kb1 = kb0 + p.kb_per_split < total ? kb0 + p.kb_per_split : total;
 }
 
 // 3xTF32 operand parts: the tensor core reads the top 19 bits of each fp32
@@ -439,34 +453,40 @@ __device__ __forceinline__ void gather_tile(const OperandSrc& s, uint8_t* dst, i
       }
     }
   } else {
-    // im2col: row = output pixel (b, oh, ow); k = (c, r, q) over the filter.
+    // im2col: row = output pixel (b, oh, ow); k = (c, fr, fq) over the filter.
+    // The filter coordinate advances incrementally along k (no divisions in
+    // the loop) and all 32 loads of a row are issued before any is stored.
     const int khw = s.kh * s.kw;
     for (int r = gtid; r < rows; r += GATHER_THREADS) {
-      int m = row0 + r;
-      bool mvalid = m < s.rows_total;
+      const int m = row0 + r;
+      const bool mvalid = m < s.rows_total;
       int ow = 0, oh = 0, b = 0;
       if (mvalid) {
         ow = m % s.wo;
-        int t = m / s.wo;
+        const int t = m / s.wo;
         oh = t % s.ho;
         b = t / s.ho;
       }
       const int ih0 = oh * s.sh - s.ph, iw0 = ow * s.sw - s.pw;
       const float* xb = s.base + (int64_t)b * s.cin * s.h * s.w;
-#pragma unroll 4
+      int c = k0 / khw;
+      int rem = k0 - c * khw;
+      int fr = rem / s.kw, fq = rem - fr * s.kw;
+      float v[BK];
+#pragma unroll
       for (int k = 0; k < BK; ++k) {
-        int kg = k0 + k;
-        float v = 0.f;
-        if (mvalid && kg < s.k_total) {
-          int c = kg / khw;
-          int rem = kg - c * khw;
-          int fr = rem / s.kw, fq = rem - fr * s.kw;
-          int ih = ih0 + fr * s.dh, iw = iw0 + fq * s.dw;
-          if (ih >= 0 && ih < s.h && iw >= 0 && iw < s.w)
-            v = __ldg(xb + ((int64_t)c * s.h + ih) * s.w + iw);
+        const int ih = ih0 + fr * s.dh, iw = iw0 + fq * s.dw;
+        const bool ok = mvalid && (k0 + k) < s.k_total && ih >= 0 && ih < s.h && iw >= 0 &&
+                        iw < s.w;
+        v[k] = ok ? __ldg(xb + ((int64_t)c * s.h + ih) * s.w + iw) : 0.f;
+        if (++fq == s.kw) {
+          fq = 0;
+          if (++fr == s.kh) { fr = 0; ++c; }
         }
-        *reinterpret_cast<float*>(dst + kmajor_offset(r, k)) = split_part(v, part);
       }
+#pragma unroll
+      for (int k = 0; k < BK; ++k)
+        *reinterpret_cast<float*>(dst + kmajor_offset(r, k)) = split_part(v[k], part);
     }
   }
 }
@@ -744,8 +764,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const bool a_gather = p.a.kind >= 2;
   const bool b_gather = p.b.kind >= 2;
   const bool any_gather = a_gather || b_gather;
-  const int total_tiles = p.batch * p.tiles_m * p.tiles_n;
-  const int total_kb = p.num_kb * p.passes;
+  // Work units: output tiles, each cut into p.splits K-slices (split-K).
+  const int total_units = p.batch * p.tiles_m * p.tiles_n * p.splits;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -778,10 +798,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        int bt, tm, tn;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        int t, sp, kb0, kb1, bt, tm, tn;
+        unit_range(p, u, t, sp, kb0, kb1);
         tile_coords(p, t, bt, tm, tn);
-        for (int kb = 0; kb < total_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
@@ -832,13 +853,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++local) {
+        int t, sp, kb0, kb1;
+        unit_range(p, u, t, sp, kb0, kb1);
         int acc = local & 1;
         uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < total_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, &abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
           uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
@@ -847,7 +870,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             uint64_t ad = a_mn ? sdesc_mnmajor(sa, kk) : sdesc_kmajor(sa, kk);
             uint64_t bd = b_mn ? sdesc_mnmajor(sb, kk) : sdesc_kmajor(sb, kk);
-            umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+            umma_tf32(d_tmem, ad, bd, idesc, ((kb - kb0) | kk) ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
@@ -867,8 +890,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool use_tma = p.epi.kind == 0 && p.epi.tma_store;
     int local = 0;
     int chunk_seq = 0;  // TMA-store staging buffer parity
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
-      int bt, tm, tn;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++local) {
+      int t, sp, kb0, kb1, bt, tm, tn;
+      unit_range(p, u, t, sp, kb0, kb1);
       tile_coords(p, t, bt, tm, tn);
       int acc = local & 1;
       uint32_t acc_phase = (local >> 1) & 1;
@@ -886,7 +910,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // alpha, bias, activation and residual in registers, row ->
           // swizzled staging tile, one TMA store per 32 x 32 chunk (clipped
           // at the edges).
-          epi_apply(p, bt, m0 + lane, n0, v);
+          // (split-K: raw partial sums, slice index as the z coordinate)
+          if (!p.epi.raw) epi_apply(p, bt, m0 + lane, n0, v);
           uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
           if (lane == 0) bulk_wait_read<1>();  // the store that used `buf` has read it
           __syncwarp();
@@ -898,7 +923,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tm_c, smem_u32(buf), n0, m0, bt);
+            tma_store_3d(&tm_c, smem_u32(buf), n0, m0, p.epi.raw ? sp : bt);
             bulk_commit();
           }
           ++chunk_seq;
@@ -918,10 +943,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      int bt, tm, tn;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      int t, sp, kb0, kb1, bt, tm, tn;
+      unit_range(p, u, t, sp, kb0, kb1);
       tile_coords(p, t, bt, tm, tn);
-      for (int kb = 0; kb < total_kb; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
         uint8_t* sa = smem + stage * C::STAGE_BYTES;
         uint8_t* sb = sa + C::A_BYTES;

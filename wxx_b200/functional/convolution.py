@@ -1,7 +1,7 @@
 """Convolutions and pooling (reference: src/wxx/functional/convolution.py)."""
 
 from .. import validation
-from ._common import F, check, dense, empty, matmul_mode_code
+from ._common import F, active_timer, check, dense, empty, matmul_mode_code
 from .pointwise import _training_only
 
 
@@ -79,8 +79,12 @@ def conv2d(tensor1, W, stride, padding, dilation, bias=None):
     b = dense(bias) if bias is not None else None
     out = empty((B, Cout, Ho, Wo), "f32", tensor1.requires_grad)
     mode = matmul_mode_code()
+    timer = active_timer()
+    ev0 = timer.start() if timer is not None else None
     check(F.wxx_conv2d(out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr, B, Cin, H, Wd,
                        Cout, KH, KW, sh, sw, ph, pw, dh, dw, 0 if mode == 0 else 1), "conv2d")
+    if timer is not None:
+        timer.stop(ev0, 2.0 * B * Ho * Wo * Cout * Cin * KH * KW, f"conv{B}x{Cin}x{H}x{Wd}->{Cout}")
     return out
 
 
