@@ -717,13 +717,19 @@ def run_ours(args, rank, world, local):
         dev.synchronize()
         ks = kt.summary()
     peaks, peak_kind = load_peaks()
-    tf32_peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2.0
+    # The GEMMs run inside a step of many milliseconds at the power cap: the
+    # sustained figure is the denominator (the burst one for kernels timed
+    # alone, the sweeps).
+    sustained = "bf16_tflops_sustained" in peaks
+    tf32_peak = peaks.get("bf16_tflops_sustained",
+                          peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])) / 2.0
     achieved = ks["flops"] / (ks["ms"] / 1000.0) / 1e12 if ks["ms"] > 0 else 0.0
     roofline = {
         "kernel": "tcgen05 kind::tf32 GEMM / implicit-GEMM conv (TMA-fed, TMEM accumulators)",
         "bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
         "frac": achieved / tf32_peak, "traffic": None,
-        "peak_basis": f"{peak_kind} bf16 dense TFLOP/s / 2 (B200 TF32 rate is half of BF16)",
+        "peak_basis": f"{peak_kind} {'sustained ' if sustained else ''}bf16 dense TFLOP/s / 2 "
+                      "(B200 TF32 rate is half of BF16; kernel timed inside a long step)",
         "gemm_share_of_step": ks["ms"] / ms if ms > 0 else None,
         "gemm_launches_per_step": ks["launches"],
     }

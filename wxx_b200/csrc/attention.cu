@@ -13,10 +13,11 @@
 // in blocks of 64 shared by both tiles:
 //   warp 0      TMA producer (Q once; K_j and V_j double-buffered, separate
 //               barriers so K_{j+2} loads as soon as S_j has read K_j)
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, per block j:
-//               S_t(j) = Q_t K_j^T for both tiles (M=128, N=64, K=hd), then
-//               O_t += P_t(j-1) V_{j-1} (M=128, N=hd, K=64; V MN-major,
-//               32B-atom swizzle), O_t accumulated in TMEM across all blocks
+//   warps 1, 10 one tcgen05.mma-issuing thread per tile (warp 1 also owns
+//               the TMEM allocation), per block j: S_t(j) = Q_t K_j^T
+//               (M=128, N=64, K=hd), then O_t += P_t(j-1) V_{j-1} (M=128,
+//               N=hd, K=64; V MN-major, 32B-atom swizzle), O_t accumulated in
+//               TMEM across all blocks
 //   warps 2..5  tile A, warps 6..9 tile B: one query row per thread,
 //               tcgen05.ld S, online softmax in the log2 domain, P to shared
 //               memory (K-major swizzled), final O / l through a TMA store
@@ -43,9 +44,32 @@ namespace {
 constexpr int BQ = 128;   // query rows per tile (UMMA M)
 constexpr int NT = 2;     // query tiles per CTA
 constexpr int BKV = 64;   // keys per block (UMMA N of S, K of PV)
-constexpr int ATT_THREADS = 64 + NT * 128;
+constexpr int ATT_THREADS = 64 + NT * 128 + 32;   // + one MMA-issuing warp per extra tile
+constexpr int MMA_WARP1 = 2 + NT * 4;               // issues tile 1's MMAs (warp 1: tile 0's)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;   // raise the max used for P only past 2^8
+
+// 2^x on the FMA pipe, for x <= 8 (arguments here are t - m with t <= m + 8).
+// x = n + f with n = round(x) (adding 1.5 * 2^23 rounds x into the low
+// mantissa bits) and f in [-0.5, 0.5]; 2^f by a degree-4 polynomial fitted
+// here to 2^f on [-0.5, 0.5] (relative-error least squares on Chebyshev
+// nodes, max relative error 2.7e-6 in fp32 Horner form); 2^n is added to the
+// exponent field (p >= 0.7, so with n >= -126 the field stays >= 0).
+// x < -126 (masked keys: -inf) gives exactly 0.  The SFU's ex2 issues at
+// about one warp instruction per 16 cycles per SM sub-partition and is the
+// softmax's bottleneck, so 3 of every 8 exponentials use this form.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float r = xc + 12582912.0f;           // 0x4B400000 + round(xc) in the bits
+  const float f = xc - (r - 12582912.0f);
+  float p = fmaf(9.570609884e-03f, f, 5.591790373e-02f);
+  p = fmaf(p, f, 2.402473231e-01f);
+  p = fmaf(p, f, 6.931218067e-01f);
+  p = fmaf(p, f, 9.999992652e-01f);
+  const int n = __float_as_int(r) - 0x4B400000;
+  const float y = __int_as_float(__float_as_int(p) + (n << 23));
+  return x < -126.0f ? 0.0f : y;
+}
 
 
 template <int HD>
@@ -86,7 +110,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __shared__ __align__(8) uint64_t q_full;
   __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   __shared__ __align__(8) uint64_t s_full[NT][2], p_full[NT], p_empty[NT];
-  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ __align__(8) uint64_t drain_bar[NT];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
@@ -116,9 +140,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     mbar_init(&q_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+      mbar_init(&k_empty[s], NT);   // one commit from each tile's MMA thread
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+      mbar_init(&v_empty[s], NT);
     }
     for (int t = 0; t < NT; ++t) {
       mbar_init(&s_full[t][0], 1);
@@ -126,7 +150,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&p_full[t], 128);
       mbar_init(&p_empty[t], 1);
     }
-    mbar_init(&drain_bar, 1);
+    for (int t = 0; t < NT; ++t) mbar_init(&drain_bar[t], 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
@@ -173,25 +197,29 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (last_v[s] >= 0) mbar_wait(&v_full[s], (last_v[s] >> 1) & 1, &no_abort, p.err);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == MMA_WARP1) {
+    // ------------------------------------------------ MMA issuers, one thread per tile
+    // Each tile's chain (S_t(j+1) issued, then wait P_t(j), then O_t += P_t(j) V_j)
+    // runs on its own thread, so one tile's softmax never holds up the other
+    // tile's next S.  K and V stages are released when both threads committed.
     if (lane == 0) {
+      const int t = (warp == 1) ? 0 : 1;
+      const int nt = t ? n_t1 : n_t0;
       const uint32_t idesc_s = idesc_tf32_mn(BQ, BKV, false, false);
       const uint32_t idesc_o = idesc_tf32_mn(BQ, HD, false, true);
       const uint32_t sbase = smem_u32(smem);
+      const uint32_t sq = sbase + t * C::Q_BYTES;
+      const uint32_t sp = sbase + C::OFF_P + t * C::P_BYTES;
       bool ok = mbar_wait(&q_full, 0, &abort_flag, p.err);
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int s = jj & 1;
         if (!mbar_wait(&v_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
         tc_fence_after();
-        const uint32_t sv = sbase + C::OFF_V + s * C::V_BYTES;
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (jj >= (t ? n_t1 : n_t0)) continue;
+        if (jj < nt) {
           if (!mbar_wait(&p_full[t], jj & 1, &abort_flag, p.err)) return false;
           tc_fence_after();
-          const uint32_t sp = sbase + C::OFF_P + t * C::P_BYTES;
+          const uint32_t sv = sbase + C::OFF_V + s * C::V_BYTES;
           const uint32_t d = tmem_base + t * C::TMEM_TILE + 2 * BKV;
 #pragma unroll
           for (int kk = 0; kk < BKV / 8; ++kk) {
@@ -208,11 +236,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int s = j & 1;
         if (!mbar_wait(&k_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sk = sbase + C::OFF_K + s * C::K_BYTES;
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (j >= (t ? n_t1 : n_t0)) continue;
-          const uint32_t sq = sbase + t * C::Q_BYTES;
+        if (j < nt) {
+          const uint32_t sk = sbase + C::OFF_K + s * C::K_BYTES;
           const uint32_t d = tmem_base + t * C::TMEM_TILE + s * BKV;
 #pragma unroll
           for (int kk = 0; kk < HD / 8; ++kk) {
@@ -226,9 +251,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && n_kv >= 1) issue_pv(n_kv - 1);
-      umma_commit(&drain_bar);
+      umma_commit(&drain_bar[t]);
       volatile int no_abort = 0;
-      mbar_wait(&drain_bar, 0, &no_abort, p.err);
+      mbar_wait(&drain_bar[t], 0, &no_abort, p.err);
     }
   } else {
     // ------------------------------------------------ softmax (one row per thread)
@@ -313,8 +338,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       for (int c = 0; c < 8; ++c) acc[c] = 0.f;
 #pragma unroll
       for (int i = 0; i < BKV; ++i) {
-        const float pv = full ? fast_exp2(fmaf(ATT_X(i), sl2, -m_use))
-                              : fast_exp2(ATT_X(i) - m_use);
+        const float arg = full ? fmaf(ATT_X(i), sl2, -m_use) : ATT_X(i) - m_use;
+        const float pv = ((i & 7) < 3) ? exp2_fma(arg) : fast_exp2(arg);
         if (i < 32) xa[i & 31] = pv; else xb[i & 31] = pv;
         acc[i & 7] += pv;
       }
