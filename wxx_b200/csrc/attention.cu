@@ -16,11 +16,12 @@
 //   warps 1, 10 one tcgen05.mma-issuing thread per tile (warp 1 also owns
 //               the TMEM allocation), per block j: S_t(j) = Q_t K_j^T
 //               (M=128, N=64, K=hd), then O_t += P_t(j-1) V_{j-1} (M=128,
-//               N=hd, K=64; V MN-major, 32B-atom swizzle), O_t accumulated in
-//               TMEM across all blocks
+//               N=hd, K=64; P from TMEM, V MN-major with the 32B-atom
+//               swizzle), O_t accumulated in TMEM across all blocks
 //   warps 2..5  tile A, warps 6..9 tile B: one query row per thread,
-//               tcgen05.ld S, online softmax in the log2 domain, P to shared
-//               memory (K-major swizzled), final O / l through a TMA store
+//               tcgen05.ld S, online softmax in the log2 domain, P written
+//               back into TMEM over S (tcgen05.st; the P V product reads its
+//               A operand from TMEM), final O / l through a TMA store
 // Two softmax warpgroups interleave on every SM sub-partition, so one tile's
 // exponentials overlap the other's, and both overlap the tensor core.
 // The running max used for P is only raised (and O in TMEM rescaled) when a
@@ -77,11 +78,12 @@ struct ACfg {
   static constexpr int Q_BYTES = BQ * HD * 4;          // per tile: 32 KB (hd 64)
   static constexpr int K_BYTES = BKV * HD * 4;         // 16 KB
   static constexpr int V_BYTES = BKV * HD * 4;         // 16 KB
-  static constexpr int P_BYTES = BQ * BKV * 4;         // per tile: 32 KB
+  static constexpr int KVS = 4;                        // K / V pipeline stages
+  static constexpr int STAGE_O_BYTES = 4 * 4096;       // per tile: O staging for the TMA store
   static constexpr int OFF_K = NT * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
-  static constexpr int SMEM = OFF_P + NT * P_BYTES + 1024;
+  static constexpr int OFF_V = OFF_K + KVS * K_BYTES;
+  static constexpr int OFF_O = OFF_V + KVS * V_BYTES;
+  static constexpr int SMEM = OFF_O + NT * STAGE_O_BYTES + 1024;
   // TMEM per tile: S double buffer (2 x 64 columns) then O (hd columns).
   static constexpr int TMEM_TILE = 2 * BKV + HD;
   static constexpr int TMEM_COLS = 512;
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   using C = ACfg<HD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full;
-  __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  __shared__ __align__(8) uint64_t k_full[C::KVS], k_empty[C::KVS], v_full[C::KVS], v_empty[C::KVS];
   __shared__ __align__(8) uint64_t s_full[NT][2], p_full[NT], p_empty[NT];
   __shared__ __align__(8) uint64_t drain_bar[NT];
   __shared__ uint32_t tmem_base_sh;
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::KVS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], NT);   // one commit from each tile's MMA thread
       mbar_init(&v_full[s], 1);
@@ -170,10 +172,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int a = 0; a < HD / 32; ++a)
           tma_load_4d(smem_u32(smem + t * C::Q_BYTES + a * (BQ * 128)), &tm_q, &q_full, a * 32, h,
                       q0 + t * BQ, b);
-      int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
+      int last_k[C::KVS], last_v[C::KVS];
+#pragma unroll
+      for (int s = 0; s < C::KVS; ++s) last_k[s] = last_v[s] = -1;
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1;
+        const int s = j % C::KVS;
+        const uint32_t par = ((j / C::KVS) & 1) ^ 1;
         if (!mbar_wait(&k_empty[s], par, &abort_flag, p.err)) { ok = false; break; }
         mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
 #pragma unroll
@@ -192,9 +196,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       // No load may still be landing when the CTA exits (abort path included).
       volatile int no_abort = 0;
       mbar_wait(&q_full, 0, &no_abort, p.err);
-      for (int s = 0; s < 2; ++s) {
-        if (last_k[s] >= 0) mbar_wait(&k_full[s], (last_k[s] >> 1) & 1, &no_abort, p.err);
-        if (last_v[s] >= 0) mbar_wait(&v_full[s], (last_v[s] >> 1) & 1, &no_abort, p.err);
+      for (int s = 0; s < C::KVS; ++s) {
+        if (last_k[s] >= 0) mbar_wait(&k_full[s], (last_k[s] / C::KVS) & 1, &no_abort, p.err);
+        if (last_v[s] >= 0) mbar_wait(&v_full[s], (last_v[s] / C::KVS) & 1, &no_abort, p.err);
       }
     }
   } else if (warp == 1 || warp == MMA_WARP1) {
@@ -209,23 +213,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const uint32_t idesc_o = idesc_tf32_mn(BQ, HD, false, true);
       const uint32_t sbase = smem_u32(smem);
       const uint32_t sq = sbase + t * C::Q_BYTES;
-      const uint32_t sp = sbase + C::OFF_P + t * C::P_BYTES;
       bool ok = mbar_wait(&q_full, 0, &abort_flag, p.err);
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
-        const int s = jj & 1;
-        if (!mbar_wait(&v_full[s], (jj >> 1) & 1, &abort_flag, p.err)) return false;
+        const int s = jj % C::KVS;       // V stage
+        const int sb = jj & 1;           // TMEM S / P buffer
+        if (!mbar_wait(&v_full[s], (jj / C::KVS) & 1, &abort_flag, p.err)) return false;
         tc_fence_after();
         if (jj < nt) {
           if (!mbar_wait(&p_full[t], jj & 1, &abort_flag, p.err)) return false;
           tc_fence_after();
           const uint32_t sv = sbase + C::OFF_V + s * C::V_BYTES;
           const uint32_t d = tmem_base + t * C::TMEM_TILE + 2 * BKV;
+          const uint32_t pa = tmem_base + t * C::TMEM_TILE + sb * BKV;  // P_t(jj) over S_t(jj)
 #pragma unroll
           for (int kk = 0; kk < BKV / 8; ++kk) {
-            uint64_t ad = sdesc(sp + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
             uint64_t bd = sdesc(sv + kk * 1024, BKV * 128, 512, kLayoutSW128Base32B);
-            umma_tf32(d, ad, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
+            umma_tf32_ts(d, pa + kk * 8, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&p_empty[t]);
         }
@@ -233,19 +237,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         return true;
       };
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1, &abort_flag, p.err)) { ok = false; break; }
+        const int s = j % C::KVS;        // K stage
+        const int sb = j & 1;            // TMEM S buffer
+        if (!mbar_wait(&k_full[s], (j / C::KVS) & 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         if (j < nt) {
+          // S_t(j) overwrites the columns P_t(j-2) occupied: that P V product
+          // must have finished reading them.
+          if (j >= 2 && !mbar_wait(&p_empty[t], (j - 2) & 1, &abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
           const uint32_t sk = sbase + C::OFF_K + s * C::K_BYTES;
-          const uint32_t d = tmem_base + t * C::TMEM_TILE + s * BKV;
+          const uint32_t d = tmem_base + t * C::TMEM_TILE + sb * BKV;
 #pragma unroll
           for (int kk = 0; kk < HD / 8; ++kk) {
             uint64_t ad = sdesc(sq + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
             uint64_t bd = sdesc(sk + (kk >> 2) * (BKV * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
             umma_tf32(d, ad, bd, idesc_s, kk ? 1u : 0u);
           }
-          umma_commit(&s_full[t][s]);
+          umma_commit(&s_full[t][sb]);
         }
         umma_commit(&k_empty[s]);
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
@@ -274,7 +283,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int warp_lim = p.causal ? min(p.Sk, qt + quarter * 32 + 1) : p.Sk;
     const float* mrow = nullptr;
     if (HAS_MASK && qrow < p.Sq) mrow = p.mask + (int64_t)qrow * p.mask_ld;
-    uint8_t* pb = smem + C::OFF_P + tile * C::P_BYTES;
+    uint8_t* pb = smem + C::OFF_O + tile * C::STAGE_O_BYTES;
     float m_used = -INFINITY;   // max that P and l are relative to
     float l_run = 0.f;
     bool ok = true;
@@ -344,8 +353,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         acc[i & 7] += pv;
       }
       l_run += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-      // The single P buffer is free, and O holds every block < j, once the
-      // previous P V product finished.
+      // P_j -> TMEM over the S_j columns just read (row = lane, one column
+      // per key): the P V product takes its A operand from there.
+      tmem_st_32x32(lane_addr + s * BKV, xa);
+      tmem_st_32x32(lane_addr + s * BKV + 32, xb);
+#undef ATT_X
+      // The previous P V product has finished: O holds every block < j (needed
+      // by a rescale).  Waiting every block also keeps this barrier's phases
+      // within the one-phase window a parity wait can tell apart.
       if (j >= 1) {
         if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[tile], (j - 1) & 1, &abort_flag, p.err))) {
           ok = false;
@@ -353,15 +368,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         tc_fence_after();
       }
-      // P_j -> shared memory, K-major 128B-swizzled (2 atoms of 32 keys).
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        *reinterpret_cast<float4*>(pb + row * 128 + ((q ^ (row & 7)) << 4)) =
-            make_float4(xa[4 * q], xa[4 * q + 1], xa[4 * q + 2], xa[4 * q + 3]);
-        *reinterpret_cast<float4*>(pb + BQ * 128 + row * 128 + ((q ^ (row & 7)) << 4)) =
-            make_float4(xb[4 * q], xb[4 * q + 1], xb[4 * q + 2], xb[4 * q + 3]);
-      }
-#undef ATT_X
       if (warp_rescale) {
         // O in TMEM holds blocks < j relative to the old max: scale the rows
         // that raised theirs before P_j V_j accumulates on top.
@@ -374,7 +380,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           tmem_st_32x32(o_addr + c, v);
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[tile]);
     }
