@@ -547,3 +547,43 @@ def test_swiglu_padded_hidden_matches_plain(d, hidden, mode, tol, rng):
     # the padded copies follow parameter updates
     F.assign(m.w1.weight, F.from_numpy(np.zeros((d, hidden), np.float32)))
     assert np.abs(m(x).numpy()).max() == 0.0
+
+
+@pytest.mark.parametrize("shape", [((), (), 2304, 2304, 64), ((), (), 2300, 2200, 100),
+                                   ((2,), (2,), 1280, 2048, 96), ((), (), 8192, 1024, 4096)])
+@pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
+def test_matmul_stream_k_opt_in(shape, mode, rng, monkeypatch):
+    """SM-pair GEMM with the stream-K schedule (WXX_GEMM_STREAMK=1): partial
+    tiles handed between pairs through the workspace and per-tile counters."""
+    monkeypatch.setenv("WXX_GEMM_STREAMK", "1")
+    F = _w().functional
+    ba, bb, M, N, K_ = shape
+    a = rng.standard_normal(ba + (M, K_)).astype(np.float32)
+    b = rng.standard_normal(bb + (K_, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    F.set_matmul_mode(mode)
+    try:
+        got = F.matmul_add(up(a), up(b), up(bias)).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    ref = K.matmul_add(a, b, bias)
+    assert rel(got, ref) < (2e-3 if mode == "tf32" else 1e-5)
+    assert _w().backend.device_status() == 0
+
+
+@pytest.mark.parametrize("batch,M,N,kdim", [(1, 2048, 512, 4096), (1, 1024, 256, 16384),
+                                            (4, 512, 256, 4096), (1, 8192, 1024, 4096)])
+def test_matmul_3xtf32_long_k_stays_fp32_faithful(batch, M, N, kdim, rng):
+    """3xTF32 with long K: the product is summed in fp32 over slices of at
+    most 1024 K-values per pass, keeping the 1e-5 bar at any K."""
+    F = _w().functional
+    a = rng.standard_normal(((batch,) if batch > 1 else ()) + (M, kdim)).astype(np.float32)
+    b = rng.standard_normal((kdim, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    F.set_matmul_mode("3xtf32")
+    try:
+        got = F.matmul_add(up(a), up(b), up(bias)).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    assert rel(got, K.matmul_add(a, b, bias)) < 1e-5
+    assert _w().backend.device_status() == 0

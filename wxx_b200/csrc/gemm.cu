@@ -16,6 +16,7 @@
 #include <cstring>
 #include <mutex>
 
+extern "C" int wxx_memset(void* dst, int value, uint64_t nbytes);
 extern "C" int wxx_malloc(void** out, uint64_t nbytes);
 extern "C" int wxx_free(void* p);
 
@@ -107,8 +108,8 @@ bool encode_c_map(CUtensorMap* map, const GemmParams& p) {
   auto enc = get_encode();
   if (!enc || p.epi.kind != 0 || p.epi.bias_mode > 1) return false;
   if ((reinterpret_cast<uintptr_t>(p.epi.C) & 15) || ((int64_t)p.epi.ldc * 4) % 16) return false;
-  // split-K partials: z runs over the K-slices of the workspace
-  const int zdim = p.epi.raw ? p.splits : p.batch;
+  // split-K partials: z runs over (batch, K-slice) of the workspace
+  const int zdim = p.epi.raw ? p.batch * p.splits : p.batch;
   if (zdim > 1 && (p.epi.c_bs * 4) % 16) return false;
   cuuint64_t dims[3] = {(cuuint64_t)p.N, (cuuint64_t)p.M, (cuuint64_t)zdim};
   cuuint64_t strides[2] = {(cuuint64_t)p.epi.ldc * 4,
@@ -191,10 +192,45 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   }
   int pairs = max_pairs;
   if (tiles < pairs) pairs = (int)tiles;
+  // Stream-K (opt-in, WXX_GEMM_STREAMK=1) when whole waves would leave many
+  // pairs idle in the last one (> 5 % of the pair-time lost) and every pair
+  // still covers >= 1 tile.  Off by default: inside the captured GPT2 step it
+  // measured slower than whole tiles (the partial-tile traffic and the extra
+  // memset outweigh the balanced last wave), although a lone K = 4096 product
+  // gained 8 %.
+  const char* sk_env = getenv("WXX_GEMM_STREAMK");
+  const int64_t waves = (tiles + pairs - 1) / pairs;
+  const bool sk = sk_env != nullptr && sk_env[0] == '1' && tiles >= pairs &&
+                  (double)tiles / (double)(waves * pairs) < 0.95;
+  void* ws = nullptr;
+  void* flags = nullptr;
+  p.sk = 0;
+  p.sk_ws = nullptr;
+  p.sk_flags = nullptr;
+  if (sk) {
+    int st = wxx_malloc(&ws, (uint64_t)pairs * 2 * BM * BN * sizeof(float));
+    if (st == WXX_OK) st = wxx_malloc(&flags, (uint64_t)tiles * sizeof(int));
+    if (st == WXX_OK) st = wxx_memset(flags, 0, (uint64_t)tiles * sizeof(int));
+    if (st != WXX_OK) {
+      wxx_free(ws);
+      wxx_free(flags);
+      return st;
+    }
+    p.sk = 1;
+    p.sk_ws = (float*)ws;
+    p.sk_flags = (int*)flags;
+  }
   tc_gemm_pair_kernel<BN><<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1,
                                                                                      mc, p);
-  WXX_LAUNCH_CHECK();
-  return WXX_OK;
+  cudaError_t e = cudaGetLastError();
+  wxx::count_launch();
+  int st_ws = wxx_free(ws);       // stream-ordered: valid for the kernel just enqueued
+  int st_fl = wxx_free(flags);
+  if (e != cudaSuccess) {
+    wxx::set_error("SM-pair GEMM launch failed: %s", cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
+  return st_ws ? st_ws : st_fl;
 }
 
 // SM-pair tiles are used for large TMA-fed products (enough 256 x 256 tiles
@@ -231,34 +267,44 @@ int choose_splits(int64_t tiles, int total_kb) {
   return sp < 2 ? 1 : (int)sp;
 }
 
-// out = alpha * (ws[0] + ws[1] + ... ) + bias, the K-slices added in index
-// order (deterministic).  kind 0: row-major C[m*ldc + n]; kind 1: NCHW
-// C[(b*N + n)*hw + pix] with m = b*hw + pix (m fastest: coalesced writes).
+// out = alpha * (ws[0] + ws[1] + ... ) + bias, the K-slices of each batch
+// entry added in index order (deterministic); ws is [batch][slice][M][N].
+// kind 0: row-major C[b*c_bs + m*ldc + n] with bias_mode 1 (n), 2 (m, n) or
+// 3 (b, m, n); kind 1 (batch 1): NCHW C[(img*N + n)*hw + pix] with
+// m = img*hw + pix (m fastest there: coalesced writes).
 __global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restrict__ ws,
-                                     int splits, int M, int N, float alpha,
-                                     const float* __restrict__ bias, int kind, int64_t ldc,
-                                     int hw) {
+                                     int splits, int batch, int M, int N, float alpha,
+                                     const float* __restrict__ bias, int bias_mode, int kind,
+                                     int64_t ldc, int64_t c_bs, int hw) {
   const int64_t MN = (int64_t)M * N;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < MN;
+  const int64_t total = MN * batch;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / MN;
+    const int64_t r = i - b * MN;
     int64_t m, n;
     if (kind == 0) {
-      m = i / N;
-      n = i - m * N;
+      m = r / N;
+      n = r - m * N;
     } else {
-      n = i / M;
-      m = i - n * M;
+      n = r / M;
+      m = r - n * M;
     }
     const int64_t src = m * N + n;
-    float acc = ws[src];
-    for (int k = 1; k < splits; ++k) acc += ws[(int64_t)k * MN + src];
+    const float* w = ws + b * splits * MN;
+    float acc = w[src];
+    for (int k = 1; k < splits; ++k) acc += w[(int64_t)k * MN + src];
     float v = acc * alpha;
-    if (bias != nullptr) v += bias[n];
+    if (bias != nullptr) {
+      if (bias_mode == 1) v += bias[n];
+      else if (bias_mode == 2) v += bias[src];
+      else v += bias[b * MN + src];
+    }
     if (kind == 0) {
-      C[m * ldc + n] = v;
+      C[b * c_bs + m * ldc + n] = v;
     } else {
-      const int64_t b = m / hw, pix = m - b * hw;
-      C[(b * N + n) * hw + pix] = v;
+      const int64_t img = m / hw, pix = m - img * hw;
+      C[(img * N + n) * hw + pix] = v;
     }
   }
 }
@@ -266,11 +312,25 @@ __global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restr
 int run_tc(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
            const CUtensorMap& b1, GemmParams& p);
 
-// Sets p.splits / p.kb_per_split for BN-wide tiles; true when split-K applies.
+// Longest tensor-core accumulation chain (K-blocks over all passes) allowed in
+// 3xTF32 mode.  The TMEM accumulator loses precision along a chain (measured:
+// 3xTF32 max error 2.7e-6 at K = 1024, 1.1e-5 at 4096, 3.7e-5 at 16384 with
+// whole-K accumulation; 0.7e-6 to 3.9e-6 when 512-deep slices are summed in
+// fp32 on the CUDA cores), so fp32-faithful products are cut into slices.
+constexpr int kMaxChainKb3x = 96;
+
+// Sets p.splits / p.kb_per_split for BN-wide tiles; true when split-K applies:
+// few output tiles (batch 1), or a 3xTF32 product longer than kMaxChainKb3x.
 bool plan_splits(GemmParams& p, int bn) {
   const int total_kb = p.num_kb * p.passes;
-  const int64_t tiles = (int64_t)p.batch * ((p.M + BM - 1) / BM) * ((p.N + bn - 1) / bn);
-  int sp = (p.batch == 1 && p.N % 4 == 0) ? choose_splits(tiles, total_kb) : 1;
+  if (p.N % 4) return false;   // the workspace is written by TMA stores
+  int sp = 1;
+  if (p.passes > 1 && total_kb > kMaxChainKb3x) {
+    sp = (total_kb + kMaxChainKb3x - 1) / kMaxChainKb3x;
+  } else if (p.batch == 1) {
+    const int64_t tiles = ((p.M + BM - 1) / BM) * (int64_t)((p.N + bn - 1) / bn);
+    sp = choose_splits(tiles, total_kb);
+  }
   if (sp <= 1) return false;
   p.kb_per_split = (total_kb + sp - 1) / sp;
   p.splits = (total_kb + p.kb_per_split - 1) / p.kb_per_split;   // no empty slice
@@ -285,7 +345,7 @@ int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUten
   const EpiParams real = p.epi;
   const int64_t MN = (int64_t)p.M * p.N;
   void* ws = nullptr;
-  int st = wxx_malloc(&ws, (uint64_t)p.splits * MN * sizeof(float));
+  int st = wxx_malloc(&ws, (uint64_t)p.batch * p.splits * MN * sizeof(float));
   if (st) return st;
   p.epi.kind = 0;
   p.epi.C = (float*)ws;
@@ -297,10 +357,10 @@ int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUten
   p.epi.raw = 1;
   st = run_tc(bn, a0, a1, b0, b1, p);
   if (st == WXX_OK) {
-    splitk_reduce_kernel<<<wxx::grid_for(MN, 256), 256, 0, wxx::stream()>>>(
-        real.C, (const float*)ws, p.splits, p.M, p.N, real.alpha,
-        real.bias_mode == 1 ? real.bias : nullptr, real.kind,
-        real.kind == 0 ? (int64_t)real.ldc : 0, real.hw_out);
+    splitk_reduce_kernel<<<wxx::grid_for(MN * p.batch, 256), 256, 0, wxx::stream()>>>(
+        real.C, (const float*)ws, p.splits, p.batch, p.M, p.N, real.alpha,
+        real.bias_mode ? real.bias : nullptr, real.bias_mode, real.kind,
+        real.kind == 0 ? (int64_t)real.ldc : 0, real.kind == 0 ? real.c_bs : 0, real.hw_out);
     cudaError_t e = cudaGetLastError();
     wxx::count_launch();
     if (e != cudaSuccess) {
@@ -512,7 +572,9 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   CUtensorMap mc;
   memset(&mc, 0, sizeof(mc));
   int64_t pair_tiles = batch * ((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
-  bool pair = bn == 256 && pair_enabled() && pair_tiles >= wxx::num_sms() / 2 &&
+  // 3xTF32 products longer than one accumulation chain go to split-K instead.
+  const bool long_3x = p.passes > 1 && p.num_kb * p.passes > kMaxChainKb3x;
+  bool pair = bn == 256 && pair_enabled() && !long_3x && pair_tiles >= wxx::num_sms() / 2 &&
               encode_c_map(&mc, p);
   setup_operand(da, BM, true, p.a, &ma0);
   setup_operand(db, pair ? BM : bn, true, p.b, &mb0);
@@ -537,7 +599,7 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   int st;
   if (pair) {
     st = launch_pair<256>(ma0, ma1, mb0, mb1, mc, p);
-  } else if (act == 0 && res == nullptr && bias_mode <= 1 && plan_splits(p, bn)) {
+  } else if (act == 0 && res == nullptr && plan_splits(p, bn)) {
     st = run_splitk(bn, ma0, ma1, mb0, mb1, p);
   } else {
     st = run_tc(bn, ma0, ma1, mb0, mb1, p);

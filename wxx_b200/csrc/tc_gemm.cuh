@@ -360,7 +360,7 @@ struct EpiParams {
   int act;                // 0 none, 1 GELU (tanh form)
   const float* res;       // residual (M, N) per batch, or NULL
   int64_t res_ld, res_bs;
-  int raw;                // split-K: raw partial sums to the workspace map, slice index as z
+  int raw;                // split-K: raw partial sums to the workspace map, z = batch * splits + slice
 };
 
 struct GemmParams {
@@ -372,6 +372,13 @@ struct GemmParams {
   int passes;             // 1 = TF32; 3 = 3xTF32 (hi*lo, lo*hi, hi*hi)
   int splits;             // K-slices per tile (split-K; 1 = whole K)
   int kb_per_split;       // K-blocks (over all passes) per slice
+  // SM-pair kernel, stream-K: the pairs share the tile-major K-block
+  // iterations evenly; a pair that does not reach a tile's last K-block
+  // leaves its raw partial in sk_ws (slot = its pair index) and counts it in
+  // sk_flags[tile]; the pair finishing the tile adds it.
+  int sk;
+  float* sk_ws;
+  int* sk_flags;
   OperandSrc a, b;
   EpiParams epi;
   int* err;
@@ -935,7 +942,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tm_c, smem_u32(buf), n0, m0, p.epi.raw ? sp : bt);
+            tma_store_3d(&tm_c, smem_u32(buf), n0, m0, p.epi.raw ? bt * p.splits + sp : bt);
             bulk_commit();
           }
           ++chunk_seq;
@@ -995,6 +1002,65 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // the leader), warps 2..5 epilogue of this CTA's 128 rows.
 constexpr int PAIR_THREADS = 192;
 
+// First K-block iteration of pair q when W iterations are shared by P pairs.
+__device__ __forceinline__ int64_t sk_start(int q, int64_t W, int P) {
+  return (int64_t)q * W / P;
+}
+
+// Number of work units of `pair`: strided whole tiles, or (stream-K) the
+// tiles its iteration range touches.
+__device__ __forceinline__ int pair_units(const GemmParams& p, int pair, int np, int tiles,
+                                          int kb) {
+  if (!p.sk) return pair < tiles ? (tiles - 1 - pair) / np + 1 : 0;
+  const int64_t W = (int64_t)tiles * kb;
+  const int64_t a = sk_start(pair, W, np), b = sk_start(pair + 1, W, np);
+  if (a >= b) return 0;
+  return (int)((b - 1) / kb - a / kb + 1);
+}
+
+// Unit i of `pair`: tile t and its K-block range [k0, k1).  Stream-K order:
+// first the head of the pair's last tile (a contributor: never waits), then
+// the tail of its first tile (the finisher: waits for the previous pair's
+// first unit, and its epilogue overlaps the main loops that follow), then the
+// whole tiles in between.
+__device__ __forceinline__ void pair_unit(const GemmParams& p, int pair, int np, int tiles, int kb,
+                                          int i, int& t, int& k0, int& k1) {
+  if (!p.sk) {
+    t = pair + i * np;
+    k0 = 0;
+    k1 = kb;
+    return;
+  }
+  const int64_t W = (int64_t)tiles * kb;
+  const int64_t a = sk_start(pair, W, np), b = sk_start(pair + 1, W, np);
+  const int t_first = (int)(a / kb), t_last = (int)((b - 1) / kb);
+  const int head = (int)(b - (int64_t)t_last * kb);    // K-blocks of the last tile
+  const int tail0 = (int)(a - (int64_t)t_first * kb);  // first K-block in the first tile
+  const bool has_con = head < kb;
+  const bool has_fin = tail0 > 0;
+  if (has_con) {
+    if (i == 0) { t = t_last; k0 = 0; k1 = head; return; }
+    --i;
+  }
+  if (has_fin) {
+    if (i == 0) { t = t_first; k0 = tail0; k1 = kb; return; }
+    --i;
+  }
+  t = t_first + (has_fin ? 1 : 0) + i;
+  k0 = 0;
+  k1 = kb;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_add(int* ptr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
 template <int BN>
 struct PairCfg {
   static constexpr int A_BYTES = BM * BK * 4;                 // 16 KB
@@ -1037,6 +1103,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
   const int num_pairs = gridDim.x >> 1;
   const int total_tiles = p.batch * p.tiles_m * p.tiles_n;
   const int total_kb = p.num_kb * p.passes;
+  const int n_units = pair_units(p, pair, num_pairs, total_tiles, total_kb);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -1071,12 +1138,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += num_pairs) {
-        int bt, tm, tn;
+      for (int u = 0; u < n_units && ok; ++u) {
+        int t, k0, k1, bt, tm, tn;
+        pair_unit(p, pair, num_pairs, total_tiles, total_kb, u, t, k0, k1);
         tile_coords(p, t, bt, tm, tn);
         const int row_a = tm * PM + (int)rank * BM;
         const int row_b = tn * BN + (int)rank * (BN / 2);
-        for (int kb = 0; kb < total_kb; ++kb) {
+        for (int kb = k0; kb < k1; ++kb) {
           if (!mbar_wait_cl(&empty_bar[stage], phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
@@ -1126,13 +1194,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += num_pairs, ++local) {
+      for (int u = 0; u < n_units && ok; ++u, ++local) {
+        int t, k0, k1;
+        pair_unit(p, pair, num_pairs, total_tiles, total_kb, u, t, k0, k1);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_cl(&tempty_bar[acc], acc_phase ^ 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < total_kb; ++kb) {
+        for (int kb = k0; kb < k1; ++kb) {
           if (!mbar_wait_cl(&full_bar[stage], phase, &abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
@@ -1141,7 +1211,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             uint64_t ad = a_mn ? sdesc_mnmajor(sa, kk) : sdesc_kmajor(sa, kk);
             uint64_t bd = b_mn ? sdesc_mnmajor(sb, kk) : sdesc_kmajor(sb, kk);
-            umma2_tf32(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+            umma2_tf32(d_tmem, ad, bd, idesc, ((kb - k0) | kk) ? 1u : 0u);
           }
           const uint32_t eb = smem_u32(&empty_bar[stage]);
           umma2_commit(eb);
@@ -1167,8 +1237,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
     int local = 0;
     int chunk_seq = 0;
-    for (int t = pair; t < total_tiles; t += num_pairs, ++local) {
-      int bt, tm, tn;
+    for (int u = 0; u < n_units; ++u, ++local) {
+      int t, k0, k1, bt, tm, tn;
+      pair_unit(p, pair, num_pairs, total_tiles, total_kb, u, t, k0, k1);
       tile_coords(p, t, bt, tm, tn);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -1177,12 +1248,69 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
       tc_fence_after();
       const int m0 = tm * PM + (int)rank * BM + quarter * 32;
       const uint32_t row_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      // Stream-K roles.  A warp's share of a tile's partial (its 32 rows x BN
+      // columns) is stored in register order, [chunk][quad][lane] float4s, so
+      // every store and load of the warp covers 512 contiguous bytes; slot =
+      // the contributing pair, then its CTA rank and the warp's quarter.
+      const bool contributor = k1 < total_kb;
+      const bool finisher = k0 > 0;
+      if (contributor) {
+        float4* wq = reinterpret_cast<float4*>(
+            p.sk_ws + (((int64_t)pair * 2 + rank) * 4 + quarter) * (32 * BN));
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld_32x32(row_addr + (uint32_t)c, v);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            wq[((c >> 5) * 8 + q) * 32 + lane] =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_release_add(p.sk_flags + t, 1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        continue;
+      }
+      const float* prow = nullptr;
+      if (finisher) {
+        // The head of this tile was computed by the previous pair (whose
+        // range holds at least one whole tile); its 8 epilogue warps each
+        // count their rows in sk_flags[t].
+        bool ready = true;
+        if (lane == 0) {
+          unsigned long long t_start = globaltimer();
+          while (ld_acquire_gpu(p.sk_flags + t) < 8) {
+            if (abort_flag || globaltimer() - t_start > kWaitLimitNs) {
+              if (!abort_flag) wxx_device_fail(p.err, WXX_DEV_ERR_MBAR_TIMEOUT);
+              abort_flag = 1;
+              ready = false;
+              break;
+            }
+          }
+        }
+        ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
+        if (!ready) break;
+        prow = p.sk_ws + (((int64_t)(pair - 1) * 2 + rank) * 4 + quarter) * (32 * BN);
+      }
 #pragma unroll 1
       for (int c = 0; c < BN && m0 < p.M; c += 32) {
         const int n0 = tn * BN + c;
         if (n0 >= p.N) break;
         float v[32];
         tmem_ld_32x32(row_addr + (uint32_t)c, v);
+        if (prow != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 w = __ldcg(reinterpret_cast<const float4*>(prow) + ((c >> 5) * 8 + q) * 32 + lane);
+            v[4 * q] += w.x;
+            v[4 * q + 1] += w.y;
+            v[4 * q + 2] += w.z;
+            v[4 * q + 3] += w.w;
+          }
+        }
         epi_apply(p, bt, m0 + lane, n0, v);
         uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
         if (lane == 0) bulk_wait_read<1>();

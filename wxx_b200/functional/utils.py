@@ -208,7 +208,7 @@ def linear(x, weight, bias=None, *, activation=None, residual=None):
     like the output or None.  The result has the same bits as
     ``matmul_add`` followed by ``gelu`` / ``residual + y``, which is the path
     taken when the fused form does not apply (fp32 SIMT mode, N not a
-    multiple of 4)."""
+    multiple of 4, 3xTF32 with K > 1024)."""
     if activation not in (None, "gelu"):
         raise ValueError(f"activation must be None or 'gelu', got {activation!r}")
     a = dense(x)
@@ -224,7 +224,9 @@ def linear(x, weight, bias=None, *, activation=None, residual=None):
         raise ValueError(f"linear: residual {tuple(residual.shape)} is not {tuple(out_shape)}")
     mode = matmul_mode_code()
     M = int(math.prod(a.shape[:-1])) if len(a.shape) > 1 else 1
-    if mode not in (0, 1) or N % 4 or K == 0:
+    # 3xTF32 products with K > 1024 are summed in slices (split-K) to bound
+    # the tensor-core accumulation chain; that path has no fused epilogue.
+    if mode not in (0, 1) or N % 4 or K == 0 or (mode == 1 and K > 1024):
         y = matmul_add(x, weight, bias)
         if activation == "gelu":
             y = y.gelu()
