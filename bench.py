@@ -204,6 +204,13 @@ SWEEPS["fftconv"] = Sweep("fftconv", [(16, 256, 16384), (256, 16384)],
                           lambda F, x, h: F.fftconv(x, h, 32768, out_len=16384),
                           528 * 2 ** 20, "GB/s", "hbm",
                           "fft_row_kernel<14, conv> (+ rfft of h)", flush_l2=False)
+# Hyena's fft_conv1d at the hyena workload's shape (B 16, D 256, L 8192,
+# n 16384): x and y once each (128 MiB each), h once (8 MiB), its spectrum
+# written and read (2 x 16 MiB).
+SWEEPS["fftconv_hyena"] = Sweep("fftconv_hyena", [(16, 256, 8192), (256, 8192)],
+                                lambda F, x, h: F.fftconv(x, h, 16384, out_len=8192),
+                                296 * 2 ** 20, "GB/s", "hbm",
+                                "fft_row_kernel<13, conv> (+ rfft of h)", flush_l2=False)
 # GPT2-scaled attention core (B 8, S 1024, 16 heads x 64, causal): useful
 # FLOPs are the two products over the S(S+1)/2 unmasked (query, key) pairs.
 SWEEPS["attention"] = Sweep("attention", [(8, 1024, 1024)] * 3,
@@ -332,6 +339,9 @@ def _sweep_cpu(sw, arrays):
     if sw.name == "fftconv":
         return lambda: np.fft.irfft(np.fft.rfft(arrays[0], 32768) * np.fft.rfft(arrays[1], 32768),
                                     32768)[..., :16384]
+    if sw.name == "fftconv_hyena":
+        return lambda: np.fft.irfft(np.fft.rfft(arrays[0], 16384) * np.fft.rfft(arrays[1], 16384),
+                                    16384)[..., :8192]
     if sw.name == "attention":
         def attn():
             B, S, D = arrays[0].shape
@@ -360,6 +370,9 @@ def _sweep_cpu_sample(sw, rng):
                 rng.standard_normal((256, 16384), dtype=np.float32)], 1 / 16
     if sw.name == "attention":
         return [rng.standard_normal((1, 1024, 1024), dtype=np.float32) for _ in range(3)], 1 / 8
+    if sw.name == "fftconv_hyena":
+        return [rng.standard_normal((1, 256, 8192), dtype=np.float32),
+                rng.standard_normal((256, 8192), dtype=np.float32)], 1 / 16
     if sw.name == "matmul_8192":
         return [rng.standard_normal((1024, 8192), dtype=np.float32),
                 rng.standard_normal((8192, 8192), dtype=np.float32)], 1 / 8

@@ -31,6 +31,7 @@ int require_init();                 // WXX_OK once wxx_init() succeeded
 cudaStream_t stream();              // library stream of the current device
 int num_sms();                      // SM count of the current device
 int* device_error_word();           // device pointer to the error word
+int fft_init_tables();              // FFT twiddle tables (fft.cu), run by wxx_init
 
 // Grid size for a grid-stride elementwise kernel: enough CTAs to fill the
 // GPU (a multiple of the SM count) but never more than the work needs.

@@ -41,7 +41,12 @@ __device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2
 
 // Shared-memory index with one pad slot per 32 elements (breaks the
 // power-of-two strides of the first Stockham pass into distinct banks).
-__device__ __forceinline__ int pad(int i) { return i + (i >> 5); }
+// Shared-memory padding: one spare slot after every 16 values.  Every access
+// pattern of a pass (16 consecutive indices per half-warp on load; 17j + r
+// or consecutive indices on store) then takes the minimum two wavefronts per
+// warp, and because the pass strides are multiples of 16, pad(i + c*16m) =
+// pad(i) + c*17m: each thread computes one base and uses constant offsets.
+__device__ __forceinline__ int swz(int i) { return i + (i >> 4); }
 
 __host__ __device__ constexpr int bitrev_c(int i, int bits) {
   int r = 0;
@@ -82,9 +87,84 @@ __device__ __forceinline__ float2 rot16(float2 b, int q) {
   return make_float2(b.x * c - b.y * s, b.x * s + b.y * c);
 }
 
-// In-register radix-R DFT (R <= 16), natural order in and out.
+// e^{-2 pi i q / 32} = cos32(q) - i sin32(q), q = 0..15 (written out like
+// cos16 / sin16 so that every use folds to constants).
+__host__ __device__ constexpr float cos32(int q) {
+  return q == 0 ? 1.0f
+       : q == 1 ? 0.98078528040323043f
+       : q == 2 ? 0.92387953251128674f
+       : q == 3 ? 0.83146961230254524f
+       : q == 4 ? 0.70710678118654757f
+       : q == 5 ? 0.55557023301960229f
+       : q == 6 ? 0.38268343236508984f
+       : q == 7 ? 0.19509032201612833f
+       : q == 8 ? 6.123233995736766e-17f
+       : q == 9 ? -0.19509032201612819f
+       : q == 10 ? -0.38268343236508973f
+       : q == 11 ? -0.55557023301960196f
+       : q == 12 ? -0.70710678118654746f
+       : q == 13 ? -0.83146961230254535f
+       : q == 14 ? -0.92387953251128674f
+                 : -0.98078528040323043f;
+}
+__host__ __device__ constexpr float sin32(int q) {
+  return q == 0 ? 0.0f
+       : q == 1 ? 0.19509032201612825f
+       : q == 2 ? 0.38268343236508978f
+       : q == 3 ? 0.55557023301960218f
+       : q == 4 ? 0.70710678118654746f
+       : q == 5 ? 0.83146961230254524f
+       : q == 6 ? 0.92387953251128674f
+       : q == 7 ? 0.98078528040323043f
+       : q == 8 ? 1.0f
+       : q == 9 ? 0.98078528040323043f
+       : q == 10 ? 0.92387953251128674f
+       : q == 11 ? 0.83146961230254546f
+       : q == 12 ? 0.70710678118654757f
+       : q == 13 ? 0.55557023301960218f
+       : q == 14 ? 0.38268343236508989f
+                 : 0.19509032201612861f;
+}
+
+// Multiplies b by e^{-+2 pi i q/32}, q < 16, special-casing 1 and -+i.
+template <bool INV>
+__device__ __forceinline__ float2 rot32(float2 b, int q) {
+  if (q == 0) return b;
+  if (q == 8) return INV ? make_float2(-b.y, b.x) : make_float2(b.y, -b.x);
+  float c = cos32(q), s = INV ? sin32(q) : -sin32(q);
+  return make_float2(b.x * c - b.y * s, b.x * s + b.y * c);
+}
+
+template <int R, bool INV>
+__device__ __forceinline__ void reg_fft(float2 (&v)[R]);
+
+// 32-point DFT as two 16-point DFTs (even / odd samples) and one combine
+// stage: X[k] = E[k] + w^k O[k], X[k + 16] = E[k] - w^k O[k], w = e^{-2 pi i/32}.
+template <bool INV>
+__device__ __forceinline__ void reg_fft32(float2 (&v)[32]) {
+  float2 e[16], o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    e[i] = v[2 * i];
+    o[i] = v[2 * i + 1];
+  }
+  reg_fft<16, INV>(e);
+  reg_fft<16, INV>(o);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float2 b = rot32<INV>(o[k], k);
+    v[k] = cadd(e[k], b);
+    v[k + 16] = csub(e[k], b);
+  }
+}
+
+// In-register radix-R DFT (R <= 32), natural order in and out.
 template <int R, bool INV>
 __device__ __forceinline__ void reg_fft(float2 (&v)[R]) {
+  if constexpr (R == 32) {
+    reg_fft32<INV>(v);
+    return;
+  }
   constexpr int BITS = log2_c(R);
   float2 t[R];
 #pragma unroll
@@ -96,7 +176,8 @@ __device__ __forceinline__ void reg_fft(float2 (&v)[R]) {
 #pragma unroll
       for (int j = 0; j < m / 2; ++j) {
         float2 a = t[k + j];
-        float2 b = rot16<INV>(t[k + j + m / 2], j * (16 / m));
+        float2 b = R <= 16 ? rot16<INV>(t[k + j + m / 2], j * (16 / m))
+                           : rot32<INV>(t[k + j + m / 2], j * (32 / m));
         t[k + j] = cadd(a, b);
         t[k + j + m / 2] = csub(a, b);
       }
@@ -106,37 +187,107 @@ __device__ __forceinline__ void reg_fft(float2 (&v)[R]) {
   for (int i = 0; i < R; ++i) v[i] = t[i];
 }
 
-struct Twiddles {
-  const float2* fine;    // e^{-2 pi i f / N}, f < F
-  const float2* coarse;  // e^{-2 pi i c F / N}, c < N / F
-  int fbits;
-};
+// ------------------------------------------------------------ twiddle tables
+//
+// One table per transform size N = 2^L complex values (L <= kMaxSmemLogN),
+// filled once per device (wxx::fft_init_tables, at wxx_init) in double
+// precision:
+//   for each pass in order (radix R, sub-transform size NS before it):
+//     (R - 1) * NS entries  w[(r - 1) * NS + k] = exp(-2 pi i r k / (R NS))
+//   then N/2 + 1 entries    u[k] = exp(-i pi k / N)   (real-FFT unpack / pack)
+// Stored [r - 1][k], so a warp's twiddle loads (consecutive k) are contiguous.
 
-__device__ __forceinline__ float2 twiddle(const Twiddles& tw, int t) {
-  return cmul(tw.coarse[t >> tw.fbits], tw.fine[t & ((1 << tw.fbits) - 1)]);
+constexpr int kMaxSmemLogN = 14;  // N = 16384 complex values per CTA
+
+// Radix of the pass that follows sub-transforms of size ns in an n-point
+// transform (n = 2^L): radix-16 passes, then either one radix-32 pass
+// (L = 1 mod 4), two (L = 2 mod 4, L >= 10) or a final radix 2/4/8 -- the
+// larger radices come last, where every store stride is a multiple of 16.
+__host__ __device__ constexpr int pass_radix(int n, int ns) {
+  const int L = log2_c(n), done = log2_c(ns);
+  const int tail32 = (L >= 10 && L % 4 == 2) ? 2 : ((L >= 5 && L % 4 == 1) ? 1 : 0);
+  const int head = L - 5 * tail32;
+  if (done < head) return head - done >= 4 ? 16 : (1 << (head - done));
+  return 32;
 }
 
-// One in-place Stockham pass of radix R over N values (sub-transform size Ns
-// so far).  Each butterfly j loads buf[j + r*N/R], applies the twiddles
-// w^(r * (j mod Ns) * N/(Ns R)), runs the radix-R DFT and stores to
-// ((j - j mod Ns) * R + j mod Ns) + r*Ns.  All loads finish (barrier) before
-// any store, so a single buffer suffices.
-template <int R, int PER, int T, bool INV>
-__device__ __forceinline__ void stockham_pass(float2* buf, int N, int Ns, const Twiddles& tw) {
-  const int nb = N / R;
+__host__ __device__ constexpr int tw_passes_size(int n) {
+  int total = 0;
+  for (int ns = 1; ns < n; ns *= pass_radix(n, ns)) total += (pass_radix(n, ns) - 1) * ns;
+  return total;
+}
+
+__host__ __device__ constexpr int tw_size(int l) { return tw_passes_size(1 << l) + (1 << l) / 2 + 1; }
+
+__host__ __device__ constexpr int tw_offset(int l) {
+  int o = 0;
+  for (int i = 0; i < l; ++i) o += tw_size(i);
+  return o;
+}
+
+constexpr int kTwTotal = tw_offset(kMaxSmemLogN + 1);
+static __device__ float2 g_fft_tw[kTwTotal];
+
+__global__ void fft_twiddle_init_kernel() {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < kTwTotal; e += gridDim.x * blockDim.x) {
+    int l = 0;
+    while (l < kMaxSmemLogN && e >= tw_offset(l + 1)) ++l;
+    int local = e - tw_offset(l);
+    const int n = 1 << l;
+    double angle = 0.0;   // in units of pi
+    bool done = false;
+    for (int ns = 1; ns < n && !done; ns *= pass_radix(n, ns)) {
+      const int r = pass_radix(n, ns);
+      const int seg = (r - 1) * ns;
+      if (local < seg) {
+        const int rr = local / ns + 1, k = local % ns;
+        angle = -2.0 * (double)rr * (double)k / ((double)r * (double)ns);
+        done = true;
+      } else {
+        local -= seg;
+      }
+    }
+    if (!done) angle = -(double)local / (double)n;
+    double sn, cs;
+    sincospi(angle, &sn, &cs);
+    g_fft_tw[e] = make_float2((float)cs, (float)sn);
+  }
+}
+
+// One in-place Stockham pass of radix R over N values whose sub-transforms
+// so far have size NS (compile-time, so every stride is a constant).
+// Butterfly j loads buf[j + r*N/R], multiplies by w[(r-1)*NS + j mod NS],
+// runs the radix-R DFT in registers and stores to
+// (j - j mod NS) * R + j mod NS + r*NS.  All loads finish (barrier) before any
+// store, so a single buffer suffices.
+template <int N, int R, int NS, int T, bool INV>
+__device__ __forceinline__ void fft_pass(float2* buf, const float2* __restrict__ tw) {
+  constexpr int NB = N / R;
+  constexpr int PER = (NB + T - 1) / T;
+  // Constant-offset forms (see swz): loads stride NB, stores stride NS.
+  constexpr bool LOAD_LIN = NB % 16 == 0;
+  // NS == 1 with R = 16 or 32: d = R j is a multiple of 16, so
+  // pad(d + r) = pad(d) + r + r / 16.
+  constexpr bool STORE_LIN = NS % 16 == 0 || (NS == 1 && (R == 16 || R == 32));
   float2 v[PER][R];
 #pragma unroll
   for (int p = 0; p < PER; ++p) {
-    int j = threadIdx.x + p * T;
-    if (j < nb) {
+    const int j = threadIdx.x + p * T;
+    if (NB % T == 0 || j < NB) {
+      if constexpr (LOAD_LIN) {
+        const float2* lb = buf + swz(j);
 #pragma unroll
-      for (int r = 0; r < R; ++r) v[p][r] = buf[pad(j + r * nb)];
-      int k = j & (Ns - 1);
-      if (Ns > 1) {
-        int step = N / (Ns * R);
+        for (int r = 0; r < R; ++r) v[p][r] = lb[r * (NB / 16 * 17)];
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) v[p][r] = buf[swz(j + r * NB)];
+      }
+      if (NS > 1) {
+        const int k = j & (NS - 1);
+        const float2* tb = tw + k;
 #pragma unroll
         for (int r = 1; r < R; ++r) {
-          float2 w = twiddle(tw, r * k * step);
+          float2 w = __ldg(tb + (r - 1) * NS);
           if (INV) w.y = -w.y;
           v[p][r] = cmul(v[p][r], w);
         }
@@ -147,32 +298,32 @@ __device__ __forceinline__ void stockham_pass(float2* buf, int N, int Ns, const 
   __syncthreads();
 #pragma unroll
   for (int p = 0; p < PER; ++p) {
-    int j = threadIdx.x + p * T;
-    if (j < nb) {
-      int k = j & (Ns - 1);
-      int d = (j - k) * R + k;
+    const int j = threadIdx.x + p * T;
+    if (NB % T == 0 || j < NB) {
+      const int k = j & (NS - 1);
+      const int d = (j - k) * R + k;
+      if constexpr (STORE_LIN) {
+        float2* sb = buf + swz(d);
 #pragma unroll
-      for (int r = 0; r < R; ++r) buf[pad(d + r * Ns)] = v[p][r];
+        for (int r = 0; r < R; ++r) sb[NS == 1 ? r + (r >> 4) : r * (NS / 16 * 17)] = v[p][r];
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) buf[swz(d + r * NS)] = v[p][r];
+      }
     }
   }
   __syncthreads();
 }
 
-template <int LOGN, int T, bool INV>
-__device__ __forceinline__ void fft_smem(float2* buf, const Twiddles& tw) {
-  constexpr int N = 1 << LOGN;
-  constexpr int FULL = LOGN / 4;
-  constexpr int REM = LOGN % 4;
-  constexpr int P16 = (N / 16 + T - 1) / T > 0 ? (N / 16 + T - 1) / T : 1;
-  int Ns = 1;
-#pragma unroll 1
-  for (int i = 0; i < FULL; ++i) {
-    stockham_pass<16, P16, T, INV>(buf, N, Ns, tw);
-    Ns *= 16;
+// All passes of an N-point transform: radix 16 while it fits, then one pass
+// of the remaining radix; the table pointer advances pass by pass.
+template <int N, int T, bool INV, int NS = 1>
+__device__ __forceinline__ void fft_passes(float2* buf, const float2* __restrict__ tw) {
+  if constexpr (NS < N) {
+    constexpr int R = pass_radix(N, NS);
+    fft_pass<N, R, NS, T, INV>(buf, tw);
+    fft_passes<N, T, INV, NS * R>(buf, tw + (R - 1) * NS);
   }
-  if constexpr (REM == 1) stockham_pass<2, (N / 2 + T - 1) / T, T, INV>(buf, N, Ns, tw);
-  if constexpr (REM == 2) stockham_pass<4, (N / 4 + T - 1) / T, T, INV>(buf, N, Ns, tw);
-  if constexpr (REM == 3) stockham_pass<8, (N / 8 + T - 1) / T, T, INV>(buf, N, Ns, tw);
 }
 
 // ------------------------------------------------------------ row kernels
@@ -206,72 +357,70 @@ constexpr int kModeConv = 2;
 template <int LOGN>
 struct RowCfg {
   static constexpr int N = 1 << LOGN;
-  static constexpr int T = N / 16 < 64 ? 64 : (N / 16 > 512 ? 512 : N / 16);
-  static constexpr int F = N < 128 ? N : 128;          // fine table size
-  static constexpr int FBITS = log2_c(F);
-  static constexpr int NC = N / F;                      // coarse table size
-  static constexpr int SMEM = (N + N / 32 + 1 + F + NC) * 8;
-  static constexpr int MINB = LOGN >= 14 ? 1 : 2;
+  // One radix-16 butterfly per thread (radix-32 passes leave half of them
+  // idle): holding two across a pass's barrier sends one to local memory.
+  static constexpr int TB = N / 16;
+  static constexpr int T = TB < 64 ? 64 : (TB > 512 ? 512 : TB);
+  static constexpr int SMEM = (N + N / 16 + 1) * 8;
+  static constexpr int MINB = T >= 512 ? 1 : 2;
 };
 
 // Unpacks Z (FFT of the packed real signal) into the real-FFT bins X[k] and
 // X[N-k] for k in [0, N/2] (thread-owned pairs).
-__device__ __forceinline__ void rfft_unpack_pair(float2 zk, float2 znk, int k, int N, float2& xk,
+// exp(-i pi k / N) computed directly (global-memory path, N beyond the tables).
+__device__ __forceinline__ float2 unpack_twiddle(int k, int N) {
+  float s, c;
+  sincospif(-(float)k / (float)N, &s, &c);
+  return make_float2(c, s);
+}
+
+// u = exp(-i pi k / N) from the table.
+__device__ __forceinline__ void rfft_unpack_pair(float2 zk, float2 znk, float2 u, float2& xk,
                                                  float2& xnk) {
   float2 bc = cconj(znk);
   float2 fe = cscale(cadd(zk, bc), 0.5f);
   float2 d = csub(zk, bc);
   float2 fo = make_float2(0.5f * d.y, -0.5f * d.x);  // (zk - bc) / (2i)
-  float s, c;
-  sincospif(-(float)k / (float)N, &s, &c);
-  float2 wf = cmul(make_float2(c, s), fo);
+  float2 wf = cmul(u, fo);
   xk = cadd(fe, wf);
   xnk = cconj(csub(fe, wf));
 }
 
 // Packs the Hermitian spectrum pair (Y[k], Y[N-k]) into Z'[k], Z'[N-k] of the
 // length-N complex signal whose inverse FFT interleaves the real output.
-__device__ __forceinline__ void irfft_pack_pair(float2 yk, float2 ynk, int k, int N, float2& zk,
+// u = exp(-i pi k / N) from the table (conj(u) is applied).
+__device__ __forceinline__ void irfft_pack_pair(float2 yk, float2 ynk, float2 u, float2& zk,
                                                 float2& znk) {
   float2 bc = cconj(ynk);
   float2 fe = cscale(cadd(yk, bc), 0.5f);
   float2 d = cscale(csub(yk, bc), 0.5f);
-  float s, c;
-  sincospif((float)k / (float)N, &s, &c);  // conj(w^k), w = e^{-i pi / N}
-  float2 fo = cmul(make_float2(c, s), d);
+  float2 fo = cmul(cconj(u), d);
   zk = make_float2(fe.x - fo.y, fe.y + fo.x);     // fe + i fo
   znk = make_float2(fe.x + fo.y, -fe.y + fo.x);   // conj(fe) + i conj(fo)
 }
 
+// One CTA per row.  The inverse transform is evaluated as
+// IFFT(z) = conj(FFT(conj(z))) / N: the packed spectrum is stored conjugated
+// and the output conjugated back, so a single (forward) instance of the
+// passes serves both directions (one copy of the unrolled code, which keeps
+// the conv kernel free of register spills).
 template <int LOGN, int MODE>
 __global__ void __launch_bounds__(RowCfg<LOGN>::T, RowCfg<LOGN>::MINB)
     fft_row_kernel(RowArgs a) {
   using C = RowCfg<LOGN>;
   constexpr int N = C::N;
   constexpr int T = C::T;
-  extern __shared__ float2 sm[];
-  float2* buf = sm;
-  float2* fine = sm + (N + N / 32 + 1);
-  float2* coarse = fine + C::F;
+  extern __shared__ float2 buf[];
+  const float2* tw = g_fft_tw + tw_offset(LOGN);
+  const float2* utw = tw + tw_passes_size(N);   // exp(-i pi k / N), k <= N/2
   const int tid = threadIdx.x;
 
   int d = blockIdx.x / a.rows_b;
   int b = blockIdx.x - d * a.rows_b;
   int64_t row = (int64_t)b * a.rows_d + d;
 
-  for (int i = tid; i < C::F; i += T) {
-    float s, c;
-    sincospif(-2.0f * (float)i / (float)N, &s, &c);
-    fine[i] = make_float2(c, s);
-  }
-  for (int i = tid; i < C::NC; i += T) {
-    float s, c;
-    sincospif(-2.0f * (float)(i * C::F) / (float)N, &s, &c);
-    coarse[i] = make_float2(c, s);
-  }
-  Twiddles tw{fine, coarse, C::FBITS};
-
   if (MODE != kModeIrfft) {
+    // z[m] = x[2m] + i x[2m+1], zero-padded / truncated to N
     const float* x = a.in + a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd;
     const int len = a.in_len;
     const bool vec = a.in_st == 1 && ((reinterpret_cast<uintptr_t>(x) & 7) == 0);
@@ -284,47 +433,10 @@ __global__ void __launch_bounds__(RowCfg<LOGN>::T, RowCfg<LOGN>::MINB)
       } else if (t0 < len) {
         z.x = x[(int64_t)t0 * a.in_st];
       }
-      buf[pad(m)] = z;
-    }
-    __syncthreads();
-    fft_smem<LOGN, T, false>(buf, tw);
-
-    if (MODE == kModeRfft) {
-      float2* X = a.spec_out + row * a.out_ld;
-      for (int k = tid; k <= N / 2; k += T) {
-        float2 zk = buf[pad(k)];
-        if (k == 0) {
-          X[0] = make_float2(zk.x + zk.y, 0.f);
-          X[N] = make_float2(zk.x - zk.y, 0.f);
-        } else {
-          float2 xk, xnk;
-          rfft_unpack_pair(zk, buf[pad(N - k)], k, N, xk, xnk);
-          X[k] = xk;
-          if (k != N - k) X[N - k] = xnk;
-        }
-      }
-      return;
-    }
-    // Fused convolution: Y = X * H, packed for the inverse transform.
-    const float2* H = a.H + (int64_t)d * a.h_ld;
-    for (int k = tid; k <= N / 2; k += T) {
-      float2 zk = buf[pad(k)];
-      if (k == 0) {
-        float y0 = (zk.x + zk.y) * H[0].x;   // bins 0 and N are real
-        float yn = (zk.x - zk.y) * H[N].x;
-        buf[pad(0)] = make_float2(0.5f * (y0 + yn), 0.5f * (y0 - yn));
-      } else {
-        float2 xk, xnk;
-        rfft_unpack_pair(zk, buf[pad(N - k)], k, N, xk, xnk);
-        float2 yk = cmul(xk, H[k]);
-        float2 ynk = cmul(xnk, H[N - k]);
-        float2 pk, pnk;
-        irfft_pack_pair(yk, ynk, k, N, pk, pnk);
-        buf[pad(k)] = pk;
-        if (k != N - k) buf[pad(N - k)] = pnk;
-      }
+      buf[swz(m)] = z;
     }
   } else {
+    // conj of the packed spectrum Z'[k] (bins beyond the input are zero)
     const float2* Y = a.spec_in + row * a.spec_ld;
     const int len = a.spec_len;
     for (int k = tid; k <= N / 2; k += T) {
@@ -332,18 +444,59 @@ __global__ void __launch_bounds__(RowCfg<LOGN>::T, RowCfg<LOGN>::MINB)
       float2 ynk = (N - k) < len ? Y[N - k] : make_float2(0.f, 0.f);
       if (k == 0) {
         float y0 = yk.x, yn = ynk.x;  // imaginary parts of bins 0 and N are ignored
-        buf[pad(0)] = make_float2(0.5f * (y0 + yn), 0.5f * (y0 - yn));
+        buf[swz(0)] = make_float2(0.5f * (y0 + yn), -0.5f * (y0 - yn));
       } else {
         float2 pk, pnk;
-        irfft_pack_pair(yk, ynk, k, N, pk, pnk);
-        buf[pad(k)] = pk;
-        if (k != N - k) buf[pad(N - k)] = pnk;
+        irfft_pack_pair(yk, ynk, __ldg(utw + k), pk, pnk);
+        buf[swz(k)] = cconj(pk);
+        if (k != N - k) buf[swz(N - k)] = cconj(pnk);
       }
     }
   }
   __syncthreads();
-  fft_smem<LOGN, T, true>(buf, tw);
 
+#pragma unroll 1
+  for (int phase = (MODE == kModeIrfft) ? 1 : 0; phase < 2; ++phase) {
+    fft_passes<N, T, false>(buf, tw);
+    if (phase == 1) break;
+    if (MODE == kModeRfft) {
+      float2* X = a.spec_out + row * a.out_ld;
+      for (int k = tid; k <= N / 2; k += T) {
+        float2 zk = buf[swz(k)];
+        if (k == 0) {
+          X[0] = make_float2(zk.x + zk.y, 0.f);
+          X[N] = make_float2(zk.x - zk.y, 0.f);
+        } else {
+          float2 xk, xnk;
+          rfft_unpack_pair(zk, buf[swz(N - k)], __ldg(utw + k), xk, xnk);
+          X[k] = xk;
+          if (k != N - k) X[N - k] = xnk;
+        }
+      }
+      return;
+    }
+    // Fused convolution: Y = X * H, packed (conjugated) for the inverse.
+    const float2* H = a.H + (int64_t)d * a.h_ld;
+    for (int k = tid; k <= N / 2; k += T) {
+      float2 zk = buf[swz(k)];
+      if (k == 0) {
+        float y0 = (zk.x + zk.y) * H[0].x;   // bins 0 and N are real
+        float yn = (zk.x - zk.y) * H[N].x;
+        buf[swz(0)] = make_float2(0.5f * (y0 + yn), -0.5f * (y0 - yn));
+      } else {
+        const float2 u = __ldg(utw + k);
+        float2 xk, xnk;
+        rfft_unpack_pair(zk, buf[swz(N - k)], u, xk, xnk);
+        float2 pk, pnk;
+        irfft_pack_pair(cmul(xk, H[k]), cmul(xnk, H[N - k]), u, pk, pnk);
+        buf[swz(k)] = cconj(pk);
+        if (k != N - k) buf[swz(N - k)] = cconj(pnk);
+      }
+    }
+    __syncthreads();
+  }
+
+  // y[2m] + i y[2m+1] = conj(FFT(conj Z'))[m] / N
   float* y = a.out + row * a.out_ld;
   const float scale = 1.0f / (float)N;
   const int olen = a.out_len;
@@ -351,7 +504,8 @@ __global__ void __launch_bounds__(RowCfg<LOGN>::T, RowCfg<LOGN>::MINB)
   for (int m = tid; m < N; m += T) {
     int t0 = 2 * m;
     if (t0 >= olen) break;
-    float2 z = cscale(buf[pad(m)], scale);
+    const float2 w = buf[swz(m)];
+    const float2 z = make_float2(w.x * scale, -w.y * scale);
     if (t0 + 1 < olen) {
       if (vec) *reinterpret_cast<float2*>(y + t0) = z;
       else { y[t0] = z.x; y[t0 + 1] = z.y; }
@@ -441,7 +595,7 @@ __global__ void unpack_global_kernel(float2* __restrict__ z, RowArgs a, int N, i
         X[N] = make_float2(zk.x - zk.y, 0.f);
       } else {
         float2 xk, xnk;
-        rfft_unpack_pair(zk, zr[N - k], k, N, xk, xnk);
+        rfft_unpack_pair(zk, zr[N - k], unpack_twiddle(k, N), xk, xnk);
         X[k] = xk;
         if (k != N - k) X[N - k] = xnk;
       }
@@ -452,8 +606,8 @@ __global__ void unpack_global_kernel(float2* __restrict__ z, RowArgs a, int N, i
         zr[0] = make_float2(0.5f * (y0 + yn), 0.5f * (y0 - yn));
       } else {
         float2 xk, xnk, pk, pnk;
-        rfft_unpack_pair(zk, zr[N - k], k, N, xk, xnk);
-        irfft_pack_pair(cmul(xk, H[k]), cmul(xnk, H[N - k]), k, N, pk, pnk);
+        rfft_unpack_pair(zk, zr[N - k], unpack_twiddle(k, N), xk, xnk);
+        irfft_pack_pair(cmul(xk, H[k]), cmul(xnk, H[N - k]), unpack_twiddle(k, N), pk, pnk);
         zr[k] = pk;
         if (k != N - k) zr[N - k] = pnk;
       }
@@ -477,7 +631,7 @@ __global__ void pack_spectrum_global_kernel(float2* __restrict__ z, RowArgs a, i
       zr[0] = make_float2(0.5f * (yk.x + ynk.x), 0.5f * (yk.x - ynk.x));
     } else {
       float2 pk, pnk;
-      irfft_pack_pair(yk, ynk, k, N, pk, pnk);
+      irfft_pack_pair(yk, ynk, unpack_twiddle(k, N), pk, pnk);
       zr[k] = pk;
       if (k != N - k) zr[N - k] = pnk;
     }
@@ -546,8 +700,6 @@ int ilog2_exact(int64_t n) {
   return l;
 }
 
-constexpr int kMaxSmemLogN = 14;  // N = 16384 complex values per CTA
-
 // Runs `mode` over all rows, choosing the shared-memory or global path.
 int run_rows(int mode, int64_t n, RowArgs a, int64_t rows, const float2* Hspec) {
   if (rows == 0) return WXX_OK;
@@ -606,6 +758,15 @@ int run_rows(int mode, int64_t n, RowArgs a, int64_t rows, const float2* Hspec) 
 }
 
 }  // namespace
+
+namespace wxx {
+// Fills the FFT twiddle tables of every shared-memory size (called by wxx_init).
+int fft_init_tables() {
+  fft_twiddle_init_kernel<<<64, 256, 0, wxx::stream()>>>();
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+}  // namespace wxx
 
 // X[r, k] (c64, row stride out_ld complex) = rfft(x[r, :in_len], n), k <= n/2.
 // x rows are dense with row stride in_ld floats.

@@ -177,6 +177,10 @@ WXX_EXPORT int wxx_init(int device) {
   WXX_CUDA_CHECK(cudaMemset(g.err_word, 0, 256));
   g.device = device;
   g.ready = true;
+  // Constant tables of the kernels, filled once here (never inside a capture).
+  int st = wxx::fft_init_tables();
+  if (st != WXX_OK) return st;
+  WXX_CUDA_CHECK(cudaStreamSynchronize(g.stream));
   return WXX_OK;
 }
 
