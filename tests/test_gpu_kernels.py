@@ -128,6 +128,20 @@ def test_causal_conv1d_dense_and_transposed(rng):
                                rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("B,L,D,K_", [(2, 1000, 70, 3), (3, 300, 33, 8), (1, 129, 40, 9),
+                                      (2, 8192, 64, 3)])
+def test_causal_conv1d_transposed_tiles(B, L, D, K_, rng):
+    """Transposed (B, L, D) views: 32 x 128 tiles with ragged edges, K up to
+    8 in registers, K = 9 on the generic kernel."""
+    F = _w().functional
+    xt = rng.standard_normal((B, L, D)).astype(np.float32)
+    w = rng.standard_normal((D, K_)).astype(np.float32)
+    b = rng.standard_normal(D).astype(np.float32)
+    got = F.causal_conv1d(up(xt).permute(0, 2, 1), up(w), up(b)).numpy()
+    np.testing.assert_allclose(got, K.causal_conv1d(np.transpose(xt, (0, 2, 1)), w, b),
+                               rtol=1e-5, atol=1e-5)
+
+
 def test_decay_window(rng):
     F = _w().functional
     d = rng.random((4, 33)).astype(np.float32)

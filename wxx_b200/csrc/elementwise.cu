@@ -361,34 +361,50 @@ __global__ void causal_conv1d_kernel(float* __restrict__ out, const float* __res
 }
 
 // Transposed-input variant: x element (b, d, n) lives at x_off + b*sb + n*sl + d
-// (sc == 1).  A CTA handles a 32(d) x 32(n) tile, reading rows of x coalesced
-// along d and writing out coalesced along n.
-__global__ void causal_conv1d_tr_kernel(float* __restrict__ out, const float* __restrict__ x,
-                                        int64_t x_off, int64_t sb, int64_t sl,
-                                        const float* __restrict__ w,
-                                        const float* __restrict__ bias, int B, int D, int L,
-                                        int K) {
-  extern __shared__ float tile[];  // (32 + K - 1) x 33
-  int b = blockIdx.z;
-  int d0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-  int rows = 32 + K - 1;
+// (sc == 1).  A CTA handles a 32(d) x 128(n) tile: the (128 + K - 1) x 32
+// input rows are read coalesced along d into shared memory (row stride 33),
+// each thread then produces 16 outputs (4 channels x 4 positions 32 apart)
+// written coalesced along n, with its channels' taps in registers.
+constexpr int kConvTileN = 128;
+constexpr int kConvMaxK = 8;
+
+__global__ void __launch_bounds__(256) causal_conv1d_tr_kernel(
+    float* __restrict__ out, const float* __restrict__ x, int64_t x_off, int64_t sb, int64_t sl,
+    const float* __restrict__ w, const float* __restrict__ bias, int B, int D, int L, int K) {
+  extern __shared__ float tile[];  // (kConvTileN + K - 1) x 33
+  const int b = blockIdx.z;
+  const int d0 = blockIdx.y * 32, n0 = blockIdx.x * kConvTileN;
+  const int rows = kConvTileN + K - 1;
   const float* xb = x + x_off + (int64_t)b * sb;
+  const int d = d0 + threadIdx.x;
   for (int r = threadIdx.y; r < rows; r += blockDim.y) {
-    int n = n0 - (K - 1) + r;
-    int d = d0 + threadIdx.x;
+    const int n = n0 - (K - 1) + r;
     float v = 0.f;
     if (n >= 0 && n < L && d < D) v = xb[(int64_t)n * sl + d];
     tile[r * 33 + threadIdx.x] = v;
   }
   __syncthreads();
-  for (int dd = threadIdx.y; dd < 32; dd += blockDim.y) {
-    int d = d0 + dd, n = n0 + threadIdx.x;
-    if (d >= D || n >= L) continue;
-    float acc = bias[d];
-    for (int k = 0; k < K; ++k) {
-      if (n >= k) acc = acc + w[d * K + k] * tile[(threadIdx.x + K - 1 - k) * 33 + dd];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int dd = threadIdx.y + 8 * c;
+    const int dc = d0 + dd;
+    if (dc >= D) continue;
+    float wk[kConvMaxK];
+#pragma unroll
+    for (int k = 0; k < kConvMaxK; ++k) wk[k] = k < K ? w[dc * K + k] : 0.f;
+    const float bv = bias[dc];
+    float* orow = out + ((int64_t)b * D + dc) * L;
+#pragma unroll
+    for (int q = 0; q < kConvTileN / 32; ++q) {
+      const int i = threadIdx.x + 32 * q;   // position inside the tile
+      const int n = n0 + i;
+      if (n >= L) continue;
+      float acc = bv;
+#pragma unroll
+      for (int k = 0; k < kConvMaxK; ++k)
+        if (k < K && n >= k) acc = acc + wk[k] * tile[(i + K - 1 - k) * 33 + dd];
+      orow[n] = acc;
     }
-    out[((int64_t)b * D + d) * L + n] = acc;
   }
 }
 
@@ -673,9 +689,9 @@ WXX_EXPORT int wxx_causal_conv1d(float* out, const float* x, int64_t x_off, int6
   WXX_REQUIRE(B >= 0 && D >= 0 && L >= 0 && K >= 1, "wxx_causal_conv1d: bad sizes");
   if ((int64_t)B * D * L == 0) return WXX_OK;
   cudaStream_t s = wxx::stream();
-  if (sc == 1 && K <= 64 && B <= 65535) {
-    dim3 grid((L + 31) / 32, (D + 31) / 32, B);
-    size_t smem = (size_t)(32 + K - 1) * 33 * sizeof(float);
+  if (sc == 1 && K <= kConvMaxK && B <= 65535) {
+    dim3 grid((L + kConvTileN - 1) / kConvTileN, (D + 31) / 32, B);
+    size_t smem = (size_t)(kConvTileN + K - 1) * 33 * sizeof(float);
     causal_conv1d_tr_kernel<<<grid, dim3(32, 8), smem, s>>>(out, x, x_off, sb, sl, w, bias, B, D, L,
                                                             K);
   } else {
