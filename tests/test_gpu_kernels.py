@@ -403,8 +403,9 @@ def test_pooling(rng):
 
 # ------------------------------------------------------------ FFT
 
-@pytest.mark.parametrize("rows,L,n", [(3, 5, 8), (4, 16, 16), (2, 100, 256), (5, 1000, 1024),
-                                      (3, 3000, 4096), (2, 8192, 16384), (2, 16384, 32768),
+@pytest.mark.parametrize("rows,L,n", [(3, 5, 8), (4, 16, 16), (2, 100, 256), (3, 512, 512),
+                                      (5, 1000, 1024), (2, 2047, 2048), (3, 3000, 4096),
+                                      (2, 8192, 8192), (2, 8192, 16384), (2, 16384, 32768),
                                       (2, 20, 2), (3, 1, 1), (2, 40000, 65536)])
 def test_rfft_irfft(rows, L, n, rng):
     F = _w().functional
@@ -434,7 +435,8 @@ def test_complex_mul_broadcast(rng):
     assert rel(got, K.complex_mul(a, b, conj_b=True)) < 1e-6
 
 
-@pytest.mark.parametrize("B,D,L", [(2, 3, 64), (3, 4, 1000), (2, 8, 8192), (1, 4, 16384),
+@pytest.mark.parametrize("B,D,L", [(2, 3, 64), (2, 3, 200), (3, 2, 300), (3, 4, 1000),
+                                   (2, 3, 1500), (2, 2, 3000), (2, 8, 8192), (1, 4, 16384),
                                    (1, 2, 40000)])
 def test_fftconv_matches_reference_chain(B, D, L, rng):
     F = _w().functional
@@ -447,6 +449,22 @@ def test_fftconv_matches_reference_chain(B, D, L, rng):
     # the unfused reference chain through the public ops gives the same result
     chain = F.irfft(F.complex_mul(F.rfft(up(x), n)[0], F.rfft(up(h), n)[0]), n)
     assert rel(chain.numpy()[..., :L], ref) < 2e-5
+
+
+@pytest.mark.parametrize("L", [300, 8192])
+def test_fftconv_strided_and_unaligned_input(L, rng):
+    """x as a (B, L, D) -> (B, D, L) transposed view and as a view starting
+    one element into its rows (neither takes the 16-byte vector loads)."""
+    F = _w().functional
+    B, D = 2, 3
+    n = 1 << (2 * L - 1).bit_length()
+    h = rng.standard_normal((D, L)).astype(np.float32)
+    xt = rng.standard_normal((B, L, D)).astype(np.float32)
+    got = F.fftconv(up(xt).permute(0, 2, 1), up(h), n, out_len=L).numpy()
+    assert rel(got, K.fftconv(np.ascontiguousarray(xt.transpose(0, 2, 1)), h, n, L)) < 2e-5
+    xw = rng.standard_normal((B, D, L + 1)).astype(np.float32)
+    got = F.fftconv(up(xw)[:, :, 1:], up(h), n, out_len=L - 5).numpy()
+    assert rel(got, K.fftconv(np.ascontiguousarray(xw[:, :, 1:]), h, n, L - 5)) < 2e-5
 
 
 # ------------------------------------------------------------ fused attention

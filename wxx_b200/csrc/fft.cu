@@ -655,18 +655,580 @@ __global__ void unpack_real_global_kernel(const float2* __restrict__ z, RowArgs 
   }
 }
 
+// ------------------------------------------------------------ planar pair kernels (N >= 256)
+//
+// The production path for N = 256 .. 16384 complex values per row.  Every
+// thread carries two butterflies, one per lane of Blackwell's paired FP32
+// instructions (add/sub/mul/fma .f32x2): a CP holds the real parts of two
+// complex values in one 64-bit register pair and their imaginary parts in
+// another, so one paired instruction does the arithmetic of both butterflies.
+// The row sits in shared memory as two planar float arrays (re, im), padded
+// by two floats every 32 (pad2), so the two lanes of a pair are adjacent and
+// 8-byte aligned and every pass moves them with 64-bit accesses.
+//
+// Per fused convolution the shared-memory traffic is cut three ways:
+//  * the first forward pass reads x straight from global memory;
+//  * the last forward pass, the spectrum product and the first inverse pass
+//    run in registers: that pass pairs butterfly j with its mirror N/R - j,
+//    whose outputs are exactly the bins N - k the real-FFT unpack needs, and
+//    the first inverse pass (stride N/R, like the last forward pass) reads
+//    the same elements the thread already holds;
+//  * the last inverse pass writes y straight to global memory.
+// A micro-benchmark of one 8192-point radix-16 pass: 2.65 us per SM with the
+// float2 butterflies (~900 issued instructions per butterfly, mostly integer
+// moves), 0.65 us with the paired form (~125), which is ~80 % of the
+// shared-memory bandwidth.
+
+typedef unsigned long long u64;
+
+__device__ __forceinline__ u64 p_add(u64 a, u64 b) {
+  u64 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 p_sub(u64 a, u64 b) {
+  u64 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 p_mul(u64 a, u64 b) {
+  u64 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 p_fma(u64 a, u64 b, u64 c) {
+  u64 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ u64 p_make(float lo, float hi) {
+  return ((u64)__float_as_uint(hi) << 32) | (u64)__float_as_uint(lo);
+}
+__device__ __forceinline__ float p_lo(u64 a) { return __uint_as_float((unsigned)a); }
+__device__ __forceinline__ float p_hi(u64 a) { return __uint_as_float((unsigned)(a >> 32)); }
+
+struct CP {
+  u64 re, im;
+};
+
+__device__ __forceinline__ float2 cp_get(const CP& v, int lane) {
+  return lane == 0 ? make_float2(p_lo(v.re), p_lo(v.im)) : make_float2(p_hi(v.re), p_hi(v.im));
+}
+__device__ __forceinline__ void cp_set(CP& v, int lane, float2 z) {
+  if (lane == 0) {
+    v.re = p_make(z.x, p_hi(v.re));
+    v.im = p_make(z.y, p_hi(v.im));
+  } else {
+    v.re = p_make(p_lo(v.re), z.x);
+    v.im = p_make(p_lo(v.im), z.y);
+  }
+}
+
+// v <- v * exp(-i theta) for lane-wise (cos theta, sin theta) = (c, s).
+__device__ __forceinline__ void p_twiddle(CP& v, u64 c, u64 s) {
+  const u64 re = p_fma(v.re, c, p_mul(v.im, s));
+  v.im = p_sub(p_mul(v.im, c), p_mul(v.re, s));
+  v.re = re;
+}
+
+// a, b <- a + w b, a - w b with w = exp(-2 pi i Q / R), R <= 32.
+template <int R, int Q>
+__device__ __forceinline__ void p_bfly(CP& a, CP& b) {
+  constexpr int q32 = Q * (32 / R);
+  CP s, d;
+  if constexpr (q32 == 0) {
+    s = CP{p_add(a.re, b.re), p_add(a.im, b.im)};
+    d = CP{p_sub(a.re, b.re), p_sub(a.im, b.im)};
+  } else if constexpr (q32 == 8) {  // w = -i: w b = (b.im, -b.re)
+    s = CP{p_add(a.re, b.im), p_sub(a.im, b.re)};
+    d = CP{p_sub(a.re, b.im), p_add(a.im, b.re)};
+  } else {
+    // w b = (re c + im s) + i (im c - re s), (c, s) = (cos, sin)(2 pi Q / R)
+    constexpr float c = cos32(q32), sn = sin32(q32);
+    const u64 C = p_make(c, c), S = p_make(sn, sn), NS = p_make(-sn, -sn);
+    const u64 wr = p_fma(b.re, C, p_mul(b.im, S));
+    const u64 wi = p_fma(b.im, C, p_mul(b.re, NS));
+    s = CP{p_add(a.re, wr), p_add(a.im, wi)};
+    d = CP{p_sub(a.re, wr), p_sub(a.im, wi)};
+  }
+  a = s;
+  b = d;
+}
+
+template <int R, int M, int K, int J>
+__device__ __forceinline__ void p_stage(CP (&t)[R]) {
+  if constexpr (K < R) {
+    if constexpr (J < M / 2) {
+      p_bfly<R, J * (R / M)>(t[K + J], t[K + J + M / 2]);
+      p_stage<R, M, K, J + 1>(t);
+    } else {
+      p_stage<R, M, K + M, 0>(t);
+    }
+  }
+}
+
+template <int R, int M = 2>
+__device__ __forceinline__ void p_stages(CP (&t)[R]) {
+  if constexpr (M <= R) {
+    p_stage<R, M, 0, 0>(t);
+    p_stages<R, M * 2>(t);
+  }
+}
+
+// Radix-R forward DFT of both lanes, natural order in and out.
+template <int R>
+__device__ __forceinline__ void p_dft(CP (&v)[R]) {
+  CP t[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) t[bitrev_c(i, log2_c(R))] = v[i];
+  p_stages<R>(t);
+#pragma unroll
+  for (int i = 0; i < R; ++i) v[i] = t[i];
+}
+
+__device__ __forceinline__ int pad2(int i) { return i + ((i >> 5) << 1); }
+__host__ __device__ constexpr int padded2(int n) { return n + n / 16; }
+__device__ __forceinline__ u64 lds2(const float* p) { return *reinterpret_cast<const u64*>(p); }
+__device__ __forceinline__ void sts2(float* p, u64 v) { *reinterpret_cast<u64*>(p) = v; }
+__device__ __forceinline__ u64 ldg2(const float* p) { return __ldg(reinterpret_cast<const u64*>(p)); }
+
+// Pass plan for N = 2^L (L = 8..14): forward radices first to last; the
+// inverse runs them in reverse order.  Radix 32 appears only where a thread
+// block of N/32 threads has the registers for it (L = 13: 256 threads).
+__host__ __device__ constexpr int pp_count(int L) { return L <= 8 ? 2 : (L == 14 ? 4 : 3); }
+__host__ __device__ constexpr int pp_radix(int L, int p) {
+  return L == 8    ? 16
+         : L == 9  ? 8
+         : L == 10 ? (p == 1 ? 4 : 16)
+         : L == 11 ? (p == 1 ? 8 : 16)
+         : L == 12 ? 16
+         : L == 13 ? (p == 1 ? 32 : 16)
+                   : (p == 2 ? 4 : 16);
+}
+// Sub-transform size before forward pass p / inverse pass q.
+__host__ __device__ constexpr int pp_ns_fwd(int L, int p) {
+  int ns = 1;
+  for (int i = 0; i < p; ++i) ns *= pp_radix(L, i);
+  return ns;
+}
+__host__ __device__ constexpr int pp_radix_inv(int L, int q) { return pp_radix(L, pp_count(L) - 1 - q); }
+__host__ __device__ constexpr int pp_ns_inv(int L, int q) {
+  int ns = 1;
+  for (int i = 0; i < q; ++i) ns *= pp_radix_inv(L, i);
+  return ns;
+}
+
+// Twiddle tables (floats): for each L = 8..14, the forward passes p = 1..P-1
+// then the inverse passes q = 1..P-1, each a segment of (R-1)*NS cosines
+// followed by (R-1)*NS sines of 2 pi r k / (R NS), entry (r-1)*NS + k.
+constexpr int kPairMinL = 8;
+__host__ __device__ constexpr int pt_seg(int R, int NS) { return 2 * (R - 1) * NS; }
+__host__ __device__ constexpr int pt_size(int L) {
+  int s = 0;
+  for (int p = 1; p < pp_count(L); ++p) s += pt_seg(pp_radix(L, p), pp_ns_fwd(L, p));
+  for (int q = 1; q < pp_count(L); ++q) s += pt_seg(pp_radix_inv(L, q), pp_ns_inv(L, q));
+  return s;
+}
+__host__ __device__ constexpr int pt_base(int L) {
+  int o = 0;
+  for (int l = kPairMinL; l < L; ++l) o += pt_size(l);
+  return o;
+}
+__host__ __device__ constexpr int pt_fwd_off(int L, int p) {
+  int o = pt_base(L);
+  for (int i = 1; i < p; ++i) o += pt_seg(pp_radix(L, i), pp_ns_fwd(L, i));
+  return o;
+}
+__host__ __device__ constexpr int pt_inv_off(int L, int q) {
+  int o = pt_fwd_off(L, pp_count(L));
+  for (int i = 1; i < q; ++i) o += pt_seg(pp_radix_inv(L, i), pp_ns_inv(L, i));
+  return o;
+}
+constexpr int kPtTotal = pt_base(kMaxSmemLogN + 1);
+static __device__ __align__(16) float g_fft_ptw[kPtTotal];
+
+__global__ void fft_pair_twiddle_init_kernel() {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < kPtTotal; e += gridDim.x * blockDim.x) {
+    int L = kPairMinL;
+    while (L < kMaxSmemLogN && e >= pt_base(L + 1)) ++L;
+    int local = e - pt_base(L);
+    const int P = pp_count(L);
+    for (int s = 0; s < 2 * (P - 1); ++s) {
+      const bool inv = s >= P - 1;
+      const int idx = inv ? s - (P - 1) + 1 : s + 1;
+      const int R = inv ? pp_radix_inv(L, idx) : pp_radix(L, idx);
+      const int NS = inv ? pp_ns_inv(L, idx) : pp_ns_fwd(L, idx);
+      const int seg = pt_seg(R, NS);
+      if (local < seg) {
+        const int half = (R - 1) * NS;
+        const bool is_sin = local >= half;
+        const int i = is_sin ? local - half : local;
+        const int rr = i / NS + 1, k = i % NS;
+        double sn, cs;
+        sincospi(2.0 * (double)rr * (double)k / ((double)R * (double)NS), &sn, &cs);
+        g_fft_ptw[e] = (float)(is_sin ? sn : cs);
+        break;
+      }
+      local -= seg;
+    }
+  }
+}
+
+template <int L>
+struct PCfg {
+  static constexpr int N = 1 << L;
+  static constexpr int P = pp_count(L);
+  static constexpr int T = N / 32 < 32 ? 32 : N / 32;
+  static constexpr int SMEM = 2 * padded2(N) * 4;
+};
+
+// Forward pass 0 (NS = 1) from the real input row: z[m] = x[2m] + i x[2m+1].
+// Output r of butterfly j goes to j R + r; the two lanes' outputs r, r+1 are
+// regrouped into one 64-bit store per lane.
+template <int N, int R, int T>
+__device__ __forceinline__ void pp_first(float* sre, float* sim, const float* x, int64_t st,
+                                         int len, bool vec) {
+  constexpr int NB = N / R, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int q = threadIdx.x + p * T;
+    if (PAIRS % T == 0 || q < PAIRS) {
+      const int j = 2 * q;
+      CP v[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int t0 = 2 * (j + r * NB);
+        float4 xv;
+        if (vec && t0 + 3 < len) {
+          xv = *reinterpret_cast<const float4*>(x + t0);
+        } else {
+          xv.x = t0 < len ? x[(int64_t)t0 * st] : 0.f;
+          xv.y = t0 + 1 < len ? x[(int64_t)(t0 + 1) * st] : 0.f;
+          xv.z = t0 + 2 < len ? x[(int64_t)(t0 + 2) * st] : 0.f;
+          xv.w = t0 + 3 < len ? x[(int64_t)(t0 + 3) * st] : 0.f;
+        }
+        v[r].re = p_make(xv.x, xv.z);
+        v[r].im = p_make(xv.y, xv.w);
+      }
+      p_dft<R>(v);
+#pragma unroll
+      for (int r = 0; r < R; r += 2) {
+        sts2(sre + pad2(j * R + r), p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
+        sts2(sim + pad2(j * R + r), p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
+        sts2(sre + pad2((j + 1) * R + r), p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
+        sts2(sim + pad2((j + 1) * R + r), p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// One in-place Stockham pass (NS >= 2) over shared memory, lanes = butterflies
+// j, j+1 (j even, so both share the block j - j mod NS and twiddle k, k+1).
+template <int N, int R, int NS, int T>
+__device__ __forceinline__ void pp_pass(float* sre, float* sim, const float* __restrict__ tw) {
+  constexpr int NB = N / R, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
+  CP v[PER][R];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int q = threadIdx.x + p * T;
+    if (PAIRS % T == 0 || q < PAIRS) {
+      const int j = 2 * q;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        v[p][r].re = lds2(sre + pad2(j + r * NB));
+        v[p][r].im = lds2(sim + pad2(j + r * NB));
+      }
+      const int k = j & (NS - 1);
+#pragma unroll
+      for (int r = 1; r < R; ++r)
+        p_twiddle(v[p][r], ldg2(tw + (r - 1) * NS + k), ldg2(tw + (R - 1 + r - 1) * NS + k));
+      p_dft<R>(v[p]);
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int q = threadIdx.x + p * T;
+    if (PAIRS % T == 0 || q < PAIRS) {
+      const int j = 2 * q;
+      const int k = j & (NS - 1);
+      const int d = (j - k) * R + k;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        sts2(sre + pad2(d + r * NS), v[p][r].re);
+        sts2(sim + pad2(d + r * NS), v[p][r].im);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// The mirror step on one bin pair (k, N-k), k in [1, N/2]: z = (Z[k], Z[N-k])
+// of the packed forward transform in, conj of the packed inverse input out
+// (conv), the two spectrum bins written out (rfft), or the packed inverse
+// input made from the spectrum (irfft, z unused).
+template <int MODE>
+__device__ __forceinline__ void pp_bin_pair(int k, int N, float2 zk, float2 znk, float2& ok,
+                                            float2& onk, const float2* __restrict__ utw,
+                                            const RowArgs& a, int64_t row, int d) {
+  const float2 u = __ldg(utw + k);
+  if (MODE == kModeRfft) {
+    float2 xk, xnk;
+    rfft_unpack_pair(zk, znk, u, xk, xnk);
+    float2* X = a.spec_out + row * a.out_ld;
+    X[k] = xk;
+    if (k != N - k) X[N - k] = xnk;
+    return;
+  }
+  float2 yk, ynk;
+  if (MODE == kModeConv) {
+    float2 xk, xnk;
+    rfft_unpack_pair(zk, znk, u, xk, xnk);
+    const float2* H = a.H + (int64_t)d * a.h_ld;
+    yk = cmul(xk, __ldg(H + k));
+    ynk = cmul(xnk, __ldg(H + N - k));
+  } else {
+    const float2* Y = a.spec_in + row * a.spec_ld;
+    yk = k < a.spec_len ? Y[k] : make_float2(0.f, 0.f);
+    ynk = (N - k) < a.spec_len ? Y[N - k] : make_float2(0.f, 0.f);
+  }
+  float2 pk, pnk;
+  irfft_pack_pair(yk, ynk, u, pk, pnk);
+  ok = cconj(pk);
+  onk = cconj(pnk);
+}
+
+// Bins 0 and N (both real) -> conj of the packed inverse input Z'[0].
+template <int MODE>
+__device__ __forceinline__ float2 pp_bin_dc(int N, float2 z0, const RowArgs& a, int64_t row, int d) {
+  if (MODE == kModeRfft) {
+    float2* X = a.spec_out + row * a.out_ld;
+    X[0] = make_float2(z0.x + z0.y, 0.f);
+    X[N] = make_float2(z0.x - z0.y, 0.f);
+    return z0;
+  }
+  float y0, yn;
+  if (MODE == kModeConv) {
+    const float2* H = a.H + (int64_t)d * a.h_ld;
+    y0 = (z0.x + z0.y) * __ldg(&H[0].x);
+    yn = (z0.x - z0.y) * __ldg(&H[N].x);
+  } else {
+    const float2* Y = a.spec_in + row * a.spec_ld;
+    y0 = 0 < a.spec_len ? Y[0].x : 0.f;
+    yn = N < a.spec_len ? Y[N].x : 0.f;
+  }
+  return make_float2(0.5f * (y0 + yn), -0.5f * (y0 - yn));
+}
+
+// Last forward pass (radix R, NS = N/R) + the bin-pair step + first inverse
+// pass (radix R, NS = 1), in registers.  Lanes: butterflies j and N/R - j
+// (thread 0: 0 and N/(2R), each its own mirror).  Output r of butterfly j
+// holds Z[j + r N/R], whose mirror N - k is output R-1-r of butterfly N/R - j.
+template <int N, int R, int T, int MODE>
+__device__ __forceinline__ void pp_mirror(float* sre, float* sim, const float* __restrict__ tw,
+                                          const float2* __restrict__ utw, const RowArgs& a,
+                                          int64_t row, int d) {
+  constexpr int NB = N / R, NS = NB, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
+  CP v[PER][R];
+  int jj0[PER], jj1[PER];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int q = threadIdx.x + p * T;
+    const int j0 = q, j1 = q == 0 ? NB / 2 : NB - q;
+    jj0[p] = j0;
+    jj1[p] = j1;
+    if (PAIRS % T == 0 || q < PAIRS) {
+      if (MODE != kModeIrfft) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          v[p][r].re = p_make(sre[pad2(j0 + r * NB)], sre[pad2(j1 + r * NB)]);
+          v[p][r].im = p_make(sim[pad2(j0 + r * NB)], sim[pad2(j1 + r * NB)]);
+        }
+#pragma unroll
+        for (int r = 1; r < R; ++r) {
+          const float* tc = tw + (r - 1) * NS;
+          const float* ts = tw + (R - 1 + r - 1) * NS;
+          p_twiddle(v[p][r], p_make(__ldg(tc + j0), __ldg(tc + j1)),
+                    p_make(__ldg(ts + j0), __ldg(ts + j1)));
+        }
+        p_dft<R>(v[p]);
+      }
+      if (q != 0) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          // pair (lane 0 output r, lane 1 output R-1-r); the smaller bin leads
+          const bool lo_first = r < R / 2;
+          const int k = lo_first ? j0 + r * NB : j1 + (R - 1 - r) * NB;
+          float2 z0 = cp_get(v[p][r], 0), z1 = cp_get(v[p][R - 1 - r], 1);
+          float2 ok, onk;
+          pp_bin_pair<MODE>(k, N, lo_first ? z0 : z1, lo_first ? z1 : z0, ok, onk, utw, a, row, d);
+          if (MODE != kModeRfft) {
+            cp_set(v[p][r], 0, lo_first ? ok : onk);
+            cp_set(v[p][R - 1 - r], 1, lo_first ? onk : ok);
+          }
+        }
+      } else {
+        // lane 0 = butterfly 0: bins r NB; pairs (r, R-r), r = R/2 its own
+        {
+          const float2 o = pp_bin_dc<MODE>(N, cp_get(v[p][0], 0), a, row, d);
+          if (MODE != kModeRfft) cp_set(v[p][0], 0, o);
+        }
+#pragma unroll
+        for (int r = 1; r <= R / 2; ++r) {
+          float2 ok, onk;
+          pp_bin_pair<MODE>(r * NB, N, cp_get(v[p][r], 0), cp_get(v[p][R - r], 0), ok, onk, utw,
+                            a, row, d);
+          if (MODE != kModeRfft) {
+            if (r != R / 2) cp_set(v[p][R - r], 0, onk);
+            cp_set(v[p][r], 0, ok);
+          }
+        }
+        // lane 1 = butterfly NB/2: bins NB/2 + r NB; pairs (r, R-1-r)
+#pragma unroll
+        for (int r = 0; r < R / 2; ++r) {
+          float2 ok, onk;
+          pp_bin_pair<MODE>(NB / 2 + r * NB, N, cp_get(v[p][r], 1), cp_get(v[p][R - 1 - r], 1),
+                            ok, onk, utw, a, row, d);
+          if (MODE != kModeRfft) {
+            cp_set(v[p][r], 1, ok);
+            cp_set(v[p][R - 1 - r], 1, onk);
+          }
+        }
+      }
+      if (MODE != kModeRfft) p_dft<R>(v[p]);
+    }
+  }
+  if (MODE == kModeRfft) return;
+  __syncthreads();
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int q = threadIdx.x + p * T;
+    if (PAIRS % T == 0 || q < PAIRS) {
+      const int j0 = jj0[p], j1 = jj1[p];
+#pragma unroll
+      for (int r = 0; r < R; r += 2) {
+        sts2(sre + pad2(j0 * R + r), p_make(p_lo(v[p][r].re), p_lo(v[p][r + 1].re)));
+        sts2(sim + pad2(j0 * R + r), p_make(p_lo(v[p][r].im), p_lo(v[p][r + 1].im)));
+        sts2(sre + pad2(j1 * R + r), p_make(p_hi(v[p][r].re), p_hi(v[p][r + 1].re)));
+        sts2(sim + pad2(j1 * R + r), p_make(p_hi(v[p][r].im), p_hi(v[p][r + 1].im)));
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Last inverse pass (radix R, NS = N/R) to the real output row:
+// y[2m] + i y[2m+1] = conj(W[m]) / N.
+template <int N, int R, int T>
+__device__ __forceinline__ void pp_last(const float* sre, const float* sim,
+                                        const float* __restrict__ tw, float* y, int olen,
+                                        bool vec) {
+  constexpr int NB = N / R, NS = NB, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
+  const float scale = 1.0f / (float)N;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    const int q = threadIdx.x + p * T;
+    if (PAIRS % T == 0 || q < PAIRS) {
+      const int j = 2 * q;
+      CP v[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        v[r].re = lds2(sre + pad2(j + r * NB));
+        v[r].im = lds2(sim + pad2(j + r * NB));
+      }
+#pragma unroll
+      for (int r = 1; r < R; ++r)
+        p_twiddle(v[r], ldg2(tw + (r - 1) * NS + j), ldg2(tw + (R - 1 + r - 1) * NS + j));
+      p_dft<R>(v);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int t0 = 2 * (j + r * NS);
+        if (t0 >= olen) break;
+        const float4 o = make_float4(p_lo(v[r].re) * scale, -p_lo(v[r].im) * scale,
+                                     p_hi(v[r].re) * scale, -p_hi(v[r].im) * scale);
+        if (vec && t0 + 3 < olen) {
+          *reinterpret_cast<float4*>(y + t0) = o;
+        } else {
+          y[t0] = o.x;
+          if (t0 + 1 < olen) y[t0 + 1] = o.y;
+          if (t0 + 2 < olen) y[t0 + 2] = o.z;
+          if (t0 + 3 < olen) y[t0 + 3] = o.w;
+        }
+      }
+    }
+  }
+}
+
+template <int L, int T, int p>
+__device__ __forceinline__ void pp_fwd_middle(float* sre, float* sim) {
+  if constexpr (p <= pp_count(L) - 2) {
+    pp_pass<(1 << L), pp_radix(L, p), pp_ns_fwd(L, p), T>(sre, sim, g_fft_ptw + pt_fwd_off(L, p));
+    pp_fwd_middle<L, T, p + 1>(sre, sim);
+  }
+}
+
+template <int L, int T, int q>
+__device__ __forceinline__ void pp_inv_middle(float* sre, float* sim) {
+  if constexpr (q <= pp_count(L) - 2) {
+    pp_pass<(1 << L), pp_radix_inv(L, q), pp_ns_inv(L, q), T>(sre, sim,
+                                                              g_fft_ptw + pt_inv_off(L, q));
+    pp_inv_middle<L, T, q + 1>(sre, sim);
+  }
+}
+
+// One CTA per row, N = 2^L complex values (n = 2N real samples).
+template <int L, int MODE>
+__global__ void __launch_bounds__(PCfg<L>::T, 1) fft_pair_kernel(RowArgs a) {
+  using C = PCfg<L>;
+  constexpr int N = C::N, T = C::T, P = C::P;
+  extern __shared__ __align__(16) float psm[];
+  float* sre = psm;
+  float* sim = psm + padded2(N);
+  const float2* utw = g_fft_tw + tw_offset(L) + tw_passes_size(N);  // exp(-i pi k / N)
+
+  const int d = blockIdx.x / a.rows_b;
+  const int b = blockIdx.x - d * a.rows_b;
+  const int64_t row = (int64_t)b * a.rows_d + d;
+
+  if (MODE != kModeIrfft) {
+    const float* x = a.in + a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd;
+    const bool vec = a.in_st == 1 && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    pp_first<N, pp_radix(L, 0), T>(sre, sim, x, a.in_st, a.in_len, vec);
+    pp_fwd_middle<L, T, 1>(sre, sim);
+  }
+  pp_mirror<N, pp_radix(L, P - 1), T, MODE>(sre, sim, g_fft_ptw + pt_fwd_off(L, P - 1), utw, a,
+                                            row, d);
+  if (MODE == kModeRfft) return;
+  pp_inv_middle<L, T, 1>(sre, sim);
+  float* y = a.out + row * a.out_ld;
+  const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  pp_last<N, pp_radix_inv(L, P - 1), T>(sre, sim, g_fft_ptw + pt_inv_off(L, P - 1), y, a.out_len,
+                                        vec);
+}
+
 // ------------------------------------------------------------ dispatch
 
 template <int LOGN, int MODE>
 int launch_row(const RowArgs& a, int64_t rows) {
-  using C = RowCfg<LOGN>;
   static bool attr = false;
-  if (!attr) {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(fft_row_kernel<LOGN, MODE>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    attr = true;
+  if constexpr (LOGN >= kPairMinL) {
+    using C = PCfg<LOGN>;
+    if (!attr) {
+      WXX_CUDA_CHECK(cudaFuncSetAttribute(fft_pair_kernel<LOGN, MODE>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      attr = true;
+    }
+    fft_pair_kernel<LOGN, MODE><<<(unsigned)rows, C::T, C::SMEM, wxx::stream()>>>(a);
+  } else {
+    using C = RowCfg<LOGN>;
+    if (!attr) {
+      WXX_CUDA_CHECK(cudaFuncSetAttribute(fft_row_kernel<LOGN, MODE>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      attr = true;
+    }
+    fft_row_kernel<LOGN, MODE><<<(unsigned)rows, C::T, C::SMEM, wxx::stream()>>>(a);
   }
-  fft_row_kernel<LOGN, MODE><<<(unsigned)rows, C::T, C::SMEM, wxx::stream()>>>(a);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }
@@ -763,6 +1325,8 @@ namespace wxx {
 // Fills the FFT twiddle tables of every shared-memory size (called by wxx_init).
 int fft_init_tables() {
   fft_twiddle_init_kernel<<<64, 256, 0, wxx::stream()>>>();
+  WXX_LAUNCH_CHECK();
+  fft_pair_twiddle_init_kernel<<<64, 256, 0, wxx::stream()>>>();
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }
