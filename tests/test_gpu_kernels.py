@@ -436,8 +436,8 @@ def test_complex_mul_broadcast(rng):
 
 
 @pytest.mark.parametrize("B,D,L", [(2, 3, 64), (2, 3, 200), (3, 2, 300), (3, 4, 1000),
-                                   (2, 3, 1500), (2, 2, 3000), (2, 8, 8192), (1, 4, 16384),
-                                   (1, 2, 40000)])
+                                   (2, 3, 1001), (2, 3, 1500), (2, 2, 3000), (2, 8, 8192),
+                                   (3, 100, 8192), (1, 4, 16384), (1, 2, 40000)])
 def test_fftconv_matches_reference_chain(B, D, L, rng):
     F = _w().functional
     x = rng.standard_normal((B, D, L)).astype(np.float32)

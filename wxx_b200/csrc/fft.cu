@@ -21,6 +21,7 @@
 // shared memory) use the same algorithm with radix-2 Stockham passes through
 // global scratch.
 #include "common.cuh"
+#include "tc_gemm.cuh"  // mbarrier helpers (bounded waits)
 
 #include <cstring>
 
@@ -663,8 +664,8 @@ __global__ void unpack_real_global_kernel(const float2* __restrict__ z, RowArgs 
 // complex values in one 64-bit register pair and their imaginary parts in
 // another, so one paired instruction does the arithmetic of both butterflies.
 // The row sits in shared memory as two planar float arrays (re, im), padded
-// by two floats every 32 (pad2), so the two lanes of a pair are adjacent and
-// 8-byte aligned and every pass moves them with 64-bit accesses.
+// (pad3), so the two lanes of a pair are adjacent and 8-byte aligned and
+// every pass moves them with 64-bit accesses.
 //
 // Per fused convolution the shared-memory traffic is cut three ways:
 //  * the first forward pass reads x straight from global memory;
@@ -786,84 +787,129 @@ __device__ __forceinline__ void p_dft(CP (&v)[R]) {
   for (int i = 0; i < R; ++i) v[i] = t[i];
 }
 
-__device__ __forceinline__ int pad2(int i) { return i + ((i >> 5) << 1); }
-__host__ __device__ constexpr int padded2(int n) { return n + n / 16; }
+// Shared-memory index of element i of a planar row: two spare floats every 32
+// and sixteen more every 512.  The two lanes of a pair stay adjacent and
+// 8-byte aligned, and the 64-bit store patterns of a half-warp in every pass
+// of the plans below (groups of 8 pairs, 256 or 512 elements apart in the
+// radix-16 and radix-32 passes) fall on 32 distinct banks.
+__device__ __forceinline__ int pad3(int i) { return i + ((i >> 5) << 1) + ((i >> 9) << 4); }
+__host__ __device__ constexpr int padded3(int n) { return n + n / 16 + n / 32 + 32; }
 __device__ __forceinline__ u64 lds2(const float* p) { return *reinterpret_cast<const u64*>(p); }
 __device__ __forceinline__ void sts2(float* p, u64 v) { *reinterpret_cast<u64*>(p) = v; }
 __device__ __forceinline__ u64 ldg2(const float* p) { return __ldg(reinterpret_cast<const u64*>(p)); }
 
-// Pass plan for N = 2^L (L = 8..14): forward radices first to last; the
-// inverse runs them in reverse order.  Radix 32 appears only where a thread
-// block of N/32 threads has the registers for it (L = 13: 256 threads).
-__host__ __device__ constexpr int pp_count(int L) { return L <= 8 ? 2 : (L == 14 ? 4 : 3); }
-__host__ __device__ constexpr int pp_radix(int L, int p) {
-  return L == 8    ? 16
-         : L == 9  ? 8
-         : L == 10 ? (p == 1 ? 4 : 16)
-         : L == 11 ? (p == 1 ? 8 : 16)
-         : L == 12 ? 16
-         : L == 13 ? (p == 1 ? 32 : 16)
-                   : (p == 2 ? 4 : 16);
+__device__ __forceinline__ CP cp_mul(const CP& a, const CP& b) {
+  return CP{p_sub(p_mul(a.re, b.re), p_mul(a.im, b.im)), p_fma(a.re, b.im, p_mul(a.im, b.re))};
+}
+__device__ __forceinline__ CP cp_sqr(const CP& a) {
+  return CP{p_sub(p_mul(a.re, a.re), p_mul(a.im, a.im)), p_mul(p_add(a.re, a.re), a.im)};
+}
+// a * exp(-i pi Q / R) for a compile-time angle (R <= 16: a multiple of pi/16).
+template <int R, int Q>
+__device__ __forceinline__ CP cp_rot_half(const CP& a) {
+  if constexpr (Q == 0) {
+    return a;
+  } else {
+    constexpr int q32 = Q * (16 / R);   // exp(-i pi Q / R) = exp(-2 pi i q32 / 32)
+    constexpr float c = cos32(q32), sn = sin32(q32);
+    const u64 C = p_make(c, c), S = p_make(sn, sn);
+    // (re + i im)(c - i sn)
+    return CP{p_fma(a.re, C, p_mul(a.im, S)), p_sub(p_mul(a.im, C), p_mul(a.re, S))};
+  }
+}
+__device__ __forceinline__ float f_sel(bool c, float a, float b) { return c ? a : b; }
+
+struct PBuf {
+  float* re;
+  float* im;
+};
+
+// Pass plans for N = 2^L (L = 8..14), variant V = 0 (fft_pair_kernel) or
+// V = 1 (the staged convolution at L = 13): forward radices first to last;
+// the inverse runs them in reverse order.  L = 13, V = 0 has a radix-32
+// middle pass, three passes each way at 256 threads (measured: 19.4k cycles
+// per row against 21.5k with the radix-32 pass first); the staged kernel
+// transforms in place, where a radix-32 pass would hold 128 registers across
+// its barrier, so its radix-32 pass comes first (reading the staged input)
+// and last (writing global memory).  L = 14 has 512 threads (128 registers
+// each) and four passes; smaller rows a small first radix, then radix 16.
+__host__ __device__ constexpr int pp_count(int L, int V = 0) {
+  return L == 8 ? 2 : (L == 14 ? 4 : 3);
+}
+__host__ __device__ constexpr int pp_radix(int L, int V, int p) {
+  return L == 13   ? (p == (V ? 0 : 1) ? 32 : 16)
+         : L == 14 ? (p == 2 ? 4 : 16)
+         : (p == 0 && (L - 8) % 4 != 0) ? (1 << ((L - 8) % 4))
+                                         : 16;
 }
 // Sub-transform size before forward pass p / inverse pass q.
-__host__ __device__ constexpr int pp_ns_fwd(int L, int p) {
+__host__ __device__ constexpr int pp_ns_fwd(int L, int V, int p) {
   int ns = 1;
-  for (int i = 0; i < p; ++i) ns *= pp_radix(L, i);
+  for (int i = 0; i < p; ++i) ns *= pp_radix(L, V, i);
   return ns;
 }
-__host__ __device__ constexpr int pp_radix_inv(int L, int q) { return pp_radix(L, pp_count(L) - 1 - q); }
-__host__ __device__ constexpr int pp_ns_inv(int L, int q) {
+__host__ __device__ constexpr int pp_radix_inv(int L, int V, int q) {
+  return pp_radix(L, V, pp_count(L, V) - 1 - q);
+}
+__host__ __device__ constexpr int pp_ns_inv(int L, int V, int q) {
   int ns = 1;
-  for (int i = 0; i < q; ++i) ns *= pp_radix_inv(L, i);
+  for (int i = 0; i < q; ++i) ns *= pp_radix_inv(L, V, i);
   return ns;
 }
 
-// Twiddle tables (floats): for each L = 8..14, the forward passes p = 1..P-1
-// then the inverse passes q = 1..P-1, each a segment of (R-1)*NS cosines
-// followed by (R-1)*NS sines of 2 pi r k / (R NS), entry (r-1)*NS + k.
+// Twiddle tables (floats), one block per plan (L = 8..14 with V = 0, then
+// L = 13 with V = 1): the forward passes p = 1..P-1 then the inverse passes
+// q = 1..P-1, each a segment of (R-1)*NS cosines followed by (R-1)*NS sines of
+// 2 pi r k / (R NS), entry (r-1)*NS + k.
 constexpr int kPairMinL = 8;
+constexpr int kPlans = 8;
+__host__ __device__ constexpr int plan_L(int i) { return i == 7 ? 13 : kPairMinL + i; }
+__host__ __device__ constexpr int plan_V(int i) { return i == 7 ? 1 : 0; }
+__host__ __device__ constexpr int plan_index(int L, int V) { return V ? 7 : L - kPairMinL; }
 __host__ __device__ constexpr int pt_seg(int R, int NS) { return 2 * (R - 1) * NS; }
-__host__ __device__ constexpr int pt_size(int L) {
+__host__ __device__ constexpr int pt_size(int L, int V) {
   int s = 0;
-  for (int p = 1; p < pp_count(L); ++p) s += pt_seg(pp_radix(L, p), pp_ns_fwd(L, p));
-  for (int q = 1; q < pp_count(L); ++q) s += pt_seg(pp_radix_inv(L, q), pp_ns_inv(L, q));
+  for (int p = 1; p < pp_count(L, V); ++p) s += pt_seg(pp_radix(L, V, p), pp_ns_fwd(L, V, p));
+  for (int q = 1; q < pp_count(L, V); ++q) s += pt_seg(pp_radix_inv(L, V, q), pp_ns_inv(L, V, q));
   return s;
 }
-__host__ __device__ constexpr int pt_base(int L) {
+__host__ __device__ constexpr int pt_base_i(int i) {
   int o = 0;
-  for (int l = kPairMinL; l < L; ++l) o += pt_size(l);
+  for (int k = 0; k < i; ++k) o += pt_size(plan_L(k), plan_V(k));
   return o;
 }
-__host__ __device__ constexpr int pt_fwd_off(int L, int p) {
-  int o = pt_base(L);
-  for (int i = 1; i < p; ++i) o += pt_seg(pp_radix(L, i), pp_ns_fwd(L, i));
+__host__ __device__ constexpr int pt_base(int L, int V) { return pt_base_i(plan_index(L, V)); }
+__host__ __device__ constexpr int pt_fwd_off(int L, int V, int p) {
+  int o = pt_base(L, V);
+  for (int i = 1; i < p; ++i) o += pt_seg(pp_radix(L, V, i), pp_ns_fwd(L, V, i));
   return o;
 }
-__host__ __device__ constexpr int pt_inv_off(int L, int q) {
-  int o = pt_fwd_off(L, pp_count(L));
-  for (int i = 1; i < q; ++i) o += pt_seg(pp_radix_inv(L, i), pp_ns_inv(L, i));
+__host__ __device__ constexpr int pt_inv_off(int L, int V, int q) {
+  int o = pt_fwd_off(L, V, pp_count(L, V));
+  for (int i = 1; i < q; ++i) o += pt_seg(pp_radix_inv(L, V, i), pp_ns_inv(L, V, i));
   return o;
 }
-constexpr int kPtTotal = pt_base(kMaxSmemLogN + 1);
+constexpr int kPtTotal = pt_base_i(kPlans);
 static __device__ __align__(16) float g_fft_ptw[kPtTotal];
 
 __global__ void fft_pair_twiddle_init_kernel() {
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < kPtTotal; e += gridDim.x * blockDim.x) {
-    int L = kPairMinL;
-    while (L < kMaxSmemLogN && e >= pt_base(L + 1)) ++L;
-    int local = e - pt_base(L);
-    const int P = pp_count(L);
+    int i = 0;
+    while (i + 1 < kPlans && e >= pt_base_i(i + 1)) ++i;
+    const int L = plan_L(i), V = plan_V(i);
+    int local = e - pt_base_i(i);
+    const int P = pp_count(L, V);
     for (int s = 0; s < 2 * (P - 1); ++s) {
       const bool inv = s >= P - 1;
       const int idx = inv ? s - (P - 1) + 1 : s + 1;
-      const int R = inv ? pp_radix_inv(L, idx) : pp_radix(L, idx);
-      const int NS = inv ? pp_ns_inv(L, idx) : pp_ns_fwd(L, idx);
+      const int R = inv ? pp_radix_inv(L, V, idx) : pp_radix(L, V, idx);
+      const int NS = inv ? pp_ns_inv(L, V, idx) : pp_ns_fwd(L, V, idx);
       const int seg = pt_seg(R, NS);
       if (local < seg) {
         const int half = (R - 1) * NS;
         const bool is_sin = local >= half;
-        const int i = is_sin ? local - half : local;
-        const int rr = i / NS + 1, k = i % NS;
+        const int j = is_sin ? local - half : local;
+        const int rr = j / NS + 1, k = j % NS;
         double sn, cs;
         sincospi(2.0 * (double)rr * (double)k / ((double)R * (double)NS), &sn, &cs);
         g_fft_ptw[e] = (float)(is_sin ? sn : cs);
@@ -877,17 +923,20 @@ __global__ void fft_pair_twiddle_init_kernel() {
 template <int L>
 struct PCfg {
   static constexpr int N = 1 << L;
-  static constexpr int P = pp_count(L);
+  static constexpr int P = pp_count(L, 0);
   static constexpr int T = N / 32 < 32 ? 32 : N / 32;
-  static constexpr int SMEM = 2 * padded2(N) * 4;
+  static constexpr int BUF = 2 * padded3(N);  // floats of one planar row (re, then im)
+  // Two row buffers where they fit: passes then run out of place, with one
+  // barrier each and every thread storing as soon as its butterflies are done.
+  static constexpr bool DB = 2 * BUF * 4 <= 200 * 1024;
+  static constexpr int SMEM = (DB ? 2 : 1) * BUF * 4;
 };
 
 // Forward pass 0 (NS = 1) from the real input row: z[m] = x[2m] + i x[2m+1].
 // Output r of butterfly j goes to j R + r; the two lanes' outputs r, r+1 are
 // regrouped into one 64-bit store per lane.
-template <int N, int R, int T>
-__device__ __forceinline__ void pp_first(float* sre, float* sim, const float* x, int64_t st,
-                                         int len, bool vec) {
+template <int N, int R, int T, bool SMEMX = false>
+__device__ __forceinline__ void pp_first(PBuf dst, const float* x, int64_t st, int len, bool vec) {
   constexpr int NB = N / R, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
 #pragma unroll
   for (int p = 0; p < PER; ++p) {
@@ -899,7 +948,10 @@ __device__ __forceinline__ void pp_first(float* sre, float* sim, const float* x,
       for (int r = 0; r < R; ++r) {
         const int t0 = 2 * (j + r * NB);
         float4 xv;
-        if (vec && t0 + 3 < len) {
+        if (SMEMX) {
+          // staged row: len floats, len % 4 == 0
+          xv = t0 < len ? *reinterpret_cast<const float4*>(x + t0) : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else if (vec && t0 + 3 < len) {
           xv = *reinterpret_cast<const float4*>(x + t0);
         } else {
           xv.x = t0 < len ? x[(int64_t)t0 * st] : 0.f;
@@ -913,95 +965,148 @@ __device__ __forceinline__ void pp_first(float* sre, float* sim, const float* x,
       p_dft<R>(v);
 #pragma unroll
       for (int r = 0; r < R; r += 2) {
-        sts2(sre + pad2(j * R + r), p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
-        sts2(sim + pad2(j * R + r), p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
-        sts2(sre + pad2((j + 1) * R + r), p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
-        sts2(sim + pad2((j + 1) * R + r), p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
+        sts2(dst.re + pad3(j * R + r), p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
+        sts2(dst.im + pad3(j * R + r), p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
+        sts2(dst.re + pad3((j + 1) * R + r), p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
+        sts2(dst.im + pad3((j + 1) * R + r), p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
       }
     }
   }
   __syncthreads();
 }
 
-// One in-place Stockham pass (NS >= 2) over shared memory, lanes = butterflies
-// j, j+1 (j even, so both share the block j - j mod NS and twiddle k, k+1).
-template <int N, int R, int NS, int T>
-__device__ __forceinline__ void pp_pass(float* sre, float* sim, const float* __restrict__ tw) {
+// Loads butterflies j, j+1 (j even) of a Stockham pass, applies the twiddles
+// of k = j mod NS, k+1, and transforms them.
+template <int N, int R, int NS>
+__device__ __forceinline__ void pp_load_dft(CP (&v)[R], PBuf src, int j,
+                                            const float* __restrict__ tw) {
+  constexpr int NB = N / R;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    v[r].re = lds2(src.re + pad3(j + r * NB));
+    v[r].im = lds2(src.im + pad3(j + r * NB));
+  }
+  const int k = j & (NS - 1);
+#pragma unroll
+  for (int r = 1; r < R; ++r)
+    p_twiddle(v[r], ldg2(tw + (r - 1) * NS + k), ldg2(tw + (R - 1 + r - 1) * NS + k));
+  p_dft<R>(v);
+}
+
+template <int N, int R, int NS>
+__device__ __forceinline__ void pp_store(const CP (&v)[R], PBuf dst, int j) {
+  const int k = j & (NS - 1);
+  const int d = (j - k) * R + k;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    sts2(dst.re + pad3(d + r * NS), v[r].re);
+    sts2(dst.im + pad3(d + r * NS), v[r].im);
+  }
+}
+
+// One Stockham pass (NS >= 2), lanes = butterflies j, j+1.  In place (src ==
+// dst) every load precedes a barrier and every store; out of place each
+// thread stores its butterflies right after transforming them.
+template <int N, int R, int NS, int T, bool INPLACE>
+__device__ __forceinline__ void pp_pass(PBuf src, PBuf dst, const float* __restrict__ tw) {
   constexpr int NB = N / R, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
-  CP v[PER][R];
+  if constexpr (INPLACE) {
+    CP v[PER][R];
 #pragma unroll
-  for (int p = 0; p < PER; ++p) {
-    const int q = threadIdx.x + p * T;
-    if (PAIRS % T == 0 || q < PAIRS) {
-      const int j = 2 * q;
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        v[p][r].re = lds2(sre + pad2(j + r * NB));
-        v[p][r].im = lds2(sim + pad2(j + r * NB));
-      }
-      const int k = j & (NS - 1);
-#pragma unroll
-      for (int r = 1; r < R; ++r)
-        p_twiddle(v[p][r], ldg2(tw + (r - 1) * NS + k), ldg2(tw + (R - 1 + r - 1) * NS + k));
-      p_dft<R>(v[p]);
+    for (int p = 0; p < PER; ++p) {
+      const int q = threadIdx.x + p * T;
+      if (PAIRS % T == 0 || q < PAIRS) pp_load_dft<N, R, NS>(v[p], src, 2 * q, tw);
     }
-  }
-  __syncthreads();
+    __syncthreads();
 #pragma unroll
-  for (int p = 0; p < PER; ++p) {
-    const int q = threadIdx.x + p * T;
-    if (PAIRS % T == 0 || q < PAIRS) {
-      const int j = 2 * q;
-      const int k = j & (NS - 1);
-      const int d = (j - k) * R + k;
+    for (int p = 0; p < PER; ++p) {
+      const int q = threadIdx.x + p * T;
+      if (PAIRS % T == 0 || q < PAIRS) pp_store<N, R, NS>(v[p], dst, 2 * q);
+    }
+  } else {
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        sts2(sre + pad2(d + r * NS), v[p][r].re);
-        sts2(sim + pad2(d + r * NS), v[p][r].im);
+    for (int p = 0; p < PER; ++p) {
+      const int q = threadIdx.x + p * T;
+      if (PAIRS % T == 0 || q < PAIRS) {
+        CP v[R];
+        pp_load_dft<N, R, NS>(v, src, 2 * q, tw);
+        pp_store<N, R, NS>(v, dst, 2 * q);
       }
     }
   }
   __syncthreads();
 }
 
-// The mirror step on one bin pair (k, N-k), k in [1, N/2]: z = (Z[k], Z[N-k])
-// of the packed forward transform in, conj of the packed inverse input out
-// (conv), the two spectrum bins written out (rfft), or the packed inverse
-// input made from the spectrum (irfft, z unused).
-template <int MODE>
-__device__ __forceinline__ void pp_bin_pair(int k, int N, float2 zk, float2 znk, float2& ok,
-                                            float2& onk, const float2* __restrict__ utw,
-                                            const RowArgs& a, int64_t row, int d) {
-  const float2 u = __ldg(utw + k);
-  if (MODE == kModeRfft) {
-    float2 xk, xnk;
-    rfft_unpack_pair(zk, znk, u, xk, xnk);
-    float2* X = a.spec_out + row * a.out_ld;
-    X[k] = xk;
-    if (k != N - k) X[N - k] = xnk;
-    return;
-  }
-  float2 yk, ynk;
-  if (MODE == kModeConv) {
-    float2 xk, xnk;
-    rfft_unpack_pair(zk, znk, u, xk, xnk);
-    const float2* H = a.H + (int64_t)d * a.h_ld;
-    yk = cmul(xk, __ldg(H + k));
-    ynk = cmul(xnk, __ldg(H + N - k));
+// The mirror step on two bin pairs at once, one per lane: zk = (Z[k0], Z[k1])
+// and znk = (Z[N-k0], Z[N-k1]) of the packed forward transform, u =
+// exp(-i pi k / N) per lane.  Out: the conj of the packed inverse input at
+// the same places (conv: after the product with the filter spectrum H; irfft:
+// made from the input spectrum, z unused), or the spectrum bins written to
+// global memory (rfft).  The algebra of rfft_unpack_pair / irfft_pack_pair,
+// written out on paired registers.
+template <typename Ld>
+__device__ __forceinline__ float2 ld_h(const float2* p) {
+  return Ld::kShared ? *p : __ldg(p);
+}
+struct HFromGlobal { static constexpr bool kShared = false; };
+struct HFromShared { static constexpr bool kShared = true; };
+
+template <int MODE, typename HL>
+__device__ __forceinline__ void pp_bin_pairs2(int k0, int k1, int N, CP& zk, CP& znk, const CP& u,
+                                              const RowArgs& a, int64_t row, const float2* H) {
+  const u64 ur = u.re, ui = u.im;
+  const u64 half = p_make(0.5f, 0.5f);
+  CP yk, ynk;
+  if (MODE != kModeIrfft) {
+    // X[k] = fe + u fo, X[N-k] = conj(fe - u fo), fe = (Z[k] + conj Z[N-k]) / 2,
+    // fo = (Z[k] - conj Z[N-k]) / 2i = (dim, -dre)
+    const u64 fe_re = p_mul(p_add(zk.re, znk.re), half);
+    const u64 fe_im = p_mul(p_sub(zk.im, znk.im), half);
+    const u64 dre = p_mul(p_sub(zk.re, znk.re), half);
+    const u64 dim = p_mul(p_add(zk.im, znk.im), half);
+    const u64 wr = p_fma(ur, dim, p_mul(ui, dre));
+    const u64 wi = p_sub(p_mul(ui, dim), p_mul(ur, dre));
+    const CP xk{p_add(fe_re, wr), p_add(fe_im, wi)};
+    const CP xnk{p_sub(fe_re, wr), p_sub(wi, fe_im)};
+    if (MODE == kModeRfft) {
+      float2* X = a.spec_out + row * a.out_ld;
+      X[k0] = make_float2(p_lo(xk.re), p_lo(xk.im));
+      X[k1] = make_float2(p_hi(xk.re), p_hi(xk.im));
+      X[N - k0] = make_float2(p_lo(xnk.re), p_lo(xnk.im));
+      X[N - k1] = make_float2(p_hi(xnk.re), p_hi(xnk.im));
+      return;
+    }
+    const float2 h0 = ld_h<HL>(H + k0), h1 = ld_h<HL>(H + k1);
+    const float2 g0 = ld_h<HL>(H + N - k0), g1 = ld_h<HL>(H + N - k1);
+    const u64 hr = p_make(h0.x, h1.x), hi = p_make(h0.y, h1.y);
+    const u64 gr = p_make(g0.x, g1.x), gi = p_make(g0.y, g1.y);
+    yk = CP{p_sub(p_mul(xk.re, hr), p_mul(xk.im, hi)), p_fma(xk.re, hi, p_mul(xk.im, hr))};
+    ynk = CP{p_sub(p_mul(xnk.re, gr), p_mul(xnk.im, gi)), p_fma(xnk.re, gi, p_mul(xnk.im, gr))};
   } else {
     const float2* Y = a.spec_in + row * a.spec_ld;
-    yk = k < a.spec_len ? Y[k] : make_float2(0.f, 0.f);
-    ynk = (N - k) < a.spec_len ? Y[N - k] : make_float2(0.f, 0.f);
+    const int len = a.spec_len;
+    const float2 z = make_float2(0.f, 0.f);
+    const float2 y0 = k0 < len ? Y[k0] : z, y1 = k1 < len ? Y[k1] : z;
+    const float2 n0 = N - k0 < len ? Y[N - k0] : z, n1 = N - k1 < len ? Y[N - k1] : z;
+    yk = CP{p_make(y0.x, y1.x), p_make(y0.y, y1.y)};
+    ynk = CP{p_make(n0.x, n1.x), p_make(n0.y, n1.y)};
   }
-  float2 pk, pnk;
-  irfft_pack_pair(yk, ynk, u, pk, pnk);
-  ok = cconj(pk);
-  onk = cconj(pnk);
+  // Z'[k] = fe + i fo, Z'[N-k] = conj(fe) + i conj(fo), fe = (Y[k] + conj Y[N-k]) / 2,
+  // fo = conj(u) (Y[k] - conj Y[N-k]) / 2; stored conjugated
+  const u64 fe_re = p_mul(p_add(yk.re, ynk.re), half);
+  const u64 fe_im = p_mul(p_sub(yk.im, ynk.im), half);
+  const u64 dr = p_mul(p_sub(yk.re, ynk.re), half);
+  const u64 di = p_mul(p_add(yk.im, ynk.im), half);
+  const u64 fo_re = p_fma(ur, dr, p_mul(ui, di));
+  const u64 fo_im = p_sub(p_mul(ur, di), p_mul(ui, dr));
+  zk = CP{p_sub(fe_re, fo_im), p_sub(p_sub(p_make(0.f, 0.f), fe_im), fo_re)};
+  znk = CP{p_add(fe_re, fo_im), p_sub(fe_im, fo_re)};
 }
 
 // Bins 0 and N (both real) -> conj of the packed inverse input Z'[0].
-template <int MODE>
-__device__ __forceinline__ float2 pp_bin_dc(int N, float2 z0, const RowArgs& a, int64_t row, int d) {
+template <int MODE, typename HL>
+__device__ __forceinline__ float2 pp_bin_dc(int N, float2 z0, const RowArgs& a, int64_t row,
+                                            const float2* H) {
   if (MODE == kModeRfft) {
     float2* X = a.spec_out + row * a.out_ld;
     X[0] = make_float2(z0.x + z0.y, 0.f);
@@ -1010,9 +1115,8 @@ __device__ __forceinline__ float2 pp_bin_dc(int N, float2 z0, const RowArgs& a, 
   }
   float y0, yn;
   if (MODE == kModeConv) {
-    const float2* H = a.H + (int64_t)d * a.h_ld;
-    y0 = (z0.x + z0.y) * __ldg(&H[0].x);
-    yn = (z0.x - z0.y) * __ldg(&H[N].x);
+    y0 = (z0.x + z0.y) * ld_h<HL>(H).x;
+    yn = (z0.x - z0.y) * ld_h<HL>(H + N).x;
   } else {
     const float2* Y = a.spec_in + row * a.spec_ld;
     y0 = 0 < a.spec_len ? Y[0].x : 0.f;
@@ -1021,98 +1125,142 @@ __device__ __forceinline__ float2 pp_bin_dc(int N, float2 z0, const RowArgs& a, 
   return make_float2(0.5f * (y0 + yn), -0.5f * (y0 - yn));
 }
 
+template <int N, int R>
+__device__ __forceinline__ void pp_store_transposed(const CP (&v)[R], PBuf dst, int j0, int j1) {
+#pragma unroll
+  for (int r = 0; r < R; r += 2) {
+    sts2(dst.re + pad3(j0 * R + r), p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
+    sts2(dst.im + pad3(j0 * R + r), p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
+    sts2(dst.re + pad3(j1 * R + r), p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
+    sts2(dst.im + pad3(j1 * R + r), p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
+  }
+}
+
+// The bin-pair step of pp_mirror for outputs r and its mirrors, r < R/2.
+// Lanes of an ordinary thread: butterflies j0 and j1 = N/R - j0, so v[r]
+// holds two bins k < N/2 and the lane-swapped v[R-1-r] their mirrors.  Thread
+// 0 (s0) has butterflies 0 and N/(2R), each its own mirror: its lane 1 pairs
+// v[r] with v[R-1-r] as above, its lane 0 pairs v[r] with v[R-r] (r >= 1) and,
+// at r = 0, takes the self-mirrored bin N/2 (output R/2); bin 0 is done apart.
+// Selects keep every thread on one instruction stream.
+template <int N, int R, int MODE, typename HL, int r>
+__device__ __forceinline__ void pp_pairs(CP (&w)[R], const CP& u, bool s0, int j0, int j1,
+                                         const RowArgs& a, int64_t row, const float2* H) {
+  if constexpr (r < R / 2) {
+    constexpr int NB = N / R;
+    CP ur = cp_rot_half<R, r>(u);  // u[j + r N/R] = u[j] exp(-i pi r / R)
+    CP zk, znk;
+    int k0 = j0 + r * NB;
+    const int k1 = j1 + r * NB;
+    if constexpr (r == 0) {
+      ur.re = p_make(f_sel(s0, 0.f, p_lo(ur.re)), p_hi(ur.re));
+      ur.im = p_make(f_sel(s0, -1.f, p_lo(ur.im)), p_hi(ur.im));
+      k0 = s0 ? N / 2 : k0;
+      zk.re = p_make(f_sel(s0, p_lo(w[R / 2].re), p_lo(w[0].re)), p_hi(w[0].re));
+      zk.im = p_make(f_sel(s0, p_lo(w[R / 2].im), p_lo(w[0].im)), p_hi(w[0].im));
+      znk.re = p_make(f_sel(s0, p_lo(w[R / 2].re), p_hi(w[R - 1].re)),
+                      f_sel(s0, p_hi(w[R - 1].re), p_lo(w[R - 1].re)));
+      znk.im = p_make(f_sel(s0, p_lo(w[R / 2].im), p_hi(w[R - 1].im)),
+                      f_sel(s0, p_hi(w[R - 1].im), p_lo(w[R - 1].im)));
+    } else {
+      zk = w[r];
+      znk.re = p_make(f_sel(s0, p_lo(w[R - r].re), p_hi(w[R - 1 - r].re)),
+                      f_sel(s0, p_hi(w[R - 1 - r].re), p_lo(w[R - 1 - r].re)));
+      znk.im = p_make(f_sel(s0, p_lo(w[R - r].im), p_hi(w[R - 1 - r].im)),
+                      f_sel(s0, p_hi(w[R - 1 - r].im), p_lo(w[R - 1 - r].im)));
+    }
+    pp_bin_pairs2<MODE, HL>(k0, k1, N, zk, znk, ur, a, row, H);
+    if (MODE != kModeRfft) {
+      if constexpr (r == 0) {
+        w[0].re = p_make(f_sel(s0, p_lo(w[0].re), p_lo(zk.re)), p_hi(zk.re));
+        w[0].im = p_make(f_sel(s0, p_lo(w[0].im), p_lo(zk.im)), p_hi(zk.im));
+        w[R / 2].re = p_make(f_sel(s0, p_lo(zk.re), p_lo(w[R / 2].re)), p_hi(w[R / 2].re));
+        w[R / 2].im = p_make(f_sel(s0, p_lo(zk.im), p_lo(w[R / 2].im)), p_hi(w[R / 2].im));
+      } else {
+        w[r] = zk;
+        w[R - r].re = p_make(f_sel(s0, p_lo(znk.re), p_lo(w[R - r].re)), p_hi(w[R - r].re));
+        w[R - r].im = p_make(f_sel(s0, p_lo(znk.im), p_lo(w[R - r].im)), p_hi(w[R - r].im));
+      }
+      w[R - 1 - r].re = p_make(f_sel(s0, p_lo(w[R - 1 - r].re), p_hi(znk.re)),
+                               f_sel(s0, p_hi(znk.re), p_lo(znk.re)));
+      w[R - 1 - r].im = p_make(f_sel(s0, p_lo(w[R - 1 - r].im), p_hi(znk.im)),
+                               f_sel(s0, p_hi(znk.im), p_lo(znk.im)));
+    }
+    pp_pairs<N, R, MODE, HL, r + 1>(w, u, s0, j0, j1, a, row, H);
+  }
+}
+
 // Last forward pass (radix R, NS = N/R) + the bin-pair step + first inverse
 // pass (radix R, NS = 1), in registers.  Lanes: butterflies j and N/R - j
-// (thread 0: 0 and N/(2R), each its own mirror).  Output r of butterfly j
-// holds Z[j + r N/R], whose mirror N - k is output R-1-r of butterfly N/R - j.
-template <int N, int R, int T, int MODE>
-__device__ __forceinline__ void pp_mirror(float* sre, float* sim, const float* __restrict__ tw,
-                                          const float2* __restrict__ utw, const RowArgs& a,
-                                          int64_t row, int d) {
-  constexpr int NB = N / R, NS = NB, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
-  CP v[PER][R];
-  int jj0[PER], jj1[PER];
+// (thread 0: 0 and N/(2R)).  Output r of butterfly j holds Z[j + r N/R],
+// whose mirror N - k is output R-1-r of butterfly N/R - j; the first inverse
+// pass reads input r of butterfly j from j + r N/R, exactly the element in
+// hand, and writes j R + r.  The pass twiddles exp(-2 pi i r j / N) are
+// products of two table roots (u[2j], u[8j] with u[k] = exp(-i pi k / N)), at
+// most three roundings from exact.
+template <int N, int R, int T, int MODE, bool INPLACE, typename HL = HFromGlobal>
+__device__ __forceinline__ void pp_mirror(PBuf src, PBuf dst, const float2* __restrict__ utw,
+                                          const RowArgs& a, int64_t row, const float2* H) {
+  static_assert(R == 16, "the mirror pass is radix 16");
+  constexpr int NB = N / R, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
+  constexpr int KEEP = INPLACE ? PER : 1;
+  CP v[KEEP][R];
 #pragma unroll
   for (int p = 0; p < PER; ++p) {
+    CP(&w)[R] = v[INPLACE ? p : 0];
     const int q = threadIdx.x + p * T;
-    const int j0 = q, j1 = q == 0 ? NB / 2 : NB - q;
-    jj0[p] = j0;
-    jj1[p] = j1;
+    const bool s0 = q == 0;
+    const int j0 = q, j1 = s0 ? NB / 2 : NB - q;
     if (PAIRS % T == 0 || q < PAIRS) {
+      const float2 ua = __ldg(utw + j0), ub = __ldg(utw + j1);
+      const CP u{p_make(ua.x, ub.x), p_make(ua.y, ub.y)};
       if (MODE != kModeIrfft) {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          v[p][r].re = p_make(sre[pad2(j0 + r * NB)], sre[pad2(j1 + r * NB)]);
-          v[p][r].im = p_make(sim[pad2(j0 + r * NB)], sim[pad2(j1 + r * NB)]);
+          w[r].re = p_make(src.re[pad3(j0 + r * NB)], src.re[pad3(j1 + r * NB)]);
+          w[r].im = p_make(src.im[pad3(j0 + r * NB)], src.im[pad3(j1 + r * NB)]);
+        }
+        const float2 a1 = __ldg(utw + 2 * j0), b1 = __ldg(utw + 2 * j1);
+        const float2 a4 = __ldg(utw + 8 * j0), b4 = __ldg(utw + 8 * j1);
+        CP z[R];
+        z[1] = CP{p_make(a1.x, b1.x), p_make(a1.y, b1.y)};
+        z[4] = CP{p_make(a4.x, b4.x), p_make(a4.y, b4.y)};
+        z[2] = cp_sqr(z[1]);
+        z[3] = cp_mul(z[2], z[1]);
+        z[8] = cp_sqr(z[4]);
+        z[12] = cp_mul(z[8], z[4]);
+#pragma unroll
+        for (int r = 1; r < 4; ++r) {
+          z[4 + r] = cp_mul(z[4], z[r]);
+          z[8 + r] = cp_mul(z[8], z[r]);
+          z[12 + r] = cp_mul(z[12], z[r]);
         }
 #pragma unroll
-        for (int r = 1; r < R; ++r) {
-          const float* tc = tw + (r - 1) * NS;
-          const float* ts = tw + (R - 1 + r - 1) * NS;
-          p_twiddle(v[p][r], p_make(__ldg(tc + j0), __ldg(tc + j1)),
-                    p_make(__ldg(ts + j0), __ldg(ts + j1)));
-        }
-        p_dft<R>(v[p]);
-      }
-      if (q != 0) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          // pair (lane 0 output r, lane 1 output R-1-r); the smaller bin leads
-          const bool lo_first = r < R / 2;
-          const int k = lo_first ? j0 + r * NB : j1 + (R - 1 - r) * NB;
-          float2 z0 = cp_get(v[p][r], 0), z1 = cp_get(v[p][R - 1 - r], 1);
-          float2 ok, onk;
-          pp_bin_pair<MODE>(k, N, lo_first ? z0 : z1, lo_first ? z1 : z0, ok, onk, utw, a, row, d);
-          if (MODE != kModeRfft) {
-            cp_set(v[p][r], 0, lo_first ? ok : onk);
-            cp_set(v[p][R - 1 - r], 1, lo_first ? onk : ok);
-          }
-        }
+        for (int r = 1; r < R; ++r) w[r] = cp_mul(w[r], z[r]);
+        p_dft<R>(w);
       } else {
-        // lane 0 = butterfly 0: bins r NB; pairs (r, R-r), r = R/2 its own
-        {
-          const float2 o = pp_bin_dc<MODE>(N, cp_get(v[p][0], 0), a, row, d);
-          if (MODE != kModeRfft) cp_set(v[p][0], 0, o);
-        }
 #pragma unroll
-        for (int r = 1; r <= R / 2; ++r) {
-          float2 ok, onk;
-          pp_bin_pair<MODE>(r * NB, N, cp_get(v[p][r], 0), cp_get(v[p][R - r], 0), ok, onk, utw,
-                            a, row, d);
-          if (MODE != kModeRfft) {
-            if (r != R / 2) cp_set(v[p][R - r], 0, onk);
-            cp_set(v[p][r], 0, ok);
-          }
-        }
-        // lane 1 = butterfly NB/2: bins NB/2 + r NB; pairs (r, R-1-r)
-#pragma unroll
-        for (int r = 0; r < R / 2; ++r) {
-          float2 ok, onk;
-          pp_bin_pair<MODE>(NB / 2 + r * NB, N, cp_get(v[p][r], 1), cp_get(v[p][R - 1 - r], 1),
-                            ok, onk, utw, a, row, d);
-          if (MODE != kModeRfft) {
-            cp_set(v[p][r], 1, ok);
-            cp_set(v[p][R - 1 - r], 1, onk);
-          }
-        }
+        for (int r = 0; r < R; ++r) w[r] = CP{0ull, 0ull};
       }
-      if (MODE != kModeRfft) p_dft<R>(v[p]);
+      if (s0) {
+        const float2 o = pp_bin_dc<MODE, HL>(N, cp_get(w[0], 0), a, row, H);
+        if (MODE != kModeRfft) cp_set(w[0], 0, o);
+      }
+      pp_pairs<N, R, MODE, HL, 0>(w, u, s0, j0, j1, a, row, H);
+      if (MODE != kModeRfft) {
+        p_dft<R>(w);
+        if (!INPLACE) pp_store_transposed<N, R>(w, dst, j0, j1);
+      }
     }
   }
   if (MODE == kModeRfft) return;
-  __syncthreads();
+  if (INPLACE) {
+    __syncthreads();
 #pragma unroll
-  for (int p = 0; p < PER; ++p) {
-    const int q = threadIdx.x + p * T;
-    if (PAIRS % T == 0 || q < PAIRS) {
-      const int j0 = jj0[p], j1 = jj1[p];
-#pragma unroll
-      for (int r = 0; r < R; r += 2) {
-        sts2(sre + pad2(j0 * R + r), p_make(p_lo(v[p][r].re), p_lo(v[p][r + 1].re)));
-        sts2(sim + pad2(j0 * R + r), p_make(p_lo(v[p][r].im), p_lo(v[p][r + 1].im)));
-        sts2(sre + pad2(j1 * R + r), p_make(p_hi(v[p][r].re), p_hi(v[p][r + 1].re)));
-        sts2(sim + pad2(j1 * R + r), p_make(p_hi(v[p][r].im), p_hi(v[p][r + 1].im)));
-      }
+    for (int p = 0; p < PER; ++p) {
+      const int q = threadIdx.x + p * T;
+      if (PAIRS % T == 0 || q < PAIRS)
+        pp_store_transposed<N, R>(v[p], dst, q, q == 0 ? NB / 2 : NB - q);
     }
   }
   __syncthreads();
@@ -1121,9 +1269,8 @@ __device__ __forceinline__ void pp_mirror(float* sre, float* sim, const float* _
 // Last inverse pass (radix R, NS = N/R) to the real output row:
 // y[2m] + i y[2m+1] = conj(W[m]) / N.
 template <int N, int R, int T>
-__device__ __forceinline__ void pp_last(const float* sre, const float* sim,
-                                        const float* __restrict__ tw, float* y, int olen,
-                                        bool vec) {
+__device__ __forceinline__ void pp_last(PBuf src, const float* __restrict__ tw, float* y,
+                                        int olen, bool vec) {
   constexpr int NB = N / R, NS = NB, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
   const float scale = 1.0f / (float)N;
 #pragma unroll
@@ -1132,15 +1279,7 @@ __device__ __forceinline__ void pp_last(const float* sre, const float* sim,
     if (PAIRS % T == 0 || q < PAIRS) {
       const int j = 2 * q;
       CP v[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        v[r].re = lds2(sre + pad2(j + r * NB));
-        v[r].im = lds2(sim + pad2(j + r * NB));
-      }
-#pragma unroll
-      for (int r = 1; r < R; ++r)
-        p_twiddle(v[r], ldg2(tw + (r - 1) * NS + j), ldg2(tw + (R - 1 + r - 1) * NS + j));
-      p_dft<R>(v);
+      pp_load_dft<N, R, NS>(v, src, j, tw);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int t0 = 2 * (j + r * NS);
@@ -1160,20 +1299,24 @@ __device__ __forceinline__ void pp_last(const float* sre, const float* sim,
   }
 }
 
-template <int L, int T, int p>
-__device__ __forceinline__ void pp_fwd_middle(float* sre, float* sim) {
-  if constexpr (p <= pp_count(L) - 2) {
-    pp_pass<(1 << L), pp_radix(L, p), pp_ns_fwd(L, p), T>(sre, sim, g_fft_ptw + pt_fwd_off(L, p));
-    pp_fwd_middle<L, T, p + 1>(sre, sim);
+// Middle passes; with two buffers each pass reads buffer CUR and writes the other.
+template <int L, int V, int T, bool DB, int p, int CUR>
+__device__ __forceinline__ void pp_fwd_middle(const PBuf (&bufs)[2]) {
+  if constexpr (p <= pp_count(L, V) - 2) {
+    constexpr int NXT = DB ? 1 - CUR : CUR;
+    pp_pass<(1 << L), pp_radix(L, V, p), pp_ns_fwd(L, V, p), T, !DB>(
+        bufs[CUR], bufs[NXT], g_fft_ptw + pt_fwd_off(L, V, p));
+    pp_fwd_middle<L, V, T, DB, p + 1, NXT>(bufs);
   }
 }
 
-template <int L, int T, int q>
-__device__ __forceinline__ void pp_inv_middle(float* sre, float* sim) {
-  if constexpr (q <= pp_count(L) - 2) {
-    pp_pass<(1 << L), pp_radix_inv(L, q), pp_ns_inv(L, q), T>(sre, sim,
-                                                              g_fft_ptw + pt_inv_off(L, q));
-    pp_inv_middle<L, T, q + 1>(sre, sim);
+template <int L, int V, int T, bool DB, int q, int CUR>
+__device__ __forceinline__ void pp_inv_middle(const PBuf (&bufs)[2]) {
+  if constexpr (q <= pp_count(L, V) - 2) {
+    constexpr int NXT = DB ? 1 - CUR : CUR;
+    pp_pass<(1 << L), pp_radix_inv(L, V, q), pp_ns_inv(L, V, q), T, !DB>(
+        bufs[CUR], bufs[NXT], g_fft_ptw + pt_inv_off(L, V, q));
+    pp_inv_middle<L, V, T, DB, q + 1, NXT>(bufs);
   }
 }
 
@@ -1182,9 +1325,15 @@ template <int L, int MODE>
 __global__ void __launch_bounds__(PCfg<L>::T, 1) fft_pair_kernel(RowArgs a) {
   using C = PCfg<L>;
   constexpr int N = C::N, T = C::T, P = C::P;
+  constexpr bool DB = C::DB;
   extern __shared__ __align__(16) float psm[];
-  float* sre = psm;
-  float* sim = psm + padded2(N);
+  const PBuf bufs[2] = {PBuf{psm, psm + padded3(N)},
+                        DB ? PBuf{psm + C::BUF, psm + C::BUF + padded3(N)}
+                           : PBuf{psm, psm + padded3(N)}};
+  // buffer holding the row before the mirror pass / before the last pass
+  constexpr int CUR_MIRROR = DB ? (P - 2) % 2 : 0;
+  constexpr int CUR_INV = DB ? 1 - CUR_MIRROR : 0;
+  constexpr int CUR_LAST = DB ? (CUR_INV + P - 2) % 2 : 0;
   const float2* utw = g_fft_tw + tw_offset(L) + tw_passes_size(N);  // exp(-i pi k / N)
 
   const int d = blockIdx.x / a.rows_b;
@@ -1194,17 +1343,114 @@ __global__ void __launch_bounds__(PCfg<L>::T, 1) fft_pair_kernel(RowArgs a) {
   if (MODE != kModeIrfft) {
     const float* x = a.in + a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd;
     const bool vec = a.in_st == 1 && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
-    pp_first<N, pp_radix(L, 0), T>(sre, sim, x, a.in_st, a.in_len, vec);
-    pp_fwd_middle<L, T, 1>(sre, sim);
+    pp_first<N, pp_radix(L, 0, 0), T>(bufs[0], x, a.in_st, a.in_len, vec);
+    pp_fwd_middle<L, 0, T, DB, 1, 0>(bufs);
   }
-  pp_mirror<N, pp_radix(L, P - 1), T, MODE>(sre, sim, g_fft_ptw + pt_fwd_off(L, P - 1), utw, a,
-                                            row, d);
+  pp_mirror<N, pp_radix(L, 0, P - 1), T, MODE, !DB>(bufs[CUR_MIRROR], bufs[CUR_INV], utw, a, row,
+                                                 MODE == kModeConv ? a.H + (int64_t)d * a.h_ld
+                                                                   : nullptr);
   if (MODE == kModeRfft) return;
-  pp_inv_middle<L, T, 1>(sre, sim);
+  pp_inv_middle<L, 0, T, DB, 1, CUR_INV>(bufs);
   float* y = a.out + row * a.out_ld;
   const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
-  pp_last<N, pp_radix_inv(L, P - 1), T>(sre, sim, g_fft_ptw + pt_inv_off(L, P - 1), y, a.out_len,
-                                        vec);
+  pp_last<N, pp_radix_inv(L, 0, P - 1), T>(bufs[CUR_LAST], g_fft_ptw + pt_inv_off(L, 0, P - 1), y,
+                                           a.out_len, vec);
+}
+
+// Persistent fused convolution for L <= 13 with the next row's inputs staged
+// in shared memory while the current row is transformed: one async bulk copy
+// (cp.async.bulk, no multicast) brings the next row's x (issued once the
+// first pass has consumed the current one) and one its filter-spectrum row
+// (issued once the mirror pass has used the current one), each completing
+// on its own mbarrier.  The first pass and the spectrum product then read
+// shared memory instead of waiting on HBM and L2.  The row is transformed in
+// place (one planar buffer).  Requirements (checked by the host): x rows
+// contiguous, 16-byte aligned, staged length a multiple of 4 floats; H rows
+// 16-byte aligned with N + 2 complex values readable.
+template <int L>
+struct SCfg {
+  static constexpr int N = 1 << L;
+  static constexpr int T = PCfg<L>::T;
+  static constexpr int X_FLOATS = 2 * N;            // staged x (at most n reals)
+  static constexpr int H_FLOATS = 2 * (N + 2);      // staged H row (N + 2 complex)
+  static constexpr int BUF_FLOATS = 2 * padded3(N);
+  static constexpr int SMEM = (X_FLOATS + H_FLOATS + BUF_FLOATS) * 4;
+};
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          wxx_tc::smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(wxx_tc::smem_u32(bar))
+      : "memory");
+}
+
+template <int L>
+__global__ void __launch_bounds__(SCfg<L>::T, 1)
+    fft_conv_staged_kernel(RowArgs a, int64_t rows, int xlen, int* err) {
+  using C = SCfg<L>;
+  constexpr int N = C::N, T = C::T, V = L == 13 ? 1 : 0, P = pp_count(L, V);
+  extern __shared__ __align__(128) float ssm[];
+  __shared__ __align__(8) uint64_t bars[2];  // [0] x staged, [1] H staged
+  __shared__ int abort_flag;
+  float* sx = ssm;
+  float2* sh = reinterpret_cast<float2*>(ssm + C::X_FLOATS);
+  float* bb = ssm + C::X_FLOATS + C::H_FLOATS;
+  const PBuf bufs[2] = {PBuf{bb, bb + padded3(N)}, PBuf{bb, bb + padded3(N)}};
+  const float2* utw = g_fft_tw + tw_offset(L) + tw_passes_size(N);
+  const uint32_t xbytes = (uint32_t)xlen * 4u, hbytes = (uint32_t)(N + 2) * 8u;
+
+  auto x_row = [&](int64_t r) {
+    const int d = (int)(r / a.rows_b), b = (int)(r - (int64_t)d * a.rows_b);
+    return a.in + a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd;
+  };
+  auto h_row = [&](int64_t r) { return a.H + (r / a.rows_b) * a.h_ld; };
+
+  if (threadIdx.x == 0) {
+    wxx_tc::mbar_init(&bars[0], 1);
+    wxx_tc::mbar_init(&bars[1], 1);
+    wxx_tc::fence_barrier_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  int64_t r = blockIdx.x;
+  if (threadIdx.x == 0 && r < rows) {
+    wxx_tc::mbar_arrive_expect_tx(&bars[0], xbytes);
+    bulk_g2s(sx, x_row(r), xbytes, &bars[0]);
+    wxx_tc::mbar_arrive_expect_tx(&bars[1], hbytes);
+    bulk_g2s(sh, h_row(r), hbytes, &bars[1]);
+  }
+  uint32_t phase = 0;
+  for (; r < rows; r += gridDim.x, phase ^= 1u) {
+    const int64_t nxt = r + gridDim.x;
+    const int d = (int)(r / a.rows_b), b = (int)(r - (int64_t)d * a.rows_b);
+    const int64_t row = (int64_t)b * a.rows_d + d;
+
+    bool ok = wxx_tc::mbar_wait(&bars[0], phase, &abort_flag, err);
+    if (__syncthreads_or(!ok)) return;
+    pp_first<N, pp_radix(L, V, 0), T, true>(bufs[0], sx, 1, xlen, true);
+    if (threadIdx.x == 0 && nxt < rows) {
+      wxx_tc::mbar_arrive_expect_tx(&bars[0], xbytes);
+      bulk_g2s(sx, x_row(nxt), xbytes, &bars[0]);
+    }
+    pp_fwd_middle<L, V, T, false, 1, 0>(bufs);
+
+    ok = wxx_tc::mbar_wait(&bars[1], phase, &abort_flag, err);
+    if (__syncthreads_or(!ok)) return;
+    pp_mirror<N, pp_radix(L, V, P - 1), T, kModeConv, true, HFromShared>(bufs[0], bufs[0], utw, a,
+                                                                       row, sh);
+    if (threadIdx.x == 0 && nxt < rows) {
+      wxx_tc::mbar_arrive_expect_tx(&bars[1], hbytes);
+      bulk_g2s(sh, h_row(nxt), hbytes, &bars[1]);
+    }
+    pp_inv_middle<L, V, T, false, 1, 0>(bufs);
+    float* y = a.out + row * a.out_ld;
+    const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    pp_last<N, pp_radix_inv(L, V, P - 1), T>(bufs[0], g_fft_ptw + pt_inv_off(L, V, P - 1), y,
+                                             a.out_len, vec);
+    __syncthreads();  // the next row's first pass overwrites the buffer
+  }
 }
 
 // ------------------------------------------------------------ dispatch
@@ -1262,6 +1508,38 @@ int ilog2_exact(int64_t n) {
   return l;
 }
 
+// The staged persistent convolution, when the rows allow bulk copies.
+template <int L>
+int launch_conv_staged(const RowArgs& a, int64_t rows, int xlen) {
+  using C = SCfg<L>;
+  static int grid_cap = 0;
+  if (grid_cap == 0) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(fft_conv_staged_kernel<L>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    int dev = 0, sms = 0, per_sm = 0;
+    WXX_CUDA_CHECK(cudaGetDevice(&dev));
+    WXX_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    WXX_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fft_conv_staged_kernel<L>,
+                                                                 C::T, C::SMEM));
+    grid_cap = sms * (per_sm > 0 ? per_sm : 1);
+  }
+  const unsigned grid = (unsigned)(rows < grid_cap ? rows : grid_cap);
+  fft_conv_staged_kernel<L><<<grid, C::T, C::SMEM, wxx::stream()>>>(a, rows, xlen,
+                                                                    wxx::device_error_word());
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+// x and H rows that a bulk copy can move (16-byte aligned starts and sizes).
+bool conv_stageable(const RowArgs& a, int N, int* xlen) {
+  const int64_t xl = a.in_len < 2 * (int64_t)N ? a.in_len : 2 * (int64_t)N;
+  *xlen = (int)xl;
+  const uintptr_t x0 = reinterpret_cast<uintptr_t>(a.in + a.in_off);
+  return a.in_st == 1 && xl > 0 && xl % 4 == 0 && (x0 & 15) == 0 && a.in_sb % 4 == 0 &&
+         a.in_sd % 4 == 0 && (reinterpret_cast<uintptr_t>(a.H) & 15) == 0 && a.h_ld % 2 == 0 &&
+         a.h_ld >= N + 2;
+}
+
 // Runs `mode` over all rows, choosing the shared-memory or global path.
 int run_rows(int mode, int64_t n, RowArgs a, int64_t rows, const float2* Hspec) {
   if (rows == 0) return WXX_OK;
@@ -1275,6 +1553,17 @@ int run_rows(int mode, int64_t n, RowArgs a, int64_t rows, const float2* Hspec) 
   int N = (int)(n / 2);
   WXX_REQUIRE(rows < (int64_t(1) << 31), "fft: too many rows");
   if (logN <= kMaxSmemLogN) {
+    int xlen = 0;
+    if (mode == kModeConv && logN >= kPairMinL && logN <= 13 && conv_stageable(a, N, &xlen)) {
+      switch (logN) {
+        case 8: return launch_conv_staged<8>(a, rows, xlen);
+        case 9: return launch_conv_staged<9>(a, rows, xlen);
+        case 10: return launch_conv_staged<10>(a, rows, xlen);
+        case 11: return launch_conv_staged<11>(a, rows, xlen);
+        case 12: return launch_conv_staged<12>(a, rows, xlen);
+        default: return launch_conv_staged<13>(a, rows, xlen);
+      }
+    }
     if (mode == kModeRfft) return launch_row_any<kModeRfft>(logN, a, rows);
     if (mode == kModeIrfft) return launch_row_any<kModeIrfft>(logN, a, rows);
     return launch_row_any<kModeConv>(logN, a, rows);
@@ -1409,12 +1698,14 @@ WXX_EXPORT int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, 
                            int64_t n, int out_len) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(ilog2_exact(n) >= 0, "wxx_fftconv: n=%lld is not a positive power of two", (long long)n);
-  int64_t bins = n / 2 + 1;
+  // spectrum rows of n/2 + 2 complex values: 16-byte aligned, so the fused
+  // kernel can bulk-copy them
+  int64_t ld = n / 2 + 2;
   void* Hs = nullptr;
-  int st = wxx_malloc(&Hs, (uint64_t)D * bins * sizeof(float2));
+  int st = wxx_malloc(&Hs, (uint64_t)D * ld * sizeof(float2));
   if (st) return st;
-  st = wxx_rfft(Hs, bins, h, h_ld, D, Lh, n);
-  if (st == WXX_OK) st = wxx_fftconv_spectrum(y, x, x_off, sb, sd, sl, Hs, bins, B, D, L, n, out_len);
+  st = wxx_rfft(Hs, ld, h, h_ld, D, Lh, n);
+  if (st == WXX_OK) st = wxx_fftconv_spectrum(y, x, x_off, sb, sd, sl, Hs, ld, B, D, L, n, out_len);
   int st2 = wxx_free(Hs);
   return st ? st : st2;
 }
