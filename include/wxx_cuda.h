@@ -205,6 +205,13 @@ int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int64_t sb, in
 /* nn/hyena.py:208-216 fft_conv1d with a time-domain filter h (D, Lh) */
 int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd, int64_t sl,
                 const float* h, int64_t h_ld, int Lh, int B, int D, int L, int64_t n, int out_len);
+/* nn/hyena.py:240 z = gates[i] * fft_conv1d(z, h): wxx_fftconv whose output is
+ * multiplied by a strided (B, D, out_len) gate view (element strides g_sb,
+ * g_sd, g_sl from g_off) as it is stored. */
+int wxx_fftconv_gated(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                      int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D, int L,
+                      int64_t n, int out_len, const float* gate, int64_t g_off, int64_t g_sb,
+                      int64_t g_sd, int64_t g_sl);
 /* No counterpart in the reference.  wxx_fftconv without any allocation: the
  * filter spectrum lives in a fixed 16 MiB device array inside the library.
  * Limits: n <= 32768 and D*(n/2+1) <= 2^21 complex values, else WXX_E_ARG and

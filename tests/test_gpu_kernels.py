@@ -467,6 +467,25 @@ def test_fftconv_strided_and_unaligned_input(L, rng):
     assert rel(got, K.fftconv(np.ascontiguousarray(xw[:, :, 1:]), h, n, L - 5)) < 2e-5
 
 
+@pytest.mark.parametrize("B,D,L", [(2, 3, 40), (3, 100, 8192), (2, 3, 1001), (1, 2, 16384),
+                                   (1, 2, 40000)])
+def test_fftconv_gated(B, D, L, rng):
+    """gate * fftconv(x, h) in one pass (Hyena's gates[i] * fft_conv1d(z, h)):
+    a dense gate and a transposed (B, L, D) -> (B, D, L) gate view, on the
+    small-row, staged, pair, 14-bit and global-memory paths."""
+    F = _w().functional
+    n = 1 << (2 * L - 1).bit_length()
+    x = rng.standard_normal((B, D, L)).astype(np.float32)
+    h = rng.standard_normal((D, L)).astype(np.float32)
+    g = rng.standard_normal((B, D, L)).astype(np.float32)
+    ref = K.fftconv(x, h, n, L) * g
+    got = F.fftconv(up(x), up(h), n, out_len=L, gate=up(g)).numpy()
+    assert rel(got, ref) < 2e-5
+    gt = np.ascontiguousarray(g.transpose(0, 2, 1))
+    got = F.fftconv(up(x), up(h), n, out_len=L, gate=up(gt).permute(0, 2, 1)).numpy()
+    assert rel(got, ref) < 2e-5
+
+
 # ------------------------------------------------------------ fused attention
 
 def _attention_ref(q, k, v, H, mask=None, causal=False):

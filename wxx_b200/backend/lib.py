@@ -98,6 +98,8 @@ SIGNATURES = {
                              c_int, c_int, c_int, c_i64, c_int],
     "wxx_fftconv": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64, c_int,
                     c_int, c_int, c_int, c_i64, c_int],
+    "wxx_fftconv_gated": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64, c_int,
+                          c_int, c_int, c_int, c_i64, c_int, c_void_p, c_i64, c_i64, c_i64, c_i64],
     "wxx_fftconv_static": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64,
                            c_int, c_int, c_int, c_int, c_i64, c_int],
     "wxx_nccl_unique_id": [P_u8],

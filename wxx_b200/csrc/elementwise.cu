@@ -361,48 +361,56 @@ __global__ void causal_conv1d_kernel(float* __restrict__ out, const float* __res
 }
 
 // Transposed-input variant: x element (b, d, n) lives at x_off + b*sb + n*sl + d
-// (sc == 1).  A CTA handles a 32(d) x 128(n) tile: the (128 + K - 1) x 32
-// input rows are read coalesced along d into shared memory (row stride 33),
-// each thread then produces 16 outputs (4 channels x 4 positions 32 apart)
-// written coalesced along n, with its channels' taps in registers.
-constexpr int kConvTileN = 128;
+// (sc == 1).  A CTA handles a 128(d) x 64(n) tile: the (64 + K - 1) input rows
+// of 128 channels (512 contiguous bytes each) are read into shared memory
+// with row pitch 129, so both the row stores (lanes along d) and the column
+// reads (lanes along n) hit 32 distinct banks.  Warp w then produces channels
+// 16w .. 16w+15, each lane two positions 32 apart, written coalesced along n;
+// a channel's K taps are warp-uniform loads.
+constexpr int kConvTileD = 128;
+constexpr int kConvTileN = 64;
+constexpr int kConvPitch = kConvTileD + 1;
 constexpr int kConvMaxK = 8;
 
 __global__ void __launch_bounds__(256) causal_conv1d_tr_kernel(
     float* __restrict__ out, const float* __restrict__ x, int64_t x_off, int64_t sb, int64_t sl,
     const float* __restrict__ w, const float* __restrict__ bias, int B, int D, int L, int K) {
-  extern __shared__ float tile[];  // (kConvTileN + K - 1) x 33
+  extern __shared__ float tile[];  // (kConvTileN + K - 1) x kConvPitch
   const int b = blockIdx.z;
-  const int d0 = blockIdx.y * 32, n0 = blockIdx.x * kConvTileN;
+  const int d0 = blockIdx.y * kConvTileD, n0 = blockIdx.x * kConvTileN;
   const int rows = kConvTileN + K - 1;
   const float* xb = x + x_off + (int64_t)b * sb;
-  const int d = d0 + threadIdx.x;
-  for (int r = threadIdx.y; r < rows; r += blockDim.y) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int r = warp; r < rows; r += 8) {
     const int n = n0 - (K - 1) + r;
-    float v = 0.f;
-    if (n >= 0 && n < L && d < D) v = xb[(int64_t)n * sl + d];
-    tile[r * 33 + threadIdx.x] = v;
+    const bool in = n >= 0 && n < L;
+    const float* xr = xb + (int64_t)n * sl + d0;
+#pragma unroll
+    for (int j = 0; j < kConvTileD / 32; ++j) {
+      const int dd = 32 * j + lane;
+      tile[r * kConvPitch + dd] = (in && d0 + dd < D) ? xr[dd] : 0.f;
+    }
   }
   __syncthreads();
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int dd = threadIdx.y + 8 * c;
+#pragma unroll 4
+  for (int c = 0; c < kConvTileD / 8; ++c) {
+    const int dd = warp * (kConvTileD / 8) + c;
     const int dc = d0 + dd;
-    if (dc >= D) continue;
+    if (dc >= D) break;
     float wk[kConvMaxK];
 #pragma unroll
-    for (int k = 0; k < kConvMaxK; ++k) wk[k] = k < K ? w[dc * K + k] : 0.f;
-    const float bv = bias[dc];
+    for (int k = 0; k < kConvMaxK; ++k) wk[k] = k < K ? __ldg(w + dc * K + k) : 0.f;
+    const float bv = __ldg(bias + dc);
     float* orow = out + ((int64_t)b * D + dc) * L;
 #pragma unroll
     for (int q = 0; q < kConvTileN / 32; ++q) {
-      const int i = threadIdx.x + 32 * q;   // position inside the tile
+      const int i = lane + 32 * q;  // position inside the tile
       const int n = n0 + i;
       if (n >= L) continue;
       float acc = bv;
 #pragma unroll
       for (int k = 0; k < kConvMaxK; ++k)
-        if (k < K && n >= k) acc = acc + wk[k] * tile[(i + K - 1 - k) * 33 + dd];
+        if (k < K && n >= k) acc = acc + wk[k] * tile[(i + K - 1 - k) * kConvPitch + dd];
       orow[n] = acc;
     }
   }
@@ -690,10 +698,9 @@ WXX_EXPORT int wxx_causal_conv1d(float* out, const float* x, int64_t x_off, int6
   if ((int64_t)B * D * L == 0) return WXX_OK;
   cudaStream_t s = wxx::stream();
   if (sc == 1 && K <= kConvMaxK && B <= 65535) {
-    dim3 grid((L + kConvTileN - 1) / kConvTileN, (D + 31) / 32, B);
-    size_t smem = (size_t)(kConvTileN + K - 1) * 33 * sizeof(float);
-    causal_conv1d_tr_kernel<<<grid, dim3(32, 8), smem, s>>>(out, x, x_off, sb, sl, w, bias, B, D, L,
-                                                            K);
+    dim3 grid((L + kConvTileN - 1) / kConvTileN, (D + kConvTileD - 1) / kConvTileD, B);
+    size_t smem = (size_t)(kConvTileN + K - 1) * kConvPitch * sizeof(float);
+    causal_conv1d_tr_kernel<<<grid, 256, smem, s>>>(out, x, x_off, sb, sl, w, bias, B, D, L, K);
   } else {
     int64_t total = (int64_t)B * D * L;
     causal_conv1d_kernel<<<wxx::grid_for(total, kThreads), kThreads, 0, s>>>(

@@ -349,6 +349,9 @@ struct RowArgs {
   int64_t out_ld;
   int out_len;
   int rows_b, rows_d;  // row (b, d) -> output row b*rows_d + d
+  // optional gate (conv mode): y[b, d, t] *= gate[g_off + b*g_sb + d*g_sd + t*g_st]
+  const float* gate;
+  int64_t g_off, g_sb, g_sd, g_st;
 };
 
 constexpr int kModeRfft = 0;
@@ -502,11 +505,18 @@ __global__ void __launch_bounds__(RowCfg<LOGN>::T, RowCfg<LOGN>::MINB)
   const float scale = 1.0f / (float)N;
   const int olen = a.out_len;
   const bool vec = ((reinterpret_cast<uintptr_t>(y) & 7) == 0);
+  const float* g = a.gate == nullptr
+                       ? nullptr
+                       : a.gate + a.g_off + (int64_t)b * a.g_sb + (int64_t)d * a.g_sd;
   for (int m = tid; m < N; m += T) {
     int t0 = 2 * m;
     if (t0 >= olen) break;
     const float2 w = buf[swz(m)];
-    const float2 z = make_float2(w.x * scale, -w.y * scale);
+    float2 z = make_float2(w.x * scale, -w.y * scale);
+    if (g != nullptr) {
+      z.x *= g[(int64_t)t0 * a.g_st];
+      if (t0 + 1 < olen) z.y *= g[(int64_t)(t0 + 1) * a.g_st];
+    }
     if (t0 + 1 < olen) {
       if (vec) *reinterpret_cast<float2*>(y + t0) = z;
       else { y[t0] = z.x; y[t0 + 1] = z.y; }
@@ -529,7 +539,10 @@ __global__ void fft_n1_kernel(RowArgs a, int mode, int64_t rows) {
     }
     float x0 = a.in_len > 0 ? a.in[a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd] : 0.f;
     if (mode == kModeRfft) a.spec_out[row * a.out_ld] = make_float2(x0, 0.f);
-    else if (a.out_len > 0) a.out[row * a.out_ld] = x0 * a.H[(int64_t)d * a.h_ld].x;
+    else if (a.out_len > 0)
+      a.out[row * a.out_ld] =
+          x0 * a.H[(int64_t)d * a.h_ld].x *
+          (a.gate != nullptr ? a.gate[a.g_off + (int64_t)b * a.g_sb + (int64_t)d * a.g_sd] : 1.f);
   }
 }
 
@@ -650,6 +663,12 @@ __global__ void unpack_real_global_kernel(const float2* __restrict__ z, RowArgs 
     int t0 = 2 * m;
     if (t0 >= a.out_len) continue;
     float2 v = cscale(z[row * N + m], scale);
+    if (a.gate != nullptr) {
+      const int b = (int)(row / a.rows_d), d = (int)(row - (int64_t)b * a.rows_d);
+      const float* g = a.gate + a.g_off + (int64_t)b * a.g_sb + (int64_t)d * a.g_sd;
+      v.x *= g[(int64_t)t0 * a.g_st];
+      if (t0 + 1 < a.out_len) v.y *= g[(int64_t)(t0 + 1) * a.g_st];
+    }
     float* y = a.out + row * a.out_ld;
     y[t0] = v.x;
     if (t0 + 1 < a.out_len) y[t0 + 1] = v.y;
@@ -1268,9 +1287,10 @@ __device__ __forceinline__ void pp_mirror(PBuf src, PBuf dst, const float2* __re
 
 // Last inverse pass (radix R, NS = N/R) to the real output row:
 // y[2m] + i y[2m+1] = conj(W[m]) / N.
-template <int N, int R, int T>
+template <int N, int R, int T, bool GSHARED = false>
 __device__ __forceinline__ void pp_last(PBuf src, const float* __restrict__ tw, float* y,
-                                        int olen, bool vec) {
+                                        int olen, bool vec, const float* g = nullptr,
+                                        int64_t g_st = 1, bool gvec = false) {
   constexpr int NB = N / R, NS = NB, PAIRS = NB / 2, PER = (PAIRS + T - 1) / T;
   const float scale = 1.0f / (float)N;
 #pragma unroll
@@ -1284,8 +1304,20 @@ __device__ __forceinline__ void pp_last(PBuf src, const float* __restrict__ tw, 
       for (int r = 0; r < R; ++r) {
         const int t0 = 2 * (j + r * NS);
         if (t0 >= olen) break;
-        const float4 o = make_float4(p_lo(v[r].re) * scale, -p_lo(v[r].im) * scale,
-                                     p_hi(v[r].re) * scale, -p_hi(v[r].im) * scale);
+        float4 o = make_float4(p_lo(v[r].re) * scale, -p_lo(v[r].im) * scale,
+                               p_hi(v[r].re) * scale, -p_hi(v[r].im) * scale);
+        if (g != nullptr) {
+          if (gvec && t0 + 3 < olen) {
+            const float4 gv = GSHARED ? *reinterpret_cast<const float4*>(g + t0)
+                                      : __ldg(reinterpret_cast<const float4*>(g + t0));
+            o = make_float4(o.x * gv.x, o.y * gv.y, o.z * gv.z, o.w * gv.w);
+          } else {
+            o.x *= g[(int64_t)t0 * g_st];
+            if (t0 + 1 < olen) o.y *= g[(int64_t)(t0 + 1) * g_st];
+            if (t0 + 2 < olen) o.z *= g[(int64_t)(t0 + 2) * g_st];
+            if (t0 + 3 < olen) o.w *= g[(int64_t)(t0 + 3) * g_st];
+          }
+        }
         if (vec && t0 + 3 < olen) {
           *reinterpret_cast<float4*>(y + t0) = o;
         } else {
@@ -1318,6 +1350,17 @@ __device__ __forceinline__ void pp_inv_middle(const PBuf (&bufs)[2]) {
         bufs[CUR], bufs[NXT], g_fft_ptw + pt_inv_off(L, V, q));
     pp_inv_middle<L, V, T, DB, q + 1, NXT>(bufs);
   }
+}
+
+// Gate row of (b, d) and whether it takes 16-byte vector loads.
+__device__ __forceinline__ const float* gate_row(const RowArgs& a, int b, int d, bool& gvec) {
+  if (a.gate == nullptr) {
+    gvec = false;
+    return nullptr;
+  }
+  const float* g = a.gate + a.g_off + (int64_t)b * a.g_sb + (int64_t)d * a.g_sd;
+  gvec = a.g_st == 1 && (reinterpret_cast<uintptr_t>(g) & 15) == 0;
+  return g;
 }
 
 // One CTA per row, N = 2^L complex values (n = 2N real samples).
@@ -1353,16 +1396,19 @@ __global__ void __launch_bounds__(PCfg<L>::T, 1) fft_pair_kernel(RowArgs a) {
   pp_inv_middle<L, 0, T, DB, 1, CUR_INV>(bufs);
   float* y = a.out + row * a.out_ld;
   const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  bool gvec;
+  const float* g = MODE == kModeConv ? gate_row(a, b, d, gvec) : nullptr;
   pp_last<N, pp_radix_inv(L, 0, P - 1), T>(bufs[CUR_LAST], g_fft_ptw + pt_inv_off(L, 0, P - 1), y,
-                                           a.out_len, vec);
+                                           a.out_len, vec, g, a.g_st, gvec);
 }
 
 // Persistent fused convolution for L <= 13 with the next row's inputs staged
 // in shared memory while the current row is transformed: one async bulk copy
 // (cp.async.bulk, no multicast) brings the next row's x (issued once the
-// first pass has consumed the current one) and one its filter-spectrum row
-// (issued once the mirror pass has used the current one), each completing
-// on its own mbarrier.  The first pass and the spectrum product then read
+// first pass has consumed the current one), one its filter-spectrum row
+// (issued once the mirror pass has used the current one) and, for the gated
+// form, one its gate row (issued at the end of the row), each completing on
+// its own mbarrier.  The first pass and the spectrum product then read
 // shared memory instead of waiting on HBM and L2.  The row is transformed in
 // place (one planar buffer).  Requirements (checked by the host): x rows
 // contiguous, 16-byte aligned, staged length a multiple of 4 floats; H rows
@@ -1371,10 +1417,10 @@ template <int L>
 struct SCfg {
   static constexpr int N = 1 << L;
   static constexpr int T = PCfg<L>::T;
-  static constexpr int X_FLOATS = 2 * N;            // staged x (at most n reals)
   static constexpr int H_FLOATS = 2 * (N + 2);      // staged H row (N + 2 complex)
   static constexpr int BUF_FLOATS = 2 * padded3(N);
-  static constexpr int SMEM = (X_FLOATS + H_FLOATS + BUF_FLOATS) * 4;
+  // shared memory: staged x (xlen floats), staged gate (glen), H row, row buffer
+  static constexpr int smem(int xlen, int glen) { return (xlen + glen + H_FLOATS + BUF_FLOATS) * 4; }
 };
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
@@ -1388,18 +1434,24 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 template <int L>
 __global__ void __launch_bounds__(SCfg<L>::T, 1)
-    fft_conv_staged_kernel(RowArgs a, int64_t rows, int xlen, int* err) {
+    fft_conv_staged_kernel(RowArgs a, int64_t rows, int xlen, int glen, int* err) {
   using C = SCfg<L>;
   constexpr int N = C::N, T = C::T, V = L == 13 ? 1 : 0, P = pp_count(L, V);
   extern __shared__ __align__(128) float ssm[];
-  __shared__ __align__(8) uint64_t bars[2];  // [0] x staged, [1] H staged
+  __shared__ __align__(8) uint64_t bars[3];  // x, H, gate staged
   __shared__ int abort_flag;
   float* sx = ssm;
-  float2* sh = reinterpret_cast<float2*>(ssm + C::X_FLOATS);
-  float* bb = ssm + C::X_FLOATS + C::H_FLOATS;
+  float* sg = ssm + xlen;
+  float2* sh = reinterpret_cast<float2*>(ssm + xlen + glen);
+  float* bb = ssm + xlen + glen + C::H_FLOATS;
   const PBuf bufs[2] = {PBuf{bb, bb + padded3(N)}, PBuf{bb, bb + padded3(N)}};
   const float2* utw = g_fft_tw + tw_offset(L) + tw_passes_size(N);
   const uint32_t xbytes = (uint32_t)xlen * 4u, hbytes = (uint32_t)(N + 2) * 8u;
+  const uint32_t gbytes = (uint32_t)glen * 4u;
+  auto g_row = [&](int64_t r) {
+    const int d = (int)(r / a.rows_b), b = (int)(r - (int64_t)d * a.rows_b);
+    return a.gate + a.g_off + (int64_t)b * a.g_sb + (int64_t)d * a.g_sd;
+  };
 
   auto x_row = [&](int64_t r) {
     const int d = (int)(r / a.rows_b), b = (int)(r - (int64_t)d * a.rows_b);
@@ -1410,6 +1462,7 @@ __global__ void __launch_bounds__(SCfg<L>::T, 1)
   if (threadIdx.x == 0) {
     wxx_tc::mbar_init(&bars[0], 1);
     wxx_tc::mbar_init(&bars[1], 1);
+    wxx_tc::mbar_init(&bars[2], 1);
     wxx_tc::fence_barrier_init();
     abort_flag = 0;
   }
@@ -1420,6 +1473,10 @@ __global__ void __launch_bounds__(SCfg<L>::T, 1)
     bulk_g2s(sx, x_row(r), xbytes, &bars[0]);
     wxx_tc::mbar_arrive_expect_tx(&bars[1], hbytes);
     bulk_g2s(sh, h_row(r), hbytes, &bars[1]);
+    if (glen > 0) {
+      wxx_tc::mbar_arrive_expect_tx(&bars[2], gbytes);
+      bulk_g2s(sg, g_row(r), gbytes, &bars[2]);
+    }
   }
   uint32_t phase = 0;
   for (; r < rows; r += gridDim.x, phase ^= 1u) {
@@ -1447,9 +1504,22 @@ __global__ void __launch_bounds__(SCfg<L>::T, 1)
     pp_inv_middle<L, V, T, false, 1, 0>(bufs);
     float* y = a.out + row * a.out_ld;
     const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
-    pp_last<N, pp_radix_inv(L, V, P - 1), T>(bufs[0], g_fft_ptw + pt_inv_off(L, V, P - 1), y,
-                                             a.out_len, vec);
+    if (glen > 0) {
+      ok = wxx_tc::mbar_wait(&bars[2], phase, &abort_flag, err);
+      if (__syncthreads_or(!ok)) return;
+      pp_last<N, pp_radix_inv(L, V, P - 1), T, true>(bufs[0], g_fft_ptw + pt_inv_off(L, V, P - 1),
+                                                     y, a.out_len, vec, sg, 1, true);
+    } else {
+      bool gvec;
+      const float* g = gate_row(a, b, d, gvec);
+      pp_last<N, pp_radix_inv(L, V, P - 1), T>(bufs[0], g_fft_ptw + pt_inv_off(L, V, P - 1), y,
+                                               a.out_len, vec, g, a.g_st, gvec);
+    }
     __syncthreads();  // the next row's first pass overwrites the buffer
+    if (glen > 0 && threadIdx.x == 0 && nxt < rows) {
+      wxx_tc::mbar_arrive_expect_tx(&bars[2], gbytes);
+      bulk_g2s(sg, g_row(nxt), gbytes, &bars[2]);
+    }
   }
 }
 
@@ -1509,35 +1579,53 @@ int ilog2_exact(int64_t n) {
 }
 
 // The staged persistent convolution, when the rows allow bulk copies.
+// Dynamic shared memory the staged kernels may request: the opt-in limit per
+// block less their static shared variables (mbarriers, abort flag) and slack.
+constexpr int kMaxDynSmem = 227 * 1024 - 256;
+
 template <int L>
-int launch_conv_staged(const RowArgs& a, int64_t rows, int xlen) {
+int launch_conv_staged(const RowArgs& a, int64_t rows, int xlen, int glen) {
   using C = SCfg<L>;
-  static int grid_cap = 0;
-  if (grid_cap == 0) {
+  static int sms = 0;
+  if (sms == 0) {
     WXX_CUDA_CHECK(cudaFuncSetAttribute(fft_conv_staged_kernel<L>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    int dev = 0, sms = 0, per_sm = 0;
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
+    int dev = 0;
     WXX_CUDA_CHECK(cudaGetDevice(&dev));
     WXX_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    WXX_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fft_conv_staged_kernel<L>,
-                                                                 C::T, C::SMEM));
-    grid_cap = sms * (per_sm > 0 ? per_sm : 1);
   }
-  const unsigned grid = (unsigned)(rows < grid_cap ? rows : grid_cap);
-  fft_conv_staged_kernel<L><<<grid, C::T, C::SMEM, wxx::stream()>>>(a, rows, xlen,
-                                                                    wxx::device_error_word());
+  const int smem = C::smem(xlen, glen);
+  int per_sm = 0;
+  WXX_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fft_conv_staged_kernel<L>,
+                                                               C::T, smem));
+  const int64_t cap = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+  const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+  fft_conv_staged_kernel<L><<<grid, C::T, smem, wxx::stream()>>>(a, rows, xlen, glen,
+                                                                 wxx::device_error_word());
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }
 
-// x and H rows that a bulk copy can move (16-byte aligned starts and sizes).
-bool conv_stageable(const RowArgs& a, int N, int* xlen) {
+// Rows that bulk copies can move (16-byte aligned starts and sizes): x and H
+// always, the gate when it has them too (else the last pass loads it from
+// global memory).  Returns false when the staged kernel does not apply.
+bool conv_stageable(const RowArgs& a, int L, int* xlen, int* glen) {
+  const int N = 1 << L;
   const int64_t xl = a.in_len < 2 * (int64_t)N ? a.in_len : 2 * (int64_t)N;
   *xlen = (int)xl;
   const uintptr_t x0 = reinterpret_cast<uintptr_t>(a.in + a.in_off);
-  return a.in_st == 1 && xl > 0 && xl % 4 == 0 && (x0 & 15) == 0 && a.in_sb % 4 == 0 &&
-         a.in_sd % 4 == 0 && (reinterpret_cast<uintptr_t>(a.H) & 15) == 0 && a.h_ld % 2 == 0 &&
-         a.h_ld >= N + 2;
+  if (!(a.in_st == 1 && xl > 0 && xl % 4 == 0 && (x0 & 15) == 0 && a.in_sb % 4 == 0 &&
+        a.in_sd % 4 == 0 && (reinterpret_cast<uintptr_t>(a.H) & 15) == 0 && a.h_ld % 2 == 0 &&
+        a.h_ld >= N + 2))
+    return false;
+  const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.gate + a.g_off);
+  *glen = (a.gate != nullptr && a.g_st == 1 && a.out_len > 0 && a.out_len % 4 == 0 &&
+           (g0 & 15) == 0 && a.g_sb % 4 == 0 && a.g_sd % 4 == 0)
+              ? a.out_len
+              : 0;
+  const int fixed = 2 * (N + 2) + 2 * padded3(N);
+  if ((*xlen + *glen + fixed) * 4 > kMaxDynSmem) *glen = 0;
+  return (*xlen + *glen + fixed) * 4 <= kMaxDynSmem;
 }
 
 // Runs `mode` over all rows, choosing the shared-memory or global path.
@@ -1553,15 +1641,16 @@ int run_rows(int mode, int64_t n, RowArgs a, int64_t rows, const float2* Hspec) 
   int N = (int)(n / 2);
   WXX_REQUIRE(rows < (int64_t(1) << 31), "fft: too many rows");
   if (logN <= kMaxSmemLogN) {
-    int xlen = 0;
-    if (mode == kModeConv && logN >= kPairMinL && logN <= 13 && conv_stageable(a, N, &xlen)) {
+    int xlen = 0, glen = 0;
+    if (mode == kModeConv && logN >= kPairMinL && logN <= 13 &&
+        conv_stageable(a, logN, &xlen, &glen)) {
       switch (logN) {
-        case 8: return launch_conv_staged<8>(a, rows, xlen);
-        case 9: return launch_conv_staged<9>(a, rows, xlen);
-        case 10: return launch_conv_staged<10>(a, rows, xlen);
-        case 11: return launch_conv_staged<11>(a, rows, xlen);
-        case 12: return launch_conv_staged<12>(a, rows, xlen);
-        default: return launch_conv_staged<13>(a, rows, xlen);
+        case 8: return launch_conv_staged<8>(a, rows, xlen, glen);
+        case 9: return launch_conv_staged<9>(a, rows, xlen, glen);
+        case 10: return launch_conv_staged<10>(a, rows, xlen, glen);
+        case 11: return launch_conv_staged<11>(a, rows, xlen, glen);
+        case 12: return launch_conv_staged<12>(a, rows, xlen, glen);
+        default: return launch_conv_staged<13>(a, rows, xlen, glen);
       }
     }
     if (mode == kModeRfft) return launch_row_any<kModeRfft>(logN, a, rows);
@@ -1665,9 +1754,22 @@ WXX_EXPORT int wxx_irfft(float* y, int64_t out_ld, const void* X, int64_t in_ld,
 //   y[b, d, t] = irfft(rfft(x[b, d, :], n) * H[d, :], n)[t],  t < out_len
 // x is a strided (B, D, L) view (element strides sb, sd, sl from x_off);
 // H is (D, n/2+1) c64 with row stride h_ld; y is dense (B, D, out_len).
+static int fftconv_spectrum_impl(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                                 int64_t sl, const void* H, int64_t h_ld, int B, int D, int L,
+                                 int64_t n, int out_len, const float* gate, int64_t g_off,
+                                 int64_t g_sb, int64_t g_sd, int64_t g_sl);
+
 WXX_EXPORT int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int64_t sb,
                                     int64_t sd, int64_t sl, const void* H, int64_t h_ld, int B,
                                     int D, int L, int64_t n, int out_len) {
+  return fftconv_spectrum_impl(y, x, x_off, sb, sd, sl, H, h_ld, B, D, L, n, out_len, nullptr, 0,
+                               0, 0, 0);
+}
+
+static int fftconv_spectrum_impl(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                                 int64_t sl, const void* H, int64_t h_ld, int B, int D, int L,
+                                 int64_t n, int out_len, const float* gate, int64_t g_off,
+                                 int64_t g_sb, int64_t g_sd, int64_t g_sl) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(ilog2_exact(n) >= 0, "wxx_fftconv: n=%lld is not a positive power of two", (long long)n);
   WXX_REQUIRE(out_len >= 0 && out_len <= n, "wxx_fftconv: out_len must be in [0, n]");
@@ -1686,6 +1788,11 @@ WXX_EXPORT int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int
   a.out_len = out_len;
   a.rows_b = B;
   a.rows_d = D;
+  a.gate = gate;
+  a.g_off = g_off;
+  a.g_sb = g_sb;
+  a.g_sd = g_sd;
+  a.g_st = g_sl;
   return run_rows(kModeConv, n, a, (int64_t)B * D, (const float2*)H);
 }
 
@@ -1693,9 +1800,35 @@ WXX_EXPORT int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int
 // stride h_ld floats): computes H = rfft(h, n) into a temporary and runs
 // wxx_fftconv_spectrum.  This is Hyena's fft_conv1d (nn/hyena.py:208-216):
 //   y = irfft(rfft(x, n) * rfft(h, n), n)[..., :out_len]
+static int fftconv_impl(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                        int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D, int L,
+                        int64_t n, int out_len, const float* gate, int64_t g_off, int64_t g_sb,
+                        int64_t g_sd, int64_t g_sl);
+
 WXX_EXPORT int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
                            int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D, int L,
                            int64_t n, int out_len) {
+  return fftconv_impl(y, x, x_off, sb, sd, sl, h, h_ld, Lh, B, D, L, n, out_len, nullptr, 0, 0, 0,
+                      0);
+}
+
+// Gated form: y[b, d, t] = gate[b, d, t] * fftconv(x, h)[b, d, t] for a
+// strided (B, D, out_len) gate view (element strides g_sb, g_sd, g_sl from
+// g_off).  Hyena's z = gates[i] * fft_conv1d(z, h) (nn/hyena.py:240) in one
+// pass: the product is applied as the output is stored.
+WXX_EXPORT int wxx_fftconv_gated(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                                 int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D,
+                                 int L, int64_t n, int out_len, const float* gate, int64_t g_off,
+                                 int64_t g_sb, int64_t g_sd, int64_t g_sl) {
+  WXX_REQUIRE(gate != nullptr, "wxx_fftconv_gated: gate is null");
+  return fftconv_impl(y, x, x_off, sb, sd, sl, h, h_ld, Lh, B, D, L, n, out_len, gate, g_off,
+                      g_sb, g_sd, g_sl);
+}
+
+static int fftconv_impl(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                        int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D, int L,
+                        int64_t n, int out_len, const float* gate, int64_t g_off, int64_t g_sb,
+                        int64_t g_sd, int64_t g_sl) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(ilog2_exact(n) >= 0, "wxx_fftconv: n=%lld is not a positive power of two", (long long)n);
   // spectrum rows of n/2 + 2 complex values: 16-byte aligned, so the fused
@@ -1705,7 +1838,9 @@ WXX_EXPORT int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, 
   int st = wxx_malloc(&Hs, (uint64_t)D * ld * sizeof(float2));
   if (st) return st;
   st = wxx_rfft(Hs, ld, h, h_ld, D, Lh, n);
-  if (st == WXX_OK) st = wxx_fftconv_spectrum(y, x, x_off, sb, sd, sl, Hs, ld, B, D, L, n, out_len);
+  if (st == WXX_OK)
+    st = fftconv_spectrum_impl(y, x, x_off, sb, sd, sl, Hs, ld, B, D, L, n, out_len, gate, g_off,
+                               g_sb, g_sd, g_sl);
   int st2 = wxx_free(Hs);
   return st ? st : st2;
 }

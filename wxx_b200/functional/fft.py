@@ -155,10 +155,12 @@ def irfft(tensor1, n=None):
     return out
 
 
-def fftconv(x, h, n, out_len=None):
+def fftconv(x, h, n, out_len=None, gate=None):
     """Causal FFT convolution ``irfft(rfft(x, n) * rfft(h, n), n)[..., :out_len]``
     of a (B, D, L) view ``x`` with a (D, Lh) filter ``h`` broadcast over the
-    batch, in one fused pass per row (the spectra stay on chip)."""
+    batch, in one fused pass per row (the spectra stay on chip).  With a
+    (B, D, out_len) ``gate`` view the result is ``gate * fftconv(x, h)``
+    (Hyena's ``gates[i] * fft_conv1d(z, h)``), multiplied as it is stored."""
     if len(x.shape) != 3 or len(h.shape) != 2:
         raise ValueError(f"fftconv expects x (B, D, L) and h (D, Lh), got {x.shape}, {h.shape}")
     B, D, L = x.shape
@@ -172,8 +174,20 @@ def fftconv(x, h, n, out_len=None):
     if any(s < 0 for s in x.stride):
         x = x.contiguous()
     hd = dense(h)
-    out = empty((B, D, out_len), "f32", x.requires_grad or h.requires_grad)
-    check(F.wxx_fftconv(out.buffer.ptr, x.buffer.ptr, x.offset, x.stride[0], x.stride[1],
-                        x.stride[2], hd.ptr, h.shape[1], h.shape[1], B, D, L, n, out_len),
+    if gate is None:
+        out = empty((B, D, out_len), "f32", x.requires_grad or h.requires_grad)
+        check(F.wxx_fftconv(out.buffer.ptr, x.buffer.ptr, x.offset, x.stride[0], x.stride[1],
+                            x.stride[2], hd.ptr, h.shape[1], h.shape[1], B, D, L, n, out_len),
+              "fftconv")
+        return out
+    if tuple(gate.shape) != (B, D, out_len):
+        raise ValueError(f"fftconv: gate shape {gate.shape} != {(B, D, out_len)}")
+    if any(s < 0 for s in gate.stride):
+        gate = gate.contiguous()
+    out = empty((B, D, out_len), "f32", x.requires_grad or h.requires_grad or gate.requires_grad)
+    check(F.wxx_fftconv_gated(out.buffer.ptr, x.buffer.ptr, x.offset, x.stride[0], x.stride[1],
+                              x.stride[2], hd.ptr, h.shape[1], h.shape[1], B, D, L, n, out_len,
+                              gate.buffer.ptr, gate.offset, gate.stride[0], gate.stride[1],
+                              gate.stride[2]),
           "fftconv")
     return out

@@ -94,10 +94,11 @@ class HyenaOperator(Module):
             size = _next_pow2(length)
         return size
 
-    def fft_conv1d(self, x, h):
-        """Linear convolution of (B, D, L) with (D, L), fused on the GPU."""
+    def fft_conv1d(self, x, h, gate=None):
+        """Linear convolution of (B, D, L) with (D, L), fused on the GPU; with
+        ``gate`` the result is multiplied by it in the same pass."""
         length = x.shape[-1]
-        return functional.fftconv(x, h, self._fft_size(length), out_len=length)
+        return functional.fftconv(x, h, self._fft_size(length), out_len=length, gate=gate)
 
     def _decay_window(self, stage, length):
         return autograd.decay_window(self.decay).forward(self.decay, stage, length)
@@ -114,7 +115,7 @@ class HyenaOperator(Module):
         for i in range(self.order):
             h = self.filter_mlp[i](length)
             h = h * self._decay_window(i, length)
-            z = gates[i] * self.fft_conv1d(z, h)
+            z = self.fft_conv1d(z, h, gate=gates[i])
         return self.out_proj(z.transpose(1, 2))
 
 
