@@ -575,11 +575,42 @@ def test_linear_fp32_mode_and_ragged_n_fall_back(rng):
     assert rel(got32, K.matmul_add(x, w, b)) < 1e-5
 
 
-@pytest.mark.parametrize("d,hidden", [(64, 170), (256, 682)])
+@pytest.mark.parametrize("shape", [(300, 64, 72), (1000, 256, 1376), (4096, 256, 2048),
+                                   (130, 40, 200)])
+@pytest.mark.parametrize("mode,tol", [("tf32", 2e-3), ("3xtf32", 1e-5)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_linear_swiglu_epilogue(shape, mode, tol, with_bias, rng):
+    """linear(x, W, activation='swiglu'): columns 2j, 2j+1 of x @ W (+ bias)
+    are (gate, up) and the GEMM epilogue writes silu(gate) * up, against the
+    unfused GEMM + silu + product (same GEMM sums, same silu) and the oracle.
+    Shapes cover single-SM and SM-pair tiles and ragged M / N edges."""
+    F = _w().functional
+    M, Kd, N = shape
+    x = rng.standard_normal((M, Kd)).astype(np.float32)
+    w = (rng.standard_normal((Kd, N)) / np.sqrt(Kd)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32) if with_bias else None
+    F.set_matmul_mode(mode)
+    try:
+        got = F.linear(up(x), up(w), None if b is None else up(b), activation="swiglu").numpy()
+        y = F.linear(up(x), up(w), None if b is None else up(b)).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    assert got.shape == (M, N // 2)
+    g, u = y[:, 0::2], y[:, 1::2]
+    gc = np.clip(g, -88, 88)
+    unfused = (g * (1.0 / (1.0 + np.exp(-gc)))) * u
+    assert rel(got, unfused) < 1e-5
+    yr = K.matmul_add(x, w, b)
+    gr, ur = yr[:, 0::2], yr[:, 1::2]
+    assert rel(got, gr / (1.0 + np.exp(-gr)) * ur) < 4 * tol
+
+
+@pytest.mark.parametrize("d,hidden", [(64, 170), (256, 682), (64, 128)])
 @pytest.mark.parametrize("mode,tol", [("tf32", 2e-3), ("3xtf32", 1e-5)])
 def test_swiglu_padded_hidden_matches_plain(d, hidden, mode, tol, rng):
-    """SwiGLU with a hidden width that is not a multiple of 4 runs on
-    zero-padded weights (TMA-fed GEMMs) against the plain expression.  The
+    """SwiGLU through the fused path (W1 and W2 interleaved into one GEMM with
+    the paired-GLU epilogue, hidden width padded to a multiple of 4, then W3
+    with the residual in its epilogue) against the plain expression.  The
     GEMMs may split K differently, and in TF32 mode the intermediate is then
     truncated to 10 mantissa bits, so the TF32 bound is the matmul one."""
     wxx = _w()
@@ -595,6 +626,14 @@ def test_swiglu_padded_hidden_matches_plain(d, hidden, mode, tol, rng):
         F.set_matmul_mode("tf32")
     assert got.shape == ref.shape
     assert rel(got, ref) < tol, rel(got, ref)
+    # residual fused into the last GEMM
+    r = up(rng.standard_normal((2, 300, d)).astype(np.float32))
+    F.set_matmul_mode(mode)
+    try:
+        got_r = m.forward(x, residual=r).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    assert rel(got_r, got + r.numpy()) < 1e-5   # split-K vs whole-K sums in the last GEMM
     # the padded copies follow parameter updates
     F.assign(m.w1.weight, F.from_numpy(np.zeros((d, hidden), np.float32)))
     assert np.abs(m(x).numpy()).max() == 0.0

@@ -101,6 +101,13 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return (x < -10.0f) ? 0.0f : r;
 }
 
+// silu(x) = x * sigmoid(x), sigmoid with the reference's +-88 input clamp
+// (sigmoid.wgsl:18-19); shared by the unary kernel and the GEMM's GLU epilogue.
+__device__ __forceinline__ float silu_ref(float x) {
+  const float xc = fminf(fmaxf(x, -88.0f), 88.0f);
+  return x * (1.0f / (1.0f + expf(-xc)));
+}
+
 // Records the first device-side error code; later errors are dropped so the
 // host sees the root cause.
 __device__ __forceinline__ void wxx_device_fail(int* err_word, int code) {

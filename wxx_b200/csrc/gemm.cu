@@ -111,7 +111,8 @@ bool encode_c_map(CUtensorMap* map, const GemmParams& p) {
   // split-K partials: z runs over (batch, K-slice) of the workspace
   const int zdim = p.epi.raw ? p.batch * p.splits : p.batch;
   if (zdim > 1 && (p.epi.c_bs * 4) % 16) return false;
-  cuuint64_t dims[3] = {(cuuint64_t)p.N, (cuuint64_t)p.M, (cuuint64_t)zdim};
+  const int64_t ncols = p.epi.act == 2 ? p.N / 2 : p.N;   // paired GLU halves the width
+  cuuint64_t dims[3] = {(cuuint64_t)ncols, (cuuint64_t)p.M, (cuuint64_t)zdim};
   cuuint64_t strides[2] = {(cuuint64_t)p.epi.ldc * 4,
                            (cuuint64_t)(zdim > 1 ? p.epi.c_bs : (int64_t)p.epi.ldc * p.M) * 4};
   cuuint32_t box[3] = {32, 32, 1};
@@ -144,6 +145,8 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   CUtensorMap mc;
   memset(&mc, 0, sizeof(mc));
   p.epi.tma_store = encode_c_map(&mc, p) ? 1 : 0;
+  WXX_REQUIRE(p.epi.act != 2 || p.epi.tma_store,
+              "gemm: the paired GLU epilogue needs a TMA-storable output");
   WXX_REQUIRE(p.epi.tma_store || !p.epi.raw, "gemm: split-K workspace is not TMA-storable");
   WXX_REQUIRE(p.epi.tma_store || (p.epi.act == 0 && p.epi.res == nullptr),
               "gemm: a fused activation/residual needs a TMA-storable C");
@@ -200,7 +203,7 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   // gained 8 %.
   const char* sk_env = getenv("WXX_GEMM_STREAMK");
   const int64_t waves = (tiles + pairs - 1) / pairs;
-  const bool sk = sk_env != nullptr && sk_env[0] == '1' && tiles >= pairs &&
+  const bool sk = sk_env != nullptr && sk_env[0] == '1' && p.epi.act != 2 && tiles >= pairs &&
                   (double)tiles / (double)(waves * pairs) < 0.95;
   void* ws = nullptr;
   void* flags = nullptr;
@@ -555,10 +558,11 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   // splits gathered operands on the fly.
   OperandDesc da{A, M, K, batch, lda, a_bs, trans_a == 0, a_bs == 0 && batch > 1};
   OperandDesc db{B, N, K, batch, ldb, b_bs, trans_b != 0, b_bs == 0 && batch > 1};
+  const int64_t n_out = act == 2 ? N / 2 : N;
   p.epi.kind = 0;
   p.epi.C = C;
-  p.epi.c_bs = M * N;
-  p.epi.ldc = (int)N;
+  p.epi.c_bs = M * n_out;
+  p.epi.ldc = (int)n_out;
   p.epi.bias = bias;
   p.epi.bias_mode = bias_mode;
   p.epi.bias_bs = M * N;
@@ -624,7 +628,9 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
 // Linear layer with its follow-up fused into the GEMM epilogue:
 //   C (M, N dense) = act(alpha * A @ op(B) + bias) + residual
 // A (M, K) row stride lda; B (K, N) row stride ldb, or (N, K) with trans_b = 1;
-// bias (N) or NULL; residual (M, N dense) or NULL; act 0 none, 1 GELU (tanh).
+// bias (N) or NULL; residual (M, N dense) or NULL; act 0 none, 1 GELU (tanh),
+// 2 paired GLU: product columns 2j, 2j+1 are (gate, up) of output column j,
+// C (M, N/2) = silu(gate) * up (no residual; N a multiple of 8).
 // mode 0 TF32, 1 3xTF32.  C must be 16-byte aligned and N a multiple of 4.
 WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float* bias,
                           const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
@@ -632,7 +638,9 @@ WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float*
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(M >= 0 && N >= 0 && K > 0, "wxx_linear: bad sizes (K must be positive)");
   WXX_REQUIRE(mode == 0 || mode == 1, "wxx_linear: mode %d not in {0, 1}", mode);
-  WXX_REQUIRE(act == 0 || act == 1, "wxx_linear: act %d not in {0, 1}", act);
+  WXX_REQUIRE(act >= 0 && act <= 2, "wxx_linear: act %d not in {0, 1, 2}", act);
+  WXX_REQUIRE(act != 2 || (residual == nullptr && N % 8 == 0),
+              "wxx_linear: the paired GLU takes no residual and needs N a multiple of 8");
   WXX_REQUIRE(!(reinterpret_cast<uintptr_t>(C) & 15) && N % 4 == 0,
               "wxx_linear: C must be 16-byte aligned with N a multiple of 4");
   if (M * N == 0) return WXX_OK;

@@ -357,7 +357,7 @@ struct EpiParams {
   int hw_out;             // conv: Ho*Wo
   int tma_store;          // kind 0 with bias_mode <= 1: C written by TMA stores
   // TMA-store path only: C = act(alpha * AB + bias) + res
-  int act;                // 0 none, 1 GELU (tanh form)
+  int act;                // 0 none, 1 GELU (tanh form), 2 paired GLU (C has N/2 columns)
   const float* res;       // residual (M, N) per batch, or NULL
   int64_t res_ld, res_bs;
   int raw;                // split-K: raw partial sums to the workspace map, z = batch * splits + slice
@@ -757,6 +757,21 @@ __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, in
   }
 }
 
+// act == 2 (paired GLU): product columns 2j and 2j+1 are the gate and the up
+// projection of output column j, out[j] = silu(gate) * up.  v holds product
+// columns n0 .. n0+31 and w columns n0+32 .. n0+63, both after alpha and
+// bias; on return v holds output columns n0/2 .. n0/2 + 31.
+__device__ __forceinline__ void epi_glu(float (&v)[32], const float (&w)[32]) {
+  float o[32];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    o[j] = silu_ref(v[2 * j]) * v[2 * j + 1];
+    o[16 + j] = silu_ref(w[2 * j]) * w[2 * j + 1];
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = o[j];
+}
+
 // ------------------------------------------------------------ the kernel
 
 template <int BN>
@@ -919,18 +934,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int m0 = tm * BM + quarter * 32;
       uint32_t row_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      const bool glu = p.epi.act == 2;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < BN; c += glu ? 64 : 32) {
         float v[32];
         tmem_ld_32x32(row_addr + (uint32_t)c, v);
         int n0 = tn * BN + c;
         if (n0 >= p.N) continue;
+        int nc = n0;  // output column of v[0]
+        if (glu) {
+          float w[32];
+          tmem_ld_32x32(row_addr + (uint32_t)(c + 32), w);
+          epi_apply(p, bt, m0 + lane, n0, v);
+          epi_apply(p, bt, m0 + lane, n0 + 32, w);
+          epi_glu(v, w);
+          nc = n0 / 2;
+        }
         if (use_tma) {
           // alpha, bias, activation and residual in registers, row ->
           // swizzled staging tile, one TMA store per 32 x 32 chunk (clipped
           // at the edges).
           // (split-K: raw partial sums, slice index as the z coordinate)
-          if (!p.epi.raw) epi_apply(p, bt, m0 + lane, n0, v);
+          if (!p.epi.raw && !glu) epi_apply(p, bt, m0 + lane, n0, v);
           uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
           if (lane == 0) bulk_wait_read<1>();  // the store that used `buf` has read it
           __syncwarp();
@@ -942,7 +967,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tm_c, smem_u32(buf), n0, m0, p.epi.raw ? bt * p.splits + sp : bt);
+            tma_store_3d(&tm_c, smem_u32(buf), nc, m0, p.epi.raw ? bt * p.splits + sp : bt);
             bulk_commit();
           }
           ++chunk_seq;
@@ -1295,12 +1320,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
         if (!ready) break;
         prow = p.sk_ws + (((int64_t)(pair - 1) * 2 + rank) * 4 + quarter) * (32 * BN);
       }
+      const bool glu = p.epi.act == 2;  // never with stream-K partials (host)
 #pragma unroll 1
-      for (int c = 0; c < BN && m0 < p.M; c += 32) {
+      for (int c = 0; c < BN && m0 < p.M; c += glu ? 64 : 32) {
         const int n0 = tn * BN + c;
         if (n0 >= p.N) break;
         float v[32];
         tmem_ld_32x32(row_addr + (uint32_t)c, v);
+        int nc = n0;
+        if (glu) {
+          float w[32];
+          tmem_ld_32x32(row_addr + (uint32_t)(c + 32), w);
+          epi_apply(p, bt, m0 + lane, n0, v);
+          epi_apply(p, bt, m0 + lane, n0 + 32, w);
+          epi_glu(v, w);
+          nc = n0 / 2;
+        }
         if (prow != nullptr) {
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
@@ -1311,7 +1346,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
             v[4 * q + 3] += w.w;
           }
         }
-        epi_apply(p, bt, m0 + lane, n0, v);
+        if (!glu) epi_apply(p, bt, m0 + lane, n0, v);
         uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
         if (lane == 0) bulk_wait_read<1>();
         __syncwarp();
@@ -1322,7 +1357,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_3d(&tm_c, smem_u32(buf), n0, m0, bt);
+          tma_store_3d(&tm_c, smem_u32(buf), nc, m0, bt);
           bulk_commit();
         }
         ++chunk_seq;

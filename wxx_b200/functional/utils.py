@@ -199,25 +199,34 @@ def matmul_add(tensor1, tensor2, tensor3, transpose_A=False, transpose_B=False, 
     return out
 
 
+_ACTIVATIONS = {None: 0, "gelu": 1, "swiglu": 2}
+
+
 def linear(x, weight, bias=None, *, activation=None, residual=None):
     """``act(x @ weight + bias) + residual`` with the activation and the
     residual add fused into the GEMM epilogue.
 
     ``x`` (..., K), ``weight`` (K, N) (nn.Linear layout), ``bias`` (N,) or
-    None, ``activation`` None or ``"gelu"`` (tanh form), ``residual`` shaped
-    like the output or None.  The result has the same bits as
-    ``matmul_add`` followed by ``gelu`` / ``residual + y``, which is the path
-    taken when the fused form does not apply (fp32 SIMT mode, N not a
+    None, ``residual`` shaped like the output or None.  ``activation``:
+    None, ``"gelu"`` (tanh form) or ``"swiglu"``: the weight's columns 2j and
+    2j+1 hold the gate and the up projection of output column j, and the
+    (..., N/2) result is ``silu(gate) * up`` (SwiGLU's ``silu(x W1) * (x W2)``
+    from one GEMM; no residual).  The result has the same bits as
+    ``matmul_add`` followed by the activation / ``residual + y``, which is the
+    path taken when the fused form does not apply (fp32 SIMT mode, N not a
     multiple of 4, 3xTF32 with K > 1024)."""
-    if activation not in (None, "gelu"):
-        raise ValueError(f"activation must be None or 'gelu', got {activation!r}")
+    if activation not in _ACTIVATIONS:
+        raise ValueError(f"activation must be None, 'gelu' or 'swiglu', got {activation!r}")
     a = dense(x)
     w = dense(weight)
     K = a.shape[-1]
     N = w.shape[-1]
     if len(w.shape) != 2 or w.shape[0] != K:
         raise ValueError(f"linear: weight {tuple(w.shape)} does not match input {tuple(a.shape)}")
-    out_shape = list(a.shape[:-1]) + [N]
+    glu = activation == "swiglu"
+    if glu and (N % 2 or residual is not None):
+        raise ValueError("linear: 'swiglu' needs an even output width and no residual")
+    out_shape = list(a.shape[:-1]) + [N // 2 if glu else N]
     if bias is not None and tuple(bias.shape) != (N,):
         raise ValueError(f"linear: bias {tuple(bias.shape)} is not ({N},)")
     if residual is not None and list(residual.shape) != out_shape:
@@ -226,10 +235,13 @@ def linear(x, weight, bias=None, *, activation=None, residual=None):
     M = int(math.prod(a.shape[:-1])) if len(a.shape) > 1 else 1
     # 3xTF32 products with K > 1024 are summed in slices (split-K) to bound
     # the tensor-core accumulation chain; that path has no fused epilogue.
-    if mode not in (0, 1) or N % 4 or K == 0 or (mode == 1 and K > 1024):
+    if (mode not in (0, 1) or N % (8 if glu else 4) or K == 0 or (mode == 1 and K > 1024)):
         y = matmul_add(x, weight, bias)
         if activation == "gelu":
             y = y.gelu()
+        elif glu:
+            from .activations import silu
+            y = silu(y[..., 0::2]) * y[..., 1::2]
         return y if residual is None else residual + y
     requires_grad = (x.requires_grad or weight.requires_grad
                      or (bias is not None and bias.requires_grad)
@@ -242,8 +254,8 @@ def linear(x, weight, bias=None, *, activation=None, residual=None):
     timer = active_timer()
     ev0 = timer.start() if timer is not None else None
     check(F.wxx_linear(out.buffer.ptr, a.ptr, w.ptr, None if b is None else b.ptr,
-                       None if r is None else r.ptr, M, N, K, K, N, 0,
-                       1 if activation == "gelu" else 0, 1.0, mode), "linear")
+                       None if r is None else r.ptr, M, N, K, K, N, 0, _ACTIVATIONS[activation],
+                       1.0, mode), "linear")
     if timer is not None:
         timer.stop(ev0, 2.0 * M * N * K, f"{M}x{N}x{K}")
     return out

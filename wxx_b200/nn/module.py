@@ -432,33 +432,38 @@ class SwiGLU(Module):
         self.w2 = Linear(d_model, hidden_dim, bias=False)
         self.w3 = Linear(hidden_dim, d_model, bias=False)
 
-    def forward(self, x):
-        h = self.hidden_dim
-        if h % 4 and functional.get_matmul_mode() != "fp32" and len(x.shape) >= 2:
-            return self._forward_padded(x)
-        return self.w3(functional.silu(self.w1(x)) * self.w2(x))
+    def forward(self, x, residual=None):
+        """``w3(silu(w1 x) * w2 x)`` (+ ``residual``, fused into the last GEMM)."""
+        mode = functional.get_matmul_mode()
+        d_in = self.w1.weight.shape[0]
+        if mode != "fp32" and len(x.shape) >= 2 and (mode == "tf32" or d_in <= 1024):
+            return self._forward_fused(x, residual)
+        y = self.w3(functional.silu(self.w1(x)) * self.w2(x))
+        return y if residual is None else residual + y
 
-    def _forward_padded(self, x):
-        """Same product with the hidden width rounded up to a multiple of 4, so
-        every operand row is 16-byte aligned and the GEMMs are TMA-fed.  The
-        weights are copied each call into zero-padded buffers owned by the
-        module: the extra columns give silu(0) * 0 = 0 and meet zero rows of
-        W3, which is what the GEMM's K tail reads anyway."""
+    def _forward_fused(self, x, residual):
+        """Two GEMMs instead of three plus two elementwise passes: W1 and W2
+        interleaved column by column into one weight, whose GEMM epilogue
+        writes silu(x W1) * (x W2) directly (``linear(..., "swiglu")``), then
+        W3 with the residual add in its epilogue.  The hidden width is rounded
+        up to a multiple of 4 so every operand row is 16-byte aligned: the
+        extra columns hold zero weights (silu(0) * 0 = 0) and meet zero rows of
+        W3.  The weights are copied each call into buffers owned by the
+        module."""
         h = self.hidden_dim
         hp = (h + 3) // 4 * 4
         d_in = self.w1.weight.shape[0]
         d_out = self.w3.weight.shape[1]
-        cache = self.__dict__.get("_pad_cache")
+        cache = self.__dict__.get("_glu_cache")
         if cache is None or cache[0] != hp:
-            cache = (hp, Tensor((d_in, hp), value=0.0), Tensor((d_in, hp), value=0.0),
-                     Tensor((hp, d_out), value=0.0))
-            object.__setattr__(self, "_pad_cache", cache)
-        _, w1p, w2p, w3p = cache
-        functional.assign(w1p.narrow(1, 0, h), self.w1.weight)
-        functional.assign(w2p.narrow(1, 0, h), self.w2.weight)
+            cache = (hp, Tensor((d_in, 2 * hp), value=0.0), Tensor((hp, d_out), value=0.0))
+            object.__setattr__(self, "_glu_cache", cache)
+        _, w12, w3p = cache
+        functional.assign(w12[:, 0:2 * h:2], self.w1.weight)
+        functional.assign(w12[:, 1:2 * h:2], self.w2.weight)
         functional.assign(w3p.narrow(0, 0, h), self.w3.weight)
-        g = functional.silu(functional.linear(x, w1p)) * functional.linear(x, w2p)
-        return functional.linear(g, w3p)
+        g = functional.linear(x, w12, activation="swiglu")
+        return functional.linear(g, w3p, residual=residual)
 
 
 class TiedLinear(Module):
