@@ -203,14 +203,14 @@ SWEEPS["softmax"] = Sweep("softmax", [(64, 8, 1024, 1024)], lambda F, x: F.softm
 SWEEPS["fftconv"] = Sweep("fftconv", [(16, 256, 16384), (256, 16384)],
                           lambda F, x, h: F.fftconv(x, h, 32768, out_len=16384),
                           528 * 2 ** 20, "GB/s", "hbm",
-                          "fft_row_kernel<14, conv> (+ rfft of h)", flush_l2=False)
+                          "fft_pair_kernel<14, conv> (+ rfft of h)", flush_l2=False)
 # Hyena's fft_conv1d at the hyena workload's shape (B 16, D 256, L 8192,
 # n 16384): x and y once each (128 MiB each), h once (8 MiB), its spectrum
 # written and read (2 x 16 MiB).
 SWEEPS["fftconv_hyena"] = Sweep("fftconv_hyena", [(16, 256, 8192), (256, 8192)],
                                 lambda F, x, h: F.fftconv(x, h, 16384, out_len=8192),
                                 296 * 2 ** 20, "GB/s", "hbm",
-                                "fft_row_kernel<13, conv> (+ rfft of h)", flush_l2=False)
+                                "fft_conv_staged_kernel<13> (+ rfft of h)", flush_l2=False)
 # GPT2-scaled attention core (B 8, S 1024, 16 heads x 64, causal): useful
 # FLOPs are the two products over the S(S+1)/2 unmasked (query, key) pairs.
 SWEEPS["attention"] = Sweep("attention", [(8, 1024, 1024)] * 3,

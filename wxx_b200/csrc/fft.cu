@@ -1287,7 +1287,9 @@ __device__ __forceinline__ void pp_mirror(PBuf src, PBuf dst, const float2* __re
 
 // Last inverse pass (radix R, NS = N/R) to the real output row:
 // y[2m] + i y[2m+1] = conj(W[m]) / N.
-template <int N, int R, int T, bool GSHARED = false>
+constexpr int kGateNone = 0, kGateGlobal = 1, kGateShared = 2;
+
+template <int N, int R, int T, int GATE = kGateNone>
 __device__ __forceinline__ void pp_last(PBuf src, const float* __restrict__ tw, float* y,
                                         int olen, bool vec, const float* g = nullptr,
                                         int64_t g_st = 1, bool gvec = false) {
@@ -1306,10 +1308,10 @@ __device__ __forceinline__ void pp_last(PBuf src, const float* __restrict__ tw, 
         if (t0 >= olen) break;
         float4 o = make_float4(p_lo(v[r].re) * scale, -p_lo(v[r].im) * scale,
                                p_hi(v[r].re) * scale, -p_hi(v[r].im) * scale);
-        if (g != nullptr) {
+        if (GATE != kGateNone) {
           if (gvec && t0 + 3 < olen) {
-            const float4 gv = GSHARED ? *reinterpret_cast<const float4*>(g + t0)
-                                      : __ldg(reinterpret_cast<const float4*>(g + t0));
+            const float4 gv = GATE == kGateShared ? *reinterpret_cast<const float4*>(g + t0)
+                                                  : __ldg(reinterpret_cast<const float4*>(g + t0));
             o = make_float4(o.x * gv.x, o.y * gv.y, o.z * gv.z, o.w * gv.w);
           } else {
             o.x *= g[(int64_t)t0 * g_st];
@@ -1398,8 +1400,12 @@ __global__ void __launch_bounds__(PCfg<L>::T, 1) fft_pair_kernel(RowArgs a) {
   const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   bool gvec;
   const float* g = MODE == kModeConv ? gate_row(a, b, d, gvec) : nullptr;
-  pp_last<N, pp_radix_inv(L, 0, P - 1), T>(bufs[CUR_LAST], g_fft_ptw + pt_inv_off(L, 0, P - 1), y,
-                                           a.out_len, vec, g, a.g_st, gvec);
+  if (g != nullptr)
+    pp_last<N, pp_radix_inv(L, 0, P - 1), T, kGateGlobal>(
+        bufs[CUR_LAST], g_fft_ptw + pt_inv_off(L, 0, P - 1), y, a.out_len, vec, g, a.g_st, gvec);
+  else
+    pp_last<N, pp_radix_inv(L, 0, P - 1), T>(bufs[CUR_LAST], g_fft_ptw + pt_inv_off(L, 0, P - 1),
+                                             y, a.out_len, vec);
 }
 
 // Persistent fused convolution for L <= 13 with the next row's inputs staged
@@ -1504,16 +1510,19 @@ __global__ void __launch_bounds__(SCfg<L>::T, 1)
     pp_inv_middle<L, V, T, false, 1, 0>(bufs);
     float* y = a.out + row * a.out_ld;
     const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    const float* tl = g_fft_ptw + pt_inv_off(L, V, P - 1);
     if (glen > 0) {
       ok = wxx_tc::mbar_wait(&bars[2], phase, &abort_flag, err);
       if (__syncthreads_or(!ok)) return;
-      pp_last<N, pp_radix_inv(L, V, P - 1), T, true>(bufs[0], g_fft_ptw + pt_inv_off(L, V, P - 1),
-                                                     y, a.out_len, vec, sg, 1, true);
-    } else {
+      pp_last<N, pp_radix_inv(L, V, P - 1), T, kGateShared>(bufs[0], tl, y, a.out_len, vec, sg, 1,
+                                                            true);
+    } else if (a.gate != nullptr) {
       bool gvec;
       const float* g = gate_row(a, b, d, gvec);
-      pp_last<N, pp_radix_inv(L, V, P - 1), T>(bufs[0], g_fft_ptw + pt_inv_off(L, V, P - 1), y,
-                                               a.out_len, vec, g, a.g_st, gvec);
+      pp_last<N, pp_radix_inv(L, V, P - 1), T, kGateGlobal>(bufs[0], tl, y, a.out_len, vec, g,
+                                                            a.g_st, gvec);
+    } else {
+      pp_last<N, pp_radix_inv(L, V, P - 1), T>(bufs[0], tl, y, a.out_len, vec);
     }
     __syncthreads();  // the next row's first pass overwrites the buffer
     if (glen > 0 && threadIdx.x == 0 && nxt < rows) {
