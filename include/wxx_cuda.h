@@ -173,6 +173,26 @@ int wxx_linear(float* C, const float* A, const float* B, const float* bias,
 int wxx_conv2d(float* Y, const float* X, const float* W, const float* bias, int B, int Cin,
                int H, int Wd, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int dh,
                int dw, int mode);
+/* nn/resnet.py:31-79 ResBlock's conv -> BatchNorm (eval, functional/normalization.py:148-206)
+ * (-> + shortcut) -> relu in the conv's epilogue: Y = relu?(bn(conv(X) + bias) + residual).
+ * rm == NULL: no batchnorm; residual NCHW like Y or NULL; relu 0/1.  Same values as the
+ * separate kernels. */
+int wxx_conv2d_bn(float* Y, const float* X, const float* W, const float* bias, int B, int Cin,
+                  int H, int Wd, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int dh,
+                  int dw, int mode, const float* rm, const float* rv, const float* gamma,
+                  const float* beta, float eps, const float* residual, int relu);
+/* The same convolution + follow-up ops on channels-last tensors: X (B, H, W, Cin) NHWC,
+ * W (Cout, Cin, KH, KW) as above, residual and Y (B, Ho, Wo, Cout) NHWC.  The A operand is
+ * fetched by 4-D TMA boxes (one filter tap x 32 channels x a 128-pixel output tile per
+ * K-block).  Needs Cin % 32 == 0, Cout % 4 == 0, 16-byte aligned X / Y and 128-pixel output
+ * tiles that are boxes (Wo a multiple of 128, or Wo | 128 and Ho a multiple or divisor of
+ * 128 / Wo); else WXX_E_ARG.  No reference counterpart for the layout (the reference is NCHW
+ * throughout); ResNet uses it between its stem and its pooling. */
+int wxx_conv2d_nhwc(float* Y, const float* X, const float* W, const float* bias, int B, int Cin,
+                    int H, int Wd, int Cout, int KH, int KW, int sh, int sw, int ph, int pw,
+                    int dh, int dw, int mode, const float* rm, const float* rv,
+                    const float* gamma, const float* beta, float eps, const float* residual,
+                    int relu);
 
 /* nn/module.py:460-495 MultiHeadAttention core fused (QK^T * scale (+ mask), softmax, PV)
  * on tcgen05 TF32.  Q (B, Sq, H, hd) row stride q_ld, K/V (B, Sk, H, hd) row stride kv_ld,

@@ -390,6 +390,102 @@ def test_conv2d(shape, mode, rng):
     assert rel(got, ref) < (2e-3 if mode == "tf32" else 1e-5)
 
 
+@pytest.mark.parametrize("shape", CONV_SHAPES)
+@pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
+@pytest.mark.parametrize("post", ["bn", "bn_relu", "bn_res_relu"])
+def test_conv2d_bn_epilogue(shape, mode, post, rng):
+    """conv2d_bn: eval batchnorm (+ residual) (+ relu) in the conv epilogue or
+    the split-K reduce, against the separate conv2d / batchnorm / add / relu
+    ops on the same inputs (same fp32 operations, so equal up to the
+    compiler's choice of fused multiply-adds)."""
+    F = _w().functional
+    B, C, H, W, O, k, s, p, d = shape
+    x = rng.standard_normal((B, C, H, W)).astype(np.float32)
+    w = (rng.standard_normal((O, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    rm = rng.standard_normal(O).astype(np.float32)
+    rv = rng.uniform(0.5, 2.0, O).astype(np.float32)
+    g = rng.standard_normal(O).astype(np.float32)
+    b = rng.standard_normal(O).astype(np.float32)
+    rmt, rvt, gt, bt = up(rm), up(rv), up(g), up(b)
+    F.set_matmul_mode(mode)
+    try:
+        y = F.conv2d(up(x), up(w), (s, s), (p, p), (d, d))
+        ref, _, _ = F.batchnorm(y, gt, bt, rmt, rvt, False)
+        res = None
+        if post == "bn_res_relu":
+            res = up(rng.standard_normal(tuple(y.shape)).astype(np.float32))
+            ref = ref + res
+        if post != "bn":
+            ref = F.relu(ref)
+        got = F.conv2d_bn(up(x), up(w), (s, s), (p, p), (d, d), bn=(rmt, rvt, gt, bt, 1e-5),
+                          residual=res, relu=post != "bn").numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    ref = ref.numpy()
+    assert got.shape == ref.shape
+    assert np.abs(got - ref).max() <= 1e-6 * max(1.0, np.abs(ref).max())
+
+
+NHWC_SHAPES = [
+    # B, Cin, H, W, Cout, k, stride, pad, dil
+    (8, 64, 8, 8, 64, 3, 1, 1, 1),
+    (3, 64, 8, 8, 64, 3, 1, 1, 1),        # partial last tile
+    (8, 64, 8, 8, 128, 3, 2, 1, 1),
+    (8, 64, 8, 8, 128, 1, 2, 0, 1),
+    (4, 256, 2, 2, 512, 3, 2, 1, 1),
+    (2, 32, 16, 16, 32, 3, 1, 2, 2),
+    (1, 32, 3, 256, 32, 3, 1, 1, 1),       # Wo = 256: one row per tile
+    (16, 256, 4, 4, 512, 3, 1, 1, 1),      # split-K
+    (32, 512, 1, 1, 512, 3, 1, 1, 1),
+    (16, 128, 4, 4, 256, 3, 2, 1, 1),
+]
+
+
+@pytest.mark.parametrize("shape", NHWC_SHAPES)
+@pytest.mark.parametrize("mode,tol", [("tf32", 2e-3), ("3xtf32", 1e-5)])
+@pytest.mark.parametrize("post", ["none", "bn_relu", "bn_res_relu"])
+def test_conv2d_nhwc(shape, mode, tol, post, rng):
+    """Channels-last convolution (TMA-box A operand) with its batchnorm /
+    residual / ReLU epilogue against the oracle's NCHW convolution."""
+    F = _w().functional
+    B, C, H, W, O, k, s, p, d = shape
+    x = rng.standard_normal((B, C, H, W)).astype(np.float32)
+    w = (rng.standard_normal((O, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    y = K.conv2d(x, w, (s, s), (p, p), (d, d), None).astype(np.float64)
+    bn = res_t = None
+    if post != "none":
+        rm = rng.standard_normal(O).astype(np.float32)
+        rv = rng.uniform(0.5, 2.0, O).astype(np.float32)
+        g = rng.standard_normal(O).astype(np.float32)
+        b = rng.standard_normal(O).astype(np.float32)
+        bn = (up(rm), up(rv), up(g), up(b), 1e-5)
+        sc = lambda v: v[None, :, None, None]
+        y = (y - sc(rm)) / np.sqrt(sc(rv).astype(np.float64) + 1e-5) * sc(g) + sc(b)
+        if post == "bn_res_relu":
+            r = rng.standard_normal(y.shape).astype(np.float32)
+            res_t = up(np.ascontiguousarray(r.transpose(0, 2, 3, 1)))
+            y = y + r
+        y = np.maximum(y, 0.0)
+    xh = up(np.ascontiguousarray(x.transpose(0, 2, 3, 1)))
+    F.set_matmul_mode(mode)
+    try:
+        got = F.conv2d_nhwc(xh, up(w), (s, s), (p, p), (d, d), bn=bn, residual=res_t,
+                            relu=post != "none").numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    assert got.shape == (B, y.shape[2], y.shape[3], O)
+    assert rel(got.transpose(0, 3, 1, 2), y) < tol
+
+
+def test_conv2d_nhwc_rejects_unsupported(rng):
+    F = _w().functional
+    x = up(rng.standard_normal((2, 7, 7, 64)).astype(np.float32))
+    w = up(rng.standard_normal((64, 64, 3, 3)).astype(np.float32))
+    assert not F.conv2d_nhwc_supported(64, 64, 7, 7)
+    with pytest.raises(ValueError):
+        F.conv2d_nhwc(x, w, (1, 1), (1, 1), (1, 1))
+
+
 def test_pooling(rng):
     F = _w().functional
     x = rng.standard_normal((4, 6, 16, 16)).astype(np.float32)

@@ -278,7 +278,7 @@ int choose_splits(int64_t tiles, int total_kb) {
 __global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restrict__ ws,
                                      int splits, int batch, int M, int N, float alpha,
                                      const float* __restrict__ bias, int bias_mode, int kind,
-                                     int64_t ldc, int64_t c_bs, int hw) {
+                                     int64_t ldc, int64_t c_bs, int hw, ConvPost post) {
   const int64_t MN = (int64_t)M * N;
   const int64_t total = MN * batch;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -304,10 +304,12 @@ __global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restr
       else v += bias[b * MN + src];
     }
     if (kind == 0) {
-      C[b * c_bs + m * ldc + n] = v;
+      const int64_t o = b * c_bs + m * ldc + n;
+      C[o] = conv_post(post, v, (int)n, o);
     } else {
       const int64_t img = m / hw, pix = m - img * hw;
-      C[(img * N + n) * hw + pix] = v;
+      const int64_t o = (img * N + n) * hw + pix;
+      C[o] = conv_post(post, v, (int)n, o);
     }
   }
 }
@@ -358,12 +360,16 @@ int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUten
   p.epi.bias_mode = 0;
   p.epi.alpha = 1.0f;
   p.epi.raw = 1;
+  p.epi.act = 0;
+  p.epi.res = nullptr;
+  memset(&p.epi.post, 0, sizeof(p.epi.post));
   st = run_tc(bn, a0, a1, b0, b1, p);
   if (st == WXX_OK) {
     splitk_reduce_kernel<<<wxx::grid_for(MN * p.batch, 256), 256, 0, wxx::stream()>>>(
         real.C, (const float*)ws, p.splits, p.batch, p.M, p.N, real.alpha,
         real.bias_mode ? real.bias : nullptr, real.bias_mode, real.kind,
-        real.kind == 0 ? (int64_t)real.ldc : 0, real.kind == 0 ? real.c_bs : 0, real.hw_out);
+        real.kind == 0 ? (int64_t)real.ldc : 0, real.kind == 0 ? real.c_bs : 0, real.hw_out,
+        real.post);
     cudaError_t e = cudaGetLastError();
     wxx::count_launch();
     if (e != cudaSuccess) {
@@ -651,9 +657,211 @@ WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float*
 // Y (NCHW [B, Cout, Ho, Wo]) = conv2d(X [B, Cin, H, W], Wt [Cout, Cin, KH, KW]) (+ bias[Cout])
 // with stride (sh, sw), padding (ph, pw), dilation (dh, dw);
 // Ho = (H + 2ph - dh(KH-1) - 1)/sh + 1.  mode: 0 TF32, 1 3xTF32, 2 fp32 (3xTF32 path).
+namespace {
+int conv2d_impl(float* Y, const float* X, const float* Wt, const float* bias, int B, int Cin, int H,
+                int W, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw,
+                int mode, const ConvPost& post);
+
+// W (Cout, Cin, KH*KW) -> Wr (Cout, KH*KW, Cin): the NHWC convolution's K order.
+__global__ void conv_weight_reorder_kernel(float* __restrict__ wr, const float* __restrict__ w,
+                                           int cout, int cin, int taps) {
+  const int64_t total = (int64_t)cout * cin * taps;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = i / ((int64_t)cin * taps);
+    const int r = (int)(i - o * cin * taps);
+    const int t = r / cin, c = r - t * cin;
+    wr[i] = w[(o * cin + c) * taps + t];
+  }
+}
+
+// 128-pixel output tiles as one TMA box (W, H, images) of output positions;
+// false when the output geometry does not split that way.
+bool nhwc_box(int Ho, int Wo, int* bw, int* bh, int* bb) {
+  if (Wo >= BM) {
+    if (Wo % BM) return false;
+    *bw = BM; *bh = 1; *bb = 1;
+    return true;
+  }
+  if (BM % Wo) return false;
+  const int rows = BM / Wo;
+  *bw = Wo;
+  if (Ho >= rows) {
+    if (Ho % rows) return false;
+    *bh = rows; *bb = 1;
+    return true;
+  }
+  if (rows % Ho) return false;
+  *bh = Ho; *bb = rows / Ho;
+  return true;
+}
+
+// 4-D map of an NHWC tensor (C, W, H, B) for the conv operand: boxes of 32
+// channels x bw x bh x bb positions, W and H traversed with the conv stride.
+bool encode_nhwc_map(CUtensorMap* map, const float* base, int C, int W, int H, int B, int bw,
+                     int bh, int bb, int sw, int sh) {
+  auto enc = get_encode();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) || C % 32) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)C * 4, (cuuint64_t)W * C * 4, (cuuint64_t)H * W * C * 4};
+  cuuint32_t box[4] = {32, (cuuint32_t)(bw * sw), (cuuint32_t)(bh * sh), (cuuint32_t)bb};
+  cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
+  if (box[1] > 256 || box[2] > 256 || box[3] > 256 || sw > 8 || sh > 8) return false;
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+// NHWC convolution with the same follow-up ops as wxx_conv2d_bn:
+//   Y (B, Ho, Wo, Cout) = relu?(bn(conv(X) + bias) + residual)
+// X (B, H, W, Cin) NHWC, W (Cout, Cin, KH, KW) as in the reference, residual
+// NHWC like Y or NULL.  An implicit GEMM whose A operand is fetched by TMA:
+// each K-block is 32 channels of one filter tap and each 128-row tile one 4-D
+// box of X (padding read as zeros, the stride as the box's traversal
+// stride), so nothing is gathered by threads.  Requires Cin % 32 == 0,
+// Cout % 4 == 0, 16-byte aligned X and Y, and an output geometry whose
+// 128-pixel tiles are boxes (Wo a multiple of 128, or Wo dividing 128 and Ho
+// a multiple or a divisor of 128 / Wo); else WXX_E_ARG.
+WXX_EXPORT int wxx_conv2d_nhwc(float* Y, const float* X, const float* Wt, const float* bias, int B,
+                               int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw,
+                               int ph, int pw, int dh, int dw, int mode, const float* rm,
+                               const float* rv, const float* gamma, const float* beta, float eps,
+                               const float* residual, int relu) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(B >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0 && KH > 0 && KW > 0,
+              "wxx_conv2d_nhwc: bad sizes");
+  WXX_REQUIRE(sh > 0 && sw > 0 && dh > 0 && dw > 0 && ph >= 0 && pw >= 0,
+              "wxx_conv2d_nhwc: bad stride/padding/dilation");
+  WXX_REQUIRE(rm == nullptr || (rv && gamma && beta),
+              "wxx_conv2d_nhwc: batchnorm needs mean, variance, gamma and beta");
+  const int Ho = (H + 2 * ph - dh * (KH - 1) - 1) / sh + 1;
+  const int Wo = (W + 2 * pw - dw * (KW - 1) - 1) / sw + 1;
+  WXX_REQUIRE(Ho > 0 && Wo > 0, "wxx_conv2d_nhwc: empty output");
+  int bw = 0, bh = 0, bb = 0;
+  WXX_REQUIRE(Cin % 32 == 0 && Cout % 4 == 0 && nhwc_box(Ho, Wo, &bw, &bh, &bb) &&
+                  !(reinterpret_cast<uintptr_t>(X) & 15) && !(reinterpret_cast<uintptr_t>(Y) & 15),
+              "wxx_conv2d_nhwc: unsupported geometry (Cin %% 32, Cout %% 4, 128-pixel boxes, "
+              "alignment)");
+  const int64_t Mrows = (int64_t)B * Ho * Wo;
+  const int64_t K = (int64_t)Cin * KH * KW;
+  WXX_REQUIRE(Mrows < (int64_t(1) << 31) && K < (int64_t(1) << 31), "wxx_conv2d_nhwc: too large");
+  if (Mrows == 0) return WXX_OK;
+  cudaStream_t s = wxx::stream();
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = (int)Mrows;
+  p.N = Cout;
+  p.K = (int)K;
+  p.batch = 1;
+  p.num_kb = (int)(K / BK);
+  p.passes = mode == 0 ? 1 : 3;
+  p.splits = 1;
+  p.kb_per_split = p.num_kb * p.passes;
+  p.err = wxx::device_error_word();
+  const int bn = pick_bn(Mrows, Cout, 1);
+  // B: the weights reordered to (Cout, tap, Cin), K-major
+  void* wr = nullptr;
+  void* lo_x = nullptr;
+  void* lo_w = nullptr;
+  int st = wxx_malloc(&wr, (uint64_t)Cout * K * sizeof(float));
+  if (st) return st;
+  conv_weight_reorder_kernel<<<wxx::grid_for((int64_t)Cout * K, 256), 256, 0, s>>>(
+      (float*)wr, Wt, Cout, Cin, KH * KW);
+  wxx::count_launch();
+  CUtensorMap ma0, ma1, mb0, mb1;
+  memset(&ma0, 0, sizeof(ma0));
+  memset(&mb0, 0, sizeof(mb0));
+  OperandDesc db{(const float*)wr, Cout, K, 1, K, 0, true, false};
+  setup_operand(db, bn, true, p.b, &mb0);
+  // A: the NHWC input through 4-D boxes
+  memset(&p.a, 0, sizeof(p.a));
+  p.a.kind = 4;
+  p.a.cin = Cin; p.a.h = H; p.a.w = W; p.a.kh = KH; p.a.kw = KW;
+  p.a.sh = sh; p.a.sw = sw; p.a.ph = ph; p.a.pw = pw; p.a.dh = dh; p.a.dw = dw;
+  p.a.ho = Ho; p.a.wo = Wo;
+  bool ok = p.b.kind == 0 && encode_nhwc_map(&ma0, X, Cin, W, H, B, bw, bh, bb, sw, sh);
+  ma1 = ma0;
+  mb1 = mb0;
+  if (ok && mode != 0) {
+    // 3xTF32: the low parts of both operands, precomputed
+    const int64_t nx = (int64_t)B * H * W * Cin;
+    st = wxx_malloc(&lo_x, (uint64_t)nx * sizeof(float));
+    if (st == WXX_OK) {
+      tf32_residual_kernel<<<wxx::grid_for(nx / 4 + 1, 256), 256, 0, s>>>((float*)lo_x, X, nx);
+      wxx::count_launch();
+      ok = encode_nhwc_map(&ma1, (const float*)lo_x, Cin, W, H, B, bw, bh, bb, sw, sh);
+      if (ok) st = make_residual(db, p.b, bn, &mb1, &lo_w);
+    }
+  }
+  if (st == WXX_OK && !ok) {
+    wxx::set_error("wxx_conv2d_nhwc: tensor maps could not be encoded");
+    st = WXX_E_ARG;
+  }
+  if (st == WXX_OK) {
+    p.epi.kind = 0;
+    p.epi.C = Y;
+    p.epi.ldc = Cout;
+    p.epi.c_bs = Mrows * Cout;
+    p.epi.bias = bias;
+    p.epi.bias_mode = bias ? 1 : 0;
+    p.epi.alpha = 1.0f;
+    p.epi.res = residual;
+    p.epi.res_ld = Cout;
+    p.epi.res_bs = Mrows * Cout;
+    p.epi.post.rm = rm;
+    p.epi.post.rv = rv;
+    p.epi.post.g = gamma;
+    p.epi.post.b = beta;
+    p.epi.post.eps = eps;
+    p.epi.post.res = residual;   // read by the split-K reduce
+    p.epi.post.relu = relu ? 1 : 0;
+    st = plan_splits(p, bn) ? run_splitk(bn, ma0, ma1, mb0, mb1, p)
+                            : run_tc(bn, ma0, ma1, mb0, mb1, p);
+  }
+  // stream-ordered frees: valid for the kernels just enqueued
+  const int s1 = wxx_free(wr), s2 = wxx_free(lo_x), s3 = wxx_free(lo_w);
+  return st ? st : (s1 ? s1 : (s2 ? s2 : s3));
+}
+
 WXX_EXPORT int wxx_conv2d(float* Y, const float* X, const float* Wt, const float* bias, int B,
                           int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw, int ph,
                           int pw, int dh, int dw, int mode) {
+  ConvPost post;
+  memset(&post, 0, sizeof(post));
+  return conv2d_impl(Y, X, Wt, bias, B, Cin, H, W, Cout, KH, KW, sh, sw, ph, pw, dh, dw, mode,
+                     post);
+}
+
+// wxx_conv2d with ResNet's follow-up ops in the epilogue (or the split-K
+// reduce): y = relu?(bn(conv(x) + bias) + residual) where bn is eval-mode
+// batchnorm with running mean / variance rm, rv and affine gamma, beta
+// (NULL rm: none; the batchnorm kernel's expression), residual NCHW like Y
+// or NULL, relu 0/1.  Values equal the separate conv2d / batchnorm / add /
+// relu kernels' (same fp32 operations in the same order).
+WXX_EXPORT int wxx_conv2d_bn(float* Y, const float* X, const float* Wt, const float* bias, int B,
+                             int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw,
+                             int ph, int pw, int dh, int dw, int mode, const float* rm,
+                             const float* rv, const float* gamma, const float* beta, float eps,
+                             const float* residual, int relu) {
+  WXX_REQUIRE(rm == nullptr || (rv && gamma && beta),
+              "wxx_conv2d_bn: batchnorm needs mean, variance, gamma and beta");
+  ConvPost post;
+  post.rm = rm;
+  post.rv = rv;
+  post.g = gamma;
+  post.b = beta;
+  post.eps = eps;
+  post.res = residual;
+  post.relu = relu ? 1 : 0;
+  return conv2d_impl(Y, X, Wt, bias, B, Cin, H, W, Cout, KH, KW, sh, sw, ph, pw, dh, dw, mode,
+                     post);
+}
+
+namespace {
+int conv2d_impl(float* Y, const float* X, const float* Wt, const float* bias, int B, int Cin, int H,
+                int W, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw,
+                int mode, const ConvPost& post) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(B >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0 && KH > 0 && KW > 0,
               "wxx_conv2d: bad sizes");
@@ -698,6 +906,8 @@ WXX_EXPORT int wxx_conv2d(float* Y, const float* X, const float* Wt, const float
   p.epi.bias_mode = bias ? 1 : 0;
   p.epi.alpha = 1.0f;
   p.epi.hw_out = Ho * Wo;
+  p.epi.post = post;
   if (plan_splits(p, bn)) return run_splitk(bn, ma, ma, mb, mb, p);
   return run_tc(bn, ma, ma, mb, mb, p);
 }
+}  // namespace

@@ -341,9 +341,39 @@ struct OperandSrc {
   int64_t bs, s_row, s_k;
   int rows_total;         // valid rows (M or N)
   int k_total;            // valid K
-  // im2col (kind 3)
+  // im2col (kind 3); kind 4 (NHWC convolution input, TMA) uses cin, kw,
+  // strides, padding, dilation, ho, wo: K-block kc is 32 channels of one
+  // filter tap (k = (fh * KW + fw) * cin + c) and a 128-row tile is one 4-D
+  // box (32 channels, W, H, images) of the input at the tap's offset
   int cin, h, w, kh, kw, sh, sw, ph, pw, dh, dw, ho, wo;
 };
+
+// Convolution output post-ops, applied after alpha and the conv bias:
+// eval-mode batchnorm of channel n with the batchnorm kernel's expression
+// (x - mean) * rsqrt(var + eps) * gamma + beta, then + residual (laid out like
+// the output, at the output's own index), then ReLU -- ResNet's conv -> bn
+// (-> add) -> relu chain in the conv's epilogue, with the same fp32
+// operations.  NCHW outputs (kind 1) and the split-K reduce read `res` here;
+// row-major (NHWC) outputs stored by TMA read the residual from EpiParams.res.
+struct ConvPost {
+  const float* rm;        // running mean (NULL: no batchnorm)
+  const float* rv;        // running variance
+  const float* g;         // gamma
+  const float* b;         // beta
+  float eps;
+  const float* res;       // residual (B, N, Ho, Wo) or NULL
+  int relu;
+};
+
+__device__ __forceinline__ float conv_post(const ConvPost& c, float v, int n, int64_t idx) {
+  if (c.rm != nullptr) {
+    const float inv = rsqrtf(c.rv[n] + c.eps);
+    v = (v - c.rm[n]) * inv * c.g[n] + c.b[n];
+  }
+  if (c.res != nullptr) v = v + c.res[idx];
+  if (c.relu) v = fmaxf(0.0f, v);
+  return v;
+}
 
 struct EpiParams {
   int kind;               // 0 = row-major matrix C, 1 = NCHW convolution output
@@ -361,6 +391,7 @@ struct EpiParams {
   const float* res;       // residual (M, N) per batch, or NULL
   int64_t res_ld, res_bs;
   int raw;                // split-K: raw partial sums to the workspace map, z = batch * splits + slice
+  ConvPost post;          // kind 1 only
 };
 
 struct GemmParams {
@@ -601,13 +632,15 @@ __device__ __forceinline__ void epi_store(const GemmParams& p, int bt, int m, in
   } else {
     // NCHW: row m = (b, pixel), column n = output channel.
     int b = m / e.hw_out, pix = m - b * e.hw_out;
-    float* out = e.C + (int64_t)b * p.N * e.hw_out + pix;
+    const int64_t base = (int64_t)b * p.N * e.hw_out + pix;
+    float* out = e.C + base;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       int n = n0 + j;
       if (n < p.N) {
         float o = v[j] * e.alpha;
         if (e.bias_mode == 1) o += e.bias[n];
+        o = conv_post(e.post, o, n, base + (int64_t)n * e.hw_out);
         out[(int64_t)n * e.hw_out] = o;
       }
     }
@@ -738,6 +771,15 @@ __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, in
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
   }
+  if (e.post.rm != nullptr) {
+    // eval batchnorm of column n (the batchnorm kernel's expression)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j < p.N ? n0 + j : p.N - 1;
+      const float inv = rsqrtf(__ldg(e.post.rv + n) + e.post.eps);
+      v[j] = (v[j] - __ldg(e.post.rm + n)) * inv * __ldg(e.post.g + n) + __ldg(e.post.b + n);
+    }
+  }
   if (e.res != nullptr && m < p.M) {
     const float* r = e.res + (int64_t)bt * e.res_bs + (int64_t)m * e.res_ld + n0;
     if (n0 + 32 <= p.N && !(reinterpret_cast<uintptr_t>(r) & 15)) {
@@ -754,6 +796,10 @@ __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, in
       for (int j = 0; j < 32; ++j)
         if (n0 + j < p.N) v[j] += __ldg(r + j);
     }
+  }
+  if (e.post.relu) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fmaxf(0.0f, v[j]);
   }
 }
 
@@ -795,8 +841,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const bool a_gather = p.a.kind >= 2;
-  const bool b_gather = p.b.kind >= 2;
+  const bool a_gather = p.a.kind == 2 || p.a.kind == 3;
+  const bool b_gather = p.b.kind == 2 || p.b.kind == 3;
   const bool any_gather = a_gather || b_gather;
   // Work units: output tiles, each cut into p.splits K-slices (split-K).
   const int total_units = p.batch * p.tiles_m * p.tiles_n * p.splits;
@@ -850,6 +896,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int zb = p.a.bcast_batch ? 0 : bt;
             if (p.a.kind == 0) {
               tma_load_3d(smem_u32(sa), ma, &full_bar[stage], kc, tm * BM, zb);
+            } else if (p.a.kind == 4) {
+              const int tap = kc / p.a.cin, c0 = kc - tap * p.a.cin;
+              const int fh = tap / p.a.kw, fw = tap - fh * p.a.kw;
+              const int hw = p.a.ho * p.a.wo, m0 = tm * BM;
+              const int b0 = m0 / hw, r = m0 - b0 * hw;
+              const int ho0 = r / p.a.wo, wo0 = r - ho0 * p.a.wo;
+              tma_load_4d(smem_u32(sa), ma, &full_bar[stage], c0,
+                          wo0 * p.a.sw - p.a.pw + fw * p.a.dw, ho0 * p.a.sh - p.a.ph + fh * p.a.dh,
+                          b0);
             } else {
 #pragma unroll
               for (int j = 0; j < BM / 32; ++j)

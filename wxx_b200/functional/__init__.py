@@ -36,6 +36,9 @@ from .convolution import (
     causal_conv1d,
     causal_conv1d_backward,
     conv2d,
+    conv2d_bn,
+    conv2d_nhwc,
+    conv2d_nhwc_supported,
     conv2ddw,
     conv2ddx,
     conv2dtranspose,

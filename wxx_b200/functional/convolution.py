@@ -63,6 +63,80 @@ def conv2d(tensor1, W, stride, padding, dilation, bias=None):
     """NCHW cross-correlation as an implicit GEMM on the tcgen05 tensor cores
     (functional/convolution.py:658-729): rows = B*Ho*Wo output pixels,
     columns = Cout, K = Cin*KH*KW, the im2col gather done by producer warps."""
+    return _conv2d(tensor1, W, stride, padding, dilation, bias, None, None, False)
+
+
+def conv2d_bn(tensor1, W, stride, padding, dilation, bias=None, *, bn=None, residual=None,
+              relu=False):
+    """``conv2d`` followed by eval-mode batchnorm, an optional residual add and
+    an optional ReLU, all applied in the convolution's epilogue (ResNet's
+    conv -> bn (-> + shortcut) -> relu chain, functional/normalization.py:
+    148-206 in eval mode).  ``bn`` is ``(running_mean, running_var, gamma,
+    beta, eps)`` or None; ``residual`` is shaped like the output.  The values
+    equal the separate ``conv2d`` / ``batchnorm`` / ``+`` / ``relu`` ops (the
+    same fp32 operations in the same order)."""
+    return _conv2d(tensor1, W, stride, padding, dilation, bias, bn, residual, relu)
+
+
+def conv2d_nhwc_supported(cin, cout, ho, wo):
+    """True when ``conv2d_nhwc`` takes these channel counts and output size:
+    Cin a multiple of 32, Cout of 4, and 128-pixel output tiles that are
+    boxes of the output (Wo a multiple of 128, or Wo dividing 128 and Ho a
+    multiple or a divisor of 128 / Wo)."""
+    if cin % 32 or cout % 4 or ho < 1 or wo < 1:
+        return False
+    if wo >= 128:
+        return wo % 128 == 0
+    if 128 % wo:
+        return False
+    rows = 128 // wo
+    return ho % rows == 0 if ho >= rows else rows % ho == 0
+
+
+def conv2d_nhwc(tensor1, W, stride, padding, dilation, bias=None, *, bn=None, residual=None,
+                relu=False):
+    """``conv2d_bn`` on channels-last tensors: ``tensor1`` (B, H, W, Cin) NHWC,
+    ``W`` (Cout, Cin, KH, KW) as in the reference, ``residual`` and the result
+    (B, Ho, Wo, Cout) NHWC.  The implicit GEMM's A operand is fetched by TMA
+    boxes (one filter tap x 32 channels x a 128-pixel tile per K-block), so
+    the rows of im2col are never gathered by threads; see
+    ``conv2d_nhwc_supported`` for the shapes it takes."""
+    x = dense(tensor1)
+    w = dense(W)
+    B, H, Wd, Cin = x.shape
+    Cout, Cin_w, KH, KW = w.shape
+    if Cin_w != Cin:
+        raise ValueError(f"conv2d: input has {Cin} channels, weight expects {Cin_w}")
+    sh, sw = stride
+    ph, pw = padding
+    dh, dw = dilation
+    Ho = (H + 2 * ph - dh * (KH - 1) - 1) // sh + 1
+    Wo = (Wd + 2 * pw - dw * (KW - 1) - 1) // sw + 1
+    if not conv2d_nhwc_supported(Cin, Cout, Ho, Wo):
+        raise ValueError(f"conv2d_nhwc: unsupported shape Cin={Cin} Cout={Cout} out={(Ho, Wo)}")
+    if residual is not None and tuple(residual.shape) != (B, Ho, Wo, Cout):
+        raise ValueError(f"conv2d: residual {tuple(residual.shape)} is not {(B, Ho, Wo, Cout)}")
+    b = dense(bias) if bias is not None else None
+    out = empty((B, Ho, Wo, Cout), "f32", tensor1.requires_grad)
+    if bn is not None:
+        rm, rv, g, beta, eps = bn
+        rm, rv, g, beta = (dense(t) for t in (rm, rv, g, beta))
+        bn_args = (rm.ptr, rv.ptr, g.ptr, beta.ptr, float(eps))
+    else:
+        bn_args = (None, None, None, None, 0.0)
+    r = dense(residual) if residual is not None else None
+    mode = matmul_mode_code()
+    timer = active_timer()
+    ev0 = timer.start() if timer is not None else None
+    check(F.wxx_conv2d_nhwc(out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr, B, Cin, H,
+                            Wd, Cout, KH, KW, sh, sw, ph, pw, dh, dw, 0 if mode == 0 else 1,
+                            *bn_args, None if r is None else r.ptr, int(bool(relu))), "conv2d")
+    if timer is not None:
+        timer.stop(ev0, 2.0 * B * Ho * Wo * Cout * Cin * KH * KW, f"conv{B}x{H}x{Wd}x{Cin}->{Cout}")
+    return out
+
+
+def _conv2d(tensor1, W, stride, padding, dilation, bias, bn, residual, relu):
     x = dense(tensor1)
     w = dense(W)
     B, Cin, H, Wd = x.shape
@@ -81,8 +155,25 @@ def conv2d(tensor1, W, stride, padding, dilation, bias=None):
     mode = matmul_mode_code()
     timer = active_timer()
     ev0 = timer.start() if timer is not None else None
-    check(F.wxx_conv2d(out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr, B, Cin, H, Wd,
-                       Cout, KH, KW, sh, sw, ph, pw, dh, dw, 0 if mode == 0 else 1), "conv2d")
+    args = (out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr, B, Cin, H, Wd, Cout, KH,
+            KW, sh, sw, ph, pw, dh, dw, 0 if mode == 0 else 1)
+    if bn is None and residual is None and not relu:
+        check(F.wxx_conv2d(*args), "conv2d")
+    else:
+        if residual is not None and tuple(residual.shape) != (B, Cout, Ho, Wo):
+            raise ValueError(f"conv2d: residual {tuple(residual.shape)} is not {(B, Cout, Ho, Wo)}")
+        if bn is not None:
+            rm, rv, g, beta, eps = bn
+            rm, rv, g, beta = (dense(t) for t in (rm, rv, g, beta))
+            for t in (rm, rv, g, beta):
+                if tuple(t.shape) != (Cout,):
+                    raise ValueError(f"conv2d: batchnorm parameter {tuple(t.shape)} is not ({Cout},)")
+            bn_args = (rm.ptr, rv.ptr, g.ptr, beta.ptr, float(eps))
+        else:
+            bn_args = (None, None, None, None, 0.0)
+        r = dense(residual) if residual is not None else None
+        check(F.wxx_conv2d_bn(*args, *bn_args, None if r is None else r.ptr, int(bool(relu))),
+              "conv2d")
     if timer is not None:
         timer.stop(ev0, 2.0 * B * Ho * Wo * Cout * Cin * KH * KW, f"conv{B}x{Cin}x{H}x{Wd}->{Cout}")
     return out

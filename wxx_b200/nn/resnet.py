@@ -1,6 +1,28 @@
 """ResNet-18 (reference: src/wxx/nn/resnet.py)."""
 
+from .. import functional
+from ..backend import context
 from .module import AdaptiveAvgPool2d, BatchNorm, Conv2D, Linear, MaxPool2d, Module, Sequential
+
+
+def _conv_bn(x, conv, bn, residual=None, relu=False):
+    """conv -> eval batchnorm (-> + residual) (-> relu) in one convolution."""
+    return functional.conv2d_bn(x, conv.W, conv.stride, conv.padding, conv.dilation, conv.bias,
+                                bn=(bn.running_mean, bn.running_std, bn.weight, bn.bias, 1e-5),
+                                residual=residual, relu=relu)
+
+
+def _conv_nhwc(h, conv, bn, residual=None, relu=False):
+    """The same on channels-last activations (functional.conv2d_nhwc)."""
+    return functional.conv2d_nhwc(h, conv.W, conv.stride, conv.padding, conv.dilation, conv.bias,
+                                  bn=(bn.running_mean, bn.running_std, bn.weight, bn.bias, 1e-5),
+                                  residual=residual, relu=relu)
+
+
+def _conv_out_hw(conv, h, w):
+    kh, kw = conv.kernel
+    (sh, sw), (ph, pw), (dh, dw) = conv.stride, conv.padding, conv.dilation
+    return (h + 2 * ph - dh * (kh - 1) - 1) // sh + 1, (w + 2 * pw - dw * (kw - 1) - 1) // sw + 1
 
 
 class ResBlock(Module):
@@ -20,12 +42,42 @@ class ResBlock(Module):
             self.sh = True
 
     def forward(self, x):
+        if context.MODE != 0:
+            # inference: batchnorm, the shortcut add and the ReLUs ride in the
+            # convolutions' epilogues (same values as the lines below)
+            sc = x
+            if self.sh:
+                conv, bn = self.shortcut._modules.values()
+                sc = _conv_bn(x, conv, bn)
+            out = _conv_bn(x, self.conv1, self.bn1, relu=True)
+            return _conv_bn(out, self.conv2, self.bn2, residual=sc, relu=True)
         # The reference evaluates bn1 up to three times here (resnet.py:33); in
         # inference mode the extra evaluations are pure and are skipped.
         out = self.bn1(self.conv1(x)).relu()
         out = self.bn2(self.conv2(out))
         out = out + self.shortcut(x)
         return out.relu()
+
+    def nhwc_shape(self, shape):
+        """Output (B, Ho, Wo, C) of the channels-last path for an NHWC input
+        shape, or None when a convolution's shape does not suit it."""
+        B, H, W, C = shape
+        out_c = self.conv1.W.shape[0]
+        ho, wo = _conv_out_hw(self.conv1, H, W)
+        if not (functional.conv2d_nhwc_supported(C, out_c, ho, wo)
+                and functional.conv2d_nhwc_supported(out_c, out_c, ho, wo)):
+            return None
+        return (B, ho, wo, out_c)
+
+    def forward_nhwc(self, h):
+        """Inference on channels-last activations: three (or two) convolutions,
+        each with its batchnorm, the shortcut add and the ReLUs in its epilogue."""
+        sc = h
+        if self.sh:
+            conv, bn = self.shortcut._modules.values()
+            sc = _conv_nhwc(h, conv, bn)
+        out = _conv_nhwc(h, self.conv1, self.bn1, relu=True)
+        return _conv_nhwc(out, self.conv2, self.bn2, residual=sc, relu=True)
 
 
 class ResNet18(Module):
@@ -50,8 +102,23 @@ class ResNet18(Module):
         return Sequential(*layers)
 
     def forward(self, x):
-        out = self.bn1(self.conv1(x)).relu()
-        out = self.maxpool(out)
+        if context.MODE != 0:
+            out = self.maxpool(_conv_bn(x, self.conv1, self.bn1, relu=True))
+            blocks = [blk for layer in (self.layer1, self.layer2, self.layer3, self.layer4)
+                      for blk in layer._modules.values()]
+            shape = (out.shape[0], out.shape[2], out.shape[3], out.shape[1])
+            for blk in blocks:
+                shape = blk.nhwc_shape(shape) if shape is not None else None
+            if shape is not None:
+                # channels-last from the first block to the pooling: the
+                # convolutions' A operands then load as TMA boxes
+                h = out.permute(0, 2, 3, 1).contiguous()
+                for blk in blocks:
+                    h = blk.forward_nhwc(h)
+                B, H, W, C = h.shape
+                return self.fc(functional.mean(h.reshape((B, H * W, C)), axis=1))
+        else:
+            out = self.maxpool(self.bn1(self.conv1(x)).relu())
         out = self.layer1(out)
         out = self.layer2(out)
         out = self.layer3(out)
