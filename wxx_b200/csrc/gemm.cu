@@ -536,6 +536,12 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
     if (bias_mode == 0) return WXX_OK;
     mode = 2;  // the SIMT kernel adds the bias to the zero product
   }
+  // Tiny skinny products with a long K (ResNet's 256 x 10 x 512 classifier:
+  // two gathered tiles walking 16 K-blocks) finish sooner on the exact-fp32
+  // SIMT kernel; the fused epilogues (act / residual) stay on the tensor cores.
+  if (mode != 2 && act == 0 && res == nullptr && N < 16 && K >= 256 &&
+      batch * M * N * K <= (int64_t(1) << 22) && batch <= 65535)
+    mode = 2;
   if (mode == 2) {
     WXX_REQUIRE(batch <= 65535, "wxx_matmul: SIMT path supports batch <= 65535");
     dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), (unsigned)batch);
@@ -663,15 +669,23 @@ int conv2d_impl(float* Y, const float* X, const float* Wt, const float* bias, in
                 int mode, const ConvPost& post);
 
 // W (Cout, Cin, KH*KW) -> Wr (Cout, KH*KW, Cin): the NHWC convolution's K order.
-__global__ void conv_weight_reorder_kernel(float* __restrict__ wr, const float* __restrict__ w,
-                                           int cout, int cin, int taps) {
-  const int64_t total = (int64_t)cout * cin * taps;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t o = i / ((int64_t)cin * taps);
-    const int r = (int)(i - o * cin * taps);
-    const int t = r / cin, c = r - t * cin;
-    wr[i] = w[(o * cin + c) * taps + t];
+// One CTA per output channel transposes its (Cin x taps) block through shared
+// memory, so both the reads and the writes are contiguous.
+__global__ void __launch_bounds__(256) conv_weight_reorder_kernel(float* __restrict__ wr,
+                                                                  const float* __restrict__ w,
+                                                                  int cout, int cin, int taps) {
+  extern __shared__ float blk[];   // cin * taps
+  const int n = cin * taps;
+  for (int o = blockIdx.x; o < cout; o += gridDim.x) {
+    const float* src = w + (int64_t)o * n;
+    float* dst = wr + (int64_t)o * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) blk[i] = src[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int t = i / cin, c = i - t * cin;
+      dst[i] = blk[c * taps + t];
+    }
+    __syncthreads();
   }
 }
 
@@ -766,9 +780,20 @@ WXX_EXPORT int wxx_conv2d_nhwc(float* Y, const float* X, const float* Wt, const 
   void* lo_w = nullptr;
   int st = wxx_malloc(&wr, (uint64_t)Cout * K * sizeof(float));
   if (st) return st;
-  conv_weight_reorder_kernel<<<wxx::grid_for((int64_t)Cout * K, 256), 256, 0, s>>>(
-      (float*)wr, Wt, Cout, Cin, KH * KW);
-  wxx::count_launch();
+  {
+    const size_t smem = (size_t)K * sizeof(float);
+    static size_t smem_set = 48 * 1024;
+    if (smem > smem_set) {
+      WXX_CUDA_CHECK(cudaFuncSetAttribute(conv_weight_reorder_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+      smem_set = smem;
+    }
+    WXX_REQUIRE(smem <= 200 * 1024, "wxx_conv2d_nhwc: filter too large (Cin*KH*KW)");
+    conv_weight_reorder_kernel<<<Cout < 1184 ? Cout : 1184, 256, smem, s>>>((float*)wr, Wt, Cout,
+                                                                           Cin, KH * KW);
+    wxx::count_launch();
+  }
   CUtensorMap ma0, ma1, mb0, mb1;
   memset(&ma0, 0, sizeof(ma0));
   memset(&mb0, 0, sizeof(mb0));

@@ -116,7 +116,9 @@ class ResNet18(Module):
                 for blk in blocks:
                     h = blk.forward_nhwc(h)
                 B, H, W, C = h.shape
-                return self.fc(functional.mean(h.reshape((B, H * W, C)), axis=1))
+                pooled = (h.reshape((B, C)) if H * W == 1
+                          else functional.mean(h.reshape((B, H * W, C)), axis=1))
+                return self.fc(pooled)
         else:
             out = self.maxpool(self.bn1(self.conv1(x)).relu())
         out = self.layer1(out)
