@@ -450,6 +450,49 @@ int make_residual(const OperandDesc& d, const OperandSrc& src, int box_rows, CUt
 
 // ------------------------------------------------------------ exact fp32 SIMT
 
+// C[b] (M x N, N <= kSkinnyN) = alpha * op(A[b]) op(B[b]) + bias: one warp per
+// output row, lanes striding K, the N partial sums combined by shuffles in a
+// fixed order (deterministic).
+constexpr int kSkinnyN = 16;
+
+__global__ void __launch_bounds__(256) skinny_gemm_kernel(
+    float* __restrict__ C, const float* __restrict__ A, const float* __restrict__ B,
+    const float* __restrict__ bias, int64_t batch, int M, int N, int K, int64_t a_bs,
+    int64_t b_bs, int64_t lda, int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = (((int64_t)blockIdx.x * blockDim.x) + threadIdx.x) >> 5; row < batch * M;
+       row += warps) {
+    const int64_t bt = row / M;
+    const int m = (int)(row - bt * M);
+    const float* Ab = A + bt * a_bs;
+    const float* Bb = B + bt * b_bs;
+    float acc[kSkinnyN];
+#pragma unroll
+    for (int n = 0; n < kSkinnyN; ++n) acc[n] = 0.f;
+    for (int k = lane; k < K; k += 32) {
+      const float a = trans_a ? Ab[(int64_t)k * lda + m] : Ab[(int64_t)m * lda + k];
+#pragma unroll
+      for (int n = 0; n < kSkinnyN; ++n)
+        if (n < N)
+          acc[n] = fmaf(a, trans_b ? Bb[(int64_t)n * ldb + k] : Bb[(int64_t)k * ldb + n], acc[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < kSkinnyN; ++n) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], off);
+    }
+    if (lane < N) {
+      float v = 0.f;
+#pragma unroll
+      for (int n = 0; n < kSkinnyN; ++n) v = (n == lane) ? acc[n] : v;
+      v *= alpha;
+      if (bias_mode == 1) v += bias[lane];
+      C[bt * M * N + (int64_t)m * N + lane] = v;
+    }
+  }
+}
+
 // 64x64 output tile, K-step 16, 4x4 outputs per thread, fp32 FMA.
 __global__ void __launch_bounds__(256) simt_gemm_kernel(
     float* __restrict__ C, const float* __restrict__ A, const float* __restrict__ B,
@@ -536,12 +579,19 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
     if (bias_mode == 0) return WXX_OK;
     mode = 2;  // the SIMT kernel adds the bias to the zero product
   }
-  // Tiny skinny products with a long K (ResNet's 256 x 10 x 512 classifier:
-  // two gathered tiles walking 16 K-blocks) finish sooner on the exact-fp32
-  // SIMT kernel; the fused epilogues (act / residual) stay on the tensor cores.
-  if (mode != 2 && act == 0 && res == nullptr && N < 16 && K >= 256 &&
-      batch * M * N * K <= (int64_t(1) << 22) && batch <= 65535)
-    mode = 2;
+  // Skinny products with a long K (ResNet's 256 x 10 x 512 classifier: two
+  // gathered tensor-core tiles walking 16 K-blocks) run one warp per output
+  // row in exact fp32; the fused epilogues (act / residual) stay on the
+  // tensor cores.
+  if (act == 0 && res == nullptr && N <= kSkinnyN && K >= 256 &&
+      batch * M * N * K <= (int64_t(1) << 24) && bias_mode <= 1) {
+    const int64_t rows = batch * M;
+    skinny_gemm_kernel<<<wxx::grid_for(rows * 32, 256), 256, 0, s>>>(
+        C, A, B, bias, batch, (int)M, (int)N, (int)K, a_bs, b_bs, lda, ldb, trans_a, trans_b,
+        bias_mode, alpha);
+    WXX_LAUNCH_CHECK();
+    return WXX_OK;
+  }
   if (mode == 2) {
     WXX_REQUIRE(batch <= 65535, "wxx_matmul: SIMT path supports batch <= 65535");
     dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), (unsigned)batch);
@@ -884,6 +934,73 @@ WXX_EXPORT int wxx_conv2d_bn(float* Y, const float* X, const float* Wt, const fl
 }
 
 namespace {
+// Direct convolution for inputs with few channels (ResNet's 3-channel stem,
+// K = 147): an implicit GEMM would gather 147-wide rows for little tensor
+// work.  One CTA per (image, group of 16 output channels) holds the
+// zero-padded image and the group's filters in shared memory; each thread
+// accumulates 16 channels of its output pixels in exact fp32 (taps in the
+// reference's (c, kh, kw) order) and applies bias and the post-ops.
+constexpr int kDirectCG = 16;
+
+__global__ void __launch_bounds__(256) conv_direct_kernel(
+    float* __restrict__ Y, const float* __restrict__ X, const float* __restrict__ Wt,
+    const float* __restrict__ bias, int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw,
+    int ph, int pw, int dh, int dw, int Ho, int Wo, ConvPost post) {
+  extern __shared__ float dsm[];
+  const int Hp = H + 2 * ph, Wp = W + 2 * pw;
+  float* img = dsm;                              // Cin x Hp x Wp
+  float* wts = dsm + Cin * Hp * Wp;              // taps x kDirectCG (channel fastest)
+  const int groups = (Cout + kDirectCG - 1) / kDirectCG;
+  const int b = blockIdx.x / groups, n0 = (blockIdx.x - b * groups) * kDirectCG;
+  const int taps = Cin * KH * KW;
+  const float* xb = X + (int64_t)b * Cin * H * W;
+  for (int i = threadIdx.x; i < Cin * Hp * Wp; i += blockDim.x) {
+    const int c = i / (Hp * Wp), r = i - c * Hp * Wp;
+    const int y = r / Wp - ph, x = r % Wp - pw;
+    img[i] = (y >= 0 && y < H && x >= 0 && x < W) ? xb[((int64_t)c * H + y) * W + x] : 0.f;
+  }
+  for (int i = threadIdx.x; i < taps * kDirectCG; i += blockDim.x) {
+    const int t = i / kDirectCG, j = i - t * kDirectCG;
+    wts[i] = n0 + j < Cout ? Wt[(int64_t)(n0 + j) * taps + t] : 0.f;
+  }
+  __syncthreads();
+  const int hw = Ho * Wo;
+  for (int pix = threadIdx.x; pix < hw; pix += blockDim.x) {
+    const int ho = pix / Wo, wo = pix - ho * Wo;
+    float acc[kDirectCG];
+#pragma unroll
+    for (int j = 0; j < kDirectCG; ++j) acc[j] = 0.f;
+    int t = 0;
+    for (int c = 0; c < Cin; ++c) {
+      for (int kh = 0; kh < KH; ++kh) {
+        const float* row = img + (c * Hp + ho * sh + kh * dh) * Wp + wo * sw;
+        for (int kw = 0; kw < KW; ++kw, ++t) {
+          const float xv = row[kw * dw];
+          const float4* wv = reinterpret_cast<const float4*>(wts + t * kDirectCG);
+#pragma unroll
+          for (int q = 0; q < kDirectCG / 4; ++q) {
+            const float4 w4 = wv[q];
+            acc[4 * q] = fmaf(xv, w4.x, acc[4 * q]);
+            acc[4 * q + 1] = fmaf(xv, w4.y, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(xv, w4.z, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(xv, w4.w, acc[4 * q + 3]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kDirectCG; ++j) {
+      const int n = n0 + j;
+      if (n < Cout) {
+        float o = acc[j];
+        if (bias != nullptr) o += bias[n];
+        const int64_t idx = ((int64_t)b * Cout + n) * hw + pix;
+        Y[idx] = conv_post(post, o, n, idx);
+      }
+    }
+  }
+}
+
 int conv2d_impl(float* Y, const float* X, const float* Wt, const float* bias, int B, int Cin, int H,
                 int W, int Cout, int KH, int KW, int sh, int sw, int ph, int pw, int dh, int dw,
                 int mode, const ConvPost& post) {
@@ -899,6 +1016,23 @@ int conv2d_impl(float* Y, const float* X, const float* Wt, const float* bias, in
   int64_t K = (int64_t)Cin * KH * KW;
   WXX_REQUIRE(Mrows < (int64_t(1) << 31) && K < (int64_t(1) << 31), "wxx_conv2d: too large");
   if (Mrows == 0) return WXX_OK;
+  {
+    const size_t smem = ((size_t)Cin * (H + 2 * ph) * (W + 2 * pw) + (size_t)K * kDirectCG) * 4;
+    if (Cin <= 4 && smem <= 96 * 1024 && B <= 65535 * 8) {
+      static size_t smem_set = 48 * 1024;
+      if (smem > smem_set) {
+        WXX_CUDA_CHECK(cudaFuncSetAttribute(conv_direct_kernel,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            96 * 1024));
+        smem_set = 96 * 1024;
+      }
+      const int64_t blocks = (int64_t)B * ((Cout + kDirectCG - 1) / kDirectCG);
+      conv_direct_kernel<<<(unsigned)blocks, 256, smem, wxx::stream()>>>(
+          Y, X, Wt, bias, Cin, H, W, Cout, KH, KW, sh, sw, ph, pw, dh, dw, Ho, Wo, post);
+      WXX_LAUNCH_CHECK();
+      return WXX_OK;
+    }
+  }
   GemmParams p;
   memset(&p, 0, sizeof(p));
   p.M = (int)Mrows;
