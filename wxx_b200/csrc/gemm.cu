@@ -942,10 +942,12 @@ namespace {
 // reference's (c, kh, kw) order) and applies bias and the post-ops.
 constexpr int kDirectCG = 16;
 
+template <int KWT>   // filter width (0: any, read from kw_rt)
 __global__ void __launch_bounds__(256) conv_direct_kernel(
     float* __restrict__ Y, const float* __restrict__ X, const float* __restrict__ Wt,
-    const float* __restrict__ bias, int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw,
-    int ph, int pw, int dh, int dw, int Ho, int Wo, ConvPost post) {
+    const float* __restrict__ bias, int Cin, int H, int W, int Cout, int KH, int kw_rt, int sh,
+    int sw, int ph, int pw, int dh, int dw, int Ho, int Wo, ConvPost post) {
+  const int KW = KWT > 0 ? KWT : kw_rt;
   extern __shared__ float dsm[];
   const int Hp = H + 2 * ph, Wp = W + 2 * pw;
   float* img = dsm;                              // Cin x Hp x Wp
@@ -954,36 +956,56 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(
   const int b = blockIdx.x / groups, n0 = (blockIdx.x - b * groups) * kDirectCG;
   const int taps = Cin * KH * KW;
   const float* xb = X + (int64_t)b * Cin * H * W;
-  for (int i = threadIdx.x; i < Cin * Hp * Wp; i += blockDim.x) {
-    const int c = i / (Hp * Wp), r = i - c * Hp * Wp;
-    const int y = r / Wp - ph, x = r % Wp - pw;
-    img[i] = (y >= 0 && y < H && x >= 0 && x < W) ? xb[((int64_t)c * H + y) * W + x] : 0.f;
+  // padded image: one padded row per iteration, no divisions per element
+  for (int r = threadIdx.x >> 5; r < Cin * Hp; r += blockDim.x >> 5) {
+    const int c = r / Hp, y = r - c * Hp - ph;
+    float* dst = img + r * Wp;
+    const bool rowin = y >= 0 && y < H;
+    const float* src = xb + ((int64_t)c * H + y) * W;
+    for (int x = (threadIdx.x & 31); x < Wp; x += 32) {
+      const int xs = x - pw;
+      dst[x] = (rowin && xs >= 0 && xs < W) ? src[xs] : 0.f;
+    }
   }
   for (int i = threadIdx.x; i < taps * kDirectCG; i += blockDim.x) {
-    const int t = i / kDirectCG, j = i - t * kDirectCG;
+    const int t = i >> 4, j = i & (kDirectCG - 1);
     wts[i] = n0 + j < Cout ? Wt[(int64_t)(n0 + j) * taps + t] : 0.f;
   }
   __syncthreads();
-  const int hw = Ho * Wo;
-  for (int pix = threadIdx.x; pix < hw; pix += blockDim.x) {
+  // two output pixels per thread (pix and pix + half): every weight load
+  // feeds 32 FMAs
+  const int hw = Ho * Wo, half = (hw + 1) / 2;
+  for (int pix = threadIdx.x; pix < half; pix += blockDim.x) {
+    const int pix2 = pix + half;
+    const bool two = pix2 < hw;
     const int ho = pix / Wo, wo = pix - ho * Wo;
-    float acc[kDirectCG];
+    const int ho2 = two ? pix2 / Wo : ho, wo2 = two ? pix2 - ho2 * Wo : wo;
+    float acc[kDirectCG], acc2[kDirectCG];
 #pragma unroll
-    for (int j = 0; j < kDirectCG; ++j) acc[j] = 0.f;
-    int t = 0;
+    for (int j = 0; j < kDirectCG; ++j) acc[j] = acc2[j] = 0.f;
+    const float4* wv = reinterpret_cast<const float4*>(wts);
     for (int c = 0; c < Cin; ++c) {
       for (int kh = 0; kh < KH; ++kh) {
         const float* row = img + (c * Hp + ho * sh + kh * dh) * Wp + wo * sw;
-        for (int kw = 0; kw < KW; ++kw, ++t) {
-          const float xv = row[kw * dw];
-          const float4* wv = reinterpret_cast<const float4*>(wts + t * kDirectCG);
+        const float* row2 = img + (c * Hp + ho2 * sh + kh * dh) * Wp + wo2 * sw;
 #pragma unroll
-          for (int q = 0; q < kDirectCG / 4; ++q) {
-            const float4 w4 = wv[q];
-            acc[4 * q] = fmaf(xv, w4.x, acc[4 * q]);
-            acc[4 * q + 1] = fmaf(xv, w4.y, acc[4 * q + 1]);
-            acc[4 * q + 2] = fmaf(xv, w4.z, acc[4 * q + 2]);
-            acc[4 * q + 3] = fmaf(xv, w4.w, acc[4 * q + 3]);
+        for (int kw = 0; kw < (KWT > 0 ? KWT : 1); ++kw) {
+          for (int kk = 0; kk < (KWT > 0 ? 1 : KW); ++kk) {
+            const int k = KWT > 0 ? kw : kk;
+            const float xv = row[k * dw], xv2 = row2[k * dw];
+#pragma unroll
+            for (int q = 0; q < kDirectCG / 4; ++q) {
+              const float4 w4 = wv[q];
+              acc[4 * q] = fmaf(xv, w4.x, acc[4 * q]);
+              acc[4 * q + 1] = fmaf(xv, w4.y, acc[4 * q + 1]);
+              acc[4 * q + 2] = fmaf(xv, w4.z, acc[4 * q + 2]);
+              acc[4 * q + 3] = fmaf(xv, w4.w, acc[4 * q + 3]);
+              acc2[4 * q] = fmaf(xv2, w4.x, acc2[4 * q]);
+              acc2[4 * q + 1] = fmaf(xv2, w4.y, acc2[4 * q + 1]);
+              acc2[4 * q + 2] = fmaf(xv2, w4.z, acc2[4 * q + 2]);
+              acc2[4 * q + 3] = fmaf(xv2, w4.w, acc2[4 * q + 3]);
+            }
+            wv += kDirectCG / 4;
           }
         }
       }
@@ -992,10 +1014,16 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(
     for (int j = 0; j < kDirectCG; ++j) {
       const int n = n0 + j;
       if (n < Cout) {
+        const float bv = bias != nullptr ? bias[n] : 0.f;
+        const int64_t base = ((int64_t)b * Cout + n) * hw;
         float o = acc[j];
-        if (bias != nullptr) o += bias[n];
-        const int64_t idx = ((int64_t)b * Cout + n) * hw + pix;
-        Y[idx] = conv_post(post, o, n, idx);
+        if (bias != nullptr) o += bv;
+        Y[base + pix] = conv_post(post, o, n, base + pix);
+        if (two) {
+          float o2 = acc2[j];
+          if (bias != nullptr) o2 += bv;
+          Y[base + pix2] = conv_post(post, o2, n, base + pix2);
+        }
       }
     }
   }
@@ -1019,16 +1047,36 @@ int conv2d_impl(float* Y, const float* X, const float* Wt, const float* bias, in
   {
     const size_t smem = ((size_t)Cin * (H + 2 * ph) * (W + 2 * pw) + (size_t)K * kDirectCG) * 4;
     if (Cin <= 4 && smem <= 96 * 1024 && B <= 65535 * 8) {
-      static size_t smem_set = 48 * 1024;
-      if (smem > smem_set) {
-        WXX_CUDA_CHECK(cudaFuncSetAttribute(conv_direct_kernel,
+      static bool attr = false;
+      if (!attr) {
+        WXX_CUDA_CHECK(cudaFuncSetAttribute(conv_direct_kernel<7>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             96 * 1024));
-        smem_set = 96 * 1024;
+        WXX_CUDA_CHECK(cudaFuncSetAttribute(conv_direct_kernel<3>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            96 * 1024));
+        WXX_CUDA_CHECK(cudaFuncSetAttribute(conv_direct_kernel<0>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            96 * 1024));
+        attr = true;
       }
-      const int64_t blocks = (int64_t)B * ((Cout + kDirectCG - 1) / kDirectCG);
-      conv_direct_kernel<<<(unsigned)blocks, 256, smem, wxx::stream()>>>(
-          Y, X, Wt, bias, Cin, H, W, Cout, KH, KW, sh, sw, ph, pw, dh, dw, Ho, Wo, post);
+      const unsigned blocks = (unsigned)((int64_t)B * ((Cout + kDirectCG - 1) / kDirectCG));
+      // one thread per pair of output pixels, up to 256
+      const int pairs = (Ho * Wo + 1) / 2;
+      const int threads = pairs >= 256 ? 256 : ((pairs + 31) / 32) * 32;
+      cudaStream_t st = wxx::stream();
+      if (KW == 7)
+        conv_direct_kernel<7><<<blocks, threads, smem, st>>>(Y, X, Wt, bias, Cin, H, W, Cout, KH,
+                                                             KW, sh, sw, ph, pw, dh, dw, Ho, Wo,
+                                                             post);
+      else if (KW == 3)
+        conv_direct_kernel<3><<<blocks, threads, smem, st>>>(Y, X, Wt, bias, Cin, H, W, Cout, KH,
+                                                             KW, sh, sw, ph, pw, dh, dw, Ho, Wo,
+                                                             post);
+      else
+        conv_direct_kernel<0><<<blocks, threads, smem, st>>>(Y, X, Wt, bias, Cin, H, W, Cout, KH,
+                                                             KW, sh, sw, ph, pw, dh, dw, Ho, Wo,
+                                                             post);
       WXX_LAUNCH_CHECK();
       return WXX_OK;
     }
