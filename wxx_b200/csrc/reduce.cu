@@ -77,14 +77,65 @@ __global__ void __launch_bounds__(256) row_reduce_kernel(float* __restrict__ out
     float acc = 0.f;
     bool vec = ((reinterpret_cast<uintptr_t>(p) & 15) == 0);
     int64_t n4 = vec ? n / 4 : 0;
-    for (int64_t i = threadIdx.x; i < n4; i += 256) {
-      float4 v = reinterpret_cast<const float4*>(p)[i];
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    int64_t i = threadIdx.x;
+    // four 16-byte loads in flight per thread, added in the same order as
+    // the one-at-a-time loop
+    for (; i + 768 < n4; i += 1024) {
+      const float4 v0 = __ldg(p4 + i), v1 = __ldg(p4 + i + 256), v2 = __ldg(p4 + i + 512),
+                   v3 = __ldg(p4 + i + 768);
+      acc += reduce_elem(v0.x, mode) + reduce_elem(v0.y, mode) + reduce_elem(v0.z, mode) +
+             reduce_elem(v0.w, mode);
+      acc += reduce_elem(v1.x, mode) + reduce_elem(v1.y, mode) + reduce_elem(v1.z, mode) +
+             reduce_elem(v1.w, mode);
+      acc += reduce_elem(v2.x, mode) + reduce_elem(v2.y, mode) + reduce_elem(v2.z, mode) +
+             reduce_elem(v2.w, mode);
+      acc += reduce_elem(v3.x, mode) + reduce_elem(v3.y, mode) + reduce_elem(v3.z, mode) +
+             reduce_elem(v3.w, mode);
+    }
+    for (; i < n4; i += 256) {
+      float4 v = __ldg(p4 + i);
       acc += reduce_elem(v.x, mode) + reduce_elem(v.y, mode) + reduce_elem(v.z, mode) +
              reduce_elem(v.w, mode);
     }
     for (int64_t i = n4 * 4 + threadIdx.x; i < n; i += 256) acc += reduce_elem(p[i], mode);
     float t = block_sum<8>(acc, sh);
     if (threadIdx.x == 0) out[row] = mode == 1 ? t / (float)n : t;
+  }
+}
+
+// One warp per row for long rows when there are many of them: each lane keeps
+// eight 16-byte loads in flight (4 KB per warp), rows spread over every SM.
+__global__ void __launch_bounds__(256) row_reduce_warp_vec_kernel(float* __restrict__ out,
+                                                                  const float* __restrict__ x,
+                                                                  int64_t rows, int64_t n,
+                                                                  int mode) {
+  const int l = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += warps) {
+    const float* p = x + row * n;
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    const int64_t n4 = n / 4;   // rows are 16-byte aligned (checked by the host)
+    float acc = 0.f;
+    int64_t i = l;
+    for (; i + 224 < n4; i += 256) {
+      float4 v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[q] = __ldg(p4 + i + 32 * q);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        acc += reduce_elem(v[q].x, mode) + reduce_elem(v[q].y, mode) + reduce_elem(v[q].z, mode) +
+               reduce_elem(v[q].w, mode);
+    }
+    for (; i < n4; i += 32) {
+      const float4 v = __ldg(p4 + i);
+      acc += reduce_elem(v.x, mode) + reduce_elem(v.y, mode) + reduce_elem(v.z, mode) +
+             reduce_elem(v.w, mode);
+    }
+    for (int64_t j = n4 * 4 + l; j < n; j += 32) acc += reduce_elem(p[j], mode);
+    acc = warp_sum(acc);
+    if (l == 0) out[row] = mode == 1 ? acc / (float)n : acc;
   }
 }
 
@@ -125,7 +176,24 @@ __global__ void __launch_bounds__(256) col_reduce_cluster_kernel(float* __restri
   for (int64_t o = blockIdx.y; o < outer; o += gridDim.y) {
     const float* base = x + o * reduce * inner;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int64_t r = r_begin + ty; r < r_end; r += 16) {
+    int64_t r = r_begin + ty;
+    if (c0 + 3 < inner && ((reinterpret_cast<uintptr_t>(base + c0) | (inner * 4)) & 15) == 0) {
+      // 16-byte loads, eight rows in flight, same per-thread addition order
+      for (; r + 112 < r_end; r += 128) {
+        float4 v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          v[q] = __ldg(reinterpret_cast<const float4*>(base + (r + 16 * q) * inner + c0));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          a0 += reduce_elem(v[q].x, mode);
+          a1 += reduce_elem(v[q].y, mode);
+          a2 += reduce_elem(v[q].z, mode);
+          a3 += reduce_elem(v[q].w, mode);
+        }
+      }
+    }
+    for (; r < r_end; r += 16) {
       const float* p = base + r * inner + c0;
       if (c0 + 3 < inner) {
         a0 += reduce_elem(p[0], mode);
@@ -551,6 +619,10 @@ WXX_EXPORT int wxx_reduce(float* out, const float* x, int64_t outer, int64_t red
     if (reduce <= 1024) {
       unsigned grid = (unsigned)((outer + 7) / 8);
       row_reduce_warp_kernel<<<grid, 256, 0, s>>>(out, x, outer, (int)reduce, mode);
+    } else if (outer >= 2 * (int64_t)wxx::num_sms() * 8 && reduce % 4 == 0 &&
+               (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+      row_reduce_warp_vec_kernel<<<wxx::grid_for(outer * 32, 256), 256, 0, s>>>(out, x, outer,
+                                                                               reduce, mode);
     } else {
       row_reduce_kernel<<<wxx::grid_for(outer * 256, 256, 16), 256, 0, s>>>(out, x, outer, reduce,
                                                                             mode);
