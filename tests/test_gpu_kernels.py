@@ -206,6 +206,20 @@ def test_argmax_ties_follow_reference_tree(rng):
     assert np.array_equal(i2.numpy(), np.zeros(2, np.uint32))
 
 
+@pytest.mark.parametrize("n", [1, 31, 200, 256, 257, 1000, 4096, 5003])
+@pytest.mark.parametrize("op", [0, 1])
+def test_argminmax_ties_and_nans_all_row_lengths(n, op, rng):
+    """Heavy ties and scattered NaNs on row lengths around the 256-slot and
+    32-lane boundaries: indices bit-exact against the reference tree."""
+    F = _w().functional
+    x = rng.integers(0, 4, size=(37, n)).astype(np.float32)
+    x[rng.random(x.shape) < 0.02] = np.nan
+    vals, idx = (F.max if op == 0 else F.min)(up(x), 1)
+    rv, ri = K.argminmax(x, 1, op)
+    assert np.array_equal(idx.numpy(), ri)
+    assert np.array_equal(vals.numpy(), rv, equal_nan=True)
+
+
 @pytest.mark.parametrize("shape,dim", [((3, 5), -1), ((32, 256, 256), -1), ((8, 1024), -1),
                                        ((4, 3000), -1), ((6, 9, 5), 1)])
 def test_softmax(shape, dim, rng):

@@ -230,6 +230,76 @@ __global__ void __launch_bounds__(256) col_reduce_cluster_kernel(float* __restri
 
 // ------------------------------------------------------------ argmax / argmin
 
+// The same rule with one warp per output row (inner == 1): lane l holds the
+// slots l + 32 j (j = 0..7), each scanning its stride-256 sequence in order;
+// the tree's strides 128, 64 and 32 pair slots of one lane (j with j + 4,
+// j + 2, j + 1) and strides 16..1 pair lanes by shuffles -- the same
+// comparisons in the same order as the CTA form below, without shared memory
+// or barriers.  The row is read in 128-byte warp segments.
+__global__ void __launch_bounds__(256) argminmax_warp_kernel(float* __restrict__ vals,
+                                                             uint32_t* __restrict__ idx,
+                                                             const float* __restrict__ x,
+                                                             int64_t rows, int64_t reduce,
+                                                             int op) {
+  const int l = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += warps) {
+    const float* base = x + row * reduce;
+    float bv[8];
+    uint32_t bi[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      bv[j] = op == 0 ? -1e38f : 1e38f;
+      bi[j] = 0;
+    }
+    for (int64_t r0 = 0; r0 < reduce; r0 += 256) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t r = r0 + l + 32 * j;
+        v[j] = r < reduce ? __ldg(base + r) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t r = r0 + l + 32 * j;
+        const bool better = op == 0 ? (v[j] > bv[j]) : (v[j] < bv[j]);
+        if (r < reduce && better) {
+          bv[j] = v[j];
+          bi[j] = (uint32_t)r;
+        }
+      }
+    }
+#pragma unroll
+    for (int s = 4; s >= 1; s >>= 1) {   // slot strides 128, 64, 32
+#pragma unroll
+      for (int j = 0; j < s; ++j) {
+        const bool better = op == 0 ? (bv[j + s] > bv[j]) : (bv[j + s] < bv[j]);
+        if (better) {
+          bv[j] = bv[j + s];
+          bi[j] = bi[j + s];
+        }
+      }
+    }
+    float b = bv[0];
+    uint32_t a = bi[0];
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, b, s);
+      const uint32_t oi = __shfl_down_sync(0xffffffffu, a, s);
+      const bool better = op == 0 ? (ov > b) : (ov < b);
+      if (l < s && better) {
+        b = ov;
+        a = oi;
+      }
+    }
+    if (l == 0) {
+      vals[row] = b;
+      idx[row] = a;
+    }
+  }
+}
+
 // One CTA of exactly 256 threads per output, reproducing reduce_minmax.wgsl:
 // thread t scans r = t, t+256, ... keeping the first strictly better value
 // (initial value -1e38 for max / 1e38 for min, index 0); then a tree over the
@@ -645,6 +715,12 @@ WXX_EXPORT int wxx_argminmax(float* vals, uint32_t* idx, const float* x, int64_t
   WXX_REQUIRE(op == 0 || op == 1, "wxx_argminmax: op must be 0 (max) or 1 (min)");
   int64_t total = outer * inner;
   if (total == 0) return WXX_OK;
+  if (inner == 1) {
+    argminmax_warp_kernel<<<wxx::grid_for(outer * 32, 256), 256, 0, wxx::stream()>>>(
+        vals, idx, x, outer, reduce, op);
+    WXX_LAUNCH_CHECK();
+    return WXX_OK;
+  }
   unsigned grid = (unsigned)(total < (int64_t)wxx::num_sms() * 64 ? total : (int64_t)wxx::num_sms() * 64);
   argminmax_kernel<<<grid, 256, 0, wxx::stream()>>>(vals, idx, x, outer, reduce, inner, op);
   WXX_LAUNCH_CHECK();
