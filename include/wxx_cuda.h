@@ -168,6 +168,13 @@ int wxx_matmul(float* C, const float* A, const float* B, const float* bias, int6
 int wxx_linear(float* C, const float* A, const float* B, const float* bias,
                const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
                int64_t ldb, int trans_b, int act, float alpha, int mode);
+/* nn/hyena.py:242 out_proj(z.transpose(1, 2)): wxx_linear over a batch whose A operand is a
+ * strided view, A[b] at A + b*a_bs with row stride lda, transposed when trans_a (A[b] stored
+ * (K, M)), B shared by the batch, residual (batch, M, N) dense or NULL; act 0 or 1. */
+int wxx_linear_batched(float* C, const float* A, const float* B, const float* bias,
+                       const float* residual, int64_t batch, int64_t M, int64_t N, int64_t K,
+                       int64_t a_bs, int64_t lda, int trans_a, int64_t ldb, int trans_b, int act,
+                       float alpha, int mode);
 /* functional/convolution.py:658-729 conv2d (conv2d.wgsl), NCHW implicit GEMM on tcgen05.
  * mode 0 TF32, 1 or 2 3xTF32. */
 int wxx_conv2d(float* Y, const float* X, const float* W, const float* bias, int B, int Cin,

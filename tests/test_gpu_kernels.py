@@ -685,6 +685,30 @@ def test_linear_fp32_mode_and_ragged_n_fall_back(rng):
     assert rel(got32, K.matmul_add(x, w, b)) < 1e-5
 
 
+@pytest.mark.parametrize("shape", [(2, 8192, 256, 256), (3, 300, 64, 36), (2, 129, 40, 20)])
+@pytest.mark.parametrize("mode,tol", [("tf32", 2e-3), ("3xtf32", 1e-5)])
+def test_linear_on_batch_transposed_view(shape, mode, tol, rng):
+    """linear(z.transpose(1, 2), W, residual=r) with z (B, K, M) dense: the
+    GEMM reads the view as a transposed operand (no copy); Hyena's out
+    projection.  Against the oracle and the copied-input path."""
+    F = _w().functional
+    B, M, Kd, N = shape
+    z = rng.standard_normal((B, Kd, M)).astype(np.float32)
+    w = (rng.standard_normal((Kd, N)) / np.sqrt(Kd)).astype(np.float32)
+    r = rng.standard_normal((B, M, N)).astype(np.float32)
+    F.set_matmul_mode(mode)
+    try:
+        got = F.linear(up(z).transpose(1, 2), up(w), residual=up(r)).numpy()
+        copied = F.linear(up(np.ascontiguousarray(z.transpose(0, 2, 1))), up(w),
+                          residual=up(r)).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    ref = K.matmul_add(np.ascontiguousarray(z.transpose(0, 2, 1)), w, None) + r
+    assert got.shape == (B, M, N)
+    assert rel(got, ref) < tol
+    assert rel(got, copied) < tol
+
+
 @pytest.mark.parametrize("shape", [(300, 64, 72), (1000, 256, 1376), (4096, 256, 2048),
                                    (130, 40, 200)])
 @pytest.mark.parametrize("mode,tol", [("tf32", 2e-3), ("3xtf32", 1e-5)])

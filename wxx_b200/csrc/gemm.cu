@@ -687,6 +687,27 @@ WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float*
                      bias_mode, alpha, mode, 0, nullptr);
 }
 
+// Batched form of wxx_linear for an A operand given as a strided view:
+//   C[b] (M, N dense) = act(alpha * op(A[b]) @ op(B) + bias) + residual[b]
+// A[b] at A + b*a_bs with row stride lda, op(A) = A or A^T (trans_a: A[b] is
+// stored (K, M) -- a (B, K, M) activation read as (B, M, K) without a copy);
+// B (K, N) or (N, K) with trans_b, shared by the batch; residual (batch, M,
+// N) dense or NULL.  Same requirements as wxx_linear.
+WXX_EXPORT int wxx_linear_batched(float* C, const float* A, const float* B, const float* bias,
+                                  const float* residual, int64_t batch, int64_t M, int64_t N,
+                                  int64_t K, int64_t a_bs, int64_t lda, int trans_a, int64_t ldb,
+                                  int trans_b, int act, float alpha, int mode) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(batch >= 1 && M >= 0 && N >= 0 && K > 0, "wxx_linear_batched: bad sizes");
+  WXX_REQUIRE(mode == 0 || mode == 1, "wxx_linear_batched: mode %d not in {0, 1}", mode);
+  WXX_REQUIRE(act == 0 || act == 1, "wxx_linear_batched: act %d not in {0, 1}", act);
+  WXX_REQUIRE(!(reinterpret_cast<uintptr_t>(C) & 15) && N % 4 == 0,
+              "wxx_linear_batched: C must be 16-byte aligned with N a multiple of 4");
+  if (batch * M * N == 0) return WXX_OK;
+  return matmul_impl(C, A, B, bias, batch, M, N, K, a_bs, 0, lda, ldb, trans_a, trans_b,
+                     bias ? 1 : 0, alpha, mode, act, residual);
+}
+
 // Linear layer with its follow-up fused into the GEMM epilogue:
 //   C (M, N dense) = act(alpha * A @ op(B) + bias) + residual
 // A (M, K) row stride lda; B (K, N) row stride ldb, or (N, K) with trans_b = 1;

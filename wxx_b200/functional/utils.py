@@ -202,6 +202,42 @@ def matmul_add(tensor1, tensor2, tensor3, transpose_A=False, transpose_B=False, 
 _ACTIVATIONS = {None: 0, "gelu": 1, "swiglu": 2}
 
 
+def _linear_batch_transposed(x, weight, bias, activation, residual):
+    """``linear`` for a (B, M, K) view of a dense (B, K, M) activation (Hyena's
+    ``out_proj(z.transpose(1, 2))``, nn/hyena.py:242): the GEMM reads each
+    batch's A as a transposed (MN-major) operand instead of copying the view.
+    None when the input is not such a view or the fused form does not apply."""
+    if len(x.shape) != 3 or activation not in (None, "gelu"):
+        return None
+    B, M, K = x.shape
+    if x.stride[1] != 1 or x.stride[2] != M or M < 2 or K < 2:
+        return None
+    w = dense(weight)
+    N = w.shape[-1]
+    mode = matmul_mode_code()
+    if (len(w.shape) != 2 or w.shape[0] != K or mode not in (0, 1) or N % 4
+            or (mode == 1 and K > 1024)):
+        return None
+    if bias is not None and tuple(bias.shape) != (N,):
+        raise ValueError(f"linear: bias {tuple(bias.shape)} is not ({N},)")
+    if residual is not None and tuple(residual.shape) != (B, M, N):
+        raise ValueError(f"linear: residual {tuple(residual.shape)} is not {(B, M, N)}")
+    requires_grad = (x.requires_grad or weight.requires_grad
+                     or (bias is not None and bias.requires_grad)
+                     or (residual is not None and residual.requires_grad))
+    out = empty([B, M, N], "f32", requires_grad)
+    b = dense(bias) if bias is not None else None
+    r = dense(residual) if residual is not None else None
+    timer = active_timer()
+    ev0 = timer.start() if timer is not None else None
+    check(F.wxx_linear_batched(out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr,
+                               None if r is None else r.ptr, B, M, N, K, x.stride[0], M, 1, N, 0,
+                               _ACTIVATIONS[activation], 1.0, mode), "linear")
+    if timer is not None:
+        timer.stop(ev0, 2.0 * B * M * N * K, f"{B}x{M}x{N}x{K}T")
+    return out
+
+
 def linear(x, weight, bias=None, *, activation=None, residual=None):
     """``act(x @ weight + bias) + residual`` with the activation and the
     residual add fused into the GEMM epilogue.
@@ -217,6 +253,9 @@ def linear(x, weight, bias=None, *, activation=None, residual=None):
     multiple of 4, 3xTF32 with K > 1024)."""
     if activation not in _ACTIVATIONS:
         raise ValueError(f"activation must be None, 'gelu' or 'swiglu', got {activation!r}")
+    y = _linear_batch_transposed(x, weight, bias, activation, residual)
+    if y is not None:
+        return y
     a = dense(x)
     w = dense(weight)
     K = a.shape[-1]
