@@ -101,11 +101,14 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return (x < -10.0f) ? 0.0f : r;
 }
 
-// silu(x) = x * sigmoid(x), sigmoid with the reference's +-88 input clamp
-// (sigmoid.wgsl:18-19); shared by the unary kernel and the GEMM's GLU epilogue.
-__device__ __forceinline__ float silu_ref(float x) {
+// silu(x) = x * sigmoid(x) = x / (1 + e^(-x)), the exponent with the
+// reference's +-88 sigmoid input clamp (sigmoid.wgsl:18-19), evaluated as
+// 2^(-x log2 e) on the ex2 unit and a fast divide (a few ulp; no branch, no
+// slow division path).  Shared by the unary kernel and the GEMM's GLU
+// epilogue, so the fused and unfused forms agree.
+__device__ __forceinline__ float silu_lib(float x) {
   const float xc = fminf(fmaxf(x, -88.0f), 88.0f);
-  return x * (1.0f / (1.0f + expf(-xc)));
+  return __fdividef(x, 1.0f + fast_exp2(xc * -1.4426950408889634f));
 }
 
 // Records the first device-side error code; later errors are dropped so the

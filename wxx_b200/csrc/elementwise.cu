@@ -211,7 +211,7 @@ __device__ __forceinline__ float apply_unary(int op, float x) {
     case 10: return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f);     // sign
     case 11: return -x;
     case 12: return x * x;
-    case 13: return silu_ref(x);                                      // silu = sigmoid(x) * x
+    case 13: return silu_lib(x);                                      // silu = sigmoid(x) * x
     case 14: {                                                        // selu
       const float alpha = 1.6732632423543772848170429916717f;
       const float scale = 1.0507009873554804934193349852946f;

@@ -128,7 +128,10 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   using C = Cfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<BN>,
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<BN, false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM_BYTES));
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<BN, true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         C::SMEM_BYTES));
     attr_set = true;
@@ -151,7 +154,12 @@ int launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b
   WXX_REQUIRE(p.epi.tma_store || (p.epi.act == 0 && p.epi.res == nullptr),
               "gemm: a fused activation/residual needs a TMA-storable C");
   int grid = (int)(tiles < wxx::num_sms() ? tiles : wxx::num_sms());
-  tc_gemm_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
+  if (p.epi.act == 2)
+    tc_gemm_kernel<BN, true><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1,
+                                                                                mc, p);
+  else
+    tc_gemm_kernel<BN, false><<<grid, NUM_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0,
+                                                                                 b1, mc, p);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }
@@ -163,7 +171,10 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   using C = PairCfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN>,
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM_BYTES));
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         C::SMEM_BYTES));
     attr_set = true;
@@ -185,7 +196,7 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     cfg.dynamicSmemBytes = C::SMEM_BYTES;
     cfg.stream = wxx::stream();
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void*)tc_gemm_pair_kernel<BN>, &cfg) !=
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)tc_gemm_pair_kernel<BN, false>, &cfg) !=
             cudaSuccess ||
         n <= 0) {
       cudaGetLastError();
@@ -223,8 +234,12 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     p.sk_ws = (float*)ws;
     p.sk_flags = (int*)flags;
   }
-  tc_gemm_pair_kernel<BN><<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1,
-                                                                                     mc, p);
+  if (p.epi.act == 2)
+    tc_gemm_pair_kernel<BN, true><<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(
+        a0, a1, b0, b1, mc, p);
+  else
+    tc_gemm_pair_kernel<BN, false><<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(
+        a0, a1, b0, b1, mc, p);
   cudaError_t e = cudaGetLastError();
   wxx::count_launch();
   int st_ws = wxx_free(ws);       // stream-ordered: valid for the kernel just enqueued

@@ -755,6 +755,10 @@ __device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
 
 // Epilogue math of the TMA-store path for row m, columns n0..n0+31:
 // v = act(alpha * v + bias[n]) + res[m, n].
+// POST: apply the convolution post-ops (batchnorm, ReLU) when EpiParams.post
+// asks for them; the SM-pair kernel, which never computes a convolution,
+// compiles without them.
+template <bool POST = true>
 __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, int n0,
                                           float (&v)[32]) {
   const EpiParams& e = p.epi;
@@ -771,7 +775,7 @@ __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, in
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
   }
-  if (e.post.rm != nullptr) {
+  if (POST && e.post.rm != nullptr) {
     // eval batchnorm of column n (the batchnorm kernel's expression)
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -797,30 +801,33 @@ __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, in
         if (n0 + j < p.N) v[j] += __ldg(r + j);
     }
   }
-  if (e.post.relu) {
+  if (POST && e.post.relu) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = fmaxf(0.0f, v[j]);
   }
 }
 
 // act == 2 (paired GLU): product columns 2j and 2j+1 are the gate and the up
-// projection of output column j, out[j] = silu(gate) * up.  v holds product
-// columns n0 .. n0+31 and w columns n0+32 .. n0+63, both after alpha and
-// bias; on return v holds output columns n0/2 .. n0/2 + 31.
-__device__ __forceinline__ void epi_glu(float (&v)[32], const float (&w)[32]) {
-  float o[32];
+// projection of output column j, out[j] = silu(gate) * up.  Reads product
+// columns n0 .. n0+63 of this thread's row from TMEM in two halves (alpha and
+// bias applied) and leaves output columns n0/2 .. n0/2 + 31 in v.
+template <bool POST>
+__device__ __forceinline__ void epi_glu_load(const GemmParams& p, int bt, int m, int n0,
+                                             uint32_t taddr, float (&v)[32]) {
+  float w[32];
+  tmem_ld_32x32(taddr, w);
+  epi_apply<POST>(p, bt, m, n0, w);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    o[j] = silu_ref(v[2 * j]) * v[2 * j + 1];
-    o[16 + j] = silu_ref(w[2 * j]) * w[2 * j + 1];
-  }
+  for (int j = 0; j < 16; ++j) v[j] = silu_lib(w[2 * j]) * w[2 * j + 1];
+  tmem_ld_32x32(taddr + 32u, w);
+  epi_apply<POST>(p, bt, m, n0 + 32, w);
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = o[j];
+  for (int j = 0; j < 16; ++j) v[16 + j] = silu_lib(w[2 * j]) * w[2 * j + 1];
 }
 
 // ------------------------------------------------------------ the kernel
 
-template <int BN>
+template <int BN, bool GLU = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0,
                    const __grid_constant__ CUtensorMap tm_a1,
@@ -989,21 +996,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int m0 = tm * BM + quarter * 32;
       uint32_t row_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      const bool glu = p.epi.act == 2;
+      constexpr bool glu = GLU;   // host: GLU <=> p.epi.act == 2
 #pragma unroll 1
       for (int c = 0; c < BN; c += glu ? 64 : 32) {
         float v[32];
-        tmem_ld_32x32(row_addr + (uint32_t)c, v);
         int n0 = tn * BN + c;
-        if (n0 >= p.N) continue;
         int nc = n0;  // output column of v[0]
-        if (glu) {
-          float w[32];
-          tmem_ld_32x32(row_addr + (uint32_t)(c + 32), w);
-          epi_apply(p, bt, m0 + lane, n0, v);
-          epi_apply(p, bt, m0 + lane, n0 + 32, w);
-          epi_glu(v, w);
+        if constexpr (glu) {
+          if (n0 >= p.N) continue;
+          epi_glu_load<true>(p, bt, m0 + lane, n0, row_addr + (uint32_t)c, v);
           nc = n0 / 2;
+        } else {
+          tmem_ld_32x32(row_addr + (uint32_t)c, v);
+          if (n0 >= p.N) continue;
         }
         if (use_tma) {
           // alpha, bias, activation and residual in registers, row ->
@@ -1155,7 +1160,7 @@ struct PairCfg {
   static_assert(TMEM_COLS <= 512, "TMEM");
 };
 
-template <int BN>
+template <int BN, bool GLU = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a0,
                         const __grid_constant__ CUtensorMap tm_a1,
@@ -1375,21 +1380,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
         if (!ready) break;
         prow = p.sk_ws + (((int64_t)(pair - 1) * 2 + rank) * 4 + quarter) * (32 * BN);
       }
-      const bool glu = p.epi.act == 2;  // never with stream-K partials (host)
+      constexpr bool glu = GLU;  // host: GLU <=> p.epi.act == 2, never with stream-K partials
 #pragma unroll 1
       for (int c = 0; c < BN && m0 < p.M; c += glu ? 64 : 32) {
         const int n0 = tn * BN + c;
         if (n0 >= p.N) break;
         float v[32];
-        tmem_ld_32x32(row_addr + (uint32_t)c, v);
         int nc = n0;
-        if (glu) {
-          float w[32];
-          tmem_ld_32x32(row_addr + (uint32_t)(c + 32), w);
-          epi_apply(p, bt, m0 + lane, n0, v);
-          epi_apply(p, bt, m0 + lane, n0 + 32, w);
-          epi_glu(v, w);
+        if constexpr (glu) {
+          epi_glu_load<false>(p, bt, m0 + lane, n0, row_addr + (uint32_t)c, v);
           nc = n0 / 2;
+        } else {
+          tmem_ld_32x32(row_addr + (uint32_t)c, v);
         }
         if (prow != nullptr) {
 #pragma unroll
@@ -1401,7 +1403,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
             v[4 * q + 3] += w.w;
           }
         }
-        if (!glu) epi_apply(p, bt, m0 + lane, n0, v);
+        if (!glu) epi_apply<false>(p, bt, m0 + lane, n0, v);
         uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
         if (lane == 0) bulk_wait_read<1>();
         __syncwarp();
