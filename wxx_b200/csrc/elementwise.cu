@@ -378,14 +378,28 @@ __global__ void __launch_bounds__(256) causal_conv1d_tr_kernel(
   const int rows = kConvTileN + K - 1;
   const float* xb = x + x_off + (int64_t)b * sb;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int r = warp; r < rows; r += 8) {
+  // all of this warp's rows (at most kRowsPerWarp) loaded before any store:
+  // up to 36 loads in flight per thread
+  constexpr int kRowsPerWarp = (kConvTileN + kConvMaxK - 1 + 7) / 8;
+  float vals[kRowsPerWarp][kConvTileD / 32];
+#pragma unroll
+  for (int it = 0; it < kRowsPerWarp; ++it) {
+    const int r = warp + 8 * it;
     const int n = n0 - (K - 1) + r;
-    const bool in = n >= 0 && n < L;
+    const bool in = r < rows && n >= 0 && n < L;
     const float* xr = xb + (int64_t)n * sl + d0;
 #pragma unroll
     for (int j = 0; j < kConvTileD / 32; ++j) {
       const int dd = 32 * j + lane;
-      tile[r * kConvPitch + dd] = (in && d0 + dd < D) ? xr[dd] : 0.f;
+      vals[it][j] = (in && d0 + dd < D) ? __ldg(xr + dd) : 0.f;
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < kRowsPerWarp; ++it) {
+    const int r = warp + 8 * it;
+    if (r < rows) {
+#pragma unroll
+      for (int j = 0; j < kConvTileD / 32; ++j) tile[r * kConvPitch + 32 * j + lane] = vals[it][j];
     }
   }
   __syncthreads();
