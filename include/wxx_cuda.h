@@ -175,6 +175,18 @@ int wxx_linear_batched(float* C, const float* A, const float* B, const float* bi
                        const float* residual, int64_t batch, int64_t M, int64_t N, int64_t K,
                        int64_t a_bs, int64_t lda, int trans_a, int64_t ldb, int trans_b, int act,
                        float alpha, int mode);
+/* nn/hyena.py:227-234 (HyenaOperator.forward): v = short_conv(proj_v(x).transpose(1, 2)) and
+ * the gates short_conv(chunk(proj_x(x))[i].transpose(1, 2)) in one tcgen05 GEMM whose epilogue
+ * applies the causal taps (CausalShortConv1d, nn/hyena.py:77-99) and writes channels first.
+ * Y (M, N) = A @ op(B) + bias with row = b * seq_len + n (M a multiple of seq_len);
+ * out[b, c, n] (M/seq_len, N, seq_len dense) = conv_b[c'] + sum_{k < conv_k, k <= n}
+ * conv_w[c', k] * Y[row - k, c], c' = c % conv_ch.  A (M, K) row stride lda; B (K, N) row
+ * stride ldb, or (N, K) with trans_b; bias (N) or NULL; conv_k 1..4; mode 0 TF32, 1 3xTF32
+ * (K <= 1024).  WXX_E_UNSUPPORTED, nothing enqueued, when A or B is not TMA-addressable. */
+int wxx_linear_short_conv(float* out, const float* A, const float* B, const float* bias, int64_t M,
+                          int64_t N, int64_t K, int64_t lda, int64_t ldb, int trans_b,
+                          int64_t seq_len, const float* conv_w, const float* conv_b, int conv_ch,
+                          int conv_k, int mode);
 /* functional/convolution.py:658-729 conv2d (conv2d.wgsl), NCHW implicit GEMM on tcgen05.
  * mode 0 TF32, 1 or 2 3xTF32. */
 int wxx_conv2d(float* Y, const float* X, const float* W, const float* bias, int B, int Cin,

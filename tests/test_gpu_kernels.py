@@ -811,3 +811,65 @@ def test_matmul_3xtf32_long_k_stays_fp32_faithful(batch, M, N, kdim, rng):
         F.set_matmul_mode("tf32")
     assert rel(got, K.matmul_add(a, b, bias)) < 1e-5
     assert _w().backend.device_status() == 0
+
+
+# ------------------------------------------------------------ projection + short conv
+
+def _short_conv_ref(x, w, b, cw, cb):
+    """Oracle: y = x @ w (+ b), transposed to (B, N, L), then the causal taps
+    of conv row c % C on channel c."""
+    y = K.matmul_add(x, w, b)                      # (B, L, N)
+    yt = np.ascontiguousarray(y.transpose(0, 2, 1))
+    C = cw.shape[0]
+    reps = yt.shape[1] // C
+    return K.causal_conv1d(yt, np.tile(cw, (reps, 1)), np.tile(cb, reps))
+
+
+@pytest.mark.parametrize("shape", [(2, 300, 64, 128, 64, 3), (3, 257, 32, 96, 96, 4),
+                                   (2, 1000, 256, 1024, 256, 3), (1, 64, 64, 64, 64, 1),
+                                   (4, 33, 16, 32, 16, 2), (5, 1, 32, 64, 64, 3),
+                                   (2, 8192, 256, 256, 256, 3)])
+@pytest.mark.parametrize("mode,tol", [("tf32", 2e-3), ("3xtf32", 1e-5)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_linear_short_conv(shape, mode, tol, with_bias, rng):
+    """Hyena's proj -> transpose -> short causal conv as one GEMM whose
+    epilogue applies the taps (rows of a tile overlap by taps - 1 so every
+    warp holds its own halo): against the composition of the separate GEMM,
+    transposed view and causal conv kernels, and the oracle.  Shapes cover
+    one and many pair tiles, sequence boundaries inside a warp's rows
+    (L = 33, 257, 300), one-position sequences and 1..4 taps."""
+    F = _w().functional
+    B, L, Kd, N, C, taps = shape
+    x = rng.standard_normal((B, L, Kd)).astype(np.float32)
+    w = (rng.standard_normal((Kd, N)) / np.sqrt(Kd)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32) if with_bias else None
+    cw = rng.standard_normal((C, taps)).astype(np.float32)
+    cb = rng.standard_normal(C).astype(np.float32)
+    F.set_matmul_mode(mode)
+    try:
+        bd = None if b is None else up(b)
+        got = F.linear_short_conv(up(x), up(w), bd, up(cw), up(cb)).numpy()
+        y = F.linear(up(x), up(w), bd).transpose(1, 2)
+        parts = [F.causal_conv1d(y[:, i * C:(i + 1) * C, :], up(cw), up(cb)).numpy()
+                 for i in range(N // C)]
+    finally:
+        F.set_matmul_mode("tf32")
+    composed = np.concatenate(parts, axis=1)
+    ref = _short_conv_ref(x, w, b, cw, cb)
+    assert got.shape == (B, N, L)
+    assert rel(got, ref) < tol
+    assert rel(got, composed) < (1e-5 if mode == "tf32" else 1e-6)
+    assert _w().backend.device_status() == 0
+
+
+def test_linear_short_conv_unaligned_input_falls_back(rng):
+    """K = 6 (rows not 16-byte aligned for the tensor memory accelerator): the
+    library reports the fused form unsupported and the composition runs."""
+    F = _w().functional
+    x = rng.standard_normal((2, 40, 6)).astype(np.float32)
+    w = rng.standard_normal((6, 8)).astype(np.float32)
+    cw = rng.standard_normal((8, 3)).astype(np.float32)
+    cb = rng.standard_normal(8).astype(np.float32)
+    got = F.linear_short_conv(up(x), up(w), None, up(cw), up(cb)).numpy()
+    assert rel(got, _short_conv_ref(x, w, None, cw, cb)) < 2e-3
+    assert _w().backend.device_status() == 0

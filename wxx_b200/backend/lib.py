@@ -89,6 +89,8 @@ SIGNATURES = {
                    c_i64, c_int, c_int, c_float, c_int],
     "wxx_linear_batched": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64,
                            c_i64, c_i64, c_i64, c_int, c_i64, c_int, c_int, c_float, c_int],
+    "wxx_linear_short_conv": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64,
+                              c_i64, c_int, c_i64, c_void_p, c_void_p, c_int, c_int, c_int],
     "wxx_conv2d": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14,
     "wxx_conv2d_bn": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14
                      + [c_void_p] * 4 + [c_float, c_void_p, c_int],

@@ -171,15 +171,21 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   using C = PairCfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, false>,
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, kPairEpiPlain>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         C::SMEM_BYTES));
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, true>,
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, kPairEpiGlu>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM_BYTES));
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, kPairEpiConv>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         C::SMEM_BYTES));
     attr_set = true;
   }
-  p.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+  // Rows per pair tile: 256, or for the short-conv epilogue 8 warps of 32 rows
+  // whose first conv_k - 1 rows overlap the previous warp's.
+  const int tile_rows = p.epi.kind == 2 ? 8 * (32 - (p.epi.conv_k - 1)) : 2 * BM;
+  p.tiles_m = (p.M + tile_rows - 1) / tile_rows;
   p.tiles_n = (p.N + BN - 1) / BN;
   int64_t a_bytes = (int64_t)p.M * p.K * 4;
   p.group_m = (a_bytes <= (48ll << 20) || p.tiles_m <= 8) ? p.tiles_m : 8;
@@ -196,7 +202,7 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     cfg.dynamicSmemBytes = C::SMEM_BYTES;
     cfg.stream = wxx::stream();
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void*)tc_gemm_pair_kernel<BN, false>, &cfg) !=
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)tc_gemm_pair_kernel<BN, kPairEpiPlain>, &cfg) !=
             cudaSuccess ||
         n <= 0) {
       cudaGetLastError();
@@ -214,7 +220,8 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   // gained 8 %.
   const char* sk_env = getenv("WXX_GEMM_STREAMK");
   const int64_t waves = (tiles + pairs - 1) / pairs;
-  const bool sk = sk_env != nullptr && sk_env[0] == '1' && p.epi.act != 2 && tiles >= pairs &&
+  const bool sk = sk_env != nullptr && sk_env[0] == '1' && p.epi.act != 2 && p.epi.kind == 0 &&
+                  tiles >= pairs &&
                   (double)tiles / (double)(waves * pairs) < 0.95;
   void* ws = nullptr;
   void* flags = nullptr;
@@ -234,12 +241,15 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     p.sk_ws = (float*)ws;
     p.sk_flags = (int*)flags;
   }
-  if (p.epi.act == 2)
-    tc_gemm_pair_kernel<BN, true><<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(
-        a0, a1, b0, b1, mc, p);
+  if (p.epi.kind == 2)
+    tc_gemm_pair_kernel<BN, kPairEpiConv>
+        <<<2 * pairs, PAIR_THREADS_CONV, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
+  else if (p.epi.act == 2)
+    tc_gemm_pair_kernel<BN, kPairEpiGlu>
+        <<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
   else
-    tc_gemm_pair_kernel<BN, false><<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(
-        a0, a1, b0, b1, mc, p);
+    tc_gemm_pair_kernel<BN, kPairEpiPlain>
+        <<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
   cudaError_t e = cudaGetLastError();
   wxx::count_launch();
   int st_ws = wxx_free(ws);       // stream-ordered: valid for the kernel just enqueued
@@ -744,6 +754,93 @@ WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float*
   if (M * N == 0) return WXX_OK;
   return matmul_impl(C, A, B, bias, 1, M, N, K, 0, 0, lda, ldb, 0, trans_b, bias ? 1 : 0, alpha,
                      mode, act, residual);
+}
+
+// Linear projection followed by a depthwise short causal convolution along
+// the sequence, written channels-first: Hyena's projection, transpose and
+// short conv (hyena.py: proj_v / proj_x, transpose(1, 2), short_conv) in one
+// tcgen05 GEMM whose epilogue applies the taps.
+//   Y (M, N) = alpha * A @ op(B) + bias, row = b * seq_len + n
+//   out[b, c, n] (M / seq_len, N, seq_len dense) = conv_b[c']
+//       + sum over k < conv_k with k <= n of conv_w[c', k] * Y[row - k, c],  c' = c % conv_ch
+// A (M, K) with row stride lda, B (K, N) row stride ldb or (N, K) with
+// trans_b, bias (N) or NULL, conv_w (conv_ch, conv_k), conv_b (conv_ch);
+// conv_k in 1..4; mode 0 TF32, 1 3xTF32 (K <= 1024).  Returns
+// WXX_E_UNSUPPORTED (nothing enqueued) when A or B is not TMA-addressable.
+WXX_EXPORT int wxx_linear_short_conv(float* out, const float* A, const float* B, const float* bias,
+                                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                     int trans_b, int64_t seq_len, const float* conv_w,
+                                     const float* conv_b, int conv_ch, int conv_k, int mode) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(M >= 0 && N >= 0 && K > 0 && seq_len > 0,
+              "wxx_linear_short_conv: bad sizes (K and seq_len must be positive)");
+  WXX_REQUIRE(M % seq_len == 0, "wxx_linear_short_conv: M = %lld is not a multiple of seq_len %lld",
+              (long long)M, (long long)seq_len);
+  WXX_REQUIRE(conv_k >= 1 && conv_k <= 4, "wxx_linear_short_conv: conv_k %d not in 1..4", conv_k);
+  WXX_REQUIRE(conv_ch >= 1 && conv_w != nullptr && conv_b != nullptr,
+              "wxx_linear_short_conv: conv weights missing");
+  WXX_REQUIRE(mode == 0 || mode == 1, "wxx_linear_short_conv: mode %d not in {0, 1}", mode);
+  WXX_REQUIRE(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31),
+              "wxx_linear_short_conv: dimension exceeds 2^31");
+  if (M * N == 0) return WXX_OK;
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = 1;
+  p.num_kb = (int)((K + BK - 1) / BK);
+  p.passes = mode == 1 ? 3 : 1;
+  p.splits = 1;
+  p.kb_per_split = p.num_kb * p.passes;
+  p.err = wxx::device_error_word();
+  if (p.passes > 1 && p.num_kb * p.passes > kMaxChainKb3x) {
+    wxx::set_error("wxx_linear_short_conv: 3xTF32 with K = %lld > 1024 is not fused",
+                   (long long)K);
+    return WXX_E_UNSUPPORTED;
+  }
+  p.epi.kind = 2;
+  p.epi.C = out;
+  p.epi.c_bs = N * seq_len;
+  p.epi.ldc = (int)N;
+  p.epi.bias = bias;
+  p.epi.bias_mode = bias ? 1 : 0;
+  p.epi.alpha = 1.0f;
+  p.epi.conv_len = (int)seq_len;
+  p.epi.conv_k = conv_k;
+  p.epi.conv_ch = conv_ch;
+  p.epi.conv_w = conv_w;
+  p.epi.conv_b = conv_b;
+  CUtensorMap ma0, ma1, mb0, mb1, mc;
+  memset(&ma0, 0, sizeof(ma0));
+  memset(&mb0, 0, sizeof(mb0));
+  memset(&mc, 0, sizeof(mc));
+  OperandDesc da{A, M, K, 1, lda, 0, true, false};
+  OperandDesc db{B, N, K, 1, ldb, 0, trans_b != 0, false};
+  setup_operand(da, 32, true, p.a, &ma0);   // 32-row boxes, one per epilogue warp
+  setup_operand(db, BM, true, p.b, &mb0);
+  if (p.a.kind != 0 || p.b.kind >= 2) {
+    wxx::set_error("wxx_linear_short_conv: operands are not TMA-addressable (16-byte aligned "
+                   "rows needed)");
+    return WXX_E_UNSUPPORTED;
+  }
+  ma1 = ma0;
+  mb1 = mb0;
+  void* lo_a = nullptr;
+  void* lo_b = nullptr;
+  if (mode == 1) {
+    int st = make_residual(da, p.a, 32, &ma1, &lo_a);
+    if (st == WXX_OK) st = make_residual(db, p.b, BM, &mb1, &lo_b);
+    if (st != WXX_OK) {
+      wxx_free(lo_a);
+      wxx_free(lo_b);
+      return st;
+    }
+  }
+  int st = launch_pair<256>(ma0, ma1, mb0, mb1, mc, p);
+  int st_a = wxx_free(lo_a);
+  int st_b = wxx_free(lo_b);
+  return st ? st : (st_a ? st_a : st_b);
 }
 
 // Y (NCHW [B, Cout, Ho, Wo]) = conv2d(X [B, Cin, H, W], Wt [Cout, Cin, KH, KW]) (+ bias[Cout])

@@ -376,7 +376,8 @@ __device__ __forceinline__ float conv_post(const ConvPost& c, float v, int n, in
 }
 
 struct EpiParams {
-  int kind;               // 0 = row-major matrix C, 1 = NCHW convolution output
+  int kind;               // 0 = row-major matrix C, 1 = NCHW convolution output,
+                          // 2 = short causal conv along rows, written (B, N, L) (pair kernel)
   float* C;
   int64_t c_bs;           // batch stride of C (elements)
   int ldc;                // row stride of C (elements), kind 0
@@ -392,6 +393,12 @@ struct EpiParams {
   int64_t res_ld, res_bs;
   int raw;                // split-K: raw partial sums to the workspace map, z = batch * splits + slice
   ConvPost post;          // kind 1 only
+  // kind 2: rows are (sequence b, position n) = (row / conv_len, row % conv_len);
+  // C[b, c, n] (c_bs = N * conv_len) = conv_b[c'] + sum_k conv_w[c', k] * Y[row - k, c]
+  // over taps k < conv_k with n >= k, c' = c % conv_ch, Y = alpha * AB + bias.
+  int conv_len, conv_k, conv_ch;
+  const float* conv_w;
+  const float* conv_b;
 };
 
 struct GemmParams {
@@ -825,6 +832,125 @@ __device__ __forceinline__ void epi_glu_load(const GemmParams& p, int bt, int m,
   for (int j = 0; j < 16; ++j) v[16 + j] = silu_lib(w[2 * j]) * w[2 * j + 1];
 }
 
+// Short causal convolution epilogue (EpiParams kind 2).
+//
+// conv_stage_weights: once per tile, each epilogue warp copies the taps of
+// the tile's BN columns into its own 8 KB of shared memory, column c at
+// ws[8 c] = (w0, w1, w2, conv bias, w3, projection bias, 0, 0): the loads of
+// all columns are in flight together, and the chunk loop below reads them as
+// warp-uniform (broadcast) 16-byte shared loads -- one per column for up to
+// three taps without a projection bias -- instead of waiting on a global
+// load per column.
+__device__ __forceinline__ void conv_stage_weights(const GemmParams& p, int c0, int cnt, int lane,
+                                                   float* ws) {
+  const EpiParams& e = p.epi;
+  const int K = e.conv_k;
+#pragma unroll 4
+  for (int cl = lane; cl < cnt; cl += 32) {
+    const int c = c0 + cl;
+    float4 w = make_float4(0.f, 0.f, 0.f, 0.f), t = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < p.N) {
+      const int cw = c % e.conv_ch;
+      const float* wr = e.conv_w + (int64_t)cw * K;
+      w.x = __ldg(wr);
+      if (K > 1) w.y = __ldg(wr + 1);
+      if (K > 2) w.z = __ldg(wr + 2);
+      w.w = __ldg(e.conv_b + cw);
+      if (K > 3) t.x = __ldg(wr + 3);
+      if (e.bias_mode == 1) t.y = __ldg(e.bias + c);
+    }
+    reinterpret_cast<float4*>(ws)[2 * cl] = w;
+    reinterpret_cast<float4*>(ws)[2 * cl + 1] = t;
+  }
+  __syncwarp();
+}
+
+// One 32-column chunk: lane i holds row `row` (= the warp's first row + i),
+// v[j] its column n0 + j (local column cl0 + j of the tile).  Taps reach back
+// up to three rows, which sit in lanes i-1 .. i-3 of the same warp (the tile
+// rows overlap so that the first KT - 1 lanes of every warp are such halo
+// rows; they are not stored).  Lanes hold consecutive positions, so each
+// column's store is one coalesced run along n of the (B, N, L) output.  The
+// tap order and the multiply-adds are those of the standalone causal conv.
+// KT (the tap count) is a template parameter so that a group of 8 columns is
+// one branch-free block the compiler interleaves; the group's tap loads come
+// before its first global store (a load cannot move across a store it may
+// alias), so one shared-memory latency covers 8 columns.
+template <int KT>
+__device__ __forceinline__ void epi_conv_tr(const GemmParams& p, int row, bool own, int n0,
+                                            int cl0, const float* ws, const float (&v)[32]) {
+  const EpiParams& e = p.epi;
+  const int L = e.conv_len;
+  own = own && row >= 0 && row < p.M;
+  const int rr = row < 0 ? 0 : row;
+  const int b = rr / L, n = rr - b * L;
+  float* out = e.C + (int64_t)b * e.c_bs + n;
+  const float4* wq = reinterpret_cast<const float4*>(ws) + 2 * cl0;
+  const bool has_bias = e.bias_mode == 1;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float4 w[8], t[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) w[q] = wq[2 * (8 * g + q)];
+    if (KT > 3 || has_bias) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t[q] = wq[2 * (8 * g + q) + 1];
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) t[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float x[8], acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      x[q] = has_bias ? v[8 * g + q] * e.alpha + t[q].y : v[8 * g + q] * e.alpha;
+      acc[q] = w[q].w;
+      acc[q] = acc[q] + w[q].x * x[q];
+    }
+    if constexpr (KT > 1) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float x1 = __shfl_up_sync(0xffffffffu, x[q], 1);
+        if (n >= 1) acc[q] = acc[q] + w[q].y * x1;
+      }
+    }
+    if constexpr (KT > 2) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float x2 = __shfl_up_sync(0xffffffffu, x[q], 2);
+        if (n >= 2) acc[q] = acc[q] + w[q].z * x2;
+      }
+    }
+    if constexpr (KT > 3) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float x3 = __shfl_up_sync(0xffffffffu, x[q], 3);
+        if (n >= 3) acc[q] = acc[q] + t[q].x * x3;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int c = n0 + 8 * g + q;
+      if (own && c < p.N) out[(int64_t)c * L] = acc[q];
+    }
+  }
+}
+
+// Columns [c0, c0 + cnt) of the tile (TMEM columns from row_addr on) for a
+// warp whose first row is mc.
+template <int KT>
+__device__ __forceinline__ void epi_conv_tile(const GemmParams& p, int c0, int cnt, int mc,
+                                              int lane, uint32_t row_addr, float* ws) {
+  constexpr int hal = KT - 1;
+#pragma unroll 1
+  for (int c = 0; c < cnt; c += 32) {
+    const int n0 = c0 + c;
+    if (n0 >= p.N) break;
+    float v[32];
+    tmem_ld_32x32(row_addr + (uint32_t)c, v);
+    epi_conv_tr<KT>(p, mc + lane, lane >= hal, n0, c, ws, v);
+  }
+}
+
 // ------------------------------------------------------------ the kernel
 
 template <int BN, bool GLU = false>
@@ -1086,6 +1212,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // Roles per CTA: warp 0 TMA producer, warp 1 TMEM allocator (+ MMA issuer in
 // the leader), warps 2..5 epilogue of this CTA's 128 rows.
 constexpr int PAIR_THREADS = 192;
+// The short-conv epilogue (EpiParams kind 2) runs 8 epilogue warps: two per
+// TMEM lane quarter, each on half of the tile's columns, so every SM
+// sub-partition has a second warp to issue while one waits.
+constexpr int PAIR_THREADS_CONV = 320;
 
 // First K-block iteration of pair q when W iterations are shared by P pairs.
 __device__ __forceinline__ int64_t sk_start(int q, int64_t W, int P) {
@@ -1158,16 +1288,24 @@ struct PairCfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static_assert(TMEM_COLS <= 512, "TMEM");
+  static_assert(BN * 32 <= EPI_WARP_BYTES, "short-conv taps of a tile fit a warp's staging");
 };
 
-template <int BN, bool GLU = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
+// Epilogue forms of the SM-pair kernel (template parameter EPI).
+constexpr int kPairEpiPlain = 0;   // TMA-store epilogue (bias, GELU, residual, stream-K)
+constexpr int kPairEpiGlu = 1;     // paired GLU (act == 2)
+constexpr int kPairEpiConv = 2;    // short causal conv written (B, N, L) (kind 2), 8 warps
+
+template <int BN, int EPI = kPairEpiPlain>
+__global__ void __cluster_dims__(2, 1, 1)
+    __launch_bounds__(EPI == kPairEpiConv ? PAIR_THREADS_CONV : PAIR_THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a0,
                         const __grid_constant__ CUtensorMap tm_a1,
                         const __grid_constant__ CUtensorMap tm_b0,
                         const __grid_constant__ CUtensorMap tm_b1,
                         const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
   using C = PairCfg<BN>;
+  constexpr bool GLU = EPI == kPairEpiGlu;
   constexpr int PM = 2 * BM;  // rows per pair tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];   // leader: both CTAs' loads landed
@@ -1189,6 +1327,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
   const int total_tiles = p.batch * p.tiles_m * p.tiles_n;
   const int total_kb = p.num_kb * p.passes;
   const int n_units = pair_units(p, pair, num_pairs, total_tiles, total_kb);
+  const int n_epi = (int)(blockDim.x >> 5) - 2;   // 4, or 8 for the short-conv epilogue
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -1198,7 +1337,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull_bar[s], 1);
-      mbar_init(&tempty_bar[s], 2 * 4);   // one arrive per epilogue warp of both CTAs
+      mbar_init(&tempty_bar[s], 2 * n_epi);   // one arrive per epilogue warp of both CTAs
     }
     mbar_init(&drain_bar, 1);
     fence_barrier_init();
@@ -1240,7 +1379,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
           const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
           const int za = p.a.bcast_batch ? 0 : bt;
-          if (p.a.kind == 0) {
+          if (EPI == kPairEpiConv) {
+            // overlapping 32-row boxes: each warp's rows start conv_k - 1 early
+            const int hal = p.epi.conv_k - 1, cu = 32 - hal;
+            const int r0 = tm * 8 * cu + (int)rank * 4 * cu - hal;
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j)
+              tma_load_3d_pair(smem_u32(sa + j * 4096), ma, fb, kc, r0 + j * cu, za);
+          } else if (p.a.kind == 0) {
             tma_load_3d_pair(smem_u32(sa), ma, fb, kc, row_a, za);
           } else {
 #pragma unroll
@@ -1317,7 +1463,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
   } else {
     // ---------------------------------------------------- epilogue (both CTAs)
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
-    uint8_t* wstage = smem + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_WARP_BYTES;
+    const int ew = warp - 2;       // epilogue warp index: 0..3, or 0..7 (kind 2)
+    uint8_t* wstage = smem + C::STAGES * C::STAGE_BYTES + ew * (C::EPI_BYTES / n_epi);
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
     int local = 0;
@@ -1379,6 +1526,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
         ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
         if (!ready) break;
         prow = p.sk_ws + (((int64_t)(pair - 1) * 2 + rank) * 4 + quarter) * (32 * BN);
+      }
+      if constexpr (EPI == kPairEpiConv) {
+        const int hal = p.epi.conv_k - 1, cu = 32 - hal;
+        const int mc = tm * 8 * cu + (int)rank * 4 * cu + quarter * cu - hal;
+        // this warp's columns [c_lo, c_lo + c_cnt) of the tile and its share of
+        // the staging area (32 bytes of taps per column)
+        const int c_cnt = BN * 4 / n_epi;
+        const int c_lo = (ew >> 2) * c_cnt;
+        float* ws = reinterpret_cast<float*>(wstage);
+        if (mc + hal < p.M) {
+          conv_stage_weights(p, tn * BN + c_lo, c_cnt, lane, ws);
+          switch (p.epi.conv_k) {
+            case 1: epi_conv_tile<1>(p, tn * BN + c_lo, c_cnt, mc, lane, row_addr + c_lo, ws); break;
+            case 2: epi_conv_tile<2>(p, tn * BN + c_lo, c_cnt, mc, lane, row_addr + c_lo, ws); break;
+            case 3: epi_conv_tile<3>(p, tn * BN + c_lo, c_cnt, mc, lane, row_addr + c_lo, ws); break;
+            default: epi_conv_tile<4>(p, tn * BN + c_lo, c_cnt, mc, lane, row_addr + c_lo, ws); break;
+          }
+        }
+        __syncwarp();   // the next tile restages ws
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        continue;
       }
       constexpr bool glu = GLU;  // host: GLU <=> p.epi.act == 2, never with stream-K partials
 #pragma unroll 1

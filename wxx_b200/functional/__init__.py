@@ -108,6 +108,7 @@ from .utils import (
     from_numpy,
     from_tensor,
     linear,
+    linear_short_conv,
     linspace,
     masked_fill,
     matmul_add,

@@ -300,6 +300,61 @@ def linear(x, weight, bias=None, *, activation=None, residual=None):
     return out
 
 
+_E_UNSUPPORTED = -4
+
+
+def linear_short_conv(x, weight, bias, conv_weight, conv_bias):
+    """Hyena's projection + transpose + short causal conv (nn/hyena.py:227-234)
+    as one tcgen05 GEMM whose epilogue applies the taps and writes channels
+    first: ``x`` (B, L, K), ``weight`` (K, N), ``bias`` (N,) or None,
+    ``conv_weight`` (C, k), ``conv_bias`` (C,) with column c using conv row
+    c % C.  Returns (B, N, L) = ``causal_conv1d(linear(x, weight,
+    bias).transpose(1, 2))`` with the conv weights tiled over N.  That
+    composition (CUDA kernels too) is taken when the fused kernel does not
+    apply: fp32 SIMT mode, more than four taps, or operands the tensor memory
+    accelerator cannot address."""
+    if len(x.shape) != 3:
+        raise ValueError(f"linear_short_conv expects a (B, L, K) input, got {x.shape}")
+    Bsz, L, K = x.shape
+    w = dense(weight)
+    if len(w.shape) != 2 or w.shape[0] != K:
+        raise ValueError(f"linear_short_conv: weight {tuple(w.shape)} does not match input {x.shape}")
+    N = w.shape[1]
+    if len(conv_weight.shape) != 2 or tuple(conv_bias.shape) != (conv_weight.shape[0],):
+        raise ValueError("linear_short_conv: conv weight must be (C, k) with a (C,) bias")
+    C, taps = conv_weight.shape
+    if N % C:
+        raise ValueError(f"linear_short_conv: {N} output columns are not a multiple of {C} channels")
+    if bias is not None and tuple(bias.shape) != (N,):
+        raise ValueError(f"linear_short_conv: bias {tuple(bias.shape)} is not ({N},)")
+    mode = matmul_mode_code()
+    grad = (x.requires_grad or weight.requires_grad or conv_weight.requires_grad
+            or conv_bias.requires_grad or (bias is not None and bias.requires_grad))
+    if mode in (0, 1) and 1 <= taps <= 4 and K > 0 and Bsz * L * N > 0:
+        a = dense(x)
+        cw = dense(conv_weight)
+        cb = dense(conv_bias)
+        b = dense(bias) if bias is not None else None
+        out = empty([Bsz, N, L], "f32", grad)
+        timer = active_timer()
+        ev0 = timer.start() if timer is not None else None
+        st = F.wxx_linear_short_conv(out.buffer.ptr, a.ptr, w.ptr, None if b is None else b.ptr,
+                                     Bsz * L, N, K, K, N, 0, L, cw.ptr, cb.ptr, C, taps, mode)
+        if st == 0:
+            if timer is not None:
+                timer.stop(ev0, 2.0 * Bsz * L * N * K, f"{Bsz * L}x{N}x{K}conv")
+            return out
+        if st != _E_UNSUPPORTED:
+            check(st, "linear_short_conv")
+    from .convolution import causal_conv1d
+    y = linear(x, weight, bias).transpose(1, 2)
+    if C == N:
+        return causal_conv1d(y, conv_weight, conv_bias)
+    parts = [causal_conv1d(y[:, i * C:(i + 1) * C, :], conv_weight, conv_bias)
+             for i in range(N // C)]
+    return concat(parts, 1)
+
+
 def _equal_impl(tensor1, tensor2, mode, number=0):
     a = dense(tensor1)
     b = dense(tensor2) if tensor2 is not None else None

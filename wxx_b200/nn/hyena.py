@@ -106,12 +106,23 @@ class HyenaOperator(Module):
 
     def forward(self, x, residual=None):
         _, length, _ = x.shape
-        v = self.proj_v(x)
-        gates = list(self.proj_x(x).chunk(self.order, dim=-1))
-        v = v.transpose(1, 2)
-        gates = [g.transpose(1, 2) for g in gates]
-        v = self.short_conv(v)
-        gates = [self.short_conv(g) for g in gates]
+        if context.MODE != 0:
+            # inference: each projection, its transpose and the short conv are
+            # one GEMM writing (B, channels, L); the gates are channel slices
+            conv = self.short_conv
+            v = functional.linear_short_conv(x, self.proj_v.weight, self.proj_v.bias,
+                                             conv.weight, conv.bias)
+            g = functional.linear_short_conv(x, self.proj_x.weight, self.proj_x.bias,
+                                             conv.weight, conv.bias)
+            D = self.d_model
+            gates = [g[:, i * D:(i + 1) * D, :] for i in range(self.order)]
+        else:
+            v = self.proj_v(x)
+            gates = list(self.proj_x(x).chunk(self.order, dim=-1))
+            v = v.transpose(1, 2)
+            gates = [g.transpose(1, 2) for g in gates]
+            v = self.short_conv(v)
+            gates = [self.short_conv(g) for g in gates]
         z = v
         for i in range(self.order):
             h = self.filter_mlp[i](length)
