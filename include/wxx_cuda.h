@@ -114,6 +114,15 @@ int wxx_causal_conv1d(float* out, const float* x, int64_t x_off, int64_t sb, int
 /* functional/pointwise.py:357-404 decay_window (decay_window.wgsl) */
 int wxx_decay_window(float* out, const float* decay, int rows, int channels, int length,
                      int stage);
+/* nn/hyena.py:127-130 ImplicitFilter.forward (Linear -> Sine(omega) -> Linear over the positional
+ * encoding, transposed) and :236-239 (h * decay_window) for all `n` filters of an operator in one
+ * launch, exact fp32: out (n, D, L) dense, filter i = (sin(omega * (pe @ w1[i] + b1[i])) @ w2[i]
+ * + b2[i])^T * exp(-|decay[i, d]| * t).  pe (L, F); w1[i] (F, H), b1[i] (H), w2[i] (H, D),
+ * b2[i] (D) device arrays passed as host arrays of n device pointers; decay (n, D).  n <= 8,
+ * F <= 32, H <= 64 and a multiple of 4, else WXX_E_UNSUPPORTED with nothing enqueued. */
+int wxx_hyena_filters(float* out, const float* pe, int L, int F, int H, int D, int n,
+                      const float* const* w1, const float* const* b1, const float* const* w2,
+                      const float* const* b2, float omega, const float* decay);
 /* functional/fft.py:168-213 complex_mul (complex_mul.wgsl) */
 int wxx_complex_mul(void* out, const void* a, int64_t a_off, const int64_t* stride_a,
                     const void* b, int64_t b_off, const int64_t* stride_b, int rank,

@@ -873,3 +873,64 @@ def test_linear_short_conv_unaligned_input_falls_back(rng):
     got = F.linear_short_conv(up(x), up(w), None, up(cw), up(cb)).numpy()
     assert rel(got, _short_conv_ref(x, w, None, cw, cb)) < 2e-3
     assert _w().backend.device_status() == 0
+
+
+# ------------------------------------------------------------ Hyena implicit filters
+
+def _filters_ref(pe, l1, l2, omega, decay):
+    """fp64 restatement of ImplicitFilter.forward (Linear -> Sine -> Linear,
+    transposed) times decay_window(decay, i, L) for each filter i."""
+    pe = np.asarray(pe, np.float64)
+    L = pe.shape[0]
+    t = np.arange(L, dtype=np.float64)
+    out = []
+    for i, ((w1, b1), (w2, b2)) in enumerate(zip(l1, l2)):
+        hid = np.sin(omega * (pe @ w1.astype(np.float64) + b1))
+        y = (hid @ w2.astype(np.float64) + b2).T
+        out.append(y * np.exp(-np.abs(decay[i].astype(np.float64))[:, None] * t[None, :]))
+    return np.stack(out)
+
+
+@pytest.mark.parametrize("L,F,H,D,n", [(8192, 17, 64, 256, 4), (300, 17, 64, 48, 2),
+                                       (33, 5, 32, 100, 1), (1, 17, 64, 64, 3),
+                                       (1000, 32, 16, 130, 8)])
+def test_hyena_filters(L, F, H, D, n, rng):
+    """All implicit filters of an operator from one exact-fp32 kernel, written
+    (n, D, L): against the fp64 restatement and the composed modules run with
+    3xTF32 products (the default TF32 products err by ~1e-2 after the sine's
+    omega = 10 scaling)."""
+    wxx = _w()
+    Fn = wxx.functional
+    pe = rng.standard_normal((L, F)).astype(np.float32)
+    l1 = [((rng.standard_normal((F, H)) / np.sqrt(F)).astype(np.float32),
+           (0.1 * rng.standard_normal(H)).astype(np.float32)) for _ in range(n)]
+    l2 = [((rng.standard_normal((H, D)) / np.sqrt(H)).astype(np.float32),
+           (0.1 * rng.standard_normal(D)).astype(np.float32)) for _ in range(n)]
+    decay = (0.01 * rng.random((n, D))).astype(np.float32)
+    got = Fn.hyena_filters(up(pe), [(up(w), up(b)) for w, b in l1],
+                           [(up(w), up(b)) for w, b in l2], 10.0, up(decay)).numpy()
+    ref = _filters_ref(pe, l1, l2, 10.0, decay)
+    assert got.shape == (n, D, L)
+    assert rel(got, ref) < 2e-5
+    Fn.set_matmul_mode("3xtf32")
+    try:
+        for i in range(n):
+            y = Fn.linear(up(pe), up(l1[i][0]), up(l1[i][1]))
+            y = (y * 10.0).sin()                      # Sine(omega), nn/module.py
+            y = Fn.linear(y, up(l2[i][0]), up(l2[i][1])).transpose(0, 1)
+            comp = (y * Fn.decay_window(up(decay), i, L)).numpy()
+            assert rel(got[i], comp) < 2e-4
+    finally:
+        Fn.set_matmul_mode("tf32")
+    assert wxx.backend.device_status() == 0
+
+
+def test_hyena_filters_outside_limits_returns_none(rng):
+    Fn = _w().functional
+    pe = up(rng.standard_normal((16, 40)).astype(np.float32))      # F = 40 > 32
+    w1 = up(rng.standard_normal((40, 8)).astype(np.float32))
+    b1 = up(rng.standard_normal(8).astype(np.float32))
+    w2 = up(rng.standard_normal((8, 4)).astype(np.float32))
+    b2 = up(rng.standard_normal(4).astype(np.float32))
+    assert Fn.hyena_filters(pe, [(w1, b1)], [(w2, b2)], 10.0,
+                            up(np.zeros((1, 4), np.float32))) is None

@@ -30,6 +30,7 @@ SOURCES = [
     "gemm.cu",
     "fft.cu",
     "fft_static.cu",
+    "hyena_filter.cu",
     "attention.cu",
     "pool.cu",
     "nccl.cu",

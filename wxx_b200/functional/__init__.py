@@ -80,6 +80,7 @@ from .pointwise import (
     clampbackwards,
     decay_window,
     decay_window_backward,
+    hyena_filters,
     exp,
     log,
     mul_backward,

@@ -140,6 +140,47 @@ def decay_window(decay, stage, length):
     return out
 
 
+def hyena_filters(pe, linears1, linears2, omega, decay):
+    """All ``n`` implicit filters of a Hyena operator (nn/hyena.py:127-130 and
+    :236-239) in one exact-fp32 kernel: filter i is ``(sin(omega * (pe @ W1_i
+    + b1_i)) @ W2_i + b2_i)^T * decay_window(decay, i, L)``, returned as an
+    (n, D, L) tensor.  ``linears1[i]`` / ``linears2[i]`` are ``(weight,
+    bias)`` pairs with weights (F, H) and (H, D).  None when the shapes are
+    outside the kernel's limits (n <= 8, F <= 32, H <= 64 and a multiple of 4);
+    the caller then composes the separate ops."""
+    import ctypes
+
+    L, Fdim = pe.shape
+    n = len(linears1)
+    if n == 0 or len(linears2) != n or tuple(decay.shape)[0] < n:
+        return None
+    H = linears1[0][0].shape[1]
+    D = linears2[0][0].shape[1]
+    if n > 8 or Fdim > 32 or H > 64 or H % 4:
+        return None
+    for (w1, b1), (w2, b2) in zip(linears1, linears2):
+        if (tuple(w1.shape) != (Fdim, H) or b1 is None or tuple(b1.shape) != (H,)
+                or tuple(w2.shape) != (H, D) or b2 is None or tuple(b2.shape) != (D,)):
+            return None
+    if tuple(decay.shape)[1] != D:
+        return None
+    keep = [dense(t) for pair in list(linears1) + list(linears2) for t in pair]
+    ptrs = [t.ptr for t in keep]
+    arr = ctypes.c_void_p * n
+    w1p = arr(*ptrs[0:2 * n:2])
+    b1p = arr(*ptrs[1:2 * n:2])
+    w2p = arr(*ptrs[2 * n::2])
+    b2p = arr(*ptrs[2 * n + 1::2])
+    pd = dense(pe)
+    dd = dense(decay)
+    out = empty((n, D, L), "f32", False)
+    st = F.wxx_hyena_filters(out.buffer.ptr, pd.ptr, L, Fdim, H, D, n, w1p, b1p, w2p, b2p,
+                             float(omega), dd.ptr)
+    if st != 0:
+        check(st, "hyena_filters")
+    return out
+
+
 def _training_only(name):
     def fn(*args, **kwargs):
         raise NotImplementedError(f"{name} is a training kernel; not part of this backend")

@@ -104,6 +104,26 @@ class HyenaOperator(Module):
     def _decay_window(self, stage, length):
         return autograd.decay_window(self.decay).forward(self.decay, stage, length)
 
+    def _filters_fused(self, length):
+        """Inference: every filter_mlp[i](length) * decay_window(i) of this
+        operator from one kernel, as an (order, D, L) tensor; None when the
+        filters do not have the plain Linear -> Sine -> Linear form or exceed
+        the kernel's limits."""
+        lin1, lin2, omegas, pes = [], [], set(), set()
+        for filt in self.filter_mlp:
+            mods = list(filt.mlp._modules.values())
+            if (len(mods) != 3 or not isinstance(mods[0], Linear) or not isinstance(mods[1], Sine)
+                    or not isinstance(mods[2], Linear)):
+                return None
+            lin1.append((mods[0].weight, mods[0].bias))
+            lin2.append((mods[2].weight, mods[2].bias))
+            omegas.add(mods[1].omega)
+            pes.add(filt.positional_encoding.features)
+        if len(omegas) != 1 or len(pes) != 1:
+            return None
+        pe = self.filter_mlp[0].positional_encoding(length)
+        return functional.hyena_filters(pe, lin1, lin2, omegas.pop(), self.decay)
+
     def forward(self, x, residual=None):
         _, length, _ = x.shape
         if context.MODE != 0:
@@ -124,9 +144,13 @@ class HyenaOperator(Module):
             v = self.short_conv(v)
             gates = [self.short_conv(g) for g in gates]
         z = v
+        hs = self._filters_fused(length) if context.MODE != 0 else None
         for i in range(self.order):
-            h = self.filter_mlp[i](length)
-            h = h * self._decay_window(i, length)
+            if hs is not None:
+                h = hs[i]
+            else:
+                h = self.filter_mlp[i](length)
+                h = h * self._decay_window(i, length)
             z = self.fft_conv1d(z, h, gate=gates[i])
         if residual is not None:
             # the block's residual add rides in the projection's GEMM epilogue
