@@ -934,3 +934,52 @@ def test_hyena_filters_outside_limits_returns_none(rng):
     b2 = up(rng.standard_normal(4).astype(np.float32))
     assert Fn.hyena_filters(pe, [(w1, b1)], [(w2, b2)], 10.0,
                             up(np.zeros((1, 4), np.float32))) is None
+
+
+# ------------------------------------------------------------ K-major weights, strided q/k/v
+
+@pytest.mark.parametrize("M,Kd,N", [(300, 64, 72), (4096, 1024, 3072), (130, 40, 200)])
+@pytest.mark.parametrize("act,res", [(None, False), ("gelu", False), (None, True)])
+@pytest.mark.parametrize("mode,tol", [("tf32", 2e-3), ("3xtf32", 1e-5)])
+def test_linear_transposed_weight(M, Kd, N, act, res, mode, tol, rng):
+    """linear(x, W^T stored (N, K), transpose_weight=True) -- the K-major
+    operand GPT2's inference layers feed the GEMM -- against the (K, N)
+    layout and the oracle."""
+    F = _w().functional
+    x = rng.standard_normal((M, Kd)).astype(np.float32)
+    w = (rng.standard_normal((Kd, N)) / np.sqrt(Kd)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    r = rng.standard_normal((M, N)).astype(np.float32) if res else None
+    F.set_matmul_mode(mode)
+    try:
+        rd = None if r is None else up(r)
+        got = F.linear(up(x), up(np.ascontiguousarray(w.T)), up(b), activation=act, residual=rd,
+                       transpose_weight=True).numpy()
+        plain = F.linear(up(x), up(w), up(b), activation=act, residual=rd).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    ref = K.matmul_add(x, w, b)
+    if act == "gelu":
+        ref = K.unary(ref, "gelu")
+    if r is not None:
+        ref = ref + r
+    assert got.shape == (M, N)
+    assert rel(got, ref) < tol
+    assert rel(got, plain) < (1e-5 if mode == "tf32" else 1e-6)
+
+
+@pytest.mark.parametrize("B,S,H,hd", [(2, 256, 4, 64), (3, 100, 2, 32)])
+def test_attention_reads_column_blocks_in_place(B, S, H, hd, rng):
+    """q, k, v given as column blocks of one (B, S, 3D) projection output
+    (row stride 3D): the kernel reads them in place, same bits as dense
+    copies."""
+    F = _w().functional
+    D = H * hd
+    qkv = rng.standard_normal((B, S, 3 * D)).astype(np.float32)
+    t = up(qkv)
+    q, k, v = t[..., 0:D], t[..., D:2 * D], t[..., 2 * D:3 * D]
+    got = F.attention(q, k, v, H, causal=True).numpy()
+    dq, dk, dv = (up(np.ascontiguousarray(qkv[..., i * D:(i + 1) * D])) for i in range(3))
+    ref = F.attention(dq, dk, dv, H, causal=True).numpy()
+    assert np.array_equal(got, ref)
+    assert _w().backend.device_status() == 0

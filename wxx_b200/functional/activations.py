@@ -96,6 +96,21 @@ def attention_supported(q, n_heads, mask=None):
     return True
 
 
+def _attention_rows(t):
+    """(t, row stride) for a (B, S, D) operand whose rows are unit-stride,
+    16-byte aligned and evenly spaced across the batch (a dense tensor or a
+    column block of a wider one); a dense copy otherwise."""
+    B, S, D = t.shape
+    if t.is_dense():
+        return t, D
+    st = t.stride
+    ld = st[1] if S > 1 else (st[0] if B > 1 else D)
+    if (st[2] == 1 and ld >= D and ld % 4 == 0 and t.offset % 4 == 0
+            and (B == 1 or st[0] == S * ld)):
+        return t, ld
+    return dense(t), D
+
+
 def attention(q, k, v, n_heads, mask=None, causal=False, scale=None):
     """Fused multi-head attention ``softmax(scale * Q K^T + mask) V``.
 
@@ -108,13 +123,20 @@ def attention(q, k, v, n_heads, mask=None, causal=False, scale=None):
     matmul -> scale -> add mask -> softmax -> matmul chain up to rounding."""
     import math
 
-    q = dense(q)
-    k = dense(k)
-    v = dense(v)
+    if len(q.shape) != 3 or len(k.shape) != 3 or len(v.shape) != 3:
+        raise ValueError(f"attention: q {q.shape}, k {k.shape}, v {v.shape} must be 3-D")
     B, Sq, D = q.shape
     Sk = k.shape[1]
     if tuple(k.shape) != (B, Sk, D) or tuple(v.shape) != (B, Sk, D):
         raise ValueError(f"attention: q {q.shape}, k {k.shape}, v {v.shape} do not match")
+    # Row-strided views (e.g. the q / k / v column blocks of one fused QKV
+    # projection) are read in place: the kernel takes a row stride.
+    q, q_ld = _attention_rows(q)
+    k, k_ld = _attention_rows(k)
+    v, v_ld = _attention_rows(v)
+    if k_ld != v_ld:
+        k, k_ld = dense(k), D
+        v, v_ld = dense(v), D
     hd = D // n_heads
     if scale is None:
         scale = 1.0 / math.sqrt(hd)
@@ -124,6 +146,6 @@ def attention(q, k, v, n_heads, mask=None, causal=False, scale=None):
             raise ValueError(f"attention: mask shape {mask.shape} != {(Sq, Sk)}")
         mptr, mld = mask.ptr, mask.stride[0]
     out = empty((B, Sq, D), "f32", q.requires_grad or k.requires_grad or v.requires_grad)
-    check(F.wxx_attention(out.buffer.ptr, q.ptr, k.ptr, v.ptr, B, n_heads, Sq, Sk, hd, D, D, D,
+    check(F.wxx_attention(out.buffer.ptr, q.ptr, k.ptr, v.ptr, B, n_heads, Sq, Sk, hd, q_ld, k_ld, D,
                           float(scale), mptr, mld, int(bool(causal))), "attention")
     return out

@@ -336,6 +336,26 @@ class AdaptiveAvgPool2d(Module):
         return autograd.adaptive_avgpooling2d(x).forward(x, self.output_size)
 
 
+def kmajor_weight(owner, name, linears):
+    """The weights of ``linears`` (each nn.Linear's (K, N_i)) transposed and
+    stacked into one (sum N_i, K) buffer owned by ``owner`` -- the K-major
+    operand the tensor-core GEMM reads fastest (``linear(...,
+    transpose_weight=True)``).  The copy is refreshed from the parameters on
+    every call, so it never goes stale; one transpose kernel per weight."""
+    K = linears[0].weight.shape[0]
+    ns = [lin.weight.shape[1] for lin in linears]
+    total = sum(ns)
+    buf = owner.__dict__.get(name)
+    if buf is None or tuple(buf.shape) != (total, K):
+        buf = Tensor((total, K), value=0.0)
+        object.__setattr__(owner, name, buf)
+    row = 0
+    for lin, n in zip(linears, ns):
+        functional.assign(buf.narrow(0, row, n), lin.weight.transpose(0, 1))
+        row += n
+    return buf
+
+
 class MultiHeadAttention(Module):
     """Multi-head self-attention (module.py:447-495).
 
@@ -371,7 +391,18 @@ class MultiHeadAttention(Module):
         fused_ok = context.MODE != 0 or self.drop.p == 0
         if fused_ok and functional.attention_supported(x, self.n_heads, mask):
             causal = bool(getattr(mask, "_wxx_causal", False))
-            o = functional.attention(self.q(x), self.k(x), self.v(x), self.n_heads,
+            if context.MODE != 0 and self.q.bias is None and self.k.bias is None \
+                    and self.v.bias is None:
+                # inference: q, k, v from one N = 3D product over a K-major
+                # copy of the three weights; attention reads the column
+                # blocks of its output in place
+                D = self.d_model
+                qkv = functional.linear(x, kmajor_weight(self, "_qkv_t", [self.q, self.k, self.v]),
+                                        transpose_weight=True)
+                q, k, v = qkv[..., 0:D], qkv[..., D:2 * D], qkv[..., 2 * D:3 * D]
+            else:
+                q, k, v = self.q(x), self.k(x), self.v(x)
+            o = functional.attention(q, k, v, self.n_heads,
                                      mask=None if causal else mask, causal=causal,
                                      scale=1.0 / math.sqrt(self.head_dim))
             if residual is not None:
