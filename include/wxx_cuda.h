@@ -114,6 +114,11 @@ int wxx_causal_conv1d(float* out, const float* x, int64_t x_off, int64_t sb, int
 /* functional/pointwise.py:357-404 decay_window (decay_window.wgsl) */
 int wxx_decay_window(float* out, const float* decay, int rows, int channels, int length,
                      int stage);
+/* nn/module.py MultiHeadAttention q/k/v weights (module.py:447-495, each (K, N)) transposed and
+ * stacked in one launch into the (n*N, K) K-major operand of the fused QKV projection:
+ * dst[b*cols + c, r] = srcs[b][r, c]; srcs is a host array of n <= 8 device pointers to dense
+ * (rows, cols) arrays. */
+int wxx_transpose_stack(float* dst, const float* const* srcs, int n, int rows, int cols);
 /* nn/hyena.py:127-130 ImplicitFilter.forward (Linear -> Sine(omega) -> Linear over the positional
  * encoding, transposed) and :236-239 (h * decay_window) for all `n` filters of an operator in one
  * launch, exact fp32: out (n, D, L) dense, filter i = (sin(omega * (pe @ w1[i] + b1[i])) @ w2[i]

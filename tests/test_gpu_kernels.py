@@ -983,3 +983,14 @@ def test_attention_reads_column_blocks_in_place(B, S, H, hd, rng):
     ref = F.attention(dq, dk, dv, H, causal=True).numpy()
     assert np.array_equal(got, ref)
     assert _w().backend.device_status() == 0
+
+
+@pytest.mark.parametrize("n,rows,cols", [(3, 1024, 1024), (2, 100, 70), (1, 33, 5), (8, 64, 96)])
+def test_transpose_stack(n, rows, cols, rng):
+    """n (rows, cols) weights transposed and stacked into one (n*cols, rows)
+    buffer by one launch (the fused QKV operand): bit-exact copies."""
+    F = _w().functional
+    ws = [rng.standard_normal((rows, cols)).astype(np.float32) for _ in range(n)]
+    out = up(np.zeros((n * cols, rows), np.float32))
+    assert F.transpose_stack(out, [up(w) for w in ws])
+    assert np.array_equal(out.numpy(), np.concatenate([w.T for w in ws], axis=0))

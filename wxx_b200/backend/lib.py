@@ -69,6 +69,7 @@ SIGNATURES = {
     "wxx_causal_conv1d": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_void_p,
                           c_int, c_int, c_int, c_int],
     "wxx_decay_window": [c_void_p, c_void_p, c_int, c_int, c_int, c_int],
+    "wxx_transpose_stack": [c_void_p, c_void_p, c_int, c_int, c_int],
     "wxx_hyena_filters": [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                           c_void_p, c_void_p, c_void_p, c_float, c_void_p],
     "wxx_complex_mul": [c_void_p, c_void_p, c_i64, P_i64, c_void_p, c_i64, P_i64, c_int, P_i64,

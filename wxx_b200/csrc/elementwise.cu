@@ -302,6 +302,31 @@ __global__ void transpose_kernel(float* __restrict__ dst, const float* __restric
   }
 }
 
+// Stacked transposes in one launch: dst[b * cols + c, r] = src_b[r, c] for up
+// to 8 dense (rows x cols) sources (blockIdx.z = b).  Builds the K-major
+// (n * N, K) operand of a fused projection from n nn.Linear (K, N) weights.
+struct StackSrc {
+  const float* p[8];
+};
+
+__global__ void transpose_stack_kernel(float* __restrict__ dst, StackSrc srcs, int rows,
+                                       int cols) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const float* s = srcs.p[b];
+  float* d = dst + (int64_t)b * rows * cols;
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    int r = r0 + k, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[k][threadIdx.x] = __ldg(s + (int64_t)r * cols + c);
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += 8) {
+    int c = c0 + k, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) d[(int64_t)c * rows + r] = tile[threadIdx.x][k];
+  }
+}
+
 // ------------------------------------------------------------ embed
 
 // out[t, :] = W[ids[t], :]; one warp-row of float4 per token.  Ids outside the
@@ -717,6 +742,27 @@ WXX_EXPORT int wxx_causal_conv1d(float* out, const float* x, int64_t x_off, int6
     causal_conv1d_kernel<<<wxx::grid_for(total, kThreads), kThreads, 0, s>>>(
         out, x, x_off, sb, sc, sl, w, bias, B, D, L, K);
   }
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+// dst (n * cols, rows) dense = the transposes of n dense (rows, cols) sources
+// stacked along dst's rows; srcs is a host array of n device pointers, n <= 8.
+WXX_EXPORT int wxx_transpose_stack(float* dst, const float* const* srcs, int n, int rows,
+                                   int cols) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(n >= 1 && n <= 8 && rows >= 0 && cols >= 0 && srcs != nullptr,
+              "wxx_transpose_stack: n %d not in 1..8 or bad sizes", n);
+  if ((int64_t)rows * cols == 0) return WXX_OK;
+  StackSrc ss;
+  memset(&ss, 0, sizeof(ss));
+  for (int i = 0; i < n; ++i) {
+    WXX_REQUIRE(srcs[i] != nullptr, "wxx_transpose_stack: source %d is NULL", i);
+    ss.p[i] = srcs[i];
+  }
+  dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)n);
+  WXX_REQUIRE(grid.y <= 65535, "wxx_transpose_stack: %d rows exceed the grid", rows);
+  transpose_stack_kernel<<<grid, dim3(32, 8), 0, wxx::stream()>>>(dst, ss, rows, cols);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }

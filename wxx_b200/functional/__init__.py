@@ -110,6 +110,7 @@ from .utils import (
     from_tensor,
     linear,
     linear_short_conv,
+    transpose_stack,
     linspace,
     masked_fill,
     matmul_add,

@@ -309,6 +309,27 @@ def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_we
 _E_UNSUPPORTED = -4
 
 
+def transpose_stack(out, weights):
+    """Writes the transposes of ``weights`` (n <= 8 dense-able (K, N) tensors
+    of one shape) stacked along rows into the dense (n * N, K) tensor ``out``
+    with one kernel launch.  False (nothing written) when the shapes do not
+    allow it."""
+    import ctypes
+
+    n = len(weights)
+    if n < 1 or n > 8 or not out.is_dense() or out.type != "f32":
+        return False
+    K, N = weights[0].shape
+    if any(tuple(w.shape) != (K, N) or w.type != "f32" for w in weights):
+        return False
+    if tuple(out.shape) != (n * N, K):
+        return False
+    ws = [dense(w) for w in weights]
+    srcs = (ctypes.c_void_p * n)(*[w.ptr for w in ws])
+    check(F.wxx_transpose_stack(out.ptr, srcs, n, K, N), "transpose_stack")
+    return True
+
+
 def linear_short_conv(x, weight, bias, conv_weight, conv_bias):
     """Hyena's projection + transpose + short causal conv (nn/hyena.py:227-234)
     as one tcgen05 GEMM whose epilogue applies the taps and writes channels

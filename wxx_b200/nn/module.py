@@ -341,7 +341,8 @@ def kmajor_weight(owner, name, linears):
     stacked into one (sum N_i, K) buffer owned by ``owner`` -- the K-major
     operand the tensor-core GEMM reads fastest (``linear(...,
     transpose_weight=True)``).  The copy is refreshed from the parameters on
-    every call, so it never goes stale; one transpose kernel per weight."""
+    every call, so it never goes stale; weights of one shape are transposed
+    by a single launch (``functional.transpose_stack``)."""
     K = linears[0].weight.shape[0]
     ns = [lin.weight.shape[1] for lin in linears]
     total = sum(ns)
@@ -349,6 +350,8 @@ def kmajor_weight(owner, name, linears):
     if buf is None or tuple(buf.shape) != (total, K):
         buf = Tensor((total, K), value=0.0)
         object.__setattr__(owner, name, buf)
+    if functional.transpose_stack(buf, [lin.weight for lin in linears]):
+        return buf
     row = 0
     for lin, n in zip(linears, ns):
         functional.assign(buf.narrow(0, row, n), lin.weight.transpose(0, 1))
