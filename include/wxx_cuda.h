@@ -226,6 +226,19 @@ int wxx_conv2d_nhwc(float* Y, const float* X, const float* W, const float* bias,
                     int dh, int dw, int mode, const float* rm, const float* rv,
                     const float* gamma, const float* beta, float eps, const float* residual,
                     int relu);
+/* wxx_conv2d_nhwc with Wp already in the convolution's K order, (Cout, KH*KW, Cin), as written
+ * by wxx_conv_weight_pack: no per-call reorder launch. */
+int wxx_conv2d_nhwc_packed(float* Y, const float* X, const float* Wp, const float* bias, int B,
+                           int Cin, int H, int Wd, int Cout, int KH, int KW, int sh, int sw,
+                           int ph, int pw, int dh, int dw, int mode, const float* rm,
+                           const float* rv, const float* gamma, const float* beta, float eps,
+                           const float* residual, int relu);
+/* nn/resnet.py forward (channels-last stages): the weights of up to 24 convolutions
+ * (nn/module.py Conv2d.W, (cout, cin, taps)) reordered to (cout, taps, cin) in one launch;
+ * dst, src, cout, cin, taps are host arrays of n entries (device pointers for dst / src);
+ * cin * taps <= 51200. */
+int wxx_conv_weight_pack(float* const* dst, const float* const* src, const int* cout,
+                         const int* cin, const int* taps, int n);
 
 /* nn/module.py:460-495 MultiHeadAttention core fused (QK^T * scale (+ mask), softmax, PV)
  * on tcgen05 TF32.  Q (B, Sq, H, hd) row stride q_ld, K/V (B, Sk, H, hd) row stride kv_ld,

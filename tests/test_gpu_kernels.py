@@ -994,3 +994,24 @@ def test_transpose_stack(n, rows, cols, rng):
     out = up(np.zeros((n * cols, rows), np.float32))
     assert F.transpose_stack(out, [up(w) for w in ws])
     assert np.array_equal(out.numpy(), np.concatenate([w.T for w in ws], axis=0))
+
+
+@pytest.mark.parametrize("shape", NHWC_SHAPES)
+def test_conv2d_nhwc_packed_weights(shape, rng):
+    """Weights reordered for all convolutions in one launch (conv_weight_pack,
+    ResNet's channels-last stages) give the same bits as each convolution
+    reordering its own; the packed tensor is (Cout, KH, KW, Cin)."""
+    F = _w().functional
+    B, C, H, W, O, k, s, p, d = shape
+    x = rng.standard_normal((B, H, W, C)).astype(np.float32)
+    w = rng.standard_normal((O, C, k, k)).astype(np.float32)
+    w2 = rng.standard_normal((O // 2 * 2, C, 1, 1)).astype(np.float32)
+    pk = up(np.zeros((O, k, k, C), np.float32))
+    pk2 = up(np.zeros((w2.shape[0], 1, 1, C), np.float32))
+    assert F.conv_weight_pack([up(w), up(w2)], [pk, pk2])
+    assert np.array_equal(pk.numpy(), w.transpose(0, 2, 3, 1))
+    assert np.array_equal(pk2.numpy(), w2.transpose(0, 2, 3, 1))
+    got = F.conv2d_nhwc(up(x), up(w), (s, s), (p, p), (d, d), relu=True, packed=pk).numpy()
+    ref = F.conv2d_nhwc(up(x), up(w), (s, s), (p, p), (d, d), relu=True).numpy()
+    assert np.array_equal(got, ref)
+    assert _w().backend.device_status() == 0

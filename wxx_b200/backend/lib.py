@@ -99,6 +99,9 @@ SIGNATURES = {
                      + [c_void_p] * 4 + [c_float, c_void_p, c_int],
     "wxx_conv2d_nhwc": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14
                        + [c_void_p] * 4 + [c_float, c_void_p, c_int],
+    "wxx_conv2d_nhwc_packed": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14
+                              + [c_void_p] * 4 + [c_float, c_void_p, c_int],
+    "wxx_conv_weight_pack": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int],
     "wxx_attention": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                       c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int],
     "wxx_maxpool2d": [c_void_p, c_void_p, c_void_p] + [c_int] * 10,

@@ -872,6 +872,33 @@ __global__ void __launch_bounds__(256) conv_weight_reorder_kernel(float* __restr
   }
 }
 
+// The same reorder for up to kPackMax filters in one launch (blockIdx.y =
+// filter): a network's convolutions pack their weights together instead of
+// each paying a small launch of its own.
+constexpr int kPackMax = 24;
+struct PackArgs {
+  float* dst[kPackMax];
+  const float* src[kPackMax];
+  int cout[kPackMax], cin[kPackMax], taps[kPackMax];
+};
+
+__global__ void __launch_bounds__(256) conv_weight_pack_kernel(PackArgs a) {
+  extern __shared__ float blk[];
+  const int f = blockIdx.y;
+  const int cin = a.cin[f], taps = a.taps[f], n = cin * taps;
+  for (int o = blockIdx.x; o < a.cout[f]; o += gridDim.x) {
+    const float* src = a.src[f] + (int64_t)o * n;
+    float* dst = a.dst[f] + (int64_t)o * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) blk[i] = src[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int t = i / cin, c = i - t * cin;
+      dst[i] = blk[c * taps + t];
+    }
+    __syncthreads();
+  }
+}
+
 // 128-pixel output tiles as one TMA box (W, H, images) of output positions;
 // false when the output geometry does not split that way.
 bool nhwc_box(int Ho, int Wo, int* bw, int* bh, int* bb) {
@@ -920,12 +947,12 @@ bool encode_nhwc_map(CUtensorMap* map, const float* base, int C, int W, int H, i
 // Cout % 4 == 0, 16-byte aligned X and Y, and an output geometry whose
 // 128-pixel tiles are boxes (Wo a multiple of 128, or Wo dividing 128 and Ho
 // a multiple or a divisor of 128 / Wo); else WXX_E_ARG.
-WXX_EXPORT int wxx_conv2d_nhwc(float* Y, const float* X, const float* Wt, const float* bias, int B,
-                               int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw,
-                               int ph, int pw, int dh, int dw, int mode, const float* rm,
-                               const float* rv, const float* gamma, const float* beta, float eps,
-                               const float* residual, int relu) {
-  WXX_REQUIRE_INIT();
+namespace {
+int conv2d_nhwc_impl(float* Y, const float* X, const float* Wt, bool packed, const float* bias,
+                     int B, int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw,
+                     int ph, int pw, int dh, int dw, int mode, const float* rm, const float* rv,
+                     const float* gamma, const float* beta, float eps, const float* residual,
+                     int relu) {
   WXX_REQUIRE(B >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0 && KH > 0 && KW > 0,
               "wxx_conv2d_nhwc: bad sizes");
   WXX_REQUIRE(sh > 0 && sw > 0 && dh > 0 && dw > 0 && ph >= 0 && pw >= 0,
@@ -961,9 +988,14 @@ WXX_EXPORT int wxx_conv2d_nhwc(float* Y, const float* X, const float* Wt, const 
   void* wr = nullptr;
   void* lo_x = nullptr;
   void* lo_w = nullptr;
-  int st = wxx_malloc(&wr, (uint64_t)Cout * K * sizeof(float));
-  if (st) return st;
-  {
+  int st = WXX_OK;
+  if (packed) {
+    wr = const_cast<float*>(Wt);   // already (Cout, tap, Cin); not freed below
+  } else {
+    st = wxx_malloc(&wr, (uint64_t)Cout * K * sizeof(float));
+    if (st) return st;
+  }
+  if (!packed) {
     const size_t smem = (size_t)K * sizeof(float);
     static size_t smem_set = 48 * 1024;
     if (smem > smem_set) {
@@ -1028,8 +1060,70 @@ WXX_EXPORT int wxx_conv2d_nhwc(float* Y, const float* X, const float* Wt, const 
                             : run_tc(bn, ma0, ma1, mb0, mb1, p);
   }
   // stream-ordered frees: valid for the kernels just enqueued
-  const int s1 = wxx_free(wr), s2 = wxx_free(lo_x), s3 = wxx_free(lo_w);
+  const int s1 = packed ? WXX_OK : wxx_free(wr), s2 = wxx_free(lo_x), s3 = wxx_free(lo_w);
   return st ? st : (s1 ? s1 : (s2 ? s2 : s3));
+}
+}  // namespace
+
+WXX_EXPORT int wxx_conv2d_nhwc(float* Y, const float* X, const float* Wt, const float* bias, int B,
+                               int Cin, int H, int W, int Cout, int KH, int KW, int sh, int sw,
+                               int ph, int pw, int dh, int dw, int mode, const float* rm,
+                               const float* rv, const float* gamma, const float* beta, float eps,
+                               const float* residual, int relu) {
+  WXX_REQUIRE_INIT();
+  return conv2d_nhwc_impl(Y, X, Wt, false, bias, B, Cin, H, W, Cout, KH, KW, sh, sw, ph, pw, dh,
+                          dw, mode, rm, rv, gamma, beta, eps, residual, relu);
+}
+
+// wxx_conv2d_nhwc with the weights already in the NHWC convolution's K order,
+// Wp (Cout, KH*KW, Cin) as written by wxx_conv_weight_pack: no reorder launch
+// and no scratch for it.
+WXX_EXPORT int wxx_conv2d_nhwc_packed(float* Y, const float* X, const float* Wp, const float* bias,
+                                      int B, int Cin, int H, int W, int Cout, int KH, int KW,
+                                      int sh, int sw, int ph, int pw, int dh, int dw, int mode,
+                                      const float* rm, const float* rv, const float* gamma,
+                                      const float* beta, float eps, const float* residual,
+                                      int relu) {
+  WXX_REQUIRE_INIT();
+  return conv2d_nhwc_impl(Y, X, Wp, true, bias, B, Cin, H, W, Cout, KH, KW, sh, sw, ph, pw, dh,
+                          dw, mode, rm, rv, gamma, beta, eps, residual, relu);
+}
+
+// Reorders n <= 24 convolution weights W_i (cout[i], cin[i], taps[i]) to
+// (cout[i], taps[i], cin[i]) in one launch; dst/src are host arrays of device
+// pointers; cin[i] * taps[i] <= 51200.
+WXX_EXPORT int wxx_conv_weight_pack(float* const* dst, const float* const* src, const int* cout,
+                                    const int* cin, const int* taps, int n) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(n >= 0 && n <= kPackMax && (n == 0 || (dst && src && cout && cin && taps)),
+              "wxx_conv_weight_pack: n %d not in 0..%d or NULL arrays", n, kPackMax);
+  if (n == 0) return WXX_OK;
+  PackArgs a;
+  memset(&a, 0, sizeof(a));
+  int max_n = 1, max_cout = 1;
+  for (int i = 0; i < n; ++i) {
+    WXX_REQUIRE(dst[i] && src[i] && cout[i] >= 0 && cin[i] > 0 && taps[i] > 0 &&
+                    (int64_t)cin[i] * taps[i] <= 51200,
+                "wxx_conv_weight_pack: filter %d has bad sizes", i);
+    a.dst[i] = dst[i];
+    a.src[i] = src[i];
+    a.cout[i] = cout[i];
+    a.cin[i] = cin[i];
+    a.taps[i] = taps[i];
+    if (cin[i] * taps[i] > max_n) max_n = cin[i] * taps[i];
+    if (cout[i] > max_cout) max_cout = cout[i];
+  }
+  const size_t smem = (size_t)max_n * sizeof(float);
+  static size_t smem_set = 48 * 1024;
+  if (smem > smem_set) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(conv_weight_pack_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    smem_set = smem;
+  }
+  dim3 grid((unsigned)(max_cout < 512 ? max_cout : 512), (unsigned)n);
+  conv_weight_pack_kernel<<<grid, 256, smem, wxx::stream()>>>(a);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
 }
 
 WXX_EXPORT int wxx_conv2d(float* Y, const float* X, const float* Wt, const float* bias, int B,

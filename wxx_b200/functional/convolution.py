@@ -93,14 +93,40 @@ def conv2d_nhwc_supported(cin, cout, ho, wo):
     return ho % rows == 0 if ho >= rows else rows % ho == 0
 
 
+def conv_weight_pack(weights, outs):
+    """Reorders each (Cout, Cin, KH, KW) weight in ``weights`` into the dense
+    (Cout, KH, KW, Cin) tensor at the same index of ``outs`` -- the K order
+    of the channels-last convolution -- in one launch (up to 24 weights).
+    False (nothing written) when the arguments do not fit."""
+    import ctypes
+
+    n = len(weights)
+    if n == 0 or n > 24 or len(outs) != n:
+        return False
+    ws = [dense(w) for w in weights]
+    for w, o in zip(ws, outs):
+        co, ci, kh, kw = w.shape
+        if tuple(o.shape) != (co, kh, kw, ci) or not o.is_dense() or ci * kh * kw > 51200:
+            return False
+    ints = ctypes.c_int * n
+    ptrs = ctypes.c_void_p * n
+    check(F.wxx_conv_weight_pack(ptrs(*[o.ptr for o in outs]), ptrs(*[w.ptr for w in ws]),
+                                 ints(*[w.shape[0] for w in ws]), ints(*[w.shape[1] for w in ws]),
+                                 ints(*[w.shape[2] * w.shape[3] for w in ws]), n),
+          "conv_weight_pack")
+    return True
+
+
 def conv2d_nhwc(tensor1, W, stride, padding, dilation, bias=None, *, bn=None, residual=None,
-                relu=False):
+                relu=False, packed=None):
     """``conv2d_bn`` on channels-last tensors: ``tensor1`` (B, H, W, Cin) NHWC,
     ``W`` (Cout, Cin, KH, KW) as in the reference, ``residual`` and the result
     (B, Ho, Wo, Cout) NHWC.  The implicit GEMM's A operand is fetched by TMA
     boxes (one filter tap x 32 channels x a 128-pixel tile per K-block), so
     the rows of im2col are never gathered by threads; see
-    ``conv2d_nhwc_supported`` for the shapes it takes."""
+    ``conv2d_nhwc_supported`` for the shapes it takes.  ``packed``: ``W``
+    already reordered to (Cout, KH, KW, Cin) by ``conv_weight_pack`` (the
+    convolution then skips its own reorder launch)."""
     x = dense(tensor1)
     w = dense(W)
     B, H, Wd, Cin = x.shape
@@ -128,9 +154,17 @@ def conv2d_nhwc(tensor1, W, stride, padding, dilation, bias=None, *, bn=None, re
     mode = matmul_mode_code()
     timer = active_timer()
     ev0 = timer.start() if timer is not None else None
-    check(F.wxx_conv2d_nhwc(out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr, B, Cin, H,
-                            Wd, Cout, KH, KW, sh, sw, ph, pw, dh, dw, 0 if mode == 0 else 1,
-                            *bn_args, None if r is None else r.ptr, int(bool(relu))), "conv2d")
+    if packed is not None:
+        pk = dense(packed)
+        if tuple(pk.shape) != (Cout, KH, KW, Cin):
+            raise ValueError(f"conv2d_nhwc: packed weight {tuple(pk.shape)} is not "
+                             f"{(Cout, KH, KW, Cin)}")
+        fn, wptr = F.wxx_conv2d_nhwc_packed, pk.ptr
+    else:
+        fn, wptr = F.wxx_conv2d_nhwc, w.ptr
+    check(fn(out.buffer.ptr, x.ptr, wptr, None if b is None else b.ptr, B, Cin, H,
+             Wd, Cout, KH, KW, sh, sw, ph, pw, dh, dw, 0 if mode == 0 else 1,
+             *bn_args, None if r is None else r.ptr, int(bool(relu))), "conv2d")
     if timer is not None:
         timer.stop(ev0, 2.0 * B * Ho * Wo * Cout * Cin * KH * KW, f"conv{B}x{H}x{Wd}x{Cin}->{Cout}")
     return out

@@ -2,6 +2,7 @@
 
 from .. import functional
 from ..backend import context
+from ..Tensor import Tensor
 from .module import AdaptiveAvgPool2d, BatchNorm, Conv2D, Linear, MaxPool2d, Module, Sequential
 
 
@@ -12,11 +13,14 @@ def _conv_bn(x, conv, bn, residual=None, relu=False):
                                 residual=residual, relu=relu)
 
 
-def _conv_nhwc(h, conv, bn, residual=None, relu=False):
-    """The same on channels-last activations (functional.conv2d_nhwc)."""
+def _conv_nhwc(h, conv, bn, residual=None, relu=False, packed=None):
+    """The same on channels-last activations (functional.conv2d_nhwc);
+    ``packed`` maps a convolution to its weight already in the channels-last
+    K order (functional.conv_weight_pack), when the caller packed them."""
+    pw = packed.get(id(conv)) if packed else None
     return functional.conv2d_nhwc(h, conv.W, conv.stride, conv.padding, conv.dilation, conv.bias,
                                   bn=(bn.running_mean, bn.running_std, bn.weight, bn.bias, 1e-5),
-                                  residual=residual, relu=relu)
+                                  residual=residual, relu=relu, packed=pw)
 
 
 def _conv_out_hw(conv, h, w):
@@ -69,15 +73,22 @@ class ResBlock(Module):
             return None
         return (B, ho, wo, out_c)
 
-    def forward_nhwc(self, h):
+    def nhwc_convs(self):
+        """The convolutions forward_nhwc runs, in order."""
+        convs = [self.conv1, self.conv2]
+        if self.sh:
+            convs.insert(0, list(self.shortcut._modules.values())[0])
+        return convs
+
+    def forward_nhwc(self, h, packed=None):
         """Inference on channels-last activations: three (or two) convolutions,
         each with its batchnorm, the shortcut add and the ReLUs in its epilogue."""
         sc = h
         if self.sh:
             conv, bn = self.shortcut._modules.values()
-            sc = _conv_nhwc(h, conv, bn)
-        out = _conv_nhwc(h, self.conv1, self.bn1, relu=True)
-        return _conv_nhwc(out, self.conv2, self.bn2, residual=sc, relu=True)
+            sc = _conv_nhwc(h, conv, bn, packed=packed)
+        out = _conv_nhwc(h, self.conv1, self.bn1, relu=True, packed=packed)
+        return _conv_nhwc(out, self.conv2, self.bn2, residual=sc, relu=True, packed=packed)
 
 
 class ResNet18(Module):
@@ -101,6 +112,21 @@ class ResNet18(Module):
             layers.append(ResBlock(self.in_channels, out_channels, stride=1))
         return Sequential(*layers)
 
+    def _pack_nhwc_weights(self, blocks):
+        """Every channels-last convolution's weight reordered to its K order
+        by one launch per call, into buffers owned by this module (refreshed
+        each call, so they follow the parameters); None if they do not fit
+        one launch."""
+        convs = [c for blk in blocks for c in blk.nhwc_convs()]
+        bufs = self.__dict__.get("_nhwc_packed")
+        shapes = [(c.W.shape[0], c.W.shape[2], c.W.shape[3], c.W.shape[1]) for c in convs]
+        if bufs is None or [tuple(b.shape) for b in bufs] != shapes:
+            bufs = [Tensor(sh, value=0.0) for sh in shapes]
+            object.__setattr__(self, "_nhwc_packed", bufs)
+        if not functional.conv_weight_pack([c.W for c in convs], bufs):
+            return None
+        return {id(c): b for c, b in zip(convs, bufs)}
+
     def forward(self, x):
         if context.MODE != 0:
             out = self.maxpool(_conv_bn(x, self.conv1, self.bn1, relu=True))
@@ -113,8 +139,9 @@ class ResNet18(Module):
                 # channels-last from the first block to the pooling: the
                 # convolutions' A operands then load as TMA boxes
                 h = out.permute(0, 2, 3, 1).contiguous()
+                packed = self._pack_nhwc_weights(blocks)
                 for blk in blocks:
-                    h = blk.forward_nhwc(h)
+                    h = blk.forward_nhwc(h, packed)
                 B, H, W, C = h.shape
                 pooled = (h.reshape((B, C)) if H * W == 1
                           else functional.mean(h.reshape((B, H * W, C)), axis=1))
