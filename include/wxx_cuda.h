@@ -279,9 +279,10 @@ int wxx_fftconv_gated(float* y, const float* x, int64_t x_off, int64_t sb, int64
                       int64_t n, int out_len, const float* gate, int64_t g_off, int64_t g_sb,
                       int64_t g_sd, int64_t g_sl);
 /* No counterpart in the reference.  wxx_fftconv without any allocation: the
- * filter spectrum lives in a fixed 16 MiB device array inside the library.
- * Limits: n <= 32768 and D*(n/2+1) <= 2^21 complex values, else WXX_E_ARG and
- * nothing is launched.  The scratch needs no zeroing (each call writes it
+ * filter spectrum lives in a fixed device array inside the library (32 MiB +
+ * 4 KiB, rows n/2+2 complex values apart).  Limits: n <= 32768,
+ * D*(n/2+2) <= 4194816 complex values (256 rows at n = 32768) and
+ * 0 <= out_len <= n, else WXX_E_ARG and nothing is launched.  The scratch needs no zeroing (each call writes it
  * before reading it).  One array per device: calls that overlap on the device
  * (other streams or threads) race on it.  The first call on a device looks up
  * the array's address (cudaGetSymbolAddress, may load device code); make it

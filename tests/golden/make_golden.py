@@ -18,7 +18,7 @@ helpers and formulas.  This script
       LayerNorm / RMSNorm          tests/test_normalization.py:13-31
       Hyena positional encoding    tests/test_hyena.py:246-266
 and writes the inputs and expected outputs to tests/golden/reference_golden.npz.
-Run it where the reference is mounted:  python tests/golden/make_golden.py [REF_ROOT]
+Run it where the reference is mounted:  python tests/golden/make_golden.py REF_ROOT
 """
 
 import ast
@@ -136,4 +136,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the wxx reference checkout>")
+    main(sys.argv[1])

@@ -29,8 +29,13 @@ def up(a, dtype=np.float32):
 
 
 def rel(got, ref):
-    got = np.asarray(got, np.float64)
-    ref = np.asarray(ref, np.float64)
+    """max |got - ref| / max |ref|; complex arrays are compared as complex
+    numbers (modulus of the difference), so imaginary parts count."""
+    cplx = np.iscomplexobj(got) or np.iscomplexobj(ref)
+    dt = np.complex128 if cplx else np.float64
+    got = np.asarray(got, dt)
+    ref = np.asarray(ref, dt)
+    assert got.shape == ref.shape, (got.shape, ref.shape)
     scale = max(np.abs(ref).max(), 1e-30) if ref.size else 1.0
     return float(np.abs(got - ref).max() / scale) if ref.size else 0.0
 
@@ -537,12 +542,47 @@ def test_irfft_truncated_and_padded_spectrum(rng):
         assert rel(got, K.irfft(X, n)) < 2e-5
 
 
-def test_complex_mul_broadcast(rng):
+def _crand(rng, shape):
+    return (rng.standard_normal(shape) + 1j * rng.standard_normal(shape)).astype(np.complex64)
+
+
+@pytest.mark.parametrize("conj_a,conj_b", [(False, False), (True, False), (False, True),
+                                           (True, True)])
+def test_complex_mul_broadcast(conj_a, conj_b, rng):
+    """complex_mul.wgsl:57-61 with every conj flag: the products are compared
+    as complex numbers, so a wrong sign on an imaginary part fails."""
     F = _w().functional
-    a = (rng.standard_normal((3, 4, 9)) + 1j * rng.standard_normal((3, 4, 9))).astype(np.complex64)
-    b = (rng.standard_normal((4, 9)) + 1j * rng.standard_normal((4, 9))).astype(np.complex64)
-    got = F.complex_mul(F.from_numpy_complex(a), F.from_numpy_complex(b), conj_b=True).numpy()
-    assert rel(got, K.complex_mul(a, b, conj_b=True)) < 1e-6
+    a = _crand(rng, (3, 4, 9))
+    b = _crand(rng, (4, 9))
+    got = F.complex_mul(F.from_numpy_complex(a), F.from_numpy_complex(b),
+                        conj_a=conj_a, conj_b=conj_b).numpy()
+    assert got.dtype == np.complex64
+    ref = K.complex_mul(a, b, conj_a=conj_a, conj_b=conj_b)
+    assert rel(got, ref) < 1e-6
+    assert rel(got.imag, ref.imag) < 1e-6
+
+
+def test_complex_mul_strided_views(rng):
+    """A transposed / sliced c64 view on either side (the reference's strided
+    complex operands) against the same product of dense copies."""
+    F = _w().functional
+    a = _crand(rng, (5, 6, 7))
+    b = _crand(rng, (7, 6))
+    ta = F.from_numpy_complex(a)[:, 1:5]                      # (5, 4, 7) strided rows
+    tb = F.from_numpy_complex(b).permute(1, 0)[1:5]           # (4, 7) transposed view
+    got = F.complex_mul(ta, tb, conj_a=True).numpy()
+    ref = K.complex_mul(a[:, 1:5], b.T[1:5], conj_a=True)
+    assert rel(got, ref) < 1e-6
+
+
+def test_complex_conj_and_add_inplace(rng):
+    F = _w().functional
+    a = _crand(rng, (3, 1000))
+    b = _crand(rng, (3, 1000))
+    assert np.array_equal(F.complex_conj(F.from_numpy_complex(a)).numpy(), np.conj(a))
+    acc = F.from_numpy_complex(a)
+    F.complex_add_inplace(acc, F.from_numpy_complex(b))
+    assert np.array_equal(acc.numpy(), a + b)
 
 
 @pytest.mark.parametrize("B,D,L", [(2, 3, 64), (2, 3, 200), (3, 2, 300), (3, 4, 1000),

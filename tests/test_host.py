@@ -123,3 +123,55 @@ def test_oracle_not_imported_by_product():
 
 def test_numpy_available():
     assert np.__version__
+
+
+def test_validation_contracts():
+    from wxx_b200 import validation as v
+
+    assert v.normalize_shape(3) == (3,)
+    assert v.normalize_shape((2, -1), allow_infer=True) == (2, -1)
+    with pytest.raises(ValueError):
+        v.normalize_shape((2, -1))
+    with pytest.raises(ValueError):
+        v.normalize_shape((-1, -1), allow_infer=True)
+    with pytest.raises(TypeError):
+        v.normalize_shape((2, 1.5))
+    with pytest.raises(TypeError):
+        v.normalize_shape((2, True))
+    with pytest.raises(ValueError):
+        v.infer_shape((4, -1), 6)
+    with pytest.raises(ValueError):
+        v.infer_shape((0, -1), 0)
+    assert v.normalize_dim(-1, 3) == 2
+    with pytest.raises(IndexError):
+        v.normalize_dim(0, 0)
+    with pytest.raises(TypeError):
+        v.normalize_dim("1", 2)
+    assert v.normalize_dims((-1, 0), 3) == (2, 0)
+    with pytest.raises(ValueError):
+        v.normalize_dims((1, -2), 3, allow_duplicates=False)
+    assert v.check_rank((1, 2), min_rank=2, max_rank=None) == 2
+    with pytest.raises(ValueError):
+        v.check_rank((1,), min_rank=2, max_rank=2)
+    assert v.check_same_shape((2, 3), [2, 3]) == (2, 3)
+    with pytest.raises(ValueError):
+        v.check_same_shape((2, 3), (3, 2))
+    assert v.check_broadcastable((3, 1), (2, 3, 4)) == (2, 3, 4)
+    with pytest.raises(ValueError):
+        v.check_broadcastable((2, 4), (3, 4))
+    assert v.numel(()) == 1 and v.numel((2, 0, 3)) == 0
+
+
+def test_npz_state_dict_round_trip(tmp_path):
+    from wxx_b200 import serialization as s
+
+    state = {"blocks.0.w": np.arange(6, dtype=np.float32).reshape(2, 3),
+             "ids": np.array([1, 2], np.uint32)}
+    path = s.save(state, tmp_path / "ckpt")
+    assert path.endswith(".npz")
+    back = s.load(tmp_path / "ckpt")
+    assert set(back) == set(state)
+    for k in state:
+        assert back[k].dtype == state[k].dtype and np.array_equal(back[k], state[k])
+    one = s.load(s.save(np.ones(3, np.float32), str(tmp_path / "one.npz")))
+    assert list(one) == ["tensor"]

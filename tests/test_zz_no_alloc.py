@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 
 WXX_E_ARG = -1
 MAX_N = 32768
-MAX_SPECTRUM = 1 << 21
+MAX_SPECTRUM = 256 * (MAX_N // 2 + 2)     # complex values, rows n/2 + 2 apart
 
 
 def _setup():
@@ -40,7 +40,9 @@ def _mem_stats(lib):
 
 @pytest.mark.parametrize("B,D,L,Lh,n,out_len", [(2, 64, 1024, 1024, 2048, 1024),
                                                 (3, 5, 300, 200, 1024, 300),
-                                                (1, 127, 16384, 16384, 32768, 16384)])
+                                                (2, 8, 100, 100, 256, 100),
+                                                (1, 256, 8192, 8192, 16384, 8192),
+                                                (1, 256, 16384, 16384, 32768, 16384)])
 def test_static_matches_allocating_entry_point(B, D, L, Lh, n, out_len, rng):
     wxx, lib = _setup()
     F = wxx.functional
@@ -78,9 +80,12 @@ def test_static_rejects_sizes_beyond_its_limits(rng):
     assert "exceeds" in lib.last_error()
     # D * (n/2 + 1) above the fixed scratch (pointers are never read: the
     # size check comes first and nothing is launched)
-    D = MAX_SPECTRUM // (MAX_N // 2 + 1) + 1
+    D = MAX_SPECTRUM // (MAX_N // 2 + 2) + 1
     assert _call(lib, lib.F.wxx_fftconv_static, y, x, h, 1, D, 8, 8, MAX_N, 8) == WXX_E_ARG
     assert "static scratch" in lib.last_error()
+    # out_len beyond n: refused before the filter transform is launched
+    assert _call(lib, lib.F.wxx_fftconv_static, y, x, h, 1, 2, 8, 8, 16, 17) == WXX_E_ARG
+    assert "out_len" in lib.last_error()
     # not a power of two
     assert _call(lib, lib.F.wxx_fftconv_static, y, x, h, 1, 2, 8, 8, 24, 8) == WXX_E_ARG
     lib.check(lib.F.wxx_launch_count(count), "launch count")

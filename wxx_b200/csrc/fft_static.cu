@@ -17,12 +17,19 @@
 //
 // Limits (checked on the host before anything is enqueued; a call beyond them
 // returns WXX_E_ARG with a message and launches nothing):
-//   * D * (n/2 + 1) <= kStaticSpecComplex complex values (16 MiB of scratch);
+//   * D * (n/2 + 2) <= kStaticSpecComplex = 256 * 16386 complex values
+//     (32 MiB + 4 KiB of scratch): 256 filter rows at n = 32768, the largest
+//     filter of the configured workloads;
 //   * n <= 32768, the largest size whose rows are transformed in shared
-//     memory (larger sizes need ping-pong buffers that would be allocated).
+//     memory (larger sizes need ping-pong buffers that would be allocated);
+//   * 0 <= out_len <= n.
+//
+// The spectrum rows are stored n/2 + 2 complex values apart (a multiple of 16
+// bytes), the same layout wxx_fftconv allocates, so the persistent staged
+// kernel that bulk-copies each filter row into shared memory runs here too.
 //
 // Scratch contents: nothing has to start at zero.  Every call first writes the
-// whole D x (n/2+1) prefix of the array (rfft of the zero-padded filter) and
+// whole D x (n/2+2) prefix of the array (rfft of the zero-padded filter) and
 // only then reads it, on the same stream.
 //
 // Concurrency: there is ONE scratch array per device.  Two calls that can
@@ -50,11 +57,12 @@ extern "C" int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int
 
 namespace {
 
-constexpr int64_t kStaticSpecComplex = int64_t(1) << 21;   // 2 Mi complex values
-constexpr int64_t kStaticSpecBytes = kStaticSpecComplex * 8;  // 16 MiB
-constexpr int64_t kStaticMaxN = 32768;                     // shared-memory FFT rows only
+constexpr int64_t kStaticMaxN = 32768;                      // shared-memory FFT rows only
+constexpr int64_t kStaticSpecComplex = 256 * (kStaticMaxN / 2 + 2);  // 4 194 816 values
+constexpr int64_t kStaticSpecBytes = kStaticSpecComplex * 8;
 constexpr int kMaxDevices = 64;
-static_assert(kStaticSpecBytes == (int64_t(16) << 20), "scratch size is documented as 16 MiB");
+static_assert(kStaticSpecBytes == (int64_t(32) << 20) + 4096,
+              "scratch size is documented as 32 MiB + 4 KiB");
 
 static __device__ __align__(256) float2 g_static_spectrum[kStaticSpecComplex];
 
@@ -102,15 +110,17 @@ WXX_EXPORT int wxx_fftconv_static(float* y, const float* x, int64_t x_off, int64
               "wxx_fftconv_static: n=%lld exceeds the allocation-free limit %lld",
               (long long)n, (long long)kStaticMaxN);
   WXX_REQUIRE(D >= 0 && B >= 0 && L >= 0 && Lh >= 0, "wxx_fftconv_static: negative size");
-  int64_t bins = n / 2 + 1;
-  WXX_REQUIRE((int64_t)D * bins <= kStaticSpecComplex,
-              "wxx_fftconv_static: D*(n/2+1)=%lld complex values exceed the static scratch "
+  WXX_REQUIRE(out_len >= 0 && out_len <= n, "wxx_fftconv_static: out_len=%d must be in [0, n]",
+              out_len);
+  const int64_t ld = n / 2 + 2;  // 16-byte multiple: the staged kernel's bulk copies apply
+  WXX_REQUIRE((int64_t)D * ld <= kStaticSpecComplex,
+              "wxx_fftconv_static: D*(n/2+2)=%lld complex values exceed the static scratch "
               "of %lld",
-              (long long)((int64_t)D * bins), (long long)kStaticSpecComplex);
+              (long long)((int64_t)D * ld), (long long)kStaticSpecComplex);
   void* Hs = nullptr;
   int st = static_spectrum(&Hs);
   if (st) return st;
-  st = wxx_rfft(Hs, bins, h, h_ld, D, Lh, n);
+  st = wxx_rfft(Hs, ld, h, h_ld, D, Lh, n);
   if (st) return st;
-  return wxx_fftconv_spectrum(y, x, x_off, sb, sd, sl, Hs, bins, B, D, L, n, out_len);
+  return wxx_fftconv_spectrum(y, x, x_off, sb, sd, sl, Hs, ld, B, D, L, n, out_len);
 }

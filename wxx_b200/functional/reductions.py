@@ -1,14 +1,8 @@
 """Reductions (reference: src/wxx/functional/reductions.py)."""
 
-import ctypes
-
-from .. import validation
-from ..Tensor import Tensor
 from ..backend.dispatch import _get_reduce_dims, keepdims_shape
 from ._common import F, check, dense, empty
 from .pointwise import _training_only
-
-pythonmin = min
 
 
 def _reduce(tensor1, axis, keepdims, mode):
@@ -77,4 +71,3 @@ def std(tensor1, axis=None, keepdims=False, *, keepdim=None):
 
 
 maxmin_backward = _training_only("maxmin_backward")
-_unused = (ctypes, Tensor, validation, pythonmin)
