@@ -243,6 +243,24 @@ SWEEPS["attention"] = Sweep("attention", [(8, 1024, 1024)] * 3,
                             lambda F, q, k, v: F.attention(q, k, v, 16, causal=True),
                             4.0 * 64 * 8 * 16 * (1024 * 1025 // 2), "TFLOP/s", "tensor",
                             "attention_kernel<64> (tcgen05 kind::tf32, TMEM S/O)", flush_l2=True)
+def _gpt2_scaled_gemms(F, x1, x4, wqkv, wo, w1, w2, emb):
+    """The GEMM launches of one GPT2-scaled layer plus the LM head, at the
+    default workload's per-GPU shapes (8 x 1024 tokens, d 1024): fused QKV
+    (K-major stacked weight), out projection + residual, FC1 + GELU, FC2 +
+    residual, tied LM head (N = 50304)."""
+    F.linear(x1, wqkv, transpose_weight=True)
+    F.linear(x1, wo, residual=x1)
+    F.linear(x1, w1, activation="gelu")
+    F.linear(x4, w2, residual=x1)
+    return F.matmul_add(x1, emb, None, transpose_B=True)
+
+
+_T, _D, _V = 8192, 1024, 50304
+SWEEPS["gemm_gpt2_scaled"] = Sweep(
+    "gemm_gpt2_scaled", [(_T, _D), (_T, 4 * _D), (3 * _D, _D), (_D, _D), (_D, 4 * _D),
+                         (4 * _D, _D), (_V, _D)], _gpt2_scaled_gemms,
+    2.0 * _T * _D * (3 * _D + _D + 4 * _D + 4 * _D + _V), "TFLOP/s", "tensor",
+    "tc_gemm_pair_kernel<256> (tcgen05 kind::tf32, cta_group::2)", flush_l2=False)
 for _ax in (0, 1):
     SWEEPS[f"sum_axis{_ax}"] = Sweep(
         f"sum_axis{_ax}", [(4096, 4096)], (lambda ax: lambda F, x: F.sum(x, ax))(_ax),
@@ -255,6 +273,32 @@ for _ax in (0, 1):
 
 
 # ------------------------------------------------------------------ helpers
+
+def load_traffic(name):
+    """Measured DRAM bytes per launch of a workload's dominant kernel, from the
+    ncu capture summarised in profiles/ (None when no capture covers it)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            rec = json.load(f).get(name)
+    except (OSError, ValueError):
+        return None
+    if not rec:
+        return None
+    return {"bytes_per_launch": rec["traffic_bytes_per_launch"],
+            "algorithmic_bytes_per_launch": rec["algorithmic_bytes_per_launch"],
+            "kernel": rec["kernel"], "source": rec["source"],
+            "metric": "dram__bytes_read.sum + dram__bytes_write.sum (one ncu capture)"}
+
+
+def _traffic_keys(name):
+    """roofline keys: ``traffic`` (DRAM bytes per launch, or None) and its
+    provenance."""
+    t = load_traffic(name)
+    if t is None:
+        return {"traffic": None}
+    return {"traffic": t["bytes_per_launch"], "traffic_unit": "bytes per launch",
+            "traffic_detail": t}
+
 
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -368,6 +412,15 @@ def _sweep_cpu(sw, arrays):
     if sw.name == "fftconv_hyena":
         return lambda: np.fft.irfft(np.fft.rfft(arrays[0], 16384) * np.fft.rfft(arrays[1], 16384),
                                     16384)[..., :8192]
+    if sw.name == "gemm_gpt2_scaled":
+        def gemms():
+            x1, x4, wqkv, wo, w1, w2, emb = arrays
+            np.matmul(x1, wqkv.T)
+            np.matmul(x1, wo) + x1
+            np.matmul(x1, w1)
+            np.matmul(x4, w2) + x1
+            return np.matmul(x1, emb.T)
+        return gemms
     if sw.name == "attention":
         def attn():
             B, S, D = arrays[0].shape
@@ -399,6 +452,9 @@ def _sweep_cpu_sample(sw, rng):
     if sw.name == "fftconv_hyena":
         return [rng.standard_normal((1, 256, 8192), dtype=np.float32),
                 rng.standard_normal((256, 8192), dtype=np.float32)], 1 / 16
+    if sw.name == "gemm_gpt2_scaled":
+        shapes = [(256,) + sw.shapes[0][1:], (256,) + sw.shapes[1][1:]] + list(sw.shapes[2:])
+        return [rng.standard_normal(s, dtype=np.float32) for s in shapes], 256 / sw.shapes[0][0]
     if sw.name == "matmul_8192":
         return [rng.standard_normal((1024, 8192), dtype=np.float32),
                 rng.standard_normal((8192, 8192), dtype=np.float32)], 1 / 8
@@ -501,7 +557,8 @@ def run_sweep(args, rank, world, local):
                    if sw.flush_l2 else "inputs larger than L2", "parallelism": "replicas"},
         "roofline": {"kernel": sw.kernel, "bound": sw.bound, "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s" if sw.bound == "tensor" else "GB/s",
-                     "frac": achieved / peak, "traffic": None, "peak_basis": basis},
+                     "frac": achieved / peak, "peak_basis": basis,
+                     **_traffic_keys(sw.name)},
         "clocks": clocks, "gpu_launches": int(launches),
         "e2e": {"value": e2e_value, "unit": sw.unit,
                 "h2d_bytes_per_step": int(sum(a.nbytes for a in host)),
@@ -761,7 +818,7 @@ def run_ours(args, rank, world, local):
     roofline = {
         "kernel": "tcgen05 kind::tf32 GEMM / implicit-GEMM conv (TMA-fed, TMEM accumulators)",
         "bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-        "frac": achieved / tf32_peak, "traffic": None,
+        "frac": achieved / tf32_peak, **_traffic_keys(wl.name),
         "peak_basis": f"{peak_kind} {'sustained ' if sustained else ''}bf16 dense TFLOP/s / 2 "
                       "(B200 TF32 rate is half of BF16; kernel timed inside a long step)",
         "gemm_share_of_step": ks["ms"] / ms if ms > 0 else None,
