@@ -117,8 +117,9 @@ int wxx_decay_window(float* out, const float* decay, int rows, int channels, int
 /* nn/module.py MultiHeadAttention q/k/v weights (module.py:447-495, each (K, N)) transposed and
  * stacked in one launch into the (n*N, K) K-major operand of the fused QKV projection:
  * dst[b*cols + c, r] = srcs[b][r, c]; srcs is a host array of n <= 8 device pointers to dense
- * (rows, cols) arrays. */
-int wxx_transpose_stack(float* dst, const float* const* srcs, int n, int rows, int cols);
+ * (rows, cols) arrays.  round_tf32 = 1 stores the values rounded to the nearest TF32 value. */
+int wxx_transpose_stack(float* dst, const float* const* srcs, int n, int rows, int cols,
+                        int round_tf32);
 /* nn/hyena.py:127-130 ImplicitFilter.forward (Linear -> Sine(omega) -> Linear over the positional
  * encoding, transposed) and :236-239 (h * decay_window) for all `n` filters of an operator in one
  * launch, exact fp32: out (n, D, L) dense, filter i = (sin(omega * (pe @ w1[i] + b1[i])) @ w2[i]
@@ -152,12 +153,15 @@ int wxx_softmax(float* y, const float* x, int64_t outer, int64_t n, int64_t inne
 /* nn/module.py:484-488 (score + mask, then softmax) fused: row r uses mask row r % mask_rows. */
 int wxx_softmax_masked(float* y, const float* x, int64_t rows, int64_t n, const float* mask,
                        int64_t mask_ld, int64_t mask_rows);
-/* functional/normalization.py:82-145 meanvarnorm (meanvarnorm.wgsl), eps 1e-5 */
+/* functional/normalization.py:82-145 meanvarnorm (meanvarnorm.wgsl), eps 1e-5.
+ * out_tf32 = 1 stores y rounded to the nearest TF32 value (for a y that only feeds TF32
+ * products, e.g. the LayerNorm before a projection); 0 stores the fp32 result. */
 int wxx_layernorm(float* y, float* mean, float* inv_std, const float* x, const float* gamma,
-                  const float* beta, int64_t outer, int64_t n, int64_t inner, float eps);
-/* functional/normalization.py:24-79 rmsnorm (rmsnorm.wgsl), eps 1e-6 */
+                  const float* beta, int64_t outer, int64_t n, int64_t inner, float eps,
+                  int out_tf32);
+/* functional/normalization.py:24-79 rmsnorm (rmsnorm.wgsl), eps 1e-6; out_tf32 as above */
 int wxx_rmsnorm(float* y, float* inv_rms, const float* x, const float* gamma, int64_t outer,
-                int64_t n, int64_t inner, float eps);
+                int64_t n, int64_t inner, float eps, int out_tf32);
 /* functional/normalization.py:148-206 batchnorm (batchnorm.wgsl) */
 int wxx_batchnorm(float* y, float* saved_mean, float* saved_inv, const float* x,
                   const float* gamma, const float* beta, float* running_mean, float* running_var,
@@ -169,7 +173,8 @@ int wxx_batchnorm(float* y, float* saved_mean, float* saved_inv, const float* x,
  * trans_a: element (m, k) at A[b*a_bs + k*lda + m]; else A[b*a_bs + m*lda + k].
  * trans_b: element (k, n) at B[b*b_bs + n*ldb + k]; else B[b*b_bs + k*ldb + n].
  * a_bs/b_bs = 0 broadcasts over the batch.  bias_mode 0 none, 1 (N,), 2 (M,N), 3 (batch,M,N).
- * mode 0 TF32 tcgen05, 1 3xTF32 tcgen05, 2 fp32 SIMT.  C = alpha * op(A) op(B) + bias. */
+ * mode 0 TF32 tcgen05, 1 3xTF32 tcgen05, 2 fp32 SIMT, 3 TF32 tcgen05 with C rounded to the
+ * nearest TF32 value.  C = alpha * op(A) op(B) + bias. */
 int wxx_matmul(float* C, const float* A, const float* B, const float* bias, int64_t batch,
                int64_t M, int64_t N, int64_t K, int64_t a_bs, int64_t b_bs, int64_t lda,
                int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha, int mode);
@@ -178,7 +183,8 @@ int wxx_matmul(float* C, const float* A, const float* B, const float* bias, int6
  * the GEMM epilogue: C = act(alpha * A @ op(B) + bias) + residual.
  * A (M, K) row stride lda; B (K, N) row stride ldb, or (N, K) with trans_b = 1;
  * bias (N) or NULL; residual (M, N dense) or NULL; act 0 none, 1 GELU (tanh).
- * mode 0 TF32, 1 3xTF32.  C 16-byte aligned, N a multiple of 4. */
+ * mode 0 TF32, 1 3xTF32, 3 TF32 with C rounded to the nearest TF32 value (for a C read only
+ * by TF32 products).  C 16-byte aligned, N a multiple of 4. */
 int wxx_linear(float* C, const float* A, const float* B, const float* bias,
                const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
                int64_t ldb, int trans_b, int act, float alpha, int mode);
@@ -242,10 +248,11 @@ int wxx_conv_weight_pack(float* const* dst, const float* const* src, const int* 
 
 /* nn/module.py:460-495 MultiHeadAttention core fused (QK^T * scale (+ mask), softmax, PV)
  * on tcgen05 TF32.  Q (B, Sq, H, hd) row stride q_ld, K/V (B, Sk, H, hd) row stride kv_ld,
- * O (B, Sq, H, hd) row stride o_ld; hd 32 or 64; causal masks keys after the query. */
+ * O (B, Sq, H, hd) row stride o_ld; hd 32 or 64; causal masks keys after the query.
+ * out_tf32 = 1 stores O rounded to the nearest TF32 value (an O read only by TF32 products). */
 int wxx_attention(float* O, const float* Q, const float* K, const float* V, int B, int H, int Sq,
                   int Sk, int hd, int64_t q_ld, int64_t kv_ld, int64_t o_ld, float scale,
-                  const float* mask, int64_t mask_ld, int causal);
+                  const float* mask, int64_t mask_ld, int causal, int out_tf32);
 
 /* ---------------------------------------------------------------- pooling */
 
@@ -297,6 +304,12 @@ int wxx_fftconv_static(float* y, const float* x, int64_t x_off, int64_t sb, int6
 int wxx_nccl_unique_id(uint8_t* out128);
 int wxx_nccl_init(const uint8_t* id128, int nranks, int rank);
 int wxx_nccl_allgather(void* recv, const void* send, uint64_t nbytes);
+/* The all-gather on a separate communication stream, ordered after the work already on the
+ * library stream; the library stream keeps computing.  wxx_nccl_wait(slot) makes the library
+ * stream wait for the last gather issued with that slot (0..3).  Both buffers must stay
+ * allocated until that wait is enqueued. */
+int wxx_nccl_allgather_async(void* recv, const void* send, uint64_t nbytes, int slot);
+int wxx_nccl_wait(int slot);
 int wxx_nccl_async_error(int* code);
 int wxx_nccl_destroy(int abort);
 

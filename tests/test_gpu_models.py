@@ -6,7 +6,9 @@ checked in 3xTF32 mode (fp32-faithful contractions), and tighter (1e-4) for
 GPT2.  In TF32 mode the tensor cores read each fp32 operand truncated to a
 10-bit mantissa (measured on B200: products match truncated operands to fp32
 rounding), so the logit error is a property of TF32 arithmetic at this
-depth; it is bounded at 5e-3 for GPT2 config 0 and 1e-2 relative for ResNet18.
+depth.  Outputs that feed only products are stored rounded to nearest TF32,
+which took GPT2 config 0 from 2.7e-3 to 1.5e-3 (measured on B200); it is
+bounded at 2.5e-3 there and at 1e-2 relative for ResNet18.
 """
 
 import numpy as np
@@ -31,7 +33,7 @@ def _run(model, ids_or_x, is_ids=True):
         return model(t).numpy()
 
 
-@pytest.mark.parametrize("mode,tol", [("tf32", 5e-3), ("3xtf32", 1e-4)])
+@pytest.mark.parametrize("mode,tol", [("tf32", 2.5e-3), ("3xtf32", 1e-4)])
 def test_gpt2_config1_logits(mode, tol):
     """GPT2(1024, 256, 8, 6), batch 4, seq 256."""
     wxx = _wxx()

@@ -69,7 +69,7 @@ SIGNATURES = {
     "wxx_causal_conv1d": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_void_p,
                           c_int, c_int, c_int, c_int],
     "wxx_decay_window": [c_void_p, c_void_p, c_int, c_int, c_int, c_int],
-    "wxx_transpose_stack": [c_void_p, c_void_p, c_int, c_int, c_int],
+    "wxx_transpose_stack": [c_void_p, c_void_p, c_int, c_int, c_int, c_int],
     "wxx_hyena_filters": [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                           c_void_p, c_void_p, c_void_p, c_float, c_void_p],
     "wxx_complex_mul": [c_void_p, c_void_p, c_i64, P_i64, c_void_p, c_i64, P_i64, c_int, P_i64,
@@ -82,8 +82,8 @@ SIGNATURES = {
     "wxx_softmax": [c_void_p, c_void_p, c_i64, c_i64, c_i64],
     "wxx_softmax_masked": [c_void_p, c_void_p, c_i64, c_i64, c_void_p, c_i64, c_i64],
     "wxx_layernorm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64,
-                      c_i64, c_float],
-    "wxx_rmsnorm": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_float],
+                      c_i64, c_float, c_int],
+    "wxx_rmsnorm": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_float, c_int],
     "wxx_batchnorm": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                       c_void_p, c_int, c_int, c_i64, c_float, c_float, c_int],
     "wxx_matmul": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_i64,
@@ -103,7 +103,7 @@ SIGNATURES = {
                               + [c_void_p] * 4 + [c_float, c_void_p, c_int],
     "wxx_conv_weight_pack": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int],
     "wxx_attention": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
-                      c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int],
+                      c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int, c_int],
     "wxx_maxpool2d": [c_void_p, c_void_p, c_void_p] + [c_int] * 10,
     "wxx_adaptive_avgpool2d": [c_void_p, c_void_p] + [c_int] * 6,
     "wxx_rfft": [c_void_p, c_i64, c_void_p, c_i64, c_i64, c_i64, c_i64],
@@ -119,6 +119,8 @@ SIGNATURES = {
     "wxx_nccl_unique_id": [P_u8],
     "wxx_nccl_init": [P_u8, c_int, c_int],
     "wxx_nccl_allgather": [c_void_p, c_void_p, c_u64],
+    "wxx_nccl_allgather_async": [c_void_p, c_void_p, c_u64, c_int],
+    "wxx_nccl_wait": [c_int],
     "wxx_nccl_async_error": [P_int],
     "wxx_nccl_destroy": [c_int],
 }

@@ -96,6 +96,7 @@ struct AttnParams {
   int n_qpairs;
   float scale;
   int causal;
+  int out_tf32;           // O stored rounded to the nearest TF32 value
   const float* mask;      // additive (Sq, Sk) mask, row stride mask_ld, or NULL
   int64_t mask_ld;
   int* err;
@@ -348,7 +349,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < BKV; ++i) {
         const float arg = full ? fmaf(ATT_X(i), sl2, -m_use) : ATT_X(i) - m_use;
-        const float pv = ((i & 7) < 3) ? exp2_fma(arg) : fast_exp2(arg);
+        // p in [0, 2^8] (finite, non-negative) rounded to the nearest TF32
+        // value by integer ops on its bits (ties away from zero): the P V
+        // product then reads it exactly, and the row sum l below adds the
+        // same rounded values, so the weights applied to V sum to one.
+        const float pv = __uint_as_float(
+            (__float_as_uint(((i & 7) < 3) ? exp2_fma(arg) : fast_exp2(arg)) + 0x1000u) &
+            0xFFFFE000u);
         if (i < 32) xa[i & 31] = pv; else xb[i & 31] = pv;
         acc[i & 7] += pv;
       }
@@ -401,9 +408,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
 #pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] *= inv;
+        if (p.out_tf32) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = tf32_rna(v[i]);
+        }
+#pragma unroll
         for (int q = 0; q < 8; ++q)
           *reinterpret_cast<float4*>(st + lane * 128 + ((q ^ (lane & 7)) << 4)) =
-              make_float4(v[4 * q] * inv, v[4 * q + 1] * inv, v[4 * q + 2] * inv, v[4 * q + 3] * inv);
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -458,7 +471,7 @@ bool encode_bshd(CUtensorMap* map, const float* base, int B, int S, int H, int H
 template <int HD>
 int launch_attention(float* O, const float* Q, const float* K, const float* V, int B, int H,
                      int Sq, int Sk, int64_t q_ld, int64_t kv_ld, int64_t o_ld, float scale,
-                     const float* mask, int64_t mask_ld, int causal) {
+                     const float* mask, int64_t mask_ld, int causal, int out_tf32) {
   using C = ACfg<HD>;
   CUtensorMap mq, mk, mv, mo;
   if (!encode_bshd(&mq, Q, B, Sq, H, HD, q_ld, q_ld * Sq, BQ, false) ||
@@ -485,6 +498,7 @@ int launch_attention(float* O, const float* Q, const float* K, const float* V, i
   p.n_qpairs = (Sq + NT * BQ - 1) / (NT * BQ);
   p.scale = scale;
   p.causal = causal;
+  p.out_tf32 = out_tf32 ? 1 : 0;
   p.mask = mask;
   p.mask_ld = mask_ld;
   p.err = wxx::device_error_word();
@@ -506,18 +520,20 @@ int launch_attention(float* O, const float* Q, const float* K, const float* V, i
 // with row stride kv_ld; O: (B, Sq, H, hd) with row stride o_ld.
 // hd must be 32 or 64 and scale > 0; pointers and strides 16-byte aligned.  causal = 1 masks
 // keys after the query position; mask (Sq x Sk, row stride mask_ld) is added
-// to the scaled scores when given.
+// to the scaled scores when given.  The probabilities enter the P V product
+// rounded to the nearest TF32 value; out_tf32 = 1 also stores O rounded so
+// (for an O read only by the TF32 output projection).
 WXX_EXPORT int wxx_attention(float* O, const float* Q, const float* K, const float* V, int B,
                              int H, int Sq, int Sk, int hd, int64_t q_ld, int64_t kv_ld,
                              int64_t o_ld, float scale, const float* mask, int64_t mask_ld,
-                             int causal) {
+                             int causal, int out_tf32) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(B > 0 && H > 0 && Sq > 0 && Sk > 0, "wxx_attention: empty problem");
   WXX_REQUIRE(hd == 32 || hd == 64, "wxx_attention: head dim %d not in {32, 64}", hd);
   WXX_REQUIRE(scale > 0.f, "wxx_attention: scale must be positive");
   if (hd == 32)
     return launch_attention<32>(O, Q, K, V, B, H, Sq, Sk, q_ld, kv_ld, o_ld, scale, mask, mask_ld,
-                                causal);
+                                causal, out_tf32);
   return launch_attention<64>(O, Q, K, V, B, H, Sq, Sk, q_ld, kv_ld, o_ld, scale, mask, mask_ld,
-                              causal);
+                              causal, out_tf32);
 }

@@ -111,6 +111,18 @@ __device__ __forceinline__ float silu_lib(float x) {
   return __fdividef(x, 1.0f + fast_exp2(xc * -1.4426950408889634f));
 }
 
+// x rounded to the nearest TF32 value (10 explicit mantissa bits, ties away
+// from zero), returned as an fp32 whose low 13 mantissa bits are zero.  A
+// tcgen05 kind::tf32 product reads an fp32 operand by dropping those bits
+// (truncation toward zero, a bias of half a TF32 ulp on average); a value
+// stored already rounded is read exactly, so an activation that only ever
+// feeds TF32 products loses half as much and without the bias.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 // Records the first device-side error code; later errors are dropped so the
 // host sees the root cause.
 __device__ __forceinline__ void wxx_device_fail(int* err_word, int code) {

@@ -310,7 +310,7 @@ struct StackSrc {
 };
 
 __global__ void transpose_stack_kernel(float* __restrict__ dst, StackSrc srcs, int rows,
-                                       int cols) {
+                                       int cols, int round_tf32) {
   __shared__ float tile[32][33];
   const int b = blockIdx.z;
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
@@ -323,7 +323,10 @@ __global__ void transpose_stack_kernel(float* __restrict__ dst, StackSrc srcs, i
   __syncthreads();
   for (int k = threadIdx.y; k < 32; k += 8) {
     int c = c0 + k, r = r0 + threadIdx.x;
-    if (r < rows && c < cols) d[(int64_t)c * rows + r] = tile[threadIdx.x][k];
+    if (r < rows && c < cols) {
+      const float v = tile[threadIdx.x][k];
+      d[(int64_t)c * rows + r] = round_tf32 ? tf32_rna(v) : v;
+    }
   }
 }
 
@@ -748,8 +751,10 @@ WXX_EXPORT int wxx_causal_conv1d(float* out, const float* x, int64_t x_off, int6
 
 // dst (n * cols, rows) dense = the transposes of n dense (rows, cols) sources
 // stacked along dst's rows; srcs is a host array of n device pointers, n <= 8.
+// round_tf32 = 1 stores the values rounded to the nearest TF32 value (a copy
+// read only as a TF32 GEMM operand).
 WXX_EXPORT int wxx_transpose_stack(float* dst, const float* const* srcs, int n, int rows,
-                                   int cols) {
+                                   int cols, int round_tf32) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(n >= 1 && n <= 8 && rows >= 0 && cols >= 0 && srcs != nullptr,
               "wxx_transpose_stack: n %d not in 1..8 or bad sizes", n);
@@ -762,7 +767,8 @@ WXX_EXPORT int wxx_transpose_stack(float* dst, const float* const* srcs, int n, 
   }
   dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)n);
   WXX_REQUIRE(grid.y <= 65535, "wxx_transpose_stack: %d rows exceed the grid", rows);
-  transpose_stack_kernel<<<grid, dim3(32, 8), 0, wxx::stream()>>>(dst, ss, rows, cols);
+  transpose_stack_kernel<<<grid, dim3(32, 8), 0, wxx::stream()>>>(dst, ss, rows, cols,
+                                                                 round_tf32 ? 1 : 0);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }

@@ -303,7 +303,8 @@ int choose_splits(int64_t tiles, int total_kb) {
 __global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restrict__ ws,
                                      int splits, int batch, int M, int N, float alpha,
                                      const float* __restrict__ bias, int bias_mode, int kind,
-                                     int64_t ldc, int64_t c_bs, int hw, ConvPost post) {
+                                     int64_t ldc, int64_t c_bs, int hw, ConvPost post,
+                                     int round_tf32) {
   const int64_t MN = (int64_t)M * N;
   const int64_t total = MN * batch;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -330,7 +331,8 @@ __global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restr
     }
     if (kind == 0) {
       const int64_t o = b * c_bs + m * ldc + n;
-      C[o] = conv_post(post, v, (int)n, o);
+      v = conv_post(post, v, (int)n, o);
+      C[o] = round_tf32 ? tf32_rna(v) : v;
     } else {
       const int64_t img = m / hw, pix = m - img * hw;
       const int64_t o = (img * N + n) * hw + pix;
@@ -385,6 +387,7 @@ int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUten
   p.epi.bias_mode = 0;
   p.epi.alpha = 1.0f;
   p.epi.raw = 1;
+  p.epi.round_tf32 = 0;
   p.epi.act = 0;
   p.epi.res = nullptr;
   memset(&p.epi.post, 0, sizeof(p.epi.post));
@@ -394,7 +397,7 @@ int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUten
         real.C, (const float*)ws, p.splits, p.batch, p.M, p.N, real.alpha,
         real.bias_mode ? real.bias : nullptr, real.bias_mode, real.kind,
         real.kind == 0 ? (int64_t)real.ldc : 0, real.kind == 0 ? real.c_bs : 0, real.hw_out,
-        real.post);
+        real.post, real.kind == 0 ? real.round_tf32 : 0);
     cudaError_t e = cudaGetLastError();
     wxx::count_launch();
     if (e != cudaSuccess) {
@@ -591,7 +594,11 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
                 int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha, int mode,
                 int act, const float* res) {
   WXX_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "wxx_matmul: negative size");
-  WXX_REQUIRE(mode >= 0 && mode <= 2, "wxx_matmul: mode %d not in 0..2", mode);
+  WXX_REQUIRE(mode >= 0 && mode <= 3, "wxx_matmul: mode %d not in 0..3", mode);
+  // mode 3: TF32 products with the stored result rounded to the nearest TF32
+  // value, for outputs that are read only as operands of TF32 products.
+  const int round_out = mode == 3 ? 1 : 0;
+  if (round_out) mode = 0;
   WXX_REQUIRE(bias_mode >= 0 && bias_mode <= 3, "wxx_matmul: bias_mode %d not in 0..3", bias_mode);
   WXX_REQUIRE(bias_mode == 0 || bias != nullptr, "wxx_matmul: bias_mode %d needs a bias", bias_mode);
   WXX_REQUIRE(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31),
@@ -608,7 +615,7 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   // gathered tensor-core tiles walking 16 K-blocks) run one warp per output
   // row in exact fp32; the fused epilogues (act / residual) stay on the
   // tensor cores.
-  if (act == 0 && res == nullptr && N <= kSkinnyN && K >= 256 &&
+  if (!round_out && act == 0 && res == nullptr && N <= kSkinnyN && K >= 256 &&
       batch * M * N * K <= (int64_t(1) << 24) && bias_mode <= 1) {
     const int64_t rows = batch * M;
     skinny_gemm_kernel<<<wxx::grid_for(rows * 32, 256), 256, 0, s>>>(
@@ -658,6 +665,7 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   p.epi.res = res;
   p.epi.res_ld = N;
   p.epi.res_bs = M * N;
+  p.epi.round_tf32 = round_out;
   // SM-pair tiles when the product is large and every operand is TMA-fed;
   // each CTA then loads 128-row boxes of both A and B.
   CUtensorMap mc;
@@ -724,7 +732,8 @@ WXX_EXPORT int wxx_linear_batched(float* C, const float* A, const float* B, cons
                                   int trans_b, int act, float alpha, int mode) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(batch >= 1 && M >= 0 && N >= 0 && K > 0, "wxx_linear_batched: bad sizes");
-  WXX_REQUIRE(mode == 0 || mode == 1, "wxx_linear_batched: mode %d not in {0, 1}", mode);
+  WXX_REQUIRE(mode == 0 || mode == 1 || mode == 3,
+              "wxx_linear_batched: mode %d not in {0, 1, 3}", mode);
   WXX_REQUIRE(act == 0 || act == 1, "wxx_linear_batched: act %d not in {0, 1}", act);
   WXX_REQUIRE(!(reinterpret_cast<uintptr_t>(C) & 15) && N % 4 == 0,
               "wxx_linear_batched: C must be 16-byte aligned with N a multiple of 4");
@@ -739,13 +748,15 @@ WXX_EXPORT int wxx_linear_batched(float* C, const float* A, const float* B, cons
 // bias (N) or NULL; residual (M, N dense) or NULL; act 0 none, 1 GELU (tanh),
 // 2 paired GLU: product columns 2j, 2j+1 are (gate, up) of output column j,
 // C (M, N/2) = silu(gate) * up (no residual; N a multiple of 8).
-// mode 0 TF32, 1 3xTF32.  C must be 16-byte aligned and N a multiple of 4.
+// mode 0 TF32, 1 3xTF32, 3 TF32 with C rounded to the nearest TF32 value
+// (for outputs read only by TF32 products).  C must be 16-byte aligned and N
+// a multiple of 4.
 WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float* bias,
                           const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
                           int64_t ldb, int trans_b, int act, float alpha, int mode) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(M >= 0 && N >= 0 && K > 0, "wxx_linear: bad sizes (K must be positive)");
-  WXX_REQUIRE(mode == 0 || mode == 1, "wxx_linear: mode %d not in {0, 1}", mode);
+  WXX_REQUIRE(mode == 0 || mode == 1 || mode == 3, "wxx_linear: mode %d not in {0, 1, 3}", mode);
   WXX_REQUIRE(act >= 0 && act <= 2, "wxx_linear: act %d not in {0, 1, 2}", act);
   WXX_REQUIRE(act != 2 || (residual == nullptr && N % 8 == 0),
               "wxx_linear: the paired GLU takes no residual and needs N a multiple of 8");

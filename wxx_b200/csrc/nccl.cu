@@ -29,6 +29,23 @@ struct NcclApi {
 NcclApi g_api;
 ncclComm_t g_comm = nullptr;
 
+// Asynchronous gathers: a second stream carries the all-gathers so the
+// library stream can go on computing (the next step's forward) while a
+// step's outputs cross NVLink.  Each slot has a "gather done" event.
+constexpr int kAsyncSlots = 4;
+cudaStream_t g_comm_stream = nullptr;
+cudaEvent_t g_ready = nullptr;             // library stream -> comm stream
+cudaEvent_t g_done[kAsyncSlots] = {};      // comm stream -> library stream
+
+int ensure_comm_stream() {
+  if (g_comm_stream) return WXX_OK;
+  WXX_CUDA_CHECK(cudaStreamCreateWithFlags(&g_comm_stream, cudaStreamNonBlocking));
+  WXX_CUDA_CHECK(cudaEventCreateWithFlags(&g_ready, cudaEventDisableTiming));
+  for (int i = 0; i < kAsyncSlots; ++i)
+    WXX_CUDA_CHECK(cudaEventCreateWithFlags(&g_done[i], cudaEventDisableTiming));
+  return WXX_OK;
+}
+
 int load_api() {
   if (g_api.handle) return WXX_OK;
   const char* names[] = {"libnccl.so.2", "libnccl.so"};
@@ -104,6 +121,42 @@ WXX_EXPORT int wxx_nccl_allgather(void* recv, const void* send, uint64_t nbytes)
                "ncclAllGather");
 }
 
+// All-gather on the communication stream, ordered after everything enqueued
+// on the library stream so far (send is complete when it starts).  The
+// library stream does not wait for it: call wxx_nccl_wait(slot) before any
+// library-stream work that reads recv or overwrites send.  The caller keeps
+// both buffers allocated until that wait is enqueued (frees are ordered on
+// the library stream only).  slot in [0, 4).
+WXX_EXPORT int wxx_nccl_allgather_async(void* recv, const void* send, uint64_t nbytes, int slot) {
+  WXX_REQUIRE_INIT();
+  if (!g_comm) {
+    wxx::set_error("wxx_nccl_allgather_async: call wxx_nccl_init first");
+    return WXX_E_STATE;
+  }
+  WXX_REQUIRE(slot >= 0 && slot < kAsyncSlots, "wxx_nccl_allgather_async: slot %d not in [0, %d)",
+              slot, kAsyncSlots);
+  int st = ensure_comm_stream();
+  if (st) return st;
+  WXX_CUDA_CHECK(cudaEventRecord(g_ready, wxx::stream()));
+  WXX_CUDA_CHECK(cudaStreamWaitEvent(g_comm_stream, g_ready, 0));
+  st = check(g_api.AllGather(send, recv, (size_t)nbytes, ncclUint8, g_comm, g_comm_stream),
+             "ncclAllGather");
+  if (st) return st;
+  WXX_CUDA_CHECK(cudaEventRecord(g_done[slot], g_comm_stream));
+  return WXX_OK;
+}
+
+// Makes the library stream wait for the last asynchronous gather of `slot`
+// (no host wait).  A slot never used is already complete.
+WXX_EXPORT int wxx_nccl_wait(int slot) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(slot >= 0 && slot < kAsyncSlots, "wxx_nccl_wait: slot %d not in [0, %d)", slot,
+              kAsyncSlots);
+  if (!g_comm_stream) return WXX_OK;
+  WXX_CUDA_CHECK(cudaStreamWaitEvent(wxx::stream(), g_done[slot], 0));
+  return WXX_OK;
+}
+
 // Reads the communicator's asynchronous error state (0 = healthy).
 WXX_EXPORT int wxx_nccl_async_error(int* code) {
   if (!g_comm) {
@@ -120,6 +173,10 @@ WXX_EXPORT int wxx_nccl_async_error(int* code) {
 // a peer is known to be gone); 0 is the orderly destroy.
 WXX_EXPORT int wxx_nccl_destroy(int abort) {
   if (!g_comm) return WXX_OK;
+  if (g_comm_stream && !abort) {
+    // orderly: the last gathers finish before the communicator goes
+    WXX_CUDA_CHECK(cudaStreamSynchronize(g_comm_stream));
+  }
   ncclResult_t r = abort ? g_api.CommAbort(g_comm) : g_api.CommDestroy(g_comm);
   g_comm = nullptr;
   return check(r, abort ? "ncclCommAbort" : "ncclCommDestroy");

@@ -492,6 +492,9 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(float* __restrict__ y,
                                                         const float* __restrict__ g,
                                                         const float* __restrict__ b,
                                                         int64_t rows, int n, float eps, int kind) {
+  // kind bit 0: RMSNorm (else LayerNorm); bit 1: y rounded to the nearest TF32 value
+  const bool rnd = (kind & 2) != 0;
+  kind &= 1;
   int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   int l = threadIdx.x & 31;
   if (row >= rows) return;
@@ -521,7 +524,10 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(float* __restrict__ y,
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int c = k * 32 + l;
-      if (c < n) q[c] = (v[k] - mean) * inv * g[c] + b[c];
+      if (c < n) {
+        const float o = (v[k] - mean) * inv * g[c] + b[c];
+        q[c] = rnd ? tf32_rna(o) : o;
+      }
     }
     if (l == 0) {
       if (stat0) stat0[row] = mean;
@@ -536,7 +542,10 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(float* __restrict__ y,
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       int c = k * 32 + l;
-      if (c < n) q[c] = v[k] * inv * g[c];
+      if (c < n) {
+        const float o = v[k] * inv * g[c];
+        q[c] = rnd ? tf32_rna(o) : o;
+      }
     }
     if (l == 0 && stat0) stat0[row] = inv;
   }
@@ -551,6 +560,8 @@ __global__ void __launch_bounds__(256) norm_generic_kernel(float* __restrict__ y
                                                            const float* __restrict__ b,
                                                            int64_t outer, int64_t n,
                                                            int64_t inner, float eps, int kind) {
+  const bool rnd = (kind & 2) != 0;   // bit 1: y rounded to the nearest TF32 value
+  kind &= 1;
   __shared__ float sh[8];
   int64_t total = outer * inner;
   for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
@@ -568,8 +579,10 @@ __global__ void __launch_bounds__(256) norm_generic_kernel(float* __restrict__ y
       }
       float var = fmaxf(0.f, block_sum<8>(ss, sh) / (float)n);
       float inv = var > 0.f ? rsqrtf(var + eps) : 0.f;
-      for (int64_t r = threadIdx.x; r < n; r += 256)
-        q[r * inner] = (p[r * inner] - mean) * inv * g[r] + b[r];
+      for (int64_t r = threadIdx.x; r < n; r += 256) {
+        const float o = (p[r * inner] - mean) * inv * g[r] + b[r];
+        q[r * inner] = rnd ? tf32_rna(o) : o;
+      }
       if (threadIdx.x == 0) {
         if (stat0) stat0[t] = mean;
         if (stat1) stat1[t] = inv;
@@ -582,7 +595,10 @@ __global__ void __launch_bounds__(256) norm_generic_kernel(float* __restrict__ y
       }
       float ms = block_sum<8>(ss, sh) / (float)n;
       float inv = ms > 0.f ? rsqrtf(ms + eps) : 0.f;
-      for (int64_t r = threadIdx.x; r < n; r += 256) q[r * inner] = p[r * inner] * inv * g[r];
+      for (int64_t r = threadIdx.x; r < n; r += 256) {
+        const float o = p[r * inner] * inv * g[r];
+        q[r * inner] = rnd ? tf32_rna(o) : o;
+      }
       if (threadIdx.x == 0 && stat0) stat0[t] = inv;
     }
   }
@@ -788,19 +804,23 @@ int launch_norm(float* y, float* s0, float* s1, const float* x, const float* g, 
 }  // namespace
 
 // LayerNorm over the reduce axis of x (outer, n, inner); gamma/beta have n
-// entries; mean/inv_std (outer*inner) may be NULL.
+// entries; mean/inv_std (outer*inner) may be NULL.  out_tf32 = 1 stores y
+// rounded to the nearest TF32 value (y read only by TF32 products).
 WXX_EXPORT int wxx_layernorm(float* y, float* mean, float* inv_std, const float* x,
                              const float* gamma, const float* beta, int64_t outer, int64_t n,
-                             int64_t inner, float eps) {
+                             int64_t inner, float eps, int out_tf32) {
   WXX_REQUIRE_INIT();
-  return launch_norm(y, mean, inv_std, x, gamma, beta, outer, n, inner, eps, 0);
+  return launch_norm(y, mean, inv_std, x, gamma, beta, outer, n, inner, eps,
+                     out_tf32 ? 2 : 0);
 }
 
-// RMSNorm over the reduce axis; inv_rms (outer*inner) may be NULL.
+// RMSNorm over the reduce axis; inv_rms (outer*inner) may be NULL; out_tf32
+// as for wxx_layernorm.
 WXX_EXPORT int wxx_rmsnorm(float* y, float* inv_rms, const float* x, const float* gamma,
-                           int64_t outer, int64_t n, int64_t inner, float eps) {
+                           int64_t outer, int64_t n, int64_t inner, float eps, int out_tf32) {
   WXX_REQUIRE_INIT();
-  return launch_norm(y, inv_rms, nullptr, x, gamma, gamma, outer, n, inner, eps, 1);
+  return launch_norm(y, inv_rms, nullptr, x, gamma, gamma, outer, n, inner, eps,
+                     out_tf32 ? 3 : 1);
 }
 
 // BatchNorm over NCHW x (B, C, hw).  training=0: running statistics are used

@@ -392,6 +392,7 @@ struct EpiParams {
   const float* res;       // residual (M, N) per batch, or NULL
   int64_t res_ld, res_bs;
   int raw;                // split-K: raw partial sums to the workspace map, z = batch * splits + slice
+  int round_tf32;         // kind 0: store C rounded to the nearest TF32 value (tf32_rna)
   ConvPost post;          // kind 1 only
   // kind 2: rows are (sequence b, position n) = (row / conv_len, row % conv_len);
   // C[b, c, n] (c_bs = N * conv_len) = conv_b[c'] + sum_k conv_w[c', k] * Y[row - k, c]
@@ -583,6 +584,10 @@ __device__ __forceinline__ void epi_store_rows(const GemmParams& p, int bt, int 
         for (int i = 0; i < 4; ++i)
           if (n + i < p.N) o[i] += brow[n + i];
       }
+      if (e.round_tf32) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = tf32_rna(o[i]);
+      }
       float* crow = cbase + (int64_t)m * e.ldc;
       if (vec_ok && n + 3 < p.N) {
         *reinterpret_cast<float4*>(crow + n) = make_float4(o[0], o[1], o[2], o[3]);
@@ -623,6 +628,12 @@ __device__ __forceinline__ void epi_store(const GemmParams& p, int bt, int m, in
           o.z += brow[n0 + j + 2];
           o.w += brow[n0 + j + 3];
         }
+        if (e.round_tf32) {
+          o.x = tf32_rna(o.x);
+          o.y = tf32_rna(o.y);
+          o.z = tf32_rna(o.z);
+          o.w = tf32_rna(o.w);
+        }
         *reinterpret_cast<float4*>(crow + n0 + j) = o;
       }
     } else {
@@ -632,7 +643,7 @@ __device__ __forceinline__ void epi_store(const GemmParams& p, int bt, int m, in
         if (n < p.N) {
           float o = v[j] * e.alpha;
           if (brow) o += brow[n];
-          crow[n] = o;
+          crow[n] = e.round_tf32 ? tf32_rna(o) : o;
         }
       }
     }
@@ -767,7 +778,7 @@ __device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
 // compiles without them.
 template <bool POST = true>
 __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, int n0,
-                                          float (&v)[32]) {
+                                          float (&v)[32], bool may_round = true) {
   const EpiParams& e = p.epi;
   const float alpha = e.alpha;
   if (e.bias_mode == 1) {
@@ -812,6 +823,10 @@ __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, in
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = fmaxf(0.0f, v[j]);
   }
+  if (may_round && e.round_tf32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = tf32_rna(v[j]);
+  }
 }
 
 // act == 2 (paired GLU): product columns 2j and 2j+1 are the gate and the up
@@ -821,15 +836,21 @@ __device__ __forceinline__ void epi_apply(const GemmParams& p, int bt, int m, in
 template <bool POST>
 __device__ __forceinline__ void epi_glu_load(const GemmParams& p, int bt, int m, int n0,
                                              uint32_t taddr, float (&v)[32]) {
+  // TF32 rounding is skipped for the gate / up products and applied to the
+  // GLU output that is stored.
   float w[32];
   tmem_ld_32x32(taddr, w);
-  epi_apply<POST>(p, bt, m, n0, w);
+  epi_apply<POST>(p, bt, m, n0, w, false);
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = silu_lib(w[2 * j]) * w[2 * j + 1];
   tmem_ld_32x32(taddr + 32u, w);
-  epi_apply<POST>(p, bt, m, n0 + 32, w);
+  epi_apply<POST>(p, bt, m, n0 + 32, w, false);
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[16 + j] = silu_lib(w[2 * j]) * w[2 * j + 1];
+  if (p.epi.round_tf32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = tf32_rna(v[j]);
+  }
 }
 
 // Short causal convolution epilogue (EpiParams kind 2).

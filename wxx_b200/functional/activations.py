@@ -111,7 +111,7 @@ def _attention_rows(t):
     return dense(t), D
 
 
-def attention(q, k, v, n_heads, mask=None, causal=False, scale=None):
+def attention(q, k, v, n_heads, mask=None, causal=False, scale=None, *, feeds_tf32=False):
     """Fused multi-head attention ``softmax(scale * Q K^T + mask) V``.
 
     ``q`` (B, Sq, D), ``k``/``v`` (B, Sk, D) are the projection outputs with
@@ -120,7 +120,9 @@ def attention(q, k, v, n_heads, mask=None, causal=False, scale=None):
     (B, Sq, D) in the same merged layout.  ``causal`` masks keys after the
     query position (what GPT2's -1e9 upper-triangular mask does); ``mask`` is
     an additive (Sq, Sk) view.  Same values as the unfused
-    matmul -> scale -> add mask -> softmax -> matmul chain up to rounding."""
+    matmul -> scale -> add mask -> softmax -> matmul chain up to rounding.
+    ``feeds_tf32``: the result is read only by a TF32 product (the output
+    projection), so it is stored rounded to the nearest TF32 value."""
     import math
 
     if len(q.shape) != 3 or len(k.shape) != 3 or len(v.shape) != 3:
@@ -147,5 +149,6 @@ def attention(q, k, v, n_heads, mask=None, causal=False, scale=None):
         mptr, mld = mask.ptr, mask.stride[0]
     out = empty((B, Sq, D), "f32", q.requires_grad or k.requires_grad or v.requires_grad)
     check(F.wxx_attention(out.buffer.ptr, q.ptr, k.ptr, v.ptr, B, n_heads, Sq, Sk, hd, q_ld, k_ld, D,
-                          float(scale), mptr, mld, int(bool(causal))), "attention")
+                          float(scale), mptr, mld, int(bool(causal)), int(bool(feeds_tf32))),
+          "attention")
     return out

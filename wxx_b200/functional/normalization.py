@@ -7,26 +7,33 @@ rows beyond 65535 are normalised too.
 """
 
 from ..backend.dispatch import _get_reduce_dims
-from ._common import F, check, dense, empty
+from ._common import F, check, dense, empty, get_matmul_mode
 from .pointwise import _training_only
 
 
-def rmsnorm(tensor1, gamma, axis=None):
+def _round_flag(feeds_tf32):
+    return int(bool(feeds_tf32) and get_matmul_mode() == "tf32")
+
+
+def rmsnorm(tensor1, gamma, axis=None, *, feeds_tf32=False):
     """``y = x * rsqrt(mean(x^2) + 1e-6) * gamma`` (inv = 0 for all-zero rows);
-    returns ``(y, inv_rms)``."""
+    returns ``(y, inv_rms)``.  ``feeds_tf32``: y is read only by TF32 tensor-core
+    products, so in tf32 matmul mode it is stored rounded to the nearest TF32
+    value (the product then reads it exactly instead of truncating it)."""
     x = dense(tensor1)
     g = dense(gamma)
     outer, red, inner, out_shape = _get_reduce_dims(x.shape, axis)
     out = empty(x.shape, "f32")
     irms = empty(out_shape, "f32")
-    check(F.wxx_rmsnorm(out.buffer.ptr, irms.buffer.ptr, x.ptr, g.ptr, outer, red, inner, 1e-6),
-          "rmsnorm")
+    check(F.wxx_rmsnorm(out.buffer.ptr, irms.buffer.ptr, x.ptr, g.ptr, outer, red, inner, 1e-6,
+                        _round_flag(feeds_tf32)), "rmsnorm")
     return out, irms
 
 
-def meanvarnorm(tensor1, gamma, beta, axis=None):
+def meanvarnorm(tensor1, gamma, beta, axis=None, *, feeds_tf32=False):
     """LayerNorm ``(x - mean) * inv * gamma + beta``, ``inv = rsqrt(var + 1e-5)``
-    (0 when the variance is 0); returns ``(y, mean, inv_std)``."""
+    (0 when the variance is 0); returns ``(y, mean, inv_std)``.  ``feeds_tf32``
+    as for ``rmsnorm``."""
     x = dense(tensor1)
     g = dense(gamma)
     b = dense(beta)
@@ -35,7 +42,7 @@ def meanvarnorm(tensor1, gamma, beta, axis=None):
     mean = empty(out_shape, "f32")
     inv = empty(out_shape, "f32")
     check(F.wxx_layernorm(out.buffer.ptr, mean.buffer.ptr, inv.buffer.ptr, x.ptr, g.ptr, b.ptr,
-                          outer, red, inner, 1e-5), "meanvarnorm")
+                          outer, red, inner, 1e-5, _round_flag(feeds_tf32)), "meanvarnorm")
     return out, mean, inv
 
 

@@ -202,7 +202,7 @@ def matmul_add(tensor1, tensor2, tensor3, transpose_A=False, transpose_B=False, 
 _ACTIVATIONS = {None: 0, "gelu": 1, "swiglu": 2}
 
 
-def _linear_batch_transposed(x, weight, bias, activation, residual):
+def _linear_batch_transposed(x, weight, bias, activation, residual, feeds_tf32=False):
     """``linear`` for a (B, M, K) view of a dense (B, K, M) activation (Hyena's
     ``out_proj(z.transpose(1, 2))``, nn/hyena.py:242): the GEMM reads each
     batch's A as a transposed (MN-major) operand instead of copying the view.
@@ -232,13 +232,15 @@ def _linear_batch_transposed(x, weight, bias, activation, residual):
     ev0 = timer.start() if timer is not None else None
     check(F.wxx_linear_batched(out.buffer.ptr, x.ptr, w.ptr, None if b is None else b.ptr,
                                None if r is None else r.ptr, B, M, N, K, x.stride[0], M, 1, N, 0,
-                               _ACTIVATIONS[activation], 1.0, mode), "linear")
+                               _ACTIVATIONS[activation], 1.0,
+                               3 if (feeds_tf32 and mode == 0) else mode), "linear")
     if timer is not None:
         timer.stop(ev0, 2.0 * B * M * N * K, f"{B}x{M}x{N}x{K}T")
     return out
 
 
-def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_weight=False):
+def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_weight=False,
+           feeds_tf32=False):
     """``act(x @ weight + bias) + residual`` with the activation and the
     residual add fused into the GEMM epilogue.
 
@@ -255,11 +257,16 @@ def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_we
     ``transpose_weight``: ``weight`` is given as (N, K) (output, input), i.e.
     the transpose of the nn.Linear layout, and the GEMM reads it as a K-major
     operand -- the faster tensor-core operand form (~15 % on GPT2's K = 1024
-    products); the result is ``x @ weight.T``."""
+    products); the result is ``x @ weight.T``.
+
+    ``feeds_tf32``: the result is read only by TF32 tensor-core products (the
+    next GEMM or the attention kernel), so in tf32 mode it is stored rounded
+    to the nearest TF32 value, which that product then reads exactly (it would
+    otherwise truncate it); no effect in 3xtf32 / fp32 modes."""
     if activation not in _ACTIVATIONS:
         raise ValueError(f"activation must be None, 'gelu' or 'swiglu', got {activation!r}")
     if not transpose_weight:
-        y = _linear_batch_transposed(x, weight, bias, activation, residual)
+        y = _linear_batch_transposed(x, weight, bias, activation, residual, feeds_tf32)
         if y is not None:
             return y
     a = dense(x)
@@ -300,7 +307,8 @@ def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_we
     ev0 = timer.start() if timer is not None else None
     check(F.wxx_linear(out.buffer.ptr, a.ptr, w.ptr, None if b is None else b.ptr,
                        None if r is None else r.ptr, M, N, K, K, K if transpose_weight else N,
-                       int(bool(transpose_weight)), _ACTIVATIONS[activation], 1.0, mode), "linear")
+                       int(bool(transpose_weight)), _ACTIVATIONS[activation], 1.0,
+                       3 if (feeds_tf32 and mode == 0) else mode), "linear")
     if timer is not None:
         timer.stop(ev0, 2.0 * M * N * K, f"{M}x{N}x{K}")
     return out
@@ -309,11 +317,12 @@ def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_we
 _E_UNSUPPORTED = -4
 
 
-def transpose_stack(out, weights):
+def transpose_stack(out, weights, *, round_tf32=False):
     """Writes the transposes of ``weights`` (n <= 8 dense-able (K, N) tensors
     of one shape) stacked along rows into the dense (n * N, K) tensor ``out``
-    with one kernel launch.  False (nothing written) when the shapes do not
-    allow it."""
+    with one kernel launch (values rounded to the nearest TF32 value when
+    ``round_tf32``).  False (nothing written) when the shapes do not allow
+    it."""
     import ctypes
 
     n = len(weights)
@@ -326,7 +335,8 @@ def transpose_stack(out, weights):
         return False
     ws = [dense(w) for w in weights]
     srcs = (ctypes.c_void_p * n)(*[w.ptr for w in ws])
-    check(F.wxx_transpose_stack(out.ptr, srcs, n, K, N), "transpose_stack")
+    check(F.wxx_transpose_stack(out.ptr, srcs, n, K, N, int(bool(round_tf32))),
+          "transpose_stack")
     return True
 
 

@@ -35,10 +35,13 @@ class GPT2Block(Module):
         if context.MODE != 0 or self.drop.p == 0:
             # Dropout is the identity: the residual adds and the GELU ride in
             # the GEMM epilogues (same values as the unfused lines below).
-            h = self.attn.forward(self.ln1(x), mask, residual=x)
+            # Under inference mode the LayerNorm outputs and the GELU output
+            # feed only TF32 products and are stored rounded to TF32.
+            h = self.attn.forward(self.ln1.forward_into_gemm(x), mask, residual=x)
             fc1, act, fc2 = self.mlp._modules.values()
             if isinstance(fc1, Linear) and isinstance(act, GELU) and isinstance(fc2, Linear):
-                u = functional.linear(self.ln2(h), fc1.weight, fc1.bias, activation="gelu")
+                u = functional.linear(self.ln2.forward_into_gemm(h), fc1.weight, fc1.bias,
+                                      activation="gelu", feeds_tf32=context.MODE != 0)
                 return functional.linear(u, fc2.weight, fc2.bias, residual=h)
             return h + self.mlp(self.ln2(h))
         x = x + self.drop(self.attn(self.ln1(x), mask))
@@ -102,7 +105,7 @@ class GPT2(Module):
         h = self.tok_emb(x) + self.pos_emb(self._positions(seq))
         for block in self.blocks:
             h = block(h, mask)
-        return self.head(self.ln_f(h))
+        return self.head(self.ln_f.forward_into_gemm(h))
 
     def generate(self, prompt, max_new_tokens=64, temperature=1.0, top_k=None, stop_token=None,
                  rng=None):

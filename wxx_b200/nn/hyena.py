@@ -173,8 +173,9 @@ class HyenaBlock(Module):
     def forward(self, x):
         if context.MODE != 0:
             # inference: both residual adds ride in GEMM epilogues (same values)
-            x = self.mixer.forward(self.norm1(x), residual=x)
-            return self.feed_forward.forward(self.norm2(x), residual=x)
+            # (the RMSNorm outputs feed only TF32 products: stored rounded)
+            x = self.mixer.forward(self.norm1.forward_into_gemm(x), residual=x)
+            return self.feed_forward.forward(self.norm2.forward_into_gemm(x), residual=x)
         x = x + self.mixer(self.norm1(x))
         x = x + self.feed_forward(self.norm2(x))
         return x
@@ -202,7 +203,7 @@ class Hyena(Module):
         h = self.embed(x)
         for block in self.layers:
             h = block(h)
-        return self.head(self.norm(h))
+        return self.head(self.norm.forward_into_gemm(h))
 
 
 __all__ = [

@@ -226,6 +226,18 @@ class LayerNorm(Module):
             x, self.weightg, self.weightb, axis=axis_arg
         )
 
+    def forward_into_gemm(self, x):
+        """``forward(x)`` for an output read only by TF32 products (the
+        projection after a pre-LN): under inference mode in tf32 matmul mode
+        it is stored rounded to the nearest TF32 value.  Same as ``forward``
+        otherwise."""
+        if context.MODE == 0:
+            return self.forward(x)
+        axis = tuple(range(len(x.shape) - len(self.normalized_shape), len(x.shape)))
+        return functional.meanvarnorm(x, self.weightg, self.weightb,
+                                      axis=axis if len(axis) > 1 else axis[0],
+                                      feeds_tf32=True)[0]
+
 
 class RMSNorm(Module):
     """RMSNorm over the last dim (kernel eps 1e-6, as in the reference)."""
@@ -238,6 +250,14 @@ class RMSNorm(Module):
 
     def forward(self, x):
         return autograd.rmsnorm(x, self.weight).forward(x, self.weight, -1)
+
+    def forward_into_gemm(self, x):
+        """``forward(x)`` for an output read only by TF32 products: under
+        inference mode in tf32 matmul mode it is stored rounded to the
+        nearest TF32 value."""
+        if context.MODE == 0:
+            return self.forward(x)
+        return functional.rmsnorm(x, self.weight, -1, feeds_tf32=True)[0]
 
 
 class BatchNorm(Module):
@@ -336,7 +356,7 @@ class AdaptiveAvgPool2d(Module):
         return autograd.adaptive_avgpooling2d(x).forward(x, self.output_size)
 
 
-def kmajor_weight(owner, name, linears):
+def kmajor_weight(owner, name, linears, round_tf32=False):
     """The weights of ``linears`` (each nn.Linear's (K, N_i)) transposed and
     stacked into one (sum N_i, K) buffer owned by ``owner`` -- the K-major
     operand the tensor-core GEMM reads fastest (``linear(...,
@@ -350,7 +370,7 @@ def kmajor_weight(owner, name, linears):
     if buf is None or tuple(buf.shape) != (total, K):
         buf = Tensor((total, K), value=0.0)
         object.__setattr__(owner, name, buf)
-    if functional.transpose_stack(buf, [lin.weight for lin in linears]):
+    if functional.transpose_stack(buf, [lin.weight for lin in linears], round_tf32=round_tf32):
         return buf
     row = 0
     for lin, n in zip(linears, ns):
@@ -399,15 +419,20 @@ class MultiHeadAttention(Module):
                 # inference: q, k, v from one N = 3D product over a K-major
                 # copy of the three weights; attention reads the column
                 # blocks of its output in place
+                # (the copy, q/k/v and the attention output feed only TF32
+                # products: all stored rounded to the nearest TF32 value)
                 D = self.d_model
-                qkv = functional.linear(x, kmajor_weight(self, "_qkv_t", [self.q, self.k, self.v]),
-                                        transpose_weight=True)
+                rnd = functional.get_matmul_mode() == "tf32"
+                qkv = functional.linear(x, kmajor_weight(self, "_qkv_t", [self.q, self.k, self.v],
+                                                         round_tf32=rnd),
+                                        transpose_weight=True, feeds_tf32=True)
                 q, k, v = qkv[..., 0:D], qkv[..., D:2 * D], qkv[..., 2 * D:3 * D]
             else:
                 q, k, v = self.q(x), self.k(x), self.v(x)
             o = functional.attention(q, k, v, self.n_heads,
                                      mask=None if causal else mask, causal=causal,
-                                     scale=1.0 / math.sqrt(self.head_dim))
+                                     scale=1.0 / math.sqrt(self.head_dim),
+                                     feeds_tf32=context.MODE != 0)
             if residual is not None:
                 return functional.linear(o, self.out.weight, self.out.bias, residual=residual)
             return self.out(o)
@@ -496,7 +521,7 @@ class SwiGLU(Module):
         functional.assign(w12[:, 0:2 * h:2], self.w1.weight)
         functional.assign(w12[:, 1:2 * h:2], self.w2.weight)
         functional.assign(w3p.narrow(0, 0, h), self.w3.weight)
-        g = functional.linear(x, w12, activation="swiglu")
+        g = functional.linear(x, w12, activation="swiglu", feeds_tf32=context.MODE != 0)
         return functional.linear(g, w3p, residual=residual)
 
 
