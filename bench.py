@@ -663,40 +663,85 @@ def run_ours(args, rank, world, local):
     def upload(a):
         return F.from_numpy(a, dtype=np.uint32) if is_ids else F.from_numpy(a)
 
-    x_dev = upload(x_host)
+    idle = hi == lo          # more ranks than batch rows: this rank only joins the gather
+    x_dev = None if idle else upload(x_host)
     comm = wd.NcclCommunicator(rank, world, dist) if world > 1 else None
+    # What a step outputs (and, for N > 1, all-gathers): the argmax token id
+    # of every position (--gather ids, default for the language models), the
+    # fp32 logits (--gather logits), or ResNet's logits.
+    out_ids = wl.output_ids and args.gather == "ids"
+    if not wl.output_ids:
+        row_shape, out_dtype = [10], "f32"
+    elif out_ids:
+        row_shape, out_dtype = [wl.units_per_row()], "u32"
+    else:
+        row_shape, out_dtype = [wl.units_per_row(), wl.V], "f32"
 
     def forward(inp):
-        # model forward + its output: argmax ids for the language models (the
-        # tokens a generation step emits), logits for ResNet
         with wxx.backend.inferenceMode():
             out = model(inp)
-        return F.max(out, -1)[1] if wl.output_ids else out
+        return F.max(out, -1)[1] if out_ids else out
 
-    graph = None
-    if not args.eager:
-        # One CUDA graph per step: the forward is recorded once (after an
-        # eager warm-up inside capture()) and replayed with one launch; the
-        # step reads its input from x_dev.
-        graph = wxx.graph.capture(forward, x_dev)
+    # One CUDA graph per step: the forward is recorded once (after an eager
+    # warm-up inside capture()) and replayed with one launch; the step reads
+    # its input from x_dev.  With an asynchronous logits gather (N > 1,
+    # --gather logits) two graphs with separate output buffers alternate, so
+    # step k+1's forward runs while step k's logits cross NVLink.
+    pipelined = comm is not None and args.gather == "logits" and wl.output_ids
+    graphs = []
+    if not args.eager and not idle:
+        graphs = [wxx.graph.capture(forward, x_dev) for _ in range(2 if pipelined else 1)]
+    pending = [None, None]
+    counter = [0]
+    slot_rows, _ = wd.gather_layout(rows_global, world)
+    gather_desc = None if comm is None else {
+        "what": "argmax ids" if out_ids else "fp32 logits",
+        "bytes_sent_per_rank": slot_rows * int(np.prod(row_shape)) * 4,
+        "bytes_received_per_rank": (world - 1) * slot_rows * int(np.prod(row_shape)) * 4,
+        "mode": ("asynchronous on a second stream, overlapping the next step's forward"
+                 if pipelined else "on the library stream after the forward"),
+        "padded_slots": rows_global % world != 0 or rows_global < world}
 
-    def step(inp):
-        if graph is not None:
-            assert inp is x_dev
-            out = graph.replay()
-        else:
-            out = forward(inp)
-        if comm is not None and (hi - lo) * world == rows_global:
-            out = comm.allgather(out)
+    def run_forward():
+        if idle:
+            return None
+        if graphs:
+            return graphs[counter[0] % len(graphs)].replay()
+        return forward(x_dev)
+
+    def step():
+        """forward + gather; returns the step's (gathered) output or a
+        PendingGather (pipelined logits)."""
+        k = counter[0]
+        if pipelined:
+            g = k % 2
+            if pending[g] is not None:
+                pending[g].wait()       # graph g's output buffer is free again
+                pending[g] = None
+            out = run_forward()
+            pending[g] = comm.allgather_rows(out, rows_global, row_shape, out_dtype, slot=g)
+            counter[0] += 1
+            return pending[g]
+        out = run_forward()
+        counter[0] += 1
+        if comm is not None:
+            out = comm.allgather_rows(out, rows_global, row_shape, out_dtype)
         return out
 
+    def drain():
+        for g in (0, 1):
+            if pending[g] is not None:
+                pending[g].wait()
+                pending[g] = None
+
     def barrier():
+        drain()
         dev.synchronize()
         if dist is not None:
             dist.barrier()
 
     for _ in range(args.warmup):
-        step(x_dev)
+        step()
     barrier()
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[0]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].isdigit() else local
@@ -709,7 +754,9 @@ def run_ours(args, rank, world, local):
 
     def timed_steps(fn, n):
         """(device ms per step, host enqueue ms per step, launches per step).
-        With flush_l2 the L2 flush runs before every step, outside its events."""
+        With flush_l2 the L2 flush runs before every step, outside its events.
+        Pipelined gathers still in flight are waited for inside the last
+        step's events."""
         nl0 = dev.launch_count()
         host = 0.0
         if flush_buf is None:
@@ -718,6 +765,7 @@ def run_ours(args, rank, world, local):
             h = time.perf_counter()
             for _ in range(n):
                 fn()
+            drain()
             host = time.perf_counter() - h
             b.record()
             barrier()
@@ -730,6 +778,7 @@ def run_ours(args, rank, world, local):
                 a.record()
                 h = time.perf_counter()
                 fn()
+                drain()
                 host += time.perf_counter() - h
                 b.record()
                 evs.append((a, b))
@@ -738,61 +787,72 @@ def run_ours(args, rank, world, local):
         nl = dev.launch_count() - nl0 - (n * L2Flush.LAUNCHES if flush_buf is not None else 0)
         return total / n, host * 1000.0 / n, nl / n
 
-    ms, host_ms, launches = timed_steps(lambda: step(x_dev), args.steps)
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # the forward alone (no collective), then the full step (forward + gather)
+    fwd_ms = max_over_ranks(timed_steps(run_forward, args.steps)[0]) if comm is not None \
+        else None
+    ms, host_ms, launches = timed_steps(step, args.steps)
     log_path = os.environ.get("WXX_LAUNCH_LOG")
     if log_path and rank == 0:
         with open(log_path, "w") as f:
             json.dump({"before_timed": n0, "per_step": launches}, f)
     clocks = sampler.stop()
-    if dist is not None:
-        import torch
-
-        t = torch.tensor([ms], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms)
     units_total = rows_global * wl.units_per_row()
     value = units_total / (ms / 1000.0)
 
     # e2e: pinned host inputs -> device -> step (forward, output ids/logits,
-    # all-gather) -> host
-    pin_in = dev.PinnedHostBuffer(x_host.nbytes)
-    pin_in.as_numpy(x_host.dtype, x_host.shape)[...] = x_host
-    out_elems = rows_global * (wl.units_per_row() if wl.output_ids else 10)
-    pin_out = dev.PinnedHostBuffer(max(4, out_elems * 4))
-
-    from wxx_b200.Tensor import Tensor
+    # all-gather) -> host.  The gathered ids (or ResNet logits) are read back
+    # whole; with --gather logits each rank reads back its own rows of the
+    # gathered logits.
+    pin_in = dev.PinnedHostBuffer(max(4, x_host.nbytes))
+    if x_host.nbytes:
+        pin_in.as_numpy(x_host.dtype, x_host.shape)[...] = x_host
+    out_elems = rows_global * int(np.prod(row_shape))
+    own_elems = (hi - lo) * int(np.prod(row_shape))
+    d2h_elems = out_elems if (out_ids or not wl.output_ids) else own_elems
+    pin_out = dev.PinnedHostBuffer(max(4, d2h_elems * 4))
 
     def e2e_step():
-        # the graph reads its input from x_dev; the eager path gets a new buffer
-        t = x_dev if graph is not None else Tensor._empty(list(x_host.shape),
-                                                          "u32" if is_ids else "f32")
-        wxx.backend.lib.F.wxx_memcpy_h2d(t.buffer.ptr, pin_in.ptr, x_host.nbytes)
-        out = step(t)
-        wxx.backend.lib.F.wxx_memcpy_d2h_async(pin_out.ptr, out.ptr, out.nbytes)
-        return out.nbytes
+        if not idle:
+            # the graphs read their input from x_dev
+            wxx.backend.lib.F.wxx_memcpy_h2d(x_dev.buffer.ptr, pin_in.ptr, x_host.nbytes)
+        out = step()
+        if hasattr(out, "wait"):
+            out = out.wait()
+        if d2h_elems == 0:
+            return 0
+        src = out.ptr + (lo * int(np.prod(row_shape)) * 4 if d2h_elems != out_elems else 0)
+        wxx.backend.lib.F.wxx_memcpy_d2h_async(pin_out.ptr, src, d2h_elems * 4)
+        return d2h_elems * 4
 
     for _ in range(args.warmup):
         e2e_step()
     barrier()
     d2h = e2e_step()
     barrier()
-    e2e_ms = timed_steps(e2e_step, args.steps)[0]
-    if dist is not None:
-        import torch
-
-        t = torch.tensor([e2e_ms], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(timed_steps(e2e_step, args.steps)[0])
     e2e_value = units_total / (e2e_ms / 1000.0)
 
     # roofline of the dominant kernel (the tcgen05 GEMM): every GEMM launch of
     # one forward bracketed by CUDA events on the library stream.  With graphs
     # the bracketed forward is itself captured (the events become graph event
     # nodes) and replayed, so host launch gaps stay out of the kernel times.
-    if graph is not None:
+    if idle:
+        ks = {"flops": 0.0, "ms": 0.0, "launches": 0}
+    elif graphs:
         with KernelTimer() as kt:
             timed_graph = wxx.graph.CapturedGraph(
-                forward, (x_dev,), {}, arena_bytes=graph.stats()["arena_bytes"], warmup=False)
+                forward, (x_dev,), {}, arena_bytes=graphs[0].stats()["arena_bytes"],
+                warmup=False)
         runs = []
         for _ in range(3):
             if flush_buf is not None:
@@ -828,18 +888,27 @@ def run_ours(args, rank, world, local):
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak" if wl.name.startswith("gpt2") else "strong", "vs_baseline": None,
+        "scaling": "weak" if wl.rows(2) == 2 * wl.rows(1) else "strong", "vs_baseline": None,
         "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic",
-        "config": dict(wl.config(world), launch="eager" if graph is None else
-                       "CUDA graph of the forward, one replay per step"),
+        "config": dict(wl.config(world), launch="eager" if not graphs else
+                       "CUDA graph of the forward, one replay per step",
+                       gather=gather_desc),
         "roofline": roofline, "clocks": clocks,
         "gpu_launches": int(round(launches * args.steps)),
         "host_enqueue_ms_per_step": host_ms,
         "e2e": {"value": e2e_value, "unit": wl.unit,
                 "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(d2h),
                 "includes": "pinned H2D of inputs, forward, output (argmax ids or logits), "
-                            "all-gather, D2H of the gathered outputs"},
+                            "all-gather, D2H of the gathered outputs (own rows for logits)"},
     }
+    if comm is not None:
+        # SURVEY-style split: the forward alone and the step with its gather
+        line["forward_ms_per_step"] = fwd_ms
+        line["forward_value"] = units_total / (fwd_ms / 1000.0)
+        line["gather_ms_per_step"] = ms - fwd_ms
+        line["idle_ranks"] = sum(1 for r in range(world)
+                                 if wd.shard_bounds(rows_global, world, r)[0]
+                                 == wd.shard_bounds(rows_global, world, r)[1])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, units, reps, dt = time_cpu_sample(wl, seconds=args.cpu_seconds)
         line["cpu_baseline"] = {
@@ -866,6 +935,11 @@ def main(argv=None):
                     default="gpt2_scaled")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", choices=["ids", "logits", "logits-serial"], default="ids",
+                    help="language models, N > 1: all-gather the argmax token ids (default) "
+                         "or the fp32 logits (BASELINE config 5's collective; 'logits' overlaps "
+                         "step k's gather with step k+1's forward, 'logits-serial' runs it "
+                         "after the forward on the same stream)")
     ap.add_argument("--eager", action="store_true",
                     help="model workloads: launch every kernel from Python each step "
                          "instead of replaying the step's CUDA graph")

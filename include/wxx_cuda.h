@@ -298,6 +298,33 @@ int wxx_fftconv_static(float* y, const float* x, int64_t x_off, int64_t sb, int6
                        int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D, int L,
                        int64_t n, int out_len);
 
+/* ---------------------------------------------------------------- generation
+ * nn/gpt.py:108-170 GPT2.generate, on the device: a prefill forward fills per-layer K / V
+ * caches (B, max_len, D); each later token is one decode step of the new position, replayed
+ * from a CUDA graph, with the current length *cur_len (an int in device memory) read and
+ * advanced on the device. */
+/* out (B, D) = tok_emb[ids[b, p]] + pos_emb[p], p = *cur_len - 1 (nn/gpt.py:101-103 for the
+ * last position); ids row stride ids_ld. */
+int wxx_decode_embed(float* out, const uint32_t* ids, int64_t ids_ld, const int* cur_len,
+                     const float* tok_emb, const float* pos_emb, int B, int D, int vocab,
+                     int max_len);
+/* nn/module.py:460-495 for one query row per sequence: appends position p = *cur_len - 1's
+ * k_new / v_new (row b at b * qkv_ld) to Kc / Vc (B, max_len, D = H * hd, batch stride
+ * cache_bs), then O[b] (row stride o_ld) = softmax(scale q . K^T) V over positions 0..p in
+ * exact fp32; hd 32 or 64; out_tf32 = 1 stores O rounded to the nearest TF32 value. */
+int wxx_decode_attention(float* O, int64_t o_ld, const float* q, const float* k_new,
+                         const float* v_new, int64_t qkv_ld, float* Kc, float* Vc,
+                         int64_t cache_bs, int B, int H, int hd, const int* cur_len, int max_len,
+                         float scale, int out_tf32);
+/* nn/gpt.py:147-163 next-token choice for B rows of logits (row stride ld, V entries):
+ * temperature 0 -> first index of the maximum; else top_k (0 = none; values below the k-th
+ * largest dropped) and the first index whose float64 softmax cumulative probability exceeds
+ * draws[b] (0 if none).  Writes ids[b, *cur_len] and advances *cur_len; done_count is a device
+ * counter that starts at 0 and is left at 0. */
+int wxx_sample_tokens(uint32_t* ids, int64_t ids_ld, int* cur_len, unsigned* done_count,
+                      const float* logits, int64_t ld, int B, int V, float temperature, int top_k,
+                      const double* draws, int max_len);
+
 /* ---------------------------------------------------------------- NCCL
  * No reference counterpart (the reference drives one WebGPU device): the
  * all-gather of batch-sharded outputs across the GPUs of one node. */

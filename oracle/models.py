@@ -202,3 +202,39 @@ def hyena_forward(sd, ids, n_layers, order, fast=False):
         h = (h + op.mm((K.silu(w1) * w2).astype(F32), sd[ff + "w3.weight"])).astype(F32)
     x = op.rmsnorm(h, sd["norm.weight"])
     return op.mm(x, emb, tb=True).astype(F32)
+
+
+def gpt2_generate(sd, prompt, n_heads, n_layers, max_new_tokens, temperature=1.0, top_k=None,
+                  stop_token=None, rng=None, max_len=None):
+    """nn/gpt.py:108-170 GPT2.generate: each step runs the full forward over
+    the current ids (float64 logits of the last position), then greedy
+    (temperature 0: first index of the maximum) or top-k + temperature
+    softmax sampling by inverse CDF with one ``rng.random((batch, 1))`` draw
+    per step; stops early once every row emitted ``stop_token``."""
+    ids = np.ascontiguousarray(np.asarray(prompt), dtype=np.uint32)
+    if ids.ndim == 1:
+        ids = ids[None, :]
+    max_len = sd["pos_emb.weight"].shape[0] if max_len is None else max_len
+    batch, seq = ids.shape
+    steps = min(int(max_new_tokens), max_len - seq)
+    for _ in range(steps):
+        last = gpt2_forward(sd, ids, n_heads, n_layers)[:, -1, :].astype(np.float64)
+        if temperature == 0.0:
+            nxt = last.argmax(axis=-1)
+        else:
+            z = last / temperature
+            if top_k is not None:
+                k = min(int(top_k), z.shape[-1])
+                if k < z.shape[-1]:
+                    cut = np.partition(z, -k, axis=-1)[:, -k]
+                    z[z < cut[:, None]] = -np.inf
+            z -= z.max(axis=-1, keepdims=True)
+            p = np.exp(z)
+            p /= p.sum(axis=-1, keepdims=True)
+            u = rng.random((batch, 1))
+            nxt = (np.cumsum(p, axis=-1) > u).argmax(axis=-1)
+        nxt = nxt.astype(np.uint32)
+        ids = np.concatenate([ids, nxt[:, None]], axis=1)
+        if stop_token is not None and np.all(nxt == stop_token):
+            break
+    return ids

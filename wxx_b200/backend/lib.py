@@ -116,6 +116,13 @@ SIGNATURES = {
                           c_int, c_int, c_int, c_i64, c_int, c_void_p, c_i64, c_i64, c_i64, c_i64],
     "wxx_fftconv_static": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64,
                            c_int, c_int, c_int, c_int, c_i64, c_int],
+    "wxx_decode_embed": [c_void_p, c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                         c_int, c_int],
+    "wxx_decode_attention": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_void_p,
+                             c_void_p, c_i64, c_int, c_int, c_int, c_void_p, c_int, c_float,
+                             c_int],
+    "wxx_sample_tokens": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int,
+                          c_float, c_int, c_void_p, c_int],
     "wxx_nccl_unique_id": [P_u8],
     "wxx_nccl_init": [P_u8, c_int, c_int],
     "wxx_nccl_allgather": [c_void_p, c_void_p, c_u64],

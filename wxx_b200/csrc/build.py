@@ -32,6 +32,7 @@ SOURCES = [
     "fft_static.cu",
     "hyena_filter.cu",
     "attention.cu",
+    "generate.cu",
     "pool.cu",
     "nccl.cu",
 ]

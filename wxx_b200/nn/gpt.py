@@ -31,22 +31,37 @@ class GPT2Block(Module):
         self.mlp = Sequential(Linear(d_model, 4 * d_model), GELU(), Linear(4 * d_model, d_model))
         self.drop = Dropout(dropout)
 
-    def forward(self, x, mask=None):
+    def forward(self, x, mask=None, kv_cache=None):
         if context.MODE != 0 or self.drop.p == 0:
             # Dropout is the identity: the residual adds and the GELU ride in
             # the GEMM epilogues (same values as the unfused lines below).
             # Under inference mode the LayerNorm outputs and the GELU output
             # feed only TF32 products and are stored rounded to TF32.
-            h = self.attn.forward(self.ln1.forward_into_gemm(x), mask, residual=x)
+            h = self.attn.forward(self.ln1.forward_into_gemm(x), mask, residual=x,
+                                  kv_cache=kv_cache)
             fc1, act, fc2 = self.mlp._modules.values()
             if isinstance(fc1, Linear) and isinstance(act, GELU) and isinstance(fc2, Linear):
                 u = functional.linear(self.ln2.forward_into_gemm(h), fc1.weight, fc1.bias,
                                       activation="gelu", feeds_tf32=context.MODE != 0)
                 return functional.linear(u, fc2.weight, fc2.bias, residual=h)
             return h + self.mlp(self.ln2(h))
+        if kv_cache is not None:
+            raise RuntimeError("the K/V cache is filled under inference mode only")
         x = x + self.drop(self.attn(self.ln1(x), mask))
         x = x + self.drop(self.mlp(self.ln2(x)))
         return x
+
+    def decode(self, x, kv_cache, cur_len, max_len):
+        """The block for one new position per sequence, ``x`` (batch, d_model)
+        (inference mode; see ``MultiHeadAttention.decode``)."""
+        h = self.attn.decode(self.ln1.forward_into_gemm(x), kv_cache, cur_len, max_len,
+                             residual=x)
+        fc1, act, fc2 = self.mlp._modules.values()
+        if isinstance(fc1, Linear) and isinstance(act, GELU) and isinstance(fc2, Linear):
+            u = functional.linear(self.ln2.forward_into_gemm(h), fc1.weight, fc1.bias,
+                                  activation="gelu", feeds_tf32=True)
+            return functional.linear(u, fc2.weight, fc2.bias, residual=h)
+        return h + self.mlp(self.ln2(h))
 
 
 class GPT2(Module):
@@ -109,50 +124,20 @@ class GPT2(Module):
 
     def generate(self, prompt, max_new_tokens=64, temperature=1.0, top_k=None, stop_token=None,
                  rng=None):
-        """Autoregressive sampling, same contract as the reference (gpt.py:108-170)."""
-        ids = prompt.numpy() if isinstance(prompt, Tensor) else np.asarray(prompt)
-        ids = np.ascontiguousarray(ids, dtype=np.uint32)
-        if ids.ndim == 1:
-            ids = ids[None, :]
-        if ids.ndim != 2:
-            raise ValueError(f"prompt must be 1D or 2D, got shape {ids.shape}")
-        batch, seq = ids.shape
-        if seq == 0:
-            raise ValueError("prompt must contain at least one token")
-        if seq > self.max_len:
-            raise ValueError(f"prompt length {seq} > max_len {self.max_len}")
-        if temperature < 0:
-            raise ValueError("temperature must be non-negative")
-        if rng is None:
-            rng = np.random.default_rng()
-        steps = min(int(max_new_tokens), self.max_len - seq)
-        prev = context.MODE
-        context.MODE = 1
-        try:
-            for _ in range(steps):
-                logits = self.forward(from_numpy(ids, dtype=np.uint32))
-                last = logits[:, -1, :].numpy().astype(np.float64)
-                if temperature == 0.0:
-                    nxt = last.argmax(axis=-1)
-                else:
-                    last = last / temperature
-                    if top_k is not None:
-                        k = min(int(top_k), last.shape[-1])
-                        if k < last.shape[-1]:
-                            cut = np.partition(last, -k, axis=-1)[:, -k]
-                            last[last < cut[:, None]] = -np.inf
-                    last -= last.max(axis=-1, keepdims=True)
-                    probs = np.exp(last)
-                    probs /= probs.sum(axis=-1, keepdims=True)
-                    draws = rng.random((batch, 1))
-                    nxt = (np.cumsum(probs, axis=-1) > draws).argmax(axis=-1)
-                nxt = nxt.astype(np.uint32)
-                ids = np.concatenate([ids, nxt[:, None]], axis=1)
-                if stop_token is not None and np.all(nxt == stop_token):
-                    break
-        finally:
-            context.MODE = prev
-        return ids
+        """Samples up to ``max_new_tokens`` ids after ``prompt`` ((batch, seq) or
+        (seq,) ids, numpy or a u32 tensor) and returns prompt + new ids as a
+        uint32 array: the reference's contract (nn/gpt.py:108-170) --
+        ``temperature=0`` is greedy, ``top_k`` keeps the k most likely ids,
+        ``stop_token`` ends generation once every row has produced it, at most
+        ``max_len`` tokens in total, draws from ``rng`` (numpy Generator).
+
+        Runs on the device with a K/V cache: one prefill forward over the
+        prompt, then one decode step per token replayed from a CUDA graph,
+        sampling on the device (``wxx_b200.nn.generation``)."""
+        from .generation import generate
+
+        return generate(self, prompt, max_new_tokens=max_new_tokens, temperature=temperature,
+                        top_k=top_k, stop_token=stop_token, rng=rng)
 
 
 __all__ = ["GPT2", "GPT2Block"]

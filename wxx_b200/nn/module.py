@@ -407,9 +407,12 @@ class MultiHeadAttention(Module):
             .reshape((b * self.n_heads, seq, self.head_dim))
         )
 
-    def forward(self, x, mask=None, residual=None):
+    def forward(self, x, mask=None, residual=None, kv_cache=None):
         """``residual`` (shaped like the output) is added by the output
-        projection's epilogue: ``residual + attention(x)`` in one pass."""
+        projection's epilogue: ``residual + attention(x)`` in one pass.
+        ``kv_cache``: a (K, V) pair of (batch, max_len, d_model) tensors; the
+        keys and values of positions 0..seq-1 are copied into them (the
+        prefill of generation, see ``decode``)."""
         b, seq, _ = x.shape
         fused_ok = context.MODE != 0 or self.drop.p == 0
         if fused_ok and functional.attention_supported(x, self.n_heads, mask):
@@ -429,6 +432,7 @@ class MultiHeadAttention(Module):
                 q, k, v = qkv[..., 0:D], qkv[..., D:2 * D], qkv[..., 2 * D:3 * D]
             else:
                 q, k, v = self.q(x), self.k(x), self.v(x)
+            self._fill_cache(kv_cache, k, v, seq)
             o = functional.attention(q, k, v, self.n_heads,
                                      mask=None if causal else mask, causal=causal,
                                      scale=1.0 / math.sqrt(self.head_dim),
@@ -437,8 +441,10 @@ class MultiHeadAttention(Module):
                 return functional.linear(o, self.out.weight, self.out.bias, residual=residual)
             return self.out(o)
         q = self._heads(self.q(x), b, seq)
-        k = self._heads(self.k(x), b, seq)
-        v = self._heads(self.v(x), b, seq)
+        kx, vx = self.k(x), self.v(x)
+        self._fill_cache(kv_cache, kx, vx, seq)
+        k = self._heads(kx, b, seq)
+        v = self._heads(vx, b, seq)
         score = functional.matmul_add(q, k, None, transpose_B=True,
                                       alpha=1.0 / math.sqrt(self.head_dim))
         attn = functional.masked_softmax(score, mask) if mask is not None else score.softmax(-1)
@@ -451,6 +457,50 @@ class MultiHeadAttention(Module):
         )
         out = self.out(out)
         return out if residual is None else residual + out
+
+    @staticmethod
+    def _fill_cache(kv_cache, k, v, seq):
+        if kv_cache is not None:
+            functional.assign(kv_cache[0].narrow(1, 0, seq), k)
+            functional.assign(kv_cache[1].narrow(1, 0, seq), v)
+
+    def decode(self, x, kv_cache, cur_len, max_len, residual=None):
+        """One generation step for the newest position of each sequence.
+
+        ``x`` (batch, d_model): the block input of that position; ``kv_cache``
+        the (K, V) caches filled by the prefill ``forward`` and earlier steps;
+        ``cur_len`` a device int holding the number of tokens so far (the new
+        position is cur_len - 1, read on the device, so the same launches serve
+        every step and can be replayed from one CUDA graph).  The position's
+        key and value are appended to the caches and its query attends over
+        positions 0..cur_len-1 (``wxx_decode_attention``, exact fp32).
+        Returns ``residual + out(attention)`` (batch, d_model)."""
+        from ..backend.lib import F as _F, check as _check
+
+        B, D = x.shape
+        if self.q.bias is None and self.k.bias is None and self.v.bias is None:
+            w = self.__dict__.get("_qkv_t")
+            if w is None:
+                w = kmajor_weight(self, "_qkv_t", [self.q, self.k, self.v],
+                                  round_tf32=functional.get_matmul_mode() == "tf32")
+            qkv = functional.linear(x, w, transpose_weight=True)
+            qp, kp, vp, ld = qkv.ptr, qkv.ptr + 4 * D, qkv.ptr + 8 * D, 3 * D
+            keep = (qkv,)
+        else:
+            q, k, v = self.q(x), self.k(x), self.v(x)
+            qp, kp, vp, ld = q.ptr, k.ptr, v.ptr, D
+            keep = (q, k, v)
+        o = Tensor._empty([B, D], "f32")
+        Kc, Vc = kv_cache
+        _check(_F.wxx_decode_attention(o.buffer.ptr, D, qp, kp, vp, ld, Kc.ptr, Vc.ptr,
+                                       max_len * D, B, self.n_heads, self.head_dim, cur_len.ptr,
+                                       max_len, 1.0 / math.sqrt(self.head_dim),
+                                       int(functional.get_matmul_mode() == "tf32")),
+               "decode_attention")
+        del keep
+        if residual is not None:
+            return functional.linear(o, self.out.weight, self.out.bias, residual=residual)
+        return self.out(o)
 
 
 class Attention(Module):
