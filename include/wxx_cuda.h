@@ -62,6 +62,12 @@ int wxx_set_stream(void* stream);
 /* No reference counterpart (kernels have no error channel there): reads and
  * clears the device error word (1 = bounded wait expired, 2 = index out of range). */
 int wxx_device_status(int* code);
+/* No reference counterpart: self-test of the device failure path.  One CTA runs the
+ * tensor-core kernels' bounded mbarrier wait with a limit of limit_ns (0 < limit <= 10 s) on a
+ * barrier that receives its arrival only when `arrive` is 1.  *result_dev (a device int) = 1
+ * when the wait completed, 0 when it gave up; giving up sets the device error word to 1
+ * (bounded wait expired), read and cleared by wxx_device_status. */
+int wxx_wait_probe(int arrive, int64_t limit_ns, int* result_dev);
 int wxx_event_create(void** ev);
 int wxx_event_destroy(void* ev);
 int wxx_event_record(void* ev);

@@ -175,3 +175,43 @@ def test_npz_state_dict_round_trip(tmp_path):
         assert back[k].dtype == state[k].dtype and np.array_equal(back[k], state[k])
     one = s.load(s.save(np.ones(3, np.float32), str(tmp_path / "one.npz")))
     assert list(one) == ["tensor"]
+
+
+def test_nvtx_wrapping_is_opt_in():
+    import subprocess
+    import sys
+
+    code = ("import wxx_b200.functional as F;"
+            "print(getattr(F.matmul_add, '__wxx_nvtx__', None), getattr(F.fftconv, "
+            "'__wxx_nvtx__', None))")
+    env = dict(os.environ, WXX_NVTX="1", PYTHONPATH=ROOT)
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         cwd=ROOT, timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.split() == ["wxx.matmul_add", "wxx.fftconv"]
+    env.pop("WXX_NVTX")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         cwd=ROOT, timeout=300)
+    assert out.stdout.split() == ["None", "None"]
+
+
+def test_check_mode_view_extent():
+    import importlib
+
+    T = importlib.import_module("wxx_b200.Tensor")
+
+    class FakeStorage:
+        size = 4 * 12          # 12 floats
+
+    old = T._CHECK["views"]
+    T._CHECK["views"] = True
+    try:
+        ok = T.Tensor._wrap([3, 4], FakeStorage())
+        assert ok.shape == [3, 4]
+        T.Tensor._wrap([2, 2], FakeStorage(), stride=(4, 2), offset=5)     # last element 11
+        with pytest.raises(IndexError):
+            T.Tensor._wrap([2, 2], FakeStorage(), stride=(4, 2), offset=6)  # element 12
+        with pytest.raises(IndexError):
+            T.Tensor._wrap([3], FakeStorage(), stride=(-1,), offset=1)      # element -1
+    finally:
+        T._CHECK["views"] = old

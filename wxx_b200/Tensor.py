@@ -16,6 +16,8 @@ stream, as ``read_buffer`` does in the reference.
 import ctypes
 import numbers
 
+import os
+
 import numpy as np
 
 from . import validation
@@ -24,6 +26,23 @@ from .backend.lib import F, check
 
 _DTYPES = ("f32", "u32", "c64")
 _NP = {"f32": np.float32, "u32": np.uint32, "c64": np.complex64}
+
+
+# Check mode (WXX_CHECK=1, or wxx_b200.backend.observe.set_check_mode): every
+# view is checked to address only its own storage.
+_CHECK = {"views": os.environ.get("WXX_CHECK", "") == "1"}
+
+
+def _check_view_extent(t):
+    n = validation.numel(t.shape)
+    if n == 0 or t.buffer is None:
+        return
+    lo = t.offset + sum(min(0, (d - 1) * s) for d, s in zip(t.shape, t.stride))
+    hi = t.offset + sum(max(0, (d - 1) * s) for d, s in zip(t.shape, t.stride))
+    size = getattr(t.buffer, "size", None)
+    if lo < 0 or (size is not None and (hi + 1) * _itemsize(t.type) > size):
+        raise IndexError(f"view shape={t.shape} stride={t.stride} offset={t.offset} reaches "
+                         f"elements [{lo}, {hi}] outside its {size}-byte storage")
 
 
 def _itemsize(dtype):
@@ -94,6 +113,8 @@ class Tensor:
         t.requires_grad = requires_grad
         t.creator = None
         t.grad = None
+        if _CHECK["views"]:
+            _check_view_extent(t)
         return t
 
     @classmethod

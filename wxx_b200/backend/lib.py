@@ -116,6 +116,11 @@ SIGNATURES = {
                           c_int, c_int, c_int, c_i64, c_int, c_void_p, c_i64, c_i64, c_i64, c_i64],
     "wxx_fftconv_static": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64,
                            c_int, c_int, c_int, c_int, c_i64, c_int],
+    "wxx_wait_probe": [c_int, c_i64, c_void_p],
+    "wxx_set_check_mode": [c_int],
+    "wxx_get_check_mode": [P_int],
+    "wxx_nvtx_push": [ctypes.c_char_p],
+    "wxx_nvtx_pop": [],
     "wxx_decode_embed": [c_void_p, c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_int, c_int,
                          c_int, c_int],
     "wxx_decode_attention": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_void_p,

@@ -27,6 +27,11 @@ namespace wxx {
 
 void set_error(const char* fmt, ...);
 void count_launch();                // one kernel launch enqueued by this library
+// After every launch: counts it and checks the launch error.  In check mode
+// (WXX_CHECK=1 at wxx_init, or wxx_set_check_mode(1)) it also waits for the
+// kernel and reads the device error word, so a failing kernel is reported by
+// the call that launched it (file:line) instead of by a later one.
+int after_launch(const char* file, int line);
 int require_init();                 // WXX_OK once wxx_init() succeeded
 cudaStream_t stream();              // library stream of the current device
 int num_sms();                      // SM count of the current device
@@ -54,15 +59,10 @@ inline unsigned grid_for(int64_t work_items, int threads_per_cta, int ctas_per_s
     }                                                                             \
   } while (0)
 
-#define WXX_LAUNCH_CHECK()                                                        \
-  do {                                                                            \
-    wxx::count_launch();                                                          \
-    cudaError_t _wxx_e = cudaGetLastError();                                      \
-    if (_wxx_e != cudaSuccess) {                                                  \
-      wxx::set_error("kernel launch failed: %s (%s:%d)",                          \
-                     cudaGetErrorString(_wxx_e), __FILE__, __LINE__);             \
-      return WXX_E_CUDA;                                                          \
-    }                                                                             \
+#define WXX_LAUNCH_CHECK()                                          \
+  do {                                                              \
+    int _wxx_s = wxx::after_launch(__FILE__, __LINE__);             \
+    if (_wxx_s != WXX_OK) return _wxx_s;                            \
   } while (0)
 
 #define WXX_REQUIRE(cond, ...)        \

@@ -250,14 +250,10 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   else
     tc_gemm_pair_kernel<BN, kPairEpiPlain>
         <<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
-  cudaError_t e = cudaGetLastError();
-  wxx::count_launch();
+  const int st_launch = wxx::after_launch(__FILE__, __LINE__);
   int st_ws = wxx_free(ws);       // stream-ordered: valid for the kernel just enqueued
   int st_fl = wxx_free(flags);
-  if (e != cudaSuccess) {
-    wxx::set_error("SM-pair GEMM launch failed: %s", cudaGetErrorString(e));
-    return WXX_E_CUDA;
-  }
+  if (st_launch != WXX_OK) return st_launch;
   return st_ws ? st_ws : st_fl;
 }
 
@@ -398,12 +394,7 @@ int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUten
         real.bias_mode ? real.bias : nullptr, real.bias_mode, real.kind,
         real.kind == 0 ? (int64_t)real.ldc : 0, real.kind == 0 ? real.c_bs : 0, real.hw_out,
         real.post, real.kind == 0 ? real.round_tf32 : 0);
-    cudaError_t e = cudaGetLastError();
-    wxx::count_launch();
-    if (e != cudaSuccess) {
-      wxx::set_error("split-K reduce launch failed: %s", cudaGetErrorString(e));
-      st = WXX_E_CUDA;
-    }
+    st = wxx::after_launch(__FILE__, __LINE__);
   }
   int st2 = wxx_free(ws);   // stream-ordered: valid for the kernels just enqueued
   p.epi = real;
@@ -710,6 +701,48 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
 }
 
 }  // namespace
+
+namespace {
+
+// The bounded mbarrier wait of the tensor-core kernels (mbar_wait, the same
+// function) on a barrier whose only expected arrival is made when `arrive` is
+// set.  Without it nothing arrives and the wait ends after limit_ns with the
+// device error word set, as a stalled producer would leave a GEMM.
+__global__ void wait_probe_kernel(int arrive, unsigned long long limit_ns, int* err,
+                                  int* result) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && arrive) mbar_arrive(&bar);
+  const bool ok = mbar_wait(&bar, 0, &abort_flag, err, limit_ns);
+  __syncthreads();
+  if (threadIdx.x == 0) *result = ok ? 1 : 0;
+}
+
+}  // namespace
+
+// Self-test of the device-side failure path (no reference counterpart): one
+// CTA waits on an mbarrier with the tensor-core kernels' bounded wait and a
+// limit of limit_ns nanoseconds.  arrive = 1 completes the barrier (the wait
+// succeeds, *result_dev = 1); arrive = 0 leaves it pending, so the wait gives
+// up after the limit, *result_dev = 0 and wxx_device_status reports
+// WXX_DEV_ERR_MBAR_TIMEOUT (1) -- the context stays usable.  limit_ns in
+// (0, 10 s].  result_dev: one device int.
+WXX_EXPORT int wxx_wait_probe(int arrive, int64_t limit_ns, int* result_dev) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(limit_ns > 0 && limit_ns <= 10000000000ll,
+              "wxx_wait_probe: limit %lld ns outside (0, 10 s]", (long long)limit_ns);
+  WXX_REQUIRE(result_dev != nullptr, "wxx_wait_probe: result pointer is NULL");
+  wait_probe_kernel<<<1, 32, 0, wxx::stream()>>>(arrive ? 1 : 0, (unsigned long long)limit_ns,
+                                                 wxx::device_error_word(), result_dev);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
 
 WXX_EXPORT int wxx_matmul(float* C, const float* A, const float* B, const float* bias,
                           int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_bs,
@@ -1018,7 +1051,11 @@ int conv2d_nhwc_impl(float* Y, const float* X, const float* Wt, bool packed, con
     WXX_REQUIRE(smem <= 200 * 1024, "wxx_conv2d_nhwc: filter too large (Cin*KH*KW)");
     conv_weight_reorder_kernel<<<Cout < 1184 ? Cout : 1184, 256, smem, s>>>((float*)wr, Wt, Cout,
                                                                            Cin, KH * KW);
-    wxx::count_launch();
+    st = wxx::after_launch(__FILE__, __LINE__);
+    if (st != WXX_OK) {
+      wxx_free(wr);
+      return st;
+    }
   }
   CUtensorMap ma0, ma1, mb0, mb1;
   memset(&ma0, 0, sizeof(ma0));
@@ -1040,7 +1077,7 @@ int conv2d_nhwc_impl(float* Y, const float* X, const float* Wt, bool packed, con
     st = wxx_malloc(&lo_x, (uint64_t)nx * sizeof(float));
     if (st == WXX_OK) {
       tf32_residual_kernel<<<wxx::grid_for(nx / 4 + 1, 256), 256, 0, s>>>((float*)lo_x, X, nx);
-      wxx::count_launch();
+      st = wxx::after_launch(__FILE__, __LINE__);
       ok = encode_nhwc_map(&ma1, (const float*)lo_x, Cin, W, H, B, bw, bh, bb, sw, sh);
       if (ok) st = make_residual(db, p.b, bn, &mb1, &lo_w);
     }

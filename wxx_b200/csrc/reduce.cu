@@ -681,8 +681,7 @@ int launch_cluster(K kernel, dim3 grid, dim3 block, unsigned cluster_x, Args... 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   WXX_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, args...));
-  wxx::count_launch();
-  return WXX_OK;
+  return wxx::after_launch(__FILE__, __LINE__);
 }
 
 }  // namespace

@@ -11,7 +11,11 @@
 // reused by later allocations on the same stream without a device sync.  The
 // reference caps its cache at 4 MiB (device.py:33,108); here large activation
 // buffers are cached too.
+#include <cstdlib>
+
 #include "common.cuh"
+
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstdarg>
 #include <cstdio>
@@ -104,12 +108,46 @@ Arena* arena_of(void* p) {
 
 thread_local char g_err[1024] = {0};
 std::atomic<int64_t> g_launches{0};
+bool g_check_mode = false;
 
 }  // namespace
 
 namespace wxx {
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int after_launch(const char* file, int line) {
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("kernel launch failed: %s (%s:%d)", cudaGetErrorString(e), file, line);
+    return WXX_E_CUDA;
+  }
+  if (!g_check_mode) return WXX_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream(), &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+    return WXX_OK;   // a recorded launch runs later, at replay
+  e = cudaStreamSynchronize(stream());
+  if (e != cudaSuccess) {
+    set_error("kernel launched at %s:%d failed: %s", file, line, cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
+  int v = 0;
+  e = cudaMemcpy(&v, g.err_word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    set_error("reading the device error word failed: %s", cudaGetErrorString(e));
+    return WXX_E_CUDA;
+  }
+  if (v != 0) {
+    cudaMemset(g.err_word, 0, sizeof(int));
+    set_error("kernel launched at %s:%d reported device error %d (%s)", file, line, v,
+              v == WXX_DEV_ERR_MBAR_TIMEOUT ? "a bounded wait expired"
+              : v == WXX_DEV_ERR_BAD_INDEX  ? "an index outside its table"
+                                            : "unknown");
+    return v == WXX_DEV_ERR_MBAR_TIMEOUT ? WXX_E_TIMEOUT : WXX_E_ARG;
+  }
+  return WXX_OK;
+}
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -177,10 +215,36 @@ WXX_EXPORT int wxx_init(int device) {
   WXX_CUDA_CHECK(cudaMemset(g.err_word, 0, 256));
   g.device = device;
   g.ready = true;
+  const char* chk = getenv("WXX_CHECK");
+  g_check_mode = chk != nullptr && chk[0] == '1';
   // Constant tables of the kernels, filled once here (never inside a capture).
   int st = wxx::fft_init_tables();
   if (st != WXX_OK) return st;
   WXX_CUDA_CHECK(cudaStreamSynchronize(g.stream));
+  return WXX_OK;
+}
+
+// Check mode on (1) or off (0); see wxx::after_launch.  Also set by the
+// environment variable WXX_CHECK=1 at wxx_init.
+WXX_EXPORT int wxx_set_check_mode(int on) {
+  g_check_mode = on != 0;
+  return WXX_OK;
+}
+
+WXX_EXPORT int wxx_get_check_mode(int* on) {
+  *on = g_check_mode ? 1 : 0;
+  return WXX_OK;
+}
+
+// NVTX ranges around functional calls (WXX_NVTX=1 on the Python side):
+// visible in Nsight timelines, free when no tool is attached.
+WXX_EXPORT int wxx_nvtx_push(const char* name) {
+  nvtxRangePushA(name ? name : "wxx");
+  return WXX_OK;
+}
+
+WXX_EXPORT int wxx_nvtx_pop(void) {
+  nvtxRangePop();
   return WXX_OK;
 }
 

@@ -97,9 +97,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  Returns false when the
-// wall-clock limit expired or another role raised the abort flag.
+// wall-clock limit (limit_ns of %globaltimer) expired -- recording
+// WXX_DEV_ERR_MBAR_TIMEOUT and raising the abort flag -- or another role
+// raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* err) {
+                                          volatile int* abort_flag, int* err,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   unsigned long long t0 = globaltimer();
@@ -107,7 +110,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(addr, parity)) return true;
     if ((it & 255) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         wxx_device_fail(err, WXX_DEV_ERR_MBAR_TIMEOUT);
         *abort_flag = 1;
         return false;

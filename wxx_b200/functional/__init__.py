@@ -131,3 +131,8 @@ def cceloss(*args, **kwargs):
 
 
 __all__ = [name for name in dir() if not name.startswith("__")]
+
+from ..backend import observe as _observe  # noqa: E402
+
+if _observe.nvtx_requested():
+    _observe.wrap_namespace(globals(), "wxx")
