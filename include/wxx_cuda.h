@@ -68,6 +68,16 @@ int wxx_device_status(int* code);
  * when the wait completed, 0 when it gave up; giving up sets the device error word to 1
  * (bounded wait expired), read and cleared by wxx_device_status. */
 int wxx_wait_probe(int arrive, int64_t limit_ns, int* result_dev);
+/* No reference counterpart (the reference has no sanitizer mode): check mode on / off.  After
+ * every kernel launch the library then waits for the kernel and reads the device error word,
+ * so the launching call returns WXX_E_TIMEOUT (expired bounded wait) or WXX_E_ARG (index
+ * outside its table) naming its source line.  Also enabled by WXX_CHECK=1 at wxx_init. */
+int wxx_set_check_mode(int on);
+int wxx_get_check_mode(int* on);
+/* No reference counterpart (the reference has no tracing): NVTX range push / pop around a
+ * functional call (the Python side does it for every op when WXX_NVTX=1). */
+int wxx_nvtx_push(const char* name);
+int wxx_nvtx_pop(void);
 int wxx_event_create(void** ev);
 int wxx_event_destroy(void* ev);
 int wxx_event_record(void* ev);
