@@ -340,15 +340,24 @@ WXX_EXPORT int wxx_decode_attention(float* O, int64_t o_ld, const float* q, cons
   const size_t smem = (size_t)max_len * sizeof(float);
   dim3 grid((unsigned)H, (unsigned)B);
   const int D = H * hd;
+  // the largest score row this process asked for so far (attribute set outside
+  // any graph capture in practice: the first call of a size runs eagerly)
+  static size_t smem_set[2] = {0, 0};
+  const int which = hd == 32 ? 0 : 1;
+  if (smem > 48 * 1024 && smem > smem_set[which]) {
+    if (which == 0)
+      WXX_CUDA_CHECK(cudaFuncSetAttribute(decode_attention_kernel<32>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    else
+      WXX_CUDA_CHECK(cudaFuncSetAttribute(decode_attention_kernel<64>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    smem_set[which] = smem;
+  }
   if (hd == 32) {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(decode_attention_kernel<32>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     decode_attention_kernel<32><<<grid, kAttnWarps * 32, smem, wxx::stream()>>>(
         O, o_ld, q, k_new, v_new, qkv_ld, Kc, Vc, cache_bs, D, cur_len, max_len, scale, out_tf32,
         wxx::device_error_word());
   } else {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(decode_attention_kernel<64>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     decode_attention_kernel<64><<<grid, kAttnWarps * 32, smem, wxx::stream()>>>(
         O, o_ld, q, k_new, v_new, qkv_ld, Kc, Vc, cache_bs, D, cur_len, max_len, scale, out_tf32,
         wxx::device_error_word());

@@ -74,7 +74,7 @@ def _prefill(model, state, seq, temperature, top_k):
     mask = model.causal_mask(seq)
     h = model.tok_emb(ids) + model.pos_emb(model._positions(seq))
     for block, cache in zip(model.blocks, state.caches):
-        h = block(h, mask, kv_cache=cache)
+        h = block.forward(h, mask, kv_cache=cache)
     last = h.narrow(1, seq - 1, 1).reshape((state.batch, h.shape[-1]))
     logits = model.head(model.ln_f.forward_into_gemm(last))
     _sample(model, state, logits, temperature, top_k)
