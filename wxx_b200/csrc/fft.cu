@@ -1532,6 +1532,129 @@ __global__ void __launch_bounds__(SCfg<L>::T, 1)
   }
 }
 
+// ------------------------------------------------------------ two-CTA convolution (n = 16384)
+//
+// The fused convolution at N = 8192 complex values per row, sized so that two
+// CTAs share an SM (256 threads, <= 128 registers each, one 72 KB planar row
+// buffer): while one CTA waits at a pass barrier or on memory the other
+// issues.  Plan (radices of fft_pair_kernel<13>): forward 16 | 32 | 16 with the
+// last forward pass, the spectrum product and the first inverse pass fused in
+// registers (pp_mirror), then inverse 32 | 16 to global memory.  Every pass
+// transforms in place: loads, barrier, stores.  x, the filter spectrum and the
+// gate are read straight from global memory (the spectrum and gate stay in
+// L2 across the batch); the radix-32 passes are split over two threads so
+// that no thread holds more than 16 paired values.
+
+__device__ __forceinline__ u64 p_sel(bool c, u64 a, u64 b) { return c ? a : b; }
+
+// One in-place Stockham pass of radix 32 (sub-transform size NS before it)
+// over butterfly pairs (j, j+1), each pair shared by two threads: the thread of
+// parity h loads the inputs r = 2m + h (m = 0..15), twiddles them and runs a
+// 16-point DFT, giving E_h[s] = sum_m x[2m+h] w16^(ms).  The 32 outputs are
+// X[s] = E_0[s] + w32^s E_1[s] and X[s+16] = E_0[s] - w32^s E_1[s]; thread
+// h = 0 makes those of s = 0..7 and thread h = 1 those of s = 8..15, after
+// trading E_0[8..15] for E_1[0..7] with its partner (lane xor 1).
+// w32^(8+i) = -i w32^i, so both threads use the constants w32^i.
+template <int N, int NS, int T>
+__device__ __forceinline__ void pp_split32(PBuf buf, const float* __restrict__ tw) {
+  constexpr int R = 32, NB = N / R;
+  static_assert(NB == T, "one thread per half butterfly pair");
+  const int h = threadIdx.x & 1;
+  const bool odd = h != 0;
+  const int j = (threadIdx.x >> 1) * 2;
+  const int k = j & (NS - 1);
+  CP v[16];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const int r = 2 * m + h;
+    v[m].re = lds2(buf.re + pad3(j + r * NB));
+    v[m].im = lds2(buf.im + pad3(j + r * NB));
+  }
+  {
+    // m = 0: input r = h; r = 0 has no twiddle
+    const u64 c = ldg2(tw + k), sn = ldg2(tw + (R - 1) * NS + k);
+    const CP t = v[0];
+    CP w = t;
+    p_twiddle(w, c, sn);
+    v[0].re = p_sel(odd, w.re, t.re);
+    v[0].im = p_sel(odd, w.im, t.im);
+  }
+#pragma unroll
+  for (int m = 1; m < 16; ++m) {
+    const int r = 2 * m + h;
+    p_twiddle(v[m], ldg2(tw + (r - 1) * NS + k), ldg2(tw + (R - 1 + r - 1) * NS + k));
+  }
+  p_dft<16>(v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    // send E_h[8+i] (h = 0) or E_h[i] (h = 1); receive the partner's
+    const u64 sre = p_sel(odd, v[i].re, v[8 + i].re);
+    const u64 sim = p_sel(odd, v[i].im, v[8 + i].im);
+    const u64 rre = __shfl_xor_sync(0xffffffffu, sre, 1);
+    const u64 rim = __shfl_xor_sync(0xffffffffu, sim, 1);
+    // a = E_0[s], b = E_1[s], s = 8h + i
+    const CP a{p_sel(odd, rre, v[i].re), p_sel(odd, rim, v[i].im)};
+    const CP b{p_sel(odd, v[8 + i].re, rre), p_sel(odd, v[8 + i].im, rim)};
+    const float c = cos32(i), sn = sin32(i);   // constants once unrolled
+    const u64 C = p_make(c, c), S = p_make(sn, sn), NS_ = p_make(-sn, -sn);
+    // t = w32^i b = (re c + im sn) + i (im c - re sn)
+    u64 tr = p_fma(b.re, C, p_mul(b.im, S));
+    u64 ti = p_fma(b.im, C, p_mul(b.re, NS_));
+    // h = 1: t *= -i  ->  (ti, -tr)
+    const u64 ntr = p_sub(0ull, tr);
+    const u64 tr2 = p_sel(odd, ti, tr);
+    const u64 ti2 = p_sel(odd, ntr, ti);
+    v[i] = CP{p_add(a.re, tr2), p_add(a.im, ti2)};        // output 8h + i
+    v[8 + i] = CP{p_sub(a.re, tr2), p_sub(a.im, ti2)};    // output 16 + 8h + i
+  }
+  __syncthreads();   // every input is read before any output is stored
+  const int d = (j - k) * R + k;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r0 = 8 * h + i, r1 = 16 + 8 * h + i;
+    sts2(buf.re + pad3(d + r0 * NS), v[i].re);
+    sts2(buf.im + pad3(d + r0 * NS), v[i].im);
+    sts2(buf.re + pad3(d + r1 * NS), v[8 + i].re);
+    sts2(buf.im + pad3(d + r1 * NS), v[8 + i].im);
+  }
+  __syncthreads();
+}
+
+template <int L>
+struct C2Cfg {
+  static constexpr int N = 1 << L;
+  static constexpr int T = 256;
+  static constexpr int SMEM = 2 * padded3(N) * 4;   // one planar row buffer
+};
+
+template <int L, bool GATED>
+__global__ void __launch_bounds__(C2Cfg<L>::T, 2) fft_conv2_kernel(RowArgs a) {
+  static_assert(L == 13, "plan written for N = 8192");
+  constexpr int N = C2Cfg<L>::N, T = C2Cfg<L>::T;
+  extern __shared__ __align__(16) float psm[];
+  const PBuf buf{psm, psm + padded3(N)};
+  const float2* utw = g_fft_tw + tw_offset(L) + tw_passes_size(N);  // exp(-i pi k / N)
+  const int d = blockIdx.x / a.rows_b;
+  const int b = blockIdx.x - d * a.rows_b;
+  const int64_t row = (int64_t)b * a.rows_d + d;
+  const float* x = a.in + a.in_off + (int64_t)b * a.in_sb + (int64_t)d * a.in_sd;
+  const bool xvec = a.in_st == 1 && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  pp_first<N, 16, T>(buf, x, a.in_st, a.in_len, xvec);
+  pp_split32<N, 16, T>(buf, g_fft_ptw + pt_fwd_off(L, 0, 1));
+  pp_mirror<N, 16, T, kModeConv, true>(buf, buf, utw, a, row, a.H + (int64_t)d * a.h_ld);
+  pp_split32<N, 16, T>(buf, g_fft_ptw + pt_inv_off(L, 0, 1));
+  float* y = a.out + row * a.out_ld;
+  const bool vec = (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  const float* tl = g_fft_ptw + pt_inv_off(L, 0, 2);
+  if constexpr (GATED) {
+    bool gvec;
+    const float* g = gate_row(a, b, d, gvec);
+    pp_last<N, 16, T, kGateGlobal>(buf, tl, y, a.out_len, vec, g, a.g_st, gvec);
+  } else {
+    pp_last<N, 16, T>(buf, tl, y, a.out_len, vec);
+  }
+}
+
 // ------------------------------------------------------------ dispatch
 
 template <int LOGN, int MODE>
@@ -1585,6 +1708,30 @@ int ilog2_exact(int64_t n) {
   int l = 0;
   while ((int64_t(1) << l) < n) ++l;
   return l;
+}
+
+// The two-CTA convolution at N = 8192 (fft_conv2_kernel).
+template <bool GATED>
+int launch_conv2(const RowArgs& a, int64_t rows) {
+  static bool attr = false;
+  if (!attr) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(fft_conv2_kernel<13, GATED>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C2Cfg<13>::SMEM));
+    attr = true;
+  }
+  fft_conv2_kernel<13, GATED><<<(unsigned)rows, C2Cfg<13>::T, C2Cfg<13>::SMEM, wxx::stream()>>>(a);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+bool conv2_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("WXX_FFT_CONV2");
+    on = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
 }
 
 // The staged persistent convolution, when the rows allow bulk copies.
@@ -1651,6 +1798,8 @@ int run_rows(int mode, int64_t n, RowArgs a, int64_t rows, const float2* Hspec) 
   WXX_REQUIRE(rows < (int64_t(1) << 31), "fft: too many rows");
   if (logN <= kMaxSmemLogN) {
     int xlen = 0, glen = 0;
+    if (mode == kModeConv && logN == 13 && conv2_enabled())
+      return a.gate != nullptr ? launch_conv2<true>(a, rows) : launch_conv2<false>(a, rows);
     if (mode == kModeConv && logN >= kPairMinL && logN <= 13 &&
         conv_stageable(a, logN, &xlen, &glen)) {
       switch (logN) {
