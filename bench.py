@@ -84,7 +84,7 @@ class GPT2Scaled(Workload):
 
     def config(self, world):
         return {"workload": "GPT2(vocab=50304,d=1024,heads=16,layers=24) fwd, seq 1024, "
-                            "8 seq/GPU, argmax token ids all-gathered",
+                            "8 seq/GPU",
                 "global_batch": self.B_PER_GPU * world, "seq_len": self.S,
                 "parallelism": f"dp{world} (batch-sharded inference)",
                 "matmul_mode": "tf32", "l2": "inputs larger than L2 (1.4 GB weights)"}
@@ -585,6 +585,28 @@ def run_sweep(args, rank, world, local):
     return 0
 
 
+def line_config(wl, world, args):
+    """The ``config`` both arms print for a model workload (the reference arm
+    times a bounded sample of the same workload and says so in
+    ``cpu_baseline.sample``, not here)."""
+    rows = wl.rows(world)
+    gather = None
+    if world > 1:
+        out_ids = wl.output_ids and args.gather == "ids"
+        per_row = 10 if not wl.output_ids else (wl.units_per_row() * (1 if out_ids else wl.V))
+        slot = max(1, -(-rows // world))
+        gather = {"what": "argmax ids" if out_ids else "fp32 logits",
+                  "bytes_sent_per_rank": slot * per_row * 4,
+                  "bytes_received_per_rank": (world - 1) * slot * per_row * 4,
+                  "mode": ("asynchronous on a second stream, overlapping the next step's forward"
+                           if (wl.output_ids and args.gather == "logits")
+                           else "on the library stream after the forward"),
+                  "padded_slots": rows % world != 0 or rows < world}
+    return dict(wl.config(world),
+                launch="eager" if args.eager else "CUDA graph of the forward, one replay per step",
+                gather=gather)
+
+
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args, rank, world):
@@ -631,7 +653,7 @@ def run_reference(args, rank, world):
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": wl.config(world), "impl": "reference",
+        "data": "synthetic", "config": line_config(wl, world, args), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": wl.unit, "cores": cpu_cores(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -693,14 +715,6 @@ def run_ours(args, rank, world, local):
         graphs = [wxx.graph.capture(forward, x_dev) for _ in range(2 if pipelined else 1)]
     pending = [None, None]
     counter = [0]
-    slot_rows, _ = wd.gather_layout(rows_global, world)
-    gather_desc = None if comm is None else {
-        "what": "argmax ids" if out_ids else "fp32 logits",
-        "bytes_sent_per_rank": slot_rows * int(np.prod(row_shape)) * 4,
-        "bytes_received_per_rank": (world - 1) * slot_rows * int(np.prod(row_shape)) * 4,
-        "mode": ("asynchronous on a second stream, overlapping the next step's forward"
-                 if pipelined else "on the library stream after the forward"),
-        "padded_slots": rows_global % world != 0 or rows_global < world}
 
     def run_forward():
         if idle:
@@ -890,9 +904,7 @@ def run_ours(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak" if wl.rows(2) == 2 * wl.rows(1) else "strong", "vs_baseline": None,
         "dtype": "f32 (tf32 tensor-core products)", "data": "synthetic",
-        "config": dict(wl.config(world), launch="eager" if not graphs else
-                       "CUDA graph of the forward, one replay per step",
-                       gather=gather_desc),
+        "config": line_config(wl, world, args),
         "roofline": roofline, "clocks": clocks,
         "gpu_launches": int(round(launches * args.steps)),
         "host_enqueue_ms_per_step": host_ms,
