@@ -136,6 +136,9 @@ int wxx_decay_window(float* out, const float* decay, int rows, int channels, int
  * (rows, cols) arrays.  round_tf32 = 1 stores the values rounded to the nearest TF32 value. */
 int wxx_transpose_stack(float* dst, const float* const* srcs, int n, int rows, int cols,
                         int round_tf32);
+/* No reference counterpart: dst[0..n) = src[0..n) rounded to the nearest TF32 value (a weight
+ * copy read only by TF32 products, e.g. the tied LM head of nn/gpt.py). */
+int wxx_round_tf32(float* dst, const float* src, int64_t n);
 /* nn/hyena.py:127-130 ImplicitFilter.forward (Linear -> Sine(omega) -> Linear over the positional
  * encoding, transposed) and :236-239 (h * decay_window) for all `n` filters of an operator in one
  * launch, exact fp32: out (n, D, L) dense, filter i = (sin(omega * (pe @ w1[i] + b1[i])) @ w2[i]

@@ -116,3 +116,36 @@ def test_hyena_causal_and_batch_independent():
     out2 = _run(model, ids2)
     assert np.allclose(base[0, :40], out2[0, :40], atol=1e-4)
     assert np.allclose(base[1:], out2[1:], atol=1e-5)
+
+
+def test_cached_weight_copies_follow_in_place_writes():
+    """Inference reads K-major / TF32-rounded copies of the weights, kept
+    between calls; a write through the API (assign, load_state_dict) must be
+    seen by the next forward."""
+    wxx = _wxx()
+    F = wxx.functional
+    V, D, H, L, S = 128, 64, 4, 2, 32
+    sd = init.gpt2_state_dict(0, V, D, H, L, S)
+    ids = init.token_ids(1, 2, S, V)
+    model = wxx.nn.GPT2(V, D, H, L, max_len=S)
+    model.load_state_dict(sd)
+    wxx.functional.set_matmul_mode("3xtf32")
+    try:
+        first = _run(model, ids)
+        assert np.abs(first - models.gpt2_forward(sd, ids, H, L)).max() < 1e-4
+        sd2 = dict(sd)
+        for key in ("blocks.0.mlp.0.weight", "blocks.1.mlp.2.weight", "blocks.0.attn.out.weight",
+                    "blocks.1.attn.q.weight", "tok_emb.weight"):
+            sd2[key] = (sd[key] * 1.7).astype(np.float32)
+            F.assign(dict(model.named_parameters())[key],
+                     F.from_numpy(sd2[key]))
+        second = _run(model, ids)
+        assert np.abs(second - models.gpt2_forward(sd2, ids, H, L)).max() < 1e-4
+        model.load_state_dict(sd)
+        assert np.abs(_run(model, ids) - first).max() < 1e-6
+    finally:
+        wxx.functional.set_matmul_mode("tf32")
+    # TF32 mode reads the rounded copies; they follow the writes as well
+    model.load_state_dict(sd2)
+    got = _run(model, ids)
+    assert np.abs(got - models.gpt2_forward(sd2, ids, H, L)).max() < 5e-3

@@ -16,6 +16,7 @@ package on a machine without a GPU works; the first GPU operation there raises.
 """
 
 import ctypes
+import itertools
 import os
 import sys
 import weakref
@@ -64,6 +65,9 @@ def ensure_init():
         _ctx.init()
 
 
+_buffer_uids = itertools.count(1)
+
+
 class DeviceBuffer:
     """An allocation of the library's device allocator.
 
@@ -73,7 +77,12 @@ class DeviceBuffer:
     holding the same ``DeviceBuffer``.
     """
 
-    __slots__ = ("ptr", "size", "label", "__weakref__")
+    # ``uid`` names this allocation for the life of the process (object ids
+    # can be reused); ``version`` counts the in-place writes made through the
+    # library's API (``functional.assign`` and the other in-place ops), so
+    # caches derived from a buffer (K-major weight copies) can tell when it
+    # changed.
+    __slots__ = ("ptr", "size", "label", "uid", "version", "__weakref__")
 
     def __init__(self, nbytes, label="Tensor"):
         ensure_init()
@@ -82,6 +91,8 @@ class DeviceBuffer:
         self.ptr = p.value
         self.size = int(nbytes)
         self.label = label
+        self.uid = next(_buffer_uids)
+        self.version = 0
         _pool._track(self)
 
     def free(self):

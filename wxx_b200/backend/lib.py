@@ -70,6 +70,7 @@ SIGNATURES = {
                           c_int, c_int, c_int, c_int],
     "wxx_decay_window": [c_void_p, c_void_p, c_int, c_int, c_int, c_int],
     "wxx_transpose_stack": [c_void_p, c_void_p, c_int, c_int, c_int, c_int],
+    "wxx_round_tf32": [c_void_p, c_void_p, c_i64],
     "wxx_hyena_filters": [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                           c_void_p, c_void_p, c_void_p, c_float, c_void_p],
     "wxx_complex_mul": [c_void_p, c_void_p, c_i64, P_i64, c_void_p, c_i64, P_i64, c_int, P_i64,

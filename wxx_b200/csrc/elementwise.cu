@@ -773,6 +773,41 @@ WXX_EXPORT int wxx_transpose_stack(float* dst, const float* const* srcs, int n, 
   return WXX_OK;
 }
 
+namespace {
+// dst[i] = src[i] rounded to the nearest TF32 value (16-byte vectors when
+// both are aligned and n % 4 == 0).
+__global__ void round_tf32_kernel(float* __restrict__ dst, const float* __restrict__ src,
+                                  int64_t n) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) ==
+                   0 && (n & 3) == 0;
+  if (vec) {
+    const int64_t n4 = n / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      float4 v = reinterpret_cast<const float4*>(src)[i];
+      v = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+      reinterpret_cast<float4*>(dst)[i] = v;
+    }
+  } else {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+      dst[i] = tf32_rna(src[i]);
+  }
+}
+}  // namespace
+
+// dst[0..n) = src[0..n) rounded to the nearest TF32 value: a weight copy read
+// only by TF32 products (e.g. the tied LM head).
+WXX_EXPORT int wxx_round_tf32(float* dst, const float* src, int64_t n) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(n >= 0, "wxx_round_tf32: negative size");
+  if (n == 0) return WXX_OK;
+  round_tf32_kernel<<<wxx::grid_for(n / 4 + 1, kThreads), kThreads, 0, wxx::stream()>>>(dst, src,
+                                                                                       n);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
 // out (channels, length) = exp(-|decay[stage, d]| * t)
 WXX_EXPORT int wxx_decay_window(float* out, const float* decay, int rows, int channels, int length,
                                 int stage) {

@@ -102,6 +102,9 @@ def complex_add_inplace(accumulator, tensor1):
     x = dense(tensor1)
     check(F.wxx_complex_add_inplace(accumulator.ptr, x.ptr, _prod(x.shape)),
           "complex_add_inplace")
+    from .utils import mark_written
+
+    mark_written(accumulator)
     return accumulator
 
 

@@ -31,6 +31,7 @@ def assign(tensor1, val):
             bits = int(np.array([val], dtype=np.float32).view(np.uint32)[0])
         check(F.wxx_strided_fill(tensor1.buffer.ptr, tensor1.offset, dstride, rank, shape, bits),
               "assign")
+        mark_written(tensor1)
         return tensor1
     if not isinstance(val, Tensor):
         raise TypeError(f"assign expects a Tensor or a scalar, got {type(val).__name__}")
@@ -43,7 +44,16 @@ def assign(tensor1, val):
     check(F.wxx_strided_copy(tensor1.buffer.ptr, tensor1.offset, dstride, val.buffer.ptr,
                              val.offset, arr64(val.stride), rank, shape, tensor1.itemsize()),
           "assign")
+    mark_written(tensor1)
     return tensor1
+
+
+def mark_written(tensor):
+    """Records an in-place write into ``tensor``'s storage (its buffer's
+    version), so copies derived from it (``kmajor_weight``) are rebuilt."""
+    buf = tensor.buffer
+    if buf is not None and hasattr(buf, "version"):
+        buf.version += 1
 
 
 def permute(tensor1, *axes):

@@ -150,14 +150,6 @@ def generate(model, prompt, max_new_tokens=64, temperature=1.0, top_k=None, stop
         _prefill(model, state, seq, temperature, k)
         made = 1
         if made < n_new and not stopped(made):
-            # the stacked QKV weights are built once for the decode steps
-            for block in model.blocks:
-                from .module import kmajor_weight
-
-                a = block.attn
-                if a.q.bias is None and a.k.bias is None and a.v.bias is None:
-                    kmajor_weight(a, "_qkv_t", [a.q, a.k, a.v],
-                                  round_tf32=functional.get_matmul_mode() == "tf32")
             while made < n_new:
                 before_step()
                 if graph is None and use_graph and n_new - made >= 3:

@@ -8,6 +8,7 @@ from ..backend import context
 from ..functional.utils import from_numpy
 from .module import (
     GELU,
+    kmajor_weight,
     Dropout,
     Embedding,
     LayerNorm,
@@ -41,8 +42,9 @@ class GPT2Block(Module):
                                   kv_cache=kv_cache)
             fc1, act, fc2 = self.mlp._modules.values()
             if isinstance(fc1, Linear) and isinstance(act, GELU) and isinstance(fc2, Linear):
-                u = functional.linear(self.ln2.forward_into_gemm(h), fc1.weight, fc1.bias,
-                                      activation="gelu", feeds_tf32=context.MODE != 0)
+                if context.MODE != 0:
+                    return self._mlp_inference(h)
+                u = functional.linear(self.ln2(h), fc1.weight, fc1.bias, activation="gelu")
                 return functional.linear(u, fc2.weight, fc2.bias, residual=h)
             return h + self.mlp(self.ln2(h))
         if kv_cache is not None:
@@ -51,6 +53,17 @@ class GPT2Block(Module):
         x = x + self.drop(self.mlp(self.ln2(x)))
         return x
 
+    def _mlp_inference(self, h):
+        """h + FC2(GELU(FC1(LN2(h)))) over cached K-major (TF32-rounded in tf32
+        mode) weight copies, GELU and the residual in the GEMM epilogues."""
+        fc1, _, fc2 = self.mlp._modules.values()
+        rnd = functional.get_matmul_mode() == "tf32"
+        u = functional.linear(self.ln2.forward_into_gemm(h),
+                              kmajor_weight(self, "_fc1_t", [fc1], rnd), fc1.bias,
+                              activation="gelu", feeds_tf32=True, transpose_weight=True)
+        return functional.linear(u, kmajor_weight(self, "_fc2_t", [fc2], rnd), fc2.bias,
+                                 residual=h, transpose_weight=True)
+
     def decode(self, x, kv_cache, cur_len, max_len):
         """The block for one new position per sequence, ``x`` (batch, d_model)
         (inference mode; see ``MultiHeadAttention.decode``)."""
@@ -58,9 +71,7 @@ class GPT2Block(Module):
                              residual=x)
         fc1, act, fc2 = self.mlp._modules.values()
         if isinstance(fc1, Linear) and isinstance(act, GELU) and isinstance(fc2, Linear):
-            u = functional.linear(self.ln2.forward_into_gemm(h), fc1.weight, fc1.bias,
-                                  activation="gelu", feeds_tf32=True)
-            return functional.linear(u, fc2.weight, fc2.bias, residual=h)
+            return self._mlp_inference(h)
         return h + self.mlp(self.ln2(h))
 
 

@@ -356,26 +356,59 @@ class AdaptiveAvgPool2d(Module):
         return autograd.adaptive_avgpooling2d(x).forward(x, self.output_size)
 
 
+def _source_key(tensors, *extra):
+    """Identity of the data in ``tensors``: buffer uid, its write version and
+    the view geometry (an in-place write through ``functional.assign`` bumps
+    the version)."""
+    return tuple((t.buffer.uid, t.buffer.version, t.offset, tuple(t.shape), tuple(t.stride))
+                 for t in tensors) + extra
+
+
 def kmajor_weight(owner, name, linears, round_tf32=False):
     """The weights of ``linears`` (each nn.Linear's (K, N_i)) transposed and
     stacked into one (sum N_i, K) buffer owned by ``owner`` -- the K-major
     operand the tensor-core GEMM reads fastest (``linear(...,
-    transpose_weight=True)``).  The copy is refreshed from the parameters on
-    every call, so it never goes stale; weights of one shape are transposed
-    by a single launch (``functional.transpose_stack``)."""
+    transpose_weight=True)``), optionally rounded to the nearest TF32 value.
+
+    The copy is made by one launch (``functional.transpose_stack``) and kept:
+    it is rebuilt only when a source weight was written since (the buffers'
+    write versions) or replaced.  A CUDA graph recorded over a forward that
+    reads this copy keeps reading it: after changing weights, record again."""
     K = linears[0].weight.shape[0]
     ns = [lin.weight.shape[1] for lin in linears]
     total = sum(ns)
-    buf = owner.__dict__.get(name)
-    if buf is None or tuple(buf.shape) != (total, K):
+    key = _source_key([lin.weight for lin in linears], bool(round_tf32))
+    entry = owner.__dict__.get(name)
+    if entry is not None and entry[1] == key:
+        return entry[0]
+    buf = entry[0] if entry is not None and tuple(entry[0].shape) == (total, K) else None
+    if buf is None:
         buf = Tensor((total, K), value=0.0)
-        object.__setattr__(owner, name, buf)
-    if functional.transpose_stack(buf, [lin.weight for lin in linears], round_tf32=round_tf32):
-        return buf
-    row = 0
-    for lin, n in zip(linears, ns):
-        functional.assign(buf.narrow(0, row, n), lin.weight.transpose(0, 1))
-        row += n
+    if not functional.transpose_stack(buf, [lin.weight for lin in linears],
+                                      round_tf32=round_tf32):
+        row = 0
+        for lin, n in zip(linears, ns):
+            functional.assign(buf.narrow(0, row, n), lin.weight.transpose(0, 1))
+            row += n
+        key = key[:-1] + (False,)   # the fallback copy is not rounded
+    object.__setattr__(owner, name, (buf, key))
+    return buf
+
+
+def tf32_weight(owner, name, weight):
+    """A copy of ``weight`` rounded to the nearest TF32 value, kept and
+    rebuilt like ``kmajor_weight``'s (for a weight whose own buffer must stay
+    exact, e.g. the embedding that the tied LM head also reads)."""
+    from ..backend.lib import F as _F, check as _check
+
+    key = _source_key([weight])
+    entry = owner.__dict__.get(name)
+    if entry is not None and entry[1] == key:
+        return entry[0]
+    src = functional.contiguous(weight)
+    buf = Tensor._empty(list(weight.shape), "f32")
+    _check(_F.wxx_round_tf32(buf.buffer.ptr, src.ptr, int(np.prod(weight.shape))), "round_tf32")
+    object.__setattr__(owner, name, (buf, key))
     return buf
 
 
@@ -437,6 +470,11 @@ class MultiHeadAttention(Module):
                                      mask=None if causal else mask, causal=causal,
                                      scale=1.0 / math.sqrt(self.head_dim),
                                      feeds_tf32=context.MODE != 0)
+            if context.MODE != 0:
+                rnd = functional.get_matmul_mode() == "tf32"
+                return functional.linear(o, kmajor_weight(self, "_out_t", [self.out], rnd),
+                                         self.out.bias, residual=residual,
+                                         transpose_weight=True)
             if residual is not None:
                 return functional.linear(o, self.out.weight, self.out.bias, residual=residual)
             return self.out(o)
@@ -479,10 +517,8 @@ class MultiHeadAttention(Module):
 
         B, D = x.shape
         if self.q.bias is None and self.k.bias is None and self.v.bias is None:
-            w = self.__dict__.get("_qkv_t")
-            if w is None:
-                w = kmajor_weight(self, "_qkv_t", [self.q, self.k, self.v],
-                                  round_tf32=functional.get_matmul_mode() == "tf32")
+            w = kmajor_weight(self, "_qkv_t", [self.q, self.k, self.v],
+                              round_tf32=functional.get_matmul_mode() == "tf32")
             qkv = functional.linear(x, w, transpose_weight=True)
             qp, kp, vp, ld = qkv.ptr, qkv.ptr + 4 * D, qkv.ptr + 8 * D, 3 * D
             keep = (qkv,)
@@ -498,9 +534,9 @@ class MultiHeadAttention(Module):
                                        int(functional.get_matmul_mode() == "tf32")),
                "decode_attention")
         del keep
-        if residual is not None:
-            return functional.linear(o, self.out.weight, self.out.bias, residual=residual)
-        return self.out(o)
+        rnd = functional.get_matmul_mode() == "tf32"
+        return functional.linear(o, kmajor_weight(self, "_out_t", [self.out], rnd), self.out.bias,
+                                 residual=residual, transpose_weight=True)
 
 
 class Attention(Module):
@@ -557,20 +593,24 @@ class SwiGLU(Module):
         W3 with the residual add in its epilogue.  The hidden width is rounded
         up to a multiple of 4 so every operand row is 16-byte aligned: the
         extra columns hold zero weights (silu(0) * 0 = 0) and meet zero rows of
-        W3.  The weights are copied each call into buffers owned by the
-        module."""
+        W3.  The weights are copied into buffers owned by the module, and
+        copied again only when a source weight was written since (buffer
+        write versions, as for ``kmajor_weight``)."""
         h = self.hidden_dim
         hp = (h + 3) // 4 * 4
         d_in = self.w1.weight.shape[0]
         d_out = self.w3.weight.shape[1]
+        key = _source_key([self.w1.weight, self.w2.weight, self.w3.weight])
         cache = self.__dict__.get("_glu_cache")
         if cache is None or cache[0] != hp:
-            cache = (hp, Tensor((d_in, 2 * hp), value=0.0), Tensor((hp, d_out), value=0.0))
-            object.__setattr__(self, "_glu_cache", cache)
-        _, w12, w3p = cache
-        functional.assign(w12[:, 0:2 * h:2], self.w1.weight)
-        functional.assign(w12[:, 1:2 * h:2], self.w2.weight)
-        functional.assign(w3p.narrow(0, 0, h), self.w3.weight)
+            cache = (hp, Tensor((d_in, 2 * hp), value=0.0), Tensor((hp, d_out), value=0.0), None)
+        hp_, w12, w3p, done = cache
+        if done != key:
+            functional.assign(w12[:, 0:2 * h:2], self.w1.weight)
+            functional.assign(w12[:, 1:2 * h:2], self.w2.weight)
+            functional.assign(w3p.narrow(0, 0, h), self.w3.weight)
+            cache = (hp_, w12, w3p, key)
+        object.__setattr__(self, "_glu_cache", cache)
         g = functional.linear(x, w12, activation="swiglu", feeds_tf32=context.MODE != 0)
         return functional.linear(g, w3p, residual=residual)
 
@@ -584,6 +624,9 @@ class TiedLinear(Module):
 
     def forward(self, x):
         w = self._embedding.weight
+        if context.MODE != 0 and functional.get_matmul_mode() == "tf32":
+            # the product reads a TF32-rounded copy (the lookup keeps the table)
+            w = tf32_weight(self, "_w_tf32", w)
         return autograd.matmul(x, w).forward(x, w, False, True)
 
 

@@ -114,17 +114,24 @@ class ResNet18(Module):
 
     def _pack_nhwc_weights(self, blocks):
         """Every channels-last convolution's weight reordered to its K order
-        by one launch per call, into buffers owned by this module (refreshed
-        each call, so they follow the parameters); None if they do not fit
-        one launch."""
+        by one launch, into buffers owned by this module; repacked only when a
+        weight was written since (buffer write versions).  None if they do
+        not fit one launch."""
+        from .module import _source_key
+
         convs = [c for blk in blocks for c in blk.nhwc_convs()]
-        bufs = self.__dict__.get("_nhwc_packed")
+        entry = self.__dict__.get("_nhwc_packed")
         shapes = [(c.W.shape[0], c.W.shape[2], c.W.shape[3], c.W.shape[1]) for c in convs]
-        if bufs is None or [tuple(b.shape) for b in bufs] != shapes:
-            bufs = [Tensor(sh, value=0.0) for sh in shapes]
-            object.__setattr__(self, "_nhwc_packed", bufs)
-        if not functional.conv_weight_pack([c.W for c in convs], bufs):
-            return None
+        key = _source_key([c.W for c in convs])
+        if entry is None or [tuple(b.shape) for b in entry[0]] != shapes:
+            entry = ([Tensor(sh, value=0.0) for sh in shapes], None)
+        bufs, done = entry
+        if done != key:
+            if not functional.conv_weight_pack([c.W for c in convs], bufs):
+                object.__setattr__(self, "_nhwc_packed", (bufs, None))
+                return None
+            entry = (bufs, key)
+        object.__setattr__(self, "_nhwc_packed", entry)
         return {id(c): b for c, b in zip(convs, bufs)}
 
     def forward(self, x):
