@@ -28,7 +28,6 @@ The host reads the ids back once at the end, or one column per step when a
 
 import numpy as np
 
-from .. import functional
 from ..Tensor import Tensor
 from ..backend import context
 from ..backend import device as _dev
