@@ -812,6 +812,14 @@ __device__ __forceinline__ void p_dft(CP (&v)[R]) {
 // of the plans below (groups of 8 pairs, 256 or 512 elements apart in the
 // radix-16 and radix-32 passes) fall on 32 distinct banks.
 __device__ __forceinline__ int pad3(int i) { return i + ((i >> 5) << 1) + ((i >> 9) << 4); }
+// pad3 for compile-time arguments.  Address identities used by the passes
+// (all sizes powers of two):
+//   pad3(j + r*NB) = pad3(j) + pad3c(r*NB)   for j < NB, NB >= 32;
+//   pad3(X + Y)    = pad3(X) + pad3(Y)       for X a multiple of 512;
+//   pad3(k + r*NS) = k + pad3c(r*NS)         for k < NS <= 16;
+//   pad3(b + r)    = pad3(b) + r             for b a multiple of 2R', r < R' <= 32, r + b % 32 < 32;
+// so a thread computes one base per pass and every access adds a constant.
+__host__ __device__ constexpr int pad3c(int i) { return i + ((i >> 5) << 1) + ((i >> 9) << 4); }
 __host__ __device__ constexpr int padded3(int n) { return n + n / 16 + n / 32 + 32; }
 __device__ __forceinline__ u64 lds2(const float* p) { return *reinterpret_cast<const u64*>(p); }
 __device__ __forceinline__ void sts2(float* p, u64 v) { *reinterpret_cast<u64*>(p) = v; }
@@ -982,12 +990,15 @@ __device__ __forceinline__ void pp_first(PBuf dst, const float* x, int64_t st, i
         v[r].im = p_make(xv.y, xv.w);
       }
       p_dft<R>(v);
+      // j even: j R and (j + 1) R are multiples of R with room for r < R
+      // inside their 32-slot group, so pad3(base + r) = pad3(base) + r.
+      const int b0 = pad3(j * R), b1 = pad3((j + 1) * R);
 #pragma unroll
       for (int r = 0; r < R; r += 2) {
-        sts2(dst.re + pad3(j * R + r), p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
-        sts2(dst.im + pad3(j * R + r), p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
-        sts2(dst.re + pad3((j + 1) * R + r), p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
-        sts2(dst.im + pad3((j + 1) * R + r), p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
+        sts2(dst.re + b0 + r, p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
+        sts2(dst.im + b0 + r, p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
+        sts2(dst.re + b1 + r, p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
+        sts2(dst.im + b1 + r, p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
       }
     }
   }
@@ -1000,10 +1011,19 @@ template <int N, int R, int NS>
 __device__ __forceinline__ void pp_load_dft(CP (&v)[R], PBuf src, int j,
                                             const float* __restrict__ tw) {
   constexpr int NB = N / R;
+  if constexpr (NB >= 32) {
+    const int jb = pad3(j);
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    v[r].re = lds2(src.re + pad3(j + r * NB));
-    v[r].im = lds2(src.im + pad3(j + r * NB));
+    for (int r = 0; r < R; ++r) {
+      v[r].re = lds2(src.re + jb + pad3c(r * NB));
+      v[r].im = lds2(src.im + jb + pad3c(r * NB));
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      v[r].re = lds2(src.re + pad3(j + r * NB));
+      v[r].im = lds2(src.im + pad3(j + r * NB));
+    }
   }
   const int k = j & (NS - 1);
 #pragma unroll
@@ -1016,10 +1036,20 @@ template <int N, int R, int NS>
 __device__ __forceinline__ void pp_store(const CP (&v)[R], PBuf dst, int j) {
   const int k = j & (NS - 1);
   const int d = (j - k) * R + k;
+  if constexpr (NS * R >= 512 && (NS >= 32 || NS <= 16)) {
+    // d = X + k with X a multiple of NS R (>= 512) and k < NS
+    const int base = pad3(d - k) + (NS >= 32 ? pad3(k) : k);
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    sts2(dst.re + pad3(d + r * NS), v[r].re);
-    sts2(dst.im + pad3(d + r * NS), v[r].im);
+    for (int r = 0; r < R; ++r) {
+      sts2(dst.re + base + pad3c(r * NS), v[r].re);
+      sts2(dst.im + base + pad3c(r * NS), v[r].im);
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      sts2(dst.re + pad3(d + r * NS), v[r].re);
+      sts2(dst.im + pad3(d + r * NS), v[r].im);
+    }
   }
 }
 
@@ -1146,12 +1176,14 @@ __device__ __forceinline__ float2 pp_bin_dc(int N, float2 z0, const RowArgs& a, 
 
 template <int N, int R>
 __device__ __forceinline__ void pp_store_transposed(const CP (&v)[R], PBuf dst, int j0, int j1) {
+  // j R is a multiple of R <= 16 and r < R stays inside its 32-slot group
+  const int b0 = pad3(j0 * R), b1 = pad3(j1 * R);
 #pragma unroll
   for (int r = 0; r < R; r += 2) {
-    sts2(dst.re + pad3(j0 * R + r), p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
-    sts2(dst.im + pad3(j0 * R + r), p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
-    sts2(dst.re + pad3(j1 * R + r), p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
-    sts2(dst.im + pad3(j1 * R + r), p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
+    sts2(dst.re + b0 + r, p_make(p_lo(v[r].re), p_lo(v[r + 1].re)));
+    sts2(dst.im + b0 + r, p_make(p_lo(v[r].im), p_lo(v[r + 1].im)));
+    sts2(dst.re + b1 + r, p_make(p_hi(v[r].re), p_hi(v[r + 1].re)));
+    sts2(dst.im + b1 + r, p_make(p_hi(v[r].im), p_hi(v[r + 1].im)));
   }
 }
 
@@ -1234,10 +1266,19 @@ __device__ __forceinline__ void pp_mirror(PBuf src, PBuf dst, const float2* __re
       const float2 ua = __ldg(utw + j0), ub = __ldg(utw + j1);
       const CP u{p_make(ua.x, ub.x), p_make(ua.y, ub.y)};
       if (MODE != kModeIrfft) {
+        if constexpr (NB >= 32) {
+          const int b0 = pad3(j0), b1 = pad3(j1);   // j0, j1 < NB: base + constant
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          w[r].re = p_make(src.re[pad3(j0 + r * NB)], src.re[pad3(j1 + r * NB)]);
-          w[r].im = p_make(src.im[pad3(j0 + r * NB)], src.im[pad3(j1 + r * NB)]);
+          for (int r = 0; r < R; ++r) {
+            w[r].re = p_make(src.re[b0 + pad3c(r * NB)], src.re[b1 + pad3c(r * NB)]);
+            w[r].im = p_make(src.im[b0 + pad3c(r * NB)], src.im[b1 + pad3c(r * NB)]);
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            w[r].re = p_make(src.re[pad3(j0 + r * NB)], src.re[pad3(j1 + r * NB)]);
+            w[r].im = p_make(src.im[pad3(j0 + r * NB)], src.im[pad3(j1 + r * NB)]);
+          }
         }
         const float2 a1 = __ldg(utw + 2 * j0), b1 = __ldg(utw + 2 * j1);
         const float2 a4 = __ldg(utw + 8 * j0), b4 = __ldg(utw + 8 * j1);
@@ -1564,11 +1605,12 @@ __device__ __forceinline__ void pp_split32(PBuf buf, const float* __restrict__ t
   const int j = (threadIdx.x >> 1) * 2;
   const int k = j & (NS - 1);
   CP v[16];
+  // j + h NB < 512 and 2 m NB is a multiple of 512: base + constant
+  const int lb = pad3(j + h * NB);
 #pragma unroll
   for (int m = 0; m < 16; ++m) {
-    const int r = 2 * m + h;
-    v[m].re = lds2(buf.re + pad3(j + r * NB));
-    v[m].im = lds2(buf.im + pad3(j + r * NB));
+    v[m].re = lds2(buf.re + lb + pad3c(2 * m * NB));
+    v[m].im = lds2(buf.im + lb + pad3c(2 * m * NB));
   }
   {
     // m = 0: input r = h; r = 0 has no twiddle
@@ -1608,14 +1650,17 @@ __device__ __forceinline__ void pp_split32(PBuf buf, const float* __restrict__ t
     v[8 + i] = CP{p_sub(a.re, tr2), p_sub(a.im, ti2)};    // output 16 + 8h + i
   }
   __syncthreads();   // every input is read before any output is stored
-  const int d = (j - k) * R + k;
+  static_assert(NS == 16, "store offsets written for NS = 16");
+  // outputs r0 = 8h + i and r1 = 16 + 8h + i at (j - k) R + k + r NS: the
+  // (j - k) R part is a multiple of 512, and pad3(16 r) = 136 h + pad3c(16 i)
+  // (+ 256 for r1), so base + constant
+  const int sb = pad3((j - k) * R) + k + 136 * h;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int r0 = 8 * h + i, r1 = 16 + 8 * h + i;
-    sts2(buf.re + pad3(d + r0 * NS), v[i].re);
-    sts2(buf.im + pad3(d + r0 * NS), v[i].im);
-    sts2(buf.re + pad3(d + r1 * NS), v[8 + i].re);
-    sts2(buf.im + pad3(d + r1 * NS), v[8 + i].im);
+    sts2(buf.re + sb + pad3c(16 * i), v[i].re);
+    sts2(buf.im + sb + pad3c(16 * i), v[i].im);
+    sts2(buf.re + sb + pad3c(256 + 16 * i), v[8 + i].re);
+    sts2(buf.im + sb + pad3c(256 + 16 * i), v[8 + i].im);
   }
   __syncthreads();
 }
