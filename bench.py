@@ -609,9 +609,57 @@ def line_config(wl, world, args):
 
 # ------------------------------------------------------------------ reference arm
 
+def _reference_extra(args, world):
+    """The oracle's restatement of the reference's training step / sampling
+    loop on a bounded sample (one sequence), timed on the host."""
+    from oracle import init as oracle_init, models as oracle_models, train as oracle_train
+
+    rng = np.random.default_rng(7)
+    if args.workload == "gpt2_small_train":
+        V, D, H, L, S = 1024, 256, 8, 6, 256
+        sd = oracle_init.gpt2_state_dict(7, V, D, H, L, S)
+        ids = rng.integers(0, V, size=(1, S))
+        tgt = np.roll(ids, -1, axis=1)
+
+        def fn():
+            oracle_train.gpt2_loss_and_grads(sd, ids, tgt, H, L)
+
+        units, what = S, "1 x 256 tokens per step (float64 numpy forward + backward)"
+    else:
+        V, D, H, L, S = 50304, 1024, 16, 24, 1024
+        sd = oracle_init.gpt2_state_dict(7, V, D, H, L, S)
+        prompt = rng.integers(0, V, size=(1, 128))
+
+        def fn():
+            oracle_models.gpt2_generate(sd, prompt, H, L, 2, temperature=0.0)
+
+        units, what = 2, "1 prompt of 128 tokens, 2 new tokens per step (full forward per token)"
+    for _ in range(max(1, min(args.warmup, 1))):
+        fn()
+    t0 = time.perf_counter()
+    n = max(1, min(args.steps, 3))
+    for _ in range(n):
+        fn()
+    dt = (time.perf_counter() - t0) / n
+    value = units / dt
+    info = EXTRA[args.workload]
+    print(json.dumps({
+        "metric": info["metric"], "value": value, "unit": info["unit"], "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": dt * 1000, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64 (numpy)", "data": "synthetic",
+        "config": {"workload": args.workload}, "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": info["unit"], "cores": cpu_cores(),
+                         "kind": "port", "sample": what},
+        "e2e": {"value": value, "unit": info["unit"], "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
+    if args.workload in EXTRA:
+        return _reference_extra(args, world)
     if args.workload in SWEEPS:
         sw = SWEEPS[args.workload]
         arrays, frac = _sweep_cpu_sample(sw, np.random.default_rng(0))
@@ -937,13 +985,140 @@ def run_ours(args, rank, world, local):
     return 0
 
 
+# ------------------------------------------------------------------ training and generation
+
+EXTRA = {
+    # GPT2 config 0 trained: forward in training mode, CCELoss over the next
+    # token, backward, AdamW step.  FLOPs ~ 3x the forward's products.
+    "gpt2_small_train": {"metric": "GPT2 train tokens/s", "unit": "tokens/s"},
+    # GPT2-scaled generation: 8 prompts of 128 tokens, 128 new tokens each,
+    # greedy, K/V cache, one CUDA-graph replay per decode step.
+    "gpt2_scaled_generate": {"metric": "GPT2 generate tokens/s", "unit": "tokens/s"},
+}
+
+
+def run_extra(args, rank, world, local):
+    """Training step / generation throughput on one GPU (N > 1: replicas)."""
+    os.environ.setdefault("WXX_DEVICE", str(local))
+    import wxx_b200 as wxx
+    from wxx_b200.backend import device as dev
+    from wxx_b200 import distributed as wd
+
+    dist = wd.init_host_group() if world > 1 else None
+    F = wxx.functional
+    wxx.manual_seed(1234)
+    wxx.set_matmul_mode("tf32")
+    rng = np.random.default_rng(rank)
+    peaks, kind = load_peaks()
+    if args.workload == "gpt2_small_train":
+        V, D, H, L, S, B = 1024, 256, 8, 6, 256, 4
+        model = wxx.nn.GPT2(V, D, H, L, max_len=S, dropout=0.0)
+        opt = wxx.nn.AdamW(model.parameters(), lr=1e-4)
+        ids_h = rng.integers(0, V, size=(B, S), dtype=np.uint32)
+        tgt_h = np.roll(ids_h, -1, axis=1).reshape(-1)
+        loss_fn = wxx.nn.CCELoss()
+
+        def step():
+            # host batch in, loss value out: the call a training loop makes
+            i = F.from_numpy(ids_h, dtype=np.uint32)
+            t = F.from_numpy(tgt_h, dtype=np.uint32)
+            opt.zero_grad()
+            logits = model(i)
+            loss = loss_fn(logits.reshape((B * S, V)), t)
+            loss.backward()
+            opt.step()
+            return float(loss.numpy().reshape(-1)[0])
+
+        units, flops = B * S, 3 * 11.81e9
+        flush = L2Flush(F)
+    else:
+        V, D, H, L, S = 50304, 1024, 16, 24, 1024
+        B, P, N = 8, 128, 128
+        model = wxx.nn.GPT2(V, D, H, L, max_len=S)
+        prompt = rng.integers(0, V, size=(B, P), dtype=np.uint32)
+
+        def step():
+            return model.generate(prompt, max_new_tokens=N, temperature=0.0)
+
+        units, flops = B * N, None
+        flush = None
+
+    for _ in range(args.warmup):
+        step()
+    dev.synchronize()
+    if dist is not None:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    n0 = dev.launch_count()
+    total = 0.0
+    for _ in range(args.steps):
+        if flush is not None:
+            flush()
+        a, b = dev.Event(), dev.Event()
+        a.record()
+        out = step()
+        b.record()
+        dev.synchronize()
+        total += a.elapsed_ms(b)
+        del out
+    launches = dev.launch_count() - n0 - (args.steps * L2Flush.LAUNCHES if flush else 0)
+    clocks = sampler.stop()
+    ms = total / args.steps
+    if dist is not None:
+        import torch
+
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * units / (ms / 1000.0)
+    info = EXTRA[args.workload]
+    if flops is not None:
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]) / 2.0
+        ach = flops / (ms / 1000.0) / 1e12
+        roof = {"kernel": "whole step (forward + backward products, AdamW)", "bound": "tensor",
+                "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "traffic": None, "peak_basis": f"{kind} bf16 dense TFLOP/s / 2"}
+        e2e_h2d = ids_h.nbytes + tgt_h.nbytes
+        cfg = {"workload": "GPT2(1024,256,8,6) train step: fwd + CCELoss + bwd + AdamW, "
+                           "batch 4, seq 256", "parallelism": "replicas", "l2": L2_FLUSHED}
+    else:
+        # decode steps read every weight copy once per token step
+        weight_bytes = 4 * (L * 12 * D * D + V * D + S * D)
+        steps_per_call = N - 1
+        ach = weight_bytes * steps_per_call / (ms / 1000.0) / 1e9
+        peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        roof = {"kernel": "decode steps (weights streamed once per token step)", "bound": "hbm",
+                "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                "traffic": None, "peak_basis": f"{kind} HBM copy GB/s (prefill time included)"}
+        e2e_h2d = prompt.nbytes
+        cfg = {"workload": "GPT2(50304,1024,16,24) generate: 8 prompts x 128 tokens, 128 new "
+                           "tokens each, greedy, K/V cache", "parallelism": "replicas"}
+    line = {
+        "metric": info["metric"], "value": value, "unit": info["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (tf32 tensor-core products)",
+        "data": "synthetic", "config": cfg, "roofline": roof, "clocks": clocks,
+        "gpu_launches": int(launches),
+        "e2e": {"value": value, "unit": info["unit"], "h2d_bytes_per_step": int(e2e_h2d),
+                "d2h_bytes_per_step": 4 if flops is not None else B * (P + N) * 4,
+                "includes": "the public API call per step (host inputs, result read back)"},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(SWEEPS),
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(SWEEPS) + sorted(EXTRA),
                     default="gpt2_scaled")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -965,6 +1140,8 @@ def main(argv=None):
         return run_reference(args, rank, world)
     if args.workload in SWEEPS:
         return run_sweep(args, rank, world, local)
+    if args.workload in EXTRA:
+        return run_extra(args, rank, world, local)
     return run_ours(args, rank, world, local)
 
 

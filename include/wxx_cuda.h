@@ -344,6 +344,28 @@ int wxx_sample_tokens(uint32_t* ids, int64_t ids_ld, int* cur_len, unsigned* don
                       const float* logits, int64_t ld, int B, int V, float temperature, int top_k,
                       const double* draws, int max_len);
 
+/* ---------------------------------------------------------------- training
+ * Backward passes, loss and optimiser of GPT2 training (src/wxx/autograd/*.py backward
+ * methods); matmul / linear gradients use wxx_matmul, bias and affine gradients wxx_reduce. */
+/* gelubackwards.wgsl times grad_output: dx = dy * gelu'(x) (tanh form, +-10 clamps). */
+int wxx_gelu_backward(float* dx, const float* dy, const float* x, int64_t n);
+/* softmaxbackwards.wgsl over the last axis: dx = y * (dy - sum(dy * y)); rows of n <= 1024. */
+int wxx_softmax_backward(float* dx, const float* dy, const float* y, int64_t rows, int64_t n);
+/* meanvarnormdx / meanvarnormdg (autograd/normalization.py meanvarnorm.backward): dx from the
+ * saved mean and inv_std, and dyxhat = dy * xhat whose column sums are d gamma; n <= 1024. */
+int wxx_layernorm_backward(float* dx, float* dyxhat, const float* dy, const float* x,
+                           const float* mean, const float* inv, const float* gamma, int64_t rows,
+                           int64_t n);
+/* embeddx.wgsl (autograd/layers.py Embedding.backward): dW (vocab, D) = scatter-add of dY rows. */
+int wxx_embedding_backward(float* dW, const uint32_t* ids, const float* dY, int64_t n_tokens,
+                           int D, int vocab);
+/* functional/loss.py:20 cceloss (cceloss.wgsl): per-row loss and dZ = softmax - onehot. */
+int wxx_cceloss(float* loss, float* dZ, const float* Z, const uint32_t* targets, int64_t rows,
+                int K);
+/* nn/optimizer.py:38-84 AdamW.step / adamw.wgsl: one step over n parameters in place. */
+int wxx_adamw(float* p, const float* g, float* m, float* v, int64_t n, float lr, float beta1,
+              float beta2, float eps, float weight_decay, float bc1, float bc2);
+
 /* ---------------------------------------------------------------- NCCL
  * No reference counterpart (the reference drives one WebGPU device): the
  * all-gather of batch-sharded outputs across the GPUs of one node. */

@@ -161,3 +161,50 @@ def test_model_oracles_fast_vs_exact():
     a = models.gpt2_forward(sd, ids, 4, 2)
     b = models.gpt2_forward(sd, ids, 4, 2, fast=True)
     assert np.abs(a - b).max() < 1e-4
+
+
+def test_gpt2_training_oracle_matches_finite_differences():
+    """oracle.train's hand-written backward against central differences of its
+    own float64 loss on a tiny GPT2 (every parameter kind sampled)."""
+    from oracle import init, train
+
+    V, D, H, L, S = 16, 8, 2, 2, 5
+    sd = {k: v.astype(np.float64) for k, v in init.gpt2_state_dict(3, V, D, H, L, S).items()}
+    rng = np.random.default_rng(0)
+    for k in sd:   # non-trivial LayerNorm affine and biases
+        if k.endswith(("weightg", "weightb", "bias")):
+            sd[k] = sd[k] + 0.1 * rng.standard_normal(sd[k].shape)
+    ids = rng.integers(0, V, size=(2, S))
+    tgt = rng.integers(0, V, size=(2, S))
+    loss, grads = train.gpt2_loss_and_grads(sd, ids, tgt, H, L)
+    assert np.isfinite(loss)
+    keys = ["tok_emb.weight", "pos_emb.weight", "blocks.0.attn.q.weight", "blocks.1.attn.v.weight",
+            "blocks.0.attn.out.weight", "blocks.1.mlp.0.weight", "blocks.0.mlp.0.bias",
+            "blocks.1.mlp.2.weight", "blocks.0.mlp.2.bias", "blocks.0.ln1.weightg",
+            "blocks.1.ln2.weightb", "ln_f.weightg", "ln_f.weightb"]
+    eps = 1e-6
+    for key in keys:
+        flat = sd[key].reshape(-1)
+        for idx in rng.choice(flat.size, size=min(4, flat.size), replace=False):
+            old = flat[idx]
+            flat[idx] = old + eps
+            lp, _ = train.gpt2_loss_and_grads(sd, ids, tgt, H, L)
+            flat[idx] = old - eps
+            lm, _ = train.gpt2_loss_and_grads(sd, ids, tgt, H, L)
+            flat[idx] = old
+            fd = (lp - lm) / (2 * eps)
+            an = grads[key].reshape(-1)[idx]
+            assert abs(fd - an) <= 1e-6 + 1e-5 * abs(fd), (key, idx, fd, an)
+
+
+def test_adamw_oracle_first_step():
+    from oracle import train
+
+    p = np.array([1.0, -2.0, 0.5])
+    g = np.array([0.1, -0.2, 0.0])
+    z = np.zeros(3)
+    p1, m1, v1 = train.adamw_step(p, g, z, z, 1, 1e-2, 0.9, 0.999, 1e-7, 1e-4)
+    # at t = 1 the bias-corrected moments are g and g^2: the step is ~ sign(g)
+    step = np.where(g != 0, g / (np.abs(g) + 1e-7), 0.0)
+    assert np.allclose(p1, p - 1e-2 * (step + 1e-4 * p))
+    assert np.allclose(m1, 0.1 * g) and np.allclose(v1, 0.001 * g * g)

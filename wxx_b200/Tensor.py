@@ -251,19 +251,19 @@ class Tensor:
     def reshape(self, *shape):
         if len(shape) == 1 and isinstance(shape[0], (tuple, list)):
             shape = tuple(shape[0])
-        from . import functional
+        from . import autograd
 
-        return functional.reshape(self, tuple(shape))
+        return autograd.reshape(self).forward(self, tuple(shape))
 
     def view(self, *shape):
         return self.reshape(*shape)
 
     def permute(self, *axis):
-        from . import functional
+        from . import autograd
 
         if len(axis) == 1 and isinstance(axis[0], (tuple, list)):
             axis = tuple(axis[0])
-        return functional.permute(self, *axis)
+        return autograd.permute(self).forward(self, axis)
 
     def transpose(self, dim0, dim1):
         rank = len(self.shape)
@@ -279,9 +279,9 @@ class Tensor:
         return self.transpose(-1, -2)
 
     def contiguous(self):
-        from . import functional
+        from . import autograd
 
-        return functional.contiguous(self)
+        return autograd.contiguous(self).forward(self)
 
     def unsqueeze(self, dim):
         rank = len(self.shape)
@@ -326,11 +326,62 @@ class Tensor:
         self.grad = None
         return self
 
-    def backward(self):
-        raise NotImplementedError(
-            "wxx_b200 implements the inference (forward) path on B200; "
-            "backward passes are not part of this backend"
-        )
+    def backward(self, grad=None):
+        """Back-propagates from this tensor (the reference's Tensor.backward):
+        the recorded ops are visited in reverse topological order, each op's
+        ``backward`` turns its output gradient into its inputs' gradients,
+        gradients reaching one tensor along several paths are added, and
+        leaf tensors (parameters) receive theirs in ``.grad`` (added to an
+        existing ``.grad``).  The seed is ``grad`` or ones.  The graph is
+        released as it is consumed."""
+        from . import functional
+        from .backend.context import inferenceMode
+
+        if not self.requires_grad:
+            raise RuntimeError("cannot call backward on a tensor that does not require gradients")
+        seed = grad if grad is not None else Tensor(self.shape, value=1.0, dtype=self.type)
+        # reverse topological order of the tensors that need a gradient
+        order, seen = [], set()
+        stack = [(self, False)]
+        while stack:
+            t, done = stack.pop()
+            if done:
+                order.append(t)
+                continue
+            if id(t) in seen:
+                continue
+            seen.add(id(t))
+            stack.append((t, True))
+            fn = t.creator
+            if fn is not None and fn.inputs is not None:
+                for parent in fn.inputs:
+                    if isinstance(parent, Tensor) and parent.requires_grad and \
+                            id(parent) not in seen:
+                        stack.append((parent, False))
+        grads = {id(self): seed}
+        with inferenceMode():
+            for t in reversed(order):
+                g = grads.pop(id(t), None)
+                fn = t.creator
+                if fn is None:
+                    if g is not None:
+                        t.grad = g if t.grad is None else functional.pointwise(t.grad, g, 0)
+                    continue
+                if g is not None:
+                    parts = fn.backward(g)
+                    if not isinstance(parts, (tuple, list)):
+                        parts = (parts,)
+                    if len(parts) != len(fn.inputs):
+                        raise RuntimeError(f"{type(fn).__name__}.backward returned {len(parts)} "
+                                           f"gradients for {len(fn.inputs)} inputs")
+                    for parent, pg in zip(fn.inputs, parts):
+                        if pg is None or not isinstance(parent, Tensor) or \
+                                not parent.requires_grad:
+                            continue
+                        prev = grads.get(id(parent))
+                        grads[id(parent)] = pg if prev is None else functional.pointwise(prev, pg, 0)
+                fn.inputs = None
+                t.creator = None
 
     # ------------------------------------------------------------------ host access
     def numpy(self):
@@ -460,9 +511,9 @@ class Tensor:
         return functional.relu(self)
 
     def gelu(self):
-        from . import functional
+        from . import autograd
 
-        return functional.gelu(self)
+        return autograd.gelu(self).forward(self)
 
     def sin(self):
         from . import functional
@@ -490,9 +541,9 @@ class Tensor:
         return functional.selu(self)
 
     def softmax(self, dim=-1):
-        from . import functional
+        from . import autograd
 
-        return functional.softmax(self, dim)
+        return autograd.softmax(self).forward(self, dim)
 
     def square(self):
         from . import functional
@@ -535,14 +586,14 @@ class Tensor:
         return functional.clamp(self, min, max)
 
     def sum(self, axis=None, keepdims=False, *, keepdim=None):
-        from . import functional
+        from . import autograd
 
-        return functional.sum(self, axis, keepdims if keepdim is None else keepdim)
+        return autograd.sum(self).forward(self, axis, keepdims if keepdim is None else keepdim)
 
     def mean(self, axis=None, keepdims=False, *, keepdim=None):
-        from . import functional
+        from . import autograd
 
-        return functional.mean(self, axis, keepdims if keepdim is None else keepdim)
+        return autograd.mean(self).forward(self, axis, keepdims if keepdim is None else keepdim)
 
     def var(self, axis=None, keepdims=False, *, keepdim=None):
         from . import functional

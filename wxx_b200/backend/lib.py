@@ -129,6 +129,13 @@ SIGNATURES = {
                              c_int],
     "wxx_sample_tokens": [c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int,
                           c_float, c_int, c_void_p, c_int],
+    "wxx_gelu_backward": [c_void_p, c_void_p, c_void_p, c_i64],
+    "wxx_softmax_backward": [c_void_p, c_void_p, c_void_p, c_i64, c_i64],
+    "wxx_layernorm_backward": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_i64, c_i64],
+    "wxx_embedding_backward": [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int],
+    "wxx_cceloss": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_int],
+    "wxx_adamw": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64] + [c_float] * 7,
     "wxx_nccl_unique_id": [P_u8],
     "wxx_nccl_init": [P_u8, c_int, c_int],
     "wxx_nccl_allgather": [c_void_p, c_void_p, c_u64],

@@ -33,6 +33,7 @@ SOURCES = [
     "hyena_filter.cu",
     "attention.cu",
     "generate.cu",
+    "train.cu",
     "pool.cu",
     "nccl.cu",
 ]

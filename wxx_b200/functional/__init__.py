@@ -13,7 +13,6 @@ from .activations import (
     cos,
     cosback,
     gelu,
-    gelubackwards,
     masked_softmax,
     relu,
     relubackwards,
@@ -62,14 +61,12 @@ from .fft import (
     irfft,
     rfft,
 )
-from .layers import adamw, dropout, dropoutdx, embed, embeddx
+from .layers import dropout, dropoutdx, embed
 from .normalization import (
     batchnorm,
     batchnormdg,
     batchnormdx,
     meanvarnorm,
-    meanvarnormdg,
-    meanvarnormdx,
     rmsnorm,
     rmsnormdg,
     rmsnormdx,
@@ -126,8 +123,17 @@ from .utils import (
 )
 
 
-def cceloss(*args, **kwargs):
-    raise NotImplementedError("cceloss is a training kernel; not part of this backend")
+from .training import (  # noqa: E402
+    adamw,
+    cceloss,
+    embeddx,
+    gelu_backward,
+    gelubackwards,
+    layernorm_backward,
+    meanvarnormdx,
+    meanvarnormdg,
+    softmax_backward,
+)
 
 
 __all__ = [name for name in dir() if not name.startswith("__")]

@@ -54,7 +54,6 @@ def softmax(tensor1, dim):
 
 
 relubackwards = _training_only("relubackwards")
-gelubackwards = _training_only("gelubackwards")
 sigmoidbackwards = _training_only("sigmoidbackwards")
 selubackwards = _training_only("selubackwards")
 sinback = _training_only("sinback")

@@ -4,9 +4,7 @@ import random
 
 import numpy as np
 
-from .. import validation
 from ._common import F, check, dense, empty
-from .pointwise import _training_only
 
 
 def embed(tensor1, tensor2, n_token, embed_dim):
@@ -34,15 +32,20 @@ def dropout(tensor1, p, seed=None):
     x = dense(tensor1)
     if seed is None:
         seed = random.randint(0, 2**31 - 1)
+    return _apply_dropout_mask(x, p, seed), seed
+
+
+def _apply_dropout_mask(x, p, seed):
+    """x * keep / (1 - p) with keep drawn on the host from ``seed``."""
     keep = (np.random.default_rng(seed).random(tuple(x.shape)) >= p).astype(np.float32)
     from .utils import from_numpy
     from .pointwise import pointwise
 
     scale = 0.0 if p >= 1.0 else 1.0 / (1.0 - p)
-    return pointwise(pointwise(x, from_numpy(keep), 2), scale, 2), seed
+    return pointwise(pointwise(x, from_numpy(keep), 2), scale, 2)
 
 
-adamw = _training_only("adamw")
-dropoutdx = _training_only("dropoutdx")
-embeddx = _training_only("embeddx")
-_unused = (validation,)
+def dropoutdx(tensor1, p, seed):
+    """Gradient of ``dropout(x, p)`` drawn with ``seed`` (functional/layers.py:117):
+    the same mask and scale applied to the upstream gradient."""
+    return _apply_dropout_mask(dense(tensor1), p, seed)

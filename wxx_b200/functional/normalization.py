@@ -66,7 +66,5 @@ def batchnorm(tensor1, gamma, beta, running_mean, running_std, training=False):
 
 rmsnormdx = _training_only("rmsnormdx")
 rmsnormdg = _training_only("rmsnormdg")
-meanvarnormdx = _training_only("meanvarnormdx")
-meanvarnormdg = _training_only("meanvarnormdg")
 batchnormdx = _training_only("batchnormdx")
 batchnormdg = _training_only("batchnormdg")

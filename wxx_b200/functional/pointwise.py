@@ -67,6 +67,9 @@ def _pointwise(tensor1, tensor2, op):
         check(F.wxx_binary(tensor1.ptr, tensor1.ptr, 0, arr64(sa), tensor2.buffer.ptr,
                            tensor2.offset, arr64(sb), rank, arr64(out_shape), int(op)),
               "_pointwise")
+    buf = tensor1.buffer
+    if hasattr(buf, "version"):
+        buf.version += 1      # in-place write: cached weight copies are rebuilt
     return tensor1
 
 

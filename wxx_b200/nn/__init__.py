@@ -33,6 +33,8 @@ from .module import (
     RMSNorm,
     Sequential,
 )
+from .loss import CCELoss, MAELoss, loss
+from .optimizer import AdamW, Optimizer, SGD
 from .resnet import ResBlock, ResNet18
 
 __all__ = [
@@ -41,4 +43,5 @@ __all__ = [
     "HyenaBlock", "HyenaOperator", "ImplicitFilter", "LayerNorm", "Linear", "MaxPool1d",
     "MaxPool2d", "Module", "ModuleList", "MultiHeadAttention", "PositionalEncoding", "RMSNorm",
     "ResBlock", "ResNet18", "Sequential", "Sine", "SwiGLU", "TiedLinear",
+    "loss", "CCELoss", "MAELoss", "Optimizer", "SGD", "AdamW",
 ]

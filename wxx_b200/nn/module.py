@@ -18,128 +18,118 @@ from ..functional.utils import from_numpy, normal
 
 
 class Module:
+    """Base of every layer.  Attributes that are ``Parameter``s or ``Module``s
+    are registered (in assignment order) in ``_parameters`` / ``_modules``;
+    the dotted names of the parameter tree are the ``state_dict`` keys, the
+    same as the reference's (``blocks.0.attn.q.weight`` ...)."""
+
     def __init__(self):
         object.__setattr__(self, "_parameters", {})
         object.__setattr__(self, "_modules", {})
 
     def __setattr__(self, name, value):
+        registry = None
         if isinstance(value, Parameter):
-            self._parameters[name] = value
+            registry = self._parameters
         elif isinstance(value, Module):
-            self._modules[name] = value
+            registry = self._modules
         elif value is None and name in self._parameters:
-            self._parameters[name] = None
+            registry = self._parameters      # a parameter slot set to None stays listed
+        if registry is not None:
+            registry[name] = value
         object.__setattr__(self, name, value)
 
     def __call__(self, *x):
         return self.forward(*x)
 
-    def parameters(self, recurse=True):
-        """Yields ``("", parameter)`` pairs, as the reference does (module.py:39-47)."""
-        for p in self._parameters.values():
-            if p is not None:
-                yield ("", p)
-        if recurse:
-            for m in self._modules.values():
-                if m is not None:
-                    yield from m.parameters(recurse=True)
-
-    def named_parameters(self, prefix="", recurse=True):
-        for name, p in self._parameters.items():
-            if p is not None:
-                yield (prefix + name, p)
-        if recurse:
-            for name, m in self._modules.items():
-                if m is not None:
-                    yield from m.named_parameters(prefix + name + ".", recurse=True)
-
-    def state_dict(self, prefix="", destination=None):
-        """Parameter name -> host numpy array."""
-        if destination is None:
-            destination = {}
-        for name, p in self._parameters.items():
-            if p is not None:
-                destination[prefix + name] = np.asarray(p.numpy()).copy()
-        for name, m in self._modules.items():
-            if m is not None:
-                m.state_dict(prefix + name + ".", destination)
-        return destination
-
-    def _state_keys(self, prefix=""):
-        keys = [prefix + n for n, p in self._parameters.items() if p is not None]
-        for name, m in self._modules.items():
-            if m is not None:
-                keys.extend(m._state_keys(prefix + name + "."))
-        return keys
-
-    def load_state_dict(self, state_dict, strict=True):
-        """Uploads arrays (or tensors) into the parameters in place."""
-        own = set(self._state_keys())
-        for name, p in self.named_parameters():
-            if name in state_dict:
-                val = state_dict[name]
-                if isinstance(val, Tensor):
-                    src = val
-                else:
-                    arr = np.asarray(val)
-                    if p.type == "c64":
-                        src = functional.from_numpy_complex(arr)
-                    elif p.type == "u32":
-                        src = from_numpy(arr, dtype=np.uint32)
-                    else:
-                        src = from_numpy(arr)
-                if tuple(src.shape) != tuple(p.shape):
-                    raise ValueError(
-                        f"state_dict[{name!r}] has shape {tuple(src.shape)}, "
-                        f"parameter has {tuple(p.shape)}"
-                    )
-                functional.assign(p, src)
-            elif strict:
-                raise KeyError(f"Missing key in state_dict: {name}")
-        if strict:
-            missing = own - set(state_dict.keys())
-            unexpected = set(state_dict.keys()) - own
-            if missing:
-                raise RuntimeError(f"Missing keys: {sorted(missing)}")
-            if unexpected:
-                raise RuntimeError(f"Unexpected keys: {sorted(unexpected)}")
-
-    def zero_grad(self, wait=False):
-        for _, p in self.named_parameters():
-            p.grad = None
-        get_cmd_buffer().flush(wait=wait)
-
     def forward(self, *args, **kwargs):
         raise NotImplementedError
 
+    # -------------------------------------------------------- the parameter tree
+    def _walk(self, prefix="", recurse=True):
+        """(dotted name, parameter) for every non-None parameter: this
+        module's own first, then each child's subtree, in registration order."""
+        own = ((prefix + n, p) for n, p in self._parameters.items() if p is not None)
+        yield from own
+        if not recurse:
+            return
+        for child_name, child in self._modules.items():
+            if child is not None:
+                yield from child._walk(f"{prefix}{child_name}.", True)
+
+    def parameters(self, recurse=True):
+        """Yields ``("", parameter)`` pairs -- the pair shape the reference's
+        optimisers consume (module.py:39-47)."""
+        return (("", p) for _, p in self._walk("", recurse))
+
+    def named_parameters(self, prefix="", recurse=True):
+        return self._walk(prefix, recurse)
+
+    def _state_keys(self, prefix=""):
+        return [name for name, _ in self._walk(prefix)]
+
+    def state_dict(self, prefix="", destination=None):
+        """Parameter name -> host numpy array (a copy)."""
+        out = {} if destination is None else destination
+        out.update((name, np.array(p.numpy(), copy=True)) for name, p in self._walk(prefix))
+        return out
+
+    def load_state_dict(self, state_dict, strict=True):
+        """Uploads arrays (or tensors) into the parameters in place.  With
+        ``strict`` every parameter must be given and nothing else."""
+        uploaders = {"c64": functional.from_numpy_complex,
+                     "u32": lambda a: from_numpy(a, dtype=np.uint32)}
+        for name, p in self._walk():
+            if name not in state_dict:
+                if strict:
+                    raise KeyError(f"Missing key in state_dict: {name}")
+                continue
+            src = state_dict[name]
+            if not isinstance(src, Tensor):
+                src = uploaders.get(p.type, from_numpy)(np.asarray(src))
+            if tuple(src.shape) != tuple(p.shape):
+                raise ValueError(f"state_dict[{name!r}] has shape {tuple(src.shape)}, "
+                                 f"parameter has {tuple(p.shape)}")
+            functional.assign(p, src)
+        if strict:
+            own, given = set(self._state_keys()), set(state_dict)
+            if own - given:
+                raise RuntimeError(f"Missing keys: {sorted(own - given)}")
+            if given - own:
+                raise RuntimeError(f"Unexpected keys: {sorted(given - own)}")
+
+    def zero_grad(self, wait=False):
+        for _, p in self._walk():
+            p.grad = None
+        get_cmd_buffer().flush(wait=wait)
+
     def __repr__(self):
-        lines = [self.__class__.__name__ + "("]
-        for name, m in self._modules.items():
-            lines.append(f"  ({name}): {repr(m)}")
-        lines.append(")")
-        return "\n".join(lines)
+        children = [f"({n}): {c!r}".replace("\n", "\n  ") for n, c in self._modules.items()]
+        body = "".join(f"\n  {c}" for c in children)
+        return f"{type(self).__name__}({body}\n)"
 
 
-class ModuleList(Module):
-    def __init__(self, modules=None):
+class _Chain(Module):
+    """Children registered under "0", "1", ... and applied in that order."""
+
+    def __init__(self, modules=()):
         super().__init__()
-        if modules is not None:
-            for i, m in enumerate(modules):
-                setattr(self, str(i), m)
+        for m in modules:
+            self.append(m)
 
-    def __getitem__(self, idx):
-        if isinstance(idx, slice):
-            return [self._modules[str(i)] for i in range(*idx.indices(len(self)))]
-        return self._modules[str(idx)]
-
-    def __iter__(self):
-        return iter(self._modules.values())
+    def append(self, module):
+        setattr(self, str(len(self._modules)), module)
+        return self
 
     def __len__(self):
         return len(self._modules)
 
-    def append(self, module):
-        setattr(self, str(len(self._modules)), module)
+    def __iter__(self):
+        return iter(list(self._modules.values()))
+
+    def __getitem__(self, idx):
+        items = list(self._modules.values())
+        return items[idx]
 
     def forward(self, x, *args, **kwargs):
         for m in self._modules.values():
@@ -147,16 +137,14 @@ class ModuleList(Module):
         return x
 
 
-class Sequential(Module):
+class ModuleList(_Chain):
+    def __init__(self, modules=None):
+        super().__init__(() if modules is None else modules)
+
+
+class Sequential(_Chain):
     def __init__(self, *modules):
-        super().__init__()
-        for i, m in enumerate(modules):
-            setattr(self, str(i), m)
-
-    def forward(self, x, *args, **kwargs):
-        for m in self._modules.values():
-            x = m(x, *args, **kwargs)
-        return x
+        super().__init__(modules)
 
 
 class Linear(Module):
@@ -447,8 +435,8 @@ class MultiHeadAttention(Module):
         keys and values of positions 0..seq-1 are copied into them (the
         prefill of generation, see ``decode``)."""
         b, seq, _ = x.shape
-        fused_ok = context.MODE != 0 or self.drop.p == 0
-        if fused_ok and functional.attention_supported(x, self.n_heads, mask):
+        # the fused kernels record no graph: inference only
+        if context.MODE != 0 and functional.attention_supported(x, self.n_heads, mask):
             causal = bool(getattr(mask, "_wxx_causal", False))
             if context.MODE != 0 and self.q.bias is None and self.k.bias is None \
                     and self.v.bias is None:
@@ -483,9 +471,19 @@ class MultiHeadAttention(Module):
         self._fill_cache(kv_cache, kx, vx, seq)
         k = self._heads(kx, b, seq)
         v = self._heads(vx, b, seq)
-        score = functional.matmul_add(q, k, None, transpose_B=True,
-                                      alpha=1.0 / math.sqrt(self.head_dim))
-        attn = functional.masked_softmax(score, mask) if mask is not None else score.softmax(-1)
+        if context.MODE != 0:
+            # scale in the QK^T epilogue, mask inside the softmax pass
+            score = functional.matmul_add(q, k, None, transpose_B=True,
+                                          alpha=1.0 / math.sqrt(self.head_dim))
+            attn = (functional.masked_softmax(score, mask) if mask is not None
+                    else score.softmax(-1))
+        else:
+            # training: every step recorded for the backward pass
+            score = autograd.matmul(q, k).forward(q, k, False, True)
+            score = score * (1.0 / math.sqrt(self.head_dim))
+            if mask is not None:
+                score = score + mask
+            attn = score.softmax(-1)
         attn = self.drop(attn)
         out = autograd.matmul(attn, v).forward(attn, v)
         out = (

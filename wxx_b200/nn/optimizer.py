@@ -1,0 +1,65 @@
+"""Optimisers (interface: src/wxx/nn/optimizer.py): built from
+``module.parameters()`` (``("", parameter)`` pairs) and stepping the
+parameters in place from their ``.grad``."""
+
+from .. import functional
+from ..Tensor import Tensor
+
+
+class Optimizer:
+    def __init__(self, parameters):
+        self.parameters = list(parameters)
+
+    def step(self):
+        raise NotImplementedError
+
+    def zero_grad(self, wait=False):
+        for _, w in self.parameters:
+            w.grad = None
+        if wait:
+            from ..backend import device
+
+            device.synchronize()
+
+
+class SGD(Optimizer):
+    """``w -= lr * grad`` in place."""
+
+    def __init__(self, parameters, lr=0.01):
+        super().__init__(parameters)
+        self.lr = float(lr)
+
+    def step(self):
+        for _, w in self.parameters:
+            if w.grad is not None:
+                functional._pointwise(w, functional.scalarpointwise(w.grad, -self.lr, 2), 0)
+
+
+class AdamW(Optimizer):
+    """Adam with decoupled weight decay, one ``wxx_adamw`` launch per
+    parameter: ``m = b1 m + (1 - b1) g``, ``v = b2 v + (1 - b2) g^2``,
+    ``w -= lr (m / bc1 / (sqrt(v / bc2) + eps) + weight_decay w)`` with the bias
+    corrections bc = 1 - beta^t (nn/optimizer.py:38-84, adamw.wgsl)."""
+
+    def __init__(self, parameters, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-7,
+                 weight_decay=1e-4):
+        super().__init__(parameters)
+        self.params = self.parameters
+        self.lr = float(lr)
+        self.beta1, self.beta2 = float(beta1), float(beta2)
+        self.eps = float(eps)
+        self.weight_decay = float(weight_decay)
+        self.step_count = 0
+        self.state = [{"exp_avg": Tensor(p.shape, value=0.0),
+                       "exp_avg_sq": Tensor(p.shape, value=0.0)} for _, p in self.params]
+
+    def step(self):
+        self.step_count += 1
+        bc1 = 1.0 - self.beta1 ** self.step_count
+        bc2 = 1.0 - self.beta2 ** self.step_count
+        for (_, w), st in zip(self.params, self.state):
+            if w.grad is None:
+                continue
+            functional.adamw(w, functional.contiguous(w.grad), st["exp_avg"], st["exp_avg_sq"],
+                             self.step_count, self.lr, self.beta1, self.beta2, self.eps,
+                             self.weight_decay, bc1, bc2)
