@@ -947,6 +947,32 @@ def run_ours(args, rank, world, local):
         "gemm_launches_per_step": ks["launches"],
     }
 
+    # The same step with every product in 3xTF32 (the fp32-faithful mode the
+    # parity tests hold to 1e-5 of the oracle), N = 1: what exactness costs.
+    faithful = None
+    if world == 1 and not idle and not args.no_faithful:
+        wxx.set_matmul_mode("3xtf32")
+        g3 = None
+        try:
+            if graphs:
+                g3 = wxx.graph.capture(forward, x_dev)
+                fn3 = g3.replay
+            else:
+                def fn3():
+                    return forward(x_dev)
+            for _ in range(2):
+                fn3()
+            barrier()
+            n3 = max(3, min(args.steps, 10))
+            ms3 = timed_steps(fn3, n3)[0]
+            faithful = {"matmul_mode": "3xtf32", "value": units_total / (ms3 / 1000.0),
+                        "unit": wl.unit, "ms_per_step": ms3, "steps": n3,
+                        "l2": L2_FLUSHED if flush_buf is not None else "inputs > L2"}
+        finally:
+            if g3 is not None:
+                g3.close()
+            wxx.set_matmul_mode("tf32")
+
     line = {
         "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -961,8 +987,10 @@ def run_ours(args, rank, world, local):
                 "includes": "pinned H2D of inputs, forward, output (argmax ids or logits), "
                             "all-gather, D2H of the gathered outputs (own rows for logits)"},
     }
+    if faithful is not None:
+        line["faithful_3xtf32"] = faithful
     if comm is not None:
-        # SURVEY-style split: the forward alone and the step with its gather
+        # the forward alone and the step with its gather
         line["forward_ms_per_step"] = fwd_ms
         line["forward_value"] = units_total / (fwd_ms / 1000.0)
         line["gather_ms_per_step"] = ms - fwd_ms
@@ -1017,17 +1045,27 @@ def run_extra(args, rank, world, local):
         ids_h = rng.integers(0, V, size=(B, S), dtype=np.uint32)
         tgt_h = np.roll(ids_h, -1, axis=1).reshape(-1)
         loss_fn = wxx.nn.CCELoss()
+        ids_dev = F.from_numpy(ids_h, dtype=np.uint32)
+        tgt_dev = F.from_numpy(tgt_h, dtype=np.uint32)
+
+        def train_step():
+            opt.zero_grad()
+            logits = model(ids_dev)
+            loss = loss_fn(logits.reshape((B * S, V)), tgt_dev)
+            loss.backward()
+            opt.step()
+            return loss
+
+        # the whole step (forward, loss, backward, AdamW with its device step
+        # count) recorded once and replayed: one launch per step
+        graph = wxx.graph.capture(train_step)
+        lib = wxx.backend.lib.F
 
         def step():
             # host batch in, loss value out: the call a training loop makes
-            i = F.from_numpy(ids_h, dtype=np.uint32)
-            t = F.from_numpy(tgt_h, dtype=np.uint32)
-            opt.zero_grad()
-            logits = model(i)
-            loss = loss_fn(logits.reshape((B * S, V)), t)
-            loss.backward()
-            opt.step()
-            return float(loss.numpy().reshape(-1)[0])
+            lib.wxx_memcpy_h2d(ids_dev.ptr, ids_h.ctypes.data, ids_h.nbytes)
+            lib.wxx_memcpy_h2d(tgt_dev.ptr, tgt_h.ctypes.data, tgt_h.nbytes)
+            return float(graph.replay().numpy().reshape(-1)[0])
 
         units, flops = B * S, 3 * 11.81e9
         flush = L2Flush(F)
@@ -1081,7 +1119,8 @@ def run_extra(args, rank, world, local):
                 "traffic": None, "peak_basis": f"{kind} bf16 dense TFLOP/s / 2"}
         e2e_h2d = ids_h.nbytes + tgt_h.nbytes
         cfg = {"workload": "GPT2(1024,256,8,6) train step: fwd + CCELoss + bwd + AdamW, "
-                           "batch 4, seq 256", "parallelism": "replicas", "l2": L2_FLUSHED}
+                           "batch 4, seq 256, replayed from one CUDA graph",
+               "parallelism": "replicas", "l2": L2_FLUSHED}
     else:
         # decode steps read every weight copy once per token step
         weight_bytes = 4 * (L * 12 * D * D + V * D + S * D)
@@ -1122,6 +1161,8 @@ def main(argv=None):
                     default="gpt2_scaled")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-faithful", action="store_true",
+                    help="skip the extra 3xTF32 timing of the model workloads")
     ap.add_argument("--gather", choices=["ids", "logits", "logits-serial"], default="ids",
                     help="language models, N > 1: all-gather the argmax token ids (default) "
                          "or the fp32 logits (BASELINE config 5's collective; 'logits' overlaps "

@@ -264,14 +264,21 @@ int wxx_conv2d_nhwc_packed(float* Y, const float* X, const float* Wp, const floa
  * cin * taps <= 51200. */
 int wxx_conv_weight_pack(float* const* dst, const float* const* src, const int* cout,
                          const int* cin, const int* taps, int n);
+/* nn/resnet.py forward stem: conv 7x7 / stride 2 / pad 3 (Cin 1..4 -> 64, H, W <= 32) + bias
+ * (or NULL) + eval batchnorm (rm == NULL: none) + ReLU (relu = 1) + max pool 3x3 / stride 2 /
+ * pad 1, stored channels-last Y (B, Hp, Wp, 64); one launch, values equal to the separate ops. */
+int wxx_resnet_stem(float* Y, const float* X, const float* Wt, const float* bias,
+                    const float* rm, const float* rv, const float* gamma, const float* beta,
+                    float eps, int relu, int B, int Cin, int H, int W);
 
 /* nn/module.py:460-495 MultiHeadAttention core fused (QK^T * scale (+ mask), softmax, PV)
- * on tcgen05 TF32.  Q (B, Sq, H, hd) row stride q_ld, K/V (B, Sk, H, hd) row stride kv_ld,
+ * on tcgen05.  Q (B, Sq, H, hd) row stride q_ld, K/V (B, Sk, H, hd) row stride kv_ld,
  * O (B, Sq, H, hd) row stride o_ld; hd 32 or 64; causal masks keys after the query.
- * out_tf32 = 1 stores O rounded to the nearest TF32 value (an O read only by TF32 products). */
+ * mode 0: TF32 products; out_tf32 = 1 stores O rounded to the nearest TF32 value (an O read
+ * only by TF32 products).  mode 1: 3xTF32 products (fp32-faithful), out_tf32 ignored. */
 int wxx_attention(float* O, const float* Q, const float* K, const float* V, int B, int H, int Sq,
                   int Sk, int hd, int64_t q_ld, int64_t kv_ld, int64_t o_ld, float scale,
-                  const float* mask, int64_t mask_ld, int causal, int out_tf32);
+                  const float* mask, int64_t mask_ld, int causal, int out_tf32, int mode);
 
 /* ---------------------------------------------------------------- pooling */
 
@@ -365,6 +372,12 @@ int wxx_cceloss(float* loss, float* dZ, const float* Z, const uint32_t* targets,
 /* nn/optimizer.py:38-84 AdamW.step / adamw.wgsl: one step over n parameters in place. */
 int wxx_adamw(float* p, const float* g, float* m, float* v, int64_t n, float lr, float beta1,
               float beta2, float eps, float weight_decay, float bc1, float bc2);
+/* nn/optimizer.py AdamW.step with device-resident bias corrections (bc: two floats
+ * {bc1, bc2}), so a training step recorded as a CUDA graph replays with each step's own. */
+int wxx_adamw_device(float* p, const float* g, float* m, float* v, int64_t n, float lr,
+                     float beta1, float beta2, float eps, float weight_decay, const float* bc);
+/* step (one device int) += 1, then bc = {1 - beta1^step, 1 - beta2^step} (computed in double). */
+int wxx_adamw_advance(int* step, float* bc, double beta1, double beta2);
 
 /* ---------------------------------------------------------------- NCCL
  * No reference counterpart (the reference drives one WebGPU device): the

@@ -445,6 +445,54 @@ def test_conv2d_bn_epilogue(shape, mode, post, rng):
     assert np.abs(got - ref).max() <= 1e-6 * max(1.0, np.abs(ref).max())
 
 
+@pytest.mark.parametrize("B,C,H,W,bias", [(256, 3, 32, 32, False), (3, 3, 17, 23, True),
+                                           (2, 1, 1, 5, False), (5, 4, 32, 7, True)])
+def test_resnet_stem_matches_separate_ops(B, C, H, W, bias, rng):
+    """The fused stem (conv 7x7/2 + bias + eval batchnorm + ReLU + max pool
+    3x3/2 + channels-last store) gives the bits of conv2d_bn -> maxpool2d ->
+    permute(0, 2, 3, 1), and matches the float64 oracle convolution."""
+    F = _w().functional
+    x = rng.standard_normal((B, C, H, W)).astype(np.float32)
+    w = (rng.standard_normal((64, C, 7, 7)) * np.sqrt(2.0 / (C * 49))).astype(np.float32)
+    bvec = up(rng.standard_normal(64).astype(np.float32)) if bias else None
+    rm = up(rng.standard_normal(64).astype(np.float32))
+    rv = up(rng.uniform(0.5, 2.0, 64).astype(np.float32))
+    g = up(rng.standard_normal(64).astype(np.float32))
+    b = up(rng.standard_normal(64).astype(np.float32))
+    bn = (rm, rv, g, b, 1e-5)
+    got = F.resnet_stem(up(x), up(w), bvec, bn=bn, relu=True)
+    assert got is not None
+    y = F.conv2d_bn(up(x), up(w), (2, 2), (3, 3), (1, 1), bvec, bn=bn, relu=True)
+    ref = F.maxpool2d(y, (3, 3), (2, 2), (1, 1)).permute(0, 2, 3, 1).contiguous().numpy()
+    got = got.numpy()
+    assert got.shape == ref.shape
+    assert np.array_equal(got, ref)
+    conv = K.conv2d(x, w, (2, 2), (3, 3), (1, 1), None if bvec is None else bvec.numpy())
+    inv = 1.0 / np.sqrt(rv.numpy().astype(np.float64) + 1e-5)
+    z = (conv - rm.numpy()[None, :, None, None]) * (inv * g.numpy())[None, :, None, None] \
+        + b.numpy()[None, :, None, None]
+    z = np.maximum(z, 0.0)
+    Ho, Wo = z.shape[2], z.shape[3]
+    zp = np.full((B, 64, Ho + 2, Wo + 2), -np.inf)
+    zp[:, :, 1:-1, 1:-1] = z
+    Hp, Wp = (Ho - 1) // 2 + 1, (Wo - 1) // 2 + 1
+    pooled = np.full((B, 64, Hp, Wp), -np.inf)
+    for dy in range(3):
+        for dx in range(3):
+            pooled = np.maximum(pooled, zp[:, :, dy:dy + 2 * Hp - 1:2, dx:dx + 2 * Wp - 1:2])
+    assert rel(got, pooled.transpose(0, 2, 3, 1)) < 1e-5
+
+
+def test_resnet_stem_declines_other_shapes(rng):
+    F = _w().functional
+    x = up(rng.standard_normal((2, 8, 16, 16)).astype(np.float32))     # 8 input channels
+    w = up(rng.standard_normal((64, 8, 7, 7)).astype(np.float32))
+    assert F.resnet_stem(x, w) is None
+    x = up(rng.standard_normal((2, 3, 64, 64)).astype(np.float32))     # too large
+    w = up(rng.standard_normal((64, 3, 7, 7)).astype(np.float32))
+    assert F.resnet_stem(x, w) is None
+
+
 NHWC_SHAPES = [
     # B, Cin, H, W, Cout, k, stride, pad, dil
     (8, 64, 8, 8, 64, 3, 1, 1, 1),
@@ -677,6 +725,55 @@ def test_fused_attention(B, S, H, hd, kind, rng):
     ref = _attention_ref(q, k, v, H, mask, kind == "causal")
     assert got.shape == ref.shape
     assert rel(got, ref) < 4e-3, rel(got, ref)
+    assert _w().backend.device_status() == 0
+
+
+def _attention_ref64(q, k, v, H, mask=None, causal=False):
+    """nn/module.py:460-495 in float64."""
+    B, S, D = q.shape
+    Sk = k.shape[1]
+    hd = D // H
+
+    def heads(t, n):
+        return t.astype(np.float64).reshape(B, n, H, hd).transpose(0, 2, 1, 3)
+
+    s = heads(q, S) @ heads(k, Sk).transpose(0, 1, 3, 2) / np.sqrt(hd)
+    if causal:
+        s = s + np.where(np.arange(Sk)[None, :] <= np.arange(S)[:, None], 0.0, -1e9)
+    elif mask is not None:
+        s = s + mask.astype(np.float64)
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return (p @ heads(v, Sk)).transpose(0, 2, 1, 3).reshape(B, S, D)
+
+
+@pytest.mark.parametrize("B,S,H,hd,kind", [(2, 256, 4, 64, "causal"), (1, 100, 2, 32, "causal"),
+                                           (2, 300, 3, 64, "mask"), (1, 128, 2, 32, "none"),
+                                           (3, 200, 2, 64, "none"), (8, 1024, 16, 64, "causal")])
+def test_fused_attention_3xtf32(B, S, H, hd, kind, rng):
+    """The 3xTF32 form of the fused kernel is fp32-faithful: 1e-5 of the
+    largest output against a float64 restatement."""
+    F = _w().functional
+    D = H * hd
+    q = rng.standard_normal((B, S, D)).astype(np.float32)
+    k = rng.standard_normal((B, S, D)).astype(np.float32)
+    v = rng.standard_normal((B, S, D)).astype(np.float32)
+    mask = None
+    if kind == "mask":
+        mask = np.where(rng.random((S, S)) < 0.3, -1e9, rng.standard_normal((S, S))).astype(np.float32)
+        np.fill_diagonal(mask, 0.0)
+    F.set_matmul_mode("3xtf32")
+    try:
+        got = F.attention(up(q), up(k), up(v), H, mask=None if mask is None else up(mask),
+                          causal=(kind == "causal"), feeds_tf32=True).numpy()
+    finally:
+        F.set_matmul_mode("tf32")
+    ref = _attention_ref64(q, k, v, H, mask, kind == "causal")
+    assert rel(got, ref) < 1e-5, rel(got, ref)
+    tf32 = F.attention(up(q), up(k), up(v), H, mask=None if mask is None else up(mask),
+                       causal=(kind == "causal")).numpy()
+    assert rel(tf32, ref) > rel(got, ref)     # the TF32 form is the less exact one
     assert _w().backend.device_status() == 0
 
 

@@ -190,3 +190,56 @@ def test_gpt2_adamw_training_loss_falls():
     infer_loss = float((np.log(np.exp(zm).sum(-1)) - zm[np.arange(z.shape[0]), tgt.reshape(-1)])
                        .mean())
     assert abs(infer_loss - losses[-1]) < 0.2 * losses[0]
+
+
+def test_gpt2_training_step_replays_from_a_graph():
+    """A whole training step (forward, CCELoss, backward, AdamW) recorded as a
+    CUDA graph and replayed on new batches ends at the same weights and loss as
+    the eager steps (the device step count advances AdamW's bias corrections
+    on every replay; the embedding gradient's atomic adds may reorder fp32
+    sums, hence a tolerance instead of equal bits)."""
+    wxx = _w()
+    F = wxx.functional
+    V, D, H, L, S, B = 64, 32, 2, 2, 16, 2
+    rng = np.random.default_rng(11)
+    batches = [rng.integers(0, V, size=(B, S)).astype(np.uint32) for _ in range(5)]
+
+    def make():
+        model, _ = _gpt2(V, D, H, L, S)
+        opt = wxx.nn.AdamW(model.parameters(), lr=1e-2)
+        ids = up(batches[0], np.uint32)
+        tgt = up(np.roll(batches[0], -1, axis=1).reshape(-1), np.uint32)
+
+        def step():
+            opt.zero_grad()
+            logits = model(ids)
+            loss = wxx.nn.CCELoss()(logits.reshape((B * S, V)), tgt)
+            loss.backward()
+            opt.step()
+            return loss
+
+        return model, ids, tgt, step
+
+    def load(ids, tgt, k):
+        F.assign(ids, up(batches[k], np.uint32))
+        F.assign(tgt, up(np.roll(batches[k], -1, axis=1).reshape(-1), np.uint32))
+
+    m_eager, ids, tgt, step = make()
+    for k in range(5):
+        load(ids, tgt, k)
+        last_eager = float(step().numpy().reshape(-1)[0])
+
+    m_graph, ids, tgt, step = make()
+    g = wxx.graph.capture(step)                 # its warm-up run is step 1 (batch 0)
+    try:
+        for k in range(1, 5):
+            load(ids, tgt, k)
+            out = g.replay()
+        last_graph = float(out.numpy().reshape(-1)[0])
+        assert abs(last_graph - last_eager) < 1e-4 * max(1.0, abs(last_eager))
+        pe = dict(m_eager.named_parameters())
+        for name, p in m_graph.named_parameters():
+            assert rel(p.numpy(), pe[name].numpy()) < 1e-4, name
+    finally:
+        g.close()
+    assert wxx.backend.device_status() == 0

@@ -148,7 +148,7 @@ class addscaler(Function):
         return self._track(functional.scalarpointwise(a, c, 0))
 
     def backward(self, grad_output):
-        return grad_output, None
+        return (grad_output,) + (None,) * (len(self.inputs) - 1)
 
 
 class subscaler(Function):
@@ -156,7 +156,7 @@ class subscaler(Function):
         return self._track(functional.scalarpointwise(a, c, 1))
 
     def backward(self, grad_output):
-        return grad_output, None
+        return (grad_output,) + (None,) * (len(self.inputs) - 1)
 
 
 class mulscaler(Function):
@@ -165,7 +165,7 @@ class mulscaler(Function):
         return self._track(functional.scalarpointwise(a, c, 2))
 
     def backward(self, grad_output):
-        return _scale(grad_output, self.c), None
+        return (_scale(grad_output, self.c),) + (None,) * (len(self.inputs) - 1)
 
 
 class negate(Function):
@@ -478,7 +478,9 @@ class CrossEntropyLoss(Function):
 
     def backward(self, grad_output):
         g, self.grad = self.grad, None
-        return functional.pointwise(g, grad_output, 2), None
+        dz = functional.pointwise(g, grad_output, 2)
+        # constructed with the logits alone (nn/loss.py) or with the targets too
+        return (dz,) + (None,) * (len(self.inputs) - 1)
 
 
 def _training_op(name):

@@ -103,8 +103,9 @@ SIGNATURES = {
     "wxx_conv2d_nhwc_packed": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14
                               + [c_void_p] * 4 + [c_float, c_void_p, c_int],
     "wxx_conv_weight_pack": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int],
+    "wxx_resnet_stem": [c_void_p] * 8 + [c_float] + [c_int] * 5,
     "wxx_attention": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
-                      c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int, c_int],
+                      c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int, c_int, c_int],
     "wxx_maxpool2d": [c_void_p, c_void_p, c_void_p] + [c_int] * 10,
     "wxx_adaptive_avgpool2d": [c_void_p, c_void_p] + [c_int] * 6,
     "wxx_rfft": [c_void_p, c_i64, c_void_p, c_i64, c_i64, c_i64, c_i64],
@@ -136,6 +137,9 @@ SIGNATURES = {
     "wxx_embedding_backward": [c_void_p, c_void_p, c_void_p, c_i64, c_int, c_int],
     "wxx_cceloss": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_int],
     "wxx_adamw": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64] + [c_float] * 7,
+    "wxx_adamw_device": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64] + [c_float] * 5
+                        + [c_void_p],
+    "wxx_adamw_advance": [c_void_p, c_void_p, ctypes.c_double, ctypes.c_double],
     "wxx_nccl_unique_id": [P_u8],
     "wxx_nccl_init": [P_u8, c_int, c_int],
     "wxx_nccl_allgather": [c_void_p, c_void_p, c_u64],

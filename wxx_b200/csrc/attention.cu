@@ -35,6 +35,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -43,10 +44,13 @@ using namespace wxx_tc;
 namespace {
 
 constexpr int BQ = 128;   // query rows per tile (UMMA M)
-constexpr int NT = 2;     // query tiles per CTA
 constexpr int BKV = 64;   // keys per block (UMMA N of S, K of PV)
-constexpr int ATT_THREADS = 64 + NT * 128 + 32;   // + one MMA-issuing warp per extra tile
-constexpr int MMA_WARP1 = 2 + NT * 4;               // issues tile 1's MMAs (warp 1: tile 0's)
+// NT query tiles per CTA: 2 (one CTA per SM, K / V blocks shared by both
+// tiles) or 1 (two CTAs per SM: one CTA's setup, first loads and output
+// drain overlap the other's steady state).  Warps: producer, tile 0's MMA
+// thread, 4 softmax warps per tile, then (NT = 2) tile 1's MMA thread.
+__host__ __device__ constexpr int att_threads(int nt) { return 64 + nt * 128 + (nt - 1) * 32; }
+__host__ __device__ constexpr int mma_warp1(int nt) { return 2 + nt * 4; }   // tile 1's MMA warp (NT = 2)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;   // raise the max used for P only past 2^8
 
@@ -73,23 +77,61 @@ __device__ __forceinline__ float exp2_fma(float x) {
 }
 
 
-template <int HD>
+// X3: the fp32-faithful 3xTF32 form (one tile per CTA, one CTA per SM).
+// Each product x*y becomes hi(x)hi(y) + lo(x)hi(y) + hi(x)lo(y) where hi is
+// the operand as the tensor core reads it (the low 13 mantissa bits
+// dropped) and lo = x - hi(x): S = Q K^T + Qlo K^T + Q Klo^T and
+// O += P V + Plo V + P Vlo.  Klo / Vlo are made in shared memory by a split
+// warp as each block lands, Qlo (once) and Plo (per block) in TMEM by the
+// softmax warps, which also keep P unrounded.
+template <int HD, int NT, bool X3 = false>
 struct ACfg {
   static constexpr int Q_BYTES = BQ * HD * 4;          // per tile: 32 KB (hd 64)
   static constexpr int K_BYTES = BKV * HD * 4;         // 16 KB
   static constexpr int V_BYTES = BKV * HD * 4;         // 16 KB
-  static constexpr int KVS = 4;                        // K / V pipeline stages
+  static constexpr int KVS = (NT == 2 && !X3) ? 4 : 2; // K / V pipeline stages
   static constexpr int STAGE_O_BYTES = 4 * 4096;       // per tile: O staging for the TMA store
   static constexpr int OFF_K = NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KVS * K_BYTES;
-  static constexpr int OFF_O = OFF_V + KVS * V_BYTES;
-  static constexpr int SMEM = OFF_O + NT * STAGE_O_BYTES + 1024;
-  // TMEM per tile: S double buffer (2 x 64 columns) then O (hd columns).
+  static constexpr int OFF_KLO = OFF_V + KVS * V_BYTES;             // X3 only
+  static constexpr int OFF_VLO = OFF_KLO + (X3 ? KVS * K_BYTES : 0);
+  static constexpr int OFF_O = OFF_VLO + (X3 ? KVS * V_BYTES : 0);
+  // NT = 1 stages O in its Q buffer (every S product has completed by then)
+  static constexpr int SMEM = OFF_O + (NT == 2 ? NT * STAGE_O_BYTES : 0) + 1024;
+  // TMEM per tile: S double buffer (2 x 64 columns) then O (hd columns);
+  // X3 adds the Plo double buffer and Qlo.
   static constexpr int TMEM_TILE = 2 * BKV + HD;
-  static constexpr int TMEM_COLS = 512;
+  static constexpr int PLO_COL = TMEM_TILE;
+  static constexpr int QLO_COL = TMEM_TILE + 2 * BKV;
+  static constexpr int TMEM_COLS = (NT == 2 || X3) ? 512 : 256;
+  static constexpr bool ONE_PER_SM = NT == 2 || X3;
+  static_assert(NT == 1 || NT == 2, "one or two query tiles per CTA");
+  static_assert(!X3 || NT == 1, "the 3xTF32 form runs one tile per CTA");
   static_assert(NT * TMEM_TILE <= TMEM_COLS, "TMEM layout");
-  static_assert(SMEM <= 227 * 1024, "shared memory layout");
+  static_assert(!X3 || QLO_COL + HD <= TMEM_COLS, "TMEM layout (3xTF32)");
+  static_assert(NT == 2 || Q_BYTES >= STAGE_O_BYTES, "O staging in the Q buffer");
+  static_assert(SMEM <= (ONE_PER_SM ? 227 * 1024 : 112 * 1024), "shared memory layout");
 };
+
+__device__ __forceinline__ float tf32_low(float x) {
+  return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+
+// dst = lo(src) elementwise over a shared-memory tile (any layout: the
+// descriptors that read src read dst the same way), one warp.
+__device__ __forceinline__ void split_low_tile(const uint8_t* src, uint8_t* dst, int bytes,
+                                               int lane) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  for (int i = lane; i < bytes / 16; i += 32) {
+    float4 v = s4[i];
+    v.x = tf32_low(v.x);
+    v.y = tf32_low(v.y);
+    v.z = tf32_low(v.z);
+    v.w = tf32_low(v.w);
+    d4[i] = v;
+  }
+}
 
 struct AttnParams {
   int B, H, Sq, Sk;
@@ -102,18 +144,21 @@ struct AttnParams {
   int* err;
 };
 
-template <int HD, bool HAS_MASK>
-__global__ void __launch_bounds__(ATT_THREADS, 1)
+template <int HD, bool HAS_MASK, int NT, bool X3 = false>
+__global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, X3>::ONE_PER_SM ? 1 : 2)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_o, const AttnParams p) {
-  using C = ACfg<HD>;
+  using C = ACfg<HD, NT, X3>;
+  constexpr int MMA_WARP1 = mma_warp1(NT);
+  constexpr int SPLIT_WARP = att_threads(NT) / 32;   // X3: makes Klo / Vlo
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full;
   __shared__ __align__(8) uint64_t k_full[C::KVS], k_empty[C::KVS], v_full[C::KVS], v_empty[C::KVS];
   __shared__ __align__(8) uint64_t s_full[NT][2], p_full[NT], p_empty[NT];
   __shared__ __align__(8) uint64_t drain_bar[NT];
+  __shared__ __align__(8) uint64_t klo_full[C::KVS], vlo_full[C::KVS], qlo_full;   // X3
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
@@ -134,8 +179,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     if (p.causal && n) n = min(n, (qt + BQ - 1) / BKV + 1);
     return n;
   };
-  static_assert(NT == 2, "tile bookkeeping below assumes two tiles");
-  const int n_t0 = blocks_of(0), n_t1 = blocks_of(1);
+  const int n_t0 = blocks_of(0), n_t1 = NT == 2 ? blocks_of(1) : 0;
   const int n_kv = max(n_t0, n_t1);
 
   if (threadIdx.x == 0) {
@@ -154,6 +198,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&p_empty[t], 1);
     }
     for (int t = 0; t < NT; ++t) mbar_init(&drain_bar[t], 1);
+    if (X3) {
+      for (int s = 0; s < C::KVS; ++s) {
+        mbar_init(&klo_full[s], 1);
+        mbar_init(&vlo_full[s], 1);
+      }
+      mbar_init(&qlo_full, 128);
+    }
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
@@ -202,7 +253,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (last_v[s] >= 0) mbar_wait(&v_full[s], (last_v[s] / C::KVS) & 1, &no_abort, p.err);
       }
     }
-  } else if (warp == 1 || warp == MMA_WARP1) {
+  } else if (warp == 1 || (NT == 2 && warp == MMA_WARP1)) {
     // ------------------------------------------------ MMA issuers, one thread per tile
     // Each tile's chain (S_t(j+1) issued, then wait P_t(j), then O_t += P_t(j) V_j)
     // runs on its own thread, so one tile's softmax never holds up the other
@@ -215,11 +266,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const uint32_t sbase = smem_u32(smem);
       const uint32_t sq = sbase + t * C::Q_BYTES;
       bool ok = mbar_wait(&q_full, 0, &abort_flag, p.err);
+      if (X3 && ok) ok = mbar_wait(&qlo_full, 0, &abort_flag, p.err);
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int s = jj % C::KVS;       // V stage
         const int sb = jj & 1;           // TMEM S / P buffer
         if (!mbar_wait(&v_full[s], (jj / C::KVS) & 1, &abort_flag, p.err)) return false;
+        if (X3 && !mbar_wait(&vlo_full[s], (jj / C::KVS) & 1, &abort_flag, p.err)) return false;
         tc_fence_after();
         if (jj < nt) {
           if (!mbar_wait(&p_full[t], jj & 1, &abort_flag, p.err)) return false;
@@ -232,6 +285,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             uint64_t bd = sdesc(sv + kk * 1024, BKV * 128, 512, kLayoutSW128Base32B);
             umma_tf32_ts(d, pa + kk * 8, bd, idesc_o, (jj > 0 || kk > 0) ? 1u : 0u);
           }
+          if (X3) {
+            const uint32_t plo = tmem_base + C::PLO_COL + sb * BKV;
+            const uint32_t svlo = sbase + C::OFF_VLO + s * C::V_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BKV / 8; ++kk) {
+              uint64_t bd = sdesc(sv + kk * 1024, BKV * 128, 512, kLayoutSW128Base32B);
+              umma_tf32_ts(d, plo + kk * 8, bd, idesc_o, 1u);
+            }
+#pragma unroll
+            for (int kk = 0; kk < BKV / 8; ++kk) {
+              uint64_t bd = sdesc(svlo + kk * 1024, BKV * 128, 512, kLayoutSW128Base32B);
+              umma_tf32_ts(d, pa + kk * 8, bd, idesc_o, 1u);
+            }
+          }
           umma_commit(&p_empty[t]);
         }
         umma_commit(&v_empty[s]);
@@ -241,6 +308,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int s = j % C::KVS;        // K stage
         const int sb = j & 1;            // TMEM S buffer
         if (!mbar_wait(&k_full[s], (j / C::KVS) & 1, &abort_flag, p.err)) { ok = false; break; }
+        if (X3 && !mbar_wait(&klo_full[s], (j / C::KVS) & 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         if (j < nt) {
           // S_t(j) overwrites the columns P_t(j-2) occupied: that P V product
@@ -255,6 +323,22 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             uint64_t bd = sdesc(sk + (kk >> 2) * (BKV * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
             umma_tf32(d, ad, bd, idesc_s, kk ? 1u : 0u);
           }
+          if (X3) {
+            const uint32_t sklo = sbase + C::OFF_KLO + s * C::K_BYTES;
+            const uint32_t qlo = tmem_base + C::QLO_COL;
+#pragma unroll
+            for (int kk = 0; kk < HD / 8; ++kk) {
+              uint64_t ad = sdesc(sq + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+              uint64_t bd = sdesc(sklo + (kk >> 2) * (BKV * 128) + (kk & 3) * 32, 16, 1024,
+                                  kLayoutSW128);
+              umma_tf32(d, ad, bd, idesc_s, 1u);
+            }
+#pragma unroll
+            for (int kk = 0; kk < HD / 8; ++kk) {
+              uint64_t bd = sdesc(sk + (kk >> 2) * (BKV * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+              umma_tf32_ts(d, qlo + kk * 8, bd, idesc_s, 1u);
+            }
+          }
           umma_commit(&s_full[t][sb]);
         }
         umma_commit(&k_empty[s]);
@@ -264,6 +348,26 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       umma_commit(&drain_bar[t]);
       volatile int no_abort = 0;
       mbar_wait(&drain_bar[t], 0, &no_abort, p.err);
+    }
+  } else if (X3 && warp == SPLIT_WARP) {
+    // ------------------------------------------------ X3: Klo / Vlo as blocks land
+    // A stage is refilled only after the S (V: P V) products that read it
+    // and its low part committed, so the low part is never overwritten early.
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j % C::KVS;
+      const uint32_t par = (j / C::KVS) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&k_full[s], par, &abort_flag, p.err))) break;
+      split_low_tile(smem + C::OFF_K + s * C::K_BYTES, smem + C::OFF_KLO + s * C::K_BYTES,
+                     C::K_BYTES, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&klo_full[s]);
+      if (!__all_sync(0xffffffffu, mbar_wait(&v_full[s], par, &abort_flag, p.err))) break;
+      split_low_tile(smem + C::OFF_V + s * C::V_BYTES, smem + C::OFF_VLO + s * C::V_BYTES,
+                     C::V_BYTES, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&vlo_full[s]);
     }
   } else {
     // ------------------------------------------------ softmax (one row per thread)
@@ -284,10 +388,35 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int warp_lim = p.causal ? min(p.Sk, qt + quarter * 32 + 1) : p.Sk;
     const float* mrow = nullptr;
     if (HAS_MASK && qrow < p.Sq) mrow = p.mask + (int64_t)qrow * p.mask_ld;
-    uint8_t* pb = smem + C::OFF_O + tile * C::STAGE_O_BYTES;
+    uint8_t* pb = NT == 2 ? smem + C::OFF_O + tile * C::STAGE_O_BYTES : smem;
     float m_used = -INFINITY;   // max that P and l are relative to
     float l_run = 0.f;
     bool ok = true;
+    if (X3) {
+      // Qlo of this thread's query row into TMEM (the S products' third term);
+      // the row sits in 128-byte chunks with the 16-byte units XOR-swizzled by
+      // the row index (the TMA load's 128B swizzle).
+      ok = __all_sync(0xffffffffu, mbar_wait(&q_full, 0, &abort_flag, p.err));
+      if (ok) {
+        const uint32_t qlo_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + C::QLO_COL;
+#pragma unroll
+        for (int a = 0; a < HD / 32; ++a) {
+          const uint8_t* rb = smem + a * (BQ * 128) + row * 128;
+          float v[32];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 f = *reinterpret_cast<const float4*>(rb + ((q ^ (row & 7)) << 4));
+            v[4 * q] = tf32_low(f.x);
+            v[4 * q + 1] = tf32_low(f.y);
+            v[4 * q + 2] = tf32_low(f.z);
+            v[4 * q + 3] = tf32_low(f.w);
+          }
+          tmem_st_32x32(qlo_addr + a * 32, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&qlo_full);
+    }
 
     for (int j = 0; j < nt && ok; ++j) {
       const int s = j & 1;
@@ -353,9 +482,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         // value by integer ops on its bits (ties away from zero): the P V
         // product then reads it exactly, and the row sum l below adds the
         // same rounded values, so the weights applied to V sum to one.
-        const float pv = __uint_as_float(
-            (__float_as_uint(((i & 7) < 3) ? exp2_fma(arg) : fast_exp2(arg)) + 0x1000u) &
-            0xFFFFE000u);
+        // X3 keeps p exact (its low part goes through the Plo term).
+        const float pe = ((i & 7) < 3) ? exp2_fma(arg) : fast_exp2(arg);
+        const float pv = X3 ? pe : __uint_as_float((__float_as_uint(pe) + 0x1000u) & 0xFFFFE000u);
         if (i < 32) xa[i & 31] = pv; else xb[i & 31] = pv;
         acc[i & 7] += pv;
       }
@@ -364,6 +493,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       // per key): the P V product takes its A operand from there.
       tmem_st_32x32(lane_addr + s * BKV, xa);
       tmem_st_32x32(lane_addr + s * BKV + 32, xb);
+      if (X3) {
+        // Plo (the P V products' second term) into its own TMEM buffer
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          xa[i] = tf32_low(xa[i]);
+          xb[i] = tf32_low(xb[i]);
+        }
+        const uint32_t plo_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + C::PLO_COL + s * BKV;
+        tmem_st_32x32(plo_addr, xa);
+        tmem_st_32x32(plo_addr + 32, xb);
+      }
 #undef ATT_X
       // The previous P V product has finished: O holds every block < j (needed
       // by a rescale).  Waiting every block also keeps this barrier's phases
@@ -409,7 +549,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] *= inv;
-        if (p.out_tf32) {
+        if (!X3 && p.out_tf32) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = tf32_rna(v[i]);
         }
@@ -468,11 +608,47 @@ bool encode_bshd(CUtensorMap* map, const float* base, int B, int S, int H, int H
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <int HD, int NT, bool X3 = false>
+int launch_attention_nt(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                        const CUtensorMap& mo, AttnParams p, bool has_mask) {
+  using C = ACfg<HD, NT, X3>;
+  constexpr int threads = att_threads(NT) + (X3 ? 32 : 0);
+  static bool attr = false;
+  if (!attr) {
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD, false, NT, X3>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD, true, NT, X3>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr = true;
+  }
+  p.n_qpairs = (p.Sq + NT * BQ - 1) / (NT * BQ);
+  const int64_t grid = (int64_t)p.B * p.H * p.n_qpairs;
+  WXX_REQUIRE(grid < (int64_t(1) << 31), "wxx_attention: grid too large");
+  if (has_mask)
+    attention_kernel<HD, true, NT, X3>
+        <<<(unsigned)grid, threads, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
+  else
+    attention_kernel<HD, false, NT, X3>
+        <<<(unsigned)grid, threads, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+// Query tiles per CTA: WXX_ATTN_TILES=1 or 2, read once.  Default 1 (two
+// CTAs per SM): 191 against 169-179 TFLOP/s for two tiles per CTA at the
+// GPT2-scaled shape (B 8, S 1024, 16 heads x 64, causal).
+int attn_tiles_per_cta() {
+  static int nt = [] {
+    const char* e = std::getenv("WXX_ATTN_TILES");
+    return (e != nullptr && e[0] == '2') ? 2 : 1;
+  }();
+  return nt;
+}
+
 template <int HD>
 int launch_attention(float* O, const float* Q, const float* K, const float* V, int B, int H,
                      int Sq, int Sk, int64_t q_ld, int64_t kv_ld, int64_t o_ld, float scale,
-                     const float* mask, int64_t mask_ld, int causal, int out_tf32) {
-  using C = ACfg<HD>;
+                     const float* mask, int64_t mask_ld, int causal, int out_tf32, int mode) {
   CUtensorMap mq, mk, mv, mo;
   if (!encode_bshd(&mq, Q, B, Sq, H, HD, q_ld, q_ld * Sq, BQ, false) ||
       !encode_bshd(&mk, K, B, Sk, H, HD, kv_ld, kv_ld * Sk, BKV, false) ||
@@ -481,59 +657,47 @@ int launch_attention(float* O, const float* Q, const float* K, const float* V, i
     wxx::set_error("wxx_attention: operands are not 16-byte addressable for TMA");
     return WXX_E_ARG;
   }
-  static bool attr = false;
-  if (!attr) {
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD, false>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    WXX_CUDA_CHECK(cudaFuncSetAttribute(attention_kernel<HD, true>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    attr = true;
-  }
   AttnParams p;
   memset(&p, 0, sizeof(p));
   p.B = B;
   p.H = H;
   p.Sq = Sq;
   p.Sk = Sk;
-  p.n_qpairs = (Sq + NT * BQ - 1) / (NT * BQ);
   p.scale = scale;
   p.causal = causal;
-  p.out_tf32 = out_tf32 ? 1 : 0;
+  p.out_tf32 = (out_tf32 && mode == 0) ? 1 : 0;
   p.mask = mask;
   p.mask_ld = mask_ld;
   p.err = wxx::device_error_word();
-  int64_t grid = (int64_t)B * H * p.n_qpairs;
-  WXX_REQUIRE(grid < (int64_t(1) << 31), "wxx_attention: grid too large");
-  if (mask != nullptr)
-    attention_kernel<HD, true><<<(unsigned)grid, ATT_THREADS, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
-  else
-    attention_kernel<HD, false><<<(unsigned)grid, ATT_THREADS, C::SMEM, wxx::stream()>>>(mq, mk, mv, mo, p);
-  WXX_LAUNCH_CHECK();
-  return WXX_OK;
+  if (mode == 1) return launch_attention_nt<HD, 1, true>(mq, mk, mv, mo, p, mask != nullptr);
+  if (attn_tiles_per_cta() == 1) return launch_attention_nt<HD, 1>(mq, mk, mv, mo, p, mask != nullptr);
+  return launch_attention_nt<HD, 2>(mq, mk, mv, mo, p, mask != nullptr);
 }
 
 }  // namespace
 
-// O = softmax(scale * Q K^T (+ mask)) V per (batch, head), TF32 tensor cores.
+// O = softmax(scale * Q K^T (+ mask)) V per (batch, head) on the tensor cores.
 // Q: (B, Sq, H, hd) with row stride q_ld elements between consecutive
 // positions (H*hd for the merged projection output); K, V: (B, Sk, H, hd)
 // with row stride kv_ld; O: (B, Sq, H, hd) with row stride o_ld.
 // hd must be 32 or 64 and scale > 0; pointers and strides 16-byte aligned.  causal = 1 masks
 // keys after the query position; mask (Sq x Sk, row stride mask_ld) is added
-// to the scaled scores when given.  The probabilities enter the P V product
-// rounded to the nearest TF32 value; out_tf32 = 1 also stores O rounded so
-// (for an O read only by the TF32 output projection).
+// to the scaled scores when given.  mode 0: TF32 products, the probabilities
+// entering the P V product rounded to the nearest TF32 value; out_tf32 = 1
+// also stores O rounded so (for an O read only by the TF32 output
+// projection).  mode 1: 3xTF32 products (fp32-faithful; out_tf32 ignored).
 WXX_EXPORT int wxx_attention(float* O, const float* Q, const float* K, const float* V, int B,
                              int H, int Sq, int Sk, int hd, int64_t q_ld, int64_t kv_ld,
                              int64_t o_ld, float scale, const float* mask, int64_t mask_ld,
-                             int causal, int out_tf32) {
+                             int causal, int out_tf32, int mode) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(B > 0 && H > 0 && Sq > 0 && Sk > 0, "wxx_attention: empty problem");
   WXX_REQUIRE(hd == 32 || hd == 64, "wxx_attention: head dim %d not in {32, 64}", hd);
   WXX_REQUIRE(scale > 0.f, "wxx_attention: scale must be positive");
+  WXX_REQUIRE(mode == 0 || mode == 1, "wxx_attention: mode %d not in {0, 1}", mode);
   if (hd == 32)
     return launch_attention<32>(O, Q, K, V, B, H, Sq, Sk, q_ld, kv_ld, o_ld, scale, mask, mask_ld,
-                                causal, out_tf32);
+                                causal, out_tf32, mode);
   return launch_attention<64>(O, Q, K, V, B, H, Sq, Sk, q_ld, kv_ld, o_ld, scale, mask, mask_ld,
-                              causal, out_tf32);
+                              causal, out_tf32, mode);
 }

@@ -28,6 +28,7 @@ SOURCES = [
     "elementwise.cu",
     "reduce.cu",
     "gemm.cu",
+    "stem.cu",
     "fft.cu",
     "fft_static.cu",
     "hyena_filter.cu",

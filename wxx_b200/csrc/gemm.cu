@@ -512,6 +512,98 @@ __global__ void __launch_bounds__(256) skinny_gemm_kernel(
   }
 }
 
+// ------------------------------------------------------------ few rows (decode)
+
+// C (M <= 32 rows) = act(alpha * A @ W^T + bias) + res for a K-major weight W
+// (N, K): the decode step's products, where the weight is read once and each
+// of its values meets only M activations, so the time is the weight stream.
+// A tile-based GEMM gives such a product N / 256 CTAs; here a CTA takes
+// kGemvGroups x kGemvCols columns and its warps split K (kGemvKs ways), so
+// N = 1024 already spreads over 128 CTAs.  Per warp: kGemvCols weight rows
+// and 8 activation rows as float4 loads along K, 32 fp32 accumulators (column
+// c, row r at index 8c + r), reduced across the lanes by a halving exchange
+// (31 shuffles; lane l ends with the sum for index l), then over the K-split
+// warps in fixed order through shared memory.  Exact fp32 products; the
+// epilogue is the tensor-core path's (alpha, bias, GELU, residual, TF32
+// rounding of the stored value).
+constexpr int kGemvCols = 4;
+constexpr int kGemvKs = 4;
+constexpr int kGemvGroups = 2;
+constexpr int kGemvMaxRows = 32;
+
+__global__ void __launch_bounds__(256) rows_gemv_kernel(
+    float* __restrict__ C, const float* __restrict__ A, int64_t lda, const float* __restrict__ W,
+    int64_t ldw, const float* __restrict__ bias, int M, int N, int K, float alpha, int act,
+    const float* __restrict__ res, int round_out) {
+  __shared__ float part[kGemvGroups][kGemvKs][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cg = warp / kGemvKs, ks = warp % kGemvKs;
+  const int n0 = (blockIdx.x * kGemvGroups + cg) * kGemvCols;
+  const int kq = ((K + kGemvKs * 128 - 1) / (kGemvKs * 128)) * 128;
+  const int kb = ks * kq, ke = min(K, kb + kq);
+  const float* wr[kGemvCols];
+  bool wv[kGemvCols];
+#pragma unroll
+  for (int c = 0; c < kGemvCols; ++c) {
+    wv[c] = n0 + c < N;
+    wr[c] = W + (int64_t)(wv[c] ? n0 + c : 0) * ldw;
+  }
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int m0 = 0; m0 < M; m0 += 8) {
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    for (int k = kb + lane * 4; k < ke; k += 128) {
+      float4 w4[kGemvCols];
+#pragma unroll
+      for (int c = 0; c < kGemvCols; ++c)
+        w4[c] = wv[c] ? __ldg(reinterpret_cast<const float4*>(wr[c] + k)) : zero;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float4 a = (m0 + r < M)
+            ? __ldg(reinterpret_cast<const float4*>(A + (int64_t)(m0 + r) * lda + k)) : zero;
+#pragma unroll
+        for (int c = 0; c < kGemvCols; ++c) {
+          float t = acc[8 * c + r];
+          t = fmaf(a.x, w4[c].x, t);
+          t = fmaf(a.y, w4[c].y, t);
+          t = fmaf(a.z, w4[c].z, t);
+          t = fmaf(a.w, w4[c].w, t);
+          acc[8 * c + r] = t;
+        }
+      }
+    }
+    // halving exchange: after the step with distance s a lane keeps the half
+    // of its indices selected by its lane bit s, summed with its partner's
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+      const bool upper = (lane & s) != 0;
+#pragma unroll
+      for (int i = 0; i < s; ++i) {
+        const float send = upper ? acc[i] : acc[i + s];
+        const float keep = upper ? acc[i + s] : acc[i];
+        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+      }
+    }
+    part[cg][ks][lane] = acc[0];
+    __syncthreads();
+    if (ks == 0) {
+      float v = part[cg][0][lane];
+#pragma unroll
+      for (int q = 1; q < kGemvKs; ++q) v += part[cg][q][lane];
+      const int n = n0 + (lane >> 3), m = m0 + (lane & 7);
+      if (n < N && m < M) {
+        v = bias != nullptr ? v * alpha + __ldg(bias + n) : v * alpha;
+        if (act == 1) v = gelu_tanh(v);
+        if (res != nullptr) v += __ldg(res + (int64_t)m * N + n);
+        if (round_out) v = tf32_rna(v);
+        C[(int64_t)m * N + n] = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // 64x64 output tile, K-step 16, 4x4 outputs per thread, fp32 FMA.
 __global__ void __launch_bounds__(256) simt_gemm_kernel(
     float* __restrict__ C, const float* __restrict__ A, const float* __restrict__ B,
@@ -601,6 +693,21 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
     WXX_CUDA_CHECK(cudaMemsetAsync(C, 0, batch * M * N * sizeof(float), s));
     if (bias_mode == 0) return WXX_OK;
     mode = 2;  // the SIMT kernel adds the bias to the zero product
+  }
+  // A few rows against a K-major weight (generation's decode step): the
+  // weight-streaming kernel.  Batches whose A rows are consecutive and share
+  // the weight fold into rows.
+  const int64_t rows_all = batch * M;
+  if (rows_all <= kGemvMaxRows && trans_a == 0 && trans_b != 0 && act <= 1 && bias_mode <= 1 &&
+      (batch == 1 || (a_bs == M * lda && b_bs == 0)) && N >= 64 && K >= 128 && K % 4 == 0 &&
+      lda % 4 == 0 && ldb % 4 == 0 && !(reinterpret_cast<uintptr_t>(A) & 15) &&
+      !(reinterpret_cast<uintptr_t>(B) & 15) && (lda >= K || rows_all == 1)) {
+    const int64_t per_cta = kGemvGroups * kGemvCols;
+    rows_gemv_kernel<<<(unsigned)((N + per_cta - 1) / per_cta), 256, 0, s>>>(
+        C, A, lda, B, ldb, bias_mode == 1 ? bias : nullptr, (int)rows_all, (int)N, (int)K, alpha,
+        act, res, round_out);
+    WXX_LAUNCH_CHECK();
+    return WXX_OK;
   }
   // Skinny products with a long K (ResNet's 256 x 10 x 512 classifier: two
   // gathered tensor-core tiles walking 16 K-blocks) run one warp per output

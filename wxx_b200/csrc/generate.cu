@@ -51,64 +51,78 @@ __global__ void decode_embed_kernel(float* __restrict__ out, const uint32_t* __r
   }
 }
 
-constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = 256;
 
 // One CTA per (head, sequence).  Appends the new position's K and V (this
 // head's hd columns) to the caches, then o = softmax(scale * q . K^T) V over
-// positions 0..p in exact fp32 (scores in shared memory, one warp per key with
-// the head dim split over the lanes).  The position is causal by
-// construction: only keys up to the query exist.
+// positions 0..p in exact fp32.  Scores: one thread per key, its hd / 4
+// float4 loads of the key row all in flight at once (a warp per key with a
+// shuffle reduction per key would expose one memory latency per key).  P V:
+// thread t owns column quad t % (hd / 4) and every (kAttnThreads / (hd / 4))-th
+// key, and the key groups are summed in fixed order through shared memory.
+// The position is causal by construction: only keys up to the query exist.
 template <int HD>
-__global__ void __launch_bounds__(kAttnWarps * 32)
+__global__ void __launch_bounds__(kAttnThreads)
     decode_attention_kernel(float* __restrict__ O, int64_t o_ld, const float* __restrict__ q,
                             const float* __restrict__ k_new, const float* __restrict__ v_new,
                             int64_t qkv_ld, float* __restrict__ Kc, float* __restrict__ Vc,
                             int64_t cache_bs, int D, const int* __restrict__ cur_len, int max_len,
                             float scale, int out_tf32, int* err) {
-  constexpr int PER = HD / 32;   // head dims per lane
+  constexpr int NQ = HD / 4;                   // float4 per head row
+  constexpr int KG = kAttnThreads / NQ;        // key groups of the P V product
+  constexpr int NW = kAttnThreads / 32;
   extern __shared__ float s_score[];
-  __shared__ float s_red[kAttnWarps];
-  __shared__ float s_o[kAttnWarps][HD];
+  __shared__ __align__(16) float s_q[HD];
+  __shared__ float s_red[NW];
+  __shared__ __align__(16) float s_part[KG][HD];
   const int h = blockIdx.x, b = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int p = *cur_len - 1;
   if (p < 0 || p >= max_len) {
-    if (threadIdx.x == 0) wxx_device_fail(err, WXX_DEV_ERR_BAD_INDEX);
+    if (t == 0) wxx_device_fail(err, WXX_DEV_ERR_BAD_INDEX);
     return;
   }
   const int64_t col = (int64_t)h * HD;
   float* kb = Kc + b * cache_bs + col;
   float* vb = Vc + b * cache_bs + col;
-  for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+  for (int i = t; i < HD; i += kAttnThreads) {
     kb[(int64_t)p * D + i] = k_new[b * qkv_ld + col + i];
     vb[(int64_t)p * D + i] = v_new[b * qkv_ld + col + i];
+    s_q[i] = q[b * qkv_ld + col + i];
   }
-  float qv[PER];
-#pragma unroll
-  for (int e = 0; e < PER; ++e) qv[e] = q[b * qkv_ld + col + lane * PER + e];
-  __syncthreads();   // the appended K / V rows are visible to every warp
+  __syncthreads();   // the appended K / V rows and q are visible to every thread
   // scores
+  const float4* q4 = reinterpret_cast<const float4*>(s_q);
   float mx = -INFINITY;
-  for (int j = warp; j <= p; j += kAttnWarps) {
-    const float* kr = kb + (int64_t)j * D + lane * PER;
+  for (int j = t; j <= p; j += kAttnThreads) {
+    const float4* kr = reinterpret_cast<const float4*>(kb + (int64_t)j * D);
+    float4 kv[NQ];
+#pragma unroll
+    for (int e = 0; e < NQ; ++e) kv[e] = kr[e];
     float acc = 0.f;
 #pragma unroll
-    for (int e = 0; e < PER; ++e) acc = fmaf(qv[e], kr[e], acc);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    const float s = acc * scale;
-    if (lane == 0) s_score[j] = s;
-    mx = fmaxf(mx, s);
+    for (int e = 0; e < NQ; ++e) {
+      const float4 qq = q4[e];
+      acc = fmaf(qq.x, kv[e].x, acc);
+      acc = fmaf(qq.y, kv[e].y, acc);
+      acc = fmaf(qq.z, kv[e].z, acc);
+      acc = fmaf(qq.w, kv[e].w, acc);
+    }
+    const float sc = acc * scale;
+    s_score[j] = sc;
+    mx = fmaxf(mx, sc);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) s_red[warp] = mx;
   __syncthreads();
   mx = s_red[0];
 #pragma unroll
-  for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, s_red[w]);
+  for (int w = 1; w < NW; ++w) mx = fmaxf(mx, s_red[w]);
   __syncthreads();
   // probabilities and their sum
   float sum = 0.f;
-  for (int j = threadIdx.x; j <= p; j += blockDim.x) {
+  for (int j = t; j <= p; j += kAttnThreads) {
     const float e = expf(s_score[j] - mx);
     s_score[j] = e;
     sum += e;
@@ -116,28 +130,28 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) s_red[warp] = sum;
-  __syncthreads();
+  __syncthreads();   // also publishes every s_score
   sum = 0.f;
 #pragma unroll
-  for (int w = 0; w < kAttnWarps; ++w) sum += s_red[w];
-  // o = sum_j p_j v_j: warp w takes keys w, w + 4, ...; lanes split the head dims
-  float acc[PER];
-#pragma unroll
-  for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-  for (int j = warp; j <= p; j += kAttnWarps) {
+  for (int w = 0; w < NW; ++w) sum += s_red[w];
+  // o = sum_j p_j v_j
+  const int cq = t % NQ, kg = t / NQ;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = kg; j <= p; j += KG) {
     const float pj = s_score[j];
-    const float* vr = vb + (int64_t)j * D + lane * PER;
-#pragma unroll
-    for (int e = 0; e < PER; ++e) acc[e] = fmaf(pj, vr[e], acc[e]);
+    const float4 v4 = reinterpret_cast<const float4*>(vb + (int64_t)j * D)[cq];
+    acc.x = fmaf(pj, v4.x, acc.x);
+    acc.y = fmaf(pj, v4.y, acc.y);
+    acc.z = fmaf(pj, v4.z, acc.z);
+    acc.w = fmaf(pj, v4.w, acc.w);
   }
-#pragma unroll
-  for (int e = 0; e < PER; ++e) s_o[warp][lane * PER + e] = acc[e];
+  reinterpret_cast<float4*>(&s_part[kg][0])[cq] = acc;
   __syncthreads();
   const float inv = 1.0f / sum;
-  for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+  for (int i = t; i < HD; i += kAttnThreads) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) v += s_o[w][i];
+    for (int g = 0; g < KG; ++g) v += s_part[g][i];
     v *= inv;
     O[b * o_ld + col + i] = out_tf32 ? tf32_rna(v) : v;
   }
@@ -334,6 +348,9 @@ WXX_EXPORT int wxx_decode_attention(float* O, int64_t o_ld, const float* q, cons
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(B >= 0 && H > 0 && max_len > 0, "wxx_decode_attention: bad sizes");
   WXX_REQUIRE(hd == 32 || hd == 64, "wxx_decode_attention: head dim %d not in {32, 64}", hd);
+  WXX_REQUIRE(!(reinterpret_cast<uintptr_t>(Kc) & 15) && !(reinterpret_cast<uintptr_t>(Vc) & 15) &&
+                  cache_bs % 4 == 0,
+              "wxx_decode_attention: the caches must be 16-byte aligned (float4 rows)");
   WXX_REQUIRE((int64_t)max_len * 4 <= 200 * 1024,
               "wxx_decode_attention: max_len %d exceeds the shared-memory score row", max_len);
   if (B == 0) return WXX_OK;
@@ -354,11 +371,11 @@ WXX_EXPORT int wxx_decode_attention(float* O, int64_t o_ld, const float* q, cons
     smem_set[which] = smem;
   }
   if (hd == 32) {
-    decode_attention_kernel<32><<<grid, kAttnWarps * 32, smem, wxx::stream()>>>(
+    decode_attention_kernel<32><<<grid, kAttnThreads, smem, wxx::stream()>>>(
         O, o_ld, q, k_new, v_new, qkv_ld, Kc, Vc, cache_bs, D, cur_len, max_len, scale, out_tf32,
         wxx::device_error_word());
   } else {
-    decode_attention_kernel<64><<<grid, kAttnWarps * 32, smem, wxx::stream()>>>(
+    decode_attention_kernel<64><<<grid, kAttnThreads, smem, wxx::stream()>>>(
         O, o_ld, q, k_new, v_new, qkv_ld, Kc, Vc, cache_bs, D, cur_len, max_len, scale, out_tf32,
         wxx::device_error_word());
   }

@@ -62,6 +62,11 @@ struct Arena {
   cudaGraphExec_t exec = nullptr;
   int64_t kernels = 0;                           // kernel launches recorded
   int64_t launches_at_begin = 0;
+  // Pool blocks released while this capture was open: a cudaFreeAsync then
+  // would be recorded into the graph (and is invalid for memory the graph did
+  // not allocate), and kernels recorded before the release may still read the
+  // block on every replay -- so they are freed when the graph is destroyed.
+  std::vector<void*> deferred;
 };
 std::vector<Arena*> g_arenas;                    // graphs alive (guarded by g.mu)
 Arena* g_capture = nullptr;                      // arena of the open capture
@@ -336,6 +341,10 @@ WXX_EXPORT int wxx_free(void* p) {
     g.live.erase(it);
     g.active_bytes -= (int64_t)sz;
     g.n_free++;
+    if (g_capture != nullptr) {
+      g_capture->deferred.push_back(p);
+      return WXX_OK;
+    }
   }
   WXX_CUDA_CHECK(cudaFreeAsync(p, wxx::stream()));
   return WXX_OK;
@@ -614,6 +623,8 @@ WXX_EXPORT int wxx_graph_destroy(void* handle) {
   cudaError_t e = cudaStreamSynchronize(wxx::stream());
   if (a->exec) cudaGraphExecDestroy(a->exec);
   cudaFree(a->base);
+  for (void* p : a->deferred) cudaFreeAsync(p, wxx::stream());
+  a->deferred.clear();
   {
     std::lock_guard<std::mutex> lk(g.mu);
     for (size_t i = 0; i < g_arenas.size(); ++i)

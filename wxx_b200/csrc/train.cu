@@ -173,9 +173,17 @@ __global__ void __launch_bounds__(kT) cce_kernel(float* __restrict__ loss, float
 
 // AdamW step (adamw.wgsl): m = b1 m + (1 - b1) g, v = b2 v + (1 - b2) g^2,
 // p -= lr (m / bc1 / (sqrt(v / bc2) + eps) + wd p).
+// bc_dev (when not NULL) holds {bc1, bc2} in device memory, written by
+// adamw_advance_kernel: a step recorded in a CUDA graph then uses each
+// replay's own bias corrections.
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
                              float* __restrict__ m, float* __restrict__ v, int64_t n, float lr,
-                             float b1, float b2, float eps, float wd, float bc1, float bc2) {
+                             float b1, float b2, float eps, float wd, float bc1, float bc2,
+                             const float* __restrict__ bc_dev) {
+  if (bc_dev != nullptr) {
+    bc1 = bc_dev[0];
+    bc2 = bc_dev[1];
+  }
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float pi = p[i], gi = g[i];
@@ -186,6 +194,14 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
     const float step = (mi / bc1) / (sqrtf(vi / bc2) + eps);
     p[i] = pi - lr * (step + wd * pi);
   }
+}
+
+// step += 1; bc = {1 - beta1^step, 1 - beta2^step} (double, stored as float:
+// the values nn/optimizer.py computes on the host).
+__global__ void adamw_advance_kernel(int* step, float* bc, double b1, double b2) {
+  const int t = ++step[0];
+  bc[0] = (float)(1.0 - pow(b1, (double)t));
+  bc[1] = (float)(1.0 - pow(b2, (double)t));
 }
 
 }  // namespace
@@ -275,7 +291,32 @@ WXX_EXPORT int wxx_adamw(float* p, const float* g, float* m, float* v, int64_t n
   WXX_REQUIRE(n >= 0, "wxx_adamw: negative size");
   if (n == 0) return WXX_OK;
   adamw_kernel<<<wxx::grid_for(n, kT), kT, 0, wxx::stream()>>>(p, g, m, v, n, lr, beta1, beta2,
-                                                               eps, weight_decay, bc1, bc2);
+                                                               eps, weight_decay, bc1, bc2,
+                                                               nullptr);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+// nn.AdamW's step with the bias corrections read from device memory
+// (bc[0] = bc1, bc[1] = bc2, from wxx_adamw_advance).
+WXX_EXPORT int wxx_adamw_device(float* p, const float* g, float* m, float* v, int64_t n, float lr,
+                                float beta1, float beta2, float eps, float weight_decay,
+                                const float* bc) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(n >= 0 && bc != nullptr, "wxx_adamw_device: negative size or no bias corrections");
+  if (n == 0) return WXX_OK;
+  adamw_kernel<<<wxx::grid_for(n, kT), kT, 0, wxx::stream()>>>(p, g, m, v, n, lr, beta1, beta2,
+                                                               eps, weight_decay, 1.f, 1.f, bc);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
+}
+
+// Advances an optimizer's device step counter (one int) and writes the
+// step's bias corrections {1 - beta1^t, 1 - beta2^t} into bc (two floats).
+WXX_EXPORT int wxx_adamw_advance(int* step, float* bc, double beta1, double beta2) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(step != nullptr && bc != nullptr, "wxx_adamw_advance: NULL pointer");
+  adamw_advance_kernel<<<1, 1, 0, wxx::stream()>>>(step, bc, beta1, beta2);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }

@@ -81,10 +81,10 @@ def masked_softmax(score, mask):
 
 def attention_supported(q, n_heads, mask=None):
     """True when ``attention`` can run the fused tcgen05 kernel for these
-    operands (TF32 mode, head dim 32 or 64, 16-byte aligned rows)."""
+    operands (TF32 or 3xTF32 mode, head dim 32 or 64, 16-byte aligned rows)."""
     from ._common import get_matmul_mode
 
-    if get_matmul_mode() != "tf32" or len(q.shape) != 3:
+    if get_matmul_mode() not in ("tf32", "3xtf32") or len(q.shape) != 3:
         return False
     D = q.shape[-1]
     if D % n_heads or D // n_heads not in (32, 64) or D % 4:
@@ -119,9 +119,11 @@ def attention(q, k, v, n_heads, mask=None, causal=False, scale=None, *, feeds_tf
     (B, Sq, D) in the same merged layout.  ``causal`` masks keys after the
     query position (what GPT2's -1e9 upper-triangular mask does); ``mask`` is
     an additive (Sq, Sk) view.  Same values as the unfused
-    matmul -> scale -> add mask -> softmax -> matmul chain up to rounding.
+    matmul -> scale -> add mask -> softmax -> matmul chain up to rounding:
+    TF32 products in tf32 mode, 3xTF32 (fp32-faithful) in 3xtf32 mode.
     ``feeds_tf32``: the result is read only by a TF32 product (the output
-    projection), so it is stored rounded to the nearest TF32 value."""
+    projection), so in tf32 mode it is stored rounded to the nearest TF32
+    value."""
     import math
 
     if len(q.shape) != 3 or len(k.shape) != 3 or len(v.shape) != 3:
@@ -146,8 +148,14 @@ def attention(q, k, v, n_heads, mask=None, causal=False, scale=None, *, feeds_tf
         if tuple(mask.shape) != (Sq, Sk):
             raise ValueError(f"attention: mask shape {mask.shape} != {(Sq, Sk)}")
         mptr, mld = mask.ptr, mask.stride[0]
+    from ._common import get_matmul_mode
+
+    mode = get_matmul_mode()
+    if mode not in ("tf32", "3xtf32"):
+        raise ValueError(f"attention: the fused kernel runs in tf32 or 3xtf32 mode, not {mode!r}")
     out = empty((B, Sq, D), "f32", q.requires_grad or k.requires_grad or v.requires_grad)
     check(F.wxx_attention(out.buffer.ptr, q.ptr, k.ptr, v.ptr, B, n_heads, Sq, Sk, hd, q_ld, k_ld, D,
-                          float(scale), mptr, mld, int(bool(causal)), int(bool(feeds_tf32))),
+                          float(scale), mptr, mld, int(bool(causal)),
+                          int(bool(feeds_tf32) and mode == "tf32"), int(mode == "3xtf32")),
           "attention")
     return out

@@ -93,6 +93,35 @@ def conv2d_nhwc_supported(cin, cout, ho, wo):
     return ho % rows == 0 if ho >= rows else rows % ho == 0
 
 
+def resnet_stem(tensor1, W, bias=None, *, bn=None, relu=True):
+    """ResNet's stem in one launch (nn/resnet.py:31-79): ``conv2d`` 7x7 /
+    stride 2 / pad 3 to 64 channels, eval batchnorm (``bn`` = (running_mean,
+    running_var, gamma, beta, eps) or None), ReLU, ``maxpool2d`` 3x3 / stride 2
+    / pad 1, returned channels-last (B, Hp, Wp, 64) -- the same values as those
+    ops followed by ``permute(0, 2, 3, 1)``.  None when the shapes are outside
+    the kernel's (1..4 input channels, H and W up to 32)."""
+    x = dense(tensor1)
+    w = dense(W)
+    if len(x.shape) != 4 or len(w.shape) != 4:
+        return None
+    B, Cin, H, Wd = x.shape
+    if tuple(w.shape) != (64, Cin, 7, 7) or not (1 <= Cin <= 4 and 1 <= H <= 32 and 1 <= Wd <= 32):
+        return None
+    if bias is not None and tuple(bias.shape) != (64,):
+        return None
+    Ho, Wo = (H - 1) // 2 + 1, (Wd - 1) // 2 + 1
+    Hp, Wp = (Ho - 1) // 2 + 1, (Wo - 1) // 2 + 1
+    out = empty((B, Hp, Wp, 64), "f32")
+    if bn is not None:
+        rm, rv, g, b, eps = bn
+        ptrs = [dense(t).ptr for t in (rm, rv, g, b)]
+    else:
+        ptrs, eps = [None] * 4, 0.0
+    check(F.wxx_resnet_stem(out.buffer.ptr, x.ptr, w.ptr, None if bias is None else dense(bias).ptr,
+                            *ptrs, float(eps), int(bool(relu)), B, Cin, H, Wd), "resnet_stem")
+    return out
+
+
 def conv_weight_pack(weights, outs):
     """Reorders each (Cout, Cin, KH, KW) weight in ``weights`` into the dense
     (Cout, KH, KW, Cin) tensor at the same index of ``outs`` -- the K order

@@ -23,7 +23,16 @@ import ctypes
 from .backend import device as _dev
 from .backend.lib import F, check
 
-__all__ = ["CapturedGraph", "capture"]
+__all__ = ["CapturedGraph", "capture", "capturing"]
+
+_CAPTURING = [False]
+
+
+def capturing():
+    """True while a step is being recorded (host-side checks that would
+    synchronise with the device are skipped then; the kernels' own checks
+    still report through the device error word)."""
+    return _CAPTURING[0]
 
 
 def _stats():
@@ -66,11 +75,14 @@ class CapturedGraph:
         h = ctypes.c_void_p()
         check(F.wxx_graph_begin(int(arena_bytes), ctypes.byref(h)), "wxx_graph_begin")
         ok = False
+        _CAPTURING[0] = True
         try:
             out = fn(*args, **kwargs)
+            _CAPTURING[0] = False
             check(F.wxx_graph_end(h), "wxx_graph_end")
             ok = True
         finally:
+            _CAPTURING[0] = False
             if not ok:
                 out = None
                 F.wxx_graph_destroy(h)

@@ -2,8 +2,11 @@
 ``module.parameters()`` (``("", parameter)`` pairs) and stepping the
 parameters in place from their ``.grad``."""
 
+import numpy as np
+
 from .. import functional
 from ..Tensor import Tensor
+from ..functional.utils import mark_written
 
 
 class Optimizer:
@@ -36,10 +39,15 @@ class SGD(Optimizer):
 
 
 class AdamW(Optimizer):
-    """Adam with decoupled weight decay, one ``wxx_adamw`` launch per
+    """Adam with decoupled weight decay, one ``wxx_adamw_device`` launch per
     parameter: ``m = b1 m + (1 - b1) g``, ``v = b2 v + (1 - b2) g^2``,
     ``w -= lr (m / bc1 / (sqrt(v / bc2) + eps) + weight_decay w)`` with the bias
-    corrections bc = 1 - beta^t (nn/optimizer.py:38-84, adamw.wgsl)."""
+    corrections bc = 1 - beta^t (nn/optimizer.py:38-84, adamw.wgsl).
+
+    The step count t and the bias corrections live in device memory and are
+    advanced by a kernel at the start of each step, so a training step
+    recorded with ``wxx_b200.graph.capture`` replays as step t + 1, t + 2, ...
+    (``step_count`` counts the host calls)."""
 
     def __init__(self, parameters, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-7,
                  weight_decay=1e-4):
@@ -52,14 +60,23 @@ class AdamW(Optimizer):
         self.step_count = 0
         self.state = [{"exp_avg": Tensor(p.shape, value=0.0),
                        "exp_avg_sq": Tensor(p.shape, value=0.0)} for _, p in self.params]
+        self._t = Tensor((1,), value=0, dtype="u32")       # device step count
+        self._bc = Tensor((2,), value=1.0)                 # device {bc1, bc2}
 
     def step(self):
+        from ..backend.lib import F, check
+
         self.step_count += 1
-        bc1 = 1.0 - self.beta1 ** self.step_count
-        bc2 = 1.0 - self.beta2 ** self.step_count
+        check(F.wxx_adamw_advance(self._t.ptr, self._bc.ptr, self.beta1, self.beta2),
+              "adamw_advance")
         for (_, w), st in zip(self.params, self.state):
             if w.grad is None:
                 continue
-            functional.adamw(w, functional.contiguous(w.grad), st["exp_avg"], st["exp_avg_sq"],
-                             self.step_count, self.lr, self.beta1, self.beta2, self.eps,
-                             self.weight_decay, bc1, bc2)
+            g = functional.contiguous(w.grad)
+            if tuple(g.shape) != tuple(w.shape):
+                raise ValueError(f"adamw: grad shape {tuple(g.shape)} != {tuple(w.shape)}")
+            check(F.wxx_adamw_device(w.ptr, g.ptr, st["exp_avg"].ptr, st["exp_avg_sq"].ptr,
+                                     int(np.prod(w.shape)), self.lr, self.beta1, self.beta2,
+                                     self.eps, self.weight_decay, self._bc.ptr), "adamw")
+            for t in (w, st["exp_avg"], st["exp_avg_sq"]):
+                mark_written(t)

@@ -134,18 +134,37 @@ class ResNet18(Module):
         object.__setattr__(self, "_nhwc_packed", entry)
         return {id(c): b for c, b in zip(convs, bufs)}
 
+    def _stem_nhwc(self, x):
+        """conv1 -> bn1 -> relu -> maxpool as one channels-last launch, or None
+        when this stem is not the 7x7 / 2 -> 3x3 / 2 form the kernel fuses."""
+        c, mp = self.conv1, self.maxpool
+        if (tuple(c.kernel) != (7, 7) or tuple(c.stride) != (2, 2) or tuple(c.padding) != (3, 3)
+                or tuple(c.dilation) != (1, 1) or tuple(mp.kernel) != (3, 3)
+                or tuple(mp.stride) != (2, 2) or tuple(mp.padding) != (1, 1)):
+            return None
+        bn = self.bn1
+        return functional.resnet_stem(x, c.W, c.bias, relu=True,
+                                      bn=(bn.running_mean, bn.running_std, bn.weight, bn.bias,
+                                          1e-5))
+
     def forward(self, x):
         if context.MODE != 0:
-            out = self.maxpool(_conv_bn(x, self.conv1, self.bn1, relu=True))
             blocks = [blk for layer in (self.layer1, self.layer2, self.layer3, self.layer4)
                       for blk in layer._modules.values()]
-            shape = (out.shape[0], out.shape[2], out.shape[3], out.shape[1])
+            ho, wo = _conv_out_hw(self.conv1, x.shape[2], x.shape[3])
+            (kh, kw), (sh, sw), (ph, pw) = self.maxpool.kernel, self.maxpool.stride, \
+                self.maxpool.padding
+            shape = (x.shape[0], (ho + 2 * ph - kh) // sh + 1, (wo + 2 * pw - kw) // sw + 1,
+                     self.conv1.W.shape[0])
             for blk in blocks:
                 shape = blk.nhwc_shape(shape) if shape is not None else None
             if shape is not None:
                 # channels-last from the first block to the pooling: the
                 # convolutions' A operands then load as TMA boxes
-                h = out.permute(0, 2, 3, 1).contiguous()
+                h = self._stem_nhwc(x)
+                if h is None:
+                    out = self.maxpool(_conv_bn(x, self.conv1, self.bn1, relu=True))
+                    h = out.permute(0, 2, 3, 1).contiguous()
                 packed = self._pack_nhwc_weights(blocks)
                 for blk in blocks:
                     h = blk.forward_nhwc(h, packed)
@@ -153,6 +172,7 @@ class ResNet18(Module):
                 pooled = (h.reshape((B, C)) if H * W == 1
                           else functional.mean(h.reshape((B, H * W, C)), axis=1))
                 return self.fc(pooled)
+            out = self.maxpool(_conv_bn(x, self.conv1, self.bn1, relu=True))
         else:
             out = self.maxpool(self.bn1(self.conv1(x)).relu())
         out = self.layer1(out)
