@@ -1333,7 +1333,9 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(
   extern __shared__ float dsm[];
   const int Hp = H + 2 * ph, Wp = W + 2 * pw;
   float* img = dsm;                              // Cin x Hp x Wp
-  float* wts = dsm + Cin * Hp * Wp;              // taps x kDirectCG (channel fastest)
+  // taps x kDirectCG (channel fastest), read as float4: the image size is
+  // rounded up to 4 floats so the weights start 16-byte aligned
+  float* wts = dsm + ((Cin * Hp * Wp + 3) & ~3);
   const int groups = (Cout + kDirectCG - 1) / kDirectCG;
   const int b = blockIdx.x / groups, n0 = (blockIdx.x - b * groups) * kDirectCG;
   const int taps = Cin * KH * KW;
@@ -1427,7 +1429,8 @@ int conv2d_impl(float* Y, const float* X, const float* Wt, const float* bias, in
   WXX_REQUIRE(Mrows < (int64_t(1) << 31) && K < (int64_t(1) << 31), "wxx_conv2d: too large");
   if (Mrows == 0) return WXX_OK;
   {
-    const size_t smem = ((size_t)Cin * (H + 2 * ph) * (W + 2 * pw) + (size_t)K * kDirectCG) * 4;
+    const size_t smem =
+        ((((size_t)Cin * (H + 2 * ph) * (W + 2 * pw) + 3) & ~size_t(3)) + (size_t)K * kDirectCG) * 4;
     if (Cin <= 4 && smem <= 96 * 1024 && B <= 65535 * 8) {
       static bool attr = false;
       if (!attr) {

@@ -38,6 +38,7 @@ from .convolution import (
     conv2d_bn,
     conv2d_nhwc,
     conv_weight_pack,
+    resnet_stem,
     conv2d_nhwc_supported,
     conv2ddw,
     conv2ddx,
