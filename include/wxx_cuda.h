@@ -207,6 +207,15 @@ int wxx_matmul(float* C, const float* A, const float* B, const float* bias, int6
 int wxx_linear(float* C, const float* A, const float* B, const float* bias,
                const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
                int64_t ldb, int trans_b, int act, float alpha, int mode);
+/* The decode step's LayerNorm -> linear (nn/gpt.py: ln1 -> q/k/v, ln2 -> fc1, ln_f -> head) in
+ * one launch for 1 <= M <= 32 rows: C (M, N) = act(LayerNorm(A) @ W^T + bias) + residual with
+ * W (N, K) K-major, gamma / beta (K), act 0 / 1 (GELU), round_out = 1 stores C rounded to the
+ * nearest TF32 value; exact fp32.  WXX_E_UNSUPPORTED (nothing enqueued) outside N >= 64,
+ * K >= 128, K / lda / ldw multiples of 4, 16-byte aligned A, W, gamma, beta. */
+int wxx_ln_linear(float* C, const float* A, int64_t lda, const float* gamma, const float* beta,
+                  float eps, const float* W, int64_t ldw, const float* bias,
+                  const float* residual, int64_t M, int64_t N, int64_t K, int act,
+                  int round_out);
 /* nn/hyena.py:242 out_proj(z.transpose(1, 2)): wxx_linear over a batch whose A operand is a
  * strided view, A[b] at A + b*a_bs with row stride lda, transposed when trans_a (A[b] stored
  * (K, M)), B shared by the batch, residual (batch, M, N) dense or NULL; act 0 or 1. */

@@ -78,3 +78,41 @@ def test_rows_gemv_batched_rows_fold(rng):
     got = F.linear(up(x), up(w), transpose_weight=True).numpy()
     ref = x.astype(np.float64) @ w.astype(np.float64).T
     assert rel(got, ref) < 2e-6
+
+
+def _ln64(x, g, b):
+    x = x.astype(np.float64)
+    mu = x.mean(-1, keepdims=True)
+    var = ((x - mu) ** 2).mean(-1, keepdims=True)
+    return (x - mu) / np.sqrt(var + 1e-5) * g + b
+
+
+@pytest.mark.parametrize("M,N,K,act,res", [(1, 64, 128, None, False), (8, 3072, 1024, None, False),
+                                           (8, 4096, 1024, "gelu", False),
+                                           (5, 1000, 512, None, True), (32, 256, 256, "gelu", True),
+                                           (64, 256, 256, None, True)])
+def test_ln_linear_against_float64(M, N, K, act, res, rng):
+    """LayerNorm -> linear in one few-rows launch (the decode step's ln1 ->
+    q/k/v, ln2 -> fc1, ln_f -> head); 64 rows take the two-launch path."""
+    F = _F()
+    x = (rng.standard_normal((M, K)) * 3 + 1).astype(np.float32)
+    g = rng.standard_normal(K).astype(np.float32)
+    b = rng.standard_normal(K).astype(np.float32)
+    w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    r = rng.standard_normal((M, N)).astype(np.float32) if res else None
+    import wxx_b200 as wxx
+
+    wxx.set_matmul_mode("3xtf32")
+    try:
+        got = F.ln_linear(up(x), up(g), up(b), up(w), up(bias), activation=act,
+                          residual=None if r is None else up(r)).numpy()
+    finally:
+        wxx.set_matmul_mode("tf32")
+    ref = _ln64(x, g, b) @ w.astype(np.float64).T + bias
+    if act == "gelu":
+        ref = train._gelu(ref)
+    if r is not None:
+        ref = ref + r
+    assert got.shape == (M, N)
+    assert rel(got, ref) < 1e-5, rel(got, ref)

@@ -514,33 +514,60 @@ __global__ void __launch_bounds__(256) skinny_gemm_kernel(
 
 // ------------------------------------------------------------ few rows (decode)
 
-// C (M <= 32 rows) = act(alpha * A @ W^T + bias) + res for a K-major weight W
+// C (M <= 32 rows) = act(alpha * A' @ W^T + bias) + res for a K-major weight W
 // (N, K): the decode step's products, where the weight is read once and each
 // of its values meets only M activations, so the time is the weight stream.
 // A tile-based GEMM gives such a product N / 256 CTAs; here a CTA takes
-// kGemvGroups x kGemvCols columns and its warps split K (kGemvKs ways), so
-// N = 1024 already spreads over 128 CTAs.  Per warp: kGemvCols weight rows
-// and 8 activation rows as float4 loads along K, 32 fp32 accumulators (column
-// c, row r at index 8c + r), reduced across the lanes by a halving exchange
-// (31 shuffles; lane l ends with the sum for index l), then over the K-split
-// warps in fixed order through shared memory.  Exact fp32 products; the
-// epilogue is the tensor-core path's (alpha, bias, GELU, residual, TF32
-// rounding of the stored value).
+// kGemvCols columns and its 8 warps split K, so N = 1024 spreads over 256
+// CTAs with every warp's weight loads in flight at once.  Per warp:
+// kGemvCols weight rows and 8 activation rows as float4 loads along K, 32
+// fp32 accumulators (column c, row r at index 8c + r), reduced across the
+// lanes by a halving exchange (31 shuffles; lane l ends with the sum for
+// index l), then over the K-split warps in fixed order through shared
+// memory.  Exact fp32 products; the epilogue is the tensor-core path's
+// (alpha, bias, GELU, residual, TF32 rounding of the stored value).
+// LN: A' = LayerNorm(A) over its K entries (gamma, beta; the LayerNorm
+// kernel's two-pass statistics and expression), computed by every CTA for
+// the rows it needs -- the block's norm and the next product in one launch.
 constexpr int kGemvCols = 4;
-constexpr int kGemvKs = 4;
-constexpr int kGemvGroups = 2;
+constexpr int kGemvWarps = 8;
 constexpr int kGemvMaxRows = 32;
 
-__global__ void __launch_bounds__(256) rows_gemv_kernel(
+template <bool LN>
+__global__ void __launch_bounds__(kGemvWarps * 32, 2) rows_gemv_kernel(
     float* __restrict__ C, const float* __restrict__ A, int64_t lda, const float* __restrict__ W,
     int64_t ldw, const float* __restrict__ bias, int M, int N, int K, float alpha, int act,
-    const float* __restrict__ res, int round_out) {
-  __shared__ float part[kGemvGroups][kGemvKs][32];
+    const float* __restrict__ res, int round_out, const float* __restrict__ ln_g,
+    const float* __restrict__ ln_b, float ln_eps) {
+  __shared__ float part[kGemvWarps][32];
+  __shared__ float s_mu[kGemvMaxRows], s_inv[kGemvMaxRows];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cg = warp / kGemvKs, ks = warp % kGemvKs;
-  const int n0 = (blockIdx.x * kGemvGroups + cg) * kGemvCols;
-  const int kq = ((K + kGemvKs * 128 - 1) / (kGemvKs * 128)) * 128;
-  const int kb = ks * kq, ke = min(K, kb + kq);
+  const int n0 = blockIdx.x * kGemvCols;
+  const int kq = ((K + kGemvWarps * 128 - 1) / (kGemvWarps * 128)) * 128;
+  const int kb = warp * kq, ke = min(K, kb + kq);
+  if (LN) {
+    for (int m = warp; m < M; m += kGemvWarps) {
+      const float* ar = A + (int64_t)m * lda;
+      float sum = 0.f;
+      for (int k = lane; k < K; k += 32) sum += ar[k];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float mean = sum / (float)K;
+      float ss = 0.f;
+      for (int k = lane; k < K; k += 32) {
+        const float d = ar[k] - mean;
+        ss += d * d;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float var = fmaxf(0.f, ss / (float)K);
+      if (lane == 0) {
+        s_mu[m] = mean;
+        s_inv[m] = var > 0.f ? rsqrtf(var + ln_eps) : 0.f;
+      }
+    }
+    __syncthreads();
+  }
   const float* wr[kGemvCols];
   bool wv[kGemvCols];
 #pragma unroll
@@ -553,15 +580,28 @@ __global__ void __launch_bounds__(256) rows_gemv_kernel(
     float acc[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll 2
     for (int k = kb + lane * 4; k < ke; k += 128) {
       float4 w4[kGemvCols];
 #pragma unroll
       for (int c = 0; c < kGemvCols; ++c)
         w4[c] = wv[c] ? __ldg(reinterpret_cast<const float4*>(wr[c] + k)) : zero;
+      float4 g4 = zero, b4 = zero;
+      if (LN) {
+        g4 = __ldg(reinterpret_cast<const float4*>(ln_g + k));
+        b4 = __ldg(reinterpret_cast<const float4*>(ln_b + k));
+      }
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
-        const float4 a = (m0 + r < M)
+        float4 a = (m0 + r < M)
             ? __ldg(reinterpret_cast<const float4*>(A + (int64_t)(m0 + r) * lda + k)) : zero;
+        if (LN && m0 + r < M) {
+          const float mu = s_mu[m0 + r], inv = s_inv[m0 + r];
+          a.x = (a.x - mu) * inv * g4.x + b4.x;
+          a.y = (a.y - mu) * inv * g4.y + b4.y;
+          a.z = (a.z - mu) * inv * g4.z + b4.z;
+          a.w = (a.w - mu) * inv * g4.w + b4.w;
+        }
 #pragma unroll
         for (int c = 0; c < kGemvCols; ++c) {
           float t = acc[8 * c + r];
@@ -585,12 +625,12 @@ __global__ void __launch_bounds__(256) rows_gemv_kernel(
         acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
       }
     }
-    part[cg][ks][lane] = acc[0];
+    part[warp][lane] = acc[0];
     __syncthreads();
-    if (ks == 0) {
-      float v = part[cg][0][lane];
+    if (warp == 0) {
+      float v = part[0][lane];
 #pragma unroll
-      for (int q = 1; q < kGemvKs; ++q) v += part[cg][q][lane];
+      for (int q = 1; q < kGemvWarps; ++q) v += part[q][lane];
       const int n = n0 + (lane >> 3), m = m0 + (lane & 7);
       if (n < N && m < M) {
         v = bias != nullptr ? v * alpha + __ldg(bias + n) : v * alpha;
@@ -602,6 +642,29 @@ __global__ void __launch_bounds__(256) rows_gemv_kernel(
     }
     __syncthreads();
   }
+}
+
+// True when rows_gemv_kernel takes the product (see its comment).
+bool gemv_fits(int64_t rows, int64_t N, int64_t K, int64_t lda, int64_t ldb, const void* A,
+               const void* B) {
+  return rows >= 1 && rows <= kGemvMaxRows && N >= 64 && K >= 128 && K % 4 == 0 &&
+         lda % 4 == 0 && ldb % 4 == 0 && (lda >= K || rows == 1) &&
+         !(reinterpret_cast<uintptr_t>(A) & 15) && !(reinterpret_cast<uintptr_t>(B) & 15) &&
+         N < (int64_t(1) << 31) / kGemvCols;
+}
+
+int launch_gemv(float* C, const float* A, int64_t lda, const float* W, int64_t ldw,
+                const float* bias, int rows, int N, int K, float alpha, int act, const float* res,
+                int round_out, const float* ln_g, const float* ln_b, float ln_eps) {
+  const unsigned grid = (unsigned)((N + kGemvCols - 1) / kGemvCols);
+  if (ln_g != nullptr)
+    rows_gemv_kernel<true><<<grid, kGemvWarps * 32, 0, wxx::stream()>>>(
+        C, A, lda, W, ldw, bias, rows, N, K, alpha, act, res, round_out, ln_g, ln_b, ln_eps);
+  else
+    rows_gemv_kernel<false><<<grid, kGemvWarps * 32, 0, wxx::stream()>>>(
+        C, A, lda, W, ldw, bias, rows, N, K, alpha, act, res, round_out, nullptr, nullptr, 0.f);
+  WXX_LAUNCH_CHECK();
+  return WXX_OK;
 }
 
 // 64x64 output tile, K-step 16, 4x4 outputs per thread, fp32 FMA.
@@ -698,16 +761,11 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   // weight-streaming kernel.  Batches whose A rows are consecutive and share
   // the weight fold into rows.
   const int64_t rows_all = batch * M;
-  if (rows_all <= kGemvMaxRows && trans_a == 0 && trans_b != 0 && act <= 1 && bias_mode <= 1 &&
-      (batch == 1 || (a_bs == M * lda && b_bs == 0)) && N >= 64 && K >= 128 && K % 4 == 0 &&
-      lda % 4 == 0 && ldb % 4 == 0 && !(reinterpret_cast<uintptr_t>(A) & 15) &&
-      !(reinterpret_cast<uintptr_t>(B) & 15) && (lda >= K || rows_all == 1)) {
-    const int64_t per_cta = kGemvGroups * kGemvCols;
-    rows_gemv_kernel<<<(unsigned)((N + per_cta - 1) / per_cta), 256, 0, s>>>(
-        C, A, lda, B, ldb, bias_mode == 1 ? bias : nullptr, (int)rows_all, (int)N, (int)K, alpha,
-        act, res, round_out);
-    WXX_LAUNCH_CHECK();
-    return WXX_OK;
+  if (trans_a == 0 && trans_b != 0 && act <= 1 && bias_mode <= 1 &&
+      (batch == 1 || (a_bs == M * lda && b_bs == 0)) &&
+      gemv_fits(rows_all, N, K, lda, ldb, A, B)) {
+    return launch_gemv(C, A, lda, B, ldb, bias_mode == 1 ? bias : nullptr, (int)rows_all, (int)N,
+                       (int)K, alpha, act, res, round_out, nullptr, nullptr, 0.f);
   }
   // Skinny products with a long K (ResNet's 256 x 10 x 512 classifier: two
   // gathered tensor-core tiles walking 16 K-blocks) run one warp per output
@@ -905,6 +963,31 @@ WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float*
   if (M * N == 0) return WXX_OK;
   return matmul_impl(C, A, B, bias, 1, M, N, K, 0, 0, lda, ldb, 0, trans_b, bias ? 1 : 0, alpha,
                      mode, act, residual);
+}
+
+// A few rows through LayerNorm and a linear layer in one launch (the decode
+// step's ln -> q/k/v, ln2 -> fc1 and ln_f -> LM head):
+//   C (M, N dense) = act(LayerNorm(A) @ W^T + bias) + residual
+// LayerNorm over A's K entries per row (row stride lda) with gamma / beta (K)
+// and eps; W (N, K) K-major (row stride ldw); bias (N) or NULL; residual
+// (M, N) or NULL; act 0 or 1 (GELU); round_out = 1 stores C rounded to the
+// nearest TF32 value.  Exact fp32.  Returns WXX_E_UNSUPPORTED (nothing
+// enqueued) unless 1 <= M <= 32, N >= 64, K >= 128 with K, lda, ldw multiples
+// of 4 and A, W, gamma, beta 16-byte aligned.
+WXX_EXPORT int wxx_ln_linear(float* C, const float* A, int64_t lda, const float* gamma,
+                             const float* beta, float eps, const float* W, int64_t ldw,
+                             const float* bias, const float* residual, int64_t M, int64_t N,
+                             int64_t K, int act, int round_out) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(gamma != nullptr && beta != nullptr && act >= 0 && act <= 1,
+              "wxx_ln_linear: gamma / beta missing or act %d not in {0, 1}", act);
+  if (!gemv_fits(M, N, K, lda, ldw, A, W) || (reinterpret_cast<uintptr_t>(gamma) & 15) ||
+      (reinterpret_cast<uintptr_t>(beta) & 15)) {
+    wxx::set_error("wxx_ln_linear: shape or alignment outside the few-rows kernel");
+    return WXX_E_UNSUPPORTED;
+  }
+  return launch_gemv(C, A, lda, W, ldw, bias, (int)M, (int)N, (int)K, 1.0f, act, residual,
+                     round_out ? 1 : 0, gamma, beta, eps);
 }
 
 // Linear projection followed by a depthwise short causal convolution along

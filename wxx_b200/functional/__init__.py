@@ -108,6 +108,7 @@ from .utils import (
     from_numpy,
     from_tensor,
     linear,
+    ln_linear,
     linear_short_conv,
     transpose_stack,
     linspace,

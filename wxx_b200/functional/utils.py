@@ -327,6 +327,45 @@ def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_we
 _E_UNSUPPORTED = -4
 
 
+def ln_linear(x, gamma, beta, weight, bias=None, *, activation=None, residual=None,
+              feeds_tf32=False, eps=1e-5):
+    """``linear(LayerNorm(x), weight, bias, ...)`` with ``weight`` given as
+    (N, K) (``transpose_weight=True`` layout) and the LayerNorm over x's last
+    axis (``gamma``, ``beta``): for a few rows (at most 32, the decode step)
+    one launch normalises the rows and streams the weight; otherwise, or for
+    shapes that kernel does not take, the LayerNorm kernel and ``linear``."""
+    from .normalization import meanvarnorm
+
+    a = dense(x)
+    K = a.shape[-1]
+    w = dense(weight)
+    N = w.shape[0]
+    M = int(math.prod(a.shape[:-1])) if len(a.shape) > 1 else 1
+    mode = matmul_mode_code()
+    if (activation in (None, "gelu") and len(w.shape) == 2 and w.shape[1] == K
+            and tuple(gamma.shape) == (K,) and tuple(beta.shape) == (K,) and mode in (0, 1, 2)
+            and 1 <= M <= 32):
+        out_shape = list(a.shape[:-1]) + [N]
+        if residual is not None and list(residual.shape) != out_shape:
+            raise ValueError(f"ln_linear: residual {tuple(residual.shape)} is not {out_shape}")
+        if bias is not None and tuple(bias.shape) != (N,):
+            raise ValueError(f"ln_linear: bias {tuple(bias.shape)} is not ({N},)")
+        out = empty(out_shape, "f32")
+        g, bt = dense(gamma), dense(beta)
+        b = dense(bias) if bias is not None else None
+        r = dense(residual) if residual is not None else None
+        st = F.wxx_ln_linear(out.buffer.ptr, a.ptr, K, g.ptr, bt.ptr, float(eps), w.ptr, K,
+                             None if b is None else b.ptr, None if r is None else r.ptr, M, N, K,
+                             _ACTIVATIONS[activation], int(bool(feeds_tf32) and mode == 0))
+        if st != _E_UNSUPPORTED:
+            check(st, "ln_linear")
+            return out
+    axis = len(x.shape) - 1
+    h = meanvarnorm(x, gamma, beta, axis, feeds_tf32=True)[0]
+    return linear(h, weight, bias, activation=activation, residual=residual,
+                  transpose_weight=True, feeds_tf32=feeds_tf32)
+
+
 def transpose_stack(out, weights, *, round_tf32=False):
     """Writes the transposes of ``weights`` (n <= 8 dense-able (K, N) tensors
     of one shape) stacked along rows into the dense (n * N, K) tensor ``out``

@@ -88,7 +88,10 @@ def _decode_step(model, state, temperature, top_k):
                              model.vocab_size, model.max_len), "decode_embed")
     for block, cache in zip(model.blocks, state.caches):
         h = block.decode(h, cache, state.cur_len, model.max_len)
-    logits = model.head(model.ln_f.forward_into_gemm(h))
+    if hasattr(model.head, "forward_ln"):
+        logits = model.head.forward_ln(h, model.ln_f)       # ln_f and the head in one launch
+    else:
+        logits = model.head(model.ln_f.forward_into_gemm(h))
     _sample(model, state, logits, temperature, top_k)
     return logits
 

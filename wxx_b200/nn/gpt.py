@@ -64,11 +64,16 @@ class GPT2Block(Module):
     def decode(self, x, kv_cache, cur_len, max_len):
         """The block for one new position per sequence, ``x`` (batch, d_model)
         (inference mode; see ``MultiHeadAttention.decode``)."""
-        h = self.attn.decode(self.ln1.forward_into_gemm(x), kv_cache, cur_len, max_len,
-                             residual=x)
+        h = self.attn.decode(x, kv_cache, cur_len, max_len, residual=x, ln=self.ln1)
         fc1, act, fc2 = self.mlp._modules.values()
         if isinstance(fc1, Linear) and isinstance(act, GELU) and isinstance(fc2, Linear):
-            return self._mlp_inference(h)
+            # ln2 -> fc1 + GELU in one few-rows launch, fc2 + residual in another
+            rnd = functional.get_matmul_mode() == "tf32"
+            u = functional.ln_linear(h, self.ln2.weightg, self.ln2.weightb,
+                                     kmajor_weight(self, "_fc1_t", [fc1], rnd), fc1.bias,
+                                     activation="gelu", feeds_tf32=True)
+            return functional.linear(u, kmajor_weight(self, "_fc2_t", [fc2], rnd), fc2.bias,
+                                     residual=h, transpose_weight=True)
         return h + self.mlp(self.ln2(h))
 
 

@@ -500,7 +500,7 @@ class MultiHeadAttention(Module):
             functional.assign(kv_cache[0].narrow(1, 0, seq), k)
             functional.assign(kv_cache[1].narrow(1, 0, seq), v)
 
-    def decode(self, x, kv_cache, cur_len, max_len, residual=None):
+    def decode(self, x, kv_cache, cur_len, max_len, residual=None, ln=None):
         """One generation step for the newest position of each sequence.
 
         ``x`` (batch, d_model): the block input of that position; ``kv_cache``
@@ -510,6 +510,8 @@ class MultiHeadAttention(Module):
         every step and can be replayed from one CUDA graph).  The position's
         key and value are appended to the caches and its query attends over
         positions 0..cur_len-1 (``wxx_decode_attention``, exact fp32).
+        ``ln``: a LayerNorm applied to ``x`` first (fused into the q/k/v
+        product when the projections have no bias).
         Returns ``residual + out(attention)`` (batch, d_model)."""
         from ..backend.lib import F as _F, check as _check
 
@@ -517,10 +519,15 @@ class MultiHeadAttention(Module):
         if self.q.bias is None and self.k.bias is None and self.v.bias is None:
             w = kmajor_weight(self, "_qkv_t", [self.q, self.k, self.v],
                               round_tf32=functional.get_matmul_mode() == "tf32")
-            qkv = functional.linear(x, w, transpose_weight=True)
+            if ln is not None:
+                qkv = functional.ln_linear(x, ln.weightg, ln.weightb, w)
+            else:
+                qkv = functional.linear(x, w, transpose_weight=True)
             qp, kp, vp, ld = qkv.ptr, qkv.ptr + 4 * D, qkv.ptr + 8 * D, 3 * D
             keep = (qkv,)
         else:
+            if ln is not None:
+                x = ln.forward_into_gemm(x)
             q, k, v = self.q(x), self.k(x), self.v(x)
             qp, kp, vp, ld = q.ptr, k.ptr, v.ptr, D
             keep = (q, k, v)
@@ -619,6 +626,14 @@ class TiedLinear(Module):
     def __init__(self, embedding):
         super().__init__()
         object.__setattr__(self, "_embedding", embedding)
+
+    def forward_ln(self, x, ln):
+        """``forward(ln(x))`` for a few rows (generation's decode step): the
+        LayerNorm and the head product in one launch."""
+        w = self._embedding.weight
+        if context.MODE != 0 and functional.get_matmul_mode() == "tf32":
+            w = tf32_weight(self, "_w_tf32", w)
+        return functional.ln_linear(x, ln.weightg, ln.weightb, w)
 
     def forward(self, x):
         w = self._embedding.weight
