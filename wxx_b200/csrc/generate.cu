@@ -137,14 +137,24 @@ __global__ void __launch_bounds__(kAttnThreads)
   // o = sum_j p_j v_j
   const int cq = t % NQ, kg = t / NQ;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = kg; j <= p; j += KG) {
+  auto pv_add = [&](int j, const float4& v4) {
     const float pj = s_score[j];
-    const float4 v4 = reinterpret_cast<const float4*>(vb + (int64_t)j * D)[cq];
     acc.x = fmaf(pj, v4.x, acc.x);
     acc.y = fmaf(pj, v4.y, acc.y);
     acc.z = fmaf(pj, v4.z, acc.z);
     acc.w = fmaf(pj, v4.w, acc.w);
+  };
+  // four value rows in flight per thread, then one at a time for the rest
+  int j = kg;
+  for (; j + 3 * KG <= p; j += 4 * KG) {
+    float4 v4[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      v4[u] = reinterpret_cast<const float4*>(vb + (int64_t)(j + u * KG) * D)[cq];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) pv_add(j + u * KG, v4[u]);
   }
+  for (; j <= p; j += KG) pv_add(j, reinterpret_cast<const float4*>(vb + (int64_t)j * D)[cq]);
   reinterpret_cast<float4*>(&s_part[kg][0])[cq] = acc;
   __syncthreads();
   const float inv = 1.0f / sum;
