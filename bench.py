@@ -329,6 +329,13 @@ class ClockSampler:
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200", "-i", str(self.gpu), "-f", self.path],
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            # nvidia-smi takes a moment to start: a timed region of a few
+            # hundred ms would otherwise end before its first sample
+            t_end = time.time() + 3.0
+            while time.time() < t_end and self.proc.poll() is None:
+                if os.path.getsize(self.path) > 0:
+                    break
+                time.sleep(0.02)
         except Exception:
             self.proc = None
 

@@ -275,10 +275,11 @@ int wxx_conv_weight_pack(float* const* dst, const float* const* src, const int* 
                          const int* cin, const int* taps, int n);
 /* nn/resnet.py forward stem: conv 7x7 / stride 2 / pad 3 (Cin 1..4 -> 64, H, W <= 32) + bias
  * (or NULL) + eval batchnorm (rm == NULL: none) + ReLU (relu = 1) + max pool 3x3 / stride 2 /
- * pad 1, stored channels-last Y (B, Hp, Wp, 64); one launch, values equal to the separate ops. */
+ * pad 1, stored channels-last Y (B, Hp, Wp, 64); one launch, values equal to the separate ops.
+ * Wt (64, Cin, 7, 7), or with packed = 1 transposed to (Cin * 49, 64), 16-byte aligned. */
 int wxx_resnet_stem(float* Y, const float* X, const float* Wt, const float* bias,
                     const float* rm, const float* rv, const float* gamma, const float* beta,
-                    float eps, int relu, int B, int Cin, int H, int W);
+                    float eps, int relu, int B, int Cin, int H, int W, int packed);
 
 /* nn/module.py:460-495 MultiHeadAttention core fused (QK^T * scale (+ mask), softmax, PV)
  * on tcgen05.  Q (B, Sq, H, hd) row stride q_ld, K/V (B, Sk, H, hd) row stride kv_ld,
@@ -385,6 +386,12 @@ int wxx_adamw(float* p, const float* g, float* m, float* v, int64_t n, float lr,
  * {bc1, bc2}), so a training step recorded as a CUDA graph replays with each step's own. */
 int wxx_adamw_device(float* p, const float* g, float* m, float* v, int64_t n, float lr,
                      float beta1, float beta2, float eps, float weight_decay, const float* bc);
+/* wxx_adamw_device over n parameters, one launch per 128 of them: p, g, m, v are host arrays
+ * of n device pointers, len their element counts; the pointers are kernel arguments, so a
+ * step recorded in a CUDA graph replays with the same tensors. */
+int wxx_adamw_device_multi(int n, float* const* p, const float* const* g, float* const* m,
+                           float* const* v, const int64_t* len, float lr, float beta1,
+                           float beta2, float eps, float weight_decay, const float* bc);
 /* step (one device int) += 1, then bc = {1 - beta1^step, 1 - beta2^step} (computed in double). */
 int wxx_adamw_advance(int* step, float* bc, double beta1, double beta2);
 

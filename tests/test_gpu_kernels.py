@@ -462,6 +462,9 @@ def test_resnet_stem_matches_separate_ops(B, C, H, W, bias, rng):
     bn = (rm, rv, g, b, 1e-5)
     got = F.resnet_stem(up(x), up(w), bvec, bn=bn, relu=True)
     assert got is not None
+    wp = up(np.ascontiguousarray(w.reshape(64, -1).T))          # (Cin * 49, 64)
+    got_packed = F.resnet_stem(up(x), up(w), bvec, bn=bn, relu=True, packed=wp)
+    assert np.array_equal(got_packed.numpy(), got.numpy())
     y = F.conv2d_bn(up(x), up(w), (2, 2), (3, 3), (1, 1), bvec, bn=bn, relu=True)
     ref = F.maxpool2d(y, (3, 3), (2, 2), (1, 1)).permute(0, 2, 3, 1).contiguous().numpy()
     got = got.numpy()

@@ -243,3 +243,34 @@ def test_gpt2_training_step_replays_from_a_graph():
     finally:
         g.close()
     assert wxx.backend.device_status() == 0
+
+
+def test_adamw_module_multi_tensor_matches_oracle(rng):
+    """nn.AdamW steps all its parameters with one multi-tensor launch (sizes
+    across chunk boundaries, a parameter without a gradient skipped); two
+    steps against the float64 oracle with the same f32 hyperparameters."""
+    wxx = _w()
+    from wxx_b200.Tensor import Parameter
+
+    shapes = [(5000,), (3, 7), (4096,), (1,), (64, 65)]
+    host = [rng.standard_normal(s).astype(np.float32) for s in shapes]
+    params = [Parameter(up(h)) for h in host]
+    b1, b2 = float(np.float32(0.9)), float(np.float32(0.999))
+    opt = wxx.nn.AdamW([("", p) for p in params], lr=1e-2, beta1=b1, beta2=b2, eps=1e-7,
+                       weight_decay=1e-2)
+    ref = [h.astype(np.float64) for h in host]
+    mom = [np.zeros(s) for s in shapes]
+    vel = [np.zeros(s) for s in shapes]
+    for step in (1, 2):
+        grads = [rng.standard_normal(s).astype(np.float32) for s in shapes]
+        for i, p in enumerate(params):
+            p.grad = None if i == 3 else up(grads[i])
+        opt.step()
+        for i in range(len(shapes)):
+            if i == 3:
+                continue
+            ref[i], mom[i], vel[i] = train.adamw_step(ref[i], grads[i], mom[i], vel[i], step, 1e-2,
+                                                      b1, b2, 1e-7, 1e-2)
+    for i, p in enumerate(params):
+        expect = host[i] if i == 3 else ref[i]
+        assert rel(p.numpy(), expect) < 1e-5, i

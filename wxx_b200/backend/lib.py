@@ -105,7 +105,7 @@ SIGNATURES = {
     "wxx_conv2d_nhwc_packed": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_int] * 14
                               + [c_void_p] * 4 + [c_float, c_void_p, c_int],
     "wxx_conv_weight_pack": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int],
-    "wxx_resnet_stem": [c_void_p] * 8 + [c_float] + [c_int] * 5,
+    "wxx_resnet_stem": [c_void_p] * 8 + [c_float] + [c_int] * 6,
     "wxx_attention": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                       c_i64, c_i64, c_i64, c_float, c_void_p, c_i64, c_int, c_int, c_int],
     "wxx_maxpool2d": [c_void_p, c_void_p, c_void_p] + [c_int] * 10,
@@ -142,6 +142,8 @@ SIGNATURES = {
     "wxx_adamw_device": [c_void_p, c_void_p, c_void_p, c_void_p, c_i64] + [c_float] * 5
                         + [c_void_p],
     "wxx_adamw_advance": [c_void_p, c_void_p, ctypes.c_double, ctypes.c_double],
+    "wxx_adamw_device_multi": [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
+                              + [c_float] * 5 + [c_void_p],
     "wxx_nccl_unique_id": [P_u8],
     "wxx_nccl_init": [P_u8, c_int, c_int],
     "wxx_nccl_allgather": [c_void_p, c_void_p, c_u64],

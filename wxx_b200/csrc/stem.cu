@@ -30,7 +30,7 @@ constexpr int kStemLd = kStemCout + 1;                  // conv-output pixel str
 __global__ void __launch_bounds__(kStemThreads, 2)
     stem_kernel(float* __restrict__ Y, const float* __restrict__ X, const float* __restrict__ Wt,
                 const float* __restrict__ bias, ConvPost post, int Cin, int H, int W, int Ho,
-                int Wo, int Hp, int Wp) {
+                int Wo, int Hp, int Wp, int packed) {
   extern __shared__ __align__(16) float sm[];
   const int Hpad = H + 6, Wpad = W + 6;
   const int taps = Cin * 49;
@@ -47,9 +47,16 @@ __global__ void __launch_bounds__(kStemThreads, 2)
     const int y = r / Wpad - 3, x = r % Wpad - 3;
     img[i] = (y >= 0 && y < H && x >= 0 && x < W) ? xb[((int64_t)c * H + y) * W + x] : 0.f;
   }
-  for (int i = t; i < taps * kStemCout; i += kStemThreads) {
-    const int tap = i / kStemCout, n = i - tap * kStemCout;
-    wts[i] = Wt[(int64_t)n * taps + tap];
+  if (packed) {
+    // already (taps, 64): a float4 copy
+    const float4* src = reinterpret_cast<const float4*>(Wt);
+    float4* dst = reinterpret_cast<float4*>(wts);
+    for (int i = t; i < taps * kStemCout / 4; i += kStemThreads) dst[i] = __ldg(src + i);
+  } else {
+    for (int i = t; i < taps * kStemCout; i += kStemThreads) {
+      const int tap = i / kStemCout, n = i - tap * kStemCout;
+      wts[i] = Wt[(int64_t)n * taps + tap];
+    }
   }
   __syncthreads();
 
@@ -124,19 +131,22 @@ __global__ void __launch_bounds__(kStemThreads, 2)
 }  // namespace
 
 // ResNet stem (see the top of this file).  X (B, Cin, H, W) with Cin <= 4 and
-// H, W <= 32; Wt (64, Cin, 7, 7); bias (64) or NULL; batchnorm running mean /
+// H, W <= 32; Wt (64, Cin, 7, 7), or with packed = 1 the same weights
+// transposed to (Cin * 49, 64) and 16-byte aligned; bias (64) or NULL; batchnorm running mean /
 // variance, gamma, beta (64 each) with eps, or rm == NULL for none; relu 0/1.
 // Y (B, Hp, Wp, 64) channels-last with Ho = (H + 6 - 7) / 2 + 1 (Wo alike) and
 // Hp = (Ho + 2 - 3) / 2 + 1 (Wp alike).
 WXX_EXPORT int wxx_resnet_stem(float* Y, const float* X, const float* Wt, const float* bias,
                                const float* rm, const float* rv, const float* gamma,
                                const float* beta, float eps, int relu, int B, int Cin, int H,
-                               int W) {
+                               int W, int packed) {
   WXX_REQUIRE_INIT();
   WXX_REQUIRE(B >= 0 && Cin >= 1 && Cin <= 4 && H >= 1 && W >= 1 && H <= 32 && W <= 32,
               "wxx_resnet_stem: needs 1..4 input channels and H, W in 1..32");
   WXX_REQUIRE(rm == nullptr || (rv != nullptr && gamma != nullptr && beta != nullptr),
               "wxx_resnet_stem: incomplete batchnorm parameters");
+  WXX_REQUIRE(!packed || !(reinterpret_cast<uintptr_t>(Wt) & 15),
+              "wxx_resnet_stem: packed weights must be 16-byte aligned");
   if (B == 0) return WXX_OK;
   const int Ho = (H + 6 - 7) / 2 + 1, Wo = (W + 6 - 7) / 2 + 1;
   const int Hp = (Ho + 2 - 3) / 2 + 1, Wp = (Wo + 2 - 3) / 2 + 1;
@@ -160,7 +170,7 @@ WXX_EXPORT int wxx_resnet_stem(float* Y, const float* X, const float* Wt, const 
   post.eps = eps;
   post.relu = relu ? 1 : 0;
   stem_kernel<<<(unsigned)B, kStemThreads, smem, wxx::stream()>>>(Y, X, Wt, bias, post, Cin, H, W,
-                                                                  Ho, Wo, Hp, Wp);
+                                                                  Ho, Wo, Hp, Wp, packed ? 1 : 0);
   WXX_LAUNCH_CHECK();
   return WXX_OK;
 }

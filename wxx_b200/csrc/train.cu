@@ -13,6 +13,8 @@
 
 #include "common.cuh"
 
+#include <cstring>
+
 namespace {
 
 constexpr int kT = 256;
@@ -196,6 +198,48 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// Up to kAdamwMulti parameters stepped by one launch (their pointers passed by
+// value, so a recorded step replays with the same tensors): chunk c of the
+// launch belongs to the tensor whose [start, start of the next) holds it.
+constexpr int kAdamwMulti = 128;
+constexpr int kAdamwChunk = 4096;
+struct AdamwTable {
+  int n;
+  int64_t start[kAdamwMulti + 1];   // first chunk of each tensor, prefix
+  float* p[kAdamwMulti];
+  const float* g[kAdamwMulti];
+  float* m[kAdamwMulti];
+  float* v[kAdamwMulti];
+  int64_t len[kAdamwMulti];
+};
+
+__global__ void adamw_multi_kernel(const __grid_constant__ AdamwTable tab, float lr, float b1,
+                                   float b2, float eps, float wd, const float* __restrict__ bc) {
+  const float bc1 = bc[0], bc2 = bc[1];
+  const int64_t chunk = blockIdx.x;
+  int lo = 0, hi = tab.n - 1;   // last tensor whose start <= chunk
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tab.start[mid] <= chunk) lo = mid; else hi = mid - 1;
+  }
+  const int t = lo;
+  const int64_t base = (chunk - tab.start[t]) * kAdamwChunk;
+  const int64_t end = min(tab.len[t], base + kAdamwChunk);
+  float* __restrict__ p = tab.p[t];
+  const float* __restrict__ g = tab.g[t];
+  float* __restrict__ m = tab.m[t];
+  float* __restrict__ v = tab.v[t];
+  for (int64_t i = base + threadIdx.x; i < end; i += blockDim.x) {
+    const float pi = p[i], gi = g[i];
+    const float mi = b1 * m[i] + (1.0f - b1) * gi;
+    const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    const float step = (mi / bc1) / (sqrtf(vi / bc2) + eps);
+    p[i] = pi - lr * (step + wd * pi);
+  }
+}
+
 // step += 1; bc = {1 - beta1^step, 1 - beta2^step} (double, stored as float:
 // the values nn/optimizer.py computes on the host).
 __global__ void adamw_advance_kernel(int* step, float* bc, double b1, double b2) {
@@ -311,7 +355,43 @@ WXX_EXPORT int wxx_adamw_device(float* p, const float* g, float* m, float* v, in
   return WXX_OK;
 }
 
-// Advances an optimizer's device step counter (one int) and writes the
+// wxx_adamw_device over n parameters with one launch per 128 of them: p[i],
+// g[i], m[i], v[i] (host arrays of device pointers) of len[i] elements each.
+WXX_EXPORT int wxx_adamw_device_multi(int n, float* const* p, const float* const* g,
+                                      float* const* m, float* const* v, const int64_t* len,
+                                      float lr, float beta1, float beta2, float eps,
+                                      float weight_decay, const float* bc) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(n >= 0 && bc != nullptr, "wxx_adamw_device_multi: bad count or no bias corrections");
+  int i = 0;
+  while (i < n) {
+    AdamwTable tab;
+    memset(&tab, 0, sizeof(tab));
+    int64_t chunks = 0;
+    for (; i < n && tab.n < kAdamwMulti; ++i) {
+      WXX_REQUIRE(len[i] >= 0 && p[i] && g[i] && m[i] && v[i],
+                  "wxx_adamw_device_multi: tensor %d has a NULL pointer or negative size", i);
+      if (len[i] == 0) continue;
+      const int k = tab.n++;
+      tab.start[k] = chunks;
+      tab.p[k] = p[i];
+      tab.g[k] = g[i];
+      tab.m[k] = m[i];
+      tab.v[k] = v[i];
+      tab.len[k] = len[i];
+      chunks += (len[i] + kAdamwChunk - 1) / kAdamwChunk;
+    }
+    if (tab.n == 0) continue;
+    tab.start[tab.n] = chunks;
+    WXX_REQUIRE(chunks < (int64_t(1) << 31), "wxx_adamw_device_multi: too many elements");
+    adamw_multi_kernel<<<(unsigned)chunks, kT, 0, wxx::stream()>>>(tab, lr, beta1, beta2, eps,
+                                                                   weight_decay, bc);
+    WXX_LAUNCH_CHECK();
+  }
+  return WXX_OK;
+}
+
+// Advances an optimizer's device step counter (one int) and writes the// Advances an optimizer's device step counter (one int) and writes the
 // step's bias corrections {1 - beta1^t, 1 - beta2^t} into bc (two floats).
 WXX_EXPORT int wxx_adamw_advance(int* step, float* bc, double beta1, double beta2) {
   WXX_REQUIRE_INIT();

@@ -93,13 +93,15 @@ def conv2d_nhwc_supported(cin, cout, ho, wo):
     return ho % rows == 0 if ho >= rows else rows % ho == 0
 
 
-def resnet_stem(tensor1, W, bias=None, *, bn=None, relu=True):
+def resnet_stem(tensor1, W, bias=None, *, bn=None, relu=True, packed=None):
     """ResNet's stem in one launch (nn/resnet.py:31-79): ``conv2d`` 7x7 /
     stride 2 / pad 3 to 64 channels, eval batchnorm (``bn`` = (running_mean,
     running_var, gamma, beta, eps) or None), ReLU, ``maxpool2d`` 3x3 / stride 2
     / pad 1, returned channels-last (B, Hp, Wp, 64) -- the same values as those
     ops followed by ``permute(0, 2, 3, 1)``.  None when the shapes are outside
-    the kernel's (1..4 input channels, H and W up to 32)."""
+    the kernel's (1..4 input channels, H and W up to 32).  ``packed``: ``W``
+    already transposed to a dense (Cin * 49, 64) tensor (the kernel then
+    copies it instead of gathering it)."""
     x = dense(tensor1)
     w = dense(W)
     if len(x.shape) != 4 or len(w.shape) != 4:
@@ -117,8 +119,15 @@ def resnet_stem(tensor1, W, bias=None, *, bn=None, relu=True):
         ptrs = [dense(t).ptr for t in (rm, rv, g, b)]
     else:
         ptrs, eps = [None] * 4, 0.0
-    check(F.wxx_resnet_stem(out.buffer.ptr, x.ptr, w.ptr, None if bias is None else dense(bias).ptr,
-                            *ptrs, float(eps), int(bool(relu)), B, Cin, H, Wd), "resnet_stem")
+    wp = w.ptr
+    if packed is not None:
+        if tuple(packed.shape) != (Cin * 49, 64) or not packed.is_dense():
+            raise ValueError(f"resnet_stem: packed weights {tuple(packed.shape)} are not "
+                             f"({Cin * 49}, 64)")
+        wp = packed.ptr
+    check(F.wxx_resnet_stem(out.buffer.ptr, x.ptr, wp, None if bias is None else dense(bias).ptr,
+                            *ptrs, float(eps), int(bool(relu)), B, Cin, H, Wd,
+                            int(packed is not None)), "resnet_stem")
     return out
 
 

@@ -64,19 +64,33 @@ class AdamW(Optimizer):
         self._bc = Tensor((2,), value=1.0)                 # device {bc1, bc2}
 
     def step(self):
+        """One step of every parameter that has a gradient: the step count
+        kernel, then one multi-tensor launch per 128 parameters."""
+        import ctypes
+
         from ..backend.lib import F, check
 
         self.step_count += 1
         check(F.wxx_adamw_advance(self._t.ptr, self._bc.ptr, self.beta1, self.beta2),
               "adamw_advance")
+        rows = []
+        keep = []
         for (_, w), st in zip(self.params, self.state):
             if w.grad is None:
                 continue
             g = functional.contiguous(w.grad)
             if tuple(g.shape) != tuple(w.shape):
                 raise ValueError(f"adamw: grad shape {tuple(g.shape)} != {tuple(w.shape)}")
-            check(F.wxx_adamw_device(w.ptr, g.ptr, st["exp_avg"].ptr, st["exp_avg_sq"].ptr,
-                                     int(np.prod(w.shape)), self.lr, self.beta1, self.beta2,
-                                     self.eps, self.weight_decay, self._bc.ptr), "adamw")
+            keep.append(g)
+            rows.append((w.ptr, g.ptr, st["exp_avg"].ptr, st["exp_avg_sq"].ptr,
+                         int(np.prod(w.shape))))
             for t in (w, st["exp_avg"], st["exp_avg_sq"]):
                 mark_written(t)
+        if not rows:
+            return
+        n = len(rows)
+        ptrs = [(ctypes.c_void_p * n)(*[r[i] for r in rows]) for i in range(4)]
+        lens = (ctypes.c_int64 * n)(*[r[4] for r in rows])
+        check(F.wxx_adamw_device_multi(n, *ptrs, lens, self.lr, self.beta1, self.beta2,
+                                       self.eps, self.weight_decay, self._bc.ptr), "adamw")
+        del keep

@@ -1,5 +1,7 @@
 """ResNet-18 (reference: src/wxx/nn/resnet.py)."""
 
+import numpy as np
+
 from .. import functional
 from ..backend import context
 from ..Tensor import Tensor
@@ -145,7 +147,25 @@ class ResNet18(Module):
         bn = self.bn1
         return functional.resnet_stem(x, c.W, c.bias, relu=True,
                                       bn=(bn.running_mean, bn.running_std, bn.weight, bn.bias,
-                                          1e-5))
+                                          1e-5), packed=self._stem_weight())
+
+    def _stem_weight(self):
+        """conv1's weight transposed to (Cin * 49, 64), kept and rebuilt only
+        when the weight was written since (its buffer's write version)."""
+        from .module import _source_key
+
+        W = self.conv1.W
+        cout = W.shape[0]
+        taps = int(np.prod(W.shape[1:]))
+        key = _source_key([W])
+        entry = self.__dict__.get("_stem_packed")
+        if entry is not None and entry[1] == key:
+            return entry[0]
+        buf = entry[0] if entry is not None else Tensor((taps, cout), value=0.0)
+        if not functional.transpose_stack(buf, [W.reshape((cout, taps))]):
+            return None
+        object.__setattr__(self, "_stem_packed", (buf, key))
+        return buf
 
     def forward(self, x):
         if context.MODE != 0:
