@@ -756,6 +756,9 @@ def run_ours(args, rank, world, local):
 
     def forward(inp):
         with wxx.backend.inferenceMode():
+            if out_ids and hasattr(model, "forward_argmax"):
+                # the ids straight from the LM head's GEMM (logits not stored)
+                return model.forward_argmax(inp)
             out = model(inp)
         return F.max(out, -1)[1] if out_ids else out
 

@@ -207,6 +207,14 @@ int wxx_matmul(float* C, const float* A, const float* B, const float* bias, int6
 int wxx_linear(float* C, const float* A, const float* B, const float* bias,
                const float* residual, int64_t M, int64_t N, int64_t K, int64_t lda,
                int64_t ldb, int trans_b, int act, float alpha, int mode);
+/* Row-wise argmax of op(A) @ op(B) without storing the product (GPT2's forward when its output
+ * is the next-token id of every position): idx[b*M + m] (u32) and vals (or NULL) get the index
+ * and value wxx_argminmax (op 0) would return on the stored product; arguments as wxx_matmul
+ * (no bias, alpha 1, mode 0..2).  Large TMA-addressable products keep each row's maximum per
+ * 256-column tile in the SM-pair GEMM's epilogue; others go through scratch. */
+int wxx_matmul_argmax(uint32_t* idx, float* vals, const float* A, const float* B, int64_t batch,
+                      int64_t M, int64_t N, int64_t K, int64_t a_bs, int64_t b_bs, int64_t lda,
+                      int64_t ldb, int trans_a, int trans_b, int mode);
 /* The decode step's LayerNorm -> linear (nn/gpt.py: ln1 -> q/k/v, ln2 -> fc1, ln_f -> head) in
  * one launch for 1 <= M <= 32 rows: C (M, N) = act(LayerNorm(A) @ W^T + bias) + residual with
  * W (N, K) K-major, gamma / beta (K), act 0 / 1 (GELU), round_out = 1 stores C rounded to the

@@ -116,3 +116,28 @@ def test_ln_linear_against_float64(M, N, K, act, res, rng):
         ref = ref + r
     assert got.shape == (M, N)
     assert rel(got, ref) < 1e-5, rel(got, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 4096, 256), (96, 1000, 128), (1, 300, 64)])
+def test_linear_argmax_matches_stored_product(M, N, K, rng):
+    """The row argmax taken in the SM-pair GEMM's epilogue (large shapes; small
+    ones are declined) gives the ids and the tie rule of
+    max(linear(x, w), -1)[1] (the argmax kernel's lane tree: ties between
+    columns 10 and 265 go to 10, between 40 and 300 to 40)."""
+    F = _F()
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.01).astype(np.float32)
+    if N > 300:
+        w[10] = w[265] = 1.0
+        w[40] = w[300] = -1.0
+    fused = F.linear_argmax(up(x), up(w), transpose_weight=True)
+    ref = F.max(F.linear(up(x), up(w), transpose_weight=True), -1)[1].numpy()
+    if M < 2048:
+        assert fused is None          # too few output tiles for the SM-pair epilogue
+        return
+    got = fused.numpy()
+    assert got.shape == (M,) and got.dtype == np.uint32
+    assert np.array_equal(got, ref)
+    if N > 300:
+        s = x.sum(1)
+        assert np.all(got[s > 1.0] == 10) and np.all(got[s < -1.0] == 40)

@@ -149,3 +149,22 @@ def test_cached_weight_copies_follow_in_place_writes():
     model.load_state_dict(sd2)
     got = _run(model, ids)
     assert np.abs(got - models.gpt2_forward(sd2, ids, H, L)).max() < 5e-3
+
+
+@pytest.mark.parametrize("V,D,H,L,S,B", [(1024, 256, 8, 6, 256, 4), (50304, 1024, 16, 2, 1024, 2)])
+def test_gpt2_forward_argmax_equals_logits_argmax(V, D, H, L, S, B):
+    """GPT2.forward_argmax (the next-token ids straight from the tied head's
+    GEMM, the logits never stored) equals max(forward(ids), -1)[1]; the second
+    shape (the GPT2-scaled head on 2048 rows) takes the SM-pair epilogue."""
+    wxx = _wxx()
+    F = wxx.functional
+    sd = init.gpt2_state_dict(0, V, D, H, L, S)
+    ids = init.token_ids(1, B, S, V)
+    model = wxx.nn.GPT2(V, D, H, L, max_len=S)
+    model.load_state_dict(sd)
+    t = F.from_numpy(ids, dtype=np.uint32)
+    with wxx.backend.inferenceMode():
+        ref = F.max(model(t), -1)[1].numpy()
+        got = model.forward_argmax(t).numpy()
+    assert got.shape == (B, S)
+    assert np.array_equal(got, ref)

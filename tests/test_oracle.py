@@ -208,3 +208,39 @@ def test_adamw_oracle_first_step():
     step = np.where(g != 0, g / (np.abs(g) + 1e-7), 0.0)
     assert np.allclose(p1, p - 1e-2 * (step + 1e-4 * p))
     assert np.allclose(m1, 0.1 * g) and np.allclose(v1, 0.001 * g * g)
+
+
+def _amax_key(slot):
+    """bit-reversed 8-bit slot index (the reduce tree's tie order)."""
+    return int(format(slot & 255, "08b")[::-1], 2)
+
+
+def _tiled_argmax(row):
+    """The fused LM-head argmax's rule (per 256-column tile the best column,
+    equal values to the smaller key, values must exceed -1e38; then the tiles
+    merged in order with the same rule), restated on the host."""
+    n = len(row)
+    best_v, best_c, best_t = np.float32(-1e38), 0x7FFFFFFF, 0
+    for t in range((n + 255) // 256):
+        tv, tc = np.float32(-1e38), 0
+        for c in range(min(256, n - 256 * t)):
+            v = row[256 * t + c]
+            if v > tv or (v == tv and tv > np.float32(-1e38) and _amax_key(c) < _amax_key(tc)):
+                tv, tc = v, c
+        if tv > best_v or (tv == best_v and best_v > np.float32(-1e38)
+                           and _amax_key(tc) < _amax_key(best_c)):
+            best_v, best_c, best_t = tv, tc, t
+    return best_t * 256 + best_c if best_v > np.float32(-1e38) else 0
+
+
+def test_tiled_argmax_rule_matches_reference_tree():
+    """The per-tile maxima merged by bit-reversed slot order give the index of
+    reduce_minmax.wgsl's lane tree (ties, NaN, -1e38 included)."""
+    rng = np.random.default_rng(5)
+    for n in (5, 256, 300, 700, 1500):
+        for _ in range(40):
+            row = rng.integers(-3, 4, size=n).astype(np.float32)
+            row[rng.random(n) < 0.1] = np.nan
+            row[rng.random(n) < 0.05] = np.float32(-1e38)
+            _, ref = K.argminmax(row[None, :], axis=1)
+            assert _tiled_argmax(row) == int(ref[0])

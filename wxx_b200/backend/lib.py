@@ -91,6 +91,8 @@ SIGNATURES = {
                    c_i64, c_i64, c_i64, c_int, c_int, c_int, c_float, c_int],
     "wxx_linear": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64,
                    c_i64, c_int, c_int, c_float, c_int],
+    "wxx_matmul_argmax": [c_void_p, c_void_p, c_void_p, c_void_p] + [c_i64] * 8
+                         + [c_int, c_int, c_int],
     "wxx_ln_linear": [c_void_p, c_void_p, c_i64, c_void_p, c_void_p, c_float, c_void_p, c_i64,
                       c_void_p, c_void_p, c_i64, c_i64, c_i64, c_int, c_int],
     "wxx_linear_batched": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_i64, c_i64, c_i64,

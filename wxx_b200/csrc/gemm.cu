@@ -180,6 +180,9 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
     WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, kPairEpiConv>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         C::SMEM_BYTES));
+    WXX_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<BN, kPairEpiArgmax>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM_BYTES));
     attr_set = true;
   }
   // Rows per pair tile: 256, or for the short-conv epilogue 8 warps of 32 rows
@@ -221,6 +224,7 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   const char* sk_env = getenv("WXX_GEMM_STREAMK");
   const int64_t waves = (tiles + pairs - 1) / pairs;
   const bool sk = sk_env != nullptr && sk_env[0] == '1' && p.epi.act != 2 && p.epi.kind == 0 &&
+                  p.epi.amax == nullptr &&
                   tiles >= pairs &&
                   (double)tiles / (double)(waves * pairs) < 0.95;
   void* ws = nullptr;
@@ -246,6 +250,9 @@ int launch_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
         <<<2 * pairs, PAIR_THREADS_CONV, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
   else if (p.epi.act == 2)
     tc_gemm_pair_kernel<BN, kPairEpiGlu>
+        <<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
+  else if (p.epi.amax != nullptr)
+    tc_gemm_pair_kernel<BN, kPairEpiArgmax>
         <<<2 * pairs, PAIR_THREADS, C::SMEM_BYTES, wxx::stream()>>>(a0, a1, b0, b1, mc, p);
   else
     tc_gemm_pair_kernel<BN, kPairEpiPlain>
@@ -973,7 +980,7 @@ namespace {
 int matmul_impl(float* C, const float* A, const float* B, const float* bias, int64_t batch,
                 int64_t M, int64_t N, int64_t K, int64_t a_bs, int64_t b_bs, int64_t lda,
                 int64_t ldb, int trans_a, int trans_b, int bias_mode, float alpha, int mode,
-                int act, const float* res) {
+                int act, const float* res, float2* amax_ws = nullptr) {
   WXX_REQUIRE(batch >= 0 && M >= 0 && N >= 0 && K >= 0, "wxx_matmul: negative size");
   WXX_REQUIRE(mode >= 0 && mode <= 3, "wxx_matmul: mode %d not in 0..3", mode);
   // mode 3: TF32 products with the stored result rounded to the nearest TF32
@@ -992,11 +999,17 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
     if (bias_mode == 0) return WXX_OK;
     mode = 2;  // the SIMT kernel adds the bias to the zero product
   }
+  // Row maxima instead of C (wxx_matmul_argmax) only from the SM-pair
+  // kernel's epilogue; other shapes are the caller's to handle.
+  if (amax_ws != nullptr && (K == 0 || mode == 2 || act != 0 || res != nullptr || bias_mode != 0)) {
+    wxx::set_error("wxx_matmul: the row-maximum epilogue needs a plain tensor-core product");
+    return WXX_E_UNSUPPORTED;
+  }
   // A few rows against a K-major weight (generation's decode step): the
   // weight-streaming kernel.  Batches whose A rows are consecutive and share
   // the weight fold into rows.
   const int64_t rows_all = batch * M;
-  if (trans_a == 0 && trans_b != 0 && act <= 1 && bias_mode <= 1 &&
+  if (amax_ws == nullptr && trans_a == 0 && trans_b != 0 && act <= 1 && bias_mode <= 1 &&
       (batch == 1 || (a_bs == M * lda && b_bs == 0)) &&
       gemv_fits(rows_all, N, K, lda, ldb, A, B)) {
     return launch_gemv(C, A, lda, B, ldb, bias_mode == 1 ? bias : nullptr, (int)rows_all, (int)N,
@@ -1006,7 +1019,7 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   // gathered tensor-core tiles walking 16 K-blocks) run one warp per output
   // row in exact fp32; the fused epilogues (act / residual) stay on the
   // tensor cores.
-  if (!round_out && act == 0 && res == nullptr && N <= kSkinnyN && K >= 256 &&
+  if (amax_ws == nullptr && !round_out && act == 0 && res == nullptr && N <= kSkinnyN && K >= 256 &&
       batch * M * N * K <= (int64_t(1) << 24) && bias_mode <= 1) {
     const int64_t rows = batch * M;
     skinny_gemm_kernel<<<wxx::grid_for(rows * 32, 256), 256, 0, s>>>(
@@ -1057,6 +1070,8 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   p.epi.res_ld = N;
   p.epi.res_bs = M * N;
   p.epi.round_tf32 = round_out;
+  p.epi.amax = amax_ws;
+  if (amax_ws != nullptr) p.epi.C = reinterpret_cast<float*>(amax_ws);  // map only: no stores
   // SM-pair tiles when the product is large and every operand is TMA-fed;
   // each CTA then loads 128-row boxes of both A and B.
   CUtensorMap mc;
@@ -1071,6 +1086,10 @@ int matmul_impl(float* C, const float* A, const float* B, const float* bias, int
   if (pair && (p.a.kind >= 2 || p.b.kind >= 2)) {
     pair = false;
     setup_operand(db, bn, true, p.b, &mb0);
+  }
+  if (amax_ws != nullptr && !pair) {
+    wxx::set_error("wxx_matmul: the row-maximum epilogue needs the SM-pair kernel");
+    return WXX_E_UNSUPPORTED;
   }
   const int b_box = pair ? BM : bn;
   ma1 = ma0;
@@ -1198,6 +1217,98 @@ WXX_EXPORT int wxx_linear(float* C, const float* A, const float* B, const float*
   if (M * N == 0) return WXX_OK;
   return matmul_impl(C, A, B, bias, 1, M, N, K, 0, 0, lda, ldb, 0, trans_b, bias ? 1 : 0, alpha,
                      mode, act, residual);
+}
+
+namespace {
+
+// Per row: the tiles' (maximum, column within the tile) pairs merged in tile
+// order -- larger value wins, equal values go to the smaller amax_key of the
+// column within the tile (= the index mod 256 for 256-wide tiles), then to
+// the earlier tile -- the argmax kernels' choice among the positions holding
+// the row maximum.  A row with no value above -1e38 gets index 0.
+__global__ void amax_merge_kernel(uint32_t* __restrict__ idx, float* __restrict__ vals,
+                                  const float2* __restrict__ ws, int64_t rows, int tiles) {
+  // one warp per row: the lanes read the row's tile entries 32 at a time
+  // (coalesced) and the candidates are reduced by shuffles; the order
+  // (value, then smaller key, then earlier tile) is total, so the reduction
+  // order does not matter
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const float2* w = ws + r * tiles;
+    bool ok = false;
+    float bv = -1e38f;
+    int bk = 0, bt = 0, bc = 0;
+    for (int t = lane; t < tiles; t += 32) {
+      const float2 e = w[t];
+      if (e.x > -1e38f) {
+        const int c = __float_as_int(e.y), k = amax_key(c);
+        if (!ok || e.x > bv || (e.x == bv && (k < bk || (k == bk && t < bt)))) {
+          ok = true;
+          bv = e.x;
+          bk = k;
+          bt = t;
+          bc = c;
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const bool ook = __shfl_xor_sync(0xffffffffu, ok ? 1 : 0, off) != 0;
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int ok_ = __shfl_xor_sync(0xffffffffu, bk, off);
+      const int ot = __shfl_xor_sync(0xffffffffu, bt, off);
+      const int oc = __shfl_xor_sync(0xffffffffu, bc, off);
+      if (ook && (!ok || ov > bv || (ov == bv && (ok_ < bk || (ok_ == bk && ot < bt))))) {
+        ok = true;
+        bv = ov;
+        bk = ok_;
+        bt = ot;
+        bc = oc;
+      }
+    }
+    if (lane == 0) {
+      idx[r] = ok ? (uint32_t)(bt * 256 + bc) : 0u;
+      if (vals != nullptr) vals[r] = ok ? bv : -1e38f;
+    }
+  }
+}
+
+}  // namespace
+
+// Row-wise argmax of a product without storing it (the GPT2 forward whose
+// output is the next-token id of every position): idx[b*M + m] = argmax over n
+// of (op(A[b]) @ op(B))[m, n], vals (or NULL) the maxima; the index rule of
+// wxx_argminmax (op 0).  Arguments as wxx_matmul (no bias, alpha 1).  The
+// SM-pair GEMM's epilogue keeps each row's maximum per 256-column tile and a
+// small kernel merges the tiles.  Products that kernel does not take (too
+// few tiles, operands TMA cannot address, fp32 SIMT mode, K = 0) return
+// WXX_E_UNSUPPORTED with nothing enqueued: store the product and run
+// wxx_argminmax instead.
+WXX_EXPORT int wxx_matmul_argmax(uint32_t* idx, float* vals, const float* A, const float* B,
+                                 int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_bs,
+                                 int64_t b_bs, int64_t lda, int64_t ldb, int trans_a, int trans_b,
+                                 int mode) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(batch >= 0 && M >= 0 && N > 0 && K >= 0, "wxx_matmul_argmax: bad sizes");
+  WXX_REQUIRE(idx != nullptr, "wxx_matmul_argmax: idx is NULL");
+  WXX_REQUIRE(mode >= 0 && mode <= 2, "wxx_matmul_argmax: mode %d not in 0..2", mode);
+  const int64_t rows = batch * M;
+  if (rows == 0) return WXX_OK;
+  const int64_t tiles = (N + 255) / 256;
+  void* ws = nullptr;
+  int st = wxx_malloc(&ws, (uint64_t)rows * tiles * sizeof(float2));
+  if (st) return st;
+  st = K > 0 ? matmul_impl(nullptr, A, B, nullptr, batch, M, N, K, a_bs, b_bs, lda, ldb, trans_a,
+                           trans_b, 0, 1.0f, mode, 0, nullptr, reinterpret_cast<float2*>(ws))
+             : WXX_E_UNSUPPORTED;
+  if (st == WXX_OK) {
+    amax_merge_kernel<<<wxx::grid_for(rows * 32, 256), 256, 0, wxx::stream()>>>(
+        idx, vals, reinterpret_cast<const float2*>(ws), rows, (int)tiles);
+    st = wxx::after_launch(__FILE__, __LINE__);
+  }
+  const int st2 = wxx_free(ws);
+  return st ? st : st2;
 }
 
 // A few rows through LayerNorm and a linear layer in one launch (the decode

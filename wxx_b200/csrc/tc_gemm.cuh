@@ -396,6 +396,12 @@ struct EpiParams {
   int64_t res_ld, res_bs;
   int raw;                // split-K: raw partial sums to the workspace map, z = batch * splits + slice
   int round_tf32;         // kind 0: store C rounded to the nearest TF32 value (tf32_rna)
+  // SM-pair kernel, plain epilogue: instead of storing C, each row's maximum
+  // over the tile's columns (values above -1e38; among equal values the
+  // column with the smaller amax_key, the argmax kernels' tie order) goes to
+  // amax[(bt * M + m) * tiles_n + tn] as (value, column within the tile as
+  // int bits); C is not written.
+  float2* amax;
   ConvPost post;          // kind 1 only
   // kind 2: rows are (sequence b, position n) = (row / conv_len, row % conv_len);
   // C[b, c, n] (c_bs = N * conv_len) = conv_b[c'] + sum_k conv_w[c', k] * Y[row - k, c]
@@ -772,6 +778,19 @@ __device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity,
       }
     }
   }
+}
+
+// Tie order of the argmax kernels (argminmax_warp_kernel) for a position r:
+// slot = r mod 256 = lane + 32 j; the lane tree (shuffle strides 16 .. 1,
+// lower lane kept on ties) prefers the lane whose bit-reversed index is
+// smaller, and the in-lane tree over j (strides 4, 2, 1) likewise.  Among
+// equal values the smaller key wins; equal keys (the same slot) go to the
+// earlier position.
+__host__ __device__ __forceinline__ int amax_key(int slot) {
+  const int l = slot & 31, j = (slot >> 5) & 7;
+  const int lr = ((l & 1) << 4) | ((l & 2) << 2) | (l & 4) | ((l & 8) >> 2) | ((l & 16) >> 4);
+  const int jr = ((j & 1) << 2) | (j & 2) | ((j & 4) >> 2);
+  return (lr << 3) | jr;
 }
 
 // Epilogue math of the TMA-store path for row m, columns n0..n0+31:
@@ -1319,6 +1338,7 @@ struct PairCfg {
 constexpr int kPairEpiPlain = 0;   // TMA-store epilogue (bias, GELU, residual, stream-K)
 constexpr int kPairEpiGlu = 1;     // paired GLU (act == 2)
 constexpr int kPairEpiConv = 2;    // short causal conv written (B, N, L) (kind 2), 8 warps
+constexpr int kPairEpiArgmax = 3;  // row maxima per tile into EpiParams.amax, C not written
 
 template <int BN, int EPI = kPairEpiPlain>
 __global__ void __cluster_dims__(2, 1, 1)
@@ -1575,6 +1595,9 @@ __global__ void __cluster_dims__(2, 1, 1)
         continue;
       }
       constexpr bool glu = GLU;  // host: GLU <=> p.epi.act == 2, never with stream-K partials
+      constexpr bool amax = EPI == kPairEpiArgmax;
+      float best_v = -1e38f;
+      int best_c = 0;
 #pragma unroll 1
       for (int c = 0; c < BN && m0 < p.M; c += glu ? 64 : 32) {
         const int n0 = tn * BN + c;
@@ -1598,6 +1621,43 @@ __global__ void __cluster_dims__(2, 1, 1)
           }
         }
         if (!glu) epi_apply<false>(p, bt, m0 + lane, n0, v);
+        if constexpr (amax) {
+          // the chunk's maximum by a tree (independent fmaxf: NaN loses);
+          // the ordered scan with the tie keys only when it can change the
+          // row's best (kept rolled: a compact epilogue leaves the MMA and
+          // producer warps' instructions in the cache)
+          float t16[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            t16[j] = fmaxf(n0 + j < p.N ? v[j] : -INFINITY, n0 + j + 16 < p.N ? v[j + 16] : -INFINITY);
+#pragma unroll
+          for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+            for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
+          const float cm = t16[0];
+          if (cm > best_v || (cm == best_v && best_v > -1e38f)) {
+            // the chunk's columns holding its maximum, the smallest tie key
+            // among them, merged with the row's best so far
+            unsigned eq = 0u;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) eq |= (n0 + j < p.N && v[j] == cm) ? (1u << j) : 0u;
+            int kc = c, kk = 0x7fffffff;
+            for (unsigned m = eq; m != 0u; m &= m - 1u) {
+              const int col = c + __ffs(m) - 1, k = amax_key(col);
+              if (k < kk) {
+                kk = k;
+                kc = col;
+              }
+            }
+            if (cm > best_v) {
+              best_v = cm;
+              best_c = kc;
+            } else if (kk < amax_key(best_c)) {
+              best_c = kc;
+            }
+          }
+          continue;
+        }
         uint8_t* buf = wstage + (chunk_seq & 1) * 4096;
         if (lane == 0) bulk_wait_read<1>();
         __syncwarp();
@@ -1613,6 +1673,9 @@ __global__ void __cluster_dims__(2, 1, 1)
         }
         ++chunk_seq;
       }
+      if (amax && m0 + lane < p.M)   // (constexpr: only the argmax form stores here)
+        p.epi.amax[((int64_t)bt * p.M + m0 + lane) * p.tiles_n + tn] =
+            make_float2(best_v, __int_as_float(best_c));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);

@@ -109,6 +109,7 @@ from .utils import (
     from_tensor,
     linear,
     ln_linear,
+    linear_argmax,
     linear_short_conv,
     transpose_stack,
     linspace,

@@ -327,6 +327,40 @@ def linear(x, weight, bias=None, *, activation=None, residual=None, transpose_we
 _E_UNSUPPORTED = -4
 
 
+def linear_argmax(x, weight, *, transpose_weight=False):
+    """``max(x @ weight, -1)[1]`` (or ``x @ weight.T`` with
+    ``transpose_weight``) without storing the product: the u32 index of each
+    row's maximum, shaped ``x.shape[:-1]``, with the argmax kernel's tie rule.
+    For GPT2's forward when its output is the next-token id of every
+    position (the LM head's 1.65 GB of logits at the GPT2-scaled shape are
+    then neither written nor read back).  None (nothing launched) when the
+    product is not one the fused epilogue takes (few output tiles, operands
+    the tensor memory accelerator cannot address): compute the product and
+    ``max`` it then."""
+    a = dense(x)
+    w = dense(weight)
+    K = a.shape[-1]
+    if len(w.shape) != 2 or w.shape[1 if transpose_weight else 0] != K:
+        raise ValueError(f"linear_argmax: weight {tuple(w.shape)} does not match input "
+                         f"{tuple(a.shape)}")
+    N = w.shape[0] if transpose_weight else w.shape[1]
+    M = int(math.prod(a.shape[:-1])) if len(a.shape) > 1 else 1
+    out = empty(list(a.shape[:-1]), "u32")
+    mode = matmul_mode_code()
+    if M:
+        timer = active_timer()
+        ev0 = timer.start() if timer is not None else None
+        st = F.wxx_matmul_argmax(out.buffer.ptr, None, a.ptr, w.ptr, 1, M, N, K, 0, 0, K,
+                                 K if transpose_weight else N, 0, int(bool(transpose_weight)),
+                                 mode if mode in (0, 1, 2) else 0)
+        if st == _E_UNSUPPORTED:
+            return None
+        check(st, "linear_argmax")
+        if timer is not None:
+            timer.stop(ev0, 2.0 * M * N * K, f"{M}x{N}x{K} argmax")
+    return out
+
+
 def ln_linear(x, gamma, beta, weight, bias=None, *, activation=None, residual=None,
               feeds_tf32=False, eps=1e-5):
     """``linear(LayerNorm(x), weight, bias, ...)`` with ``weight`` given as

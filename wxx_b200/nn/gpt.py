@@ -135,6 +135,23 @@ class GPT2(Module):
             h = block(h, mask)
         return self.head(self.ln_f.forward_into_gemm(h))
 
+    def forward_argmax(self, x, mask=None):
+        """``forward(x).max(-1)[1]``: the next-token id (u32) of every
+        position; with the tied head the logits are never stored (the head's
+        GEMM keeps each row's maximum per column tile)."""
+        b, seq = x.shape
+        if seq > self.max_len:
+            raise ValueError(f"sequence length {seq} > max_len {self.max_len}")
+        if mask is None:
+            mask = self.causal_mask(seq)
+        h = self.tok_emb(x) + self.pos_emb(self._positions(seq))
+        for block in self.blocks:
+            h = block(h, mask)
+        h = self.ln_f.forward_into_gemm(h)
+        if hasattr(self.head, "forward_argmax"):
+            return self.head.forward_argmax(h)
+        return functional.max(self.head(h), -1)[1]
+
     def generate(self, prompt, max_new_tokens=64, temperature=1.0, top_k=None, stop_token=None,
                  rng=None):
         """Samples up to ``max_new_tokens`` ids after ``prompt`` ((batch, seq) or

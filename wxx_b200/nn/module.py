@@ -627,6 +627,15 @@ class TiedLinear(Module):
         super().__init__()
         object.__setattr__(self, "_embedding", embedding)
 
+    def forward_argmax(self, x):
+        """The index of each row's largest logit, ``forward(x).max(-1)[1]``,
+        without storing the logits (inference)."""
+        w = self._embedding.weight
+        if context.MODE != 0 and functional.get_matmul_mode() == "tf32":
+            w = tf32_weight(self, "_w_tf32", w)
+        ids = functional.linear_argmax(x, w, transpose_weight=True)
+        return ids if ids is not None else functional.max(self.forward(x), -1)[1]
+
     def forward_ln(self, x, ln):
         """``forward(ln(x))`` for a few rows (generation's decode step): the
         LayerNorm and the head product in one launch."""
