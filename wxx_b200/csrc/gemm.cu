@@ -850,6 +850,139 @@ __global__ void __launch_bounds__(256, 2) rows_gemv_async_kernel(
   }
 }
 
+// Few rows, K <= 1024, wide N (the decode step's q/k/v, fc1 and LM head):
+// every warp owns 2 weight rows (output columns) whole, so all 2 x K / 4
+// float4 loads of a lane are in flight at once; the (LayerNorm-ed) activation
+// rows sit in shared memory, staged once per CTA and pass of 8 rows, and the
+// CTA walks column blocks of 16 grid-stride with no barrier between them.
+// The 16 accumulators (column c, row r at 8c + r) are summed across the
+// lanes by a halving exchange over lane bits 3..0 and one shuffle across the
+// half-warps; exact fp32, the epilogue of rows_gemv_kernel.
+constexpr int kG3Cols = 2;
+constexpr int kG3MaxK = 1024;
+
+template <bool LN>
+__global__ void __launch_bounds__(256, 2) rows_gemv_k1k_kernel(
+    float* __restrict__ C, const float* __restrict__ A, int64_t lda, const float* __restrict__ W,
+    int64_t ldw, const float* __restrict__ bias, int M, int N, int K, float alpha, int act,
+    const float* __restrict__ res, int round_out, const float* __restrict__ ln_g,
+    const float* __restrict__ ln_b, float ln_eps) {
+  __shared__ __align__(16) float as[8 * kG3MaxK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cols_per_cta = 8 * kG3Cols;
+  const int blocks = (N + cols_per_cta - 1) / cols_per_cta;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int m0 = 0; m0 < M; m0 += 8) {
+    if (m0 > 0) __syncthreads();   // the previous pass is done with the rows
+    {
+      // warp r stages row m0 + r: its float4s in registers, two-pass
+      // statistics from them (LN), then the normalised row
+      const int r = warp, m = m0 + r;
+      const float* ar = A + (int64_t)(m < M ? m : 0) * lda;
+      float4 v[kG3MaxK / 128];
+#pragma unroll
+      for (int i = 0; i < kG3MaxK / 128; ++i) {
+        const int k = (i * 32 + lane) * 4;
+        v[i] = (m < M && k < K) ? __ldg(reinterpret_cast<const float4*>(ar + k)) : zero;
+      }
+      float mean = 0.f, inv = 1.f;
+      if (LN) {
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < kG3MaxK / 128; ++i) sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mean = sum / (float)K;
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < kG3MaxK / 128; ++i) {
+          const int k = (i * 32 + lane) * 4;
+          if (k < K) {
+            const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean,
+                        d = v[i].w - mean;
+            ss += (a * a + b * b) + (c * c + d * d);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float var = fmaxf(0.f, ss / (float)K);
+        inv = var > 0.f ? rsqrtf(var + ln_eps) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < kG3MaxK / 128; ++i) {
+        const int k = (i * 32 + lane) * 4;
+        float4 o = v[i];
+        if (LN && m < M && k < K) {
+          const float4 g4 = __ldg(reinterpret_cast<const float4*>(ln_g + k));
+          const float4 b4 = __ldg(reinterpret_cast<const float4*>(ln_b + k));
+          o.x = (o.x - mean) * inv * g4.x + b4.x;
+          o.y = (o.y - mean) * inv * g4.y + b4.y;
+          o.z = (o.z - mean) * inv * g4.z + b4.z;
+          o.w = (o.w - mean) * inv * g4.w + b4.w;
+        }
+        *reinterpret_cast<float4*>(as + r * kG3MaxK + k) = o;
+      }
+    }
+    __syncthreads();
+    for (int blk = blockIdx.x; blk < blocks; blk += gridDim.x) {
+      const int n0 = blk * cols_per_cta + warp * kG3Cols;
+      float4 w[kG3Cols][kG3MaxK / 128];
+#pragma unroll
+      for (int c = 0; c < kG3Cols; ++c) {
+        const float* wr = W + (int64_t)(n0 + c < N ? n0 + c : 0) * ldw;
+#pragma unroll
+        for (int i = 0; i < kG3MaxK / 128; ++i) {
+          const int k = (i * 32 + lane) * 4;
+          w[c][i] = (n0 + c < N && k < K) ? __ldg(reinterpret_cast<const float4*>(wr + k)) : zero;
+        }
+      }
+      float acc[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) acc[q] = 0.f;
+#pragma unroll
+      for (int i = 0; i < kG3MaxK / 128; ++i) {
+        const int k = (i * 32 + lane) * 4;
+        if (k < K) {
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const float4 a = *reinterpret_cast<const float4*>(as + r * kG3MaxK + k);
+#pragma unroll
+            for (int c = 0; c < kG3Cols; ++c) {
+              float t = acc[8 * c + r];
+              t = fmaf(a.x, w[c][i].x, t);
+              t = fmaf(a.y, w[c][i].y, t);
+              t = fmaf(a.z, w[c][i].z, t);
+              t = fmaf(a.w, w[c][i].w, t);
+              acc[8 * c + r] = t;
+            }
+          }
+        }
+      }
+      // halving exchange over lane bits 3..0 (lane l keeps index l & 15),
+      // then the two half-warps added
+#pragma unroll
+      for (int sft = 8; sft >= 1; sft >>= 1) {
+        const bool upper = (lane & sft) != 0;
+#pragma unroll
+        for (int q = 0; q < sft; ++q) {
+          const float send = upper ? acc[q] : acc[q + sft];
+          const float keep = upper ? acc[q + sft] : acc[q];
+          acc[q] = keep + __shfl_xor_sync(0xffffffffu, send, sft);
+        }
+      }
+      float v = acc[0] + __shfl_xor_sync(0xffffffffu, acc[0], 16);
+      const int n = n0 + ((lane & 15) >> 3), m = m0 + (lane & 7);
+      if (lane < 16 && n < N && m < M) {
+        v = bias != nullptr ? v * alpha + __ldg(bias + n) : v * alpha;
+        if (act == 1) v = gelu_tanh(v);
+        if (res != nullptr) v += __ldg(res + (int64_t)m * N + n);
+        if (round_out) v = tf32_rna(v);
+        C[(int64_t)m * N + n] = v;
+      }
+    }
+  }
+}
+
 // WXX_GEMV_ASYNC=1 selects the shared-memory-streamed form for K <= kGvMaxK
 // (read once); by default the register form runs: 1.07 against 1.25-1.27 ms
 // per GPT2-scaled decode step (batch 8) when measured side by side.
@@ -873,6 +1006,18 @@ bool gemv_fits(int64_t rows, int64_t N, int64_t K, int64_t lda, int64_t ldb, con
 int launch_gemv(float* C, const float* A, int64_t lda, const float* W, int64_t ldw,
                 const float* bias, int rows, int N, int K, float alpha, int act, const float* res,
                 int round_out, const float* ln_g, const float* ln_b, float ln_eps) {
+  if (K <= kG3MaxK && N >= 2048 && !gemv_async_enabled()) {
+    const int64_t blocks = (N + 8 * kG3Cols - 1) / (8 * kG3Cols);
+    const unsigned grid = (unsigned)std::min<int64_t>(blocks, 2 * (int64_t)wxx::num_sms());
+    if (ln_g != nullptr)
+      rows_gemv_k1k_kernel<true><<<grid, 256, 0, wxx::stream()>>>(
+          C, A, lda, W, ldw, bias, rows, N, K, alpha, act, res, round_out, ln_g, ln_b, ln_eps);
+    else
+      rows_gemv_k1k_kernel<false><<<grid, 256, 0, wxx::stream()>>>(
+          C, A, lda, W, ldw, bias, rows, N, K, alpha, act, res, round_out, nullptr, nullptr, 0.f);
+    WXX_LAUNCH_CHECK();
+    return WXX_OK;
+  }
   if (K <= kGvMaxK && gemv_async_enabled()) {
     const int nkc = (K + kGvKc - 1) / kGvKc;
     const size_t smem = (size_t)(kGvStages * kGvStageFloats + 8 * nkc * kGvKc) * sizeof(float);
