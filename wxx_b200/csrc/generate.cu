@@ -85,6 +85,24 @@ __global__ void __launch_bounds__(kAttnThreads)
   const int64_t col = (int64_t)h * HD;
   float* kb = Kc + b * cache_bs + col;
   float* vb = Vc + b * cache_bs + col;
+  // The P V product's value rows (thread t: column quad t % (hd / 4), keys
+  // t / (hd / 4) + KG u) are loaded first, so they arrive while the scores
+  // and the softmax run; the new position's row comes from v_new.
+  const int cq = t % NQ, kg = t / NQ;
+  constexpr int kPre = 16;
+  float4 vpre[kPre];
+#pragma unroll
+  for (int u = 0; u < kPre; ++u) {
+    const int j = kg + u * KG;
+    if (j < p) {
+      vpre[u] = reinterpret_cast<const float4*>(vb + (int64_t)j * D)[cq];
+    } else if (j == p) {
+      const float* vn = v_new + b * qkv_ld + col + cq * 4;
+      vpre[u] = make_float4(vn[0], vn[1], vn[2], vn[3]);
+    } else {
+      vpre[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   for (int i = t; i < HD; i += kAttnThreads) {
     kb[(int64_t)p * D + i] = k_new[b * qkv_ld + col + i];
     vb[(int64_t)p * D + i] = v_new[b * qkv_ld + col + i];
@@ -135,7 +153,6 @@ __global__ void __launch_bounds__(kAttnThreads)
 #pragma unroll
   for (int w = 0; w < NW; ++w) sum += s_red[w];
   // o = sum_j p_j v_j
-  const int cq = t % NQ, kg = t / NQ;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   auto pv_add = [&](int j, const float4& v4) {
     const float pj = s_score[j];
@@ -144,8 +161,13 @@ __global__ void __launch_bounds__(kAttnThreads)
     acc.z = fmaf(pj, v4.z, acc.z);
     acc.w = fmaf(pj, v4.w, acc.w);
   };
-  // four value rows in flight per thread, then one at a time for the rest
-  int j = kg;
+  // the prefetched rows, then four in flight per thread, then one at a time
+#pragma unroll
+  for (int u = 0; u < kPre; ++u) {
+    const int jj = kg + u * KG;
+    if (jj <= p) pv_add(jj, vpre[u]);
+  }
+  int j = kg + kPre * KG;
   for (; j + 3 * KG <= p; j += 4 * KG) {
     float4 v4[4];
 #pragma unroll
