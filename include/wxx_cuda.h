@@ -319,6 +319,13 @@ int wxx_irfft(float* y, int64_t out_ld, const void* X, int64_t in_ld, int64_t ro
 int wxx_fftconv_spectrum(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
                          int64_t sl, const void* H, int64_t h_ld, int B, int D, int L, int64_t n,
                          int out_len);
+/* nn/hyena.py:240 gates[i] * fft_conv1d(z, h) with a precomputed spectrum H (D rows of h_ld
+ * complex values, n/2+1 used): wxx_fftconv_spectrum with the gate view of wxx_fftconv_gated
+ * applied as the output is stored. */
+int wxx_fftconv_spectrum_gated(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
+                               int64_t sl, const void* H, int64_t h_ld, int B, int D, int L,
+                               int64_t n, int out_len, const float* gate, int64_t g_off,
+                               int64_t g_sb, int64_t g_sd, int64_t g_sl);
 /* nn/hyena.py:208-216 fft_conv1d with a time-domain filter h (D, Lh) */
 int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd, int64_t sl,
                 const float* h, int64_t h_ld, int Lh, int B, int D, int L, int64_t n, int out_len);

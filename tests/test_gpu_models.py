@@ -168,3 +168,30 @@ def test_gpt2_forward_argmax_equals_logits_argmax(V, D, H, L, S, B):
         got = model.forward_argmax(t).numpy()
     assert got.shape == (B, S)
     assert np.array_equal(got, ref)
+
+
+def test_hyena_filter_spectra_follow_writes_and_lengths():
+    """Inference keeps each Hyena operator's filter spectra between calls
+    (they do not depend on the input); a write to a filter weight or the decay,
+    or another sequence length, must give the values of a fresh computation."""
+    wxx = _wxx()
+    F = wxx.functional
+    V, D, NL, order, B = 64, 32, 2, 3, 2
+    sd = init.hyena_state_dict(0, V, D, NL, order)
+    model = wxx.nn.Hyena(V, d_model=D, n_layers=NL, order=order)
+    model.load_state_dict(sd)
+    for L in (200, 120, 200):
+        ids = init.token_ids(3, B, L, V)
+        first = _run(model, ids)
+        assert np.array_equal(_run(model, ids), first)
+        assert np.abs(first - models.hyena_forward(sd, ids, NL, order)).max() < 1e-3
+    sd2 = dict(sd)
+    params = dict(model.named_parameters())
+    for key in ("layers.0.mixer.decay", "layers.1.mixer.filter_mlp.2.mlp.2.weight",
+                "layers.0.mixer.filter_mlp.0.mlp.0.bias"):
+        sd2[key] = (sd[key] * 1.5 + 0.1).astype(np.float32)
+        F.assign(params[key], F.from_numpy(sd2[key]))
+    ids = init.token_ids(4, B, 200, V)
+    fresh = wxx.nn.Hyena(V, d_model=D, n_layers=NL, order=order)
+    fresh.load_state_dict(sd2)
+    assert np.array_equal(_run(model, ids), _run(fresh, ids))

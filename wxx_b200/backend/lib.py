@@ -116,6 +116,9 @@ SIGNATURES = {
     "wxx_irfft": [c_void_p, c_i64, c_void_p, c_i64, c_i64, c_i64, c_i64],
     "wxx_fftconv_spectrum": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64,
                              c_int, c_int, c_int, c_i64, c_int],
+    "wxx_fftconv_spectrum_gated": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p,
+                                   c_i64, c_int, c_int, c_int, c_i64, c_int, c_void_p, c_i64,
+                                   c_i64, c_i64, c_i64],
     "wxx_fftconv": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64, c_int,
                     c_int, c_int, c_int, c_i64, c_int],
     "wxx_fftconv_gated": [c_void_p, c_void_p, c_i64, c_i64, c_i64, c_i64, c_void_p, c_i64, c_int,

@@ -2019,6 +2019,20 @@ WXX_EXPORT int wxx_fftconv(float* y, const float* x, int64_t x_off, int64_t sb, 
 // strided (B, D, out_len) gate view (element strides g_sb, g_sd, g_sl from
 // g_off).  Hyena's z = gates[i] * fft_conv1d(z, h) (nn/hyena.py:240) in one
 // pass: the product is applied as the output is stored.
+// wxx_fftconv_spectrum whose output is multiplied by a strided gate view as it
+// is stored (Hyena's gates[i] * fft_conv1d(z, h) with the filter spectrum made
+// once and kept).
+WXX_EXPORT int wxx_fftconv_spectrum_gated(float* y, const float* x, int64_t x_off, int64_t sb,
+                                          int64_t sd, int64_t sl, const void* H, int64_t h_ld,
+                                          int B, int D, int L, int64_t n, int out_len,
+                                          const float* gate, int64_t g_off, int64_t g_sb,
+                                          int64_t g_sd, int64_t g_sl) {
+  WXX_REQUIRE_INIT();
+  WXX_REQUIRE(gate != nullptr, "wxx_fftconv_spectrum_gated: gate is null");
+  return fftconv_spectrum_impl(y, x, x_off, sb, sd, sl, H, h_ld, B, D, L, n, out_len, gate, g_off,
+                               g_sb, g_sd, g_sl);
+}
+
 WXX_EXPORT int wxx_fftconv_gated(float* y, const float* x, int64_t x_off, int64_t sb, int64_t sd,
                                  int64_t sl, const float* h, int64_t h_ld, int Lh, int B, int D,
                                  int L, int64_t n, int out_len, const float* gate, int64_t g_off,

@@ -58,6 +58,8 @@ from .fft import (
     complex_pad,
     complex_weights,
     fftconv,
+    fftconv_spectrum,
+    filter_spectrum,
     from_numpy_complex,
     irfft,
     rfft,

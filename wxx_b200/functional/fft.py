@@ -158,6 +158,58 @@ def irfft(tensor1, n=None):
     return out
 
 
+def filter_spectrum(h, n):
+    """The spectra of the (R, Lh) filters ``h`` for ``fftconv_spectrum`` at
+    FFT size ``n``: a (R, n//2 + 2) c64 tensor whose rows hold the n//2 + 1
+    bins of ``rfft(h, n)`` (one pad value a row keeps every row 16-byte
+    aligned for the fused kernel's bulk copies).  One launch for all rows."""
+    if len(h.shape) != 2:
+        raise ValueError(f"filter_spectrum expects (R, Lh) filters, got {h.shape}")
+    n = int(n)
+    _check_pow2(n)
+    hd = dense(h)
+    R, Lh = hd.shape
+    ld = n // 2 + 2
+    out = empty((R, ld), "c64")
+    check(F.wxx_rfft(out.buffer.ptr, ld, hd.ptr, Lh, R, Lh, n), "filter_spectrum")
+    return out
+
+
+def fftconv_spectrum(x, H, n, out_len=None, gate=None):
+    """``fftconv`` with the filter given by its spectrum ``H`` (a (D, >= n//2 +
+    1) c64 view with unit column stride, as ``filter_spectrum`` returns), so a
+    filter that does not change between calls is transformed once."""
+    if len(x.shape) != 3 or len(H.shape) != 2 or H.type != "c64":
+        raise ValueError(f"fftconv_spectrum expects x (B, D, L) and a c64 H (D, bins), got "
+                         f"{x.shape}, {H.shape}")
+    B, D, L = x.shape
+    n = int(n)
+    _check_pow2(n)
+    if H.shape[0] != D or H.shape[1] < n // 2 + 1 or H.stride[1] != 1:
+        raise ValueError(f"fftconv_spectrum: spectrum {tuple(H.shape)} does not fit D = {D}, "
+                         f"n = {n}")
+    out_len = L if out_len is None else int(out_len)
+    if not 0 <= out_len <= n:
+        raise ValueError(f"fftconv_spectrum: out_len {out_len} outside [0, {n}]")
+    if any(s < 0 for s in x.stride):
+        x = x.contiguous()
+    out = empty((B, D, out_len), "f32")
+    if gate is None:
+        check(F.wxx_fftconv_spectrum(out.buffer.ptr, x.buffer.ptr, x.offset, x.stride[0],
+                                     x.stride[1], x.stride[2], H.ptr, H.stride[0], B, D, L, n,
+                                     out_len), "fftconv_spectrum")
+        return out
+    if tuple(gate.shape) != (B, D, out_len):
+        raise ValueError(f"fftconv_spectrum: gate shape {gate.shape} != {(B, D, out_len)}")
+    if any(s < 0 for s in gate.stride):
+        gate = gate.contiguous()
+    check(F.wxx_fftconv_spectrum_gated(out.buffer.ptr, x.buffer.ptr, x.offset, x.stride[0],
+                                       x.stride[1], x.stride[2], H.ptr, H.stride[0], B, D, L, n,
+                                       out_len, gate.buffer.ptr, gate.offset, gate.stride[0],
+                                       gate.stride[1], gate.stride[2]), "fftconv_spectrum")
+    return out
+
+
 def fftconv(x, h, n, out_len=None, gate=None):
     """Causal FFT convolution ``irfft(rfft(x, n) * rfft(h, n), n)[..., :out_len]``
     of a (B, D, L) view ``x`` with a (D, Lh) filter ``h`` broadcast over the

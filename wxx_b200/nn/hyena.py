@@ -124,6 +124,29 @@ class HyenaOperator(Module):
         pe = self.filter_mlp[0].positional_encoding(length)
         return functional.hyena_filters(pe, lin1, lin2, omegas.pop(), self.decay)
 
+    def _filter_spectra(self, length):
+        """Inference: the spectra of all this operator's filters at ``length``
+        (an (order * D, n/2 + 2) c64 tensor, filter i in rows i*D .. i*D + D),
+        made by two launches (the fused filter kernel and one rfft) and kept
+        until a filter weight, the decay or the length changes (buffer write
+        versions), or None when the fused filter kernel does not apply."""
+        from .module import _source_key
+
+        srcs = [self.decay]
+        for filt in self.filter_mlp:
+            srcs.extend(p for _, p in filt.named_parameters())
+        n = self._fft_size(length)
+        key = _source_key(srcs, length, n)
+        entry = self.__dict__.get("_spectra")
+        if entry is not None and entry[1] == key:
+            return entry[0]
+        hs = self._filters_fused(length)
+        if hs is None:
+            return None
+        spec = functional.filter_spectrum(hs.reshape((self.order * self.d_model, length)), n)
+        object.__setattr__(self, "_spectra", (spec, key))
+        return spec
+
     def forward(self, x, residual=None):
         _, length, _ = x.shape
         if context.MODE != 0:
@@ -144,13 +167,17 @@ class HyenaOperator(Module):
             v = self.short_conv(v)
             gates = [self.short_conv(g) for g in gates]
         z = v
-        hs = self._filters_fused(length) if context.MODE != 0 else None
+        spec = self._filter_spectra(length) if context.MODE != 0 else None
+        D = self.d_model
         for i in range(self.order):
-            if hs is not None:
-                h = hs[i]
-            else:
-                h = self.filter_mlp[i](length)
-                h = h * self._decay_window(i, length)
+            if spec is not None:
+                # the filter spectra do not depend on the input: kept between calls
+                z = functional.fftconv_spectrum(z, spec[i * D:(i + 1) * D],
+                                                self._fft_size(length), out_len=length,
+                                                gate=gates[i])
+                continue
+            h = self.filter_mlp[i](length)
+            h = h * self._decay_window(i, length)
             z = self.fft_conv1d(z, h, gate=gates[i])
         if residual is not None:
             # the block's residual add rides in the projection's GEMM epilogue
