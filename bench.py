@@ -503,14 +503,30 @@ def run_sweep(args, rank, world, local):
     for _ in range(args.warmup):
         sw.op(F, *devs)
     dev.synchronize()
+    # The op is recorded once as a CUDA graph and each timed step is one
+    # replay: the host's Python and argument checks for a call of ~0.1 ms
+    # would otherwise show up as idle device time inside the events
+    # (``--eager`` times the direct calls).
+    graph = None
+    if not args.eager:
+        graph = wxx.graph.capture(lambda: sw.op(F, *devs))
+        for _ in range(2):
+            graph.replay()
+        dev.synchronize()
     if dist is not None:
         dist.barrier()
     sampler = ClockSampler(local)
     sampler.start()
     n0 = dev.launch_count()
-    ms = timed(args.steps, lambda: sw.op(F, *devs))
-    launches = dev.launch_count() - n0 - (args.steps * L2Flush.LAUNCHES if flush is not None else 0)
+    ms = timed(args.steps, graph.replay if graph is not None else (lambda: sw.op(F, *devs)))
+    if graph is not None:
+        launches = graph.stats()["kernels"] * args.steps
+    else:
+        launches = dev.launch_count() - n0 - (args.steps * L2Flush.LAUNCHES if flush is not None else 0)
     clocks = sampler.stop()
+    if graph is not None:
+        dev.synchronize()
+        graph.close()
     if dist is not None:
         import torch
 
@@ -561,7 +577,8 @@ def run_sweep(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{sw.name} {sw.shapes}", "l2": L2_FLUSHED
-                   if sw.flush_l2 else "inputs larger than L2", "parallelism": "replicas"},
+                   if sw.flush_l2 else "inputs larger than L2", "parallelism": "replicas",
+                   "launch": "eager" if args.eager else "CUDA graph of the op, one replay per step"},
         "roofline": {"kernel": sw.kernel, "bound": sw.bound, "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s" if sw.bound == "tensor" else "GB/s",
                      "frac": achieved / peak, "peak_basis": basis,

@@ -54,26 +54,33 @@ __host__ __device__ constexpr int mma_warp1(int nt) { return 2 + nt * 4; }   // 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;   // raise the max used for P only past 2^8
 
-// 2^x on the FMA pipe, for x <= 8 (arguments here are t - m with t <= m + 8).
-// x = n + f with n = round(x) (adding 1.5 * 2^23 rounds x into the low
-// mantissa bits) and f in [-0.5, 0.5]; 2^f by a degree-4 polynomial fitted
-// here to 2^f on [-0.5, 0.5] (relative-error least squares on Chebyshev
-// nodes, max relative error 2.7e-6 in fp32 Horner form); 2^n is added to the
-// exponent field (p >= 0.7, so with n >= -126 the field stays >= 0).
-// x < -126 (masked keys: -inf) gives exactly 0.  The SFU's ex2 issues at
-// about one warp instruction per 16 cycles per SM sub-partition and is the
-// softmax's bottleneck, so 3 of every 8 exponentials use this form.
-__device__ __forceinline__ float exp2_fma(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float r = xc + 12582912.0f;           // 0x4B400000 + round(xc) in the bits
-  const float f = xc - (r - 12582912.0f);
-  float p = fmaf(9.570609884e-03f, f, 5.591790373e-02f);
-  p = fmaf(p, f, 2.402473231e-01f);
-  p = fmaf(p, f, 6.931218067e-01f);
-  p = fmaf(p, f, 9.999992652e-01f);
-  const int n = __float_as_int(r) - 0x4B400000;
-  const float y = __int_as_float(__float_as_int(p) + (n << 23));
-  return x < -126.0f ? 0.0f : y;
+// 2^x on the FMA pipe for two arguments at once, x <= 8 (arguments here are
+// t - m with t <= m + 8).  x = n + f with n = round(x) (adding 1.5 * 2^23
+// rounds x into the low mantissa bits) and f in [-0.5, 0.5]; 2^f by a
+// degree-4 polynomial fitted here to 2^f on [-0.5, 0.5] (relative-error least
+// squares on Chebyshev nodes, max relative error 2.7e-6 in fp32 Horner form);
+// 2^n is added to the exponent field (p >= 0.7, so with n >= -126 the field
+// stays >= 0; the low bits of r hold n + 0x4B400000, whose 0x4B400000 part
+// shifts out of a 32-bit word).  x < -126 (masked keys: -inf) gives exactly
+// 0.  The adds and the Horner steps run as packed fp32 pairs.  The SFU's ex2
+// issues at about one warp instruction per 16 cycles per SM sub-partition
+// and would be the softmax's bottleneck alone, so 3 of every 8 exponentials
+// use this form.
+__device__ __forceinline__ void exp2_fma2(float x0, float x1, float& y0, float& y1) {
+  const float xc0 = fmaxf(x0, -126.0f), xc1 = fmaxf(x1, -126.0f);
+  float r0, r1, t0, t1, f0, f1;
+  add2(r0, r1, xc0, xc1, 12582912.0f, 12582912.0f);    // 0x4B400000 + round(xc) in the bits
+  sub2(t0, t1, r0, r1, 12582912.0f, 12582912.0f);
+  sub2(f0, f1, xc0, xc1, t0, t1);
+  float p0, p1;
+  fma2(p0, p1, f0, f1, 9.570609884e-03f, 9.570609884e-03f, 5.591790373e-02f, 5.591790373e-02f);
+  fma2(p0, p1, p0, p1, f0, f1, 2.402473231e-01f, 2.402473231e-01f);
+  fma2(p0, p1, p0, p1, f0, f1, 6.931218067e-01f, 6.931218067e-01f);
+  fma2(p0, p1, p0, p1, f0, f1, 9.999992652e-01f, 9.999992652e-01f);
+  const float z0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(r0) << 23));
+  const float z1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(r1) << 23));
+  y0 = x0 < -126.0f ? 0.0f : z0;
+  y1 = x1 < -126.0f ? 0.0f : z1;
 }
 
 
@@ -435,28 +442,34 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       // Every key of the block visible to every row of the warp, no mask:
       // the common case skips the per-key tests (warp-uniform branch).
       const bool full = !HAS_MASK && (k0 + BKV <= warp_lim);
+      // Row max over the block: three-input max, 8 independent chains.
       float mm[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) mm[c] = -INFINITY;
       if (full) {
 #pragma unroll
-        for (int i = 0; i < BKV; ++i) mm[i & 7] = fmaxf(mm[i & 7], ATT_X(i));
+        for (int i = 0; i < BKV; i += 2)
+          mm[(i >> 1) & 7] = fmax3(mm[(i >> 1) & 7], ATT_X(i), ATT_X(i + 1));
       } else {
 #pragma unroll
-        for (int i = 0; i < BKV; ++i) {
+        for (int i = 0; i < BKV; i += 2) {
           const int key = k0 + i;
-          float tv = ATT_X(i) * sl2;
+          float tv0, tv1;
+          mul2(tv0, tv1, ATT_X(i), ATT_X(i + 1), sl2, sl2);
           if (HAS_MASK) {
-            float mv = (mrow != nullptr && key < lim) ? __ldg(mrow + key) : 0.f;
-            tv = fmaf(mv, kLog2e, tv);
+            const float mv0 = (mrow != nullptr && key < lim) ? __ldg(mrow + key) : 0.f;
+            const float mv1 = (mrow != nullptr && key + 1 < lim) ? __ldg(mrow + key + 1) : 0.f;
+            tv0 = fmaf(mv0, kLog2e, tv0);
+            tv1 = fmaf(mv1, kLog2e, tv1);
           }
-          tv = key < lim ? tv : -INFINITY;
-          if (i < 32) xa[i & 31] = tv; else xb[i & 31] = tv;
-          mm[i & 7] = fmaxf(mm[i & 7], tv);
+          tv0 = key < lim ? tv0 : -INFINITY;
+          tv1 = key + 1 < lim ? tv1 : -INFINITY;
+          if (i < 32) { xa[i & 31] = tv0; xa[(i + 1) & 31] = tv1; }
+          else { xb[i & 31] = tv0; xb[(i + 1) & 31] = tv1; }
+          mm[(i >> 1) & 7] = fmax3(mm[(i >> 1) & 7], tv0, tv1);
         }
       }
-      float mx = fmaxf(fmaxf(fmaxf(mm[0], mm[1]), fmaxf(mm[2], mm[3])),
-                       fmaxf(fmaxf(mm[4], mm[5]), fmaxf(mm[6], mm[7])));
+      float mx = fmax3(fmax3(mm[0], mm[1], mm[2]), fmax3(mm[3], mm[4], mm[5]), fmaxf(mm[6], mm[7]));
       if (full) mx *= sl2;                        // scale > 0: max commutes with it
       // Raise the max P is taken against only when it grew past 2^8 (always
       // on the first block, which starts O); otherwise P <= 2^8 stays exact
@@ -472,23 +485,43 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       }
       // A row that sees no key yet keeps p = 0 (m_used = -inf, every t = -inf).
       const float m_use = (m_used == -INFINITY) ? 0.f : m_used;
+      // Probabilities two keys at a time (packed fp32 arithmetic); key i adds
+      // into acc[i & 7] as a scalar loop would.
       float acc[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc[c] = 0.f;
 #pragma unroll
-      for (int i = 0; i < BKV; ++i) {
-        const float arg = full ? fmaf(ATT_X(i), sl2, -m_use) : ATT_X(i) - m_use;
+      for (int i = 0; i < BKV; i += 2) {
+        float a0, a1;
+        if (full) fma2(a0, a1, ATT_X(i), ATT_X(i + 1), sl2, sl2, -m_use, -m_use);
+        else sub2(a0, a1, ATT_X(i), ATT_X(i + 1), m_use, m_use);
+        float p0, p1;
+        if ((i & 15) < 6) {
+          exp2_fma2(a0, a1, p0, p1);
+        } else {
+          p0 = fast_exp2(a0);
+          p1 = fast_exp2(a1);
+        }
         // p in [0, 2^8] (finite, non-negative) rounded to the nearest TF32
-        // value by integer ops on its bits (ties away from zero): the P V
-        // product then reads it exactly, and the row sum l below adds the
-        // same rounded values, so the weights applied to V sum to one.
-        // X3 keeps p exact (its low part goes through the Plo term).
-        const float pe = ((i & 7) < 3) ? exp2_fma(arg) : fast_exp2(arg);
-        const float pv = X3 ? pe : __uint_as_float((__float_as_uint(pe) + 0x1000u) & 0xFFFFE000u);
-        if (i < 32) xa[i & 31] = pv; else xb[i & 31] = pv;
-        acc[i & 7] += pv;
+        // value (ties away from zero): the P V product then reads it exactly,
+        // and the row sum l below adds the same rounded values, so the
+        // weights applied to V sum to one.  X3 keeps p exact (its low part
+        // goes through the Plo term).
+        if (!X3) {
+          p0 = tf32_rna(p0);
+          p1 = tf32_rna(p1);
+        }
+        if (i < 32) { xa[i & 31] = p0; xa[(i + 1) & 31] = p1; }
+        else { xb[i & 31] = p0; xb[(i + 1) & 31] = p1; }
+        add2(acc[i & 7], acc[(i + 1) & 7], acc[i & 7], acc[(i + 1) & 7], p0, p1);
       }
-      l_run += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+      {
+        float s0, s1, s2, s3, u0, u1;
+        add2(s0, s1, acc[0], acc[2], acc[1], acc[3]);
+        add2(s2, s3, acc[4], acc[6], acc[5], acc[7]);
+        add2(u0, u1, s0, s2, s1, s3);
+        l_run += u0 + u1;
+      }
       // P_j -> TMEM over the S_j columns just read (row = lane, one column
       // per key): the P V product takes its A operand from there.
       tmem_st_32x32(lane_addr + s * BKV, xa);
@@ -523,7 +556,7 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
           float v[32];
           tmem_ld_32x32(o_addr + c, v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= factor;
+          for (int i = 0; i < 32; i += 2) mul2(v[i], v[i + 1], v[i], v[i + 1], factor, factor);
           tmem_st_32x32(o_addr + c, v);
         }
       }
@@ -548,7 +581,7 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= inv;
+        for (int i = 0; i < 32; i += 2) mul2(v[i], v[i + 1], v[i], v[i + 1], inv, inv);
         if (!X3 && p.out_tf32) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = tf32_rna(v[i]);
