@@ -54,36 +54,6 @@ __host__ __device__ constexpr int mma_warp1(int nt) { return 2 + nt * 4; }   // 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.f;   // raise the max used for P only past 2^8
 
-// 2^x on the FMA pipe for two arguments at once, x <= 8 (arguments here are
-// t - m with t <= m + 8).  x = n + f with n = round(x) (adding 1.5 * 2^23
-// rounds x into the low mantissa bits) and f in [-0.5, 0.5]; 2^f by a
-// degree-4 polynomial fitted here to 2^f on [-0.5, 0.5] (relative-error least
-// squares on Chebyshev nodes, max relative error 2.7e-6 in fp32 Horner form);
-// 2^n is added to the exponent field (p >= 0.7, so with n >= -126 the field
-// stays >= 0; the low bits of r hold n + 0x4B400000, whose 0x4B400000 part
-// shifts out of a 32-bit word).  x < -126 (masked keys: -inf) gives exactly
-// 0.  The adds and the Horner steps run as packed fp32 pairs.  The SFU's ex2
-// issues at about one warp instruction per 16 cycles per SM sub-partition
-// and would be the softmax's bottleneck alone, so 3 of every 8 exponentials
-// use this form.
-__device__ __forceinline__ void exp2_fma2(float x0, float x1, float& y0, float& y1) {
-  const float xc0 = fmaxf(x0, -126.0f), xc1 = fmaxf(x1, -126.0f);
-  float r0, r1, t0, t1, f0, f1;
-  add2(r0, r1, xc0, xc1, 12582912.0f, 12582912.0f);    // 0x4B400000 + round(xc) in the bits
-  sub2(t0, t1, r0, r1, 12582912.0f, 12582912.0f);
-  sub2(f0, f1, xc0, xc1, t0, t1);
-  float p0, p1;
-  fma2(p0, p1, f0, f1, 9.570609884e-03f, 9.570609884e-03f, 5.591790373e-02f, 5.591790373e-02f);
-  fma2(p0, p1, p0, p1, f0, f1, 2.402473231e-01f, 2.402473231e-01f);
-  fma2(p0, p1, p0, p1, f0, f1, 6.931218067e-01f, 6.931218067e-01f);
-  fma2(p0, p1, p0, p1, f0, f1, 9.999992652e-01f, 9.999992652e-01f);
-  const float z0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(r0) << 23));
-  const float z1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(r1) << 23));
-  y0 = x0 < -126.0f ? 0.0f : z0;
-  y1 = x1 < -126.0f ? 0.0f : z1;
-}
-
-
 // X3: the fp32-faithful 3xTF32 form (one tile per CTA, one CTA per SM).
 // Each product x*y becomes hi(x)hi(y) + lo(x)hi(y) + hi(x)lo(y) where hi is
 // the operand as the tensor core reads it (the low 13 mantissa bits
@@ -495,21 +465,19 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
         float a0, a1;
         if (full) fma2(a0, a1, ATT_X(i), ATT_X(i + 1), sl2, sl2, -m_use, -m_use);
         else sub2(a0, a1, ATT_X(i), ATT_X(i + 1), m_use, m_use);
-        float p0, p1;
-        if ((i & 15) < 6) {
-          exp2_fma2(a0, a1, p0, p1);
-        } else {
-          p0 = fast_exp2(a0);
-          p1 = fast_exp2(a1);
-        }
+        // Every exponential on the SFU: its ex2 pipe keeps up with the rest
+        // of the loop (moving some onto an FMA-pipe polynomial measured
+        // slower, the issue slots being the tighter limit).
+        float p0 = fast_exp2(a0), p1 = fast_exp2(a1);
         // p in [0, 2^8] (finite, non-negative) rounded to the nearest TF32
-        // value (ties away from zero): the P V product then reads it exactly,
-        // and the row sum l below adds the same rounded values, so the
-        // weights applied to V sum to one.  X3 keeps p exact (its low part
-        // goes through the Plo term).
+        // value by integer ops on its bits (ties away from zero; two ALU
+        // instructions, fewer issue slots than the cvt.rna form): the P V
+        // product then reads it exactly, and the row sum l below adds the
+        // same rounded values, so the weights applied to V sum to one.  X3
+        // keeps p exact (its low part goes through the Plo term).
         if (!X3) {
-          p0 = tf32_rna(p0);
-          p1 = tf32_rna(p1);
+          p0 = __uint_as_float((__float_as_uint(p0) + 0x1000u) & 0xFFFFE000u);
+          p1 = __uint_as_float((__float_as_uint(p1) + 0x1000u) & 0xFFFFE000u);
         }
         if (i < 32) { xa[i & 31] = p0; xa[(i + 1) & 31] = p1; }
         else { xb[i & 31] = p0; xb[(i + 1) & 31] = p1; }
