@@ -75,9 +75,13 @@ struct ACfg {
   static constexpr int OFF_O = OFF_VLO + (X3 ? KVS * V_BYTES : 0);
   // NT = 1 stages O in its Q buffer (every S product has completed by then)
   static constexpr int SMEM = OFF_O + (NT == 2 ? NT * STAGE_O_BYTES : 0) + 1024;
-  // TMEM per tile: S double buffer (2 x 64 columns) then O (hd columns);
-  // X3 adds the Plo double buffer and Qlo.
-  static constexpr int TMEM_TILE = 2 * BKV + HD;
+  // TMEM per tile: SB S / P buffers of 64 columns then O (hd columns); X3
+  // adds the Plo double buffer and Qlo.  Three S buffers let the MMA thread
+  // issue S(j + 1) right after P(j - 1) V(j - 1) without waiting for that
+  // product to finish (it overwrites P(j - 2)); the 3xTF32 form keeps two,
+  // which also orders its Plo writes after the product that read them.
+  static constexpr int SB = X3 ? 2 : 3;
+  static constexpr int TMEM_TILE = SB * BKV + HD;
   static constexpr int PLO_COL = TMEM_TILE;
   static constexpr int QLO_COL = TMEM_TILE + 2 * BKV;
   static constexpr int TMEM_COLS = (NT == 2 || X3) ? 512 : 256;
@@ -133,7 +137,7 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full;
   __shared__ __align__(8) uint64_t k_full[C::KVS], k_empty[C::KVS], v_full[C::KVS], v_empty[C::KVS];
-  __shared__ __align__(8) uint64_t s_full[NT][2], p_full[NT], p_empty[NT];
+  __shared__ __align__(8) uint64_t s_full[NT][C::SB], p_full[NT][C::SB], p_empty[NT][C::SB];
   __shared__ __align__(8) uint64_t drain_bar[NT];
   __shared__ __align__(8) uint64_t klo_full[C::KVS], vlo_full[C::KVS], qlo_full;   // X3
   __shared__ uint32_t tmem_base_sh;
@@ -168,12 +172,12 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], NT);
     }
-    for (int t = 0; t < NT; ++t) {
-      mbar_init(&s_full[t][0], 1);
-      mbar_init(&s_full[t][1], 1);
-      mbar_init(&p_full[t], 128);
-      mbar_init(&p_empty[t], 1);
-    }
+    for (int t = 0; t < NT; ++t)
+      for (int sb = 0; sb < C::SB; ++sb) {
+        mbar_init(&s_full[t][sb], 1);
+        mbar_init(&p_full[t][sb], 128);
+        mbar_init(&p_empty[t][sb], 1);
+      }
     for (int t = 0; t < NT; ++t) mbar_init(&drain_bar[t], 1);
     if (X3) {
       for (int s = 0; s < C::KVS; ++s) {
@@ -247,15 +251,15 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       tc_fence_after();
       auto issue_pv = [&](int jj) -> bool {
         const int s = jj % C::KVS;       // V stage
-        const int sb = jj & 1;           // TMEM S / P buffer
+        const int sb = jj % C::SB;       // TMEM S / P buffer
         if (!mbar_wait(&v_full[s], (jj / C::KVS) & 1, &abort_flag, p.err)) return false;
         if (X3 && !mbar_wait(&vlo_full[s], (jj / C::KVS) & 1, &abort_flag, p.err)) return false;
         tc_fence_after();
         if (jj < nt) {
-          if (!mbar_wait(&p_full[t], jj & 1, &abort_flag, p.err)) return false;
+          if (!mbar_wait(&p_full[t][sb], (jj / C::SB) & 1, &abort_flag, p.err)) return false;
           tc_fence_after();
           const uint32_t sv = sbase + C::OFF_V + s * C::V_BYTES;
-          const uint32_t d = tmem_base + t * C::TMEM_TILE + 2 * BKV;
+          const uint32_t d = tmem_base + t * C::TMEM_TILE + C::SB * BKV;
           const uint32_t pa = tmem_base + t * C::TMEM_TILE + sb * BKV;  // P_t(jj) over S_t(jj)
 #pragma unroll
           for (int kk = 0; kk < BKV / 8; ++kk) {
@@ -276,21 +280,25 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
               umma_tf32_ts(d, pa + kk * 8, bd, idesc_o, 1u);
             }
           }
-          umma_commit(&p_empty[t]);
+          umma_commit(&p_empty[t][sb]);
         }
         umma_commit(&v_empty[s]);
         return true;
       };
       for (int j = 0; j < n_kv && ok; ++j) {
         const int s = j % C::KVS;        // K stage
-        const int sb = j & 1;            // TMEM S buffer
+        const int sb = j % C::SB;        // TMEM S buffer
         if (!mbar_wait(&k_full[s], (j / C::KVS) & 1, &abort_flag, p.err)) { ok = false; break; }
         if (X3 && !mbar_wait(&klo_full[s], (j / C::KVS) & 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         if (j < nt) {
-          // S_t(j) overwrites the columns P_t(j-2) occupied: that P V product
-          // must have finished reading them.
-          if (j >= 2 && !mbar_wait(&p_empty[t], (j - 2) & 1, &abort_flag, p.err)) { ok = false; break; }
+          // S_t(j) overwrites the columns P_t(j - SB) occupied: that P V
+          // product must have finished reading them.
+          if (j >= C::SB &&
+              !mbar_wait(&p_empty[t][sb], ((j - C::SB) / C::SB) & 1, &abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t sk = sbase + C::OFF_K + s * C::K_BYTES;
           const uint32_t d = tmem_base + t * C::TMEM_TILE + sb * BKV;
@@ -357,7 +365,7 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
     const int qrow = qt + row;
     const int nt = tile ? n_t1 : n_t0;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + tile * C::TMEM_TILE;
-    const uint32_t o_addr = lane_addr + 2 * BKV;
+    const uint32_t o_addr = lane_addr + C::SB * BKV;
     const float sl2 = p.scale * kLog2e;
     // Keys [0, lim) are visible to this row (causal stops at the query, Sk at
     // the end); warp_lim is the smallest lim of the warp's 32 rows.
@@ -396,8 +404,8 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
     }
 
     for (int j = 0; j < nt && ok; ++j) {
-      const int s = j & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[tile][s], (j >> 1) & 1, &abort_flag, p.err))) {
+      const int s = j % C::SB;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[tile][s], (j / C::SB) & 1, &abort_flag, p.err))) {
         ok = false;
         break;
       }
@@ -506,17 +514,16 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
         tmem_st_32x32(plo_addr + 32, xb);
       }
 #undef ATT_X
-      // The previous P V product has finished: O holds every block < j (needed
-      // by a rescale).  Waiting every block also keeps this barrier's phases
-      // within the one-phase window a parity wait can tell apart.
-      if (j >= 1) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[tile], (j - 1) & 1, &abort_flag, p.err))) {
+      if (warp_rescale) {
+        // The previous P V product has finished: O holds every block < j.
+        // (No barrier of the ring runs more than one phase ahead of these
+        // waits: P(j - 1 + SB) cannot exist before this block's P.)
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[tile][(j - 1) % C::SB],
+                                               ((j - 1) / C::SB) & 1, &abort_flag, p.err))) {
           ok = false;
           break;
         }
         tc_fence_after();
-      }
-      if (warp_rescale) {
         // O in TMEM holds blocks < j relative to the old max: scale the rows
         // that raised theirs before P_j V_j accumulates on top.
 #pragma unroll
@@ -529,12 +536,13 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
         }
       }
       tc_fence_before();
-      mbar_arrive(&p_full[tile]);
+      mbar_arrive(&p_full[tile][s]);
     }
     if (ok && nt >= 1) {
       // Last P V product done -> O complete in TMEM and the P buffer free for
       // staging the output.
-      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[tile], (nt - 1) & 1, &abort_flag, p.err));
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[tile][(nt - 1) % C::SB],
+                                             ((nt - 1) / C::SB) & 1, &abort_flag, p.err));
       tc_fence_after();
     }
     if (ok && nt >= 1) {
