@@ -164,6 +164,10 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
   const int n_kv = max(n_t0, n_t1);
 
   if (threadIdx.x == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+    prefetch_tmap(&tm_o);
     abort_flag = 0;
     mbar_init(&q_full, 1);
     for (int s = 0; s < C::KVS; ++s) {
@@ -187,6 +191,15 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       mbar_init(&qlo_full, 128);
     }
     fence_barrier_init();
+    // The query tiles start loading before the TMEM allocation and the block
+    // barrier (thread 0 is the TMA producer and initialised the barriers).
+    mbar_arrive_expect_tx(&q_full, NT * C::Q_BYTES);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int a = 0; a < HD / 32; ++a)
+        tma_load_4d(smem_u32(smem + t * C::Q_BYTES + a * (BQ * 128)), &tm_q, &q_full, a * 32, h,
+                    q0 + t * BQ, b);
   }
   if (warp == 1) tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
   tc_fence_before();
@@ -198,13 +211,6 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(&q_full, NT * C::Q_BYTES);
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int a = 0; a < HD / 32; ++a)
-          tma_load_4d(smem_u32(smem + t * C::Q_BYTES + a * (BQ * 128)), &tm_q, &q_full, a * 32, h,
-                      q0 + t * BQ, b);
       int last_k[C::KVS], last_v[C::KVS];
 #pragma unroll
       for (int s = 0; s < C::KVS; ++s) last_k[s] = last_v[s] = -1;
@@ -573,7 +579,9 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
           bulk_commit();
         }
       }
-      if (lane == 0) bulk_wait<0>();
+      // The staging buffer only has to be read before the CTA exits; the
+      // stores themselves complete before the grid does.
+      if (lane == 0) bulk_wait_read<0>();
     }
   }
 
