@@ -73,3 +73,28 @@ def test_capture_that_syncs_fails_cleanly():
     # the library still works after the failed capture
     np.testing.assert_array_equal(F.pointwise(a, a, 2).numpy(), np.arange(8, dtype=np.float32) ** 2)
     assert wxx.backend.device_status() == 0
+
+
+def test_tensor_outliving_its_graph_keeps_the_arena(rng):
+    """A tensor allocated inside a capture and still referenced when its graph
+    is closed keeps the graph's arena reserved: blocks allocated after the
+    close never overlap it, and freeing the stale tensor later releases
+    nothing but the arena (the blocks allocated meanwhile keep their data)."""
+    wxx = _w()
+    F = wxx.functional
+    x = F.from_numpy(rng.standard_normal((256, 256)).astype(np.float32))
+    g = wxx.graph.capture(lambda t: F.pointwise(t, t, 0), x)
+    out = g.replay()
+    expect = 2.0 * x.numpy()
+    assert np.array_equal(out.numpy(), expect)
+    g.close()
+    lo = out.buffer.ptr
+    keep = [F.from_numpy(np.full((256, 256), float(i), np.float32)) for i in range(64)]
+    for k in keep:
+        assert not (lo <= k.buffer.ptr < lo + 256 * 256 * 4)
+    assert np.array_equal(out.numpy(), expect)      # still readable after the close
+    del out                                         # the arena's last tensor
+    more = [F.from_numpy(np.full((256, 256), -1.0, np.float32)) for _ in range(64)]
+    for i, k in enumerate(keep):
+        assert np.all(k.numpy() == float(i))
+    assert all(np.all(m.numpy() == -1.0) for m in more)

@@ -9,21 +9,23 @@
 // O is written in the merged (B, S, H*hd) layout the output projection reads,
 // so the four head split/merge copies disappear too.
 //
-// One CTA owns two 128-row query tiles (A, B) of one (b, h); keys/values come
-// in blocks of 64 shared by both tiles:
-//   warp 0      TMA producer (Q once; K_j and V_j double-buffered, separate
-//               barriers so K_{j+2} loads as soon as S_j has read K_j)
-//   warps 1, 10 one tcgen05.mma-issuing thread per tile (warp 1 also owns
-//               the TMEM allocation), per block j: S_t(j) = Q_t K_j^T
-//               (M=128, N=64, K=hd), then O_t += P_t(j-1) V_{j-1} (M=128,
-//               N=hd, K=64; P from TMEM, V MN-major with the 32B-atom
-//               swizzle), O_t accumulated in TMEM across all blocks
-//   warps 2..5  tile A, warps 6..9 tile B: one query row per thread,
-//               tcgen05.ld S, online softmax in the log2 domain, P written
-//               back into TMEM over S (tcgen05.st; the P V product reads its
-//               A operand from TMEM), final O / l through a TMA store
-// Two softmax warpgroups interleave on every SM sub-partition, so one tile's
-// exponentials overlap the other's, and both overlap the tensor core.
+// A CTA owns one 128-row query tile of one (b, h) (the default: three CTAs
+// per SM) or two tiles sharing each K / V block (WXX_ATTN_TILES=2, one CTA
+// per SM); keys / values come in blocks of 64:
+//   warp 0      TMA producer (Q once; K_j and V_j in stages with separate
+//               barriers, so K_{j+1} loads as soon as S_j has read K_j)
+//   warp 1      (and warp 10 for a second tile) one tcgen05.mma-issuing
+//               thread per tile (warp 1 also owns the TMEM allocation): per
+//               block j S_t(j) = Q_t K_j^T (M=128, N=64, K=hd) and
+//               O_t += P_t(j) V_j (M=128, N=hd, K=64; P from TMEM, V MN-major
+//               with the 32B-atom swizzle), O_t accumulated in TMEM
+//   warps 2..5  (6..9 for a second tile) softmax: one query row per thread,
+//               tcgen05.ld S, online softmax in the log2 domain on packed
+//               fp32 pairs, P written back into TMEM over S (tcgen05.st; the
+//               P V product reads its A operand from TMEM), final O / l
+//               through a TMA store
+// Every SM sub-partition runs a softmax warp of each resident tile, so one
+// tile's exponentials overlap another's S and P V products.
 // The running max used for P is only raised (and O in TMEM rescaled) when a
 // row's max grows by more than 2^8 in probability units; P and the row sum l
 // always use the same max, so O / l is unchanged by the laziness.
@@ -46,8 +48,8 @@ namespace {
 constexpr int BQ = 128;   // query rows per tile (UMMA M)
 constexpr int BKV = 64;   // keys per block (UMMA N of S, K of PV)
 // NT query tiles per CTA: 2 (one CTA per SM, K / V blocks shared by both
-// tiles) or 1 (two CTAs per SM: one CTA's setup, first loads and output
-// drain overlap the other's steady state).  Warps: producer, tile 0's MMA
+// tiles) or 1 (three CTAs per SM: one CTA's setup, loads, waits for S and
+// output drain overlap the others' work).  Warps: producer, tile 0's MMA
 // thread, 4 softmax warps per tile, then (NT = 2) tile 1's MMA thread.
 __host__ __device__ constexpr int att_threads(int nt) { return 64 + nt * 128 + (nt - 1) * 32; }
 __host__ __device__ constexpr int mma_warp1(int nt) { return 2 + nt * 4; }   // tile 1's MMA warp (NT = 2)
@@ -63,10 +65,16 @@ constexpr float kRescaleLog2 = 8.f;   // raise the max used for P only past 2^8
 // softmax warps, which also keep P unrounded.
 template <int HD, int NT, bool X3 = false>
 struct ACfg {
+  // One TF32 tile per CTA runs three CTAs per SM: one S / P buffer and one
+  // K / V stage each (64 KB of shared memory, 128 TMEM columns), so while one
+  // CTA's softmax waits for its next S, the other two keep the tensor core
+  // and the SFU busy (measured faster than two CTAs with three S buffers and
+  // two stages each, which spend the wait inside one CTA).
+  static constexpr bool THREE = NT == 1 && !X3;
   static constexpr int Q_BYTES = BQ * HD * 4;          // per tile: 32 KB (hd 64)
   static constexpr int K_BYTES = BKV * HD * 4;         // 16 KB
   static constexpr int V_BYTES = BKV * HD * 4;         // 16 KB
-  static constexpr int KVS = (NT == 2 && !X3) ? 4 : 2; // K / V pipeline stages
+  static constexpr int KVS = (NT == 2 && !X3) ? 4 : (THREE ? 1 : 2); // K / V pipeline stages
   static constexpr int STAGE_O_BYTES = 4 * 4096;       // per tile: O staging for the TMA store
   static constexpr int OFF_K = NT * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KVS * K_BYTES;
@@ -76,22 +84,24 @@ struct ACfg {
   // NT = 1 stages O in its Q buffer (every S product has completed by then)
   static constexpr int SMEM = OFF_O + (NT == 2 ? NT * STAGE_O_BYTES : 0) + 1024;
   // TMEM per tile: SB S / P buffers of 64 columns then O (hd columns); X3
-  // adds the Plo double buffer and Qlo.  Three S buffers let the MMA thread
-  // issue S(j + 1) right after P(j - 1) V(j - 1) without waiting for that
-  // product to finish (it overwrites P(j - 2)); the 3xTF32 form keeps two,
-  // which also orders its Plo writes after the product that read them.
-  static constexpr int SB = X3 ? 2 : 3;
+  // adds the Plo double buffer and Qlo.  With two tiles per CTA (one CTA per
+  // SM) three S buffers let the MMA thread issue S(j + 1) right after
+  // P(j - 1) V(j - 1) without waiting for that product to finish (it
+  // overwrites P(j - 2)); the 3xTF32 form keeps two, which also orders its
+  // Plo writes after the product that read them.
+  static constexpr int SB = X3 ? 2 : (THREE ? 1 : 3);
   static constexpr int TMEM_TILE = SB * BKV + HD;
   static constexpr int PLO_COL = TMEM_TILE;
   static constexpr int QLO_COL = TMEM_TILE + 2 * BKV;
-  static constexpr int TMEM_COLS = (NT == 2 || X3) ? 512 : 256;
+  static constexpr int TMEM_COLS = (NT == 2 || X3) ? 512 : (THREE ? 128 : 256);
   static constexpr bool ONE_PER_SM = NT == 2 || X3;
+  static constexpr int PER_SM = ONE_PER_SM ? 1 : (THREE ? 3 : 2);
   static_assert(NT == 1 || NT == 2, "one or two query tiles per CTA");
   static_assert(!X3 || NT == 1, "the 3xTF32 form runs one tile per CTA");
   static_assert(NT * TMEM_TILE <= TMEM_COLS, "TMEM layout");
   static_assert(!X3 || QLO_COL + HD <= TMEM_COLS, "TMEM layout (3xTF32)");
   static_assert(NT == 2 || Q_BYTES >= STAGE_O_BYTES, "O staging in the Q buffer");
-  static_assert(SMEM <= (ONE_PER_SM ? 227 * 1024 : 112 * 1024), "shared memory layout");
+  static_assert(SMEM <= (ONE_PER_SM ? 227 * 1024 : (THREE ? 74 : 112) * 1024), "shared memory layout");
 };
 
 __device__ __forceinline__ float tf32_low(float x) {
@@ -126,7 +136,7 @@ struct AttnParams {
 };
 
 template <int HD, bool HAS_MASK, int NT, bool X3 = false>
-__global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, X3>::ONE_PER_SM ? 1 : 2)
+__global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, X3>::PER_SM)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
@@ -191,8 +201,9 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       mbar_init(&qlo_full, 128);
     }
     fence_barrier_init();
-    // The query tiles start loading before the TMEM allocation and the block
-    // barrier (thread 0 is the TMA producer and initialised the barriers).
+    // The query tiles and the first K / V stages start loading before the
+    // TMEM allocation and the block barrier (thread 0 is the TMA producer and
+    // initialised the barriers; the first fill of a stage waits for nothing).
     mbar_arrive_expect_tx(&q_full, NT * C::Q_BYTES);
 #pragma unroll
     for (int t = 0; t < NT; ++t)
@@ -200,6 +211,18 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       for (int a = 0; a < HD / 32; ++a)
         tma_load_4d(smem_u32(smem + t * C::Q_BYTES + a * (BQ * 128)), &tm_q, &q_full, a * 32, h,
                     q0 + t * BQ, b);
+    for (int j = 0; j < min(C::KVS, n_kv); ++j) {
+      mbar_arrive_expect_tx(&k_full[j], C::K_BYTES);
+#pragma unroll
+      for (int a = 0; a < HD / 32; ++a)
+        tma_load_4d(smem_u32(smem + C::OFF_K + j * C::K_BYTES + a * (BKV * 128)), &tm_k,
+                    &k_full[j], a * 32, h, j * BKV, b);
+      mbar_arrive_expect_tx(&v_full[j], C::V_BYTES);
+#pragma unroll
+      for (int a = 0; a < HD / 32; ++a)
+        tma_load_4d(smem_u32(smem + C::OFF_V + j * C::V_BYTES + a * (BKV * 128)), &tm_v,
+                    &v_full[j], a * 32, h, j * BKV, b);
+    }
   }
   if (warp == 1) tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
   tc_fence_before();
@@ -211,10 +234,11 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       bool ok = true;
+      const int pre = min(C::KVS, n_kv);   // stages filled before the block barrier
       int last_k[C::KVS], last_v[C::KVS];
 #pragma unroll
-      for (int s = 0; s < C::KVS; ++s) last_k[s] = last_v[s] = -1;
-      for (int j = 0; j < n_kv && ok; ++j) {
+      for (int s = 0; s < C::KVS; ++s) last_k[s] = last_v[s] = s < pre ? s : -1;
+      for (int j = pre; j < n_kv && ok; ++j) {
         const int s = j % C::KVS;
         const uint32_t par = ((j / C::KVS) & 1) ^ 1;
         if (!mbar_wait(&k_empty[s], par, &abort_flag, p.err)) { ok = false; break; }
@@ -294,6 +318,8 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
       for (int j = 0; j < n_kv && ok; ++j) {
         const int s = j % C::KVS;        // K stage
         const int sb = j % C::SB;        // TMEM S buffer
+        // One S buffer: S(j) overwrites P(j - 1), so P(j - 1) V(j - 1) goes first.
+        if (C::SB == 1 && j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
         if (!mbar_wait(&k_full[s], (j / C::KVS) & 1, &abort_flag, p.err)) { ok = false; break; }
         if (X3 && !mbar_wait(&klo_full[s], (j / C::KVS) & 1, &abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
@@ -333,7 +359,7 @@ __global__ void __launch_bounds__(att_threads(NT) + (X3 ? 32 : 0), ACfg<HD, NT, 
           umma_commit(&s_full[t][sb]);
         }
         umma_commit(&k_empty[s]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (C::SB > 1 && j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && n_kv >= 1) issue_pv(n_kv - 1);
       umma_commit(&drain_bar[t]);

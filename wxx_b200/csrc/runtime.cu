@@ -67,8 +67,14 @@ struct Arena {
   // not allocate), and kernels recorded before the release may still read the
   // block on every replay -- so they are freed when the graph is destroyed.
   std::vector<void*> deferred;
+  // Destroyed while tensors allocated inside it were still alive: the arena
+  // keeps its memory (in g_arenas, so their frees are recognised) until the
+  // last of them is freed.  Releasing it earlier would let the pool hand the
+  // range to new blocks, and a late free of an arena pointer could then
+  // release a live block that happens to start at the same address.
+  bool dead = false;
 };
-std::vector<Arena*> g_arenas;                    // graphs alive (guarded by g.mu)
+std::vector<Arena*> g_arenas;                    // arenas with memory (guarded by g.mu)
 Arena* g_capture = nullptr;                      // arena of the open capture
 
 bool arena_alloc(Arena* a, size_t sz, void** out) {
@@ -325,10 +331,18 @@ WXX_EXPORT int wxx_free(void* p) {
         return WXX_E_ARG;
       }
       // Inside the capture the block is reused by later allocations; after
-      // it, replays still write there, so it stays reserved.
-      if (a == g_capture) {
-        arena_release(a, p, ia->second);
-        a->live.erase(ia);
+      // it, replays still write there, so it stays reserved (only no longer
+      // counted as held by a tensor).
+      if (a == g_capture) arena_release(a, p, ia->second);
+      a->live.erase(ia);
+      if (a->dead && a->live.empty()) {
+        for (size_t i = 0; i < g_arenas.size(); ++i)
+          if (g_arenas[i] == a) {
+            g_arenas.erase(g_arenas.begin() + i);
+            break;
+          }
+        cudaFreeAsync(a->base, wxx::stream());
+        delete a;
       }
       return WXX_OK;
     }
@@ -631,18 +645,26 @@ WXX_EXPORT int wxx_graph_destroy(void* handle) {
   }
   cudaError_t e = cudaStreamSynchronize(wxx::stream());
   if (a->exec) cudaGraphExecDestroy(a->exec);
-  cudaFreeAsync(a->base, wxx::stream());
+  a->exec = nullptr;
   for (void* p : a->deferred) cudaFreeAsync(p, wxx::stream());
   a->deferred.clear();
   {
     std::lock_guard<std::mutex> lk(g.mu);
-    for (size_t i = 0; i < g_arenas.size(); ++i)
-      if (g_arenas[i] == a) {
-        g_arenas.erase(g_arenas.begin() + i);
-        break;
-      }
+    if (!a->live.empty()) {
+      a->dead = true;   // freed with the last of its tensors (wxx_free)
+      a = nullptr;
+    } else {
+      for (size_t i = 0; i < g_arenas.size(); ++i)
+        if (g_arenas[i] == a) {
+          g_arenas.erase(g_arenas.begin() + i);
+          break;
+        }
+    }
   }
-  delete a;
+  if (a != nullptr) {
+    cudaFreeAsync(a->base, wxx::stream());
+    delete a;
+  }
   if (e != cudaSuccess) {
     wxx::set_error("wxx_graph_destroy: %s", cudaGetErrorString(e));
     return WXX_E_CUDA;
