@@ -551,6 +551,86 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(float* __restrict__ y,
   }
 }
 
+// norm_warp_kernel with 16-byte accesses: lane l holds the float4 quads
+// l, l + 32, ... of its row (Q of them, n <= 128 Q, n a multiple of 4 and
+// every pointer 16-byte aligned).  A quarter of the load / store instructions
+// of the scalar form, the same two-pass mean / variance.
+template <int Q>
+__global__ void __launch_bounds__(256) norm_warp4_kernel(float* __restrict__ y,
+                                                         float* __restrict__ stat0,
+                                                         float* __restrict__ stat1,
+                                                         const float* __restrict__ x,
+                                                         const float* __restrict__ g,
+                                                         const float* __restrict__ b,
+                                                         int64_t rows, int n, float eps, int kind) {
+  const bool rnd = (kind & 2) != 0;
+  kind &= 1;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int l = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* p = reinterpret_cast<const float4*>(x + row * n);
+  float4* q = reinterpret_cast<float4*>(y + row * n);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  const int n4 = n >> 2;
+  float4 v[Q];
+#pragma unroll
+  for (int k = 0; k < Q; ++k) {
+    const int c = k * 32 + l;
+    v[k] = c < n4 ? p[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean = 0.f, inv;
+  if (kind == 0) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < Q; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    mean = warp_sum(s) / (float)n;
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < Q; ++k) {
+      if (k * 32 + l < n4) {
+        const float d0 = v[k].x - mean, d1 = v[k].y - mean, d2 = v[k].z - mean, d3 = v[k].w - mean;
+        ss += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+      }
+    }
+    const float var = fmaxf(0.f, warp_sum(ss) / (float)n);
+    inv = var > 0.f ? rsqrtf(var + eps) : 0.f;
+  } else {
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < Q; ++k)
+      ss += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+    const float ms = warp_sum(ss) / (float)n;
+    inv = ms > 0.f ? rsqrtf(ms + eps) : 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < Q; ++k) {
+    const int c = k * 32 + l;
+    if (c < n4) {
+      const float4 gg = __ldg(g4 + c);
+      float4 o;
+      if (kind == 0) {
+        const float4 bb = __ldg(b4 + c);
+        o = make_float4((v[k].x - mean) * inv * gg.x + bb.x, (v[k].y - mean) * inv * gg.y + bb.y,
+                        (v[k].z - mean) * inv * gg.z + bb.z, (v[k].w - mean) * inv * gg.w + bb.w);
+      } else {
+        o = make_float4(v[k].x * inv * gg.x, v[k].y * inv * gg.y, v[k].z * inv * gg.z,
+                        v[k].w * inv * gg.w);
+      }
+      if (rnd) o = make_float4(tf32_rna(o.x), tf32_rna(o.y), tf32_rna(o.z), tf32_rna(o.w));
+      q[c] = o;
+    }
+  }
+  if (l == 0) {
+    if (kind == 0) {
+      if (stat0) stat0[row] = mean;
+      if (stat1) stat1[row] = inv;
+    } else if (stat0) {
+      stat0[row] = inv;
+    }
+  }
+}
+
 // Generic (outer, reduce, inner) norm: one CTA per (o, i) column, two reads.
 __global__ void __launch_bounds__(256) norm_generic_kernel(float* __restrict__ y,
                                                            float* __restrict__ stat0,
@@ -787,7 +867,15 @@ int launch_norm(float* y, float* s0, float* s1, const float* x, const float* g, 
                 int64_t outer, int64_t n, int64_t inner, float eps, int kind) {
   if (outer * n * inner == 0) return WXX_OK;
   cudaStream_t s = wxx::stream();
-  if (inner == 1 && n <= 1024) {
+  const bool vec = n % 4 == 0 && n >= 128 &&
+                   !((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(x) |
+                      reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(b)) & 15);
+  if (inner == 1 && n <= 1024 && vec) {
+    unsigned grid = (unsigned)((outer + 7) / 8);
+    if (n <= 256) norm_warp4_kernel<2><<<grid, 256, 0, s>>>(y, s0, s1, x, g, b, outer, (int)n, eps, kind);
+    else if (n <= 512) norm_warp4_kernel<4><<<grid, 256, 0, s>>>(y, s0, s1, x, g, b, outer, (int)n, eps, kind);
+    else norm_warp4_kernel<8><<<grid, 256, 0, s>>>(y, s0, s1, x, g, b, outer, (int)n, eps, kind);
+  } else if (inner == 1 && n <= 1024) {
     unsigned grid = (unsigned)((outer + 7) / 8);
     if (n <= 128) norm_warp_kernel<4><<<grid, 256, 0, s>>>(y, s0, s1, x, g, b, outer, (int)n, eps, kind);
     else if (n <= 256) norm_warp_kernel<8><<<grid, 256, 0, s>>>(y, s0, s1, x, g, b, outer, (int)n, eps, kind);
