@@ -344,6 +344,49 @@ __global__ void splitk_reduce_kernel(float* __restrict__ C, const float* __restr
   }
 }
 
+// splitk_reduce_kernel for one row-major matrix (kind 0, batch 1) with N and
+// ldc multiples of 4, 16-byte aligned C / ws / bias and splits * M * N below
+// 2^31: four consecutive columns per thread with 16-byte loads and stores
+// and 32-bit index arithmetic (the general kernel spends most of its
+// instructions on 64-bit divisions).  Per element the same sum order and
+// epilogue as splitk_reduce_kernel, so the same bits.
+__global__ void splitk_reduce4_kernel(float* __restrict__ C, const float* __restrict__ ws,
+                                      int splits, int M, int N, float alpha,
+                                      const float* __restrict__ bias, int bias_mode, int ldc,
+                                      ConvPost post, int round_tf32) {
+  const int N4 = N >> 2;
+  const int total4 = M * N4;
+  const int MN = M * N;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += gridDim.x * blockDim.x) {
+    const int m = i / N4;
+    const int n = (i - m * N4) * 4;
+    const int src = m * N + n;
+    float4 acc = __ldg(reinterpret_cast<const float4*>(ws + src));
+    for (int k = 1; k < splits; ++k) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(ws + k * MN + src));
+      acc.x += w.x;
+      acc.y += w.y;
+      acc.z += w.z;
+      acc.w += w.w;
+    }
+    float v[4] = {acc.x * alpha, acc.y * alpha, acc.z * alpha, acc.w * alpha};
+    if (bias != nullptr) {
+      const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + (bias_mode == 1 ? n : src)));
+      v[0] += bb.x;
+      v[1] += bb.y;
+      v[2] += bb.z;
+      v[3] += bb.w;
+    }
+    const int o = m * ldc + n;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j] = conv_post(post, v[j], n + j, (int64_t)(o + j));
+      if (round_tf32) v[j] = tf32_rna(v[j]);
+    }
+    *reinterpret_cast<float4*>(C + o) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
 int run_tc(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
            const CUtensorMap& b1, GemmParams& p);
 
@@ -395,7 +438,20 @@ int run_splitk(int bn, const CUtensorMap& a0, const CUtensorMap& a1, const CUten
   p.epi.res = nullptr;
   memset(&p.epi.post, 0, sizeof(p.epi.post));
   st = run_tc(bn, a0, a1, b0, b1, p);
-  if (st == WXX_OK) {
+  const bool vec4 =
+      real.kind == 0 && p.batch == 1 && p.N % 4 == 0 && real.ldc % 4 == 0 &&
+      (int64_t)p.splits * MN < (int64_t(1) << 31) &&
+      (int64_t)(p.M - 1) * real.ldc + p.N < (int64_t(1) << 31) &&
+      (real.bias_mode == 0 || real.bias_mode == 1 || real.bias_mode == 2) &&
+      !((reinterpret_cast<uintptr_t>(real.C) | reinterpret_cast<uintptr_t>(ws) |
+         reinterpret_cast<uintptr_t>(real.bias_mode ? real.bias : nullptr)) & 15);
+  if (st == WXX_OK && vec4) {
+    splitk_reduce4_kernel<<<wxx::grid_for(MN / 4, 256), 256, 0, wxx::stream()>>>(
+        real.C, (const float*)ws, p.splits, p.M, p.N, real.alpha,
+        real.bias_mode ? real.bias : nullptr, real.bias_mode, real.ldc, real.post,
+        real.round_tf32);
+    st = wxx::after_launch(__FILE__, __LINE__);
+  } else if (st == WXX_OK) {
     splitk_reduce_kernel<<<wxx::grid_for(MN * p.batch, 256), 256, 0, wxx::stream()>>>(
         real.C, (const float*)ws, p.splits, p.batch, p.M, p.N, real.alpha,
         real.bias_mode ? real.bias : nullptr, real.bias_mode, real.kind,
