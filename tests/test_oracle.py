@@ -155,6 +155,37 @@ def test_state_dict_generators_shapes():
     assert h["layers.1.feed_forward.w1.weight"].shape == (32, int(2 * 4 * 32 / 3))
 
 
+def _hyena_structural_count(V, D, N, order, k=3, filter_hidden=64, pe_features=8):
+    """Hyena's parameter total from its structure (reference
+    tests/test_hyena.py:83-113): per block norm1 D, proj_v / proj_x / out_proj
+    (2 + order) D^2, the short conv k D + D, order filter MLPs
+    (2F+1) h + h + h D + D, the decay order D, norm2 D, SwiGLU 3 D ffn with
+    ffn = int(8 D / 3); plus the tied embedding V D and the final norm D."""
+    ffn = int(2 * (4 * D) / 3)
+    fin = 2 * pe_features + 1
+    block = (D + (2 + order) * D * D + (k * D + D)
+             + order * (fin * filter_hidden + filter_hidden + filter_hidden * D + D)
+             + order * D + D + 3 * D * ffn)
+    return N * block + V * D + D
+
+
+def test_hyena_state_dict_parameter_counts_match_reference():
+    """The Hyena state dict holds the reference's parameter total for orders
+    1-4 (reference tests/test_hyena.py:116-124) and, for its HyenaLLM
+    configuration (vocab 2048, dim 256, depth 6, order 4), the quoted
+    6 444 288 plus 6 * 4 * 2 * 8 * 64 for the filters' positional encoding
+    (tests/test_hyena.py:126-132).  The GPU model tests load this state dict
+    into ``wxx_b200.nn.Hyena`` strictly (every key, no extra key, equal
+    shapes), so the product model holds the same total."""
+    for order in (1, 2, 3, 4):
+        sd = init.hyena_state_dict(0, 32, 16, 2, order)
+        assert sum(a.size for a in sd.values()) == _hyena_structural_count(32, 16, 2, order)
+    sd = init.hyena_state_dict(0, 2048, 256, 6, 4)
+    total = sum(a.size for a in sd.values())
+    assert total == _hyena_structural_count(2048, 256, 6, 4)
+    assert total == 6_444_288 + 6 * 4 * 2 * 8 * 64
+
+
 def test_model_oracles_fast_vs_exact():
     sd = init.gpt2_state_dict(0, 64, 32, 4, 2, 16)
     ids = init.token_ids(1, 2, 16, 64)
